@@ -1,0 +1,410 @@
+"""Benchmark of the gated-candidate training step on B200.
+
+Workload (the single-GPU case the metric is quoted
+on): one gated Linear, X [8192 x 4096] bf16 N(0,1) with 1% of the channels
+(41, seeded randperm) scaled x20, base W [14336 x 4096] N(0, 0.02), K=5 packed
+candidates {Q3_K, Q4_K, Q5_K, Q6_K, Q8_0}, gates N(0,1), tau = 0.5,
+dY N(0,1).  A step is forward + dX + gate gradient through MixedQuantLinear's
+autograd (the public API): vq_mix, vq_linear_fwd, vq_linear_dx, vq_gategrad.
+Tokens per step = 8192.  Candidates are built by the round-to-nearest packer
+(libggml is unavailable), seeded; inputs are synthetic.
+
+--gpus N (torchrun, one process per GPU): the same layer tensor-parallel,
+column-parallel over its 14336 output rows (block-aligned split), with the
+exchange steps of a TP column-parallel layer: all-reduce of dX (exact input
+gradient) and all-reduce of the K gate gradients.  Total work is fixed
+("strong" scaling); value = tokens / max-over-ranks step time.
+
+--impl reference: the CPU path (the numpy restatement of the reference's
+float32 torch algorithm, layers.py:322-363 + F.linear) on the host cores, on
+a bounded token sample of the same layer, reported in the same unit.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "voodoo-dyn-quant_b200"))
+
+T_TOK, N_OUT, K_IN = 8192, 14336, 4096
+TYPES = ["Q3_K", "Q4_K", "Q5_K", "Q6_K", "Q8_0"]
+TAU = 0.5
+METRIC = "gated-distill train tokens/s"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+BPW = {"Q2_K": 84 / 256, "Q3_K": 110 / 256, "Q4_K": 144 / 256, "Q5_K": 176 / 256, "Q6_K": 210 / 256,
+       "Q8_0": 34 / 32, "IQ4_XS": 136 / 256}
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d, "measured"
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+def config(n_gpus: int, extra=None):
+    c = {
+        "workload": "config2: gated Linear X[8192x4096] W[14336x4096], K=5 {Q3_K,Q4_K,Q5_K,Q6_K,Q8_0}, "
+                    "tau=0.5, fwd+dX+gate-grad",
+        "tokens_per_step": T_TOK,
+        "candidates": TYPES,
+        "parallelism": f"tp{n_gpus}" if n_gpus > 1 else "tp1",
+        "l2": "inputs larger than L2 (X 67 MB, dY 235 MB, packed candidates 209 MB, W_mix 117 MB)",
+    }
+    if extra:
+        c.update(extra)
+    return c
+
+
+# ----------------------------------------------------------------------------- clocks
+class ClockSampler:
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if self.path is None or not os.path.exists(self.path):
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        rows = []
+        for line in open(self.path):
+            f = [x.strip() for x in line.split(",")]
+            if len(f) >= 9:
+                rows.append(f)
+        os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = sorted(float(r[1]) for r in rows if r[1].replace(".", "").isdigit())
+        mx = max(float(r[2]) for r in rows if r[2].replace(".", "").isdigit()) if rows else None
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower().startswith("active")})
+        return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": mx, "reasons": reasons,
+                "samples": len(rows)}
+
+
+# ----------------------------------------------------------------------------- setup
+def make_layer(device, rank=0, world=1):
+    import torch
+    from voodoo_quant.layers import MixedQuantLinear
+    from voodoo_quant.parallel import ShardSpec, block_aligned_split
+    from voodoo_quant.quants import rtn
+
+    g = torch.Generator(device=device).manual_seed(0)
+    w = torch.randn(N_OUT, K_IN, device=device, generator=g) * 0.02
+    full = {q: rtn.quantize(w, q) for q in TYPES}
+    gates = torch.randn(len(TYPES), generator=torch.Generator().manual_seed(1))
+    if world > 1:
+        off, n = block_aligned_split(N_OUT, world, rank)
+        spec = ShardSpec(full_out=N_OUT, full_in=K_IN, row_offset=off, row_len=n)
+        layer = MixedQuantLinear(K_IN, n, TYPES, w[off:off + n], tensor_name="bench.proj", shard_spec=spec,
+                                 candidate_bytes=full)
+    else:
+        layer = MixedQuantLinear(K_IN, N_OUT, TYPES, w, tensor_name="bench.proj", candidate_bytes=full)
+    del w, full
+    with torch.no_grad():
+        layer.gates.copy_(gates)
+    layer.set_temperature(TAU)
+    return layer
+
+
+def make_inputs(device, n_out_local, seed=2):
+    import torch
+
+    g = torch.Generator(device=device).manual_seed(seed)
+    x = torch.randn(T_TOK, K_IN, device=device, generator=g)
+    ch = torch.randperm(K_IN, generator=torch.Generator().manual_seed(3))[: K_IN // 100].to(device)
+    x[:, ch] *= 20.0
+    x = x.to(torch.bfloat16)
+    dy = torch.randn(T_TOK, n_out_local, device=device, generator=g).to(torch.bfloat16)
+    return x, dy
+
+
+# ----------------------------------------------------------------------------- GPU arm
+def run_gpu(args):
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        from voodoo_quant import parallel
+
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=300))
+        parallel.adopt_process_group(local)
+    from voodoo_quant import _C
+    from voodoo_quant.parallel import TP, all_reduce_gate_grads, tp_copy_to_parallel
+
+    _C.load_library()
+    layer = make_layer(dev, rank, world)
+    n_loc = layer.out_features
+    x, dy = make_inputs(dev, n_loc, seed=2 + rank)
+    stream = torch.cuda.current_stream()
+
+    def step(xin, dyin):
+        xg = xin.requires_grad_(True) if not xin.requires_grad else xin
+        xi = tp_copy_to_parallel(xg) if world > 1 else xg
+        y = layer(xi)
+        layer.gates.grad = None
+        torch.autograd.backward(y, dyin)
+        if world > 1:
+            all_reduce_gate_grads([layer.gates])
+        return xg
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    for _ in range(args.warmup):
+        x.grad = None
+        step(x, dy)
+    torch.cuda.synchronize()
+    barrier()
+
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        barrier()
+        torch.cuda.synchronize()
+        ev0.record(stream)
+        for _ in range(args.steps):
+            x.grad = None
+            step(x, dy)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+    ms = ev0.elapsed_time(ev1) / args.steps
+    t = torch.tensor([ms], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    clocks = clk.summary()
+    assert _C.device_error() == 0
+
+    # ---- per-kernel breakdown (same stream, CUDA events per launch) ----
+    blocks = layer._candidate_blocks()
+    probs = layer.get_probs().detach()
+    pad = layer.padded_in_features
+    ws = layer._gategrad_workspace(dev)
+    wm = _C.mix(TYPES, blocks, probs, n_loc, pad, K_IN)
+    names = ["mix", "fwd", "dx", "gategrad"]
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(args.kernel_iters)]
+    for i in range(args.kernel_iters + 2):
+        e = evs[i - 2] if i >= 2 else None
+        if e: e[0].record(stream)
+        _C.mix(TYPES, blocks, probs, n_loc, pad, K_IN, out=wm)
+        if e: e[1].record(stream)
+        _C.linear_fwd(x, wm, n_loc, K_IN)
+        if e: e[2].record(stream)
+        _C.linear_dx(dy, wm, K_IN)
+        if e: e[3].record(stream)
+        _C.gategrad(dy, x, TYPES, blocks, n_loc, K_IN, pad, workspace=ws)
+        if e: e[4].record(stream)
+    torch.cuda.synchronize()
+    kt = {n: sum(e[j].elapsed_time(e[j + 1]) for e in evs) / len(evs) for j, n in enumerate(names)}
+
+    # ---- e2e through the public API with host buffers ----
+    xh = x.detach().cpu().pin_memory()
+    dyh = dy.cpu().pin_memory()
+    gh = torch.empty(len(TYPES), dtype=torch.float32).pin_memory()
+    for i in range(args.warmup + args.e2e_steps):
+        if i == args.warmup:
+            torch.cuda.synchronize()
+            barrier()
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+        xd = xh.to(dev, non_blocking=True)
+        dyd = dyh.to(dev, non_blocking=True)
+        step(xd, dyd)
+        gh.copy_(layer.gates.grad, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = torch.tensor([e0.elapsed_time(e1) / args.e2e_steps], device=dev)
+    if world > 1:
+        dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
+    e2e_ms = float(e2e_ms.item())
+
+    if rank == 0:
+        pk, pk_kind = peaks()
+        flops_gemm = 2.0 * T_TOK * n_loc * K_IN
+        ach = {n: flops_gemm / (kt[n] * 1e-3) / 1e12 for n in ("fwd", "dx", "gategrad")}
+        packed = n_loc * K_IN * sum(BPW[q] for q in TYPES)
+        mix_bytes = packed + n_loc * K_IN * 2
+        dom = max(("fwd", "dx", "gategrad"), key=lambda n: kt[n])
+        peak_t = float(pk.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
+        peak_b = float(pk.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
+        kernels = {n: {"ms": round(kt[n], 4), "TFLOP/s": round(ach[n], 1), "frac": round(ach[n] / peak_t, 4)}
+                   for n in ("fwd", "dx", "gategrad")}
+        kernels["mix"] = {"ms": round(kt["mix"], 4), "GB/s": round(mix_bytes / (kt["mix"] * 1e-3) / 1e9, 1),
+                          "frac": round(mix_bytes / (kt["mix"] * 1e-3) / 1e9 / peak_b, 4)}
+        gemm_ms = kt["fwd"] + kt["dx"] + kt["gategrad"]
+        out = {
+            "metric": METRIC,
+            "value": round(T_TOK / (ms * 1e-3), 1),
+            "unit": "tokens/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms, 4),
+            "higher_is_better": True,
+            "scaling": "strong",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic (seeded; candidates from the round-to-nearest GGUF packer)",
+            "config": config(world),
+            "roofline": {
+                "bound": "tensor",
+                "kernel": f"gemm_{dom}",
+                "achieved": round(ach[dom], 1),
+                "peak": peak_t,
+                "unit": "TFLOP/s",
+                "frac": round(ach[dom] / peak_t, 4),
+                "peak_source": f"{pk_kind} bf16_tflops (burst)",
+                "traffic": None,
+                "mix_gemm_frac": round(3 * flops_gemm / (gemm_ms * 1e-3) / 1e12 / peak_t, 4),
+                "step_frac": round(3 * flops_gemm / (ms * 1e-3) / 1e12 / peak_t / world, 4),
+            },
+            "kernels": kernels,
+            "e2e": {
+                "value": round(T_TOK / (e2e_ms * 1e-3), 1),
+                "unit": "tokens/s",
+                "h2d_bytes_per_step": int(x.numel() * 2 + dy.numel() * 2),
+                "d2h_bytes_per_step": int(gh.numel() * 4),
+            },
+            "gpu_launches": 5 * args.steps,
+            "clocks": clocks,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            out["cpu_baseline"] = cpu_baseline(args.cpu_tokens, repeats=1)
+        print(json.dumps(out), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+# ----------------------------------------------------------------------------- CPU (reference) arm
+def _cpu_setup(t_sample: int):
+    import numpy as np
+    import torch
+
+    sys.path.insert(0, str(ROOT))
+    from oracle import mixgemm
+    from voodoo_quant.quants import rtn
+
+    torch.manual_seed(0)
+    w = torch.randn(N_OUT, K_IN) * 0.02
+    blocks = [rtn.quantize(w, q).numpy() for q in TYPES]
+    del w
+    threads = os.cpu_count() or 1
+    cands = mixgemm.decode_candidates(blocks, TYPES, N_OUT, K_IN, K_IN, threads=threads)  # untimed (cached _w_k)
+    rng = np.random.default_rng(2)
+    x = rng.standard_normal((t_sample, K_IN), dtype=np.float32)
+    x[:, rng.permutation(K_IN)[: K_IN // 100]] *= 20.0
+    dy = rng.standard_normal((t_sample, N_OUT), dtype=np.float32)
+    gates = torch.randn(len(TYPES), generator=torch.Generator().manual_seed(1)).numpy()
+    return mixgemm, cands, x, dy, gates
+
+
+def _cpu_step(mixgemm, cands, x, dy, gates):
+    threads = os.cpu_count() or 1
+    p = mixgemm.softmax_probs(gates, TAU)
+    wm = mixgemm.mixed_weight(cands, p, threads=threads)
+    mixgemm.linear_fwd(x, wm)
+    mixgemm.linear_dx(dy, wm)
+    g = mixgemm.prob_grad(dy, x, cands, threads=threads)
+    return mixgemm.gate_grad(p, g, TAU)
+
+
+def cpu_baseline(t_sample: int, repeats: int = 1):
+    cores = os.cpu_count() or 1
+    mixgemm, cands, x, dy, gates = _cpu_setup(t_sample)
+    _cpu_step(mixgemm, cands, x, dy, gates)
+    t0 = time.perf_counter()
+    for _ in range(repeats):
+        _cpu_step(mixgemm, cands, x, dy, gates)
+    dt = (time.perf_counter() - t0) / repeats
+    return {"value": round(t_sample / dt, 2), "unit": "tokens/s", "cores": cores, "kind": "port",
+            "sample": f"{t_sample} of 8192 tokens of the config-2 layer (full N, Kin, K=5), float32 numpy "
+                      f"(BLAS threads = {cores}); candidates pre-decoded like the reference's cached _w_k"}
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    mixgemm, cands, x, dy, gates = _cpu_setup(args.cpu_tokens)
+    for _ in range(args.warmup):
+        _cpu_step(mixgemm, cands, x, dy, gates)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        _cpu_step(mixgemm, cands, x, dy, gates)
+    dt = (time.perf_counter() - t0) / args.steps
+    v = round(args.cpu_tokens / dt, 2)
+    cores = os.cpu_count() or 1
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    out = {
+        "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(dt * 1e3 * T_TOK / args.cpu_tokens, 2),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded)", "config": config(world), "impl": "reference",
+        "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port",
+                         "sample": f"{args.cpu_tokens} of 8192 tokens per step, float32 numpy restatement "
+                                   "of the reference's torch CPU path"},
+        "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(out), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--kernel-iters", type=int, default=10)
+    ap.add_argument("--e2e-steps", type=int, default=10)
+    ap.add_argument("--cpu-tokens", type=int, default=2048)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_gpu(args)
+
+
+if __name__ == "__main__":
+    main()

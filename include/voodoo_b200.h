@@ -1,0 +1,140 @@
+/*
+ * voodoo_b200.h -- C ABI of libvoodoo_b200.so, the B200 (sm_100a) kernels of
+ * the gated-candidate training step of Voodoo dynamic quantisation.
+ *
+ * Conventions
+ *   - Every pointer is DEVICE memory unless a comment says "host".
+ *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default stream).
+ *   - Matrices are row-major; `ld*` are leading dimensions in ELEMENTS.
+ *     bf16 matrices used as GEMM operands need a 16-byte aligned base and a
+ *     leading dimension that is a multiple of 8.
+ *   - Packed candidates are GGUF block streams, rows contiguous, exactly the
+ *     layout ggml's quantize_* writes ([rows * cols / block_elems, block_bytes]
+ *     uint8).  Formats are ggml type ids: Q8_0 = 8, Q2_K = 10, Q3_K = 11,
+ *     Q4_K = 12, Q5_K = 13, Q6_K = 14, IQ4_XS = 23.
+ *   - Return 0 on success or a negative VQ_ERR_* code; vq_last_error() gives a
+ *     thread-local message.  No C++ exception crosses this boundary.
+ *   - Calls only enqueue work on `stream`: they never synchronise (except
+ *     vq_device_error) and never allocate; scratch space is caller-provided.
+ *   - Thread-safe for distinct streams.
+ */
+#ifndef VOODOO_B200_H
+#define VOODOO_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define VQ_ABI_VERSION 1
+
+#define VQ_OK 0
+#define VQ_ERR_INVALID (-1)     /* bad shape, alignment, null pointer, ... (Python: ValueError)   */
+#define VQ_ERR_CUDA (-2)        /* CUDA runtime / driver failure          (Python: RuntimeError) */
+#define VQ_ERR_UNSUPPORTED (-3) /* unknown or unsupported ggml type       (Python: ValueError)   */
+
+/* Message of the last failing call on this thread. */
+const char* vq_last_error(void);
+
+/* VQ_ABI_VERSION of the loaded library. */
+int vq_abi_version(void);
+
+/* Block geometry of a ggml type.  Replaces the QuantTypeInfo lookup
+ * voodoo_quant/ggml.py:158-168 (get_quant_info) for the supported formats. */
+int vq_format_info(int ggml_type, int* block_elems /* host */, int* block_bytes /* host */);
+
+/* Synchronise `stream`, then return and clear the device error word in *code
+ * (host): 0 = none; (1 << 16 | where) = an mbarrier wait gave up after its
+ * time limit; (2 << 16) = a kernel met an unknown format. */
+int vq_device_error(void* stream, int* code /* host */);
+
+/* K0 -- bit-exact dequantisation of one packed candidate into float32
+ * out[rows, cols] (cols = padded in_features, a multiple of the block size).
+ * Replaces dequantize_tensor_gpu, voodoo_quant/layers.py:298-319 (per-format
+ * decoders layers.py:62-213, quants/gpu_dequant.py:460-519) and the libggml
+ * call ggml.dequantize_tensor, voodoo_quant/ggml.py:224-269. */
+int vq_dequant(int ggml_type, const void* blocks, int64_t rows, int64_t cols, float* out, void* stream);
+
+/* K1a -- softmax candidate mixture W_mix = sum_k probs[k] * W_k, accumulated
+ * in fp32 from the bit-exact decodes and rounded once to bf16 into
+ * w_bf16[rows, ldw]; columns in [cols, ldw) are written as zero.
+ * types/blocks are HOST arrays of K entries (ggml ids / device pointers),
+ * probs is a device float[K]; padded_cols is a multiple of 256.
+ * Replaces _MixedWeightFunction.forward, voodoo_quant/layers.py:336-352,
+ * _MixedWeightFunctionLazy.forward :502-580 and get_mixed_weight :1474-1535. */
+int vq_mix(int K, const int* types, const void* const* blocks, const float* probs, int64_t rows,
+           int64_t padded_cols, int64_t cols, void* w_bf16, int64_t ldw, void* stream);
+
+/* K1b -- y[T, N] = x[T, Kin] * w[N, Kin]^T (bf16 in, fp32 accumulate in TMEM,
+ * bf16 out), persistent tcgen05 GEMM.  Replaces F.linear(x, mixed),
+ * voodoo_quant/layers.py:1730-1731. */
+int vq_linear_fwd(const void* x, int64_t T, int64_t Kin, int64_t ldx, const void* w, int64_t N, int64_t ldw,
+                  void* y, int64_t ldy, void* stream);
+
+/* K2 -- dx[T, Kin] = dy[T, N] * w[N, Kin] (w read MN-major by TMA, no
+ * transpose copy).  Replaces the input-gradient half of F.linear's autograd
+ * in MixedQuantLinear.forward, voodoo_quant/layers.py:1731. */
+int vq_linear_dx(const void* dy, int64_t T, int64_t N, int64_t lddy, const void* w, int64_t Kin, int64_t ldw,
+                 void* dx, int64_t lddx, void* stream);
+
+/* Bytes of scratch vq_gategrad needs for an [N, Kin] layer with K candidates. */
+size_t vq_gategrad_workspace_bytes(int64_t N, int64_t Kin, int K);
+
+/* K3 -- grad_probs[k] = <dy^T x, W_k> over the first Kin columns, for the K
+ * packed candidates (types/blocks HOST arrays, padded_cols = padded
+ * in_features).  dW = dy^T x is accumulated tile by tile in TMEM and reduced
+ * against re-decoded candidate tiles in the GEMM epilogue; it is never
+ * written to memory.  Fixed-order (deterministic) reduction.
+ * Replaces _MixedWeightFunction.backward, voodoo_quant/layers.py:355-363
+ * (and _MixedWeightFunctionLazy.backward :583-667) together with the weight
+ * gradient of F.linear that feeds it. */
+int vq_gategrad(const void* dy, int64_t lddy, const void* x, int64_t ldx, int64_t T, int64_t N, int64_t Kin, int K,
+                const int* types, const void* const* blocks, int64_t padded_cols, void* workspace,
+                size_t workspace_bytes, float* grad_probs, void* stream);
+
+/* K1 convenience: vq_mix into w_mix[N, ldw] followed by vq_linear_fwd. */
+int vq_mixgemm_fwd(const void* x, int64_t T, int64_t Kin, int64_t ldx, int K, const int* types,
+                   const void* const* blocks, const float* probs, int64_t N, int64_t padded_cols, void* w_mix,
+                   int64_t ldw, void* y, int64_t ldy, void* stream);
+
+/* K4 -- fused chunked-vocab CE + KL(teacher || student) on bf16 logits.
+ * Per row r: row_ce[r] = lse(s) - s[y] (0 when targets[r] < 0) and
+ * row_kl[r] = T^2 * KL(softmax(t/T) || softmax(s/T)); when dlogits != NULL it
+ * also writes d/ds = ce_weight * (softmax(s) - onehot(y))
+ *                  + kl_weight * T * (softmax(s/T) - softmax(t/T))
+ * (the gradient of ce_weight * sum(row_ce) + kl_weight * sum(row_kl)).
+ * targets are int64 token ids.  Replaces the loss of
+ * voodoo_quant/training/trainer.py:2567-2575 and _chunked_forward_loss
+ * :797-821. */
+int vq_loss_fused(const void* s_logits, int64_t lds, const void* t_logits, int64_t ldt, const int64_t* targets,
+                  int64_t rows, int64_t V, float temperature, float ce_weight, float kl_weight, float* row_ce,
+                  float* row_kl, void* dlogits, int64_t ldg, void* stream);
+
+/* K4, vocab-parallel pass 1: per-row partial statistics float[rows, 8] of this
+ * rank's vocab shard [vocab_start, vocab_start + V).  Replaces the per-chunk
+ * _global_lse MAX/SUM all-reduce inputs of _tp_vocab_parallel_losses,
+ * voodoo_quant/training/trainer.py:974-996. */
+int vq_loss_stats(const void* s_logits, int64_t lds, const void* t_logits, int64_t ldt, const int64_t* targets,
+                  int64_t vocab_start, int64_t rows, int64_t V, float temperature, float* stats, void* stream);
+
+/* K4, combine: stats[ranks, rows, 8] (all ranks' partials, rank order) ->
+ * row_lse[rows, 4] (lse(s), lse(s/T), lse(t/T), target-found flag), row_ce,
+ * row_kl.  Replaces the cross-rank logsumexp of trainer.py:974-996 and the
+ * partial-loss all-reduce :1061-1064. */
+int vq_loss_combine(const float* stats, int ranks, int64_t rows, float temperature, float* row_lse,
+                    float* row_ce, float* row_kl, void* stream);
+
+/* K4, vocab-parallel pass 2: the gradient of this rank's logits shard given
+ * the global row_lse.  Replaces the per-chunk backward of
+ * _tp_vocab_parallel_losses, trainer.py:1041-1046. */
+int vq_loss_grad(const void* s_logits, int64_t lds, const void* t_logits, int64_t ldt, const int64_t* targets,
+                 int64_t vocab_start, int64_t rows, int64_t V, float temperature, const float* row_lse,
+                 float ce_weight, float kl_weight, void* dlogits, int64_t ldg, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* VOODOO_B200_H */

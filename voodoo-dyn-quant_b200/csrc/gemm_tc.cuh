@@ -1,0 +1,306 @@
+// Persistent, warp-specialised tcgen05 GEMM for the gated Linear.
+//
+//   D[M, N] = sum_k A[m, k] * B[n, k]      (bf16 operands, fp32 accumulate in TMEM)
+//
+// Operands are streamed by TMA in 128-byte-swizzled BK = 64 slices; either
+// operand may be K-major (K contiguous) or MN-major (M/N contiguous), which
+// covers the three GEMMs of the layer without any transpose copies:
+//
+//   forward   Y  = X  W^T : A = X  [T, Kin]  K-major,  B = W [N, Kin]  K-major
+//   input grad dX = dY W  : A = dY [T, N]    K-major,  B = W [N, Kin]  MN-major
+//   weight grad dW = dY^T X: A = dY [T, N]   MN-major, B = X [T, Kin]  MN-major
+//
+// Warp roles (256 threads): warp 0 issues TMA, warp 1 issues tcgen05.mma
+// (one thread), warp 2 owns the TMEM allocation, warps 4-7 run the epilogue.
+// The accumulator is double buffered in TMEM (2 x 256 fp32 columns) so the
+// epilogue of tile i overlaps the main loop of tile i+1.
+//
+// Epilogues:
+//   kEpiStoreBf16 : D -> bf16 C[M, N] (row-major, leading dimension ldc).
+//   kEpiGateGrad  : D is a 128 x 256 tile of dW; each epilogue thread owns one
+//                   output row and dots it against the re-decoded candidate
+//                   weights of the same 256-column unit, giving per-tile
+//                   partial sums of g_k = <dW, W_k> that are written to
+//                   partials[tile][warp][k] and reduced in fixed order by
+//                   gategrad_reduce_kernel.  dW never reaches global memory.
+#pragma once
+
+#include "common.cuh"
+#include "formats.cuh"
+
+namespace vq {
+namespace gemm {
+
+constexpr int BM = 128;
+constexpr int BN = 256;
+constexpr int BK = 64;
+constexpr int STAGES = 4;
+constexpr int THREADS = 256;
+constexpr int A_STAGE = BM * BK * 2;  // 16 KiB
+constexpr int B_STAGE = BN * BK * 2;  // 32 KiB
+constexpr int TMEM_COLS = 512;        // two 256-column accumulators
+constexpr int GROUP_N = 8;            // raster: tiles sweep M inside a band of 8 N-blocks
+
+constexpr int kEpiStoreBf16 = 0;
+constexpr int kEpiGateGrad = 1;
+
+struct SmemLayout {
+  static constexpr int a_off = 0;
+  static constexpr int b_off = a_off + STAGES * A_STAGE;
+  static constexpr int bar_off = b_off + STAGES * B_STAGE;      // 8-byte barriers
+  static constexpr int n_bars = 2 * STAGES + 4;
+  static constexpr int misc_off = bar_off + n_bars * 8;         // tmem base, abort flag
+  static constexpr int total = misc_off + 16;
+  static constexpr int alloc = total + 1024;                    // slack for 1 KiB alignment
+};
+
+struct Params {
+  int M, N, K;
+  int num_m_blk, num_n_blk, num_k_blk, num_tiles;
+  // kEpiStoreBf16
+  __nv_bfloat16* C;
+  long long ldc;
+  // kEpiGateGrad: candidate rows = M (out features), valid columns = cols
+  CandSet cands;
+  int units_per_row;
+  long long cols;
+  float* partials;
+  int* err;
+};
+
+__device__ __forceinline__ void tile_coords(const Params& p, int tile, int& m_blk, int& n_blk) {
+  const int band = GROUP_N * p.num_m_blk;
+  const int g = tile / band;
+  const int first_n = g * GROUP_N;
+  const int gn = min(GROUP_N, p.num_n_blk - first_n);
+  const int r = tile - g * band;
+  m_blk = r / gn;
+  n_blk = first_n + (r - m_blk * gn);
+}
+
+template <bool kAmn, bool kBmn, int kEpi>
+__global__ void __launch_bounds__(THREADS, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Params p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t bar0 = sbase + SmemLayout::bar_off;
+  auto full_bar = [&](int s) { return bar0 + 8u * s; };
+  auto empty_bar = [&](int s) { return bar0 + 8u * (STAGES + s); };
+  auto tfull_bar = [&](int a) { return bar0 + 8u * (2 * STAGES + a); };
+  auto tempty_bar = [&](int a) { return bar0 + 8u * (2 * STAGES + 2 + a); };
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + SmemLayout::misc_off);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + SmemLayout::misc_off + 4);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(tfull_bar(a), 1);
+      mbar_init(tempty_bar(a), 4);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 2) {
+    tmem_alloc(smem_u32(tmem_holder), TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      uint32_t it = 0;
+      bool alive = true;
+      for (int tile = blockIdx.x; tile < p.num_tiles && alive; tile += gridDim.x) {
+        int m_blk, n_blk;
+        tile_coords(p, tile, m_blk, n_blk);
+        for (int kb = 0; kb < p.num_k_blk; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1u;
+          if (!mbar_wait(empty_bar(s), ph ^ 1u, abort_flag)) {
+            report_error(p.err, kDevWaitTimeout, 1);
+            alive = false;
+            break;
+          }
+          mbar_arrive_expect_tx(full_bar(s), A_STAGE + B_STAGE);
+          const uint32_t a_dst = sbase + SmemLayout::a_off + s * A_STAGE;
+          const uint32_t b_dst = sbase + SmemLayout::b_off + s * B_STAGE;
+          const int k0 = kb * BK;
+          if (kAmn) {
+#pragma unroll
+            for (int j = 0; j < BM / 64; ++j) tma_load_2d(a_dst + j * (64 * BK * 2), &tmA, full_bar(s), m_blk * BM + 64 * j, k0);
+          } else {
+            tma_load_2d(a_dst, &tmA, full_bar(s), k0, m_blk * BM);
+          }
+          if (kBmn) {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j) tma_load_2d(b_dst + j * (64 * BK * 2), &tmB, full_bar(s), n_blk * BN + 64 * j, k0);
+          } else {
+            tma_load_2d(b_dst, &tmB, full_bar(s), k0, n_blk * BN);
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16_f32(BM, BN, kAmn, kBmn);
+      uint32_t it = 0, local = 0;
+      bool alive = true;
+      for (int tile = blockIdx.x; tile < p.num_tiles && alive; tile += gridDim.x, ++local) {
+        const int acc = local & 1;
+        const uint32_t aph = (local >> 1) & 1u;
+        if (!mbar_wait(tempty_bar(acc), aph ^ 1u, abort_flag)) {
+          report_error(p.err, kDevWaitTimeout, 2);
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = 0; kb < p.num_k_blk; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1u;
+          if (!mbar_wait(full_bar(s), ph, abort_flag)) {
+            report_error(p.err, kDevWaitTimeout, 3);
+            alive = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = sbase + SmemLayout::a_off + s * A_STAGE;
+          const uint32_t b_addr = sbase + SmemLayout::b_off + s * B_STAGE;
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            // K-major: +32 bytes per 16-element K step inside the swizzle row.
+            // MN-major: +16 rows of 128 bytes per K step; MN atoms 64*BK*2 apart.
+            const uint64_t adesc = kAmn ? smem_desc_sw128(a_addr + kk * 2048, 64 * BK * 2, 1024)
+                                        : smem_desc_sw128(a_addr + kk * 32, 16, 1024);
+            const uint64_t bdesc = kBmn ? smem_desc_sw128(b_addr + kk * 2048, 64 * BK * 2, 1024)
+                                        : smem_desc_sw128(b_addr + kk * 32, 16, 1024);
+            tc_mma_bf16(d_tmem, adesc, bdesc, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+          }
+          tc_commit(empty_bar(s));  // frees this smem stage once its MMAs retire
+        }
+        if (!alive) break;
+        tc_commit(tfull_bar(acc));  // accumulator ready for the epilogue
+      }
+    }
+  } else if (warp >= 4) {
+    // --------------------------------------------------------------- epilogue
+    const int wq = warp & 3;  // TMEM lanes 32*wq .. 32*wq+31
+    uint32_t local = 0;
+    for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++local) {
+      int m_blk, n_blk;
+      tile_coords(p, tile, m_blk, n_blk);
+      const int acc = local & 1;
+      const uint32_t aph = (local >> 1) & 1u;
+      if (!mbar_wait(tfull_bar(acc), aph, abort_flag)) {
+        if (lane == 0) report_error(p.err, kDevWaitTimeout, 4);
+        break;
+      }
+      tc_fence_after();
+      const long long row = static_cast<long long>(m_blk) * BM + 32 * wq + lane;
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(32 * wq) << 16) + acc * BN;
+
+      if (kEpi == kEpiStoreBf16) {
+        const bool row_ok = row < p.M;
+        for (int c = 0; c < BN / 32; ++c) {
+          float v[32];
+          tmem_ld_32cols(t_row + c * 32, v);
+          const long long col0 = static_cast<long long>(n_blk) * BN + c * 32;
+          if (row_ok && col0 < p.N) {
+            __nv_bfloat16* dst = p.C + row * p.ldc + col0;
+            if (col0 + 32 <= p.N && ((reinterpret_cast<uintptr_t>(dst) & 15u) == 0)) {
+              __align__(16) __nv_bfloat162 pk[16];
+#pragma unroll
+              for (int j = 0; j < 16; ++j) pk[j] = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
+#pragma unroll
+              for (int j = 0; j < 4; ++j) reinterpret_cast<uint4*>(dst)[j] = reinterpret_cast<const uint4*>(pk)[j];
+            } else {
+              for (int j = 0; j < 32 && col0 + j < p.N; ++j) dst[j] = __float2bfloat16_rn(v[j]);
+            }
+          }
+        }
+      } else {
+        float g[kMaxCandidates];
+#pragma unroll
+        for (int k = 0; k < kMaxCandidates; ++k) g[k] = 0.f;
+        const bool row_ok = row < p.M;
+        const long long unit = row * p.units_per_row + n_blk;
+        for (int c = 0; c < BN / 32; ++c) {
+          float v[32];
+          tmem_ld_32cols(t_row + c * 32, v);
+          const long long col0 = static_cast<long long>(n_blk) * BN + c * 32;
+          if (!row_ok || col0 >= p.cols) continue;
+          const bool full = col0 + 32 <= p.cols;
+          for (int k = 0; k < p.cands.K; ++k) {
+            const uint8_t* u = p.cands.ptr[k] + unit * p.cands.ubytes[k];
+            float s = 0.f;
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              float w[8];
+              dec8(p.cands.fmt[k], u, 4 * c + q, w);
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                if (full || col0 + 8 * q + j < p.cols) s = fmaf(v[8 * q + j], w[j], s);
+              }
+            }
+            g[k] += s;
+          }
+        }
+        // fixed-order reduction: warp butterfly; each epilogue warp writes its
+        // own partial (no cross-warp synchronisation inside the epilogue)
+        const long long slot = (static_cast<long long>(m_blk) * p.num_n_blk + n_blk) * 4 + wq;
+        for (int k = 0; k < p.cands.K; ++k) {
+          float s = g[k];
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+          if (lane == 0) p.partials[slot * p.cands.K + k] = s;
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(tempty_bar(acc));
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+// grad_p[k] = sum over slots (in slot order) of partials[slot][k], in fp64;
+// a slot is one (tile, epilogue warp) pair.
+__global__ void gategrad_reduce_kernel(const float* __restrict__ partials, int num_tiles, int K,
+                                       float* __restrict__ grad_p) {
+  __shared__ double sh[256];
+  for (int k = 0; k < K; ++k) {
+    double s = 0.0;
+    for (int t = threadIdx.x; t < num_tiles; t += blockDim.x) s += static_cast<double>(partials[static_cast<long long>(t) * K + k]);
+    sh[threadIdx.x] = s;
+    __syncthreads();
+    for (int w = blockDim.x / 2; w > 0; w >>= 1) {
+      if (threadIdx.x < w) sh[threadIdx.x] += sh[threadIdx.x + w];
+      __syncthreads();
+    }
+    if (threadIdx.x == 0) grad_p[k] = static_cast<float>(sh[0]);
+    __syncthreads();
+  }
+}
+
+}  // namespace gemm
+}  // namespace vq

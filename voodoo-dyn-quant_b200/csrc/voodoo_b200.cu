@@ -1,0 +1,414 @@
+// libvoodoo_b200: C-ABI entry points of the B200-native gated-candidate
+// training step.  Declarations and the reference interface each one replaces
+// are in include/voodoo_b200.h.  Conventions:
+//   * every pointer argument is device memory unless documented otherwise;
+//   * `stream` is a cudaStream_t (nullptr = legacy default stream);
+//   * return 0 on success, a negative VQ_ERR_* code otherwise, with a message
+//     available from vq_last_error() (thread-local);
+//   * calls are asynchronous, never synchronise (except vq_device_error) and
+//     never allocate: workspaces are passed in by the caller.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+
+#include "common.cuh"
+#include "formats.cuh"
+#include "decode_mix.cuh"
+#include "gemm_tc.cuh"
+#include "loss.cuh"
+#include "../../include/voodoo_b200.h"
+
+namespace {
+
+thread_local char g_msg[512] = "ok";
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_msg, sizeof(g_msg), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(VQ_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+#define VQ_CUDA(call)                                   \
+  do {                                                  \
+    cudaError_t e_ = (call);                            \
+    if (e_ != cudaSuccess) return cuda_fail(e_, #call); \
+  } while (0)
+
+__device__ int g_device_error;
+
+int device_error_ptr(int** p) {
+  VQ_CUDA(cudaGetSymbolAddress(reinterpret_cast<void**>(p), g_device_error));
+  return 0;
+}
+
+int sm_count(int* n) {
+  int dev = 0;
+  VQ_CUDA(cudaGetDevice(&dev));
+  VQ_CUDA(cudaDeviceGetAttribute(n, cudaDevAttrMultiProcessorCount, dev));
+  return 0;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (fn == nullptr) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+// Row-major bf16 matrix [rows][cols] with leading dimension ld (elements);
+// TMA box = 64 columns (one 128-byte swizzle row) x box_rows rows.
+int make_map(CUtensorMap* m, const void* base, long long rows, long long cols, long long ld, int box_rows) {
+  auto fn = encode_fn();
+  if (fn == nullptr) return fail(VQ_ERR_CUDA, "cuTensorMapEncodeTiled unavailable from the driver");
+  if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0)
+    return fail(VQ_ERR_INVALID, "matrix base pointer must be 16-byte aligned");
+  if ((ld * 2) % 16 != 0) return fail(VQ_ERR_INVALID, "leading dimension %lld must be a multiple of 8 elements", ld);
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld * 2)};
+  cuuint32_t box[2] = {64u, static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1u, 1u};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(VQ_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
+  return 0;
+}
+
+bool known_format(int f) { return vq::unit_bytes(f) > 0; }
+
+int build_candset(vq::CandSet* cs, int K, const int* types, const void* const* blocks) {
+  if (K < 1 || K > vq::kMaxCandidates) return fail(VQ_ERR_INVALID, "number of candidates %d not in [1, %d]", K, vq::kMaxCandidates);
+  if (types == nullptr || blocks == nullptr) return fail(VQ_ERR_INVALID, "null candidate type/pointer array");
+  std::memset(cs, 0, sizeof(*cs));
+  cs->K = K;
+  for (int k = 0; k < K; ++k) {
+    if (!known_format(types[k])) return fail(VQ_ERR_UNSUPPORTED, "unsupported ggml type %d for candidate %d", types[k], k);
+    if (blocks[k] == nullptr) return fail(VQ_ERR_INVALID, "null block pointer for candidate %d", k);
+    if ((reinterpret_cast<uintptr_t>(blocks[k]) & 1u) != 0)
+      return fail(VQ_ERR_INVALID, "candidate %d blocks must be 2-byte aligned", k);
+    cs->fmt[k] = types[k];
+    cs->ubytes[k] = vq::unit_bytes(types[k]);
+    cs->ptr[k] = static_cast<const uint8_t*>(blocks[k]);
+  }
+  return 0;
+}
+
+template <bool kAmn, bool kBmn, int kEpi>
+int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, vq::gemm::Params p, cudaStream_t st) {
+  using namespace vq::gemm;
+  p.num_m_blk = (p.M + BM - 1) / BM;
+  p.num_n_blk = (p.N + BN - 1) / BN;
+  p.num_k_blk = (p.K + BK - 1) / BK;
+  p.num_tiles = p.num_m_blk * p.num_n_blk;
+  int sms = 0;
+  if (int rc = sm_count(&sms)) return rc;
+  auto kern = gemm_kernel<kAmn, kBmn, kEpi>;
+  VQ_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SmemLayout::alloc));
+  const int grid = p.num_tiles < sms ? p.num_tiles : sms;
+  kern<<<grid, THREADS, SmemLayout::alloc, st>>>(ta, tb, p);
+  VQ_CUDA(cudaGetLastError());
+  return 0;
+}
+
+int check_matrix(const void* p, long long rows, long long cols, long long ld, const char* name) {
+  if (rows < 0 || cols < 0) return fail(VQ_ERR_INVALID, "%s: negative shape", name);
+  if (ld < cols) return fail(VQ_ERR_INVALID, "%s: leading dimension %lld < columns %lld", name, ld, cols);
+  if (rows > 0 && cols > 0 && p == nullptr) return fail(VQ_ERR_INVALID, "%s: null pointer", name);
+  return 0;
+}
+
+int zero_rows(void* p, long long rows, long long cols, long long ld, size_t elem, cudaStream_t st) {
+  if (rows == 0 || cols == 0) return 0;
+  VQ_CUDA(cudaMemset2DAsync(p, ld * elem, 0, cols * elem, rows, st));
+  return 0;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* vq_last_error(void) { return g_msg; }
+
+int vq_abi_version(void) { return VQ_ABI_VERSION; }
+
+int vq_format_info(int ggml_type, int* block_elems, int* block_bytes) {
+  if (!known_format(ggml_type)) return fail(VQ_ERR_UNSUPPORTED, "unsupported ggml type %d", ggml_type);
+  if (block_elems) *block_elems = vq::block_elems(ggml_type);
+  if (block_bytes) *block_bytes = vq::block_bytes(ggml_type);
+  return 0;
+}
+
+int vq_device_error(void* stream, int* code) {
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int* dp = nullptr;
+  if (int rc = device_error_ptr(&dp)) return rc;
+  int h = 0;
+  VQ_CUDA(cudaMemcpyAsync(&h, dp, sizeof(int), cudaMemcpyDeviceToHost, st));
+  VQ_CUDA(cudaStreamSynchronize(st));
+  VQ_CUDA(cudaMemsetAsync(dp, 0, sizeof(int), st));
+  VQ_CUDA(cudaStreamSynchronize(st));
+  if (code) *code = h;
+  return 0;
+}
+
+int vq_dequant(int ggml_type, const void* blocks, int64_t rows, int64_t cols, float* out, void* stream) {
+  if (!known_format(ggml_type)) return fail(VQ_ERR_UNSUPPORTED, "unsupported ggml type %d", ggml_type);
+  const int bs = vq::block_elems(ggml_type);
+  if (rows < 0 || cols < 0) return fail(VQ_ERR_INVALID, "negative shape");
+  if (cols % bs != 0) return fail(VQ_ERR_INVALID, "requires in_features %% %d == 0, got %lld", bs, (long long)cols);
+  const long long total = static_cast<long long>(rows) * cols;
+  if (total == 0) return 0;
+  if (blocks == nullptr || out == nullptr) return fail(VQ_ERR_INVALID, "null pointer");
+  vq::CandSet cs;
+  const void* bl[1] = {blocks};
+  if (int rc = build_candset(&cs, 1, &ggml_type, bl)) return rc;
+  int* err = nullptr;
+  if (int rc = device_error_ptr(&err)) return rc;
+  const long long units = (total + 255) / 256;
+  const long long grid = (units + vq::kUnitsPerCta - 1) / vq::kUnitsPerCta;
+  if (grid > 0x7fffffffLL) return fail(VQ_ERR_INVALID, "tensor too large");
+  vq::decode_units_kernel<false, float><<<static_cast<unsigned>(grid), vq::kDecodeThreads, vq::decode_smem_bytes(cs),
+                                          static_cast<cudaStream_t>(stream)>>>(cs, nullptr, total, 1, total, out,
+                                                                               total, err);
+  VQ_CUDA(cudaGetLastError());
+  return 0;
+}
+
+int vq_mix(int K, const int* types, const void* const* blocks, const float* probs, int64_t rows, int64_t padded_cols,
+           int64_t cols, void* w_bf16, int64_t ldw, void* stream) {
+  vq::CandSet cs;
+  if (int rc = build_candset(&cs, K, types, blocks)) return rc;
+  if (rows < 0 || cols < 0 || padded_cols < cols) return fail(VQ_ERR_INVALID, "invalid shape");
+  if (padded_cols % 256 != 0) return fail(VQ_ERR_INVALID, "padded in_features %lld must be a multiple of 256", (long long)padded_cols);
+  if (ldw < cols || ldw > padded_cols) return fail(VQ_ERR_INVALID, "ldw %lld must be in [cols, padded_cols]", (long long)ldw);
+  if (rows == 0 || padded_cols == 0) return 0;
+  if (probs == nullptr || w_bf16 == nullptr) return fail(VQ_ERR_INVALID, "null pointer");
+  int* err = nullptr;
+  if (int rc = device_error_ptr(&err)) return rc;
+  const long long total = static_cast<long long>(rows) * padded_cols;
+  const long long units = total / 256;
+  const long long grid = (units + vq::kUnitsPerCta - 1) / vq::kUnitsPerCta;
+  if (grid > 0x7fffffffLL) return fail(VQ_ERR_INVALID, "tensor too large");
+  vq::decode_units_kernel<true, __nv_bfloat16>
+      <<<static_cast<unsigned>(grid), vq::kDecodeThreads, vq::decode_smem_bytes(cs), static_cast<cudaStream_t>(stream)>>>(
+          cs, probs, total, static_cast<int>(padded_cols / 256), cols, static_cast<__nv_bfloat16*>(w_bf16), ldw, err);
+  VQ_CUDA(cudaGetLastError());
+  return 0;
+}
+
+int vq_linear_fwd(const void* x, int64_t T, int64_t Kin, int64_t ldx, const void* w, int64_t N, int64_t ldw, void* y,
+                  int64_t ldy, void* stream) {
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (int rc = check_matrix(x, T, Kin, ldx, "x")) return rc;
+  if (int rc = check_matrix(w, N, Kin, ldw, "w")) return rc;
+  if (int rc = check_matrix(y, T, N, ldy, "y")) return rc;
+  if (T == 0 || N == 0) return 0;
+  if (Kin == 0) return zero_rows(y, T, N, ldy, 2, st);
+  if (T > 0x7fffffff || N > 0x7fffffff || Kin > 0x7fffffff) return fail(VQ_ERR_INVALID, "dimension too large");
+  CUtensorMap ta, tb;
+  if (int rc = make_map(&ta, x, T, Kin, ldx, vq::gemm::BM)) return rc;
+  if (int rc = make_map(&tb, w, N, Kin, ldw, vq::gemm::BN)) return rc;
+  vq::gemm::Params p{};
+  p.M = static_cast<int>(T);
+  p.N = static_cast<int>(N);
+  p.K = static_cast<int>(Kin);
+  p.C = static_cast<__nv_bfloat16*>(y);
+  p.ldc = ldy;
+  if (int rc = device_error_ptr(&p.err)) return rc;
+  return launch_gemm<false, false, vq::gemm::kEpiStoreBf16>(ta, tb, p, st);
+}
+
+int vq_linear_dx(const void* dy, int64_t T, int64_t N, int64_t lddy, const void* w, int64_t Kin, int64_t ldw, void* dx,
+                 int64_t lddx, void* stream) {
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (int rc = check_matrix(dy, T, N, lddy, "dy")) return rc;
+  if (int rc = check_matrix(w, N, Kin, ldw, "w")) return rc;
+  if (int rc = check_matrix(dx, T, Kin, lddx, "dx")) return rc;
+  if (T == 0 || Kin == 0) return 0;
+  if (N == 0) return zero_rows(dx, T, Kin, lddx, 2, st);
+  if (T > 0x7fffffff || N > 0x7fffffff || Kin > 0x7fffffff) return fail(VQ_ERR_INVALID, "dimension too large");
+  CUtensorMap ta, tb;
+  if (int rc = make_map(&ta, dy, T, N, lddy, vq::gemm::BM)) return rc;
+  if (int rc = make_map(&tb, w, N, Kin, ldw, 64)) return rc;
+  vq::gemm::Params p{};
+  p.M = static_cast<int>(T);
+  p.N = static_cast<int>(Kin);
+  p.K = static_cast<int>(N);
+  p.C = static_cast<__nv_bfloat16*>(dx);
+  p.ldc = lddx;
+  if (int rc = device_error_ptr(&p.err)) return rc;
+  return launch_gemm<false, true, vq::gemm::kEpiStoreBf16>(ta, tb, p, st);
+}
+
+size_t vq_gategrad_workspace_bytes(int64_t N, int64_t Kin, int K) {
+  if (N <= 0 || Kin <= 0 || K <= 0) return 0;
+  const long long tiles = ((N + vq::gemm::BM - 1) / vq::gemm::BM) * ((Kin + vq::gemm::BN - 1) / vq::gemm::BN);
+  return static_cast<size_t>(tiles) * 4 * K * sizeof(float);
+}
+
+int vq_gategrad(const void* dy, int64_t lddy, const void* x, int64_t ldx, int64_t T, int64_t N, int64_t Kin, int K,
+                const int* types, const void* const* blocks, int64_t padded_cols, void* workspace,
+                size_t workspace_bytes, float* grad_probs, void* stream) {
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  vq::CandSet cs;
+  if (int rc = build_candset(&cs, K, types, blocks)) return rc;
+  if (int rc = check_matrix(dy, T, N, lddy, "dy")) return rc;
+  if (int rc = check_matrix(x, T, Kin, ldx, "x")) return rc;
+  if (grad_probs == nullptr) return fail(VQ_ERR_INVALID, "null grad_probs");
+  if (padded_cols < Kin || padded_cols % 256 != 0)
+    return fail(VQ_ERR_INVALID, "padded in_features %lld must be a multiple of 256 and >= %lld", (long long)padded_cols,
+                (long long)Kin);
+  if (T == 0 || N == 0 || Kin == 0) {
+    VQ_CUDA(cudaMemsetAsync(grad_probs, 0, sizeof(float) * K, st));
+    return 0;
+  }
+  if (T > 0x7fffffff || N > 0x7fffffff || Kin > 0x7fffffff) return fail(VQ_ERR_INVALID, "dimension too large");
+  const size_t need = vq_gategrad_workspace_bytes(N, Kin, K);
+  if (workspace == nullptr || workspace_bytes < need)
+    return fail(VQ_ERR_INVALID, "gate-grad workspace of %zu bytes required, got %zu", need, workspace_bytes);
+  CUtensorMap ta, tb;
+  if (int rc = make_map(&ta, dy, T, N, lddy, 64)) return rc;
+  if (int rc = make_map(&tb, x, T, Kin, ldx, 64)) return rc;
+  vq::gemm::Params p{};
+  p.M = static_cast<int>(N);
+  p.N = static_cast<int>(Kin);
+  p.K = static_cast<int>(T);
+  p.cands = cs;
+  p.units_per_row = static_cast<int>(padded_cols / 256);
+  p.cols = Kin;
+  p.partials = static_cast<float*>(workspace);
+  if (int rc = device_error_ptr(&p.err)) return rc;
+  if (int rc = launch_gemm<true, true, vq::gemm::kEpiGateGrad>(ta, tb, p, st)) return rc;
+  const int slots = static_cast<int>(need / (sizeof(float) * K));
+  vq::gemm::gategrad_reduce_kernel<<<1, 256, 0, st>>>(p.partials, slots, K, grad_probs);
+  VQ_CUDA(cudaGetLastError());
+  return 0;
+}
+
+int vq_mixgemm_fwd(const void* x, int64_t T, int64_t Kin, int64_t ldx, int K, const int* types,
+                   const void* const* blocks, const float* probs, int64_t N, int64_t padded_cols, void* w_mix,
+                   int64_t ldw, void* y, int64_t ldy, void* stream) {
+  if (int rc = vq_mix(K, types, blocks, probs, N, padded_cols, Kin, w_mix, ldw, stream)) return rc;
+  return vq_linear_fwd(x, T, Kin, ldx, w_mix, N, ldw, y, ldy, stream);
+}
+
+int vq_loss_fused(const void* s_logits, int64_t lds, const void* t_logits, int64_t ldt, const int64_t* targets,
+                  int64_t rows, int64_t V, float temperature, float ce_weight, float kl_weight, float* row_ce,
+                  float* row_kl, void* dlogits, int64_t ldg, void* stream) {
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (int rc = check_matrix(s_logits, rows, V, lds, "student logits")) return rc;
+  if (int rc = check_matrix(t_logits, rows, V, ldt, "teacher logits")) return rc;
+  if (dlogits != nullptr) {
+    if (int rc = check_matrix(dlogits, rows, V, ldg, "dlogits")) return rc;
+  }
+  if (!(temperature > 0.f)) return fail(VQ_ERR_INVALID, "temperature must be > 0");
+  if (rows == 0) return 0;
+  if (V <= 0 || V > 0x7fffffff || rows > 0x7fffffff) return fail(VQ_ERR_INVALID, "invalid vocabulary size");
+  if (targets == nullptr || row_ce == nullptr || row_kl == nullptr) return fail(VQ_ERR_INVALID, "null pointer");
+  int sms = 0;
+  if (int rc = sm_count(&sms)) return rc;
+  const int grid = static_cast<int>(rows < sms ? rows : sms);
+  const bool vec = ((reinterpret_cast<uintptr_t>(s_logits) | reinterpret_cast<uintptr_t>(t_logits) |
+                     reinterpret_cast<uintptr_t>(dlogits)) & 15u) == 0 &&
+                   lds % 8 == 0 && ldt % 8 == 0 && (dlogits == nullptr || ldg % 8 == 0);
+  const auto* S = static_cast<const __nv_bfloat16*>(s_logits);
+  const auto* Tl = static_cast<const __nv_bfloat16*>(t_logits);
+  auto* G = static_cast<__nv_bfloat16*>(dlogits);
+  const auto* y = reinterpret_cast<const long long*>(targets);
+  if (temperature == 1.0f)
+    vq::loss::loss_fused_kernel<true><<<grid, vq::loss::THREADS, 0, st>>>(S, lds, Tl, ldt, y, (int)rows, (int)V, temperature,
+                                                                          ce_weight, kl_weight, row_ce, row_kl, G, ldg, vec);
+  else
+    vq::loss::loss_fused_kernel<false><<<grid, vq::loss::THREADS, 0, st>>>(S, lds, Tl, ldt, y, (int)rows, (int)V, temperature,
+                                                                           ce_weight, kl_weight, row_ce, row_kl, G, ldg, vec);
+  VQ_CUDA(cudaGetLastError());
+  return 0;
+}
+
+int vq_loss_stats(const void* s_logits, int64_t lds, const void* t_logits, int64_t ldt, const int64_t* targets,
+                  int64_t vocab_start, int64_t rows, int64_t V, float temperature, float* stats, void* stream) {
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (int rc = check_matrix(s_logits, rows, V, lds, "student logits")) return rc;
+  if (int rc = check_matrix(t_logits, rows, V, ldt, "teacher logits")) return rc;
+  if (!(temperature > 0.f)) return fail(VQ_ERR_INVALID, "temperature must be > 0");
+  if (rows == 0) return 0;
+  if (V <= 0 || V > 0x7fffffff || rows > 0x7fffffff) return fail(VQ_ERR_INVALID, "invalid vocabulary size");
+  if (targets == nullptr || stats == nullptr) return fail(VQ_ERR_INVALID, "null pointer");
+  int sms = 0;
+  if (int rc = sm_count(&sms)) return rc;
+  const int grid = static_cast<int>(rows < sms ? rows : sms);
+  const bool vec = ((reinterpret_cast<uintptr_t>(s_logits) | reinterpret_cast<uintptr_t>(t_logits)) & 15u) == 0 &&
+                   lds % 8 == 0 && ldt % 8 == 0;
+  const auto* S = static_cast<const __nv_bfloat16*>(s_logits);
+  const auto* Tl = static_cast<const __nv_bfloat16*>(t_logits);
+  const auto* y = reinterpret_cast<const long long*>(targets);
+  if (temperature == 1.0f)
+    vq::loss::loss_stats_kernel<true><<<grid, vq::loss::THREADS, 0, st>>>(S, lds, Tl, ldt, y, vocab_start, (int)rows,
+                                                                          (int)V, temperature, stats, vec);
+  else
+    vq::loss::loss_stats_kernel<false><<<grid, vq::loss::THREADS, 0, st>>>(S, lds, Tl, ldt, y, vocab_start, (int)rows,
+                                                                           (int)V, temperature, stats, vec);
+  VQ_CUDA(cudaGetLastError());
+  return 0;
+}
+
+int vq_loss_combine(const float* stats, int ranks, int64_t rows, float temperature, float* row_lse, float* row_ce,
+                    float* row_kl, void* stream) {
+  if (ranks < 1) return fail(VQ_ERR_INVALID, "ranks must be >= 1");
+  if (rows < 0 || rows > 0x7fffffff) return fail(VQ_ERR_INVALID, "invalid row count");
+  if (rows == 0) return 0;
+  if (!stats || !row_lse || !row_ce || !row_kl) return fail(VQ_ERR_INVALID, "null pointer");
+  const int threads = 256;
+  const int grid = static_cast<int>((rows + threads - 1) / threads);
+  vq::loss::loss_combine_kernel<<<grid, threads, 0, static_cast<cudaStream_t>(stream)>>>(stats, ranks, (int)rows, temperature,
+                                                                                      row_lse, row_ce, row_kl);
+  VQ_CUDA(cudaGetLastError());
+  return 0;
+}
+
+int vq_loss_grad(const void* s_logits, int64_t lds, const void* t_logits, int64_t ldt, const int64_t* targets,
+                 int64_t vocab_start, int64_t rows, int64_t V, float temperature, const float* row_lse,
+                 float ce_weight, float kl_weight, void* dlogits, int64_t ldg, void* stream) {
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (int rc = check_matrix(s_logits, rows, V, lds, "student logits")) return rc;
+  if (int rc = check_matrix(t_logits, rows, V, ldt, "teacher logits")) return rc;
+  if (int rc = check_matrix(dlogits, rows, V, ldg, "dlogits")) return rc;
+  if (!(temperature > 0.f)) return fail(VQ_ERR_INVALID, "temperature must be > 0");
+  if (rows == 0) return 0;
+  if (V <= 0 || V > 0x7fffffff || rows > 0x7fffffff) return fail(VQ_ERR_INVALID, "invalid vocabulary size");
+  if (targets == nullptr || row_lse == nullptr) return fail(VQ_ERR_INVALID, "null pointer");
+  int sms = 0;
+  if (int rc = sm_count(&sms)) return rc;
+  const int grid = static_cast<int>(rows < sms ? rows : sms);
+  const bool vec = ((reinterpret_cast<uintptr_t>(s_logits) | reinterpret_cast<uintptr_t>(t_logits) |
+                     reinterpret_cast<uintptr_t>(dlogits)) & 15u) == 0 &&
+                   lds % 8 == 0 && ldt % 8 == 0 && ldg % 8 == 0;
+  const auto* S = static_cast<const __nv_bfloat16*>(s_logits);
+  const auto* Tl = static_cast<const __nv_bfloat16*>(t_logits);
+  auto* G = static_cast<__nv_bfloat16*>(dlogits);
+  const auto* y = reinterpret_cast<const long long*>(targets);
+  if (temperature == 1.0f)
+    vq::loss::loss_grad_kernel<true><<<grid, vq::loss::THREADS, 0, st>>>(S, lds, Tl, ldt, y, vocab_start, (int)rows, (int)V,
+                                                                         temperature, row_lse, ce_weight, kl_weight, G, ldg, vec);
+  else
+    vq::loss::loss_grad_kernel<false><<<grid, vq::loss::THREADS, 0, st>>>(S, lds, Tl, ldt, y, vocab_start, (int)rows, (int)V,
+                                                                          temperature, row_lse, ce_weight, kl_weight, G, ldg, vec);
+  VQ_CUDA(cudaGetLastError());
+  return 0;
+}
+
+}  // extern "C"

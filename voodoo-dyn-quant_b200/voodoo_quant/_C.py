@@ -1,0 +1,288 @@
+"""ctypes binding of libvoodoo_b200.so (the sm_100a kernels) for torch tensors.
+
+The library is loaded from this package directory (built in-tree by
+``__graft_entry__.build()``).  There is no fallback: if the library is
+missing, or CUDA is not available, every entry point raises ``RuntimeError``.
+Status codes of the C ABI map onto the reference's exception conventions:
+invalid shapes / alignment / unknown quant types raise ``ValueError``
+(voodoo_quant/ggml.py:161-164,195-198,242-253 in the reference), CUDA
+failures raise ``RuntimeError``.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+from pathlib import Path
+
+import torch
+
+LIB_NAME = "libvoodoo_b200.so"
+LIB_PATH = Path(__file__).resolve().parent / LIB_NAME
+
+VQ_ERR_INVALID = -1
+VQ_ERR_CUDA = -2
+VQ_ERR_UNSUPPORTED = -3
+
+# ggml type ids of the supported candidate formats.
+GGML_TYPE = {"Q8_0": 8, "Q2_K": 10, "Q3_K": 11, "Q4_K": 12, "Q5_K": 13, "Q6_K": 14, "IQ4_XS": 23}
+
+_lib = None
+
+_i64 = ctypes.c_int64
+_vp = ctypes.c_void_p
+_int = ctypes.c_int
+_f32 = ctypes.c_float
+
+
+def _declare(lib):
+    sig = {
+        "vq_last_error": (ctypes.c_char_p, []),
+        "vq_abi_version": (_int, []),
+        "vq_format_info": (_int, [_int, ctypes.POINTER(_int), ctypes.POINTER(_int)]),
+        "vq_device_error": (_int, [_vp, ctypes.POINTER(_int)]),
+        "vq_dequant": (_int, [_int, _vp, _i64, _i64, _vp, _vp]),
+        "vq_mix": (_int, [_int, _vp, _vp, _vp, _i64, _i64, _i64, _vp, _i64, _vp]),
+        "vq_linear_fwd": (_int, [_vp, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _vp]),
+        "vq_linear_dx": (_int, [_vp, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _vp]),
+        "vq_gategrad_workspace_bytes": (ctypes.c_size_t, [_i64, _i64, _int]),
+        "vq_gategrad": (_int, [_vp, _i64, _vp, _i64, _i64, _i64, _i64, _int, _vp, _vp, _i64, _vp,
+                               ctypes.c_size_t, _vp, _vp]),
+        "vq_mixgemm_fwd": (_int, [_vp, _i64, _i64, _i64, _int, _vp, _vp, _vp, _i64, _i64, _vp, _i64, _vp,
+                                  _i64, _vp]),
+        "vq_loss_fused": (_int, [_vp, _i64, _vp, _i64, _vp, _i64, _i64, _f32, _f32, _f32, _vp, _vp, _vp,
+                                 _i64, _vp]),
+        "vq_loss_stats": (_int, [_vp, _i64, _vp, _i64, _vp, _i64, _i64, _i64, _f32, _vp, _vp]),
+        "vq_loss_combine": (_int, [_vp, _int, _i64, _f32, _vp, _vp, _vp, _vp]),
+        "vq_loss_grad": (_int, [_vp, _i64, _vp, _i64, _vp, _i64, _i64, _i64, _f32, _vp, _f32, _f32, _vp,
+                                _i64, _vp]),
+    }
+    for name, (res, args) in sig.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    return sig.keys()
+
+
+EXPORTED = (
+    "vq_last_error", "vq_abi_version", "vq_format_info", "vq_device_error", "vq_dequant", "vq_mix",
+    "vq_linear_fwd", "vq_linear_dx", "vq_gategrad_workspace_bytes", "vq_gategrad", "vq_mixgemm_fwd",
+    "vq_loss_fused", "vq_loss_stats", "vq_loss_combine", "vq_loss_grad",
+)
+
+
+def load_library(path: str | os.PathLike | None = None):
+    """Load (once) and return the ctypes handle; raises RuntimeError if absent."""
+    global _lib
+    if _lib is not None and path is None:
+        return _lib
+    p = Path(path) if path is not None else LIB_PATH
+    if not p.exists():
+        raise RuntimeError(
+            f"{LIB_NAME} not found at {p}; build it with `python -c 'import __graft_entry__ as g; g.build()'` "
+            "(the B200 path has no CPU fallback)"
+        )
+    lib = ctypes.CDLL(str(p))
+    _declare(lib)
+    if path is None:
+        _lib = lib
+    return lib
+
+
+def _check(rc: int) -> None:
+    if rc == 0:
+        return
+    msg = _lib.vq_last_error().decode(errors="replace")
+    if rc in (VQ_ERR_INVALID, VQ_ERR_UNSUPPORTED):
+        raise ValueError(msg)
+    raise RuntimeError(f"libvoodoo_b200: {msg}")
+
+
+def _stream(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _require_cuda(*ts: torch.Tensor) -> None:
+    load_library()
+    for t in ts:
+        if not t.is_cuda:
+            raise RuntimeError("libvoodoo_b200 kernels need CUDA tensors (no CPU fallback)")
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def format_info(qtype: str) -> tuple[int, int]:
+    lib = load_library()
+    be, bb = _int(), _int()
+    rc = lib.vq_format_info(GGML_TYPE.get(qtype, -1), ctypes.byref(be), ctypes.byref(bb))
+    _check(rc)
+    return be.value, bb.value
+
+
+def device_error(device: torch.device | None = None) -> int:
+    """Synchronise the current stream and return/clear the device error word."""
+    lib = load_library()
+    code = _int()
+    st = torch.cuda.current_stream(device).cuda_stream
+    _check(lib.vq_device_error(st, ctypes.byref(code)))
+    return code.value
+
+
+def dequant(qbytes: torch.Tensor, qtype: str, rows: int, cols: int) -> torch.Tensor:
+    """Bit-exact decode of packed blocks -> float32 [rows, cols] on the blocks' device."""
+    _require_cuda(qbytes)
+    if qtype not in GGML_TYPE:
+        raise ValueError(f"Unknown quant type: {qtype}. Supported: {list(GGML_TYPE)}")
+    be, bb = format_info(qtype)
+    if cols % be:
+        raise ValueError(f"{qtype} requires in_features % {be} == 0, got {cols}")
+    if qbytes.numel() != rows * (cols // be) * bb:
+        raise ValueError(
+            f"qweight size {qbytes.numel()} does not match {rows * (cols // be)} blocks of {bb} bytes for {qtype}"
+        )
+    qb = qbytes.contiguous()
+    out = torch.empty(rows, cols, dtype=torch.float32, device=qb.device)
+    _check(_lib.vq_dequant(GGML_TYPE[qtype], qb.data_ptr(), rows, cols, out.data_ptr(), _stream(qb)))
+    return out
+
+
+def _cand_arrays(qtypes, qbytes):
+    K = len(qtypes)
+    types = (_int * K)(*[GGML_TYPE[q] for q in qtypes])
+    ptrs = (_vp * K)(*[q.data_ptr() for q in qbytes])
+    return K, types, ptrs
+
+
+def mix(qtypes, qbytes, probs: torch.Tensor, rows: int, padded_cols: int, cols: int,
+        out: torch.Tensor | None = None) -> torch.Tensor:
+    """W_mix = sum_k probs[k] W_k -> bf16 [rows, ld] with ld = cols rounded up to 8."""
+    _require_cuda(probs, *qbytes)
+    ld = (cols + 7) // 8 * 8
+    if out is None:
+        out = torch.empty(rows, ld, dtype=torch.bfloat16, device=probs.device)
+    K, types, ptrs = _cand_arrays(qtypes, qbytes)
+    p = probs.detach().to(torch.float32).contiguous()
+    _check(_lib.vq_mix(K, types, ptrs, p.data_ptr(), rows, padded_cols, cols, out.data_ptr(), out.stride(0),
+                       _stream(p)))
+    return out
+
+
+def _as_operand(x: torch.Tensor) -> torch.Tensor:
+    """bf16, unit column stride, leading dimension a multiple of 8, 16B-aligned base."""
+    x = x.to(torch.bfloat16)
+    if x.stride(-1) != 1 or x.stride(0) % 8 != 0 or x.data_ptr() % 16 != 0:
+        cols = x.shape[1]
+        ld = (cols + 7) // 8 * 8
+        buf = torch.zeros(x.shape[0], ld, dtype=torch.bfloat16, device=x.device)
+        buf[:, :cols] = x
+        return buf
+    return x
+
+
+def linear_fwd(x: torch.Tensor, w: torch.Tensor, n_out: int | None = None, in_features: int | None = None,
+               out: torch.Tensor | None = None) -> torch.Tensor:
+    """y[T, N] = x[T, Kin] w[N, Kin]^T in bf16 with fp32 accumulation."""
+    _require_cuda(x, w)
+    kin = x.shape[1] if in_features is None else in_features
+    N = w.shape[0] if n_out is None else n_out
+    x = _as_operand(x)
+    if out is None:
+        out = torch.empty(x.shape[0], N, dtype=torch.bfloat16, device=x.device)
+    _check(_lib.vq_linear_fwd(x.data_ptr(), x.shape[0], kin, x.stride(0), w.data_ptr(), N, w.stride(0),
+                              out.data_ptr(), out.stride(0), _stream(x)))
+    return out
+
+
+def linear_dx(dy: torch.Tensor, w: torch.Tensor, in_features: int, out: torch.Tensor | None = None) -> torch.Tensor:
+    """dx[T, Kin] = dy[T, N] w[N, Kin]."""
+    _require_cuda(dy, w)
+    dy = _as_operand(dy)
+    N = w.shape[0]
+    if out is None:
+        out = torch.empty(dy.shape[0], in_features, dtype=torch.bfloat16, device=dy.device)
+    _check(_lib.vq_linear_dx(dy.data_ptr(), dy.shape[0], N, dy.stride(0), w.data_ptr(), in_features, w.stride(0),
+                             out.data_ptr(), out.stride(0), _stream(dy)))
+    return out
+
+
+def gategrad(dy: torch.Tensor, x: torch.Tensor, qtypes, qbytes, n_out: int, in_features: int, padded_cols: int,
+             workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """grad_probs[k] = <dy^T x, W_k> (float32 [K]); dW is never materialised."""
+    _require_cuda(dy, x, *qbytes)
+    dy = _as_operand(dy)
+    x = _as_operand(x)
+    K, types, ptrs = _cand_arrays(qtypes, qbytes)
+    need = _lib.vq_gategrad_workspace_bytes(n_out, in_features, K)
+    if workspace is None or workspace.numel() * workspace.element_size() < need:
+        workspace = torch.empty(max(need, 4), dtype=torch.uint8, device=x.device)
+    g = torch.empty(K, dtype=torch.float32, device=x.device)
+    _check(_lib.vq_gategrad(dy.data_ptr(), dy.stride(0), x.data_ptr(), x.stride(0), x.shape[0], n_out, in_features,
+                            K, types, ptrs, padded_cols, workspace.data_ptr(), workspace.numel(), g.data_ptr(),
+                            _stream(x)))
+    return g
+
+
+def gategrad_workspace_bytes(n_out: int, in_features: int, K: int) -> int:
+    return int(load_library().vq_gategrad_workspace_bytes(n_out, in_features, K))
+
+
+def loss_fused(s: torch.Tensor, t: torch.Tensor, targets: torch.Tensor, temperature: float, ce_weight: float,
+               kl_weight: float, want_grad: bool = True):
+    """Row CE, row T^2*KL and (optionally) d/ds for bf16 logits [rows, V]."""
+    _require_cuda(s, t, targets)
+    s = s.to(torch.bfloat16)
+    t = t.to(torch.bfloat16)
+    if s.stride(-1) != 1:
+        s = s.contiguous()
+    if t.stride(-1) != 1:
+        t = t.contiguous()
+    y = targets.to(torch.int64).contiguous()
+    rows, V = s.shape
+    ce = torch.empty(rows, dtype=torch.float32, device=s.device)
+    kl = torch.empty(rows, dtype=torch.float32, device=s.device)
+    g = torch.empty(rows, V, dtype=torch.bfloat16, device=s.device) if want_grad else None
+    _check(_lib.vq_loss_fused(s.data_ptr(), s.stride(0), t.data_ptr(), t.stride(0), y.data_ptr(), rows, V,
+                              float(temperature), float(ce_weight), float(kl_weight), ce.data_ptr(), kl.data_ptr(),
+                              _ptr(g), g.stride(0) if g is not None else V, _stream(s)))
+    return ce, kl, g
+
+
+def loss_stats(s: torch.Tensor, t: torch.Tensor, targets: torch.Tensor, vocab_start: int, temperature: float):
+    _require_cuda(s, t, targets)
+    s = s.to(torch.bfloat16)
+    t = t.to(torch.bfloat16)
+    y = targets.to(torch.int64).contiguous()
+    rows, V = s.shape
+    st = torch.empty(rows, 8, dtype=torch.float32, device=s.device)
+    _check(_lib.vq_loss_stats(s.data_ptr(), s.stride(0), t.data_ptr(), t.stride(0), y.data_ptr(), vocab_start, rows,
+                              V, float(temperature), st.data_ptr(), _stream(s)))
+    return st
+
+
+def loss_combine(stats: torch.Tensor, temperature: float):
+    """stats [R, rows, 8] -> (row_lse [rows, 4], row_ce [rows], row_kl [rows])."""
+    _require_cuda(stats)
+    stats = stats.to(torch.float32).contiguous()
+    R, rows = stats.shape[0], stats.shape[1]
+    lse = torch.empty(rows, 4, dtype=torch.float32, device=stats.device)
+    ce = torch.empty(rows, dtype=torch.float32, device=stats.device)
+    kl = torch.empty(rows, dtype=torch.float32, device=stats.device)
+    _check(_lib.vq_loss_combine(stats.data_ptr(), R, rows, float(temperature), lse.data_ptr(), ce.data_ptr(),
+                                kl.data_ptr(), _stream(stats)))
+    return lse, ce, kl
+
+
+def loss_grad(s: torch.Tensor, t: torch.Tensor, targets: torch.Tensor, vocab_start: int, temperature: float,
+              row_lse: torch.Tensor, ce_weight: float, kl_weight: float) -> torch.Tensor:
+    _require_cuda(s, t, targets, row_lse)
+    s = s.to(torch.bfloat16)
+    t = t.to(torch.bfloat16)
+    y = targets.to(torch.int64).contiguous()
+    rows, V = s.shape
+    g = torch.empty(rows, V, dtype=torch.bfloat16, device=s.device)
+    _check(_lib.vq_loss_grad(s.data_ptr(), s.stride(0), t.data_ptr(), t.stride(0), y.data_ptr(), vocab_start, rows,
+                             V, float(temperature), row_lse.contiguous().data_ptr(), float(ce_weight),
+                             float(kl_weight), g.data_ptr(), g.stride(0), _stream(s)))
+    return g

@@ -1,0 +1,565 @@
+"""Gated mixed-quant layers on the B200 kernels (drop-in for voodoo_quant/layers.py).
+
+``MixedQuantLinear`` / ``MixedQuantEmbedding`` keep the reference's
+constructor, methods and attributes (voodoo_quant/layers.py:1640-1842): K
+learnable gates, p = softmax(gates / tau), an effective weight
+W_mix = sum_k p_k W_k over K packed GGUF candidates, and argmax hard
+assignment after training.  What changes is where the work happens:
+
+* The K candidates stay packed (GGUF blocks) in one HBM arena per tensor
+  (``voodoo_quant.cache.pack_arena``); nothing dequantised is stored.
+* Forward: ``vq_mix`` decodes the K candidates bit-exactly and writes W_mix
+  once (bf16), ``vq_linear_fwd`` runs the tcgen05 GEMM.
+* Backward: ``vq_linear_dx`` reuses W_mix for dX; ``vq_gategrad`` computes
+  g_k = <dY^T X, W_k> in the dW GEMM's epilogue without materialising dW.
+  Autograd then applies the softmax Jacobian to reach the gates, exactly as
+  in the reference (``_MixedWeightFunction.backward``, :355-363).
+
+The candidate cache on disk keeps the reference format and paths
+(``_combined_cache_path``, ``_tensor_hash``, :884-943): a ``combined_lazy``
+file holding {qtype: uint8 [nblocks, block_bytes]} per tensor.  Missing
+candidates are quantised by libggml as in the reference (:1282-1340).
+"""
+
+from __future__ import annotations
+
+import hashlib
+import os
+from pathlib import Path
+from typing import Optional
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+from torch.autograd import Function
+
+import voodoo_quant
+from voodoo_quant import _C
+from voodoo_quant.cache import STORE, arena_views, pack_arena
+from voodoo_quant.ggml import GPU_FORMATS, bytes_per_weight, get_quant_info, quantize_tensor
+
+CANDIDATE_CACHE_DIR = Path(voodoo_quant.__file__).resolve().parent.parent / ".cache" / "mixed_quant_candidates"
+_CANDIDATE_CACHE_ROOT = CANDIDATE_CACHE_DIR
+
+# Keep W_mix from the forward for the backward's dX (one bf16 [out, in] per
+# layer).  False recomputes it in the backward (one more HBM-bound mix pass).
+KEEP_MIXED_WEIGHT = True
+
+
+# --------------------------------------------------------------------------- cache helpers
+def _tensor_hash(t: torch.Tensor | None) -> str:
+    """SHA-256 (first 16 hex) of the tensor's float32 bytes, streamed in 4M-element chunks.
+
+    Same key as the reference (voodoo_quant/layers.py:884-908) so an existing
+    candidate cache is found.
+    """
+    if t is None:
+        return "none"
+    flat = t.detach().contiguous().cpu().reshape(-1)
+    h = hashlib.sha256()
+    ch = 1 << 22
+    for i in range(0, flat.numel(), ch):
+        h.update(flat[i:i + ch].to(torch.float32).numpy().tobytes())
+    return h.hexdigest()[:16]
+
+
+def _safe_name(tensor_name: str) -> str:
+    return tensor_name.replace(".", "_").replace("/", "_")
+
+
+def _candidate_cache_path(tensor_name: str, candidate_type: str, mode: str, weight_hash: str,
+                          imatrix_hash: str) -> Path:
+    d = _CANDIDATE_CACHE_ROOT / _safe_name(tensor_name)
+    d.mkdir(parents=True, exist_ok=True)
+    return d / f"{candidate_type}_{mode}_w{weight_hash}_i{imatrix_hash}.pt"
+
+
+def _combined_cache_path(tensor_name: str, mode: str, weight_hash: str, imatrix_hash: str) -> Path:
+    d = _CANDIDATE_CACHE_ROOT / _safe_name(tensor_name)
+    d.mkdir(parents=True, exist_ok=True)
+    return d / f"combined_{mode}_w{weight_hash}_i{imatrix_hash}.pt"
+
+
+def _atomic_torch_save(obj, path: Path) -> None:
+    tmp = path.with_suffix(path.suffix + f".tmp{os.getpid()}")
+    torch.save(obj, tmp)
+    os.replace(tmp, path)
+
+
+def _pad_weight_and_imatrix(weight: torch.Tensor, imatrix: torch.Tensor | None):
+    """Zero-pad in_features to a multiple of 256 (imatrix padded with 1.0)."""
+    orig_in = weight.shape[1]
+    if orig_in % 256 == 0:
+        return weight, imatrix, orig_in
+    pad = 256 - orig_in % 256
+    padded = F.pad(weight, (0, pad), "constant", 0)
+    pim = None
+    if imatrix is not None:
+        pim = F.pad(imatrix.to(torch.float32).contiguous(), (0, pad), "constant", 1.0)
+    return padded, pim, orig_in
+
+
+pad_weight_and_imatrix = _pad_weight_and_imatrix
+
+
+def _padded(n: int) -> int:
+    return (n + 255) // 256 * 256
+
+
+# --------------------------------------------------------------------------- autograd functions
+class _GatedLinearFunction(Function):
+    """y = x W_mix^T with W_mix = sum_k p_k W_k; gradients for x and p."""
+
+    @staticmethod
+    def forward(ctx, x: torch.Tensor, probs: torch.Tensor, layer: "MixedQuantLinear"):
+        in_f, out_f = layer.in_features, layer.out_features
+        x2 = _C._as_operand(x.reshape(-1, in_f))
+        w_mix = layer._mix(probs)
+        y = _C.linear_fwd(x2, w_mix, out_f, in_f)
+        ctx.layer = layer
+        ctx.x_shape = x.shape
+        ctx.x_dtype = x.dtype
+        ctx.save_for_backward(x2, probs)
+        ctx.w_mix = w_mix if KEEP_MIXED_WEIGHT else None
+        return y.to(x.dtype).reshape(*x.shape[:-1], out_f)
+
+    @staticmethod
+    def backward(ctx, dy: torch.Tensor):
+        layer = ctx.layer
+        x2, probs = ctx.saved_tensors
+        dy2 = _C._as_operand(dy.reshape(-1, layer.out_features))
+        dx = dprobs = None
+        if ctx.needs_input_grad[0]:
+            w_mix = ctx.w_mix if ctx.w_mix is not None else layer._mix(probs)
+            dx = _C.linear_dx(dy2, w_mix, layer.in_features).to(ctx.x_dtype).reshape(ctx.x_shape)
+        ctx.w_mix = None
+        if ctx.needs_input_grad[1]:
+            dprobs = _C.gategrad(dy2, x2, layer.candidate_types, layer._candidate_blocks(), layer.out_features,
+                                 layer.in_features, layer.padded_in_features,
+                                 workspace=layer._gategrad_workspace(x2.device)).to(probs.dtype)
+        return dx, dprobs, None
+
+
+class _MixedWeightFunction(Function):
+    """W_mix as a tensor (get_mixed_weight); backward g_k = <G, W_k>."""
+
+    @staticmethod
+    def forward(ctx, probs: torch.Tensor, layer: "_MixedQuantBase"):
+        ctx.layer = layer
+        w = layer._mix(probs)
+        return w[:, :layer.in_features].to(layer.source_dtype)
+
+    @staticmethod
+    def backward(ctx, g: torch.Tensor):
+        layer = ctx.layer
+        gf = g.to(torch.float32)
+        out = torch.empty(layer.num_candidates, dtype=torch.float32, device=g.device)
+        for k, (qt, qb) in enumerate(zip(layer.candidate_types, layer._candidate_blocks())):
+            w = _C.dequant(qb, qt, layer.out_features, layer.padded_in_features)[:, :layer.in_features]
+            out[k] = (gf * w).sum()
+        return out, None
+
+
+class _GatedEmbeddingRowsFunction(Function):
+    """Mixed rows of a vocabulary-scale embedding; only the touched rows are decoded."""
+
+    @staticmethod
+    def forward(ctx, probs: torch.Tensor, rows: torch.Tensor, layer: "MixedQuantEmbedding"):
+        blocks = layer._row_blocks(rows)
+        w = _C.mix(layer.candidate_types, blocks, probs, rows.numel(), layer.padded_in_features,
+                   layer.embedding_dim)
+        ctx.layer = layer
+        ctx.save_for_backward(rows)
+        return w[:, :layer.embedding_dim].to(layer.source_dtype)
+
+    @staticmethod
+    def backward(ctx, g: torch.Tensor):
+        layer = ctx.layer
+        (rows,) = ctx.saved_tensors
+        gf = g.to(torch.float32)
+        blocks = layer._row_blocks(rows)
+        out = torch.empty(layer.num_candidates, dtype=torch.float32, device=g.device)
+        for k, (qt, qb) in enumerate(zip(layer.candidate_types, blocks)):
+            w = _C.dequant(qb, qt, rows.numel(), layer.padded_in_features)[:, :layer.embedding_dim]
+            out[k] = (gf * w).sum()
+        return out, None, None
+
+
+# --------------------------------------------------------------------------- modules
+class _MixedQuantBase(nn.Module):
+    """Candidate loading, gates and bookkeeping shared by Linear and Embedding."""
+
+    def __init__(self, candidate_types: list[str], source_weight: torch.Tensor, out_features: int,
+                 in_features: int, imatrix: torch.Tensor | None = None, device=None, lazy: bool = False,
+                 tensor_name: str = "unknown", qbytes_device=None, shard_spec=None,
+                 full_source_weight: torch.Tensor | None = None, candidate_bytes: dict | None = None):
+        super().__init__()
+        self.candidate_types = list(candidate_types)
+        self.num_candidates = len(self.candidate_types)
+        for qt in self.candidate_types:
+            if qt not in GPU_FORMATS:
+                get_quant_info(qt)  # unknown type -> ValueError, as in the reference
+                raise ValueError(f"{qt} has no B200 decoder; supported candidates: {list(GPU_FORMATS)}")
+        if self.num_candidates < 1 or self.num_candidates > 8:
+            raise ValueError(f"{tensor_name}: 1..8 candidates supported, got {self.num_candidates}")
+        self.out_features = out_features
+        self.in_features = in_features
+        self.lazy = lazy
+        self._tensor_name = tensor_name
+        self.shard_spec = shard_spec
+        if shard_spec is not None and full_source_weight is None and candidate_bytes is None:
+            raise ValueError(f"{tensor_name}: shard_spec requires full_source_weight "
+                             "(the unsharded weight for candidate quantization/caching)")
+        if device is None:
+            device = source_weight.device
+        self._device = torch.device(device)
+        self.gates = nn.Parameter(torch.zeros(self.num_candidates, device=self._device))
+        self.temperature = 1.0
+        self.source_dtype = source_weight.dtype
+        self.imatrix = imatrix.detach().to(torch.float32).cpu() if imatrix is not None else None
+
+        full = full_source_weight if shard_spec is not None else source_weight
+        full_in = full.shape[1] if full is not None else in_features
+        self._full_padded_in_features = _padded(full_in)
+        if candidate_bytes is None:
+            candidate_bytes = self._load_or_quantize(full, imatrix)
+        qbytes = [candidate_bytes[qt] for qt in self.candidate_types]
+        rows = shard_spec.full_out if shard_spec is not None else out_features
+        self.padded_in_features = self._full_padded_in_features
+        if shard_spec is not None:
+            qbytes = [shard_spec.slice_qbytes(qb, qt, self._full_padded_in_features)
+                      for qb, qt in zip(qbytes, self.candidate_types)]
+            rows = shard_spec.local_out
+            self.padded_in_features = shard_spec.local_padded_in(self._full_padded_in_features,
+                                                                 self.candidate_types)
+        qdev = torch.device(qbytes_device) if qbytes_device is not None else None
+        if qdev is None or (qdev.type == "cuda" and qdev.index is None):
+            if source_weight.is_cuda:
+                qdev = source_weight.device
+            elif self._device.type == "cuda":
+                qdev = self._device
+            elif qdev is None:
+                qdev = torch.device("cpu")
+        self._qbytes_device = qdev
+        arena, layout = pack_arena(self.candidate_types, qbytes, rows, self.padded_in_features, qdev,
+                                   tensor_name)
+        self.register_buffer("_cand_arena", arena, persistent=False)
+        self._cand_layout = layout
+        self._ws = None
+        STORE.register(tensor_name, self)
+
+    # ---- candidate cache (reference format) ----
+    def _load_or_quantize(self, weight: torch.Tensor, imatrix: torch.Tensor | None) -> dict:
+        weight = weight.detach().to("cpu").contiguous()
+        padded_im = None
+        if imatrix is not None:
+            _, padded_im, _ = _pad_weight_and_imatrix(
+                torch.empty(1, weight.shape[1], dtype=torch.float32), imatrix.detach().to(torch.float32).cpu())
+        wh = _tensor_hash(weight)
+        ih = _tensor_hash(padded_im) if imatrix is not None else "none"
+        name = self._tensor_name
+        found: dict[str, torch.Tensor] = {}
+        names = [name]
+        names.append(name.removeprefix("model.") if name.startswith("model.") else "model." + name)
+        for nm in names:
+            p = _combined_cache_path(nm, "lazy", wh, ih)
+            if p.exists():
+                combined = torch.load(p, weights_only=True, map_location="cpu", mmap=True)
+                for qt in self.candidate_types:
+                    if qt in combined and qt not in found:
+                        found[qt] = combined[qt]
+                break
+        missing = []
+        for qt in self.candidate_types:
+            if qt in found:
+                continue
+            p = _candidate_cache_path(name, qt, "lazy", wh, ih)
+            if p.exists():
+                found[qt] = torch.load(p, weights_only=True, map_location="cpu", mmap=True)
+            else:
+                missing.append((qt, p))
+        if missing:
+            padded, pim, _ = _pad_weight_and_imatrix(weight.to(torch.float32), padded_im if imatrix is not None else None)
+            for qt, p in missing:
+                qb = quantize_tensor(padded, qt, pim)  # libggml, exactly as the reference
+                _atomic_torch_save(qb, p)
+                found[qt] = qb
+        return found
+
+    # ---- candidate access ----
+    def _candidate_blocks(self) -> list[torch.Tensor]:
+        return arena_views(self._cand_arena, self._cand_layout)
+
+    def __getattr__(self, name: str):
+        if name.startswith("_qweight_") and name[9:].isdigit():
+            k = int(name[9:])
+            layout = self.__dict__.get("_cand_layout")
+            if layout is not None and k < len(layout):
+                return self._candidate_blocks()[k]
+        if name.startswith("_w_") and name[3:].isdigit():
+            k = int(name[3:])
+            layout = self.__dict__.get("_cand_layout")
+            if layout is not None and k < len(layout):
+                # Decoded on demand (bit-exact); never stored.
+                qb = self._candidate_blocks()[k]
+                w = _C.dequant(qb, self.candidate_types[k], self.out_features, self.padded_in_features)
+                return w[:, :self.in_features].to(self.source_dtype)
+        return super().__getattr__(name)
+
+    def _mix(self, probs: torch.Tensor) -> torch.Tensor:
+        return _C.mix(self.candidate_types, self._candidate_blocks(), probs.to(self._cand_arena.device),
+                      self.out_features, self.padded_in_features, self.in_features)
+
+    def _gategrad_workspace(self, device: torch.device) -> torch.Tensor:
+        need = _C.gategrad_workspace_bytes(self.out_features, self.in_features, self.num_candidates)
+        if self._ws is None or self._ws.device != device or self._ws.numel() < need:
+            self._ws = torch.empty(max(need, 4), dtype=torch.uint8, device=device)
+        return self._ws
+
+    # ---- gates ----
+    def set_temperature(self, temperature: float):
+        self.temperature = max(temperature, 1e-6)
+
+    def soft_probs(self) -> torch.Tensor:
+        return F.softmax(self.gates / self.temperature, dim=0)
+
+    def get_probs(self) -> torch.Tensor:
+        return self.soft_probs()
+
+    def invalidate_candidate_cache(self):
+        """No cross-step dequant cache exists on this path (candidates stay packed)."""
+
+    def get_mixed_weight(self) -> torch.Tensor:
+        return _MixedWeightFunction.apply(self.get_probs(), self)
+
+    def effective_bytes(self) -> torch.Tensor:
+        probs = self.soft_probs()
+        out_eff = getattr(self, "_full_out_features", None) or self.out_features
+        in_eff = getattr(self, "_full_in_features", None) or self.in_features
+        n = in_eff * out_eff
+        bpw = torch.tensor([bytes_per_weight(qt) for qt in self.candidate_types], dtype=probs.dtype,
+                           device=probs.device)
+        return (probs * bpw).sum() * n
+
+    def get_assignment(self) -> str:
+        return self.candidate_types[self.gates.argmax().item()]
+
+    def get_assignment_prob(self) -> float:
+        probs = self.soft_probs().detach()
+        return probs[self.gates.argmax().item()].item()
+
+    # ---- TP restriction after construction (reference :1395-1472) ----
+    def _repack(self, qbytes: list[torch.Tensor], rows: int, padded: int) -> None:
+        arena, layout = pack_arena(self.candidate_types, qbytes, rows, padded, self._cand_arena.device,
+                                   self._tensor_name)
+        self._cand_arena = arena
+        self._cand_layout = layout
+
+    def shard_rows(self, row_ranges: list[tuple[int, int]]) -> None:
+        if self.__dict__.get("_full_out_features") is not None or self.__dict__.get("_full_in_features") is not None:
+            raise RuntimeError(f"{self._tensor_name}: already row/col-sharded")
+        shard_out = sum(e - s for s, e in row_ranges)
+        if shard_out <= 0 or shard_out > self.out_features:
+            raise ValueError(f"{self._tensor_name}: invalid row ranges {row_ranges} "
+                             f"for out_features={self.out_features}")
+        new = []
+        for qb in self._candidate_blocks():
+            q2 = qb.reshape(self.out_features, -1)
+            new.append(torch.cat([q2[s:e] for s, e in row_ranges], dim=0).reshape(-1))
+        self._repack(new, shard_out, self.padded_in_features)
+        self._full_out_features = self.out_features
+        self.out_features = shard_out
+
+    def shard_cols(self, col_range: tuple[int, int]) -> None:
+        if self.__dict__.get("_full_out_features") is not None or self.__dict__.get("_full_in_features") is not None:
+            raise RuntimeError(f"{self._tensor_name}: already row/col-sharded")
+        s, e = col_range
+        if s < 0 or e > self.in_features or e <= s:
+            raise ValueError(f"{self._tensor_name}: invalid column range {col_range} "
+                             f"for in_features={self.in_features}")
+        new = []
+        for qt, qb in zip(self.candidate_types, self._candidate_blocks()):
+            info = get_quant_info(qt)
+            if s % 256 or (e - s) % 256:
+                raise ValueError(f"{self._tensor_name}: column range {col_range} is not "
+                                 f"{info.block_size}-block aligned for {qt}")
+            nbpr = self.padded_in_features // info.block_size
+            q3 = qb.view(self.out_features, nbpr, info.block_bytes)[:, s // info.block_size:e // info.block_size]
+            new.append(q3.reshape(-1))
+        self._repack(new, self.out_features, e - s)
+        self._full_in_features = self.in_features
+        self.in_features = e - s
+        self.padded_in_features = e - s
+
+
+class MixedQuantLinear(_MixedQuantBase):
+    """Linear layer whose weight is the softmax mixture of K packed candidates."""
+
+    def __init__(self, in_features: int, out_features: int, candidate_types: list[str],
+                 source_weight: torch.Tensor, imatrix: torch.Tensor | None = None, device=None,
+                 lazy: bool = False, tensor_name: str = "unknown", qbytes_device=None, shard_spec=None,
+                 full_source_weight: torch.Tensor | None = None, candidate_bytes: dict | None = None):
+        super().__init__(candidate_types=candidate_types, source_weight=source_weight,
+                         out_features=out_features, in_features=in_features, imatrix=imatrix, device=device,
+                         lazy=lazy, tensor_name=tensor_name, qbytes_device=qbytes_device,
+                         shard_spec=shard_spec, full_source_weight=full_source_weight,
+                         candidate_bytes=candidate_bytes)
+        if shard_spec is not None and shard_spec.vocab_start is not None:
+            self.tp_vocab_start = shard_spec.vocab_start
+            self.tp_vocab_end = shard_spec.vocab_start + out_features
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        spec = self.shard_spec
+        if x.device != self._cand_arena.device:
+            x = x.to(self._cand_arena.device)
+        out = _GatedLinearFunction.apply(x, self.get_probs().to(x.device), self)
+        if spec is not None and spec.col_offset is not None:
+            from voodoo_quant.parallel import tp_all_reduce_sum
+            out = tp_all_reduce_sum(out)
+        return out
+
+
+class MixedQuantEmbedding(_MixedQuantBase):
+    """Embedding whose table is the softmax mixture of K packed candidates."""
+
+    def __init__(self, num_embeddings: int, embedding_dim: int, candidate_types: list[str],
+                 source_weight: torch.Tensor, imatrix: torch.Tensor | None = None, device=None,
+                 lazy: bool = False, tensor_name: str = "unknown", qbytes_device=None, shard_spec=None,
+                 full_source_weight: torch.Tensor | None = None, candidate_bytes: dict | None = None):
+        super().__init__(candidate_types=candidate_types, source_weight=source_weight,
+                         out_features=num_embeddings, in_features=embedding_dim, imatrix=imatrix,
+                         device=device, lazy=lazy, tensor_name=tensor_name, qbytes_device=qbytes_device,
+                         shard_spec=shard_spec, full_source_weight=full_source_weight,
+                         candidate_bytes=candidate_bytes)
+        self.num_embeddings = num_embeddings
+        self.embedding_dim = embedding_dim
+        if shard_spec is not None and shard_spec.vocab_start is not None:
+            self.tp_vocab_start = shard_spec.vocab_start
+            self.tp_vocab_end = shard_spec.vocab_start + num_embeddings
+
+    def _row_blocks(self, rows: torch.Tensor) -> list[torch.Tensor]:
+        out = []
+        for qt, qb in zip(self.candidate_types, self._candidate_blocks()):
+            info = get_quant_info(qt)
+            nbpr = self.padded_in_features // info.block_size
+            out.append(qb.view(self.num_embeddings, nbpr * info.block_bytes).index_select(0, rows).reshape(-1))
+        return out
+
+    def _embedding_lookup(self, ids: torch.Tensor) -> torch.Tensor:
+        dev = self._cand_arena.device
+        rows, inverse = torch.unique(ids.reshape(-1).to(dev), return_inverse=True)
+        mixed = _GatedEmbeddingRowsFunction.apply(self.get_probs().to(dev), rows, self)
+        return mixed[inverse].reshape(*ids.shape, self.embedding_dim)
+
+    def forward(self, input: torch.Tensor) -> torch.Tensor:
+        spec = self.shard_spec
+        if spec is not None and spec.vocab_start is not None:
+            from voodoo_quant.parallel import tp_all_reduce_sum
+            v0, v1 = self.tp_vocab_start, self.tp_vocab_end
+            mask = (input < v0) | (input >= v1)
+            local = (input - v0).clamp(0, self.num_embeddings - 1)
+            emb = self._embedding_lookup(local)
+            emb = emb * (~mask).unsqueeze(-1).to(emb.device, emb.dtype)
+            return tp_all_reduce_sum(emb)
+        return self._embedding_lookup(input)
+
+
+# --------------------------------------------------------------------------- walkers
+from voodoo_quant.arch.base import DEFAULT_ATTENTION_SEGMENTS as _DEFAULT_SEGMENTS  # noqa: E402
+
+_ATTENTION_SEGMENTS: frozenset = _DEFAULT_SEGMENTS
+
+
+def resolve_candidate_types(tensor_name: str, base_candidates: list[str],
+                            attention_candidates: list[str] | None = None,
+                            non_attention_candidates: list[str] | None = None) -> list[str]:
+    """Per-role candidate menu (reference voodoo_quant/layers.py:1870-1905)."""
+    if attention_candidates is None and non_attention_candidates is None:
+        return list(base_candidates)
+    is_attn = any(seg in _ATTENTION_SEGMENTS for seg in tensor_name.split("."))
+    group = attention_candidates if (is_attn and attention_candidates) else non_attention_candidates
+    if not group:
+        return list(base_candidates)
+    return [qt for qt in group if qt in set(base_candidates)]
+
+
+def replace_linear_with_mixed_quant(module: nn.Module, candidate_types: list[str] | None, prefix: str = "",
+                                    target_names: Optional[set[str]] = None,
+                                    skip_names: Optional[set[str]] = None,
+                                    imatrix_dict: Optional[dict[str, torch.Tensor]] = None, device=None,
+                                    lazy: bool = False, attention_candidates: Optional[list[str]] = None,
+                                    non_attention_candidates: Optional[list[str]] = None,
+                                    qbytes_device=None) -> dict[str, _MixedQuantBase]:
+    """Recursively replace selected nn.Linear children (reference :1908-2066)."""
+    if candidate_types is None:
+        candidate_types = list(GPU_FORMATS)
+    skip_names = skip_names or set()
+    imatrix_dict = imatrix_dict or {}
+    replaced: dict[str, _MixedQuantBase] = {}
+    for name, child in list(module.named_children()):
+        full_name = f"{prefix}.{name}" if prefix else name
+        if name in skip_names:
+            continue
+        if isinstance(child, nn.Linear):
+            if child.bias is not None:
+                raise NotImplementedError(f"MixedQuantLinear does not support bias but {full_name} has one")
+            if target_names is not None and name not in target_names:
+                continue
+            im = imatrix_dict.get(full_name, imatrix_dict.get(full_name + ".weight"))
+            new = MixedQuantLinear(
+                in_features=child.in_features, out_features=child.out_features,
+                candidate_types=resolve_candidate_types(full_name, candidate_types, attention_candidates,
+                                                        non_attention_candidates),
+                source_weight=child.weight.data, imatrix=im, device=device, lazy=lazy, tensor_name=full_name,
+                qbytes_device=qbytes_device, shard_spec=getattr(child, "tp_shard_spec", None),
+                full_source_weight=getattr(child, "tp_full_weight", None))
+            setattr(module, name, new)
+            replaced[full_name] = new
+        else:
+            replaced.update(replace_linear_with_mixed_quant(
+                child, candidate_types, full_name, target_names, skip_names, imatrix_dict, device, lazy,
+                attention_candidates, non_attention_candidates, qbytes_device))
+    return replaced
+
+
+def replace_embedding_with_mixed_quant(module: nn.Module, candidate_types: list[str] | None, prefix: str = "",
+                                       skip_names: Optional[set[str]] = None,
+                                       imatrix_dict: Optional[dict[str, torch.Tensor]] = None, device=None,
+                                       lazy: bool = False, qbytes_device=None,
+                                       attention_candidates: Optional[list[str]] = None,
+                                       non_attention_candidates: Optional[list[str]] = None
+                                       ) -> dict[str, MixedQuantEmbedding]:
+    """Recursively replace nn.Embedding children (reference :2086-2153)."""
+    if candidate_types is None:
+        candidate_types = list(GPU_FORMATS)
+    skip_names = skip_names or set()
+    imatrix_dict = imatrix_dict or {}
+    replaced: dict[str, MixedQuantEmbedding] = {}
+    for name, child in list(module.named_children()):
+        full_name = f"{prefix}.{name}" if prefix else name
+        if name in skip_names:
+            continue
+        if isinstance(child, nn.Embedding):
+            im = imatrix_dict.get(full_name, imatrix_dict.get(full_name + ".weight"))
+            new = MixedQuantEmbedding(
+                num_embeddings=child.num_embeddings, embedding_dim=child.embedding_dim,
+                candidate_types=resolve_candidate_types(full_name, candidate_types, attention_candidates,
+                                                        non_attention_candidates),
+                source_weight=child.weight.data, imatrix=im, device=device, lazy=lazy, tensor_name=full_name,
+                qbytes_device=qbytes_device, shard_spec=getattr(child, "tp_shard_spec", None),
+                full_source_weight=getattr(child, "tp_full_weight", None))
+            setattr(module, name, new)
+            replaced[full_name] = new
+        else:
+            replaced.update(replace_embedding_with_mixed_quant(
+                child, candidate_types, full_name, skip_names, imatrix_dict, device, lazy, qbytes_device,
+                attention_candidates, non_attention_candidates))
+    return replaced
+
+
+def total_effective_bytes(replaced: dict[str, _MixedQuantBase]) -> torch.Tensor:
+    total = None
+    for layer in replaced.values():
+        eb = layer.effective_bytes()
+        total = eb if total is None else total + eb.to(total.device)
+    return total if total is not None else torch.tensor(0.0)

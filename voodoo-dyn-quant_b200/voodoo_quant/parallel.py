@@ -1,0 +1,443 @@
+"""Tensor parallelism for the gated-candidate step (drop-in for voodoo_quant/parallel.py).
+
+Same mechanism/policy split as the reference (voodoo_quant/parallel.py):
+``ShardSpec`` + ``_shard_child`` + ``Column/RowParallelLinear`` /
+``VocabParallelEmbedding`` are the mechanism; arch adapters
+(:mod:`voodoo_quant.arch`) are the policy.  One process per GPU, NCCL over
+NVLink/NVSwitch for the collectives (gloo on CPU for tests).
+
+Differences from the reference, each for a reason:
+
+* Exact input gradients.  The reference's column-parallel layers do no
+  communication in backward (parallel.py:309-331), so the summed gate
+  gradients of stacked blocks are inexact under TP.  Here every
+  column-parallel input group (attention q/k/v, MLP gate/up) is entered
+  through ``tp_copy_to_parallel`` -- identity forward, all-reduce of dX in
+  backward (Megatron's "f" operator) -- installed once per group by the
+  adapter.  ``TP.exact_input_grad = False`` restores the reference behaviour.
+* Uneven, block-aligned shards.  ``block_aligned_split`` splits a dimension
+  into 256-element units as evenly as possible (e.g. 25600 over 8 ranks =
+  13,13,13,13,12,12,12,12 units), which the reference refuses
+  (parallel.py:285-299).
+* ``tp_init`` only binds a CUDA device when CUDA is available, so the gloo
+  path runs on CPU-only hosts (the reference calls ``torch.cuda.set_device``
+  unconditionally, parallel.py:71).
+* One flat all-reduce for all gate gradients (``all_reduce_gate_grads``)
+  instead of one call per tensor (trainer.py:434-444).
+"""
+
+from __future__ import annotations
+
+import os
+from dataclasses import dataclass
+from datetime import timedelta
+
+import torch
+import torch.distributed as dist
+import torch.nn as nn
+import torch.nn.functional as F
+from torch.autograd import Function
+
+UNIT = 256  # super-block width: every TP split of an input dimension is a multiple
+
+
+class _TPState:
+    enabled = False
+    rank = 0
+    world_size = 1
+    local_rank = 0
+    group = None
+    device: torch.device | None = None
+    exact_input_grad = True
+
+
+TP = _TPState()
+
+
+def tp_init(backend: str = "nccl", timeout_min: int = 240) -> bool:
+    """Initialise TP from torchrun's env (WORLD_SIZE > 1 and RANK set)."""
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if world <= 1 or "RANK" not in os.environ:
+        return False
+    rank = int(os.environ["RANK"])
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if torch.cuda.is_available():
+        torch.cuda.set_device(local_rank)
+    if not dist.is_initialized():
+        kw = {}
+        if backend == "nccl" and torch.cuda.is_available():
+            kw["device_id"] = torch.device("cuda", local_rank)
+        dist.init_process_group(backend=backend, init_method="env://", rank=rank, world_size=world,
+                                timeout=timedelta(minutes=timeout_min), **kw)
+    _adopt_group(local_rank)
+    return True
+
+
+def _adopt_group(local_rank: int = 0) -> None:
+    TP.enabled = dist.get_world_size() > 1
+    TP.rank = dist.get_rank()
+    TP.world_size = dist.get_world_size()
+    TP.local_rank = local_rank
+    TP.group = dist.group.WORLD
+    TP.device = torch.device("cuda", local_rank) if dist.get_backend() == "nccl" else torch.device("cpu")
+
+
+def adopt_process_group(local_rank: int = 0) -> None:
+    """Use an already-initialised default process group for TP (tests, embedding)."""
+    _adopt_group(local_rank)
+
+
+def init_tp(backend: str | None = None, timeout_min: int = 240) -> tuple[int, int]:
+    if backend is None:
+        backend = "nccl" if torch.cuda.is_available() and dist.is_nccl_available() else "gloo"
+    tp_init(backend=backend, timeout_min=timeout_min)
+    return TP.rank, TP.world_size
+
+
+def tp_finalize() -> None:
+    if TP.enabled and dist.is_initialized():
+        dist.barrier()
+        dist.destroy_process_group()
+    TP.enabled = False
+    TP.rank, TP.world_size = 0, 1
+
+
+def reset_tp() -> None:
+    TP.enabled = False
+    TP.rank, TP.world_size, TP.local_rank = 0, 1, 0
+    TP.group = None
+    TP.device = None
+
+
+def barrier() -> None:
+    if TP.enabled and dist.is_initialized():
+        dist.barrier()
+
+
+def is_main_process() -> bool:
+    return TP.rank == 0
+
+
+class _AllReduceSum(Function):
+    """All-reduce SUM forward, identity backward (reference parallel.py:140-160)."""
+
+    @staticmethod
+    def forward(ctx, t: torch.Tensor) -> torch.Tensor:
+        out = t.clone().contiguous()
+        dist.all_reduce(out, op=dist.ReduceOp.SUM, group=TP.group)
+        return out
+
+    @staticmethod
+    def backward(ctx, g):
+        return g
+
+
+class _CopyToParallel(Function):
+    """Identity forward, all-reduce SUM backward (exact dX at column-parallel inputs)."""
+
+    @staticmethod
+    def forward(ctx, t: torch.Tensor) -> torch.Tensor:
+        return t.view_as(t)
+
+    @staticmethod
+    def backward(ctx, g):
+        g = g.clone().contiguous()
+        dist.all_reduce(g, op=dist.ReduceOp.SUM, group=TP.group)
+        return g
+
+
+def tp_all_reduce_sum(t: torch.Tensor) -> torch.Tensor:
+    if not TP.enabled:
+        return t
+    return _AllReduceSum.apply(t)
+
+
+all_reduce_sum = tp_all_reduce_sum
+
+
+def tp_copy_to_parallel(t: torch.Tensor) -> torch.Tensor:
+    if not TP.enabled or not TP.exact_input_grad:
+        return t
+    return _CopyToParallel.apply(t)
+
+
+def tp_broadcast(t: torch.Tensor, src: int = 0) -> torch.Tensor:
+    if TP.enabled:
+        dist.broadcast(t, src=src, group=TP.group)
+    return t
+
+
+def all_reduce_gate_grads(params) -> None:
+    """Sum the gate gradients of every rank with ONE flat all-reduce.
+
+    Same result as the reference's per-tensor loop (trainer.py:434-444); the
+    order of tensors inside the flat buffer is the (identical) parameter order
+    on every rank.
+    """
+    if not TP.enabled:
+        return
+    params = [p for p in params if p.grad is not None]
+    if not params:
+        return
+    flat = torch.cat([p.grad.reshape(-1).to(torch.float32) for p in params])
+    dist.all_reduce(flat, op=dist.ReduceOp.SUM, group=TP.group)
+    off = 0
+    for p in params:
+        n = p.grad.numel()
+        p.grad.copy_(flat[off:off + n].view_as(p.grad))
+        off += n
+
+
+def block_aligned_split(total: int, world: int, rank: int, unit: int = UNIT) -> tuple[int, int]:
+    """(offset, length) of rank's share of `total`, in whole `unit`s, as even as possible.
+
+    The first (units % world) ranks get one extra unit.  Raises ValueError when
+    `total` is not a multiple of `unit` or some rank would get nothing.
+    """
+    if total % unit:
+        raise ValueError(f"dimension {total} is not a multiple of the {unit}-element block")
+    units = total // unit
+    if units < world:
+        raise ValueError(f"dimension {total} has {units} blocks, fewer than {world} ranks")
+    base, extra = divmod(units, world)
+    start = rank * base + min(rank, extra)
+    n = base + (1 if rank < extra else 0)
+    return start * unit, n * unit
+
+
+def even_split(total: int, world: int, rank: int) -> tuple[int, int]:
+    if total % world:
+        raise ValueError(f"dimension {total} not divisible by tp={world}")
+    n = total // world
+    return rank * n, n
+
+
+@dataclass
+class ShardSpec:
+    """Maps a rank-local slice back to its FULL tensor (reference parallel.py:183-299)."""
+
+    full_out: int
+    full_in: int
+    row_offset: int | None = None
+    row_len: int | None = None
+    row_index: torch.Tensor | None = None
+    col_offset: int | None = None
+    col_len: int | None = None
+    vocab_start: int | None = None
+
+    @property
+    def local_out(self) -> int:
+        if self.row_index is not None:
+            return int(self.row_index.numel())
+        if self.row_len is not None:
+            return self.row_len
+        return self.full_out
+
+    @property
+    def local_in(self) -> int:
+        return self.col_len if self.col_len is not None else self.full_in
+
+    def describe(self) -> str:
+        kind = "row-grouped" if self.row_index is not None else (
+            "column" if self.row_len is not None else ("row" if self.col_len is not None else "none"))
+        return f"{kind}-parallel local [{self.local_out}x{self.local_in}] of full [{self.full_out}x{self.full_in}]"
+
+    def slice_weight(self, w_full: torch.Tensor) -> torch.Tensor:
+        if self.row_index is not None:
+            w = w_full[self.row_index.to(w_full.device)]
+        elif self.row_offset is not None:
+            w = w_full[self.row_offset:self.row_offset + self.row_len]
+        else:
+            w = w_full
+        if self.col_offset is not None:
+            w = w[:, self.col_offset:self.col_offset + self.col_len]
+        return w
+
+    def slice_qbytes(self, qb_full: torch.Tensor, quant_type: str, padded_full_in: int) -> torch.Tensor:
+        """Slice FULL packed blocks to this rank's rows / block-aligned columns."""
+        from voodoo_quant.ggml import get_quant_info
+
+        info = get_quant_info(quant_type)
+        bs, bb = info.block_size, info.block_bytes
+        if padded_full_in % bs != 0:
+            raise ValueError(f"{quant_type}: padded in {padded_full_in} not block-aligned ({bs})")
+        nbpr = padded_full_in // bs
+        if qb_full.numel() != self.full_out * nbpr * bb:
+            raise ValueError(f"{quant_type}: qbytes numel {qb_full.numel()} != "
+                             f"{self.full_out}x{nbpr}x{bb} expected for the FULL tensor")
+        q2 = qb_full.reshape(self.full_out, nbpr, bb)
+        if self.row_index is not None:
+            q2 = q2[self.row_index.to(q2.device)]
+        elif self.row_offset is not None:
+            q2 = q2[self.row_offset:self.row_offset + self.row_len]
+        if self.col_offset is not None:
+            if self.col_offset % UNIT or self.col_len % UNIT:
+                raise ValueError(
+                    f"{quant_type}: column slice [{self.col_offset}:{self.col_offset + self.col_len}] is not "
+                    f"aligned to the {UNIT}-weight block; TP shard boundaries must be block-aligned")
+            q2 = q2[:, self.col_offset // bs:(self.col_offset + self.col_len) // bs]
+        return q2.reshape(-1, bb)
+
+    def local_padded_in(self, padded_full_in: int, candidate_types: list[str]) -> int:
+        if self.col_len is None:
+            return padded_full_in
+        if self.col_len % UNIT:
+            raise ValueError(f"the rank-local input slice {self.col_len} is not a multiple of {UNIT}; "
+                             "use block_aligned_split for row-parallel shards")
+        return self.col_len
+
+
+class ColumnParallelLinear(nn.Linear):
+    """Output rows sharded; no communication in forward."""
+
+    def __init__(self, weight_slice: torch.Tensor, spec: ShardSpec, full_weight: torch.Tensor,
+                 vocab_start: int | None = None):
+        super().__init__(spec.full_in, spec.local_out, bias=False, device="meta", dtype=weight_slice.dtype)
+        self.weight = nn.Parameter(weight_slice, requires_grad=False)
+        self.tp_shard_spec = spec
+        self.tp_full_weight = full_weight
+        if vocab_start is not None:
+            self.tp_vocab_start = vocab_start
+            self.tp_vocab_end = vocab_start + spec.local_out
+
+
+class RowParallelLinear(nn.Linear):
+    """Input columns sharded; forward all-reduces the partial sums."""
+
+    def __init__(self, weight_slice: torch.Tensor, spec: ShardSpec, full_weight: torch.Tensor):
+        super().__init__(spec.local_in, spec.full_out, bias=False, device="meta", dtype=weight_slice.dtype)
+        self.weight = nn.Parameter(weight_slice.contiguous(), requires_grad=False)
+        self.tp_shard_spec = spec
+        self.tp_full_weight = full_weight
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        return tp_all_reduce_sum(F.linear(x.to(self.weight.device), self.weight))
+
+
+class VocabParallelEmbedding(nn.Embedding):
+    """Vocabulary rows sharded; masked lookup + all-reduce."""
+
+    def __init__(self, weight_slice: torch.Tensor, spec: ShardSpec, full_weight: torch.Tensor):
+        super().__init__(spec.local_out, spec.full_in, device="meta", dtype=weight_slice.dtype)
+        self.weight = nn.Parameter(weight_slice)
+        self.tp_shard_spec = spec
+        self.tp_full_weight = full_weight
+        self.tp_vocab_start = spec.vocab_start
+        self.tp_vocab_end = spec.vocab_start + spec.local_out
+
+    def forward(self, input: torch.Tensor) -> torch.Tensor:
+        input = input.to(self.weight.device)
+        v0, v1 = self.tp_vocab_start, self.tp_vocab_end
+        mask = (input < v0) | (input >= v1)
+        out = F.embedding((input - v0).clamp(0, self.num_embeddings - 1), self.weight)
+        out = out * (~mask).unsqueeze(-1).to(out.dtype)
+        return tp_all_reduce_sum(out)
+
+
+_PARALLEL_TYPES = (ColumnParallelLinear, RowParallelLinear, VocabParallelEmbedding)
+
+
+def _shard_child(parent: nn.Module, name: str, *, row_offset=None, row_len=None, row_index=None,
+                 col_offset=None, col_len=None, vocab_start=None) -> nn.Module:
+    """Replace parent.<name> (nn.Linear / nn.Embedding) with its rank-local parallel module."""
+    child = getattr(parent, name)
+    if isinstance(child, _PARALLEL_TYPES):
+        return child
+    if isinstance(child, nn.Linear):
+        w = child.weight.data
+        spec = ShardSpec(full_out=w.shape[0], full_in=w.shape[1], row_offset=row_offset, row_len=row_len,
+                         row_index=row_index, col_offset=col_offset, col_len=col_len, vocab_start=vocab_start)
+        sl = spec.slice_weight(w)
+        new = ColumnParallelLinear(sl, spec, w, vocab_start) if col_offset is None else RowParallelLinear(sl, spec, w)
+        setattr(parent, name, new)
+        return new
+    if isinstance(child, nn.Embedding):
+        w = child.weight.data
+        if vocab_start is None:
+            raise ValueError("embedding sharding requires vocab_start")
+        spec = ShardSpec(full_out=w.shape[0], full_in=w.shape[1], row_offset=row_offset, row_len=row_len,
+                         vocab_start=vocab_start)
+        new = VocabParallelEmbedding(spec.slice_weight(w), spec, w)
+        setattr(parent, name, new)
+        return new
+    raise TypeError(f"parallel: cannot shard {type(child).__name__} at '{name}'")
+
+
+def _install_input_copy(module: nn.Module) -> None:
+    """Route the first positional / `hidden_states` input through the f operator."""
+    if getattr(module, "_tp_input_copy", False):
+        return
+
+    def hook(mod, args, kwargs):
+        if args:
+            return (tp_copy_to_parallel(args[0]),) + tuple(args[1:]), kwargs
+        if "hidden_states" in kwargs:
+            kwargs = dict(kwargs)
+            kwargs["hidden_states"] = tp_copy_to_parallel(kwargs["hidden_states"])
+        return args, kwargs
+
+    module.register_forward_pre_hook(hook, with_kwargs=True)
+    module._tp_input_copy = True
+
+
+def tp_mlp(mlp: nn.Module) -> None:
+    """gate/up column-parallel, down row-parallel (uneven 256-aligned split allowed)."""
+    tp, r = TP.world_size, TP.rank
+    off, n = block_aligned_split(mlp.gate_proj.out_features, tp, r)
+    _shard_child(mlp, "gate_proj", row_offset=off, row_len=n)
+    _shard_child(mlp, "up_proj", row_offset=off, row_len=n)
+    _shard_child(mlp, "down_proj", col_offset=off, col_len=n)
+    _install_input_copy(mlp)
+
+
+def tp_attention_dense(attn: nn.Module, num_heads: int, num_kv_heads: int, head_dim: int) -> None:
+    """Llama-style attention: q/k/v column-parallel by whole heads, o row-parallel."""
+    tp, r = TP.world_size, TP.rank
+    if num_heads % tp or num_kv_heads % tp:
+        raise ValueError(f"attention heads ({num_heads} q / {num_kv_heads} kv) must divide tp={tp}")
+    hq, hk = num_heads // tp, num_kv_heads // tp
+    _shard_child(attn, "q_proj", row_offset=r * hq * head_dim, row_len=hq * head_dim)
+    _shard_child(attn, "k_proj", row_offset=r * hk * head_dim, row_len=hk * head_dim)
+    _shard_child(attn, "v_proj", row_offset=r * hk * head_dim, row_len=hk * head_dim)
+    _shard_child(attn, "o_proj", col_offset=r * hq * head_dim, col_len=hq * head_dim)
+    attn.tp_heads_local = hq
+    _install_input_copy(attn)
+
+
+def _shard_lm_head(model: nn.Module) -> None:
+    head, holder = None, None
+    for h, attr in ((model, "lm_head"), (getattr(model, "model", None), "lm_head")):
+        if h is not None and getattr(h, attr, None) is not None:
+            head, holder = getattr(h, attr), h
+            break
+    if head is None or isinstance(head, ColumnParallelLinear):
+        return
+    off, n = even_split(head.out_features, TP.world_size, TP.rank)
+    _shard_child(holder, "lm_head", row_offset=off, row_len=n, vocab_start=off)
+
+
+def tp_patch_model(model: nn.Module, verbose: bool = True) -> nn.Module:
+    """Shard a model in place for the current rank via its registered arch adapter."""
+    from voodoo_quant.arch import adapter_for_model
+
+    adapter = adapter_for_model(model)
+    if adapter is None:
+        raise RuntimeError(
+            f"no architecture adapter registered for {type(model).__name__} "
+            f"(model_type={getattr(getattr(model, 'config', None), 'model_type', '?')}); "
+            "tensor parallelism is refused rather than sharded blindly.")
+    text = getattr(model, "model", None)
+    if text is None or not hasattr(text, "layers"):
+        text = model
+    embed = getattr(text, "embed_tokens", None)
+    if embed is not None:
+        off, n = even_split(embed.num_embeddings, TP.world_size, TP.rank)
+        _shard_child(text, "embed_tokens", row_offset=off, row_len=n, vocab_start=off)
+    handled = 0
+    for layer in text.layers:
+        handled += len(adapter.shard_layer(layer))
+    _shard_lm_head(model)
+    if verbose and TP.rank == 0:
+        print(f"[tp] patched rank {TP.rank}/{TP.world_size} ({adapter.__name__}): {handled} submodule groups",
+              flush=True)
+    return model

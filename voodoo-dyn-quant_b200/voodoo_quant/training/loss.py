@@ -1,0 +1,119 @@
+"""Fused CE + lambda * T^2 * KL(teacher || student) on the B200 loss kernel.
+
+Replaces the reference's loss blocks (voodoo_quant/training/trainer.py):
+
+* plain path :2567-2575  -- ``distillation_loss(..., ce_reduction="valid")``:
+  mean CE over non-ignored tokens (F.cross_entropy's default, ignore id -100)
+  plus ``distill_weight`` * mean per-token T^2 * KL;
+* chunked path :797-821 -- ``ce_reduction="tokens"``: both sums divided by
+  the token count;
+* vocab-parallel path :915-1066 -- ``tp_distillation_loss``: each rank holds
+  the logits of its vocabulary shard; per-row partial statistics from one
+  pass over the shard are all-gathered once (one collective, instead of the
+  reference's MAX + SUM + SUM per token chunk), combined, and the gradient is
+  written for the local shard.
+
+The kernel reads student and teacher logits once for the statistics and once
+more (L2-resident) for the gradient, which it writes in bf16; the returned
+loss is a scalar whose backward scales that stored gradient.
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+from torch.autograd import Function
+
+from voodoo_quant import _C
+
+
+def _weights(targets: torch.Tensor, n: int, distill_weight: float, ce_reduction: str):
+    if ce_reduction == "valid":
+        n_valid = int((targets >= 0).sum().item()) if targets.numel() else 0
+        ce_w = 1.0 / max(n_valid, 1)
+    elif ce_reduction == "tokens":
+        ce_w = 1.0 / max(n, 1)
+    else:
+        raise ValueError(f"ce_reduction must be 'valid' or 'tokens', got {ce_reduction!r}")
+    return ce_w, distill_weight / max(n, 1)
+
+
+class _FusedDistillLoss(Function):
+    @staticmethod
+    def forward(ctx, s: torch.Tensor, t: torch.Tensor, y: torch.Tensor, temperature: float, ce_w: float,
+                kl_w: float):
+        need = s.requires_grad
+        ce, kl, g = _C.loss_fused(s, t, y, temperature, ce_w, kl_w, want_grad=need)
+        ctx.g = g
+        ctx.s_dtype = s.dtype
+        ce_sum, kl_sum = ce.sum(), kl.sum()
+        ctx.mark_non_differentiable(ce_sum, kl_sum)
+        return ce_w * ce_sum + kl_w * kl_sum, ce_sum, kl_sum
+
+    @staticmethod
+    def backward(ctx, g_loss, _g_ce, _g_kl):
+        g = ctx.g
+        ctx.g = None
+        if g is None:
+            return None, None, None, None, None, None
+        return (g * g_loss.to(g.dtype)).to(ctx.s_dtype), None, None, None, None, None
+
+
+def distillation_loss(student_logits: torch.Tensor, teacher_logits: torch.Tensor, targets: torch.Tensor,
+                      temperature: float = 1.0, distill_weight: float = 1.0, ce_reduction: str = "valid"):
+    """Returns (loss, lm_loss, distill_loss) like the reference's plain path.
+
+    ``loss = lm_loss + distill_weight * distill_loss`` is differentiable with
+    respect to ``student_logits`` ([..., V]); lm_loss / distill_loss are
+    detached scalars (mean CE, mean per-token T^2 * KL).
+    """
+    V = student_logits.shape[-1]
+    s = student_logits.reshape(-1, V)
+    t = teacher_logits.reshape(-1, V).detach()
+    y = targets.reshape(-1)
+    n = s.shape[0]
+    ce_w, kl_w = _weights(y, n, distill_weight, ce_reduction)
+    loss, ce_sum, kl_sum = _FusedDistillLoss.apply(s, t, y, float(temperature), ce_w, kl_w)
+    return loss, (ce_sum * ce_w).detach(), (kl_sum / max(n, 1)).detach()
+
+
+class _TPFusedDistillLoss(Function):
+    @staticmethod
+    def forward(ctx, s, t, y, vocab_start, temperature, ce_w, kl_w, group):
+        stats = _C.loss_stats(s, t, y, vocab_start, temperature)            # [rows, 8]
+        world = dist.get_world_size(group)
+        gathered = torch.empty((world,) + tuple(stats.shape), dtype=stats.dtype, device=stats.device)
+        dist.all_gather_into_tensor(gathered, stats, group=group)
+        lse, ce, kl = _C.loss_combine(gathered, temperature)
+        ctx.g = _C.loss_grad(s, t, y, vocab_start, temperature, lse, ce_w, kl_w) if s.requires_grad else None
+        ctx.s_dtype = s.dtype
+        ce_sum, kl_sum = ce.sum(), kl.sum()
+        ctx.mark_non_differentiable(ce_sum, kl_sum)
+        return ce_w * ce_sum + kl_w * kl_sum, ce_sum, kl_sum
+
+    @staticmethod
+    def backward(ctx, g_loss, _a, _b):
+        g = ctx.g
+        ctx.g = None
+        if g is None:
+            return (None,) * 8
+        return (g * g_loss.to(g.dtype)).to(ctx.s_dtype), None, None, None, None, None, None, None
+
+
+def tp_distillation_loss(student_shard: torch.Tensor, teacher_shard: torch.Tensor, targets: torch.Tensor,
+                         vocab_start: int, temperature: float = 1.0, distill_weight: float = 1.0,
+                         ce_reduction: str = "tokens", group=None):
+    """Vocabulary-parallel loss: every rank passes its [..., V/N] logits shard.
+
+    The returned loss is the exact global loss on every rank; its gradient
+    covers this rank's shard only (each rank differentiates its own logits).
+    """
+    V = student_shard.shape[-1]
+    s = student_shard.reshape(-1, V)
+    t = teacher_shard.reshape(-1, V).detach()
+    y = targets.reshape(-1)
+    n = s.shape[0]
+    ce_w, kl_w = _weights(y, n, distill_weight, ce_reduction)
+    loss, ce_sum, kl_sum = _TPFusedDistillLoss.apply(s, t, y, int(vocab_start), float(temperature), ce_w, kl_w,
+                                                     group)
+    return loss, (ce_sum * ce_w).detach(), (kl_sum / max(n, 1)).detach()
