@@ -50,6 +50,31 @@ int device_error_ptr(int** p) {
   return 0;
 }
 
+// Makes the device that owns `p` current (initialising its primary context on
+// this thread, which driver-API calls such as cuTensorMapEncodeTiled need,
+// e.g. on autograd worker threads) and restores the caller's device on exit.
+class DeviceScope {
+ public:
+  explicit DeviceScope(const void* p) {
+    cudaGetDevice(&prev_);
+    int dev = prev_;
+    cudaPointerAttributes a;
+    if (p != nullptr && cudaPointerGetAttributes(&a, p) == cudaSuccess && a.type == cudaMemoryTypeDevice)
+      dev = a.device;
+    else
+      cudaGetLastError();  // clear a sticky-free error from a host pointer query
+    cudaSetDevice(dev);
+    changed_ = dev != prev_;
+  }
+  ~DeviceScope() {
+    if (changed_) cudaSetDevice(prev_);
+  }
+
+ private:
+  int prev_ = 0;
+  bool changed_ = false;
+};
+
 int sm_count(int* n) {
   int dev = 0;
   VQ_CUDA(cudaGetDevice(&dev));
@@ -153,6 +178,7 @@ int vq_format_info(int ggml_type, int* block_elems, int* block_bytes) {
 }
 
 int vq_device_error(void* stream, int* code) {
+  DeviceScope scope(nullptr);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   int* dp = nullptr;
   if (int rc = device_error_ptr(&dp)) return rc;
@@ -166,6 +192,7 @@ int vq_device_error(void* stream, int* code) {
 }
 
 int vq_dequant(int ggml_type, const void* blocks, int64_t rows, int64_t cols, float* out, void* stream) {
+  DeviceScope scope(out);
   if (!known_format(ggml_type)) return fail(VQ_ERR_UNSUPPORTED, "unsupported ggml type %d", ggml_type);
   const int bs = vq::block_elems(ggml_type);
   if (rows < 0 || cols < 0) return fail(VQ_ERR_INVALID, "negative shape");
@@ -190,6 +217,7 @@ int vq_dequant(int ggml_type, const void* blocks, int64_t rows, int64_t cols, fl
 
 int vq_mix(int K, const int* types, const void* const* blocks, const float* probs, int64_t rows, int64_t padded_cols,
            int64_t cols, void* w_bf16, int64_t ldw, void* stream) {
+  DeviceScope scope(w_bf16);
   vq::CandSet cs;
   if (int rc = build_candset(&cs, K, types, blocks)) return rc;
   if (rows < 0 || cols < 0 || padded_cols < cols) return fail(VQ_ERR_INVALID, "invalid shape");
@@ -212,6 +240,7 @@ int vq_mix(int K, const int* types, const void* const* blocks, const float* prob
 
 int vq_linear_fwd(const void* x, int64_t T, int64_t Kin, int64_t ldx, const void* w, int64_t N, int64_t ldw, void* y,
                   int64_t ldy, void* stream) {
+  DeviceScope scope(y);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (int rc = check_matrix(x, T, Kin, ldx, "x")) return rc;
   if (int rc = check_matrix(w, N, Kin, ldw, "w")) return rc;
@@ -234,6 +263,7 @@ int vq_linear_fwd(const void* x, int64_t T, int64_t Kin, int64_t ldx, const void
 
 int vq_linear_dx(const void* dy, int64_t T, int64_t N, int64_t lddy, const void* w, int64_t Kin, int64_t ldw, void* dx,
                  int64_t lddx, void* stream) {
+  DeviceScope scope(dx);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (int rc = check_matrix(dy, T, N, lddy, "dy")) return rc;
   if (int rc = check_matrix(w, N, Kin, ldw, "w")) return rc;
@@ -263,6 +293,7 @@ size_t vq_gategrad_workspace_bytes(int64_t N, int64_t Kin, int K) {
 int vq_gategrad(const void* dy, int64_t lddy, const void* x, int64_t ldx, int64_t T, int64_t N, int64_t Kin, int K,
                 const int* types, const void* const* blocks, int64_t padded_cols, void* workspace,
                 size_t workspace_bytes, float* grad_probs, void* stream) {
+  DeviceScope scope(grad_probs);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   vq::CandSet cs;
   if (int rc = build_candset(&cs, K, types, blocks)) return rc;
@@ -309,6 +340,7 @@ int vq_mixgemm_fwd(const void* x, int64_t T, int64_t Kin, int64_t ldx, int K, co
 int vq_loss_fused(const void* s_logits, int64_t lds, const void* t_logits, int64_t ldt, const int64_t* targets,
                   int64_t rows, int64_t V, float temperature, float ce_weight, float kl_weight, float* row_ce,
                   float* row_kl, void* dlogits, int64_t ldg, void* stream) {
+  DeviceScope scope(row_ce);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (int rc = check_matrix(s_logits, rows, V, lds, "student logits")) return rc;
   if (int rc = check_matrix(t_logits, rows, V, ldt, "teacher logits")) return rc;
@@ -341,6 +373,7 @@ int vq_loss_fused(const void* s_logits, int64_t lds, const void* t_logits, int64
 
 int vq_loss_stats(const void* s_logits, int64_t lds, const void* t_logits, int64_t ldt, const int64_t* targets,
                   int64_t vocab_start, int64_t rows, int64_t V, float temperature, float* stats, void* stream) {
+  DeviceScope scope(stats);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (int rc = check_matrix(s_logits, rows, V, lds, "student logits")) return rc;
   if (int rc = check_matrix(t_logits, rows, V, ldt, "teacher logits")) return rc;
@@ -368,6 +401,7 @@ int vq_loss_stats(const void* s_logits, int64_t lds, const void* t_logits, int64
 
 int vq_loss_combine(const float* stats, int ranks, int64_t rows, float temperature, float* row_lse, float* row_ce,
                     float* row_kl, void* stream) {
+  DeviceScope scope(row_ce);
   if (ranks < 1) return fail(VQ_ERR_INVALID, "ranks must be >= 1");
   if (rows < 0 || rows > 0x7fffffff) return fail(VQ_ERR_INVALID, "invalid row count");
   if (rows == 0) return 0;
@@ -383,6 +417,7 @@ int vq_loss_combine(const float* stats, int ranks, int64_t rows, float temperatu
 int vq_loss_grad(const void* s_logits, int64_t lds, const void* t_logits, int64_t ldt, const int64_t* targets,
                  int64_t vocab_start, int64_t rows, int64_t V, float temperature, const float* row_lse,
                  float ce_weight, float kl_weight, void* dlogits, int64_t ldg, void* stream) {
+  DeviceScope scope(dlogits);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (int rc = check_matrix(s_logits, rows, V, lds, "student logits")) return rc;
   if (int rc = check_matrix(t_logits, rows, V, ldt, "teacher logits")) return rc;
