@@ -67,26 +67,41 @@ def config(n_gpus: int, extra=None):
 
 # ----------------------------------------------------------------------------- clocks
 class ClockSampler:
+    """nvidia-smi sampling (200 ms) started before the timed region; summary()
+    keeps the samples whose timestamps fall inside [mark_start, mark_end]."""
+
+    FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
     def __init__(self, index: int):
         self.index = index
         self.proc = None
         self.path = None
+        self.t0 = self.t1 = None
 
-    def __enter__(self):
+    def start(self):
         fd, self.path = tempfile.mkstemp(suffix=".csv")
         os.close(fd)
-        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
         try:
-            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={q}",
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
                                           "--format=csv,noheader,nounits", "-lms", "200"],
                                          stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
+        deadline = time.time() + 5.0   # wait for the first sample so the timed region is covered
+        while self.proc is not None and time.time() < deadline and os.path.getsize(self.path) == 0:
+            time.sleep(0.05)
         return self
 
-    def __exit__(self, *a):
+    def mark_start(self):
+        self.t0 = time.time()
+
+    def mark_end(self):
+        self.t1 = time.time()
+        time.sleep(0.25)
+
+    def stop(self):
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -95,22 +110,35 @@ class ClockSampler:
                 self.proc.kill()
 
     def summary(self):
-        if self.path is None or not os.path.exists(self.path):
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        from datetime import datetime
+
         rows = []
-        for line in open(self.path):
-            f = [x.strip() for x in line.split(",")]
-            if len(f) >= 9:
-                rows.append(f)
-        os.unlink(self.path)
-        if not rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        sm = sorted(float(r[1]) for r in rows if r[1].replace(".", "").isdigit())
-        mx = max(float(r[2]) for r in rows if r[2].replace(".", "").isdigit()) if rows else None
+        if self.path and os.path.exists(self.path):
+            for line in open(self.path):
+                f = [x.strip() for x in line.split(",")]
+                if len(f) < 9:
+                    continue
+                try:
+                    ts = datetime.strptime(f[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                except ValueError:
+                    continue
+                rows.append((ts, f))
+            os.unlink(self.path)
+        inside = [f for ts, f in rows if self.t0 is not None and self.t0 - 0.2 <= ts <= (self.t1 or ts) + 0.2]
+        use = inside or [f for _, f in rows]
+
+        def num(x):
+            try:
+                return float(x)
+            except ValueError:
+                return None
+
+        sm = sorted(v for v in (num(f[2]) for f in use) if v is not None)
+        mx = [v for v in (num(f[3]) for f in use) if v is not None]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower().startswith("active")})
-        return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": mx, "reasons": reasons,
-                "samples": len(rows)}
+        reasons = sorted({names[i] for f in use for i in range(4) if f[5 + i].lower().startswith("active")})
+        return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(inside), "samples_total": len(rows)}
 
 
 # ----------------------------------------------------------------------------- setup
@@ -196,16 +224,19 @@ def run_gpu(args):
     barrier()
 
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clk:
-        barrier()
-        torch.cuda.synchronize()
-        ev0.record(stream)
-        for _ in range(args.steps):
-            x.grad = None
-            step(x, dy)
-        ev1.record(stream)
-        torch.cuda.synchronize()
-        barrier()
+    clk = ClockSampler(local).start()
+    barrier()
+    torch.cuda.synchronize()
+    clk.mark_start()
+    ev0.record(stream)
+    for _ in range(args.steps):
+        x.grad = None
+        step(x, dy)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    clk.mark_end()
+    barrier()
+    clk.stop()
     ms = ev0.elapsed_time(ev1) / args.steps
     t = torch.tensor([ms], device=dev)
     if world > 1:
@@ -392,7 +423,7 @@ def run_reference(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=60)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--kernel-iters", type=int, default=10)

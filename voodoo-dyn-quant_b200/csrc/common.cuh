@@ -19,6 +19,7 @@ enum DeviceError : int {
   kDevOk = 0,
   kDevWaitTimeout = 1,  // an mbarrier wait exceeded kWaitTimeoutNs
   kDevBadFormat = 2,    // unknown block format reached a kernel
+  kDevBadSmemAlign = 3, // dynamic shared memory not 1024-byte aligned
 };
 
 // Every spin on an mbarrier gives up after this long, records

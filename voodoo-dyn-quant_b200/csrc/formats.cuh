@@ -1,15 +1,20 @@
 // Bit-exact GGUF block decoders for the candidate formats of the gated
 // Linear.  A "unit" is 256 consecutive weights of one row: one super-block for
-// the K-quants and IQ4_XS, eight 34-byte blocks for Q8_0.  dec8(unit, i, y)
-// writes elements 8*i .. 8*i+7 of the unit (i in [0, 32)), so one warp decodes
-// a whole unit with one call per lane.
+// the K-quants and IQ4_XS, eight 34-byte blocks for Q8_0.
+//
+// Decoders read a unit from a 4-byte aligned SHARED-memory slot (units are
+// staged there by stage_unit_warp, which realigns 2-byte aligned GGUF blocks
+// with funnel shifts), so every field is fetched with 32-bit loads.
+// dec8<fmt>(slot, i, y) writes elements 8*i .. 8*i+7 of the unit (i in
+// [0, 32)), so one warp decodes a whole unit with one call per lane.
 //
 // Every multiply/subtract is an explicitly rounded __fmul_rn / __fsub_rn in
 // the order of the reference decoders (voodoo_quant/layers.py:62-213,
 // voodoo_quant/quants/gpu_dequant.py:460-519; gguf-py 0.19.0 for Q2_K/Q3_K),
-// so the compiler cannot contract them into FMAs and the float32 results are
-// bit-identical to the reference.  All multi-byte fields sit at even offsets,
-// so 2-byte alignment of each block is all that is assumed.
+// so nothing is contracted into an FMA and the float32 results are
+// bit-identical to the reference.  Small integers are converted to float with
+// the exact identity float(0x4B000000 | q) - 2^23 = q (q < 2^23): one logic
+// op and one add instead of a quarter-rate integer conversion.
 #pragma once
 
 #include "common.cuh"
@@ -42,134 +47,380 @@ __host__ __device__ inline int unit_bytes(int fmt) {
 
 __host__ __device__ inline int block_elems(int fmt) { return fmt == kQ8_0 ? 32 : 256; }
 __host__ __device__ inline int block_bytes(int fmt) { return fmt == kQ8_0 ? 34 : unit_bytes(fmt); }
+// 32-bit words of a staged unit slot.
+__host__ __device__ inline int unit_words(int fmt) { return (unit_bytes(fmt) + 3) / 4; }
 
-__device__ __forceinline__ float ld_f16(const uint8_t* p) {
-  return __half2float(__ushort_as_half(*reinterpret_cast<const unsigned short*>(p)));
+constexpr int kMaxUnitWords = 68;  // Q8_0: 272 bytes
+
+__device__ __forceinline__ float u2f(uint32_t q) {  // exact for q < 2^23
+  return __uint_as_float(0x4B000000u | q) - 8388608.0f;
 }
 
-// 6-bit scale/min pair j of the 12-byte Q4_K/Q5_K table (get_scale_min_k4).
-__device__ __forceinline__ void k4_scale_min(const uint8_t* q, int j, int& sc, int& mn) {
+__device__ __forceinline__ float h2f(uint32_t bits16) {
+  return __half2float(__ushort_as_half(static_cast<unsigned short>(bits16)));
+}
+
+__device__ __forceinline__ uint32_t lw(const uint32_t* s, int word) { return s[word]; }
+
+__device__ __forceinline__ uint32_t byte_of(const uint32_t* s, int off) {
+  return (s[off >> 2] >> (8 * (off & 3))) & 0xFFu;
+}
+
+// Copy the `nbytes` (even) bytes at 2-byte aligned `src` into the 4-byte
+// aligned slot `dst`, one output word per lane step.  Reads only aligned
+// 32-bit words that contain at least one requested byte (so never a word
+// outside the source allocation).
+__device__ __forceinline__ void stage_unit_warp(uint32_t* dst, const uint8_t* src, int nbytes, int lane) {
+  const uintptr_t a = reinterpret_cast<uintptr_t>(src);
+  const uint32_t* s = reinterpret_cast<const uint32_t*>(a & ~uintptr_t(3));
+  const uint32_t sh = static_cast<uint32_t>(a & 3u) * 8u;  // 0 or 16
+  const int nw = (nbytes + 3) >> 2;
+  for (int w = lane; w < nw; w += 32) {
+    const uint32_t lo = __ldg(s + w);
+    const uint32_t hi = (sh != 0u && 4 * w + 3 <= nbytes) ? __ldg(s + w + 1) : 0u;
+    dst[w] = __funnelshift_r(lo, hi, sh);
+  }
+}
+
+// Two consecutive 32-bit words starting at byte offset `off` (multiple of 4).
+__device__ __forceinline__ void ld2(const uint32_t* s, int off, uint32_t& a, uint32_t& b) {
+  a = s[off >> 2];
+  b = s[(off >> 2) + 1];
+}
+
+// ---------------------------------------------------------------- decoders
+template <int F>
+struct Dec;
+
+template <>
+struct Dec<kQ8_0> {
+  __device__ __forceinline__ static void run(const uint32_t* s, int i, float (&y)[8]) {
+    const int b = i >> 2;
+    const int dof = 34 * b;
+    const float d = h2f(s[dof >> 2] >> (8 * (dof & 2)));
+    const int off = dof + 2 + 8 * (i & 3);
+    const int a = off & ~3;
+    const uint32_t sh = static_cast<uint32_t>(off & 3) * 8u;
+    const uint32_t w0 = s[a >> 2], w1 = s[(a >> 2) + 1];
+    const uint32_t w2 = sh ? s[(a >> 2) + 2] : 0u;
+    const uint32_t q0 = __funnelshift_r(w0, w1, sh), q1 = __funnelshift_r(w1, w2, sh);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const uint32_t byte = ((j < 4 ? q0 : q1) >> (8 * (j & 3))) & 0xFFu;
+      y[j] = __fmul_rn(u2f(byte ^ 0x80u) - 128.0f, d);
+    }
+  }
+};
+
+__device__ __forceinline__ void k4_scale_min_w(const uint32_t* s, int j, uint32_t& sc, uint32_t& mn) {
+  // 12-byte table at byte 4: q[0..11] = bytes 4..15 (words 1..3)
   if (j < 4) {
-    sc = q[j] & 63;
-    mn = q[j + 4] & 63;
+    sc = byte_of(s, 4 + j) & 63u;
+    mn = byte_of(s, 8 + j) & 63u;
   } else {
-    sc = (q[j + 4] & 15) | ((q[j - 4] >> 6) << 4);
-    mn = (q[j + 4] >> 4) | ((q[j] >> 6) << 4);
+    const uint32_t hi = byte_of(s, 4 + j + 4);  // q[j+4]
+    sc = (hi & 15u) | ((byte_of(s, 4 + j - 4) >> 6) << 4);
+    mn = (hi >> 4) | ((byte_of(s, 4 + j) >> 6) << 4);
   }
 }
 
-__device__ __forceinline__ void dec8_q8_0(const uint8_t* u, int i, float (&y)[8]) {
-  const uint8_t* b = u + 34 * (i >> 2);
-  const float d = ld_f16(b);
-  const int8_t* qs = reinterpret_cast<const int8_t*>(b + 2 + 8 * (i & 3));
+template <>
+struct Dec<kQ4_K> {
+  __device__ __forceinline__ static void run(const uint32_t* s, int i, float (&y)[8]) {
+    const uint32_t w0 = s[0];
+    const float d = h2f(w0), dmin = h2f(w0 >> 16);
+    const int sb = i >> 2;
+    uint32_t sc, mn;
+    k4_scale_min_w(s, sb, sc, mn);
+    const float dl = __fmul_rn(d, u2f(sc));
+    const float ml = __fmul_rn(dmin, u2f(mn));
+    uint32_t a, b;
+    ld2(s, 16 + 32 * (sb >> 1) + 8 * (i & 3), a, b);
+    const uint32_t sh = (sb & 1) * 4;
 #pragma unroll
-  for (int j = 0; j < 8; ++j) y[j] = __fmul_rn(static_cast<float>(qs[j]), d);
-}
-
-__device__ __forceinline__ void dec8_q4_k(const uint8_t* u, int i, float (&y)[8]) {
-  const float d = ld_f16(u), dmin = ld_f16(u + 2);
-  const int sb = i >> 2;  // 32-element sub-block
-  int sc, mn;
-  k4_scale_min(u + 4, sb, sc, mn);
-  const float dl = __fmul_rn(d, static_cast<float>(sc));
-  const float ml = __fmul_rn(dmin, static_cast<float>(mn));
-  const uint8_t* qs = u + 16 + 32 * (sb >> 1) + 8 * (i & 3);
-  const int sh = (sb & 1) * 4;
-#pragma unroll
-  for (int j = 0; j < 8; ++j) y[j] = __fsub_rn(__fmul_rn(dl, static_cast<float>((qs[j] >> sh) & 15)), ml);
-}
-
-__device__ __forceinline__ void dec8_q5_k(const uint8_t* u, int i, float (&y)[8]) {
-  const float d = ld_f16(u), dmin = ld_f16(u + 2);
-  const int sb = i >> 2;
-  int sc, mn;
-  k4_scale_min(u + 4, sb, sc, mn);
-  const float dl = __fmul_rn(d, static_cast<float>(sc));
-  const float ml = __fmul_rn(dmin, static_cast<float>(mn));
-  const int l0 = 8 * (i & 3);
-  const uint8_t* qh = u + 16 + l0;
-  const uint8_t* qs = u + 48 + 32 * (sb >> 1) + l0;
-  const int sh = (sb & 1) * 4;
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    const int q = ((qs[j] >> sh) & 15) + 16 * ((qh[j] >> sb) & 1);
-    y[j] = __fsub_rn(__fmul_rn(dl, static_cast<float>(q)), ml);
+    for (int j = 0; j < 8; ++j) {
+      const uint32_t q = ((j < 4 ? a : b) >> (8 * (j & 3) + sh)) & 15u;
+      y[j] = __fsub_rn(__fmul_rn(dl, u2f(q)), ml);
+    }
   }
-}
+};
 
-__device__ __forceinline__ void dec8_q6_k(const uint8_t* u, int i, float (&y)[8]) {
-  const int e0 = 8 * i;
-  const int h = e0 >> 7, g = (e0 >> 5) & 3, l0 = e0 & 31;
-  const uint8_t* ql = u + 64 * h + 32 * (g & 1) + l0;
-  const uint8_t* qh = u + 128 + 32 * h + l0;
-  const int8_t sc = reinterpret_cast<const int8_t*>(u + 192)[8 * h + (l0 >> 4) + 2 * g];
-  const float d = ld_f16(u + 208);
-  const float ds = __fmul_rn(d, static_cast<float>(sc));
-  const int lsh = (g >> 1) * 4, hsh = 2 * g;
+template <>
+struct Dec<kQ5_K> {
+  __device__ __forceinline__ static void run(const uint32_t* s, int i, float (&y)[8]) {
+    const uint32_t w0 = s[0];
+    const float d = h2f(w0), dmin = h2f(w0 >> 16);
+    const int sb = i >> 2;
+    uint32_t sc, mn;
+    k4_scale_min_w(s, sb, sc, mn);
+    const float dl = __fmul_rn(d, u2f(sc));
+    const float ml = __fmul_rn(dmin, u2f(mn));
+    const int l0 = 8 * (i & 3);
+    uint32_t ha, hb, qa, qb;
+    ld2(s, 16 + l0, ha, hb);
+    ld2(s, 48 + 32 * (sb >> 1) + l0, qa, qb);
+    const uint32_t sh = (sb & 1) * 4;
 #pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    const int q = ((ql[j] >> lsh) & 15) | (((qh[j] >> hsh) & 3) << 4);
-    y[j] = __fmul_rn(ds, static_cast<float>(q - 32));
+    for (int j = 0; j < 8; ++j) {
+      const uint32_t bsh = 8 * (j & 3);
+      const uint32_t q = (((j < 4 ? qa : qb) >> (bsh + sh)) & 15u) | ((((j < 4 ? ha : hb) >> (bsh + sb)) & 1u) << 4);
+      y[j] = __fsub_rn(__fmul_rn(dl, u2f(q)), ml);
+    }
   }
-}
+};
 
-__device__ __forceinline__ void dec8_q2_k(const uint8_t* u, int i, float (&y)[8]) {
-  const int e0 = 8 * i;
-  const int h = e0 >> 7, s = (e0 >> 5) & 3, l0 = e0 & 31;
-  const int scb = u[e0 >> 4];
-  const float d = ld_f16(u + 80), dmin = ld_f16(u + 82);
-  const float dl = __fmul_rn(d, static_cast<float>(scb & 15));
-  const float ml = __fmul_rn(dmin, static_cast<float>(scb >> 4));
-  const uint8_t* qs = u + 16 + 32 * h + l0;
+template <>
+struct Dec<kQ6_K> {
+  __device__ __forceinline__ static void run(const uint32_t* s, int i, float (&y)[8]) {
+    const int h = i >> 4, g = (i >> 2) & 3, l0 = 8 * (i & 3);
+    uint32_t la, lb, ha, hb;
+    ld2(s, 64 * h + 32 * (g & 1) + l0, la, lb);
+    ld2(s, 128 + 32 * h + l0, ha, hb);
+    const int so = 192 + 8 * h + (l0 >> 4) + 2 * g;
+    const int sc = static_cast<int>(static_cast<int8_t>(byte_of(s, so)));
+    const float d = h2f(s[52]);  // byte 208
+    const float ds = __fmul_rn(d, u2f(static_cast<uint32_t>(sc + 128)) - 128.0f);
+    const uint32_t lsh = (g >> 1) * 4, hsh = 2 * g;
 #pragma unroll
-  for (int j = 0; j < 8; ++j) y[j] = __fsub_rn(__fmul_rn(dl, static_cast<float>((qs[j] >> (2 * s)) & 3)), ml);
-}
-
-__device__ __forceinline__ int q3k_scale(const uint8_t* sc12, int j) {
-  const int lo = (sc12[j & 7] >> (4 * (j >> 3))) & 15;
-  const int hi = (sc12[8 + (j & 3)] >> (2 * (j >> 2))) & 3;
-  return (lo | (hi << 4)) - 32;
-}
-
-__device__ __forceinline__ void dec8_q3_k(const uint8_t* u, int i, float (&y)[8]) {
-  const int e0 = 8 * i;
-  const int h = e0 >> 7, s = (e0 >> 5) & 3, l0 = e0 & 31, hb = e0 >> 5;
-  const float d = ld_f16(u + 108);
-  const float dl = __fmul_rn(d, static_cast<float>(q3k_scale(u + 96, e0 >> 4)));
-  const uint8_t* hm = u + l0;
-  const uint8_t* qs = u + 32 + 32 * h + l0;
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    const int q = ((qs[j] >> (2 * s)) & 3) - 4 * (((hm[j] >> hb) & 1) ^ 1);
-    y[j] = __fmul_rn(dl, static_cast<float>(q));
+    for (int j = 0; j < 8; ++j) {
+      const uint32_t bsh = 8 * (j & 3);
+      const uint32_t q = (((j < 4 ? la : lb) >> (bsh + lsh)) & 15u) | ((((j < 4 ? ha : hb) >> (bsh + hsh)) & 3u) << 4);
+      y[j] = __fmul_rn(ds, u2f(q) - 32.0f);
+    }
   }
-}
+};
 
-__constant__ float kIQ4NL[16] = {-127.f, -104.f, -83.f, -65.f, -49.f, -35.f, -22.f, -10.f,
-                                 1.f,    13.f,   25.f,  38.f,  53.f,  69.f,  89.f,  113.f};
-
-__device__ __forceinline__ void dec8_iq4_xs(const uint8_t* u, int i, float (&y)[8]) {
-  const int ib = i >> 2, part = i & 3;  // 32-element sub-block, quarter within it
-  const float d = ld_f16(u);
-  const int sh = *reinterpret_cast<const unsigned short*>(u + 2);
-  const int ls = ((u[4 + (ib >> 1)] >> (4 * (ib & 1))) & 15) | (((sh >> (2 * ib)) & 3) << 4);
-  const float dl = __fmul_rn(d, static_cast<float>(ls - 32));
-  const uint8_t* qs = u + 8 + 16 * ib + 8 * (part & 1);
-  const int nsh = (part >> 1) * 4;
+template <>
+struct Dec<kQ2_K> {
+  __device__ __forceinline__ static void run(const uint32_t* s, int i, float (&y)[8]) {
+    const int h = i >> 4, sft = (i >> 2) & 3, l0 = 8 * (i & 3);
+    const uint32_t scb = byte_of(s, i >> 1);
+    const uint32_t wd = s[20];  // bytes 80..83: d, dmin
+    const float dl = __fmul_rn(h2f(wd), u2f(scb & 15u));
+    const float ml = __fmul_rn(h2f(wd >> 16), u2f(scb >> 4));
+    uint32_t a, b;
+    ld2(s, 16 + 32 * h + l0, a, b);
 #pragma unroll
-  for (int j = 0; j < 8; ++j) y[j] = __fmul_rn(dl, kIQ4NL[(qs[j] >> nsh) & 15]);
+    for (int j = 0; j < 8; ++j) {
+      const uint32_t q = ((j < 4 ? a : b) >> (8 * (j & 3) + 2 * sft)) & 3u;
+      y[j] = __fsub_rn(__fmul_rn(dl, u2f(q)), ml);
+    }
+  }
+};
+
+template <>
+struct Dec<kQ3_K> {
+  __device__ __forceinline__ static void run(const uint32_t* s, int i, float (&y)[8]) {
+    const int h = i >> 4, sft = (i >> 2) & 3, l0 = 8 * (i & 3), hbit = i >> 2;
+    const int j16 = i >> 1;
+    const uint32_t lo = (byte_of(s, 96 + (j16 & 7)) >> (4 * (j16 >> 3))) & 15u;
+    const uint32_t hi = (byte_of(s, 104 + (j16 & 3)) >> (2 * (j16 >> 2))) & 3u;
+    const float d = h2f(s[27]);  // byte 108
+    const float dl = __fmul_rn(d, u2f(lo | (hi << 4)) - 32.0f);
+    uint32_t ma, mb, qa, qb;
+    ld2(s, l0, ma, mb);
+    ld2(s, 32 + 32 * h + l0, qa, qb);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const uint32_t bsh = 8 * (j & 3);
+      const uint32_t low = ((j < 4 ? qa : qb) >> (bsh + 2 * sft)) & 3u;
+      const uint32_t hb = ((j < 4 ? ma : mb) >> (bsh + hbit)) & 1u;
+      y[j] = __fmul_rn(dl, u2f(low + 4u * hb) - 4.0f);  // low - 4 * (1 - hb)
+    }
+  }
+};
+
+// IQ4_NL code book packed as signed bytes (public GGUF constant).
+__device__ __forceinline__ int8_t iq4nl(uint32_t idx) {
+  constexpr uint32_t k0 = 0xBFAD9881u;  // -127 -104 -83 -65
+  constexpr uint32_t k1 = 0xF6EADDCFu;  // -49 -35 -22 -10
+  constexpr uint32_t k2 = 0x26190D01u;  // 1 13 25 38
+  constexpr uint32_t k3 = 0x71594535u;  // 53 69 89 113
+  const uint32_t lo = (idx & 8u) ? k2 : k0;
+  const uint32_t hi = (idx & 8u) ? k3 : k1;
+  return static_cast<int8_t>(__byte_perm(lo, hi, idx & 7u) & 0xFFu);
 }
 
-// Decode elements 8*i..8*i+7 of a unit.  Returns false for an unknown format.
-__device__ __forceinline__ bool dec8(int fmt, const uint8_t* unit, int i, float (&y)[8]) {
+template <>
+struct Dec<kIQ4_XS> {
+  __device__ __forceinline__ static void run(const uint32_t* s, int i, float (&y)[8]) {
+    const int ib = i >> 2, part = i & 3;
+    const uint32_t w0 = s[0];
+    const float d = h2f(w0);
+    const uint32_t shv = w0 >> 16;
+    const uint32_t ls = ((byte_of(s, 4 + (ib >> 1)) >> (4 * (ib & 1))) & 15u) | (((shv >> (2 * ib)) & 3u) << 4);
+    const float dl = __fmul_rn(d, u2f(ls) - 32.0f);
+    uint32_t a, b;
+    ld2(s, 8 + 16 * ib + 8 * (part & 1), a, b);
+    const uint32_t nsh = (part >> 1) * 4;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const uint32_t idx = ((j < 4 ? a : b) >> (8 * (j & 3) + nsh)) & 15u;
+      y[j] = __fmul_rn(dl, u2f(static_cast<uint32_t>(iq4nl(idx) + 128)) - 128.0f);
+    }
+  }
+};
+
+// --------------------------------------------------- affine decoders (mix / gate-grad)
+// Aff<F>::run(slot, i, a, b, q) gives, for elements 8i..8i+7 of a unit, the
+// exact small-integer codes q[j] (as floats) and one scale/offset pair with
+// w[j] = a * q[j] + b.  a and b are the same float32 products the exact
+// decoders form (d*sc, -dmin*m), so a*q + b equals the exact decode up to the
+// final rounding; the mixture and gate-gradient kernels (tolerance-checked)
+// use this form to spend one FMA per weight instead of a multiply-subtract.
+template <int F>
+struct Aff;
+
+template <>
+struct Aff<kQ8_0> {
+  __device__ __forceinline__ static void run(const uint32_t* s, int i, float& a, float& b, float (&q)[8]) {
+    const int bi = i >> 2;
+    const int dof = 34 * bi;
+    a = h2f(s[dof >> 2] >> (8 * (dof & 2)));
+    b = 0.f;
+    const int off = dof + 2 + 8 * (i & 3);
+    const int al = off & ~3;
+    const uint32_t sh = static_cast<uint32_t>(off & 3) * 8u;
+    const uint32_t w0 = s[al >> 2], w1 = s[(al >> 2) + 1];
+    const uint32_t w2 = sh ? s[(al >> 2) + 2] : 0u;
+    const uint32_t q0 = __funnelshift_r(w0, w1, sh) ^ 0x80808080u, q1 = __funnelshift_r(w1, w2, sh) ^ 0x80808080u;
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      q[j] = __uint_as_float(__byte_perm(j < 4 ? q0 : q1, 0x4B000000u, 0x7440u + (j & 3))) - 8388736.0f;
+  }
+};
+
+template <>
+struct Aff<kQ4_K> {
+  __device__ __forceinline__ static void run(const uint32_t* s, int i, float& a, float& b, float (&q)[8]) {
+    const uint32_t w0 = s[0];
+    const int sb = i >> 2;
+    uint32_t sc, mn;
+    k4_scale_min_w(s, sb, sc, mn);
+    a = __fmul_rn(h2f(w0), u2f(sc));
+    b = -__fmul_rn(h2f(w0 >> 16), u2f(mn));
+    uint32_t x, y;
+    ld2(s, 16 + 32 * (sb >> 1) + 8 * (i & 3), x, y);
+    const uint32_t sh = (sb & 1) * 4;
+    x = (x >> sh) & 0x0F0F0F0Fu;
+    y = (y >> sh) & 0x0F0F0F0Fu;
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      q[j] = __uint_as_float(__byte_perm(j < 4 ? x : y, 0x4B000000u, 0x7440u + (j & 3))) - 8388608.0f;
+  }
+};
+
+template <>
+struct Aff<kQ5_K> {
+  __device__ __forceinline__ static void run(const uint32_t* s, int i, float& a, float& b, float (&q)[8]) {
+    const uint32_t w0 = s[0];
+    const int sb = i >> 2;
+    uint32_t sc, mn;
+    k4_scale_min_w(s, sb, sc, mn);
+    a = __fmul_rn(h2f(w0), u2f(sc));
+    b = -__fmul_rn(h2f(w0 >> 16), u2f(mn));
+    const int l0 = 8 * (i & 3);
+    uint32_t ha, hb, x, y;
+    ld2(s, 16 + l0, ha, hb);
+    ld2(s, 48 + 32 * (sb >> 1) + l0, x, y);
+    const uint32_t sh = (sb & 1) * 4;
+    x = ((x >> sh) & 0x0F0F0F0Fu) | (((ha >> sb) & 0x01010101u) << 4);
+    y = ((y >> sh) & 0x0F0F0F0Fu) | (((hb >> sb) & 0x01010101u) << 4);
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      q[j] = __uint_as_float(__byte_perm(j < 4 ? x : y, 0x4B000000u, 0x7440u + (j & 3))) - 8388608.0f;
+  }
+};
+
+template <>
+struct Aff<kQ6_K> {
+  __device__ __forceinline__ static void run(const uint32_t* s, int i, float& a, float& b, float (&q)[8]) {
+    const int h = i >> 4, g = (i >> 2) & 3, l0 = 8 * (i & 3);
+    uint32_t la, lb, ha, hb;
+    ld2(s, 64 * h + 32 * (g & 1) + l0, la, lb);
+    ld2(s, 128 + 32 * h + l0, ha, hb);
+    const int sc = static_cast<int>(static_cast<int8_t>(byte_of(s, 192 + 8 * h + (l0 >> 4) + 2 * g)));
+    a = __fmul_rn(h2f(s[52]), u2f(static_cast<uint32_t>(sc + 128)) - 128.0f);
+    b = 0.f;
+    const uint32_t lsh = (g >> 1) * 4, hsh = 2 * g;
+    const uint32_t x = ((la >> lsh) & 0x0F0F0F0Fu) | (((ha >> hsh) & 0x03030303u) << 4);
+    const uint32_t y = ((lb >> lsh) & 0x0F0F0F0Fu) | (((hb >> hsh) & 0x03030303u) << 4);
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      q[j] = __uint_as_float(__byte_perm(j < 4 ? x : y, 0x4B000000u, 0x7440u + (j & 3))) - 8388640.0f;  // q - 32
+  }
+};
+
+template <>
+struct Aff<kQ2_K> {
+  __device__ __forceinline__ static void run(const uint32_t* s, int i, float& a, float& b, float (&q)[8]) {
+    const int h = i >> 4, sft = (i >> 2) & 3, l0 = 8 * (i & 3);
+    const uint32_t scb = byte_of(s, i >> 1);
+    const uint32_t wd = s[20];
+    a = __fmul_rn(h2f(wd), u2f(scb & 15u));
+    b = -__fmul_rn(h2f(wd >> 16), u2f(scb >> 4));
+    uint32_t x, y;
+    ld2(s, 16 + 32 * h + l0, x, y);
+    x = (x >> (2 * sft)) & 0x03030303u;
+    y = (y >> (2 * sft)) & 0x03030303u;
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      q[j] = __uint_as_float(__byte_perm(j < 4 ? x : y, 0x4B000000u, 0x7440u + (j & 3))) - 8388608.0f;
+  }
+};
+
+template <>
+struct Aff<kQ3_K> {
+  __device__ __forceinline__ static void run(const uint32_t* s, int i, float& a, float& b, float (&q)[8]) {
+    const int h = i >> 4, sft = (i >> 2) & 3, l0 = 8 * (i & 3), hbit = i >> 2;
+    const int j16 = i >> 1;
+    const uint32_t lo = (byte_of(s, 96 + (j16 & 7)) >> (4 * (j16 >> 3))) & 15u;
+    const uint32_t hi = (byte_of(s, 104 + (j16 & 3)) >> (2 * (j16 >> 2))) & 3u;
+    a = __fmul_rn(h2f(s[27]), u2f(lo | (hi << 4)) - 32.0f);
+    b = 0.f;
+    uint32_t ma, mb, x, y;
+    ld2(s, l0, ma, mb);
+    ld2(s, 32 + 32 * h + l0, x, y);
+    x = ((x >> (2 * sft)) & 0x03030303u) | (((ma >> hbit) & 0x01010101u) << 2);
+    y = ((y >> (2 * sft)) & 0x03030303u) | (((mb >> hbit) & 0x01010101u) << 2);
+#pragma unroll
+    for (int j = 0; j < 8; ++j)  // value = low + 4*hb - 4
+      q[j] = __uint_as_float(__byte_perm(j < 4 ? x : y, 0x4B000000u, 0x7440u + (j & 3))) - 8388612.0f;
+  }
+};
+
+template <>
+struct Aff<kIQ4_XS> {
+  __device__ __forceinline__ static void run(const uint32_t* s, int i, float& a, float& b, float (&q)[8]) {
+    const int ib = i >> 2, part = i & 3;
+    const uint32_t w0 = s[0];
+    const uint32_t shv = w0 >> 16;
+    const uint32_t ls = ((byte_of(s, 4 + (ib >> 1)) >> (4 * (ib & 1))) & 15u) | (((shv >> (2 * ib)) & 3u) << 4);
+    a = __fmul_rn(h2f(w0), u2f(ls) - 32.0f);
+    b = 0.f;
+    uint32_t x, y;
+    ld2(s, 8 + 16 * ib + 8 * (part & 1), x, y);
+    const uint32_t nsh = (part >> 1) * 4;
+    x = (x >> nsh) & 0x0F0F0F0Fu;
+    y = (y >> nsh) & 0x0F0F0F0Fu;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const uint32_t idx = ((j < 4 ? x : y) >> (8 * (j & 3))) & 15u;
+      q[j] = u2f(static_cast<uint32_t>(iq4nl(idx) + 128)) - 128.0f;
+    }
+  }
+};
+
+// Runtime dispatch (formats are uniform per candidate, so no divergence).
+__device__ __forceinline__ bool dec8(int fmt, const uint32_t* slot, int i, float (&y)[8]) {
   switch (fmt) {
-    case kQ8_0: dec8_q8_0(unit, i, y); return true;
-    case kQ2_K: dec8_q2_k(unit, i, y); return true;
-    case kQ3_K: dec8_q3_k(unit, i, y); return true;
-    case kQ4_K: dec8_q4_k(unit, i, y); return true;
-    case kQ5_K: dec8_q5_k(unit, i, y); return true;
-    case kQ6_K: dec8_q6_k(unit, i, y); return true;
-    case kIQ4_XS: dec8_iq4_xs(unit, i, y); return true;
+    case kQ8_0: Dec<kQ8_0>::run(slot, i, y); return true;
+    case kQ2_K: Dec<kQ2_K>::run(slot, i, y); return true;
+    case kQ3_K: Dec<kQ3_K>::run(slot, i, y); return true;
+    case kQ4_K: Dec<kQ4_K>::run(slot, i, y); return true;
+    case kQ5_K: Dec<kQ5_K>::run(slot, i, y); return true;
+    case kQ6_K: Dec<kQ6_K>::run(slot, i, y); return true;
+    case kIQ4_XS: Dec<kIQ4_XS>::run(slot, i, y); return true;
     default:
 #pragma unroll
       for (int j = 0; j < 8; ++j) y[j] = 0.f;

@@ -44,14 +44,24 @@ constexpr int GROUP_N = 8;            // raster: tiles sweep M inside a band of 
 constexpr int kEpiStoreBf16 = 0;
 constexpr int kEpiGateGrad = 1;
 
+// Shared memory: STAGES x (A, B) operand slices, the mbarriers, and for the
+// gate-gradient epilogue one staging area per epilogue warp (32 rows x one
+// candidate unit, row pitch kStagePitch words: odd, so the 32 rows of a warp
+// fall in 32 different banks).  The dynamic shared-memory window starts
+// 1024-byte aligned on sm_100 (checked at run time), as SWIZZLE_128B needs.
+constexpr int kStagePitch = kMaxUnitWords + 1;  // 69 words
+
+template <int kEpi>
 struct SmemLayout {
   static constexpr int a_off = 0;
   static constexpr int b_off = a_off + STAGES * A_STAGE;
   static constexpr int bar_off = b_off + STAGES * B_STAGE;      // 8-byte barriers
   static constexpr int n_bars = 2 * STAGES + 4;
   static constexpr int misc_off = bar_off + n_bars * 8;         // tmem base, abort flag
-  static constexpr int total = misc_off + 16;
-  static constexpr int alloc = total + 1024;                    // slack for 1 KiB alignment
+  static constexpr int stage_off = misc_off + 16;
+  static constexpr int stage_words_per_warp = 32 * kStagePitch;
+  static constexpr int stage_bytes = (kEpi == 1) ? 4 * stage_words_per_warp * 4 : 0;
+  static constexpr int total = stage_off + stage_bytes;
 };
 
 struct Params {
@@ -78,19 +88,93 @@ __device__ __forceinline__ void tile_coords(const Params& p, int tile, int& m_bl
   n_blk = first_n + (r - m_blk * gn);
 }
 
+// Stage unit n_blk of rows row0 .. row0+31 (one candidate) into the warp's
+// slot rows (pitch kStagePitch words).  Lane l copies words l, l+32, l+64 of
+// every row; all loads of 8 rows are issued before their stores, so many
+// independent loads are in flight.
+__device__ __forceinline__ void stage_rows_warp(uint32_t* dst, const uint8_t* cbase, long long row0, int M,
+                                                int upr, int n_blk, int ub, int lane) {
+  const int nw = (ub + 3) >> 2;
+#pragma unroll 1
+  for (int r0 = 0; r0 < 32; r0 += 8) {
+    uint32_t lo[8][3], hi[8][3], shv[8];
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+      const long long rr = row0 + r0 + r;
+      const bool ok = rr < M;
+      const uintptr_t a = reinterpret_cast<uintptr_t>(cbase + (ok ? (rr * upr + n_blk) * ub : 0));
+      const uint32_t* s = reinterpret_cast<const uint32_t*>(a & ~uintptr_t(3));
+      shv[r] = static_cast<uint32_t>(a & 3u) * 8u;
+#pragma unroll
+      for (int j = 0; j < 3; ++j) {
+        const int w = lane + 32 * j;
+        lo[r][j] = (ok && w < nw) ? __ldg(s + w) : 0u;
+        hi[r][j] = (ok && w < nw && shv[r] != 0u && 4 * w + 3 <= ub) ? __ldg(s + w + 1) : 0u;
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+#pragma unroll
+      for (int j = 0; j < 3; ++j) {
+        const int w = lane + 32 * j;
+        if (w < nw) dst[(r0 + r) * kStagePitch + w] = __funnelshift_r(lo[r][j], hi[r][j], shv[r]);
+      }
+    }
+  }
+}
+
+// Dot of one dW row (256 TMEM columns at t_row, fp32) with the decoded unit
+// in `slot` (this thread's row); columns at or beyond `cols` are skipped.
+// Uses the affine decode w = a*q + b per 8 weights:
+//   sum_j v_j w_j = a * sum_j v_j q_j + b * sum_j v_j.
+// All 32 lanes must call it (tcgen05.ld is warp-collective).
+template <int F>
+__device__ __forceinline__ float row_dot(const uint32_t* slot, uint32_t t_row, long long colbase, long long cols,
+                                         bool row_ok) {
+  float s = 0.f;
+#pragma unroll 1
+  for (int c = 0; c < BN / 32; ++c) {
+    float v[32];
+    tmem_ld_32cols(t_row + c * 32, v);
+    const long long col0 = colbase + c * 32;
+    if (row_ok && col0 < cols) {
+      const bool full = col0 + 32 <= cols;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        float a, b, w[8];
+        Aff<F>::run(slot, 4 * c + q, a, b, w);
+        float s1 = 0.f, s0 = 0.f;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float vj = (full || col0 + 8 * q + j < cols) ? v[8 * q + j] : 0.f;
+          s1 = fmaf(vj, w[j], s1);
+          s0 += vj;
+        }
+        s = fmaf(a, s1, s);
+        s = fmaf(b, s0, s);
+      }
+    }
+  }
+  return s;
+}
+
 template <bool kAmn, bool kBmn, int kEpi>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Params p) {
-  extern __shared__ __align__(1024) uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  using SL = SmemLayout<kEpi>;
+  extern __shared__ __align__(1024) uint8_t smem[];
   const uint32_t sbase = smem_u32(smem);
-  const uint32_t bar0 = sbase + SmemLayout::bar_off;
+  if ((sbase & 1023u) != 0) {  // uniform across the CTA: nothing has started yet
+    if (threadIdx.x == 0) report_error(p.err, kDevBadSmemAlign, 0);
+    return;
+  }
+  const uint32_t bar0 = sbase + SL::bar_off;
   auto full_bar = [&](int s) { return bar0 + 8u * s; };
   auto empty_bar = [&](int s) { return bar0 + 8u * (STAGES + s); };
   auto tfull_bar = [&](int a) { return bar0 + 8u * (2 * STAGES + a); };
   auto tempty_bar = [&](int a) { return bar0 + 8u * (2 * STAGES + 2 + a); };
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + SmemLayout::misc_off);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + SmemLayout::misc_off + 4);
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + SL::misc_off);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + SL::misc_off + 4);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -136,8 +220,8 @@ __global__ void __launch_bounds__(THREADS, 1)
             break;
           }
           mbar_arrive_expect_tx(full_bar(s), A_STAGE + B_STAGE);
-          const uint32_t a_dst = sbase + SmemLayout::a_off + s * A_STAGE;
-          const uint32_t b_dst = sbase + SmemLayout::b_off + s * B_STAGE;
+          const uint32_t a_dst = sbase + SL::a_off + s * A_STAGE;
+          const uint32_t b_dst = sbase + SL::b_off + s * B_STAGE;
           const int k0 = kb * BK;
           if (kAmn) {
 #pragma unroll
@@ -178,8 +262,8 @@ __global__ void __launch_bounds__(THREADS, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t a_addr = sbase + SmemLayout::a_off + s * A_STAGE;
-          const uint32_t b_addr = sbase + SmemLayout::b_off + s * B_STAGE;
+          const uint32_t a_addr = sbase + SL::a_off + s * A_STAGE;
+          const uint32_t b_addr = sbase + SL::b_off + s * B_STAGE;
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk) {
             // K-major: +32 bytes per 16-element K step inside the swizzle row.
@@ -233,40 +317,36 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
         }
       } else {
-        float g[kMaxCandidates];
-#pragma unroll
-        for (int k = 0; k < kMaxCandidates; ++k) g[k] = 0.f;
-        const bool row_ok = row < p.M;
-        const long long unit = row * p.units_per_row + n_blk;
-        for (int c = 0; c < BN / 32; ++c) {
-          float v[32];
-          tmem_ld_32cols(t_row + c * 32, v);
-          const long long col0 = static_cast<long long>(n_blk) * BN + c * 32;
-          if (!row_ok || col0 >= p.cols) continue;
-          const bool full = col0 + 32 <= p.cols;
-          for (int k = 0; k < p.cands.K; ++k) {
-            const uint8_t* u = p.cands.ptr[k] + unit * p.cands.ubytes[k];
-            float s = 0.f;
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              float w[8];
-              dec8(p.cands.fmt[k], u, 4 * c + q, w);
-#pragma unroll
-              for (int j = 0; j < 8; ++j) {
-                if (full || col0 + 8 * q + j < p.cols) s = fmaf(v[8 * q + j], w[j], s);
-              }
-            }
-            g[k] += s;
-          }
-        }
-        // fixed-order reduction: warp butterfly; each epilogue warp writes its
-        // own partial (no cross-warp synchronisation inside the epilogue)
+        // Gate-gradient epilogue.  For each candidate: the warp stages the 32
+        // rows' units (one 256-column unit per row) into its shared slot rows
+        // with coalesced aligned loads, then each thread decodes its own row
+        // from shared memory and dots it with the dW row read back from TMEM.
+        uint32_t* my_stage = reinterpret_cast<uint32_t*>(smem + SL::stage_off) + wq * SL::stage_words_per_warp;
+        const long long row0 = static_cast<long long>(m_blk) * BM + 32 * wq;
         const long long slot = (static_cast<long long>(m_blk) * p.num_n_blk + n_blk) * 4 + wq;
+        const bool row_ok = row < p.M;
+        const long long colbase = static_cast<long long>(n_blk) * BN;
         for (int k = 0; k < p.cands.K; ++k) {
-          float s = g[k];
+          const int ub = p.cands.ubytes[k];
+          const uint8_t* cbase = p.cands.ptr[k];
+          stage_rows_warp(my_stage, cbase, row0, p.M, p.units_per_row, n_blk, ub, lane);
+          __syncwarp();
+          const uint32_t* slot_row = my_stage + lane * kStagePitch;
+          float s = 0.f;
+          switch (p.cands.fmt[k]) {
+            case kQ8_0: s = row_dot<kQ8_0>(slot_row, t_row, colbase, p.cols, row_ok); break;
+            case kQ2_K: s = row_dot<kQ2_K>(slot_row, t_row, colbase, p.cols, row_ok); break;
+            case kQ3_K: s = row_dot<kQ3_K>(slot_row, t_row, colbase, p.cols, row_ok); break;
+            case kQ4_K: s = row_dot<kQ4_K>(slot_row, t_row, colbase, p.cols, row_ok); break;
+            case kQ5_K: s = row_dot<kQ5_K>(slot_row, t_row, colbase, p.cols, row_ok); break;
+            case kQ6_K: s = row_dot<kQ6_K>(slot_row, t_row, colbase, p.cols, row_ok); break;
+            case kIQ4_XS: s = row_dot<kIQ4_XS>(slot_row, t_row, colbase, p.cols, row_ok); break;
+            default: s = row_dot<kQ8_0>(slot_row, t_row, colbase, 0, false); break;  // keeps TMEM loads uniform
+          }
 #pragma unroll
           for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
           if (lane == 0) p.partials[slot * p.cands.K + k] = s;
+          __syncwarp();
         }
       }
       tc_fence_before();

@@ -142,9 +142,10 @@ int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, vq::gemm::Params p
   int sms = 0;
   if (int rc = sm_count(&sms)) return rc;
   auto kern = gemm_kernel<kAmn, kBmn, kEpi>;
-  VQ_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SmemLayout::alloc));
+  constexpr int smem = SmemLayout<kEpi>::total;
+  VQ_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
   const int grid = p.num_tiles < sms ? p.num_tiles : sms;
-  kern<<<grid, THREADS, SmemLayout::alloc, st>>>(ta, tb, p);
+  kern<<<grid, THREADS, smem, st>>>(ta, tb, p);
   VQ_CUDA(cudaGetLastError());
   return 0;
 }
