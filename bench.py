@@ -420,6 +420,34 @@ def run_reference(args):
     print(json.dumps(out), flush=True)
 
 
+def run_ncu_case():
+    """One launch each of the mix, gate-gradient and loss kernels at sizes an
+    ncu --set full capture finishes quickly (inputs still larger than L2):
+    config-2 candidates, gate gradient at T=4096, loss 1024 x 128256."""
+    import torch
+    from voodoo_quant import _C
+    from voodoo_quant.quants import rtn
+
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(0)
+    w = torch.randn(N_OUT, K_IN, device=dev, generator=g) * 0.02
+    blocks = [rtn.quantize(w, q) for q in TYPES]
+    del w
+    probs = torch.softmax(torch.randn(len(TYPES), device=dev, generator=g), 0)
+    _C.mix(TYPES, blocks, probs, N_OUT, K_IN, K_IN)
+    x = torch.randn(4096, K_IN, device=dev, generator=g).to(torch.bfloat16)
+    dy = torch.randn(4096, N_OUT, device=dev, generator=g).to(torch.bfloat16)
+    _C.gategrad(dy, x, TYPES, blocks, N_OUT, K_IN, K_IN)
+    V, R = 128256, 1024
+    s = (torch.randn(R, V, device=dev, generator=g) * 3).to(torch.bfloat16)
+    t = (torch.randn(R, V, device=dev, generator=g) * 3).to(torch.bfloat16)
+    y = torch.randint(0, V, (R,), device=dev, generator=g)
+    _C.loss_fused(s, t, y, 1.0, 1.0 / R, 1.0 / R)
+    torch.cuda.synchronize()
+    assert _C.device_error() == 0
+    print("ncu case ok", flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -430,8 +458,11 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--cpu-tokens", type=int, default=2048)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--ncu-case", action="store_true", help="one launch per kernel at profiling sizes")
     args = ap.parse_args()
-    if args.impl == "reference":
+    if args.ncu_case:
+        run_ncu_case()
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_gpu(args)

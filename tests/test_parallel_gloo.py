@@ -1,0 +1,165 @@
+"""Tensor-parallel host logic on CPU: gloo process groups of world size 2.
+
+Covers the pieces of voodoo_quant.parallel that need no GPU: block-aligned
+(uneven) splits, packed-block slicing invariants, the differentiable
+all-reduce, the exact input-gradient ("f") operator and the flat gate-gradient
+all-reduce.  The multi-block gradient test reproduces the reference's TP gate
+gradient error (column-parallel layers without an input all-reduce) and shows
+the f operator removes it.
+"""
+
+from __future__ import annotations
+
+import os
+import socket
+import tempfile
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def test_block_aligned_split_uneven():
+    from voodoo_quant.parallel import block_aligned_split
+
+    parts = [block_aligned_split(25600, 8, r) for r in range(8)]
+    assert [n // 256 for _, n in parts] == [13, 13, 13, 13, 12, 12, 12, 12]
+    assert parts[0][0] == 0 and all(parts[i][0] + parts[i][1] == parts[i + 1][0] for i in range(7))
+    assert sum(n for _, n in parts) == 25600
+    assert [n // 256 for _, n in (block_aligned_split(5120, 8, r) for r in range(8))] == [3, 3, 3, 3, 2, 2, 2, 2]
+    with pytest.raises(ValueError):
+        block_aligned_split(1000, 2, 0)
+    with pytest.raises(ValueError):
+        block_aligned_split(512, 4, 0)
+
+
+@pytest.mark.parametrize("fmt", ["Q4_K", "Q8_0", "Q6_K", "Q3_K", "IQ4_XS"])
+def test_slice_qbytes_equals_quantizing_the_slice(fmt):
+    """Row and 256-aligned column slices of packed blocks equal packing the
+    slice (block-local formats), the invariant of the reference's
+    tests/test_invariants.py:21-53."""
+    from voodoo_quant.parallel import ShardSpec
+    from voodoo_quant.quants import rtn
+
+    torch.manual_seed(0)
+    w = torch.randn(48, 1024) * 0.02
+    full = rtn.quantize(w, fmt)
+    rs = ShardSpec(full_out=48, full_in=1024, row_offset=16, row_len=20)
+    assert torch.equal(rs.slice_qbytes(full, fmt, 1024), rtn.quantize(w[16:36], fmt))
+    cs = ShardSpec(full_out=48, full_in=1024, col_offset=256, col_len=512)
+    assert torch.equal(cs.slice_qbytes(full, fmt, 1024).reshape(-1), rtn.quantize(w[:, 256:768], fmt).reshape(-1))
+    bad = ShardSpec(full_out=48, full_in=1024, col_offset=128, col_len=256)
+    with pytest.raises(ValueError, match="aligned"):
+        bad.slice_qbytes(full, fmt, 1024)
+
+
+def _blocks(torch_mod, d, h):
+    g = torch.Generator().manual_seed(7)
+    mk = lambda o, i: torch_mod.nn.Linear(i, o, bias=False).double()
+    blocks = []
+    for _ in range(2):
+        b = torch.nn.Module()
+        b.mlp = torch.nn.Module()
+        b.mlp.gate_proj = mk(h, d)
+        b.mlp.up_proj = mk(h, d)
+        b.mlp.down_proj = mk(d, h)
+        for lin in (b.mlp.gate_proj, b.mlp.up_proj, b.mlp.down_proj):
+            with torch.no_grad():
+                lin.weight.copy_(torch.randn(lin.weight.shape, generator=g, dtype=torch.float64) * 0.1)
+        blocks.append(b)
+    return blocks
+
+
+def _mlp_forward(mlp, x, gate):
+    return mlp.down_proj(torch.nn.functional.silu(mlp.gate_proj(x) * gate) * mlp.up_proj(x))
+
+
+class _MLP(torch.nn.Module):
+    def __init__(self, inner, gate):
+        super().__init__()
+        self.gate_proj, self.up_proj, self.down_proj = inner.gate_proj, inner.up_proj, inner.down_proj
+        self.g = gate
+
+    def forward(self, x):
+        return _mlp_forward(self, x, self.g)
+
+
+def _worker(rank, world, port, outdir, exact):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    import torch.distributed as dist
+    from voodoo_quant import parallel as P
+
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        P.adopt_process_group(0)
+        P.TP.exact_input_grad = exact
+        d, h, T = 256, 512, 6
+        torch.manual_seed(3)
+        x = torch.randn(T, d, dtype=torch.float64)
+        gy = torch.randn(T, d, dtype=torch.float64)
+        blocks = _blocks(torch, d, h)
+        gates = [torch.tensor(1.3, dtype=torch.float64, requires_grad=True) for _ in blocks]
+        mlps = [_MLP(b.mlp, g) for b, g in zip(blocks, gates)]
+        for m in mlps:
+            P.tp_mlp(m)
+        hcur = x.clone().requires_grad_(True)
+        out = hcur
+        for m in mlps:
+            out = out + m(out)
+        (out * gy).sum().backward()
+        # rank-local gate grads are partial sums over this rank's slice; the
+        # trainer sums them across ranks (one flat all-reduce here)
+        P.all_reduce_gate_grads(gates)
+        res = {"gates": [g.grad.item() for g in gates], "dx": hcur.grad.clone(), "y": out.detach().clone()}
+        # differentiable all-reduce: forward sums, backward is the identity
+        t = torch.full((3,), float(rank + 1), requires_grad=True)
+        s = P.tp_all_reduce_sum(t)
+        s.sum().backward()
+        res["ar"] = s.detach().tolist()
+        res["ar_grad"] = t.grad.tolist()
+        torch.save(res, os.path.join(outdir, f"r{rank}_{int(exact)}.pt"))
+    finally:
+        P.reset_tp()
+        dist.destroy_process_group()
+
+
+def _reference(d=256, h=512, T=6):
+    torch.manual_seed(3)
+    x = torch.randn(T, d, dtype=torch.float64)
+    gy = torch.randn(T, d, dtype=torch.float64)
+    blocks = _blocks(torch, d, h)
+    gates = [torch.tensor(1.3, dtype=torch.float64, requires_grad=True) for _ in blocks]
+    hcur = x.clone().requires_grad_(True)
+    out = hcur
+    for b, g in zip(blocks, gates):
+        out = out + _mlp_forward(b.mlp, out, g)
+    (out * gy).sum().backward()
+    return [g.grad.item() for g in gates], hcur.grad, out.detach()
+
+
+@pytest.mark.parametrize("exact", [True, False])
+def test_tp2_mlp_stack_gate_gradients(exact):
+    port = _free_port()
+    with tempfile.TemporaryDirectory() as td:
+        mp.start_processes(_worker, args=(2, port, td, exact), nprocs=2, join=True, start_method="spawn")
+        r0 = torch.load(os.path.join(td, f"r0_{int(exact)}.pt"))
+        r1 = torch.load(os.path.join(td, f"r1_{int(exact)}.pt"))
+    g_ref, dx_ref, y_ref = _reference()
+    assert torch.allclose(r0["y"], y_ref, rtol=1e-12, atol=1e-12)
+    assert r0["gates"] == r1["gates"]
+    assert r0["ar"] == [3.0, 3.0, 3.0] and r0["ar_grad"] == [1.0, 1.0, 1.0]
+    if exact:
+        # exact input gradients: the summed gate gradients equal the unsharded ones
+        for got, ref in zip(r0["gates"], g_ref):
+            assert abs(got - ref) <= 1e-9 * max(1.0, abs(ref))
+        assert torch.allclose(r0["dx"], dx_ref, rtol=1e-10, atol=1e-10)
+    else:
+        # the reference's behaviour: block 1's gate gradient is computed from a
+        # partial upstream gradient and is off after the cross-rank sum
+        assert abs(r0["gates"][0] - g_ref[0]) > 1e-3 * abs(g_ref[0])

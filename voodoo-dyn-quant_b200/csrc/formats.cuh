@@ -261,152 +261,165 @@ struct Dec<kIQ4_XS> {
   }
 };
 
-// --------------------------------------------------- affine decoders (mix / gate-grad)
-// Aff<F>::run(slot, i, a, b, q) gives, for elements 8i..8i+7 of a unit, the
-// exact small-integer codes q[j] (as floats) and one scale/offset pair with
-// w[j] = a * q[j] + b.  a and b are the same float32 products the exact
-// decoders form (d*sc, -dmin*m), so a*q + b equals the exact decode up to the
-// final rounding; the mixture and gate-gradient kernels (tolerance-checked)
-// use this form to spend one FMA per weight instead of a multiply-subtract.
+// ------------------------------------------ sub-block decoders (mix / gate-grad)
+// Chunk<F>::run(slot, c, a, b, q) decodes elements 32c .. 32c+31 of a unit as
+// exact small-integer codes q[j] (floats) plus scale/offset pairs:
+//   w[j] = a[h] * q[j] + b[h],   h = j / 16
+// (formats with one scale per 32 weights repeat the pair).  a and b are the
+// same float32 products the exact decoders form (d*sc, -dmin*m), so a*q + b
+// equals the exact decode up to its final rounding.  The mixture and
+// gate-gradient kernels (tolerance-checked) use this form: one FMA per weight,
+// with the scale work done once per sub-block.
 template <int F>
-struct Aff;
+struct Chunk;
+
+__device__ __forceinline__ void ld8(const uint32_t* s, int off, uint32_t (&w)[8]) {
+#pragma unroll
+  for (int j = 0; j < 8; ++j) w[j] = s[(off >> 2) + j];
+}
+
+// four bytes of x -> floats (byte value - sub), exact
+__device__ __forceinline__ void bytes4(uint32_t x, float sub, float* q) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) q[j] = __uint_as_float(__byte_perm(x, 0x4B000000u, 0x7440u + j)) - sub;
+}
 
 template <>
-struct Aff<kQ8_0> {
-  __device__ __forceinline__ static void run(const uint32_t* s, int i, float& a, float& b, float (&q)[8]) {
-    const int bi = i >> 2;
-    const int dof = 34 * bi;
-    a = h2f(s[dof >> 2] >> (8 * (dof & 2)));
-    b = 0.f;
-    const int off = dof + 2 + 8 * (i & 3);
+struct Chunk<kQ8_0> {
+  static constexpr bool kMin = false;
+  __device__ __forceinline__ static void run(const uint32_t* s, int c, float (&a)[2], float (&b)[2], float (&q)[32]) {
+    const int dof = 34 * c;
+    a[0] = a[1] = h2f(s[dof >> 2] >> (8 * (dof & 2)));
+    b[0] = b[1] = 0.f;
+    const int off = dof + 2;
     const int al = off & ~3;
     const uint32_t sh = static_cast<uint32_t>(off & 3) * 8u;
-    const uint32_t w0 = s[al >> 2], w1 = s[(al >> 2) + 1];
-    const uint32_t w2 = sh ? s[(al >> 2) + 2] : 0u;
-    const uint32_t q0 = __funnelshift_r(w0, w1, sh) ^ 0x80808080u, q1 = __funnelshift_r(w1, w2, sh) ^ 0x80808080u;
+    uint32_t w[9];
 #pragma unroll
-    for (int j = 0; j < 8; ++j)
-      q[j] = __uint_as_float(__byte_perm(j < 4 ? q0 : q1, 0x4B000000u, 0x7440u + (j & 3))) - 8388736.0f;
+    for (int j = 0; j < 8; ++j) w[j] = s[(al >> 2) + j];
+    w[8] = sh ? s[(al >> 2) + 8] : 0u;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) bytes4(__funnelshift_r(w[j], w[j + 1], sh) ^ 0x80808080u, 8388736.0f, &q[4 * j]);
   }
 };
 
 template <>
-struct Aff<kQ4_K> {
-  __device__ __forceinline__ static void run(const uint32_t* s, int i, float& a, float& b, float (&q)[8]) {
+struct Chunk<kQ4_K> {
+  static constexpr bool kMin = true;
+  __device__ __forceinline__ static void run(const uint32_t* s, int c, float (&a)[2], float (&b)[2], float (&q)[32]) {
     const uint32_t w0 = s[0];
-    const int sb = i >> 2;
     uint32_t sc, mn;
-    k4_scale_min_w(s, sb, sc, mn);
-    a = __fmul_rn(h2f(w0), u2f(sc));
-    b = -__fmul_rn(h2f(w0 >> 16), u2f(mn));
-    uint32_t x, y;
-    ld2(s, 16 + 32 * (sb >> 1) + 8 * (i & 3), x, y);
-    const uint32_t sh = (sb & 1) * 4;
-    x = (x >> sh) & 0x0F0F0F0Fu;
-    y = (y >> sh) & 0x0F0F0F0Fu;
+    k4_scale_min_w(s, c, sc, mn);
+    a[0] = a[1] = __fmul_rn(h2f(w0), u2f(sc));
+    b[0] = b[1] = -__fmul_rn(h2f(w0 >> 16), u2f(mn));
+    uint32_t w[8];
+    ld8(s, 16 + 32 * (c >> 1), w);
+    const uint32_t sh = (c & 1) * 4;
 #pragma unroll
-    for (int j = 0; j < 8; ++j)
-      q[j] = __uint_as_float(__byte_perm(j < 4 ? x : y, 0x4B000000u, 0x7440u + (j & 3))) - 8388608.0f;
+    for (int j = 0; j < 8; ++j) bytes4((w[j] >> sh) & 0x0F0F0F0Fu, 8388608.0f, &q[4 * j]);
   }
 };
 
 template <>
-struct Aff<kQ5_K> {
-  __device__ __forceinline__ static void run(const uint32_t* s, int i, float& a, float& b, float (&q)[8]) {
+struct Chunk<kQ5_K> {
+  static constexpr bool kMin = true;
+  __device__ __forceinline__ static void run(const uint32_t* s, int c, float (&a)[2], float (&b)[2], float (&q)[32]) {
     const uint32_t w0 = s[0];
-    const int sb = i >> 2;
     uint32_t sc, mn;
-    k4_scale_min_w(s, sb, sc, mn);
-    a = __fmul_rn(h2f(w0), u2f(sc));
-    b = -__fmul_rn(h2f(w0 >> 16), u2f(mn));
-    const int l0 = 8 * (i & 3);
-    uint32_t ha, hb, x, y;
-    ld2(s, 16 + l0, ha, hb);
-    ld2(s, 48 + 32 * (sb >> 1) + l0, x, y);
-    const uint32_t sh = (sb & 1) * 4;
-    x = ((x >> sh) & 0x0F0F0F0Fu) | (((ha >> sb) & 0x01010101u) << 4);
-    y = ((y >> sh) & 0x0F0F0F0Fu) | (((hb >> sb) & 0x01010101u) << 4);
+    k4_scale_min_w(s, c, sc, mn);
+    a[0] = a[1] = __fmul_rn(h2f(w0), u2f(sc));
+    b[0] = b[1] = -__fmul_rn(h2f(w0 >> 16), u2f(mn));
+    uint32_t w[8], h[8];
+    ld8(s, 48 + 32 * (c >> 1), w);
+    ld8(s, 16, h);
+    const uint32_t sh = (c & 1) * 4;
 #pragma unroll
     for (int j = 0; j < 8; ++j)
-      q[j] = __uint_as_float(__byte_perm(j < 4 ? x : y, 0x4B000000u, 0x7440u + (j & 3))) - 8388608.0f;
+      bytes4(((w[j] >> sh) & 0x0F0F0F0Fu) | (((h[j] >> c) & 0x01010101u) << 4), 8388608.0f, &q[4 * j]);
   }
 };
 
 template <>
-struct Aff<kQ6_K> {
-  __device__ __forceinline__ static void run(const uint32_t* s, int i, float& a, float& b, float (&q)[8]) {
-    const int h = i >> 4, g = (i >> 2) & 3, l0 = 8 * (i & 3);
-    uint32_t la, lb, ha, hb;
-    ld2(s, 64 * h + 32 * (g & 1) + l0, la, lb);
-    ld2(s, 128 + 32 * h + l0, ha, hb);
-    const int sc = static_cast<int>(static_cast<int8_t>(byte_of(s, 192 + 8 * h + (l0 >> 4) + 2 * g)));
-    a = __fmul_rn(h2f(s[52]), u2f(static_cast<uint32_t>(sc + 128)) - 128.0f);
-    b = 0.f;
+struct Chunk<kQ6_K> {
+  static constexpr bool kMin = false;
+  __device__ __forceinline__ static void run(const uint32_t* s, int c, float (&a)[2], float (&b)[2], float (&q)[32]) {
+    const int h = c >> 2, g = c & 3;
+    const float d = h2f(s[52]);
+    const int so = 192 + 8 * h + 2 * g;
+    const uint32_t sw = s[so >> 2] >> (8 * (so & 3));  // two int8 scales (so is even)
+    const int sc0 = static_cast<int>(static_cast<int8_t>(sw & 0xFFu));
+    const int sc1 = static_cast<int>(static_cast<int8_t>((sw >> 8) & 0xFFu));
+    a[0] = __fmul_rn(d, u2f(static_cast<uint32_t>(sc0 + 128)) - 128.0f);
+    a[1] = __fmul_rn(d, u2f(static_cast<uint32_t>(sc1 + 128)) - 128.0f);
+    b[0] = b[1] = 0.f;
+    uint32_t l[8], hh[8];
+    ld8(s, 64 * h + 32 * (g & 1), l);
+    ld8(s, 128 + 32 * h, hh);
     const uint32_t lsh = (g >> 1) * 4, hsh = 2 * g;
-    const uint32_t x = ((la >> lsh) & 0x0F0F0F0Fu) | (((ha >> hsh) & 0x03030303u) << 4);
-    const uint32_t y = ((lb >> lsh) & 0x0F0F0F0Fu) | (((hb >> hsh) & 0x03030303u) << 4);
 #pragma unroll
     for (int j = 0; j < 8; ++j)
-      q[j] = __uint_as_float(__byte_perm(j < 4 ? x : y, 0x4B000000u, 0x7440u + (j & 3))) - 8388640.0f;  // q - 32
+      bytes4(((l[j] >> lsh) & 0x0F0F0F0Fu) | (((hh[j] >> hsh) & 0x03030303u) << 4), 8388640.0f, &q[4 * j]);
   }
 };
 
 template <>
-struct Aff<kQ2_K> {
-  __device__ __forceinline__ static void run(const uint32_t* s, int i, float& a, float& b, float (&q)[8]) {
-    const int h = i >> 4, sft = (i >> 2) & 3, l0 = 8 * (i & 3);
-    const uint32_t scb = byte_of(s, i >> 1);
+struct Chunk<kQ2_K> {
+  static constexpr bool kMin = true;
+  __device__ __forceinline__ static void run(const uint32_t* s, int c, float (&a)[2], float (&b)[2], float (&q)[32]) {
+    const int h = c >> 2, sft = c & 3;
+    const uint32_t sw = s[c >> 1] >> (16 * (c & 1));  // scale bytes 2c, 2c+1
     const uint32_t wd = s[20];
-    a = __fmul_rn(h2f(wd), u2f(scb & 15u));
-    b = -__fmul_rn(h2f(wd >> 16), u2f(scb >> 4));
-    uint32_t x, y;
-    ld2(s, 16 + 32 * h + l0, x, y);
-    x = (x >> (2 * sft)) & 0x03030303u;
-    y = (y >> (2 * sft)) & 0x03030303u;
+    const float d = h2f(wd), dmin = h2f(wd >> 16);
+    a[0] = __fmul_rn(d, u2f(sw & 15u));
+    b[0] = -__fmul_rn(dmin, u2f((sw >> 4) & 15u));
+    a[1] = __fmul_rn(d, u2f((sw >> 8) & 15u));
+    b[1] = -__fmul_rn(dmin, u2f((sw >> 12) & 15u));
+    uint32_t w[8];
+    ld8(s, 16 + 32 * h, w);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) bytes4((w[j] >> (2 * sft)) & 0x03030303u, 8388608.0f, &q[4 * j]);
+  }
+};
+
+template <>
+struct Chunk<kQ3_K> {
+  static constexpr bool kMin = false;
+  __device__ __forceinline__ static void run(const uint32_t* s, int c, float (&a)[2], float (&b)[2], float (&q)[32]) {
+    const int h = c >> 2, sft = c & 3;
+    const float d = h2f(s[27]);
+#pragma unroll
+    for (int t = 0; t < 2; ++t) {
+      const int j16 = 2 * c + t;
+      const uint32_t lo = (byte_of(s, 96 + (j16 & 7)) >> (4 * (j16 >> 3))) & 15u;
+      const uint32_t hi = (byte_of(s, 104 + (j16 & 3)) >> (2 * (j16 >> 2))) & 3u;
+      a[t] = __fmul_rn(d, u2f(lo | (hi << 4)) - 32.0f);
+      b[t] = 0.f;
+    }
+    uint32_t w[8], m[8];
+    ld8(s, 32 + 32 * h, w);
+    ld8(s, 0, m);
 #pragma unroll
     for (int j = 0; j < 8; ++j)
-      q[j] = __uint_as_float(__byte_perm(j < 4 ? x : y, 0x4B000000u, 0x7440u + (j & 3))) - 8388608.0f;
+      bytes4(((w[j] >> (2 * sft)) & 0x03030303u) | (((m[j] >> c) & 0x01010101u) << 2), 8388612.0f, &q[4 * j]);
   }
 };
 
 template <>
-struct Aff<kQ3_K> {
-  __device__ __forceinline__ static void run(const uint32_t* s, int i, float& a, float& b, float (&q)[8]) {
-    const int h = i >> 4, sft = (i >> 2) & 3, l0 = 8 * (i & 3), hbit = i >> 2;
-    const int j16 = i >> 1;
-    const uint32_t lo = (byte_of(s, 96 + (j16 & 7)) >> (4 * (j16 >> 3))) & 15u;
-    const uint32_t hi = (byte_of(s, 104 + (j16 & 3)) >> (2 * (j16 >> 2))) & 3u;
-    a = __fmul_rn(h2f(s[27]), u2f(lo | (hi << 4)) - 32.0f);
-    b = 0.f;
-    uint32_t ma, mb, x, y;
-    ld2(s, l0, ma, mb);
-    ld2(s, 32 + 32 * h + l0, x, y);
-    x = ((x >> (2 * sft)) & 0x03030303u) | (((ma >> hbit) & 0x01010101u) << 2);
-    y = ((y >> (2 * sft)) & 0x03030303u) | (((mb >> hbit) & 0x01010101u) << 2);
-#pragma unroll
-    for (int j = 0; j < 8; ++j)  // value = low + 4*hb - 4
-      q[j] = __uint_as_float(__byte_perm(j < 4 ? x : y, 0x4B000000u, 0x7440u + (j & 3))) - 8388612.0f;
-  }
-};
-
-template <>
-struct Aff<kIQ4_XS> {
-  __device__ __forceinline__ static void run(const uint32_t* s, int i, float& a, float& b, float (&q)[8]) {
-    const int ib = i >> 2, part = i & 3;
+struct Chunk<kIQ4_XS> {
+  static constexpr bool kMin = false;
+  __device__ __forceinline__ static void run(const uint32_t* s, int c, float (&a)[2], float (&b)[2], float (&q)[32]) {
     const uint32_t w0 = s[0];
-    const uint32_t shv = w0 >> 16;
-    const uint32_t ls = ((byte_of(s, 4 + (ib >> 1)) >> (4 * (ib & 1))) & 15u) | (((shv >> (2 * ib)) & 3u) << 4);
-    a = __fmul_rn(h2f(w0), u2f(ls) - 32.0f);
-    b = 0.f;
-    uint32_t x, y;
-    ld2(s, 8 + 16 * ib + 8 * (part & 1), x, y);
-    const uint32_t nsh = (part >> 1) * 4;
-    x = (x >> nsh) & 0x0F0F0F0Fu;
-    y = (y >> nsh) & 0x0F0F0F0Fu;
+    const uint32_t ls = ((byte_of(s, 4 + (c >> 1)) >> (4 * (c & 1))) & 15u) | ((((w0 >> 16) >> (2 * c)) & 3u) << 4);
+    a[0] = a[1] = __fmul_rn(h2f(w0), u2f(ls) - 32.0f);
+    b[0] = b[1] = 0.f;
+    uint32_t w[4];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const uint32_t idx = ((j < 4 ? x : y) >> (8 * (j & 3))) & 15u;
-      q[j] = u2f(static_cast<uint32_t>(iq4nl(idx) + 128)) - 128.0f;
+    for (int j = 0; j < 4; ++j) w[j] = s[2 + 4 * c + j];  // bytes 8 + 16c ..
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const uint32_t byte = (w[j >> 2] >> (8 * (j & 3))) & 0xFFu;
+      q[j] = u2f(static_cast<uint32_t>(iq4nl(byte & 15u) + 128)) - 128.0f;
+      q[j + 16] = u2f(static_cast<uint32_t>(iq4nl(byte >> 4) + 128)) - 128.0f;
     }
   }
 };

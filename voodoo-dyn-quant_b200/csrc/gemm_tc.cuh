@@ -125,8 +125,8 @@ __device__ __forceinline__ void stage_rows_warp(uint32_t* dst, const uint8_t* cb
 
 // Dot of one dW row (256 TMEM columns at t_row, fp32) with the decoded unit
 // in `slot` (this thread's row); columns at or beyond `cols` are skipped.
-// Uses the affine decode w = a*q + b per 8 weights:
-//   sum_j v_j w_j = a * sum_j v_j q_j + b * sum_j v_j.
+// Per 32-weight sub-block with w = a[h] * q + b[h] (h = half):
+//   sum_j v_j w_j = sum_h a[h] * sum_{j in h} v_j q_j  (+ b[h] * sum_{j in h} v_j).
 // All 32 lanes must call it (tcgen05.ld is warp-collective).
 template <int F>
 __device__ __forceinline__ float row_dot(const uint32_t* slot, uint32_t t_row, long long colbase, long long cols,
@@ -138,20 +138,24 @@ __device__ __forceinline__ float row_dot(const uint32_t* slot, uint32_t t_row, l
     tmem_ld_32cols(t_row + c * 32, v);
     const long long col0 = colbase + c * 32;
     if (row_ok && col0 < cols) {
-      const bool full = col0 + 32 <= cols;
+      if (col0 + 32 > cols) {
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        float a, b, w[8];
-        Aff<F>::run(slot, 4 * c + q, a, b, w);
-        float s1 = 0.f, s0 = 0.f;
+        for (int j = 0; j < 32; ++j)
+          if (col0 + j >= cols) v[j] = 0.f;
+      }
+      float a[2], b[2], q[32];
+      Chunk<F>::run(slot, c, a, b, q);
+      float s1[2] = {0.f, 0.f};
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const float vj = (full || col0 + 8 * q + j < cols) ? v[8 * q + j] : 0.f;
-          s1 = fmaf(vj, w[j], s1);
-          s0 += vj;
-        }
-        s = fmaf(a, s1, s);
-        s = fmaf(b, s0, s);
+      for (int j = 0; j < 32; ++j) s1[j >> 4] = fmaf(v[j], q[j], s1[j >> 4]);
+      s = fmaf(a[0], s1[0], s);
+      s = fmaf(a[1], s1[1], s);
+      if (Chunk<F>::kMin) {
+        float s0[2] = {0.f, 0.f};
+#pragma unroll
+        for (int j = 0; j < 32; ++j) s0[j >> 4] += v[j];
+        s = fmaf(b[0], s0[0], s);
+        s = fmaf(b[1], s0[1], s);
       }
     }
   }
@@ -364,22 +368,23 @@ __global__ void __launch_bounds__(THREADS, 1)
 }
 
 // grad_p[k] = sum over slots (in slot order) of partials[slot][k], in fp64;
-// a slot is one (tile, epilogue warp) pair.
-__global__ void gategrad_reduce_kernel(const float* __restrict__ partials, int num_tiles, int K,
-                                       float* __restrict__ grad_p) {
-  __shared__ double sh[256];
-  for (int k = 0; k < K; ++k) {
-    double s = 0.0;
-    for (int t = threadIdx.x; t < num_tiles; t += blockDim.x) s += static_cast<double>(partials[static_cast<long long>(t) * K + k]);
-    sh[threadIdx.x] = s;
-    __syncthreads();
-    for (int w = blockDim.x / 2; w > 0; w >>= 1) {
-      if (threadIdx.x < w) sh[threadIdx.x] += sh[threadIdx.x + w];
-      __syncthreads();
-    }
-    if (threadIdx.x == 0) grad_p[k] = static_cast<float>(sh[0]);
+// a slot is one (tile, epilogue warp) pair.  One CTA per candidate; the
+// per-thread strided sums and the tree below have a fixed shape, so the
+// result is deterministic.
+__global__ void __launch_bounds__(512) gategrad_reduce_kernel(const float* __restrict__ partials, int num_slots,
+                                                              int K, float* __restrict__ grad_p) {
+  __shared__ double sh[512];
+  const int k = blockIdx.x;
+  double s = 0.0;
+  for (int t = threadIdx.x; t < num_slots; t += blockDim.x)
+    s += static_cast<double>(partials[static_cast<long long>(t) * K + k]);
+  sh[threadIdx.x] = s;
+  __syncthreads();
+  for (int w = blockDim.x / 2; w > 0; w >>= 1) {
+    if (threadIdx.x < w) sh[threadIdx.x] += sh[threadIdx.x + w];
     __syncthreads();
   }
+  if (threadIdx.x == 0) grad_p[k] = static_cast<float>(sh[0]);
 }
 
 }  // namespace gemm

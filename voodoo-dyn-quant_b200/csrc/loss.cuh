@@ -22,7 +22,7 @@
 namespace vq {
 namespace loss {
 
-constexpr int THREADS = 512;
+constexpr int THREADS = 1024;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr int kStats = 8;  // m1 z1 mq zq mt zt A sy  (sy = NaN when y is not in this shard)
 
@@ -30,15 +30,12 @@ struct MZ {  // running max and sum of exp(x - max)
   float m, z;
 };
 
-__device__ __forceinline__ float ex(float x) { return exp2f(x * kLog2e); }
-
-__device__ __forceinline__ void mz_add(MZ& a, float x) {
-  if (x > a.m) {
-    a.z = a.z * ex(a.m - x) + 1.f;
-    a.m = x;
-  } else if (x != -INFINITY) {
-    a.z += ex(x - a.m);
-  }
+// e^x as one MUFU.EX2 (flush-to-zero: results below 2^-126 become 0, which
+// only drops probabilities that are already negligible).
+__device__ __forceinline__ float ex(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x * kLog2e));
+  return y;
 }
 
 __device__ __forceinline__ MZ mz_merge(MZ a, MZ b) {
@@ -60,22 +57,51 @@ __device__ __forceinline__ void acc_init(RowAcc& r) {
   r.a = 0.f;
 }
 
+// Fold 8 values into a running (max, sum-exp): one rescale per 8 values.
+__device__ __forceinline__ void mz_add8(MZ& r, const float (&x)[8]) {
+  float mx = x[0];
+#pragma unroll
+  for (int j = 1; j < 8; ++j) mx = fmaxf(mx, x[j]);
+  const float m = fmaxf(r.m, mx);
+  if (m == -INFINITY) return;
+  float z = (r.m == -INFINITY) ? 0.f : r.z * ex(r.m - m);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) z += ex(x[j] - m);
+  r.m = m;
+  r.z = z;
+}
+
 template <bool kT1>
-__device__ __forceinline__ void acc_add(RowAcc& r, float s, float t, float inv_t) {
-  mz_add(r.s1, s);
-  if (!kT1) mz_add(r.sq, s * inv_t);
-  const float tt = kT1 ? t : t * inv_t;
-  const float d = kT1 ? (t - s) : (t - s) * inv_t;
-  if (tt > r.t.m) {
-    const float sc = (r.t.m == -INFINITY) ? 0.f : ex(r.t.m - tt);
-    r.a = r.a * sc + d;
-    r.t.z = r.t.z * sc + 1.f;
-    r.t.m = tt;
-  } else if (tt != -INFINITY) {
-    const float e = ex(tt - r.t.m);
-    r.a = fmaf(e, d, r.a);
-    r.t.z += e;
+__device__ __forceinline__ void acc_add8(RowAcc& r, const float (&s)[8], const float (&t)[8], float inv_t) {
+  mz_add8(r.s1, s);
+  float tt[8], d[8];
+  if (!kT1) {
+    float sq[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) sq[j] = s[j] * inv_t;
+    mz_add8(r.sq, sq);
   }
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    tt[j] = kT1 ? t[j] : t[j] * inv_t;
+    d[j] = kT1 ? (t[j] - s[j]) : (t[j] - s[j]) * inv_t;
+  }
+  float mx = tt[0];
+#pragma unroll
+  for (int j = 1; j < 8; ++j) mx = fmaxf(mx, tt[j]);
+  const float m = fmaxf(r.t.m, mx);
+  if (m == -INFINITY) return;
+  const float sc = (r.t.m == -INFINITY) ? 0.f : ex(r.t.m - m);
+  float z = r.t.z * sc, a = r.a * sc;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const float e = ex(tt[j] - m);
+    z += e;
+    a = fmaf(e, d[j], a);
+  }
+  r.t.m = m;
+  r.t.z = z;
+  r.a = a;
 }
 
 __device__ __forceinline__ RowAcc acc_merge(RowAcc x, RowAcc y) {
@@ -113,33 +139,70 @@ __device__ __forceinline__ void unpack8(const uint4& v, float (&f)[8]) {
 }
 
 // Pass 1 over one row, reduced across the CTA (result valid in every thread).
+// Vector path: 8 bf16 per 16-byte load, two vectors of s and t in flight per
+// thread; the scalar tail (and unaligned rows) folds 8 at a time with -inf pad.
 template <bool kT1>
 __device__ RowAcc row_stats(const __nv_bfloat16* s, const __nv_bfloat16* t, int V, float inv_t, bool vec,
                             RowAcc* sh) {
   RowAcc r;
   acc_init(r);
-  int v8 = 0;
+  int done = 0;
   if (vec) {
-    v8 = V & ~7;
+    const int nv = V >> 3;
     const uint4* s4 = reinterpret_cast<const uint4*>(s);
     const uint4* t4 = reinterpret_cast<const uint4*>(t);
-    for (int i = threadIdx.x; i < (v8 >> 3); i += THREADS) {
+    int i = threadIdx.x;
+    for (; i + THREADS < nv; i += 2 * THREADS) {
+      const uint4 a0 = __ldg(s4 + i), b0 = __ldg(t4 + i);
+      const uint4 a1 = __ldg(s4 + i + THREADS), b1 = __ldg(t4 + i + THREADS);
+      float fs[8], ft[8];
+      unpack8(a0, fs);
+      unpack8(b0, ft);
+      acc_add8<kT1>(r, fs, ft, inv_t);
+      unpack8(a1, fs);
+      unpack8(b1, ft);
+      acc_add8<kT1>(r, fs, ft, inv_t);
+    }
+    if (i < nv) {
       float fs[8], ft[8];
       unpack8(__ldg(s4 + i), fs);
       unpack8(__ldg(t4 + i), ft);
+      acc_add8<kT1>(r, fs, ft, inv_t);
+    }
+    done = nv << 3;
+  }
+  for (int i0 = done + 8 * threadIdx.x; i0 < V; i0 += 8 * THREADS) {
+    float fs[8], ft[8];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) acc_add<kT1>(r, fs[j], ft[j], inv_t);
+    for (int j = 0; j < 8; ++j) {
+      const bool ok = i0 + j < V;
+      fs[j] = ok ? __bfloat162float(s[i0 + j]) : -INFINITY;
+      ft[j] = ok ? __bfloat162float(t[i0 + j]) : -INFINITY;
+    }
+    // padded lanes: s = t = -inf contribute e^-inf = 0; their (t - s) term is
+    // multiplied by that 0 only if finite, so zero it explicitly
+    RowAcc before = r;
+    acc_add8<kT1>(r, fs, ft, inv_t);
+    if (i0 + 8 > V) {
+      // recompute A without the padded lanes (NaN from -inf - -inf)
+      float a = 0.f;
+      const float m = r.t.m;
+      for (int j = 0; j < 8 && i0 + j < V; ++j) {
+        const float tt = kT1 ? ft[j] : ft[j] * inv_t;
+        const float d = kT1 ? (ft[j] - fs[j]) : (ft[j] - fs[j]) * inv_t;
+        a = fmaf(ex(tt - m), d, a);
+      }
+      r.a = (before.t.m == -INFINITY ? 0.f : before.a * ex(before.t.m - m)) + a;
     }
   }
-  for (int i = v8 + threadIdx.x; i < V; i += THREADS)
-    acc_add<kT1>(r, __bfloat162float(s[i]), __bfloat162float(t[i]), inv_t);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) r = acc_merge(r, acc_shfl(r, o));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (lane == 0) sh[warp] = r;
   __syncthreads();
   if (warp == 0) {
-    RowAcc x = lane < THREADS / 32 ? sh[lane] : RowAcc{{-INFINITY, 0.f}, {-INFINITY, 0.f}, {-INFINITY, 0.f}, 0.f};
+    RowAcc x;
+    if (lane < THREADS / 32) x = sh[lane]; else acc_init(x);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) x = acc_merge(x, acc_shfl(x, o));
     if (lane == 0) sh[THREADS / 32] = x;
@@ -163,30 +226,34 @@ __device__ void row_grad(const __nv_bfloat16* s, const __nv_bfloat16* t, int V, 
     d = fmaf(-klw_t, ex((kT1 ? ft : ft * inv_t) - lset), d);
     return d;
   };
-  int v8 = 0;
+  int done = 0;
+  const int ybase = y_local >= 0 ? static_cast<int>(y_local >> 3) : -1;
+  const int yoff = static_cast<int>(y_local & 7);
   if (vec) {
-    v8 = V & ~7;
+    const int nv = V >> 3;
     const uint4* s4 = reinterpret_cast<const uint4*>(s);
     const uint4* t4 = reinterpret_cast<const uint4*>(t);
     uint4* g4 = reinterpret_cast<uint4*>(g);
-    for (int i = threadIdx.x; i < (v8 >> 3); i += THREADS) {
+    for (int i = threadIdx.x; i < nv; i += THREADS) {
       float fs[8], ft[8];
       unpack8(__ldg(s4 + i), fs);
       unpack8(__ldg(t4 + i), ft);
+      float d[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) d[j] = grad1(fs[j], ft[j]);
+      if (i == ybase) {  // the target falls in this vector
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          if (j == yoff) d[j] -= ce_w;
+      }
       __align__(16) __nv_bfloat162 o[4];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        float d0 = grad1(fs[2 * j], ft[2 * j]);
-        float d1 = grad1(fs[2 * j + 1], ft[2 * j + 1]);
-        const long long v = 8ll * i + 2 * j;
-        if (v == y_local) d0 -= ce_w;
-        if (v + 1 == y_local) d1 -= ce_w;
-        o[j] = __floats2bfloat162_rn(d0, d1);
-      }
+      for (int j = 0; j < 4; ++j) o[j] = __floats2bfloat162_rn(d[2 * j], d[2 * j + 1]);
       g4[i] = *reinterpret_cast<const uint4*>(o);
     }
+    done = nv << 3;
   }
-  for (int i = v8 + threadIdx.x; i < V; i += THREADS) {
+  for (int i = done + threadIdx.x; i < V; i += THREADS) {
     float d = grad1(__bfloat162float(s[i]), __bfloat162float(t[i]));
     if (i == y_local) d -= ce_w;
     g[i] = __float2bfloat16_rn(d);

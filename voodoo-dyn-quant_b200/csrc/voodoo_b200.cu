@@ -207,11 +207,11 @@ int vq_dequant(int ggml_type, const void* blocks, int64_t rows, int64_t cols, fl
   int* err = nullptr;
   if (int rc = device_error_ptr(&err)) return rc;
   const long long units = (total + 255) / 256;
-  const long long grid = (units + vq::kUnitsPerCta - 1) / vq::kUnitsPerCta;
+  const long long grid = (units + vq::kDequantUnits - 1) / vq::kDequantUnits;
   if (grid > 0x7fffffffLL) return fail(VQ_ERR_INVALID, "tensor too large");
-  vq::decode_units_kernel<false, float><<<static_cast<unsigned>(grid), vq::kDecodeThreads, vq::decode_smem_bytes(cs),
-                                          static_cast<cudaStream_t>(stream)>>>(cs, nullptr, total, 1, total, out,
-                                                                               total, err);
+  vq::dequant_units_kernel<<<static_cast<unsigned>(grid), vq::kDecodeThreads,
+                             vq::stage_smem_bytes(cs, vq::kDequantUnits), static_cast<cudaStream_t>(stream)>>>(
+      cs, total, out, err);
   VQ_CUDA(cudaGetLastError());
   return 0;
 }
@@ -228,13 +228,15 @@ int vq_mix(int K, const int* types, const void* const* blocks, const float* prob
   if (probs == nullptr || w_bf16 == nullptr) return fail(VQ_ERR_INVALID, "null pointer");
   int* err = nullptr;
   if (int rc = device_error_ptr(&err)) return rc;
-  const long long total = static_cast<long long>(rows) * padded_cols;
-  const long long units = total / 256;
-  const long long grid = (units + vq::kUnitsPerCta - 1) / vq::kUnitsPerCta;
+  if (cols > 0x7fffffffLL) return fail(VQ_ERR_INVALID, "too many columns");
+  const long long units = static_cast<long long>(rows) * (padded_cols / 256);
+  const long long grid = (units + vq::kMixUnits - 1) / vq::kMixUnits;
   if (grid > 0x7fffffffLL) return fail(VQ_ERR_INVALID, "tensor too large");
-  vq::decode_units_kernel<true, __nv_bfloat16>
-      <<<static_cast<unsigned>(grid), vq::kDecodeThreads, vq::decode_smem_bytes(cs), static_cast<cudaStream_t>(stream)>>>(
-          cs, probs, total, static_cast<int>(padded_cols / 256), cols, static_cast<__nv_bfloat16*>(w_bf16), ldw, err);
+  const int smem = vq::stage_smem_bytes(cs, vq::kMixUnits);
+  if (smem > 48 * 1024) VQ_CUDA(cudaFuncSetAttribute(vq::mix_units_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  vq::mix_units_kernel<<<static_cast<unsigned>(grid), vq::kDecodeThreads, smem, static_cast<cudaStream_t>(stream)>>>(
+      cs, probs, units, static_cast<int>(padded_cols / 256), static_cast<int>(cols),
+      static_cast<__nv_bfloat16*>(w_bf16), ldw, err);
   VQ_CUDA(cudaGetLastError());
   return 0;
 }
@@ -326,7 +328,7 @@ int vq_gategrad(const void* dy, int64_t lddy, const void* x, int64_t ldx, int64_
   if (int rc = device_error_ptr(&p.err)) return rc;
   if (int rc = launch_gemm<true, true, vq::gemm::kEpiGateGrad>(ta, tb, p, st)) return rc;
   const int slots = static_cast<int>(need / (sizeof(float) * K));
-  vq::gemm::gategrad_reduce_kernel<<<1, 256, 0, st>>>(p.partials, slots, K, grad_probs);
+  vq::gemm::gategrad_reduce_kernel<<<K, 512, 0, st>>>(p.partials, slots, K, grad_probs);
   VQ_CUDA(cudaGetLastError());
   return 0;
 }

@@ -179,7 +179,10 @@ def all_reduce_gate_grads(params) -> None:
     params = [p for p in params if p.grad is not None]
     if not params:
         return
-    flat = torch.cat([p.grad.reshape(-1).to(torch.float32) for p in params])
+    dt = params[0].grad.dtype
+    for p in params[1:]:
+        dt = torch.promote_types(dt, p.grad.dtype)
+    flat = torch.cat([p.grad.reshape(-1).to(dt) for p in params])
     dist.all_reduce(flat, op=dist.ReduceOp.SUM, group=TP.group)
     off = 0
     for p in params:
