@@ -162,6 +162,64 @@ __device__ __forceinline__ float row_dot(const uint32_t* slot, uint32_t t_row, l
   return s;
 }
 
+// Epilogue of one 128 x 256 accumulator tile held in this CTA's TMEM.
+//   row0: first output row of this warp's 32 TMEM lanes; m128: index of the
+//   128-row block (for the gate-gradient partial slots); stage: the
+//   gate-gradient staging area (4 warps x 32 rows x kStagePitch words).
+template <int kEpi>
+__device__ __forceinline__ void epilogue_tile(const Params& p, uint8_t* stage, uint32_t t_row, long long row0,
+                                              int m128, int n_blk, int wq, int lane) {
+  const long long row = row0 + lane;
+  const bool row_ok = row < p.M;
+  if (kEpi == kEpiStoreBf16) {
+    for (int c = 0; c < BN / 32; ++c) {
+      float v[32];
+      tmem_ld_32cols(t_row + c * 32, v);
+      const long long col0 = static_cast<long long>(n_blk) * BN + c * 32;
+      if (row_ok && col0 < p.N) {
+        __nv_bfloat16* dst = p.C + row * p.ldc + col0;
+        if (col0 + 32 <= p.N && ((reinterpret_cast<uintptr_t>(dst) & 15u) == 0)) {
+          __align__(16) __nv_bfloat162 pk[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) pk[j] = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) reinterpret_cast<uint4*>(dst)[j] = reinterpret_cast<const uint4*>(pk)[j];
+        } else {
+          for (int j = 0; j < 32 && col0 + j < p.N; ++j) dst[j] = __float2bfloat16_rn(v[j]);
+        }
+      }
+    }
+  } else {
+    // Gate-gradient epilogue.  For each candidate: the warp stages its 32
+    // rows' units (one 256-column unit per row) into its shared slot rows with
+    // coalesced aligned loads, then each thread decodes its own row from
+    // shared memory and dots it with the dW row read back from TMEM.
+    uint32_t* my_stage = reinterpret_cast<uint32_t*>(stage) + wq * (32 * kStagePitch);
+    const long long slot = (static_cast<long long>(m128) * p.num_n_blk + n_blk) * 4 + wq;
+    const long long colbase = static_cast<long long>(n_blk) * BN;
+    for (int k = 0; k < p.cands.K; ++k) {
+      stage_rows_warp(my_stage, p.cands.ptr[k], row0, p.M, p.units_per_row, n_blk, p.cands.ubytes[k], lane);
+      __syncwarp();
+      const uint32_t* slot_row = my_stage + lane * kStagePitch;
+      float s = 0.f;
+      switch (p.cands.fmt[k]) {
+        case kQ8_0: s = row_dot<kQ8_0>(slot_row, t_row, colbase, p.cols, row_ok); break;
+        case kQ2_K: s = row_dot<kQ2_K>(slot_row, t_row, colbase, p.cols, row_ok); break;
+        case kQ3_K: s = row_dot<kQ3_K>(slot_row, t_row, colbase, p.cols, row_ok); break;
+        case kQ4_K: s = row_dot<kQ4_K>(slot_row, t_row, colbase, p.cols, row_ok); break;
+        case kQ5_K: s = row_dot<kQ5_K>(slot_row, t_row, colbase, p.cols, row_ok); break;
+        case kQ6_K: s = row_dot<kQ6_K>(slot_row, t_row, colbase, p.cols, row_ok); break;
+        case kIQ4_XS: s = row_dot<kIQ4_XS>(slot_row, t_row, colbase, p.cols, row_ok); break;
+        default: s = row_dot<kQ8_0>(slot_row, t_row, colbase, 0, false); break;  // keeps TMEM loads uniform
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+      if (lane == 0) p.partials[slot * p.cands.K + k] = s;
+      __syncwarp();
+    }
+  }
+}
+
 template <bool kAmn, bool kBmn, int kEpi>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Params p) {
@@ -298,61 +356,10 @@ __global__ void __launch_bounds__(THREADS, 1)
         break;
       }
       tc_fence_after();
-      const long long row = static_cast<long long>(m_blk) * BM + 32 * wq + lane;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(32 * wq) << 16) + acc * BN;
 
-      if (kEpi == kEpiStoreBf16) {
-        const bool row_ok = row < p.M;
-        for (int c = 0; c < BN / 32; ++c) {
-          float v[32];
-          tmem_ld_32cols(t_row + c * 32, v);
-          const long long col0 = static_cast<long long>(n_blk) * BN + c * 32;
-          if (row_ok && col0 < p.N) {
-            __nv_bfloat16* dst = p.C + row * p.ldc + col0;
-            if (col0 + 32 <= p.N && ((reinterpret_cast<uintptr_t>(dst) & 15u) == 0)) {
-              __align__(16) __nv_bfloat162 pk[16];
-#pragma unroll
-              for (int j = 0; j < 16; ++j) pk[j] = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
-#pragma unroll
-              for (int j = 0; j < 4; ++j) reinterpret_cast<uint4*>(dst)[j] = reinterpret_cast<const uint4*>(pk)[j];
-            } else {
-              for (int j = 0; j < 32 && col0 + j < p.N; ++j) dst[j] = __float2bfloat16_rn(v[j]);
-            }
-          }
-        }
-      } else {
-        // Gate-gradient epilogue.  For each candidate: the warp stages the 32
-        // rows' units (one 256-column unit per row) into its shared slot rows
-        // with coalesced aligned loads, then each thread decodes its own row
-        // from shared memory and dots it with the dW row read back from TMEM.
-        uint32_t* my_stage = reinterpret_cast<uint32_t*>(smem + SL::stage_off) + wq * SL::stage_words_per_warp;
-        const long long row0 = static_cast<long long>(m_blk) * BM + 32 * wq;
-        const long long slot = (static_cast<long long>(m_blk) * p.num_n_blk + n_blk) * 4 + wq;
-        const bool row_ok = row < p.M;
-        const long long colbase = static_cast<long long>(n_blk) * BN;
-        for (int k = 0; k < p.cands.K; ++k) {
-          const int ub = p.cands.ubytes[k];
-          const uint8_t* cbase = p.cands.ptr[k];
-          stage_rows_warp(my_stage, cbase, row0, p.M, p.units_per_row, n_blk, ub, lane);
-          __syncwarp();
-          const uint32_t* slot_row = my_stage + lane * kStagePitch;
-          float s = 0.f;
-          switch (p.cands.fmt[k]) {
-            case kQ8_0: s = row_dot<kQ8_0>(slot_row, t_row, colbase, p.cols, row_ok); break;
-            case kQ2_K: s = row_dot<kQ2_K>(slot_row, t_row, colbase, p.cols, row_ok); break;
-            case kQ3_K: s = row_dot<kQ3_K>(slot_row, t_row, colbase, p.cols, row_ok); break;
-            case kQ4_K: s = row_dot<kQ4_K>(slot_row, t_row, colbase, p.cols, row_ok); break;
-            case kQ5_K: s = row_dot<kQ5_K>(slot_row, t_row, colbase, p.cols, row_ok); break;
-            case kQ6_K: s = row_dot<kQ6_K>(slot_row, t_row, colbase, p.cols, row_ok); break;
-            case kIQ4_XS: s = row_dot<kIQ4_XS>(slot_row, t_row, colbase, p.cols, row_ok); break;
-            default: s = row_dot<kQ8_0>(slot_row, t_row, colbase, 0, false); break;  // keeps TMEM loads uniform
-          }
-#pragma unroll
-          for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-          if (lane == 0) p.partials[slot * p.cands.K + k] = s;
-          __syncwarp();
-        }
-      }
+      epilogue_tile<kEpi>(p, smem + SL::stage_off, t_row, static_cast<long long>(m_blk) * BM + 32 * wq, m_blk,
+                          n_blk, wq, lane);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(tempty_bar(acc));
@@ -364,6 +371,193 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (warp == 2) {
     tc_fence_after();
     tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+
+// ===================================================================== 2-CTA
+// The same GEMM on a CTA pair (cluster of 2, tcgen05 cta_group::2): a pair
+// tile is 256 x 256; CTA r of the pair loads rows [128r, 128r + 128) of the
+// A tile and rows [128r, 128r + 128) of the B tile (the MMA takes A split by M
+// and B split by N across the pair), so each SM streams half of B and its
+// shared memory feeds the tensor pipe at 8 KB per 256x256x16 step instead of
+// 12 KB per 128x256x16.  One thread of the even CTA issues the MMAs; its
+// commits arrive on both CTAs' barriers (tcgen05.commit multicast); both CTAs'
+// TMA loads count on the even CTA's "full" barriers.  Each CTA's TMEM holds
+// the fp32 accumulator of its own 128 rows, so the epilogue is unchanged.
+constexpr int PSTAGES = 6;
+constexpr int PA_STAGE = 128 * BK * 2;  // 16 KiB
+constexpr int PB_STAGE = 128 * BK * 2;  // 16 KiB
+
+template <int kEpi>
+struct PairSmemLayout {
+  static constexpr int a_off = 0;
+  static constexpr int b_off = a_off + PSTAGES * PA_STAGE;
+  static constexpr int bar_off = b_off + PSTAGES * PB_STAGE;
+  static constexpr int n_bars = 2 * PSTAGES + 4;
+  static constexpr int misc_off = bar_off + n_bars * 8;
+  static constexpr int stage_off = misc_off + 16;
+  static constexpr int stage_bytes = (kEpi == 1) ? 4 * 32 * kStagePitch * 4 : 0;
+  static constexpr int total = stage_off + stage_bytes;
+};
+
+template <bool kAmn, bool kBmn, int kEpi>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Params p) {
+  using SL = PairSmemLayout<kEpi>;
+  extern __shared__ __align__(1024) uint8_t smem[];
+  const uint32_t sbase = smem_u32(smem);
+  if ((sbase & 1023u) != 0) {  // uniform in both CTAs: the layout is identical
+    if (threadIdx.x == 0) report_error(p.err, kDevBadSmemAlign, 1);
+    return;
+  }
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const uint32_t bar0 = sbase + SL::bar_off;
+  auto full_bar = [&](int s) { return bar0 + 8u * s; };
+  auto empty_bar = [&](int s) { return bar0 + 8u * (PSTAGES + s); };
+  auto tfull_bar = [&](int a) { return bar0 + 8u * (2 * PSTAGES + a); };
+  auto tempty_bar = [&](int a) { return bar0 + 8u * (2 * PSTAGES + 2 + a); };
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + SL::misc_off);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + SL::misc_off + 4);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int cluster_id = blockIdx.x >> 1, num_clusters = gridDim.x >> 1;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < PSTAGES; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(tfull_bar(a), 1);
+      mbar_init(tempty_bar(a), 8);  // 4 epilogue warps x 2 CTAs (used in the even CTA)
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 2) {
+    tmem_alloc_pair(smem_u32(tmem_holder), TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();  // barriers of both CTAs initialised, TMEM allocated
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer (both CTAs)
+    if (lane == 0) {
+      uint32_t it = 0;
+      bool alive = true;
+      for (int tile = cluster_id; tile < p.num_tiles && alive; tile += num_clusters) {
+        int m_blk, n_blk;
+        tile_coords(p, tile, m_blk, n_blk);
+        const int m0 = m_blk * 256 + 128 * static_cast<int>(rank);
+        const int n0 = n_blk * BN + 128 * static_cast<int>(rank);
+        for (int kb = 0; kb < p.num_k_blk; ++kb, ++it) {
+          const int s = it % PSTAGES;
+          const uint32_t ph = (it / PSTAGES) & 1u;
+          if (!mbar_wait(empty_bar(s), ph ^ 1u, abort_flag)) {
+            report_error(p.err, kDevWaitTimeout, 11);
+            alive = false;
+            break;
+          }
+          const uint32_t fb = map_to_rank(full_bar(s), 0);
+          if (leader) mbar_arrive_expect_tx(full_bar(s), 2 * (PA_STAGE + PB_STAGE));
+          const uint32_t a_dst = sbase + SL::a_off + s * PA_STAGE;
+          const uint32_t b_dst = sbase + SL::b_off + s * PB_STAGE;
+          const int k0 = kb * BK;
+          if (kAmn) {
+#pragma unroll
+            for (int j = 0; j < 2; ++j) tma_load_2d_pair(a_dst + j * (64 * BK * 2), &tmA, fb, m0 + 64 * j, k0);
+          } else {
+            tma_load_2d_pair(a_dst, &tmA, fb, k0, m0);
+          }
+          if (kBmn) {
+#pragma unroll
+            for (int j = 0; j < 2; ++j) tma_load_2d_pair(b_dst + j * (64 * BK * 2), &tmB, fb, n0 + 64 * j, k0);
+          } else {
+            tma_load_2d_pair(b_dst, &tmB, fb, k0, n0);
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------- MMA issuer (even CTA)
+    if (leader && lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16_f32(256, BN, kAmn, kBmn);
+      uint32_t it = 0, local = 0;
+      bool alive = true;
+      for (int tile = cluster_id; tile < p.num_tiles && alive; tile += num_clusters, ++local) {
+        const int acc = local & 1;
+        const uint32_t aph = (local >> 1) & 1u;
+        if (!mbar_wait(tempty_bar(acc), aph ^ 1u, abort_flag)) {
+          report_error(p.err, kDevWaitTimeout, 12);
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = 0; kb < p.num_k_blk; ++kb, ++it) {
+          const int s = it % PSTAGES;
+          const uint32_t ph = (it / PSTAGES) & 1u;
+          if (!mbar_wait(full_bar(s), ph, abort_flag)) {
+            report_error(p.err, kDevWaitTimeout, 13);
+            alive = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = sbase + SL::a_off + s * PA_STAGE;
+          const uint32_t b_addr = sbase + SL::b_off + s * PB_STAGE;
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            const uint64_t adesc = kAmn ? smem_desc_sw128(a_addr + kk * 2048, 64 * BK * 2, 1024)
+                                        : smem_desc_sw128(a_addr + kk * 32, 16, 1024);
+            const uint64_t bdesc = kBmn ? smem_desc_sw128(b_addr + kk * 2048, 64 * BK * 2, 1024)
+                                        : smem_desc_sw128(b_addr + kk * 32, 16, 1024);
+            tc_mma_bf16_pair(d_tmem, adesc, bdesc, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+          }
+          tc_commit_pair_mc(empty_bar(s), 0x3);  // frees stage s in both CTAs
+        }
+        if (!alive) break;
+        tc_commit_pair_mc(tfull_bar(acc), 0x3);  // accumulators ready in both CTAs
+      }
+    }
+  } else if (warp >= 4) {
+    // --------------------------------------------------------------- epilogue (both CTAs)
+    const int wq = warp & 3;
+    const uint32_t tempty_leader0 = map_to_rank(tempty_bar(0), 0);
+    const uint32_t tempty_leader1 = map_to_rank(tempty_bar(1), 0);
+    uint32_t local = 0;
+    for (int tile = cluster_id; tile < p.num_tiles; tile += num_clusters, ++local) {
+      int m_blk, n_blk;
+      tile_coords(p, tile, m_blk, n_blk);
+      const int acc = local & 1;
+      const uint32_t aph = (local >> 1) & 1u;
+      if (!mbar_wait(tfull_bar(acc), aph, abort_flag)) {
+        if (lane == 0) report_error(p.err, kDevWaitTimeout, 14);
+        break;
+      }
+      tc_fence_after();
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(32 * wq) << 16) + acc * BN;
+      const int m128 = m_blk * 2 + static_cast<int>(rank);
+      epilogue_tile<kEpi>(p, smem + SL::stage_off, t_row, static_cast<long long>(m128) * 128 + 32 * wq, m128,
+                          n_blk, wq, lane);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(acc ? tempty_leader1 : tempty_leader0);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // no CTA frees TMEM while the pair's MMAs or epilogues may still use it
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, TMEM_COLS);
   }
 }
 

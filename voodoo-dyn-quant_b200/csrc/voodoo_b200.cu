@@ -132,22 +132,42 @@ int build_candset(vq::CandSet* cs, int K, const int* types, const void* const* b
   return 0;
 }
 
+// Output rows are tiled by 256 on a CTA pair (tcgen05 cta_group::2) when M >
+// 128, else by 128 on single CTAs.  `pair` reports the choice (the tensor
+// map box of a K-major B operand and the gate-gradient slot count depend on it).
+inline bool use_pair(long long M) { return M > vq::gemm::BM; }
+
 template <bool kAmn, bool kBmn, int kEpi>
 int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, vq::gemm::Params p, cudaStream_t st) {
   using namespace vq::gemm;
-  p.num_m_blk = (p.M + BM - 1) / BM;
+  const bool pair = use_pair(p.M);
+  p.num_m_blk = pair ? (p.M + 255) / 256 : (p.M + BM - 1) / BM;
   p.num_n_blk = (p.N + BN - 1) / BN;
   p.num_k_blk = (p.K + BK - 1) / BK;
   p.num_tiles = p.num_m_blk * p.num_n_blk;
   int sms = 0;
   if (int rc = sm_count(&sms)) return rc;
-  auto kern = gemm_kernel<kAmn, kBmn, kEpi>;
-  constexpr int smem = SmemLayout<kEpi>::total;
-  VQ_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-  const int grid = p.num_tiles < sms ? p.num_tiles : sms;
-  kern<<<grid, THREADS, smem, st>>>(ta, tb, p);
+  if (pair) {
+    auto kern = gemm_pair_kernel<kAmn, kBmn, kEpi>;
+    constexpr int smem = PairSmemLayout<kEpi>::total;
+    VQ_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    const int clusters = p.num_tiles < sms / 2 ? p.num_tiles : sms / 2;
+    kern<<<2 * clusters, THREADS, smem, st>>>(ta, tb, p);
+  } else {
+    auto kern = gemm_kernel<kAmn, kBmn, kEpi>;
+    constexpr int smem = SmemLayout<kEpi>::total;
+    VQ_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    const int grid = p.num_tiles < sms ? p.num_tiles : sms;
+    kern<<<grid, THREADS, smem, st>>>(ta, tb, p);
+  }
   VQ_CUDA(cudaGetLastError());
   return 0;
+}
+
+// Gate-gradient partial slots written by the kernel launch_gemm picks.
+inline long long gategrad_slots(long long N, long long Kin) {
+  const long long m128 = use_pair(N) ? 2 * ((N + 255) / 256) : (N + vq::gemm::BM - 1) / vq::gemm::BM;
+  return m128 * ((Kin + vq::gemm::BN - 1) / vq::gemm::BN) * 4;
 }
 
 int check_matrix(const void* p, long long rows, long long cols, long long ld, const char* name) {
@@ -253,7 +273,7 @@ int vq_linear_fwd(const void* x, int64_t T, int64_t Kin, int64_t ldx, const void
   if (T > 0x7fffffff || N > 0x7fffffff || Kin > 0x7fffffff) return fail(VQ_ERR_INVALID, "dimension too large");
   CUtensorMap ta, tb;
   if (int rc = make_map(&ta, x, T, Kin, ldx, vq::gemm::BM)) return rc;
-  if (int rc = make_map(&tb, w, N, Kin, ldw, vq::gemm::BN)) return rc;
+  if (int rc = make_map(&tb, w, N, Kin, ldw, use_pair(T) ? 128 : vq::gemm::BN)) return rc;
   vq::gemm::Params p{};
   p.M = static_cast<int>(T);
   p.N = static_cast<int>(N);
@@ -289,8 +309,7 @@ int vq_linear_dx(const void* dy, int64_t T, int64_t N, int64_t lddy, const void*
 
 size_t vq_gategrad_workspace_bytes(int64_t N, int64_t Kin, int K) {
   if (N <= 0 || Kin <= 0 || K <= 0) return 0;
-  const long long tiles = ((N + vq::gemm::BM - 1) / vq::gemm::BM) * ((Kin + vq::gemm::BN - 1) / vq::gemm::BN);
-  return static_cast<size_t>(tiles) * 4 * K * sizeof(float);
+  return static_cast<size_t>(gategrad_slots(N, Kin)) * K * sizeof(float);
 }
 
 int vq_gategrad(const void* dy, int64_t lddy, const void* x, int64_t ldx, int64_t T, int64_t N, int64_t Kin, int K,
@@ -327,7 +346,7 @@ int vq_gategrad(const void* dy, int64_t lddy, const void* x, int64_t ldx, int64_
   p.partials = static_cast<float*>(workspace);
   if (int rc = device_error_ptr(&p.err)) return rc;
   if (int rc = launch_gemm<true, true, vq::gemm::kEpiGateGrad>(ta, tb, p, st)) return rc;
-  const int slots = static_cast<int>(need / (sizeof(float) * K));
+  const int slots = static_cast<int>(gategrad_slots(N, Kin));
   vq::gemm::gategrad_reduce_kernel<<<K, 512, 0, st>>>(p.partials, slots, K, grad_probs);
   VQ_CUDA(cudaGetLastError());
   return 0;
