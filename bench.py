@@ -195,7 +195,7 @@ def run_gpu(args):
         dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=300))
         parallel.adopt_process_group(local)
     from voodoo_quant import _C
-    from voodoo_quant.parallel import TP, all_reduce_gate_grads, tp_copy_to_parallel
+    from voodoo_quant.parallel import all_reduce_gate_grads
 
     _C.load_library()
     layer = make_layer(dev, rank, world)
@@ -203,10 +203,12 @@ def run_gpu(args):
     x, dy = make_inputs(dev, n_loc, seed=2 + rank)
     stream = torch.cuda.current_stream()
 
+    if world > 1:
+        layer.reduce_input_grad = True  # dX all-reduce overlapped with the gate-gradient GEMM
+
     def step(xin, dyin):
         xg = xin.requires_grad_(True) if not xin.requires_grad else xin
-        xi = tp_copy_to_parallel(xg) if world > 1 else xg
-        y = layer(xi)
+        y = layer(xg)
         layer.gates.grad = None
         torch.autograd.backward(y, dyin)
         if world > 1:
@@ -268,20 +270,47 @@ def run_gpu(args):
     kt = {n: sum(e[j].elapsed_time(e[j + 1]) for e in evs) / len(evs) for j, n in enumerate(names)}
 
     # ---- e2e through the public API with host buffers ----
+    # Every step copies its X and dY from pinned host memory and reads the
+    # gate gradient back; the copy of step i+1 runs on a side stream while
+    # step i computes (double-buffered device inputs).
     xh = x.detach().cpu().pin_memory()
     dyh = dy.cpu().pin_memory()
     gh = torch.empty(len(TYPES), dtype=torch.float32).pin_memory()
-    for i in range(args.warmup + args.e2e_steps):
+    copy_stream = torch.cuda.Stream(dev)
+    xb = [torch.empty_like(x) for _ in range(2)]
+    dyb = [torch.empty_like(dy) for _ in range(2)]
+    ready = [torch.cuda.Event() for _ in range(2)]
+    free = [torch.cuda.Event() for _ in range(2)]
+    for b in range(2):
+        free[b].record(stream)
+
+    def issue_copy(i):
+        b = i & 1
+        with torch.cuda.stream(copy_stream), torch.no_grad():
+            copy_stream.wait_event(free[b])
+            xb[b].copy_(xh, non_blocking=True)
+            dyb[b].copy_(dyh, non_blocking=True)
+            ready[b].record(copy_stream)
+
+    total = args.warmup + args.e2e_steps
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    for i in range(total):
         if i == args.warmup:
             torch.cuda.synchronize()
             barrier()
-            e0 = torch.cuda.Event(enable_timing=True)
-            e1 = torch.cuda.Event(enable_timing=True)
             e0.record(stream)
-        xd = xh.to(dev, non_blocking=True)
-        dyd = dyh.to(dev, non_blocking=True)
-        step(xd, dyd)
+        b = i & 1
+        if i == 0 or i == args.warmup:  # the first timed step copies inside the timed region
+            issue_copy(i)
+        if i + 1 < total and i + 1 != args.warmup:
+            issue_copy(i + 1)
+        stream.wait_event(ready[b])
+        xin = xb[b]
+        xin.grad = None
+        step(xin, dyb[b])
         gh.copy_(layer.gates.grad, non_blocking=True)
+        free[b].record(stream)
     e1.record(stream)
     torch.cuda.synchronize()
     e2e_ms = torch.tensor([e0.elapsed_time(e1) / args.e2e_steps], device=dev)
@@ -327,7 +356,7 @@ def run_gpu(args):
                 "peak_source": f"{pk_kind} bf16_tflops (burst)",
                 "traffic": None,
                 "mix_gemm_frac": round(3 * flops_gemm / (gemm_ms * 1e-3) / 1e12 / peak_t, 4),
-                "step_frac": round(3 * flops_gemm / (ms * 1e-3) / 1e12 / peak_t / world, 4),
+                "step_frac": round(3 * flops_gemm / (ms * 1e-3) / 1e12 / peak_t, 4),
             },
             "kernels": kernels,
             "e2e": {

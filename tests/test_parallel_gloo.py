@@ -123,6 +123,9 @@ def _worker(rank, world, port, outdir, exact):
         s.sum().backward()
         res["ar"] = s.detach().tolist()
         res["ar_grad"] = t.grad.tolist()
+        u = torch.full((4,), float(10 * (rank + 1)))
+        P.tp_all_reduce_async(u).wait()
+        res["ar_async"] = u.tolist()
         torch.save(res, os.path.join(outdir, f"r{rank}_{int(exact)}.pt"))
     finally:
         P.reset_tp()
@@ -154,6 +157,7 @@ def test_tp2_mlp_stack_gate_gradients(exact):
     assert torch.allclose(r0["y"], y_ref, rtol=1e-12, atol=1e-12)
     assert r0["gates"] == r1["gates"]
     assert r0["ar"] == [3.0, 3.0, 3.0] and r0["ar_grad"] == [1.0, 1.0, 1.0]
+    assert r0["ar_async"] == r1["ar_async"] == [30.0] * 4
     if exact:
         # exact input gradients: the summed gate gradients equal the unsharded ones
         for got, ref in zip(r0["gates"], g_ref):

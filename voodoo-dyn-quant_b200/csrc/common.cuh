@@ -214,7 +214,8 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
 }
 
 // 2-D tiled load into this CTA's shared memory whose completion is counted on
-// an mbarrier of either CTA of the pair (cluster address); no multicast.
+// an mbarrier of either CTA of the pair (cluster address); the data goes to
+// this CTA only.
 __device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const void* tmap, uint32_t bar_cluster, int x, int y) {
   asm volatile(
       "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"

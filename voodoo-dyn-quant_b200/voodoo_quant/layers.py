@@ -129,14 +129,24 @@ class _GatedLinearFunction(Function):
         x2, probs = ctx.saved_tensors
         dy2 = _C._as_operand(dy.reshape(-1, layer.out_features))
         dx = dprobs = None
+        pending = None
         if ctx.needs_input_grad[0]:
             w_mix = ctx.w_mix if ctx.w_mix is not None else layer._mix(probs)
-            dx = _C.linear_dx(dy2, w_mix, layer.in_features).to(ctx.x_dtype).reshape(ctx.x_shape)
+            dx = _C.linear_dx(dy2, w_mix, layer.in_features)
+            if layer.reduce_input_grad:
+                # column-parallel layer with a private input: sum the partial
+                # dX over the TP ranks while the gate-gradient GEMM runs
+                from voodoo_quant.parallel import tp_all_reduce_async
+                pending = tp_all_reduce_async(dx)
         ctx.w_mix = None
         if ctx.needs_input_grad[1]:
             dprobs = _C.gategrad(dy2, x2, layer.candidate_types, layer._candidate_blocks(), layer.out_features,
                                  layer.in_features, layer.padded_in_features,
                                  workspace=layer._gategrad_workspace(x2.device)).to(probs.dtype)
+        if pending is not None:
+            pending.wait()
+        if dx is not None:
+            dx = dx.to(ctx.x_dtype).reshape(ctx.x_shape)
         return dx, dprobs, None
 
 
@@ -407,6 +417,10 @@ class MixedQuantLinear(_MixedQuantBase):
         if shard_spec is not None and shard_spec.vocab_start is not None:
             self.tp_vocab_start = shard_spec.vocab_start
             self.tp_vocab_end = shard_spec.vocab_start + out_features
+        # Column-parallel layer whose input feeds no other TP shard: sum its dX
+        # over the ranks inside the backward, overlapped with the gate-gradient
+        # GEMM (instead of entering the input through parallel.tp_copy_to_parallel).
+        self.reduce_input_grad = False
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         spec = self.shard_spec

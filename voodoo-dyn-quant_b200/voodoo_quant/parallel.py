@@ -161,6 +161,19 @@ def tp_copy_to_parallel(t: torch.Tensor) -> torch.Tensor:
     return _CopyToParallel.apply(t)
 
 
+class _Done:
+    def wait(self):
+        return None
+
+
+def tp_all_reduce_async(t: torch.Tensor):
+    """In-place all-reduce SUM of `t` on the TP group, returning a handle to
+    wait on (a no-op handle when TP is disabled)."""
+    if not TP.enabled:
+        return _Done()
+    return dist.all_reduce(t, op=dist.ReduceOp.SUM, group=TP.group, async_op=True)
+
+
 def tp_broadcast(t: torch.Tensor, src: int = 0) -> torch.Tensor:
     if TP.enabled:
         dist.broadcast(t, src=src, group=TP.group)
