@@ -497,14 +497,26 @@ def resolve_candidate_types(tensor_name: str, base_candidates: list[str],
     return [qt for qt in group if qt in set(base_candidates)]
 
 
+def _provided(provider, name: str, weight: torch.Tensor, types: list[str]):
+    if provider is None:
+        return None
+    padded, _, _ = _pad_weight_and_imatrix(weight.detach(), None)
+    return provider(name, padded, types)
+
+
 def replace_linear_with_mixed_quant(module: nn.Module, candidate_types: list[str] | None, prefix: str = "",
                                     target_names: Optional[set[str]] = None,
                                     skip_names: Optional[set[str]] = None,
                                     imatrix_dict: Optional[dict[str, torch.Tensor]] = None, device=None,
                                     lazy: bool = False, attention_candidates: Optional[list[str]] = None,
                                     non_attention_candidates: Optional[list[str]] = None,
-                                    qbytes_device=None) -> dict[str, _MixedQuantBase]:
-    """Recursively replace selected nn.Linear children (reference :1908-2066)."""
+                                    qbytes_device=None, candidate_provider=None) -> dict[str, _MixedQuantBase]:
+    """Recursively replace selected nn.Linear children (reference :1908-2066).
+
+    ``candidate_provider(name, full_weight, types) -> {qtype: uint8 blocks}``,
+    when given, supplies the packed candidates of the FULL tensor (padded to a
+    multiple of 256 columns) instead of the on-disk cache / libggml.
+    """
     if candidate_types is None:
         candidate_types = list(GPU_FORMATS)
     skip_names = skip_names or set()
@@ -520,19 +532,21 @@ def replace_linear_with_mixed_quant(module: nn.Module, candidate_types: list[str
             if target_names is not None and name not in target_names:
                 continue
             im = imatrix_dict.get(full_name, imatrix_dict.get(full_name + ".weight"))
+            types = resolve_candidate_types(full_name, candidate_types, attention_candidates, non_attention_candidates)
+            full_w = getattr(child, "tp_full_weight", None)
             new = MixedQuantLinear(
-                in_features=child.in_features, out_features=child.out_features,
-                candidate_types=resolve_candidate_types(full_name, candidate_types, attention_candidates,
-                                                        non_attention_candidates),
+                in_features=child.in_features, out_features=child.out_features, candidate_types=types,
                 source_weight=child.weight.data, imatrix=im, device=device, lazy=lazy, tensor_name=full_name,
                 qbytes_device=qbytes_device, shard_spec=getattr(child, "tp_shard_spec", None),
-                full_source_weight=getattr(child, "tp_full_weight", None))
+                full_source_weight=full_w,
+                candidate_bytes=_provided(candidate_provider, full_name,
+                                          full_w if full_w is not None else child.weight.data, types))
             setattr(module, name, new)
             replaced[full_name] = new
         else:
             replaced.update(replace_linear_with_mixed_quant(
                 child, candidate_types, full_name, target_names, skip_names, imatrix_dict, device, lazy,
-                attention_candidates, non_attention_candidates, qbytes_device))
+                attention_candidates, non_attention_candidates, qbytes_device, candidate_provider))
     return replaced
 
 
@@ -541,8 +555,8 @@ def replace_embedding_with_mixed_quant(module: nn.Module, candidate_types: list[
                                        imatrix_dict: Optional[dict[str, torch.Tensor]] = None, device=None,
                                        lazy: bool = False, qbytes_device=None,
                                        attention_candidates: Optional[list[str]] = None,
-                                       non_attention_candidates: Optional[list[str]] = None
-                                       ) -> dict[str, MixedQuantEmbedding]:
+                                       non_attention_candidates: Optional[list[str]] = None,
+                                       candidate_provider=None) -> dict[str, MixedQuantEmbedding]:
     """Recursively replace nn.Embedding children (reference :2086-2153)."""
     if candidate_types is None:
         candidate_types = list(GPU_FORMATS)
@@ -555,19 +569,21 @@ def replace_embedding_with_mixed_quant(module: nn.Module, candidate_types: list[
             continue
         if isinstance(child, nn.Embedding):
             im = imatrix_dict.get(full_name, imatrix_dict.get(full_name + ".weight"))
+            types = resolve_candidate_types(full_name, candidate_types, attention_candidates, non_attention_candidates)
+            full_w = getattr(child, "tp_full_weight", None)
             new = MixedQuantEmbedding(
-                num_embeddings=child.num_embeddings, embedding_dim=child.embedding_dim,
-                candidate_types=resolve_candidate_types(full_name, candidate_types, attention_candidates,
-                                                        non_attention_candidates),
+                num_embeddings=child.num_embeddings, embedding_dim=child.embedding_dim, candidate_types=types,
                 source_weight=child.weight.data, imatrix=im, device=device, lazy=lazy, tensor_name=full_name,
                 qbytes_device=qbytes_device, shard_spec=getattr(child, "tp_shard_spec", None),
-                full_source_weight=getattr(child, "tp_full_weight", None))
+                full_source_weight=full_w,
+                candidate_bytes=_provided(candidate_provider, full_name,
+                                          full_w if full_w is not None else child.weight.data, types))
             setattr(module, name, new)
             replaced[full_name] = new
         else:
             replaced.update(replace_embedding_with_mixed_quant(
                 child, candidate_types, full_name, skip_names, imatrix_dict, device, lazy, qbytes_device,
-                attention_candidates, non_attention_candidates))
+                attention_candidates, non_attention_candidates, candidate_provider))
     return replaced
 
 

@@ -1,0 +1,127 @@
+"""Q8_0 teacher on the B200 kernels (drop-in for training/q8_teacher.py).
+
+The reference keeps the teacher's Q8_0 bytes on the GPU and dequantizes them
+per forward with torch ops before ``F.linear`` (voodoo_quant/training/
+q8_teacher.py:62-173).  Here ``Q8Linear`` is the gated path with one
+candidate: ``vq_mix`` (K = 1, p = [1]) decodes the Q8_0 blocks to a bf16
+weight in one HBM pass and ``vq_linear_fwd`` runs the tcgen05 GEMM; the
+decoded weight is dropped after the call.  ``Q8Embedding`` decodes only the
+rows the batch touches.
+"""
+
+from __future__ import annotations
+
+from typing import Callable, Optional
+
+import torch
+import torch.nn as nn
+
+from voodoo_quant import _C
+
+
+def _q8_rows(qweight: torch.Tensor, rows: int, cols: int) -> torch.Tensor:
+    return qweight.view(rows, (cols // 32) * 34)
+
+
+class Q8Linear(nn.Module):
+    """nn.Linear stand-in holding Q8_0 bytes; forward-only (teacher)."""
+
+    def __init__(self, qbytes: torch.Tensor, out_features: int, in_features: int, bias=None, device=None):
+        super().__init__()
+        if bias is not None:
+            raise NotImplementedError("Q8Linear does not support bias")
+        if in_features % 256:
+            raise ValueError(f"Q8Linear needs in_features % 256 == 0 on this path, got {in_features}")
+        self.out_features = out_features
+        self.in_features = in_features
+        dev = torch.device(device) if device is not None else qbytes.device
+        self.register_buffer("qweight", qbytes.reshape(-1, 34).to(dev).contiguous())
+        self.register_buffer("_one", torch.ones(1, dtype=torch.float32, device=dev), persistent=False)
+
+    def weight_bf16(self) -> torch.Tensor:
+        return _C.mix(["Q8_0"], [self.qweight], self._one, self.out_features, self.in_features, self.in_features)
+
+    @torch.no_grad()
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        w = self.weight_bf16()
+        y = _C.linear_fwd(x.reshape(-1, self.in_features), w, self.out_features, self.in_features)
+        return y.to(x.dtype).reshape(*x.shape[:-1], self.out_features)
+
+
+class Q8Embedding(nn.Module):
+    """nn.Embedding stand-in holding Q8_0 bytes; decodes the touched rows."""
+
+    def __init__(self, qbytes: torch.Tensor, num_embeddings: int, embedding_dim: int, device=None):
+        super().__init__()
+        self.num_embeddings = num_embeddings
+        self.embedding_dim = embedding_dim
+        dev = torch.device(device) if device is not None else qbytes.device
+        self.register_buffer("qweight", qbytes.reshape(-1, 34).to(dev).contiguous())
+        self.register_buffer("_one", torch.ones(1, dtype=torch.float32, device=dev), persistent=False)
+
+    @torch.no_grad()
+    def forward(self, ids: torch.Tensor) -> torch.Tensor:
+        rows, inverse = torch.unique(ids.reshape(-1), return_inverse=True)
+        sub = _q8_rows(self.qweight, self.num_embeddings, self.embedding_dim).index_select(0, rows)
+        w = _C.mix(["Q8_0"], [sub.reshape(-1)], self._one, rows.numel(), self.embedding_dim, self.embedding_dim)
+        return w[inverse].reshape(*ids.shape, self.embedding_dim)
+
+
+def wrap_q8_teacher(model: nn.Module, quantizer: Callable[[torch.Tensor], torch.Tensor],
+                    skip_names: Optional[set[str]] = None) -> nn.Module:
+    """Replace every nn.Linear / nn.Embedding of `model` with its Q8_0 form in place.
+
+    `quantizer(weight) -> uint8 [nblocks, 34]` produces the Q8_0 bytes (libggml
+    ``quantize_tensor(w, "Q8_0")`` or the round-to-nearest packer, which is
+    ggml's reference Q8_0 rule).  Mirrors ``wrap_q8_teacher``
+    (q8_teacher.py:176-294) for the modules on the step's path.
+    """
+    skip_names = skip_names or set()
+    for name, child in list(model.named_children()):
+        if name in skip_names:
+            continue
+        if isinstance(child, nn.Linear):
+            w = child.weight.data
+            new = Q8Linear(quantizer(w), child.out_features, child.in_features, device=w.device)
+            for attr in ("tp_shard_spec", "tp_vocab_start", "tp_vocab_end"):
+                if hasattr(child, attr):
+                    setattr(new, attr, getattr(child, attr))
+            if hasattr(child, "tp_shard_spec") and child.tp_shard_spec.col_offset is not None:
+                new = _RowParallelQ8(new)
+            setattr(model, name, new)
+            del child
+        elif isinstance(child, nn.Embedding):
+            w = child.weight.data
+            new = Q8Embedding(quantizer(w), child.num_embeddings, child.embedding_dim, device=w.device)
+            if hasattr(child, "tp_vocab_start"):
+                new = _VocabParallelQ8(new, child.tp_vocab_start, child.num_embeddings)
+            setattr(model, name, new)
+            del child
+        else:
+            wrap_q8_teacher(child, quantizer, skip_names)
+    return model
+
+
+class _RowParallelQ8(nn.Module):
+    def __init__(self, inner: Q8Linear):
+        super().__init__()
+        self.inner = inner
+        self.out_features, self.in_features = inner.out_features, inner.in_features
+
+    def forward(self, x):
+        from voodoo_quant.parallel import tp_all_reduce_sum
+        return tp_all_reduce_sum(self.inner(x))
+
+
+class _VocabParallelQ8(nn.Module):
+    def __init__(self, inner: Q8Embedding, vocab_start: int, rows: int):
+        super().__init__()
+        self.inner = inner
+        self.vocab_start, self.rows = vocab_start, rows
+
+    def forward(self, ids):
+        from voodoo_quant.parallel import tp_all_reduce_sum
+        mask = (ids < self.vocab_start) | (ids >= self.vocab_start + self.rows)
+        out = self.inner((ids - self.vocab_start).clamp(0, self.rows - 1))
+        out = out * (~mask).unsqueeze(-1).to(out.dtype)
+        return tp_all_reduce_sum(out)

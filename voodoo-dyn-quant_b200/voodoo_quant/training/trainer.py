@@ -1,0 +1,192 @@
+"""The gated-candidate distillation step (the hot loop of training/trainer.py).
+
+Keeps the reference step's semantics (voodoo_quant/training/trainer.py:
+2443-2666) and helper names:
+
+* temperature  tau_s = start * (end / start) ** (s / (S - 1))        (:199-203)
+* loss         CE + distill_weight * T^2 * KL(teacher || student)    (:2567-2575)
+               on the fused B200 loss kernel (``training.loss``)
+* size         bytes = sum of effective_bytes + non-targeted 8-bit bytes;
+               size_loss = relu(|bytes / target - 1| - tolerance)^2  (:2577-2590)
+* optimiser    AdamW(gates, lr, betas=(0.9, 0.95)), clip-norm 1.0, cosine LR
+               with eta_min 1e-3 (:2378-2379, :2607-2616); under TP the gate
+               gradients are summed with one flat all-reduce first.
+
+Only the gates train; every other parameter is frozen, as in the reference
+(:2344-2351).
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+import torch.nn as nn
+
+from voodoo_quant.layers import total_effective_bytes
+from voodoo_quant.training.loss import distillation_loss, tp_distillation_loss
+
+
+def anneal_temperature(step: int, max_steps: int, start: float, end: float) -> float:
+    if max_steps <= 1:
+        return end
+    frac = step / (max_steps - 1)
+    return start * (end / start) ** frac
+
+
+def compute_total_8bit_bytes(state_dict_meta: dict[str, tuple[int, int]]) -> float:
+    """Bytes at 8 bits per parameter, shared storages counted once (:157-178)."""
+    seen, total = set(), 0.0
+    for ptr, numel in state_dict_meta.values():
+        if ptr not in seen:
+            seen.add(ptr)
+            total += float(numel)
+    return total
+
+
+def compute_non_targeted_8bit_bytes(state_dict_meta: dict[str, tuple[int, int]], targeted_keys: set[str]) -> float:
+    """8-bit bytes of parameters that are not gated (:181-196)."""
+    ptr_bytes, ptr_targeted = {}, {}
+    for k, (ptr, numel) in state_dict_meta.items():
+        ptr_bytes[ptr] = float(numel)
+        ptr_targeted.setdefault(ptr, False)
+        if k in targeted_keys:
+            ptr_targeted[ptr] = True
+    return sum(b for p, b in ptr_bytes.items() if not ptr_targeted[p])
+
+
+def state_dict_meta(model: nn.Module) -> dict[str, tuple[int, int]]:
+    return {n: (t.untyped_storage().data_ptr(), t.numel()) for n, t in model.state_dict(keep_vars=True).items()
+            if t.is_floating_point()}
+
+
+def _tp_all_reduce_gate_grads(trainable) -> None:
+    from voodoo_quant.parallel import all_reduce_gate_grads
+
+    all_reduce_gate_grads(trainable)
+
+
+@dataclass
+class StepArgs:
+    lr: float = 0.5
+    distill_weight: float = 1.0
+    distill_temperature: float = 1.0
+    size_weight: float = 10.0
+    size_tolerance: float = 0.02
+    temp_start: float = 1.0
+    temp_end: float = 0.01
+    max_steps: int = 50
+    ce_reduction: str = "valid"  # plain path: mean CE over non-ignored tokens
+
+
+class GatedDistillTrainer:
+    """Runs gated-candidate distillation steps on a replaced student model."""
+
+    def __init__(self, student: nn.Module, teacher: nn.Module, replaced: dict, args: StepArgs,
+                 target_bytes: float, non_targeted_bytes: float, tp: bool = False):
+        self.student, self.teacher, self.replaced, self.args = student, teacher, replaced, args
+        self.target_bytes = float(target_bytes)
+        self.non_targeted_bytes = float(non_targeted_bytes)
+        self.tp = tp
+        for p in student.parameters():
+            p.requires_grad = False
+        for layer in replaced.values():
+            layer.gates.requires_grad = True
+        self.trainable = [layer.gates for layer in replaced.values()]
+        self.optimizer = torch.optim.AdamW(self.trainable, lr=args.lr, betas=(0.9, 0.95))
+        self.scheduler = torch.optim.lr_scheduler.CosineAnnealingLR(self.optimizer, T_max=args.max_steps,
+                                                                    eta_min=1e-3)
+        self.step_idx = 0
+        student.train()
+        teacher.eval()
+
+    def _vocab_start(self) -> int | None:
+        head = getattr(self.student, "lm_head", None)
+        return getattr(head, "tp_vocab_start", None)
+
+    def forward_backward(self, x: torch.Tensor, y: torch.Tensor) -> dict:
+        """Loss of one batch and its gate gradients (left in ``gates.grad``)."""
+        a = self.args
+        tau = anneal_temperature(self.step_idx, a.max_steps, a.temp_start, a.temp_end)
+        for layer in self.replaced.values():
+            layer.set_temperature(tau)
+        logits = self.student(input_ids=x).logits
+        with torch.no_grad():
+            t_logits = self.teacher(input_ids=x).logits
+        v0 = self._vocab_start()
+        if self.tp and v0 is not None:
+            kd, lm, kl = tp_distillation_loss(logits, t_logits, y, v0, a.distill_temperature, a.distill_weight,
+                                              ce_reduction="tokens")
+        else:
+            kd, lm, kl = distillation_loss(logits, t_logits, y, a.distill_temperature, a.distill_weight,
+                                           ce_reduction=a.ce_reduction)
+        del t_logits
+        current = total_effective_bytes(self.replaced).to(logits.device)
+        if self.tp:
+            from voodoo_quant.parallel import tp_all_reduce_sum
+
+            current = tp_all_reduce_sum(current)
+        current = current + self.non_targeted_bytes
+        rel = torch.abs(current / self.target_bytes - 1.0)
+        size_loss = torch.relu(rel - a.size_tolerance) ** 2
+        loss = kd + a.size_weight * size_loss
+        self.optimizer.zero_grad(set_to_none=True)
+        loss.backward()
+        if self.tp:
+            _tp_all_reduce_gate_grads(self.trainable)
+        return {"loss": loss.detach(), "lm_loss": lm, "distill_loss": kl, "size_bytes": current.detach(),
+                "size_loss": size_loss.detach(), "tau": tau}
+
+    def apply_update(self) -> None:
+        torch.nn.utils.clip_grad_norm_(self.trainable, max_norm=1.0)
+        self.optimizer.step()
+        self.scheduler.step()
+        self.step_idx += 1
+
+    def step(self, x: torch.Tensor, y: torch.Tensor) -> dict:
+        out = self.forward_backward(x, y)
+        self.apply_update()
+        return out
+
+    def assignments(self) -> dict[str, str]:
+        return {name: layer.get_assignment() for name, layer in self.replaced.items()}
+
+
+def build_distill(shape_name: str, device, seed: int = 0, args: StepArgs | None = None,
+                  candidate_provider=None, replace_embeddings: bool = True, tp: bool = False):
+    """Student (gated), Q8_0 teacher and trainer for a synthetic config.
+
+    Under TP (an initialised process group adopted by voodoo_quant.parallel)
+    both models are sharded by the Llama adapter before replacement, so the
+    candidates are packed from the FULL tensors and sliced per rank.
+    """
+    from voodoo_quant.layers import replace_embedding_with_mixed_quant, replace_linear_with_mixed_quant
+    from voodoo_quant.parallel import TP, tp_patch_model
+    from voodoo_quant.training import synthetic as S
+    from voodoo_quant.training.q8_teacher import wrap_q8_teacher
+
+    shape = S.SHAPES[shape_name]
+    provider = candidate_provider or S.rtn_candidate_provider
+    base = S.build_llama(shape, device, seed=seed)
+    meta = state_dict_meta(base)
+    total_8bit = compute_total_8bit_bytes(meta)
+    teacher = S.build_llama(shape, device, seed=seed)
+    if tp and TP.enabled:
+        tp_patch_model(base, verbose=False)
+        tp_patch_model(teacher, verbose=False)
+    wrap_q8_teacher(teacher, S.q8_quantizer)
+    skip = {"lm_head"} if shape.tied else set()
+    replaced = replace_linear_with_mixed_quant(base, shape.candidates, skip_names=skip, device=device,
+                                               candidate_provider=provider)
+    if replace_embeddings:
+        replaced.update(replace_embedding_with_mixed_quant(base, shape.candidates, device=device,
+                                                           candidate_provider=provider))
+    targeted = {n + ".weight" for n in replaced}
+    non_targeted = compute_non_targeted_8bit_bytes(meta, targeted)
+    for m in base.modules():  # drop the full-weight references kept for candidate packing
+        if hasattr(m, "tp_full_weight"):
+            m.tp_full_weight = None
+    torch.cuda.empty_cache()
+    trainer = GatedDistillTrainer(base, teacher, replaced, args or StepArgs(), shape.budget * total_8bit,
+                                  non_targeted, tp=tp and TP.enabled)
+    return trainer, shape
