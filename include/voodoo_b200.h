@@ -94,6 +94,34 @@ int vq_gategrad(const void* dy, int64_t lddy, const void* x, int64_t ldx, int64_
                 const int* types, const void* const* blocks, int64_t padded_cols, void* workspace,
                 size_t workspace_bytes, float* grad_probs, void* stream);
 
+/* Largest scratch vq_gategrad_noalloc can use: 4 MiB, which covers every
+ * unsharded layer up to a 152064 x 5120 vocabulary projection with 7
+ * candidates (vq_gategrad_workspace_bytes gives the need of a shape). */
+#define VQ_GATEGRAD_NOALLOC_SCRATCH_BYTES (4u << 20)
+
+/* vq_gategrad without a workspace argument, for callers that cannot allocate
+ * device memory: a host that binds this library over a plain C FFI and has no
+ * device allocator to hand it, or a process whose memory pool (a framework's
+ * caching allocator) owns the device memory, so that a cudaMalloc beside the
+ * pool would fail or split it.  No counterpart in the reference (its gate
+ * gradient is plain torch autograd).
+ *   - Scratch is one file-scope device array of
+ *     VQ_GATEGRAD_NOALLOC_SCRATCH_BYTES, held on every GPU that loads the
+ *     library until the process exits.  Shapes whose
+ *     vq_gategrad_workspace_bytes exceeds it are rejected (VQ_ERR_INVALID)
+ *     before anything runs; use vq_gategrad with a workspace for those.
+ *   - The first call on a device looks up the array's device address with
+ *     that device current (the device of grad_probs); make that first call
+ *     before any stream capture on the device.
+ *   - Every call shares the array.  Nothing in it needs to start at zero (each
+ *     call writes every partial slot it reads back), but calls that overlap
+ *     on the GPU (other streams, other threads) race on it: order them.
+ *   - Allocates nothing: no cudaMalloc, cudaFree or allocating library call.
+ * Arguments, results and errors are those of vq_gategrad. */
+int vq_gategrad_noalloc(const void* dy, int64_t lddy, const void* x, int64_t ldx, int64_t T, int64_t N, int64_t Kin,
+                        int K, const int* types, const void* const* blocks, int64_t padded_cols, float* grad_probs,
+                        void* stream);
+
 /* K1 convenience: vq_mix into w_mix[N, ldw] followed by vq_linear_fwd. */
 int vq_mixgemm_fwd(const void* x, int64_t T, int64_t Kin, int64_t ldx, int K, const int* types,
                    const void* const* blocks, const float* probs, int64_t N, int64_t padded_cols, void* w_mix,

@@ -11,8 +11,10 @@
 #include <cudaTypedefs.h>
 
 #include <cstdarg>
+#include <cstdint>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 
 #include "common.cuh"
 #include "formats.cuh"
@@ -183,6 +185,36 @@ int zero_rows(void* p, long long rows, long long cols, long long ld, size_t elem
   return 0;
 }
 
+// Scratch of vq_gategrad_noalloc, for callers that cannot allocate device
+// memory (a plain C-FFI host without a device allocator, or a process whose
+// memory pool owns the device).  Every GPU that loads this library holds it
+// until exit.  In host code `g_gategrad_scratch` is only a stand-in symbol:
+// its device address comes from cudaGetSymbolAddress, per device.
+static __device__ __align__(256) float g_gategrad_scratch[VQ_GATEGRAD_NOALLOC_SCRATCH_BYTES / sizeof(float)];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_scratch_mu;
+void* g_scratch_addr[kMaxDevices] = {};
+
+// Device address of the scratch on the current device, looked up once per
+// device (the first call on a device must come before any stream capture).
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  VQ_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kMaxDevices) return fail(VQ_ERR_INVALID, "device ordinal %d beyond %d", dev, kMaxDevices);
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (g_scratch_addr[dev] == nullptr) {
+    void* ptr = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&ptr, g_gategrad_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(gate-grad scratch)");
+    if (ptr == nullptr || reinterpret_cast<uintptr_t>(ptr) % 256 != 0)
+      return fail(VQ_ERR_CUDA, "gate-grad scratch address %p is not 256-byte aligned", ptr);
+    g_scratch_addr[dev] = ptr;
+  }
+  *out = g_scratch_addr[dev];
+  return 0;
+}
+
 }  // namespace
 
 extern "C" {
@@ -350,6 +382,23 @@ int vq_gategrad(const void* dy, int64_t lddy, const void* x, int64_t ldx, int64_
   vq::gemm::gategrad_reduce_kernel<<<K, 512, 0, st>>>(p.partials, slots, K, grad_probs);
   VQ_CUDA(cudaGetLastError());
   return 0;
+}
+
+int vq_gategrad_noalloc(const void* dy, int64_t lddy, const void* x, int64_t ldx, int64_t T, int64_t N, int64_t Kin,
+                        int K, const int* types, const void* const* blocks, int64_t padded_cols, float* grad_probs,
+                        void* stream) {
+  const size_t need = vq_gategrad_workspace_bytes(N, Kin, K);
+  if (need > VQ_GATEGRAD_NOALLOC_SCRATCH_BYTES)
+    return fail(VQ_ERR_INVALID,
+                "gate-grad of a %lld x %lld layer with %d candidates needs %zu bytes of scratch; "
+                "vq_gategrad_noalloc holds %zu (use vq_gategrad with a caller workspace)",
+                (long long)N, (long long)Kin, K, need, (size_t)VQ_GATEGRAD_NOALLOC_SCRATCH_BYTES);
+  if (grad_probs == nullptr) return fail(VQ_ERR_INVALID, "null grad_probs");
+  DeviceScope scope(grad_probs);
+  void* scratch = nullptr;
+  if (int rc = noalloc_scratch(&scratch)) return rc;
+  return vq_gategrad(dy, lddy, x, ldx, T, N, Kin, K, types, blocks, padded_cols, scratch,
+                     VQ_GATEGRAD_NOALLOC_SCRATCH_BYTES, grad_probs, stream);
 }
 
 int vq_mixgemm_fwd(const void* x, int64_t T, int64_t Kin, int64_t ldx, int K, const int* types,

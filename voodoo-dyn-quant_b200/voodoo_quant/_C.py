@@ -48,6 +48,7 @@ def _declare(lib):
         "vq_gategrad_workspace_bytes": (ctypes.c_size_t, [_i64, _i64, _int]),
         "vq_gategrad": (_int, [_vp, _i64, _vp, _i64, _i64, _i64, _i64, _int, _vp, _vp, _i64, _vp,
                                ctypes.c_size_t, _vp, _vp]),
+        "vq_gategrad_noalloc": (_int, [_vp, _i64, _vp, _i64, _i64, _i64, _i64, _int, _vp, _vp, _i64, _vp, _vp]),
         "vq_mixgemm_fwd": (_int, [_vp, _i64, _i64, _i64, _int, _vp, _vp, _vp, _i64, _i64, _vp, _i64, _vp,
                                   _i64, _vp]),
         "vq_loss_fused": (_int, [_vp, _i64, _vp, _i64, _vp, _i64, _i64, _f32, _f32, _f32, _vp, _vp, _vp,
@@ -66,7 +67,8 @@ def _declare(lib):
 
 EXPORTED = (
     "vq_last_error", "vq_abi_version", "vq_format_info", "vq_device_error", "vq_dequant", "vq_mix",
-    "vq_linear_fwd", "vq_linear_dx", "vq_gategrad_workspace_bytes", "vq_gategrad", "vq_mixgemm_fwd",
+    "vq_linear_fwd", "vq_linear_dx", "vq_gategrad_workspace_bytes", "vq_gategrad", "vq_gategrad_noalloc",
+    "vq_mixgemm_fwd",
     "vq_loss_fused", "vq_loss_stats", "vq_loss_combine", "vq_loss_grad",
 )
 
@@ -221,6 +223,21 @@ def gategrad(dy: torch.Tensor, x: torch.Tensor, qtypes, qbytes, n_out: int, in_f
     _check(_lib.vq_gategrad(dy.data_ptr(), dy.stride(0), x.data_ptr(), x.stride(0), x.shape[0], n_out, in_features,
                             K, types, ptrs, padded_cols, workspace.data_ptr(), workspace.numel(), g.data_ptr(),
                             _stream(x)))
+    return g
+
+
+def gategrad_noalloc(dy: torch.Tensor, x: torch.Tensor, qtypes, qbytes, n_out: int, in_features: int,
+                     padded_cols: int) -> torch.Tensor:
+    """``gategrad`` on the library's own fixed scratch (vq_gategrad_noalloc), for
+    callers that cannot allocate device scratch; the result still needs a [K]
+    output tensor.  Calls that overlap on the GPU race on the shared scratch."""
+    _require_cuda(dy, x, *qbytes)
+    dy = _as_operand(dy)
+    x = _as_operand(x)
+    K, types, ptrs = _cand_arrays(qtypes, qbytes)
+    g = torch.empty(K, dtype=torch.float32, device=x.device)
+    _check(_lib.vq_gategrad_noalloc(dy.data_ptr(), dy.stride(0), x.data_ptr(), x.stride(0), x.shape[0], n_out,
+                                    in_features, K, types, ptrs, padded_cols, g.data_ptr(), _stream(x)))
     return g
 
 
