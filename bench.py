@@ -477,8 +477,194 @@ def run_ncu_case():
     print("ncu case ok", flush=True)
 
 
+_OUR_KERNELS = ("gemm_kernel", "gemm_pair_kernel", "mix_units_kernel", "dequant_units_kernel",
+                "gategrad_reduce_kernel", "loss_fused_kernel", "loss_stats_kernel", "loss_combine_kernel",
+                "loss_grad_kernel")
+
+
+def _count_our_launches(fn):
+    """Kernels of libvoodoo_b200 launched by one call of fn (CUPTI via torch.profiler)."""
+    import torch
+
+    try:
+        with torch.profiler.profile(activities=[torch.profiler.ProfilerActivity.CUDA]) as prof:
+            fn()
+            torch.cuda.synchronize()
+        names = [e.name for e in prof.events() if e.device_type == torch.autograd.DeviceType.CUDA]
+        return sum(1 for n in names if any(k in n for k in _OUR_KERNELS))
+    except Exception:  # profiler unavailable: no claim
+        return None
+
+
+def _print_step_profile(fn, top: int = 30):
+    """Device time per kernel name over one call of fn (CUPTI via torch.profiler),
+    printed to stderr as a table: name, launches, total ms, share."""
+    import torch
+
+    with torch.profiler.profile(activities=[torch.profiler.ProfilerActivity.CUDA]) as prof:
+        fn()
+        torch.cuda.synchronize()
+    agg = {}
+    for e in prof.events():
+        if e.device_type != torch.autograd.DeviceType.CUDA:
+            continue
+        n, t = agg.get(e.name, (0, 0.0))
+        agg[e.name] = (n + 1, t + e.device_time_total / 1e3)
+    total = sum(t for _, t in agg.values()) or 1.0
+    print(f"[step profile] {len(agg)} kernel names, {sum(n for n, _ in agg.values())} launches, "
+          f"{total:.2f} ms device time", file=sys.stderr)
+    for name, (n, t) in sorted(agg.items(), key=lambda kv: -kv[1][1])[:top]:
+        print(f"[step profile] {t:9.3f} ms {100 * t / total:5.1f}% {n:6d}x  {name[:110]}", file=sys.stderr)
+
+
+def step_flops_per_token(shape) -> float:
+    """Algorithmic FLOPs per token of the distillation step: student linear
+    layers 6 x params (forward, dX and the gate-gradient GEMM), a tied
+    (unquantised) student head 4 x params (forward and dX), an untied gated
+    head 6 x, the teacher 2 x its linear params, and causal attention
+    4 * L * (S / 2) * d_attn per token forward (x3 student, x1 teacher)."""
+    hd = shape.head_dim or shape.hidden // shape.heads
+    d_attn = shape.heads * hd
+    p_layers = shape.layers * (shape.hidden * (shape.heads + 2 * shape.kv_heads) * hd + d_attn * shape.hidden +
+                               3 * shape.hidden * shape.ffn)
+    p_head = shape.vocab * shape.hidden
+    student = 6 * p_layers + (4 if shape.tied else 6) * p_head
+    teacher = 2 * (p_layers + p_head)
+    attn = 4 * shape.layers * (shape.seq / 2) * d_attn * 4
+    return float(student + teacher + attn)
+
+
+def run_model_step(args):
+    """Full gated distillation step of a synthetic model config: student
+    (every Linear and the embedding gated, K candidates) forward, Q8_0 teacher
+    forward, fused CE + T^2 KL loss, size term, backward, clip, AdamW and
+    cosine LR.  Tokens per step = batch x seq.  Under torchrun (N > 1) both
+    models are tensor-parallel over the N GPUs (Llama adapter: q/k/v by heads,
+    o row-parallel, gate/up column, down row, vocab-parallel embedding, head
+    and loss) and every rank runs the same batch; value = tokens / max-over-
+    ranks step time."""
+    import torch
+    import torch.distributed as dist
+    from voodoo_quant import _C
+    from voodoo_quant.training import synthetic as S
+    from voodoo_quant.training.trainer import StepArgs, build_distill
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        from datetime import timedelta
+        from voodoo_quant import parallel
+
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=300))
+        parallel.adopt_process_group(local)
+    _C.load_library()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(v: float) -> float:
+        t = torch.tensor([v], device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    t_build = time.perf_counter()
+    trainer, shape = build_distill(args.workload, dev, seed=0, tp=world > 1,
+                                   args=StepArgs(max_steps=args.warmup + args.steps + args.e2e_steps + 3))
+    torch.cuda.synchronize()
+    t_build = time.perf_counter() - t_build
+    x, y = S.random_tokens(shape, dev, seed=1)
+    tokens = x.numel()
+    stream = torch.cuda.current_stream()
+    for _ in range(args.warmup):
+        trainer.step(x, y)
+    torch.cuda.synchronize()
+    barrier()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clk = ClockSampler(local).start()
+    barrier()
+    torch.cuda.synchronize()
+    clk.mark_start()
+    ev0.record(stream)
+    for _ in range(args.steps):
+        out = trainer.step(x, y)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    clk.mark_end()
+    barrier()
+    clk.stop()
+    ms = max_over_ranks(ev0.elapsed_time(ev1) / args.steps)
+    assert torch.isfinite(out["loss"]).item() and _C.device_error() == 0
+
+    # e2e: token ids from pinned host memory each step, the loss read back each step
+    xh, yh = x.cpu().pin_memory(), y.cpu().pin_memory()
+    lh = torch.empty((), dtype=torch.float32).pin_memory()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(args.e2e_steps):
+        xd = xh.to(dev, non_blocking=True)
+        yd = yh.to(dev, non_blocking=True)
+        o = trainer.step(xd, yd)
+        lh.copy_(o["loss"], non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.e2e_steps)
+    launches = _count_our_launches(lambda: trainer.step(x, y))
+    if args.profile_step:
+        _print_step_profile(lambda: trainer.step(x, y)) if rank == 0 else trainer.step(x, y)
+    torch.cuda.synchronize()
+
+    if rank == 0:
+        pk, pk_kind = peaks()
+        peak_t = float(pk.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"]))
+        fpt = step_flops_per_token(shape)
+        ach = fpt * tokens / (ms * 1e-3) / 1e12
+        res = {
+            "metric": METRIC,
+            "value": round(tokens / (ms * 1e-3), 1),
+            "unit": "tokens/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms, 3),
+            "higher_is_better": True,
+            "scaling": "strong",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic (seeded random-init weights and tokens; candidates from the round-to-nearest packer)",
+            "config": {"workload": f"{args.workload}: full gated distillation step", "layers": shape.layers,
+                       "hidden": shape.hidden, "ffn": shape.ffn, "vocab": shape.vocab, "tied": shape.tied,
+                       "batch": shape.batch, "seq": shape.seq, "candidates": shape.candidates,
+                       "gated_tensors": len(trainer.replaced), "budget": shape.budget,
+                       "parallelism": f"tp{world}", "build_s": round(t_build, 1),
+                       "l2": "activations and logits far larger than L2"},
+            "roofline": {"bound": "tensor", "kernel": "whole step", "flops_per_token": fpt,
+                         "achieved": round(ach, 1), "peak": round(peak_t * world, 1), "unit": "TFLOP/s",
+                         "frac": round(ach / (peak_t * world), 4),
+                         "peak_source": f"{pk_kind} bf16_tflops_sustained x {world} GPUs", "traffic": None},
+            "e2e": {"value": round(tokens / (e2e_ms * 1e-3), 1), "unit": "tokens/s",
+                    "h2d_bytes_per_step": int(2 * tokens * 8), "d2h_bytes_per_step": 4},
+            "gpu_launches": launches * args.steps if launches is not None else None,
+            "clocks": clk.summary(),
+            "loss_last": round(float(out["loss"]), 4),
+            "size_bytes_last": float(out["size_bytes"]),
+        }
+        print(json.dumps(res), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
+    ap.add_argument("--workload", choices=["layer", "tiny", "0.6b", "8b"], default="layer",
+                    help="layer: the single gated-Linear step (default); others: full distillation step")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=60)
     ap.add_argument("--warmup", type=int, default=3)
@@ -487,12 +673,16 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--cpu-tokens", type=int, default=2048)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile-step", action="store_true",
+                    help="full-step workloads: print device time per kernel name for one step")
     ap.add_argument("--ncu-case", action="store_true", help="one launch per kernel at profiling sizes")
     args = ap.parse_args()
     if args.ncu_case:
         run_ncu_case()
     elif args.impl == "reference":
         run_reference(args)
+    elif args.workload != "layer":
+        run_model_step(args)
     else:
         run_gpu(args)
 

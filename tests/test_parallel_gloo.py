@@ -167,3 +167,69 @@ def test_tp2_mlp_stack_gate_gradients(exact):
         # the reference's behaviour: block 1's gate gradient is computed from a
         # partial upstream gradient and is off after the cross-rank sum
         assert abs(r0["gates"][0] - g_ref[0]) > 1e-3 * abs(g_ref[0])
+
+
+def _tiny_llama():
+    from transformers import LlamaConfig, LlamaForCausalLM
+
+    cfg = LlamaConfig(vocab_size=1000, hidden_size=512, intermediate_size=1024, num_hidden_layers=2,
+                      num_attention_heads=4, num_key_value_heads=2, head_dim=128, rms_norm_eps=1e-6,
+                      rope_theta=1e4, tie_word_embeddings=False, max_position_embeddings=64)
+    cfg._attn_implementation = "sdpa"
+    torch.manual_seed(11)
+    m = LlamaForCausalLM(cfg).double()
+    with torch.no_grad():
+        for n, p in m.named_parameters():
+            p.copy_(torch.randn_like(p) * (0.3 if n.endswith("norm.weight") else 0.05)
+                    + (1.0 if n.endswith("norm.weight") else 0.0))
+    ids = torch.randint(0, 1000, (2, 12), generator=torch.Generator().manual_seed(2))
+    G = torch.randn(2, 12, 1000, dtype=torch.float64, generator=torch.Generator().manual_seed(4))
+    return m, ids, G
+
+
+def _model_worker(rank, world, port, outdir):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    import torch.distributed as dist
+    from voodoo_quant import parallel as P
+
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        P.adopt_process_group(0)
+        m, ids, G = _tiny_llama()
+        P.tp_patch_model(m, verbose=False)
+        v0, v1 = m.lm_head.tp_vocab_start, m.lm_head.tp_vocab_end
+        logits = m(input_ids=ids).logits
+        (logits * G[..., v0:v1]).sum().backward()
+        norms = {n: p.grad.clone() for n, p in m.named_parameters() if n.endswith("norm.weight")}
+        emb = m.model.embed_tokens
+        torch.save({"logits": logits.detach(), "v": (v0, v1), "norms": norms,
+                    "emb_rows": (emb.tp_vocab_start, emb.tp_vocab_end), "emb_grad": emb.weight.grad.clone()},
+                   os.path.join(outdir, f"m{rank}.pt"))
+    finally:
+        P.reset_tp()
+        dist.destroy_process_group()
+
+
+def test_tp2_llama_model_matches_unsharded():
+    """The Llama adapter's full-model sharding (vocab-parallel embedding and
+    head, heads split for q/k/v/o, uneven-capable MLP split) reproduces the
+    unsharded logits, and with the exact input-gradient operators (including
+    the one on the vocab-parallel head input) every rank's replicated-parameter
+    gradients equal the unsharded ones."""
+    pytest.importorskip("transformers")
+    port = _free_port()
+    with tempfile.TemporaryDirectory() as td:
+        mp.start_processes(_model_worker, args=(2, port, td), nprocs=2, join=True, start_method="spawn")
+        rs = [torch.load(os.path.join(td, f"m{r}.pt")) for r in range(2)]
+    m, ids, G = _tiny_llama()
+    logits = m(input_ids=ids).logits
+    (logits * G).sum().backward()
+    for r in rs:
+        v0, v1 = r["v"]
+        assert torch.allclose(r["logits"], logits.detach()[..., v0:v1], rtol=1e-10, atol=1e-12)
+        for n, g in r["norms"].items():
+            ref = dict(m.named_parameters())[n].grad
+            assert torch.allclose(g, ref, rtol=1e-9, atol=1e-12), n
+        e0, e1 = r["emb_rows"]
+        assert torch.allclose(r["emb_grad"], m.model.embed_tokens.weight.grad[e0:e1], rtol=1e-9, atol=1e-12)
+    assert rs[0]["v"][1] == rs[1]["v"][0] and rs[1]["v"][1] == 1000

@@ -541,6 +541,11 @@ def replace_linear_with_mixed_quant(module: nn.Module, candidate_types: list[str
                 full_source_weight=full_w,
                 candidate_bytes=_provided(candidate_provider, full_name,
                                           full_w if full_w is not None else child.weight.data, types))
+            if getattr(child, "_tp_input_copy", False):
+                # the sharded child summed its input gradient over the ranks
+                # through a pre-hook; the gated layer does it inside its backward
+                from voodoo_quant.parallel import TP
+                new.reduce_input_grad = TP.exact_input_grad
             setattr(module, name, new)
             replaced[full_name] = new
         else:

@@ -429,7 +429,10 @@ def _shard_lm_head(model: nn.Module) -> None:
     if head is None or isinstance(head, ColumnParallelLinear):
         return
     off, n = even_split(head.out_features, TP.world_size, TP.rank)
-    _shard_child(holder, "lm_head", row_offset=off, row_len=n, vocab_start=off)
+    new = _shard_child(holder, "lm_head", row_offset=off, row_len=n, vocab_start=off)
+    # the final hidden state feeds only this vocab shard on each rank: its
+    # gradient is the sum over the ranks' shards (f operator on the head input)
+    _install_input_copy(new)
 
 
 def tp_patch_model(model: nn.Module, verbose: bool = True) -> nn.Module:
