@@ -39,6 +39,9 @@ TYPES = ["Q3_K", "Q4_K", "Q5_K", "Q6_K", "Q8_0"]
 TAU = 0.5
 METRIC = "gated-distill train tokens/s"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+# dram__bytes_read.sum + dram__bytes_write.sum per launch of each config-2 GEMM
+# at full size on one B200, from a single-pass ncu capture of this benchmark
+NCU_TRAFFIC_BYTES = {"fwd": 824.7e6, "dx": 1035.0e6, "gategrad": 1116.3e6}
 BPW = {"Q2_K": 84 / 256, "Q3_K": 110 / 256, "Q4_K": 144 / 256, "Q5_K": 176 / 256, "Q6_K": 210 / 256,
        "Q8_0": 34 / 32, "IQ4_XS": 136 / 256}
 
@@ -354,7 +357,8 @@ def run_gpu(args):
                 "unit": "TFLOP/s",
                 "frac": round(ach[dom] / peak_t, 4),
                 "peak_source": f"{pk_kind} bf16_tflops (burst)",
-                "traffic": None,
+                "traffic": NCU_TRAFFIC_BYTES[dom] if world == 1 else None,
+                "traffic_unit": "bytes per launch (ncu dram read+write, full size)",
                 "mix_gemm_frac": round(3 * flops_gemm / (gemm_ms * 1e-3) / 1e12 / peak_t, 4),
                 "step_frac": round(3 * flops_gemm / (ms * 1e-3) / 1e12 / peak_t, 4),
             },
@@ -450,9 +454,9 @@ def run_reference(args):
 
 
 def run_ncu_case():
-    """One launch each of the mix, gate-gradient and loss kernels at sizes an
-    ncu --set full capture finishes quickly (inputs still larger than L2):
-    config-2 candidates, gate gradient at T=4096, loss 1024 x 128256."""
+    """One launch each of the mix, forward GEMM, gate-gradient and loss kernels
+    at sizes an ncu --set full capture finishes quickly (inputs still larger
+    than L2): config-2 candidates, GEMMs at T=4096, loss 1024 x 128256."""
     import torch
     from voodoo_quant import _C
     from voodoo_quant.quants import rtn
@@ -463,9 +467,10 @@ def run_ncu_case():
     blocks = [rtn.quantize(w, q) for q in TYPES]
     del w
     probs = torch.softmax(torch.randn(len(TYPES), device=dev, generator=g), 0)
-    _C.mix(TYPES, blocks, probs, N_OUT, K_IN, K_IN)
+    wm = _C.mix(TYPES, blocks, probs, N_OUT, K_IN, K_IN)
     x = torch.randn(4096, K_IN, device=dev, generator=g).to(torch.bfloat16)
     dy = torch.randn(4096, N_OUT, device=dev, generator=g).to(torch.bfloat16)
+    _C.linear_fwd(x, wm, N_OUT, K_IN)
     _C.gategrad(dy, x, TYPES, blocks, N_OUT, K_IN, K_IN)
     V, R = 128256, 1024
     s = (torch.randn(R, V, device=dev, generator=g) * 3).to(torch.bfloat16)
