@@ -161,6 +161,44 @@ int vq_loss_grad(const void* s_logits, int64_t lds, const void* t_logits, int64_
                  int64_t vocab_start, int64_t rows, int64_t V, float temperature, const float* row_lse,
                  float ce_weight, float kl_weight, void* dlogits, int64_t ldg, void* stream);
 
+/* ---- Llama decoder-block elementwise work of the distillation step ----
+ * The reference's step runs the Hugging Face Llama block around the gated
+ * Linears (voodoo_quant/training/trainer.py:2538-2556 calls the student and
+ * teacher models); these replace that block's torch elementwise ops, one HBM
+ * pass each, bf16 in and out with fp32 arithmetic.  Row-major operands need a
+ * 16-byte aligned base and a leading dimension that is a multiple of 8. */
+
+/* y = w * bf16(x * rsqrt(mean(x^2) + eps)) per row of x[rows, D] (D % 8 == 0,
+ * D <= 8192, weight bf16[D]); rstd[rows] (float, may be NULL) keeps
+ * rsqrt(mean(x^2) + eps) for the backward.  Replaces LlamaRMSNorm.forward
+ * (transformers models/llama/modeling_llama.py). */
+int vq_rmsnorm_fwd(const void* x, int64_t ldx, int64_t rows, int64_t D, const void* weight, float eps, void* y,
+                   int64_t ldy, float* rstd, void* stream);
+
+/* dx = r * (g - n * mean(g * n)) with g = dy * w and n = x * r, r = rstd[row].
+ * The weight gradient is not produced (the step trains only the gates). */
+int vq_rmsnorm_bwd(const void* x, int64_t ldx, const void* dy, int64_t lddy, int64_t rows, int64_t D,
+                   const void* weight, const float* rstd, void* dx, int64_t lddx, void* stream);
+
+/* Rotary embedding of q [B, S, Hq, D] and k [B, S, Hk, D] in one launch
+ * (unit stride over D; HOST arrays q_strides/k_strides = {b, s, h} and
+ * cs_strides = {b, s} in elements, multiples of 8) with cos/sin [B, S, D];
+ * writes contiguous [B, S, H, D] outputs.  backward != 0 applies the
+ * transposed rotation (the input gradient).  D % 16 == 0.  Replaces
+ * apply_rotary_pos_emb / rotate_half (transformers modeling_llama.py). */
+int vq_rope(const void* q, const int64_t* q_strides, int64_t Hq, const void* k, const int64_t* k_strides, int64_t Hk,
+            const void* cos, const void* sin, const int64_t* cs_strides, int64_t B, int64_t S, int64_t D, int backward,
+            void* q_out, void* k_out, void* stream);
+
+/* y = silu(gate) * up over [rows, F] (F % 8 == 0).  Replaces
+ * LlamaMLP.forward's act_fn(gate_proj(x)) * up_proj(x) product. */
+int vq_swiglu_fwd(const void* gate, int64_t ldg, const void* up, int64_t ldu, int64_t rows, int64_t F, void* y,
+                  int64_t ldy, void* stream);
+
+/* dgate = dy * up * silu'(gate), dup = dy * silu(gate); both outputs share ldo. */
+int vq_swiglu_bwd(const void* gate, int64_t ldg, const void* up, int64_t ldu, const void* dy, int64_t lddy, int64_t rows,
+                  int64_t F, void* dgate, void* dup, int64_t ldo, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,121 @@
+"""Fused Llama-block kernels (RMSNorm, rotary embedding, SwiGLU) through the
+C ABI against plain PyTorch fp32 references of the same ops, forward and
+backward, and a patched model against the unpatched Hugging Face model.
+
+Tolerance: 1e-2 relative (L2) for every bf16 output against the fp32
+reference; bf16 results of the same op differ by at most one or two roundings.
+"""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+from conftest import cosine, rel_err
+
+pytestmark = pytest.mark.gpu
+
+
+def _rel(a: torch.Tensor, b: torch.Tensor) -> float:
+    return rel_err(a.detach().float().cpu().numpy(), b.detach().float().cpu().numpy())
+
+
+def _rms_ref(x, w, eps):
+    return w.float() * (x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + eps))
+
+
+@pytest.mark.parametrize("rows,D", [(1, 1024), (37, 1024), (300, 4096), (64, 5120), (5, 8192), (3, 8)])
+def test_rmsnorm_forward_backward(cuda, rows, D):
+    from voodoo_quant import _C
+
+    g = torch.Generator(device="cpu").manual_seed(rows * 7 + D)
+    x = (torch.randn(rows, D, generator=g) * 3).to(cuda, torch.bfloat16)
+    w = (1 + 0.3 * torch.randn(D, generator=g)).to(cuda, torch.bfloat16)
+    dy = torch.randn(rows, D, generator=g).to(cuda, torch.bfloat16)
+    y, rstd = _C.rmsnorm_fwd(x, w, 1e-6)
+    xf = x.float().requires_grad_(True)
+    yr = _rms_ref(xf, w, 1e-6)
+    assert _rel(y, yr.detach()) < 1e-2
+    assert torch.allclose(rstd, torch.rsqrt(x.float().pow(2).mean(-1) + 1e-6), rtol=1e-5)
+    yr.backward(dy.float())
+    dx = _C.rmsnorm_bwd(x, dy, w, rstd)
+    assert _rel(dx, xf.grad) < 1e-2
+
+
+@pytest.mark.parametrize("B,S,Hq,Hk,D", [(2, 33, 4, 2, 128), (1, 8, 3, 1, 64), (2, 16, 8, 8, 16)])
+def test_rope_forward_backward(cuda, B, S, Hq, Hk, D):
+    from voodoo_quant import _C
+
+    g = torch.Generator(device="cpu").manual_seed(B * 100 + S + D)
+    # q/k as the attention builds them: views of a projection output [B, S, H * D]
+    q = torch.randn(B, S, Hq * D, generator=g).to(cuda, torch.bfloat16).view(B, S, Hq, D)
+    k = torch.randn(B, S, Hk * D, generator=g).to(cuda, torch.bfloat16).view(B, S, Hk, D)
+    ang = torch.randn(B, S, D // 2, generator=g) * 3
+    cos = torch.cat([ang.cos(), ang.cos()], -1).to(cuda, torch.bfloat16)
+    sin = torch.cat([ang.sin(), ang.sin()], -1).to(cuda, torch.bfloat16)
+
+    def ref(t):
+        h = t.shape[-1] // 2
+        rot = torch.cat([-t[..., h:], t[..., :h]], -1)
+        return t * cos.float()[:, :, None] + rot * sin.float()[:, :, None]
+
+    qf, kf = q.float().requires_grad_(True), k.float().requires_grad_(True)
+    qr, kr = ref(qf), ref(kf)
+    qo, ko = _C.rope(q, k, cos, sin)
+    assert qo.is_contiguous() and qo.shape == q.shape
+    assert _rel(qo, qr.detach()) < 1e-2 and _rel(ko, kr.detach()) < 1e-2
+    gq = torch.randn(B, Hq, S, D, generator=g).to(cuda, torch.bfloat16).transpose(1, 2)  # SDPA-like layout
+    gk = torch.randn(B, Hk, S, D, generator=g).to(cuda, torch.bfloat16).transpose(1, 2)
+    torch.autograd.backward([qr, kr], [gq.float(), gk.float()])
+    dq, dk = _C.rope(gq, gk, cos, sin, backward=True)
+    assert _rel(dq, qf.grad) < 1e-2 and _rel(dk, kf.grad) < 1e-2
+
+
+@pytest.mark.parametrize("rows,F", [(1, 8), (129, 3072), (64, 14336)])
+def test_swiglu_forward_backward(cuda, rows, F):
+    from voodoo_quant import _C
+
+    g = torch.Generator(device="cpu").manual_seed(rows + F)
+    a = (torch.randn(rows, F, generator=g) * 2).to(cuda, torch.bfloat16)
+    u = torch.randn(rows, F, generator=g).to(cuda, torch.bfloat16)
+    dy = torch.randn(rows, F, generator=g).to(cuda, torch.bfloat16)
+    af, uf = a.float().requires_grad_(True), u.float().requires_grad_(True)
+    yr = torch.nn.functional.silu(af) * uf
+    assert _rel(_C.swiglu_fwd(a, u), yr.detach()) < 1e-2
+    yr.backward(dy.float())
+    da, du = _C.swiglu_bwd(a, u, dy)
+    assert _rel(da, af.grad) < 1e-2 and _rel(du, uf.grad) < 1e-2
+
+
+def test_block_kernels_reject_bad_shapes(cuda):
+    from voodoo_quant import _C
+
+    lib = _C.load_library()
+    x = torch.zeros(4, 12, dtype=torch.bfloat16, device=cuda)
+    w = torch.ones(12, dtype=torch.bfloat16, device=cuda)
+    rc = lib.vq_rmsnorm_fwd(x.data_ptr(), 12, 4, 12, w.data_ptr(), 1e-6, x.data_ptr(), 12, None, None)
+    assert rc == _C.VQ_ERR_INVALID and b"multiple of 8" in lib.vq_last_error()
+    with pytest.raises(ValueError, match="multiple of 16"):
+        q = torch.zeros(1, 2, 1, 8, dtype=torch.bfloat16, device=cuda)
+        _C.rope(q, q, q[0, :, 0], q[0, :, 0])
+
+
+def test_fused_llama_blocks_match_unpatched_model(cuda):
+    from voodoo_quant.fused_blocks import fuse_llama_blocks
+    from voodoo_quant.training import synthetic as S
+
+    shape = S.ModelShape(2, 512, 4, 2, 1536, 2048, False, head_dim=128, batch=2, seq=64)
+    ref = S.build_llama(shape, cuda, seed=4)
+    fused = S.build_llama(shape, cuda, seed=4)
+    assert fuse_llama_blocks(fused) == 2 * 4 + 1 and fuse_llama_blocks(fused) == 0
+    x, _ = S.random_tokens(shape, cuda, seed=5)
+    e_ref = ref.model.embed_tokens(x).detach().requires_grad_(True)
+    e_fus = e_ref.detach().clone().requires_grad_(True)
+    l_ref = ref(inputs_embeds=e_ref, use_cache=False).logits
+    l_fus = fused(inputs_embeds=e_fus, use_cache=False).logits
+    assert _rel(l_fus, l_ref) < 1e-2
+    gy = torch.randn_like(l_ref)
+    l_ref.backward(gy)
+    l_fus.backward(gy)
+    assert _rel(e_fus.grad, e_ref.grad) < 2e-2
+    assert cosine(e_fus.grad.double().flatten().cpu().numpy(), e_ref.grad.double().flatten().cpu().numpy()) > 0.999

@@ -49,3 +49,18 @@ def test_build_tiny_distill_on_host():
     assert start == 0.5
     with pytest.raises(RuntimeError, match="CUDA"):
         trainer.student(input_ids=torch.zeros(1, 4, dtype=torch.long))
+
+
+def test_fused_blocks_leave_cpu_models_unchanged():
+    """Patched modules run their original forward off the fused path (CPU here)."""
+    pytest.importorskip("transformers")
+    from voodoo_quant.fused_blocks import fuse_llama_blocks
+    from voodoo_quant.training import synthetic as S
+
+    shape = S.SHAPES["tiny"]
+    a = S.build_llama(shape, "cpu", seed=2)
+    b = S.build_llama(shape, "cpu", seed=2)
+    assert fuse_llama_blocks(b) == 2 * 4 + 1
+    x = torch.randint(0, shape.vocab, (1, 16))
+    with torch.no_grad():
+        assert torch.equal(a(input_ids=x, use_cache=False).logits, b(input_ids=x, use_cache=False).logits)

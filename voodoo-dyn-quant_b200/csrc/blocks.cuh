@@ -1,0 +1,240 @@
+// Fused elementwise kernels of the Llama decoder block around the gated
+// Linears of the distillation step (HBM-bandwidth bound, one pass each):
+//
+//   RMSNorm   y = w * bf16(x * rsqrt(mean(x^2) + eps))            (fwd)
+//             dx = r * (g - n * mean(g * n)),  g = dy * w, n = x * r (bwd)
+//   RoPE      out[:h] = x[:h] * cos[:h] - x[h:] * sin[:h]
+//             out[h:] = x[h:] * cos[h:] + x[:h] * sin[h:]   (h = D/2, fwd)
+//             dx[:h]  = g[:h] * cos[:h] + g[h:] * sin[h:]
+//             dx[h:]  = g[h:] * cos[h:] - g[:h] * sin[:h]         (bwd)
+//   SwiGLU    y = silu(a) * u,  da = dy * u * silu'(a),  du = dy * silu(a)
+//
+// The reference runs these as separate torch ops of the Hugging Face Llama
+// block (LlamaRMSNorm.forward: fp32 cast, pow, mean, rsqrt, two multiplies;
+// apply_rotary_pos_emb: rotate_half's neg + cat, two multiplies and an add
+// on the transposed q/k views; act_fn(gate) * up), i.e. 3-6 HBM passes each
+// plus their backward passes.  Here each is one pass of 16-byte vectors in
+// fp32 registers with a single rounding to bf16.
+#pragma once
+
+#include <cuda_bf16.h>
+
+#include <cstdint>
+
+namespace vq {
+namespace blocks {
+
+constexpr int kNormThreads = 128;
+constexpr int kRopeThreads = 128;
+constexpr int kEltThreads = 256;
+
+struct V8 {  // 8 bf16 values widened to fp32
+  float v[8];
+};
+
+__device__ __forceinline__ V8 load8(const __nv_bfloat16* p) {
+  const uint4 raw = *reinterpret_cast<const uint4*>(p);
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+  V8 r;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __bfloat1622float2(h[i]);
+    r.v[2 * i] = f.x;
+    r.v[2 * i + 1] = f.y;
+  }
+  return r;
+}
+
+__device__ __forceinline__ void store8(__nv_bfloat16* p, const V8& r) {
+  uint4 raw;
+  __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&raw);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(r.v[2 * i], r.v[2 * i + 1]);
+  *reinterpret_cast<uint4*>(p) = raw;
+}
+
+__device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+// Sum over the CTA (kNormThreads threads); every thread gets the total.
+__device__ __forceinline__ float block_sum(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __syncthreads();  // red may still be read by a previous call
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float t = 0.f;
+#pragma unroll
+  for (int w = 0; w < kNormThreads / 32; ++w) t += red[w];
+  return t;
+}
+
+// One CTA per row (grid-stride); a thread keeps VPT vectors of 8 in registers.
+template <int VPT>
+__global__ void __launch_bounds__(kNormThreads) rmsnorm_fwd_kernel(const __nv_bfloat16* __restrict__ x, long long ldx,
+                                                                  const __nv_bfloat16* __restrict__ w, float eps,
+                                                                  int rows, int D, __nv_bfloat16* __restrict__ y,
+                                                                  long long ldy, float* __restrict__ rstd) {
+  __shared__ float red[kNormThreads / 32];
+  const int nvec = D >> 3;
+  for (int row = blockIdx.x; row < rows; row += gridDim.x) {
+    const __nv_bfloat16* xr = x + static_cast<long long>(row) * ldx;
+    V8 v[VPT];
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) {
+      const int c = threadIdx.x + j * kNormThreads;
+      if (c < nvec) {
+        v[j] = load8(xr + 8 * c);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) ss = fmaf(v[j].v[i], v[j].v[i], ss);
+      }
+    }
+    const float r = rsqrtf(block_sum(ss, red) / static_cast<float>(D) + eps);
+    if (threadIdx.x == 0 && rstd != nullptr) rstd[row] = r;
+    __nv_bfloat16* yr = y + static_cast<long long>(row) * ldy;
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) {
+      const int c = threadIdx.x + j * kNormThreads;
+      if (c < nvec) {
+        const V8 wv = load8(w + 8 * c);
+        V8 o;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) o.v[i] = wv.v[i] * bf16_round(v[j].v[i] * r);
+        store8(yr + 8 * c, o);
+      }
+    }
+  }
+}
+
+template <int VPT>
+__global__ void __launch_bounds__(kNormThreads) rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ x, long long ldx,
+                                                                  const __nv_bfloat16* __restrict__ dy, long long lddy,
+                                                                  const __nv_bfloat16* __restrict__ w,
+                                                                  const float* __restrict__ rstd, int rows, int D,
+                                                                  __nv_bfloat16* __restrict__ dx, long long lddx) {
+  __shared__ float red[kNormThreads / 32];
+  const int nvec = D >> 3;
+  for (int row = blockIdx.x; row < rows; row += gridDim.x) {
+    const float r = rstd[row];
+    const __nv_bfloat16* xr = x + static_cast<long long>(row) * ldx;
+    const __nv_bfloat16* gr = dy + static_cast<long long>(row) * lddy;
+    V8 n[VPT], g[VPT];
+    float dot = 0.f;
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) {
+      const int c = threadIdx.x + j * kNormThreads;
+      if (c < nvec) {
+        n[j] = load8(xr + 8 * c);
+        g[j] = load8(gr + 8 * c);
+        const V8 wv = load8(w + 8 * c);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          n[j].v[i] *= r;
+          g[j].v[i] *= wv.v[i];
+          dot = fmaf(g[j].v[i], n[j].v[i], dot);
+        }
+      }
+    }
+    const float m = block_sum(dot, red) / static_cast<float>(D);
+    __nv_bfloat16* dr = dx + static_cast<long long>(row) * lddx;
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) {
+      const int c = threadIdx.x + j * kNormThreads;
+      if (c < nvec) {
+        V8 o;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) o.v[i] = r * (g[j].v[i] - n[j].v[i] * m);
+        store8(dr + 8 * c, o);
+      }
+    }
+  }
+}
+
+struct RopeSide {            // one of q / k
+  const __nv_bfloat16* in;   // [B, S, H, D] with strides (sb, ss, sh) elements, unit stride over D
+  long long sb, ss, sh;
+  int H;
+  __nv_bfloat16* out;        // contiguous [B, S, H, D]
+};
+
+// One CTA per (b, s) position (grid-stride); a work item is 8 elements of
+// the first half of one head and the matching 8 of the second half.
+template <bool kBackward>
+__global__ void __launch_bounds__(kRopeThreads) rope_kernel(RopeSide q, RopeSide k, const __nv_bfloat16* __restrict__ cos,
+                                                            const __nv_bfloat16* __restrict__ sin, long long csb,
+                                                            long long css, int B, int S, int D) {
+  const int half = D >> 1;
+  const int per_head = half >> 3;
+  const int items = (q.H + k.H) * per_head;
+  const long long positions = static_cast<long long>(B) * S;
+  for (long long pos = blockIdx.x; pos < positions; pos += gridDim.x) {
+    const int b = static_cast<int>(pos / S), s = static_cast<int>(pos % S);
+    const __nv_bfloat16* cp = cos + b * csb + s * css;
+    const __nv_bfloat16* sp = sin + b * csb + s * css;
+    for (int it = threadIdx.x; it < items; it += kRopeThreads) {
+      int h = it / per_head;
+      const int c = (it - h * per_head) * 8;
+      const RopeSide& side = h < q.H ? q : k;
+      if (h >= q.H) h -= q.H;
+      const __nv_bfloat16* src = side.in + b * side.sb + s * side.ss + h * side.sh;
+      __nv_bfloat16* dst = side.out + ((pos * side.H + h) * static_cast<long long>(D));
+      const V8 x1 = load8(src + c), x2 = load8(src + half + c);
+      const V8 c1 = load8(cp + c), c2 = load8(cp + half + c);
+      const V8 s1 = load8(sp + c), s2 = load8(sp + half + c);
+      V8 o1, o2;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        if (kBackward) {
+          o1.v[i] = fmaf(x1.v[i], c1.v[i], x2.v[i] * s2.v[i]);
+          o2.v[i] = fmaf(x2.v[i], c2.v[i], -x1.v[i] * s1.v[i]);
+        } else {
+          o1.v[i] = fmaf(x1.v[i], c1.v[i], -x2.v[i] * s1.v[i]);
+          o2.v[i] = fmaf(x2.v[i], c2.v[i], x1.v[i] * s2.v[i]);
+        }
+      }
+      store8(dst + c, o1);
+      store8(dst + half + c, o2);
+    }
+  }
+}
+
+__device__ __forceinline__ float sigmoidf_(float a) { return 1.f / (1.f + __expf(-a)); }
+
+// Flat grid-stride over rows x (F / 8) vectors.
+template <bool kBackward>
+__global__ void __launch_bounds__(kEltThreads) swiglu_kernel(const __nv_bfloat16* __restrict__ a, long long lda,
+                                                             const __nv_bfloat16* __restrict__ u, long long ldu,
+                                                             const __nv_bfloat16* __restrict__ dy, long long lddy,
+                                                             int rows, int F, __nv_bfloat16* __restrict__ out0,
+                                                             __nv_bfloat16* __restrict__ out1, long long ldo) {
+  const int nvec = F >> 3;
+  const long long total = static_cast<long long>(rows) * nvec;
+  for (long long i = blockIdx.x * static_cast<long long>(kEltThreads) + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * kEltThreads) {
+    const long long r = i / nvec;
+    const int c = static_cast<int>(i - r * nvec) * 8;
+    const V8 av = load8(a + r * lda + c), uv = load8(u + r * ldu + c);
+    if (kBackward) {
+      const V8 gv = load8(dy + r * lddy + c);
+      V8 da, du;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float sg = sigmoidf_(av.v[j]);
+        const float act = av.v[j] * sg;
+        da.v[j] = gv.v[j] * uv.v[j] * (sg * (1.f + av.v[j] * (1.f - sg)));
+        du.v[j] = gv.v[j] * act;
+      }
+      store8(out0 + r * ldo + c, da);
+      store8(out1 + r * ldo + c, du);
+    } else {
+      V8 y;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) y.v[j] = av.v[j] * sigmoidf_(av.v[j]) * uv.v[j];
+      store8(out0 + r * ldo + c, y);
+    }
+  }
+}
+
+}  // namespace blocks
+}  // namespace vq

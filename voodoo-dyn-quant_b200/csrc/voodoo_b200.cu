@@ -21,6 +21,7 @@
 #include "decode_mix.cuh"
 #include "gemm_tc.cuh"
 #include "loss.cuh"
+#include "blocks.cuh"
 #include "../../include/voodoo_b200.h"
 
 namespace {
@@ -513,6 +514,164 @@ int vq_loss_grad(const void* s_logits, int64_t lds, const void* t_logits, int64_
   else
     vq::loss::loss_grad_kernel<false><<<grid, vq::loss::THREADS, 0, st>>>(S, lds, Tl, ldt, y, vocab_start, (int)rows, (int)V,
                                                                           temperature, row_lse, ce_weight, kl_weight, G, ldg, vec);
+  VQ_CUDA(cudaGetLastError());
+  return 0;
+}
+
+}  // extern "C"
+
+// ------------------------------------------------------------------ Llama block elementwise
+namespace {
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int check_rows16(const void* p, long long rows, long long cols, long long ld, const char* name) {
+  if (int rc = check_matrix(p, rows, cols, ld, name)) return rc;
+  if (rows > 0 && cols > 0 && (!aligned16(p) || ld % 8 != 0))
+    return fail(VQ_ERR_INVALID, "%s: base must be 16-byte aligned and the leading dimension a multiple of 8", name);
+  return 0;
+}
+
+int grid_for(long long work, int per_sm) {
+  int sms = 0;
+  if (sm_count(&sms) != 0 || sms <= 0) sms = 148;
+  const long long cap = static_cast<long long>(sms) * per_sm;
+  return static_cast<int>(work < cap ? (work > 0 ? work : 1) : cap);
+}
+
+}  // namespace
+
+extern "C" {
+
+int vq_rmsnorm_fwd(const void* x, int64_t ldx, int64_t rows, int64_t D, const void* weight, float eps, void* y,
+                   int64_t ldy, float* rstd, void* stream) {
+  DeviceScope scope(y);
+  if (D <= 0 || D % 8 != 0 || D > 8 * 8 * vq::blocks::kNormThreads)
+    return fail(VQ_ERR_INVALID, "RMSNorm width %lld must be a positive multiple of 8 up to %d", (long long)D,
+                8 * 8 * vq::blocks::kNormThreads);
+  if (int rc = check_rows16(x, rows, D, ldx, "x")) return rc;
+  if (int rc = check_rows16(y, rows, D, ldy, "y")) return rc;
+  if (weight == nullptr || !aligned16(weight)) return fail(VQ_ERR_INVALID, "weight must be a 16-byte aligned pointer");
+  if (rows == 0) return 0;
+  if (rows > 0x7fffffff) return fail(VQ_ERR_INVALID, "too many rows");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int vpt = static_cast<int>((D / 8 + vq::blocks::kNormThreads - 1) / vq::blocks::kNormThreads);
+  const int grid = grid_for(rows, 16);
+  const auto* X = static_cast<const __nv_bfloat16*>(x);
+  const auto* W = static_cast<const __nv_bfloat16*>(weight);
+  auto* Y = static_cast<__nv_bfloat16*>(y);
+  using namespace vq::blocks;
+  if (vpt <= 1) rmsnorm_fwd_kernel<1><<<grid, kNormThreads, 0, st>>>(X, ldx, W, eps, (int)rows, (int)D, Y, ldy, rstd);
+  else if (vpt <= 2) rmsnorm_fwd_kernel<2><<<grid, kNormThreads, 0, st>>>(X, ldx, W, eps, (int)rows, (int)D, Y, ldy, rstd);
+  else if (vpt <= 4) rmsnorm_fwd_kernel<4><<<grid, kNormThreads, 0, st>>>(X, ldx, W, eps, (int)rows, (int)D, Y, ldy, rstd);
+  else rmsnorm_fwd_kernel<8><<<grid, kNormThreads, 0, st>>>(X, ldx, W, eps, (int)rows, (int)D, Y, ldy, rstd);
+  VQ_CUDA(cudaGetLastError());
+  return 0;
+}
+
+int vq_rmsnorm_bwd(const void* x, int64_t ldx, const void* dy, int64_t lddy, int64_t rows, int64_t D,
+                   const void* weight, const float* rstd, void* dx, int64_t lddx, void* stream) {
+  DeviceScope scope(dx);
+  if (D <= 0 || D % 8 != 0 || D > 8 * 8 * vq::blocks::kNormThreads)
+    return fail(VQ_ERR_INVALID, "RMSNorm width %lld must be a positive multiple of 8 up to %d", (long long)D,
+                8 * 8 * vq::blocks::kNormThreads);
+  if (int rc = check_rows16(x, rows, D, ldx, "x")) return rc;
+  if (int rc = check_rows16(dy, rows, D, lddy, "dy")) return rc;
+  if (int rc = check_rows16(dx, rows, D, lddx, "dx")) return rc;
+  if (weight == nullptr || !aligned16(weight)) return fail(VQ_ERR_INVALID, "weight must be a 16-byte aligned pointer");
+  if (rows == 0) return 0;
+  if (rstd == nullptr) return fail(VQ_ERR_INVALID, "null rstd");
+  if (rows > 0x7fffffff) return fail(VQ_ERR_INVALID, "too many rows");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int vpt = static_cast<int>((D / 8 + vq::blocks::kNormThreads - 1) / vq::blocks::kNormThreads);
+  const int grid = grid_for(rows, 16);
+  const auto* X = static_cast<const __nv_bfloat16*>(x);
+  const auto* G = static_cast<const __nv_bfloat16*>(dy);
+  const auto* W = static_cast<const __nv_bfloat16*>(weight);
+  auto* DX = static_cast<__nv_bfloat16*>(dx);
+  using namespace vq::blocks;
+  if (vpt <= 1) rmsnorm_bwd_kernel<1><<<grid, kNormThreads, 0, st>>>(X, ldx, G, lddy, W, rstd, (int)rows, (int)D, DX, lddx);
+  else if (vpt <= 2) rmsnorm_bwd_kernel<2><<<grid, kNormThreads, 0, st>>>(X, ldx, G, lddy, W, rstd, (int)rows, (int)D, DX, lddx);
+  else if (vpt <= 4) rmsnorm_bwd_kernel<4><<<grid, kNormThreads, 0, st>>>(X, ldx, G, lddy, W, rstd, (int)rows, (int)D, DX, lddx);
+  else rmsnorm_bwd_kernel<8><<<grid, kNormThreads, 0, st>>>(X, ldx, G, lddy, W, rstd, (int)rows, (int)D, DX, lddx);
+  VQ_CUDA(cudaGetLastError());
+  return 0;
+}
+
+int vq_rope(const void* q, const int64_t* q_strides, int64_t Hq, const void* k, const int64_t* k_strides, int64_t Hk,
+            const void* cos, const void* sin, const int64_t* cs_strides, int64_t B, int64_t S, int64_t D, int backward,
+            void* q_out, void* k_out, void* stream) {
+  DeviceScope scope(q_out);
+  if (B < 0 || S < 0 || Hq < 0 || Hk < 0) return fail(VQ_ERR_INVALID, "negative shape");
+  if (D <= 0 || D % 16 != 0) return fail(VQ_ERR_INVALID, "head dimension %lld must be a multiple of 16", (long long)D);
+  if (B == 0 || S == 0 || Hq + Hk == 0) return 0;
+  if (q_strides == nullptr || k_strides == nullptr || cs_strides == nullptr)
+    return fail(VQ_ERR_INVALID, "null stride array");
+  const void* ptrs[6] = {q, k, cos, sin, q_out, k_out};
+  for (int i = 0; i < 6; ++i) {
+    if ((i == 1 || i == 5) && Hk == 0) continue;
+    if ((i == 0 || i == 4) && Hq == 0) continue;
+    if (ptrs[i] == nullptr || !aligned16(ptrs[i])) return fail(VQ_ERR_INVALID, "pointer %d is null or not 16-byte aligned", i);
+  }
+  const int64_t st3[6] = {q_strides[0], q_strides[1], q_strides[2], k_strides[0], k_strides[1], k_strides[2]};
+  for (int i = 0; i < 6; ++i)
+    if (st3[i] < 0 || st3[i] % 8 != 0) return fail(VQ_ERR_INVALID, "q/k strides must be non-negative multiples of 8");
+  if (cs_strides[0] < 0 || cs_strides[1] < 0 || cs_strides[0] % 8 != 0 || cs_strides[1] % 8 != 0)
+    return fail(VQ_ERR_INVALID, "cos/sin strides must be non-negative multiples of 8");
+  if (B * S > 0x7fffffffLL || Hq > 65535 || Hk > 65535) return fail(VQ_ERR_INVALID, "shape too large");
+  vq::blocks::RopeSide qs{static_cast<const __nv_bfloat16*>(q), q_strides[0], q_strides[1], q_strides[2], (int)Hq,
+                          static_cast<__nv_bfloat16*>(q_out)};
+  vq::blocks::RopeSide ks{static_cast<const __nv_bfloat16*>(k), k_strides[0], k_strides[1], k_strides[2], (int)Hk,
+                          static_cast<__nv_bfloat16*>(k_out)};
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int grid = grid_for(B * S, 16);
+  const auto* C = static_cast<const __nv_bfloat16*>(cos);
+  const auto* Sn = static_cast<const __nv_bfloat16*>(sin);
+  if (backward)
+    vq::blocks::rope_kernel<true><<<grid, vq::blocks::kRopeThreads, 0, st>>>(qs, ks, C, Sn, cs_strides[0], cs_strides[1],
+                                                                            (int)B, (int)S, (int)D);
+  else
+    vq::blocks::rope_kernel<false><<<grid, vq::blocks::kRopeThreads, 0, st>>>(qs, ks, C, Sn, cs_strides[0], cs_strides[1],
+                                                                             (int)B, (int)S, (int)D);
+  VQ_CUDA(cudaGetLastError());
+  return 0;
+}
+
+int vq_swiglu_fwd(const void* gate, int64_t ldg, const void* up, int64_t ldu, int64_t rows, int64_t F, void* y,
+                  int64_t ldy, void* stream) {
+  DeviceScope scope(y);
+  if (F <= 0 || F % 8 != 0) return fail(VQ_ERR_INVALID, "SwiGLU width %lld must be a positive multiple of 8", (long long)F);
+  if (int rc = check_rows16(gate, rows, F, ldg, "gate")) return rc;
+  if (int rc = check_rows16(up, rows, F, ldu, "up")) return rc;
+  if (int rc = check_rows16(y, rows, F, ldy, "y")) return rc;
+  if (rows == 0) return 0;
+  if (rows > 0x7fffffff) return fail(VQ_ERR_INVALID, "too many rows");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int grid = grid_for((rows * (F / 8) + vq::blocks::kEltThreads - 1) / vq::blocks::kEltThreads, 8);
+  vq::blocks::swiglu_kernel<false><<<grid, vq::blocks::kEltThreads, 0, st>>>(
+      static_cast<const __nv_bfloat16*>(gate), ldg, static_cast<const __nv_bfloat16*>(up), ldu, nullptr, 0, (int)rows,
+      (int)F, static_cast<__nv_bfloat16*>(y), nullptr, ldy);
+  VQ_CUDA(cudaGetLastError());
+  return 0;
+}
+
+int vq_swiglu_bwd(const void* gate, int64_t ldg, const void* up, int64_t ldu, const void* dy, int64_t lddy, int64_t rows,
+                  int64_t F, void* dgate, void* dup, int64_t ldo, void* stream) {
+  DeviceScope scope(dgate);
+  if (F <= 0 || F % 8 != 0) return fail(VQ_ERR_INVALID, "SwiGLU width %lld must be a positive multiple of 8", (long long)F);
+  if (int rc = check_rows16(gate, rows, F, ldg, "gate")) return rc;
+  if (int rc = check_rows16(up, rows, F, ldu, "up")) return rc;
+  if (int rc = check_rows16(dy, rows, F, lddy, "dy")) return rc;
+  if (int rc = check_rows16(dgate, rows, F, ldo, "dgate")) return rc;
+  if (int rc = check_rows16(dup, rows, F, ldo, "dup")) return rc;
+  if (rows == 0) return 0;
+  if (rows > 0x7fffffff) return fail(VQ_ERR_INVALID, "too many rows");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int grid = grid_for((rows * (F / 8) + vq::blocks::kEltThreads - 1) / vq::blocks::kEltThreads, 8);
+  vq::blocks::swiglu_kernel<true><<<grid, vq::blocks::kEltThreads, 0, st>>>(
+      static_cast<const __nv_bfloat16*>(gate), ldg, static_cast<const __nv_bfloat16*>(up), ldu,
+      static_cast<const __nv_bfloat16*>(dy), lddy, (int)rows, (int)F, static_cast<__nv_bfloat16*>(dgate),
+      static_cast<__nv_bfloat16*>(dup), ldo);
   VQ_CUDA(cudaGetLastError());
   return 0;
 }

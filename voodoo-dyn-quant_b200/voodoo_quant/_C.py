@@ -57,6 +57,11 @@ def _declare(lib):
         "vq_loss_combine": (_int, [_vp, _int, _i64, _f32, _vp, _vp, _vp, _vp]),
         "vq_loss_grad": (_int, [_vp, _i64, _vp, _i64, _vp, _i64, _i64, _i64, _f32, _vp, _f32, _f32, _vp,
                                 _i64, _vp]),
+        "vq_rmsnorm_fwd": (_int, [_vp, _i64, _i64, _i64, _vp, _f32, _vp, _i64, _vp, _vp]),
+        "vq_rmsnorm_bwd": (_int, [_vp, _i64, _vp, _i64, _i64, _i64, _vp, _vp, _vp, _i64, _vp]),
+        "vq_rope": (_int, [_vp, _vp, _i64, _vp, _vp, _i64, _vp, _vp, _vp, _i64, _i64, _i64, _int, _vp, _vp, _vp]),
+        "vq_swiglu_fwd": (_int, [_vp, _i64, _vp, _i64, _i64, _i64, _vp, _i64, _vp]),
+        "vq_swiglu_bwd": (_int, [_vp, _i64, _vp, _i64, _vp, _i64, _i64, _i64, _vp, _vp, _i64, _vp]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -70,6 +75,7 @@ EXPORTED = (
     "vq_linear_fwd", "vq_linear_dx", "vq_gategrad_workspace_bytes", "vq_gategrad", "vq_gategrad_noalloc",
     "vq_mixgemm_fwd",
     "vq_loss_fused", "vq_loss_stats", "vq_loss_combine", "vq_loss_grad",
+    "vq_rmsnorm_fwd", "vq_rmsnorm_bwd", "vq_rope", "vq_swiglu_fwd", "vq_swiglu_bwd",
 )
 
 
@@ -303,3 +309,90 @@ def loss_grad(s: torch.Tensor, t: torch.Tensor, targets: torch.Tensor, vocab_sta
                              V, float(temperature), row_lse.contiguous().data_ptr(), float(ce_weight),
                              float(kl_weight), g.data_ptr(), g.stride(0), _stream(s)))
     return g
+
+
+# ---------------------------------------------------------------- Llama block elementwise
+def _rows_operand(t: torch.Tensor) -> torch.Tensor:
+    """bf16 2-D view with unit column stride, 16-byte aligned rows."""
+    t = t.to(torch.bfloat16)
+    if t.stride(-1) != 1 or t.stride(0) % 8 != 0 or t.data_ptr() % 16 != 0:
+        t = t.contiguous()
+    return t
+
+
+def rmsnorm_fwd(x: torch.Tensor, weight: torch.Tensor, eps: float):
+    """(y [rows, D] bf16, rstd [rows] float32) for x [rows, D]."""
+    _require_cuda(x, weight)
+    x = _rows_operand(x)
+    w = weight.to(torch.bfloat16).contiguous()
+    rows, D = x.shape
+    y = torch.empty(rows, D, dtype=torch.bfloat16, device=x.device)
+    rstd = torch.empty(rows, dtype=torch.float32, device=x.device)
+    _check(_lib.vq_rmsnorm_fwd(x.data_ptr(), x.stride(0), rows, D, w.data_ptr(), float(eps), y.data_ptr(), y.stride(0),
+                               rstd.data_ptr(), _stream(x)))
+    return y, rstd
+
+
+def rmsnorm_bwd(x: torch.Tensor, dy: torch.Tensor, weight: torch.Tensor, rstd: torch.Tensor) -> torch.Tensor:
+    _require_cuda(x, dy, weight, rstd)
+    x = _rows_operand(x)
+    dy = _rows_operand(dy)
+    w = weight.to(torch.bfloat16).contiguous()
+    rows, D = x.shape
+    dx = torch.empty(rows, D, dtype=torch.bfloat16, device=x.device)
+    _check(_lib.vq_rmsnorm_bwd(x.data_ptr(), x.stride(0), dy.data_ptr(), dy.stride(0), rows, D, w.data_ptr(),
+                               rstd.contiguous().data_ptr(), dx.data_ptr(), dx.stride(0), _stream(x)))
+    return dx
+
+
+def _bshd(t: torch.Tensor) -> torch.Tensor:
+    t = t.to(torch.bfloat16)
+    if t.stride(-1) != 1 or any(st % 8 for st in t.stride()[:3]) or t.data_ptr() % 16 != 0:
+        t = t.contiguous()
+    return t
+
+
+def rope(q: torch.Tensor, k: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, backward: bool = False):
+    """Rotary embedding of q [B, S, Hq, D] and k [B, S, Hk, D] with cos/sin
+    [B, S, D] (any strides with unit stride over D); returns contiguous
+    [B, S, H, D] outputs (the transposed rotation when ``backward``)."""
+    _require_cuda(q, k, cos, sin)
+    q, k = _bshd(q), _bshd(k)
+    B, S, Hq, D = q.shape
+    Hk = k.shape[2]
+    cos = cos.to(torch.bfloat16).expand(B, S, D)
+    sin = sin.to(torch.bfloat16).expand(B, S, D)
+    if cos.stride() != sin.stride() or cos.stride(-1) != 1 or cos.data_ptr() % 16 or sin.data_ptr() % 16 or \
+            any(st % 8 for st in cos.stride()[:2]):
+        cos, sin = cos.contiguous(), sin.contiguous()
+    qo = torch.empty(B, S, Hq, D, dtype=torch.bfloat16, device=q.device)
+    ko = torch.empty(B, S, Hk, D, dtype=torch.bfloat16, device=q.device)
+    qs = (ctypes.c_int64 * 3)(q.stride(0), q.stride(1), q.stride(2))
+    ks = (ctypes.c_int64 * 3)(k.stride(0), k.stride(1), k.stride(2))
+    cs = (ctypes.c_int64 * 2)(cos.stride(0), cos.stride(1))
+    _check(_lib.vq_rope(q.data_ptr(), qs, Hq, k.data_ptr(), ks, Hk, cos.data_ptr(), sin.data_ptr(), cs, B, S, D,
+                        int(backward), qo.data_ptr(), ko.data_ptr(), _stream(q)))
+    return qo, ko
+
+
+def swiglu_fwd(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
+    """silu(gate) * up for [rows, F] operands."""
+    _require_cuda(gate, up)
+    gate, up = _rows_operand(gate), _rows_operand(up)
+    rows, F = gate.shape
+    y = torch.empty(rows, F, dtype=torch.bfloat16, device=gate.device)
+    _check(_lib.vq_swiglu_fwd(gate.data_ptr(), gate.stride(0), up.data_ptr(), up.stride(0), rows, F, y.data_ptr(),
+                              y.stride(0), _stream(gate)))
+    return y
+
+
+def swiglu_bwd(gate: torch.Tensor, up: torch.Tensor, dy: torch.Tensor):
+    _require_cuda(gate, up, dy)
+    gate, up, dy = _rows_operand(gate), _rows_operand(up), _rows_operand(dy)
+    rows, F = gate.shape
+    dg = torch.empty(rows, F, dtype=torch.bfloat16, device=gate.device)
+    du = torch.empty(rows, F, dtype=torch.bfloat16, device=gate.device)
+    _check(_lib.vq_swiglu_bwd(gate.data_ptr(), gate.stride(0), up.data_ptr(), up.stride(0), dy.data_ptr(), dy.stride(0),
+                              rows, F, dg.data_ptr(), du.data_ptr(), dg.stride(0), _stream(gate)))
+    return dg, du
+

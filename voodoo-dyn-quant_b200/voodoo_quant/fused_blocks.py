@@ -1,0 +1,152 @@
+"""Fused elementwise work of the Llama decoder block for the distillation step.
+
+The reference's step runs the Hugging Face Llama block around the gated
+Linears (voodoo_quant/training/trainer.py:2538-2556).  In that block the
+RMSNorm (fp32 cast, pow, mean, rsqrt, two multiplies), the rotary embedding
+(rotate_half's neg + cat, two multiplies and an add on the transposed q/k
+views) and the SwiGLU product run as separate torch kernels, forward and
+backward: a third of an 8B step's device time and over half of a 0.6B step's.
+``fuse_llama_blocks`` routes those three through one-pass CUDA kernels of
+``libvoodoo_b200`` (``vq_rmsnorm_fwd/bwd``, ``vq_rope``,
+``vq_swiglu_fwd/bwd``).  The attention itself stays torch's
+``scaled_dot_product_attention`` (cuDNN on B200), called as the Hugging Face
+``sdpa`` path calls it for a causal, unpadded, cache-free training batch.
+
+A patched module uses the fused kernels only for CUDA bf16 activations in
+that training case; any other call (a KV cache, an explicit attention mask,
+other dtypes or devices) runs the module's original forward unchanged.
+"""
+
+from __future__ import annotations
+
+import types
+
+import torch
+import torch.nn.functional as F
+from torch.autograd import Function
+
+from voodoo_quant import _C
+
+
+class _RMSNormFn(Function):
+    @staticmethod
+    def forward(ctx, x: torch.Tensor, weight: torch.Tensor, eps: float):
+        D = x.shape[-1]
+        x2 = x.reshape(-1, D)
+        y, rstd = _C.rmsnorm_fwd(x2, weight, eps)
+        ctx.save_for_backward(x2, weight, rstd)
+        return y.view(x.shape)
+
+    @staticmethod
+    def backward(ctx, gy: torch.Tensor):
+        x2, weight, rstd = ctx.saved_tensors
+        g2 = gy.reshape(-1, x2.shape[1])
+        dx = _C.rmsnorm_bwd(x2, g2, weight, rstd) if ctx.needs_input_grad[0] else None
+        dw = None
+        if ctx.needs_input_grad[1]:
+            n = (x2.float() * rstd[:, None]).to(torch.bfloat16).float()
+            dw = (g2.float() * n).sum(0).to(weight.dtype)
+        return (dx.view(gy.shape) if dx is not None else None), dw, None
+
+
+class _RopeFn(Function):
+    """q [B, S, Hq, D], k [B, S, Hk, D] -> rotated, contiguous [B, S, H, D]."""
+
+    @staticmethod
+    def forward(ctx, q: torch.Tensor, k: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor):
+        qo, ko = _C.rope(q, k, cos, sin)
+        ctx.save_for_backward(cos, sin)
+        return qo, ko
+
+    @staticmethod
+    def backward(ctx, gq: torch.Tensor, gk: torch.Tensor):
+        cos, sin = ctx.saved_tensors
+        dq, dk = _C.rope(gq, gk, cos, sin, backward=True)
+        return dq, dk, None, None
+
+
+class _SwiGLUFn(Function):
+    @staticmethod
+    def forward(ctx, gate: torch.Tensor, up: torch.Tensor):
+        F_ = gate.shape[-1]
+        g2, u2 = gate.reshape(-1, F_), up.reshape(-1, F_)
+        y = _C.swiglu_fwd(g2, u2)
+        ctx.save_for_backward(g2, u2)
+        ctx.shape = gate.shape
+        return y.view(gate.shape)
+
+    @staticmethod
+    def backward(ctx, gy: torch.Tensor):
+        g2, u2 = ctx.saved_tensors
+        dg, du = _C.swiglu_bwd(g2, u2, gy.reshape(-1, g2.shape[1]))
+        return dg.view(ctx.shape), du.view(ctx.shape)
+
+
+def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
+    return _RMSNormFn.apply(x, weight, eps)
+
+
+def rope(q: torch.Tensor, k: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor):
+    return _RopeFn.apply(q, k, cos, sin)
+
+
+def swiglu(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
+    return _SwiGLUFn.apply(gate, up)
+
+
+def _fusable(x: torch.Tensor) -> bool:
+    return x.is_cuda and x.dtype == torch.bfloat16 and x.shape[-1] % 8 == 0
+
+
+def _rmsnorm_forward(self, hidden_states: torch.Tensor) -> torch.Tensor:
+    if not (_fusable(hidden_states) and self.weight.dtype == torch.bfloat16 and hidden_states.shape[-1] <= 8192):
+        return self._vq_orig_forward(hidden_states)
+    return rms_norm(hidden_states, self.weight, self.variance_epsilon)
+
+
+def _mlp_forward(self, x: torch.Tensor) -> torch.Tensor:
+    if not _fusable(x):
+        return self._vq_orig_forward(x)
+    g = self.gate_proj(x)
+    u = self.up_proj(x)
+    if not (_fusable(g) and g.shape == u.shape):
+        return self.down_proj(self.act_fn(g) * u)
+    return self.down_proj(swiglu(g, u))
+
+
+def _attention_forward(self, hidden_states: torch.Tensor, position_embeddings=None, attention_mask=None,
+                       past_key_values=None, **kwargs):
+    if (past_key_values is not None or attention_mask is not None or position_embeddings is None
+            or not _fusable(hidden_states) or self.head_dim % 16 or kwargs.get("output_attentions", False)):
+        return self._vq_orig_forward(hidden_states, position_embeddings=position_embeddings,
+                                     attention_mask=attention_mask, past_key_values=past_key_values, **kwargs)
+    B, S = hidden_states.shape[:2]
+    q = self.q_proj(hidden_states).view(B, S, -1, self.head_dim)
+    k = self.k_proj(hidden_states).view(B, S, -1, self.head_dim)
+    v = self.v_proj(hidden_states).view(B, S, -1, self.head_dim)
+    cos, sin = position_embeddings
+    q, k = rope(q, k, cos, sin)
+    o = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2), is_causal=S > 1,
+                                       scale=self.scaling, enable_gqa=q.shape[2] != k.shape[2])
+    o = o.transpose(1, 2).reshape(B, S, -1)
+    return self.o_proj(o), None
+
+
+def fuse_llama_blocks(model: torch.nn.Module) -> int:
+    """Route the RMSNorm, attention (rotary) and MLP (SwiGLU) modules of a
+    Hugging Face Llama model through the fused kernels, in place; returns the
+    number of modules patched.  Idempotent."""
+    from transformers.models.llama import modeling_llama as L
+
+    table = ((L.LlamaRMSNorm, _rmsnorm_forward), (L.LlamaAttention, _attention_forward),
+             (L.LlamaMLP, _mlp_forward))
+    n = 0
+    for m in model.modules():
+        for cls, fwd in table:
+            if type(m) is cls and not hasattr(m, "_vq_orig_forward"):
+                if cls is L.LlamaMLP and getattr(m.config, "hidden_act", "silu") not in ("silu", "swish"):
+                    continue
+                m._vq_orig_forward = m.forward
+                m.forward = types.MethodType(fwd, m)
+                n += 1
+    return n

@@ -110,9 +110,9 @@ class GatedDistillTrainer:
         tau = anneal_temperature(self.step_idx, a.max_steps, a.temp_start, a.temp_end)
         for layer in self.replaced.values():
             layer.set_temperature(tau)
-        logits = self.student(input_ids=x).logits
+        logits = self.student(input_ids=x, use_cache=False).logits
         with torch.no_grad():
-            t_logits = self.teacher(input_ids=x).logits
+            t_logits = self.teacher(input_ids=x, use_cache=False).logits
         v0 = self._vocab_start()
         if self.tp and v0 is not None:
             kd, lm, kl = tp_distillation_loss(logits, t_logits, y, v0, a.distill_temperature, a.distill_weight,
@@ -153,12 +153,15 @@ class GatedDistillTrainer:
 
 
 def build_distill(shape_name: str, device, seed: int = 0, args: StepArgs | None = None,
-                  candidate_provider=None, replace_embeddings: bool = True, tp: bool = False):
+                  candidate_provider=None, replace_embeddings: bool = True, tp: bool = False,
+                  fused_blocks: bool = True):
     """Student (gated), Q8_0 teacher and trainer for a synthetic config.
 
     Under TP (an initialised process group adopted by voodoo_quant.parallel)
     both models are sharded by the Llama adapter before replacement, so the
-    candidates are packed from the FULL tensors and sliced per rank.
+    candidates are packed from the FULL tensors and sliced per rank.  On a
+    CUDA device ``fused_blocks`` routes the Llama blocks' RMSNorm, rotary
+    embedding and SwiGLU through the fused kernels (``voodoo_quant.fused_blocks``).
     """
     from voodoo_quant.layers import replace_embedding_with_mixed_quant, replace_linear_with_mixed_quant
     from voodoo_quant.parallel import TP, tp_patch_model
@@ -186,6 +189,11 @@ def build_distill(shape_name: str, device, seed: int = 0, args: StepArgs | None 
     for m in base.modules():  # drop the full-weight references kept for candidate packing
         if hasattr(m, "tp_full_weight"):
             m.tp_full_weight = None
+    if fused_blocks and torch.device(device).type == "cuda":
+        from voodoo_quant.fused_blocks import fuse_llama_blocks
+
+        fuse_llama_blocks(base)
+        fuse_llama_blocks(teacher)
     torch.cuda.empty_cache()
     trainer = GatedDistillTrainer(base, teacher, replaced, args or StepArgs(), shape.budget * total_8bit,
                                   non_targeted, tp=tp and TP.enabled)
