@@ -6,11 +6,14 @@
 //   mix_units_kernel: W_mix[o, i] = sum_k p_k * W_k[o, i] -> bf16
 //       [rows, ld_out]; columns >= cols (the zero padding of in_features)
 //       are written as 0.  One thread per 32-weight sub-block: the sub-block's
-//       scales are decoded once, then one FMA per weight and candidate.
+//       scales are decoded once, then one packed FMA per two weights and
+//       candidate.
 //
-// Both stage a CTA's run of consecutive units into word-aligned shared-memory
-// slots first (several independent aligned 32-bit loads in flight per thread;
-// 2-byte aligned GGUF blocks are realigned with funnel shifts).
+// The dequant kernel stages a CTA's run of consecutive units into
+// word-aligned shared-memory slots with aligned 32-bit loads (2-byte aligned
+// GGUF blocks realigned with funnel shifts); the mix kernel copies each
+// candidate's contiguous span with 16-byte cp.async and realigns only the
+// units that are not word aligned.
 #pragma once
 
 #include "formats.cuh"
@@ -86,82 +89,213 @@ __global__ void __launch_bounds__(kDecodeThreads) dequant_units_kernel(CandSet c
   }
 }
 
+// ---------------------------------------------------------------- mixture
+// Shared-memory layout of one mix CTA (kMixUnits consecutive units): per
+// candidate a raw region holding the 16-byte aligned span of its units'
+// contiguous bytes (copied with cp.async), and, for a candidate whose units
+// are not all 4-byte aligned there (2-byte multiple unit sizes, or a base
+// pointer that is not 4-byte aligned), a region of word-aligned unit slots.
+__host__ __device__ inline int mix_raw_bytes(int ub) { return (kMixUnits * ub + 32 + 15) & ~15; }
+__host__ __device__ inline bool mix_realign(const CandSet& cs, int k) {
+  return ((cs.ubytes[k] & 3) != 0) || ((reinterpret_cast<uintptr_t>(cs.ptr[k]) & 3u) != 0);
+}
+inline int mix_smem_bytes(const CandSet& cs) {
+  int s = 0;
+  for (int k = 0; k < cs.K; ++k) {
+    s += mix_raw_bytes(cs.ubytes[k]);
+    if (mix_realign(cs, k)) s += kMixUnits * unit_words(cs.fmt[k]) * 4;
+  }
+  return s;
+}
+
+// Per-candidate addressing of one block in the mix CTA's buffer (bytes):
+// unit lu of the candidate is at slot + lu * stride, its raw bytes at
+// raw + lu * ub.
+struct MixCand {
+  int fmt, slot, stride, raw, ub;
+  float p;
+};
+
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(gsrc) : "memory");
+}
+
+// acc2[j] holds elements 2j, 2j+1; w = (p_k a[h]) * q + p_k b[h] with the
+// b part kept per half in cst.
 template <int F>
-__device__ __forceinline__ void mix_chunk(const uint32_t* slot, int c, float pk, float (&acc)[32], float (&cst)[2]) {
-  float a[2], b[2], q[32];
-  Chunk<F>::run(slot, c, a, b, q);
-  const float pa0 = pk * a[0], pa1 = pk * a[1];
+__device__ __forceinline__ void mix_chunk(const uint32_t* slot, int c, float pk, uint64_t (&acc2)[16], float (&cst)[2]) {
+  float a[2], b[2];
+  uint32_t qb[8];
+  Chunk<F>::qbytes(slot, c, a, b, qb);
+  const uint64_t pa[2] = {f2pack(pk * a[0], pk * a[0]), f2pack(pk * a[1], pk * a[1])};
+  const uint64_t nsub = f2pack(-Chunk<F>::kSub, -Chunk<F>::kSub);
   if (Chunk<F>::kMin) {
     cst[0] = fmaf(pk, b[0], cst[0]);
     cst[1] = fmaf(pk, b[1], cst[1]);
   }
 #pragma unroll
-  for (int j = 0; j < 32; ++j) acc[j] = fmaf(j < 16 ? pa0 : pa1, q[j], acc[j]);
+  for (int j = 0; j < 8; ++j) {
+    const uint64_t q01 = f2add(f2pack(magic_byte(qb[j], 0), magic_byte(qb[j], 1)), nsub);
+    const uint64_t q23 = f2add(f2pack(magic_byte(qb[j], 2), magic_byte(qb[j], 3)), nsub);
+    acc2[2 * j] = f2fma(pa[j >> 2], q01, acc2[2 * j]);
+    acc2[2 * j + 1] = f2fma(pa[j >> 2], q23, acc2[2 * j + 1]);
+  }
 }
 
-// rows * units_per_row units in total (whole units: padded cols % 256 == 0).
-__global__ void __launch_bounds__(kDecodeThreads) mix_units_kernel(CandSet cs, const float* __restrict__ probs,
-                                                                   long long total_units, int units_per_row,
-                                                                   int cols, __nv_bfloat16* __restrict__ out,
-                                                                   long long ld_out, int* err) {
-  extern __shared__ __align__(16) uint32_t stage[];
-  const long long u0 = static_cast<long long>(blockIdx.x) * kMixUnits;
+// Issue the cp.async copies of block `blk` (kMixUnits units) of every
+// candidate into the raw regions of the buffer at `buf` (layout as above).
+__device__ __forceinline__ void mix_issue(const CandSet& cs, uint8_t* buf, long long blk, long long total_units) {
+  const long long u0 = blk * kMixUnits;
   const int nunits = static_cast<int>(min(static_cast<long long>(kMixUnits), total_units - u0));
-  int o = 0;
+  int off = 0;
   for (int k = 0; k < cs.K; ++k) {
-    const int uw = unit_words(cs.fmt[k]);
-    stage_units<8, 9>(stage + o, cs.ptr[k], u0, nunits, cs.ubytes[k], uw, total_units * cs.ubytes[k]);
-    o += kMixUnits * uw;
+    const int ub = cs.ubytes[k];
+    const uintptr_t st = reinterpret_cast<uintptr_t>(cs.ptr[k]) + static_cast<uintptr_t>(u0) * ub;
+    const uintptr_t a0 = st & ~uintptr_t(15);
+    const int n16 = static_cast<int>((((st + static_cast<uintptr_t>(nunits) * ub + 15) & ~uintptr_t(15)) - a0) >> 4);
+    for (int i = threadIdx.x; i < n16; i += kDecodeThreads)
+      cp_async16(buf + off + 16 * i, reinterpret_cast<const void*>(a0 + 16 * static_cast<uintptr_t>(i)));
+    off += mix_raw_bytes(ub);
+    if (mix_realign(cs, k)) off += kMixUnits * unit_words(cs.fmt[k]) * 4;
   }
-  __syncthreads();
+}
 
-  const int lu = threadIdx.x >> 3, c = threadIdx.x & 7;
-  if (lu >= nunits) return;
-  float acc[32];
-#pragma unroll
-  for (int j = 0; j < 32; ++j) acc[j] = 0.f;
-  float cst[2] = {0.f, 0.f};
+// rows * units_per_row units in total (whole units: padded cols % 256 == 0),
+// in blocks of kMixUnits.  Persistent CTAs walk the blocks with a stride of
+// the grid; with two buffers the copies of the next block are in flight while
+// the current one is decoded.  One thread per 32-weight sub-block: its scales
+// are decoded once per candidate, then one packed FMA per two weights.
+#ifndef VQ_MIX_MIN_BLOCKS
+#define VQ_MIX_MIN_BLOCKS 4  // resident CTAs per SM the register budget is sized for
+#endif
+__global__ void __launch_bounds__(kDecodeThreads, VQ_MIX_MIN_BLOCKS)
+    mix_units_kernel(CandSet cs, const float* __restrict__ probs, long long total_units, int units_per_row, int cols,
+                     __nv_bfloat16* __restrict__ out, long long ld_out, int buf_bytes, int nbuf, int* err) {
+  extern __shared__ __align__(16) uint8_t msmem[];
+  __shared__ MixCand meta[kMaxCandidates];
+  const long long nblocks = (total_units + kMixUnits - 1) / kMixUnits;
+  const int tid = threadIdx.x;
+  const int lu = tid >> 3, c = tid & 7;
   bool ok = true;
-  int so = 0;
-  for (int k = 0; k < cs.K; ++k) {
-    const int uw = unit_words(cs.fmt[k]);
-    const uint32_t* slot = stage + so + lu * uw;
-    const float pk = __ldg(probs + k);
-    switch (cs.fmt[k]) {
-      case kQ8_0: mix_chunk<kQ8_0>(slot, c, pk, acc, cst); break;
-      case kQ2_K: mix_chunk<kQ2_K>(slot, c, pk, acc, cst); break;
-      case kQ3_K: mix_chunk<kQ3_K>(slot, c, pk, acc, cst); break;
-      case kQ4_K: mix_chunk<kQ4_K>(slot, c, pk, acc, cst); break;
-      case kQ5_K: mix_chunk<kQ5_K>(slot, c, pk, acc, cst); break;
-      case kQ6_K: mix_chunk<kQ6_K>(slot, c, pk, acc, cst); break;
-      case kIQ4_XS: mix_chunk<kIQ4_XS>(slot, c, pk, acc, cst); break;
-      default: ok = false;
+
+  long long blk = blockIdx.x;
+  if (blk < nblocks) mix_issue(cs, msmem, blk, total_units);
+  asm volatile("cp.async.commit_group;" ::: "memory");
+  for (int it = 0; blk < nblocks; blk += gridDim.x, ++it) {
+    uint8_t* buf = msmem + (nbuf == 2 ? (it & 1) * buf_bytes : 0);
+    if (nbuf == 2) {
+      const long long nb = blk + gridDim.x;
+      if (nb < nblocks) mix_issue(cs, msmem + ((it + 1) & 1) * buf_bytes, nb, total_units);
+      asm volatile("cp.async.commit_group;\ncp.async.wait_group 1;" ::: "memory");
+    } else {
+      asm volatile("cp.async.wait_group 0;" ::: "memory");
     }
-    so += kMixUnits * uw;
-  }
-  if (!ok) report_error(err, kDevBadFormat, 1);
-  const long long u = u0 + lu;
-  const long long row = u / units_per_row;
-  const int col = static_cast<int>(u - row * units_per_row) * 256 + 32 * c;
-  __nv_bfloat16* dst = out + row * ld_out + col;
-  if (col + 32 <= cols && ((reinterpret_cast<uintptr_t>(dst) & 15u) == 0)) {
-#pragma unroll
-    for (int v = 0; v < 4; ++v) {
-      __align__(16) __nv_bfloat162 h[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int e = 8 * v + 2 * j;
-        h[j] = __floats2bfloat162_rn(acc[e] + cst[e >> 4], acc[e + 1] + cst[(e + 1) >> 4]);
+    __syncthreads();
+
+    const long long u0 = blk * kMixUnits;
+    const int nunits = static_cast<int>(min(static_cast<long long>(kMixUnits), total_units - u0));
+    // per-candidate unit addressing for this block, computed once
+    if (tid == 0) {
+      int off = 0;
+      for (int k = 0; k < cs.K; ++k) {
+        const int ub = cs.ubytes[k];
+        const int delta = static_cast<int>((reinterpret_cast<uintptr_t>(cs.ptr[k]) + static_cast<uintptr_t>(u0) * ub) & 15u);
+        MixCand m;
+        m.fmt = cs.fmt[k];
+        m.p = __ldg(probs + k);
+        m.raw = off + delta;
+        m.ub = ub;
+        off += mix_raw_bytes(ub);
+        if (mix_realign(cs, k)) {
+          m.slot = off;
+          m.stride = 4 * ((ub + 3) >> 2);
+          off += kMixUnits * m.stride;
+        } else {
+          m.slot = m.raw;
+          m.stride = ub;
+        }
+        meta[k] = m;
       }
-      reinterpret_cast<uint4*>(dst)[v] = *reinterpret_cast<const uint4*>(h);
     }
-  } else {
+    __syncthreads();
+    // word-align the units of candidates that need it (8 threads per unit)
+    bool any = false;
+    for (int k = 0; k < cs.K; ++k) {
+      const MixCand m = meta[k];
+      if (m.slot == m.raw) continue;
+      any = true;
+      if (lu < nunits) {
+        const int uw = m.stride >> 2;
+        const uint32_t* raw = reinterpret_cast<const uint32_t*>(buf + (m.raw & ~15));
+        uint32_t* dst = reinterpret_cast<uint32_t*>(buf + m.slot) + lu * uw;
+        const int b0 = (m.raw & 15) + lu * m.ub;
+        const uint32_t sh = static_cast<uint32_t>(b0 & 3) * 8u;
+        for (int w = c; w < uw; w += 8) {
+          const int i = (b0 >> 2) + w;
+          dst[w] = __funnelshift_r(raw[i], raw[i + 1], sh);
+        }
+      }
+    }
+    if (any) __syncthreads();
+
+    if (lu < nunits) {
+      uint64_t acc2[16];
 #pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      const long long cc = col + j;
-      if (cc < ld_out) dst[j] = __float2bfloat16_rn(cc < cols ? acc[j] + cst[j >> 4] : 0.f);
+      for (int j = 0; j < 16; ++j) acc2[j] = 0ull;
+      float cst[2] = {0.f, 0.f};
+      for (int k = 0; k < cs.K; ++k) {
+        const MixCand m = meta[k];
+        const uint32_t* slot = reinterpret_cast<const uint32_t*>(buf + m.slot + lu * m.stride);
+        switch (m.fmt) {
+          case kQ8_0: mix_chunk<kQ8_0>(slot, c, m.p, acc2, cst); break;
+          case kQ2_K: mix_chunk<kQ2_K>(slot, c, m.p, acc2, cst); break;
+          case kQ3_K: mix_chunk<kQ3_K>(slot, c, m.p, acc2, cst); break;
+          case kQ4_K: mix_chunk<kQ4_K>(slot, c, m.p, acc2, cst); break;
+          case kQ5_K: mix_chunk<kQ5_K>(slot, c, m.p, acc2, cst); break;
+          case kQ6_K: mix_chunk<kQ6_K>(slot, c, m.p, acc2, cst); break;
+          case kIQ4_XS: mix_chunk<kIQ4_XS>(slot, c, m.p, acc2, cst); break;
+          default: ok = false;
+        }
+      }
+      float acc[32];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const float2 v = f2unpack(acc2[j]);
+        acc[2 * j] = v.x;
+        acc[2 * j + 1] = v.y;
+      }
+      const long long u = u0 + lu;
+      const long long row = u / units_per_row;
+      const int col = static_cast<int>(u - row * units_per_row) * 256 + 32 * c;
+      __nv_bfloat16* dst = out + row * ld_out + col;
+      if (col + 32 <= cols && ((reinterpret_cast<uintptr_t>(dst) & 15u) == 0)) {
+#pragma unroll
+        for (int v = 0; v < 4; ++v) {
+          __align__(16) __nv_bfloat162 h[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int e = 8 * v + 2 * j;
+            h[j] = __floats2bfloat162_rn(acc[e] + cst[e >> 4], acc[e + 1] + cst[(e + 1) >> 4]);
+          }
+          reinterpret_cast<uint4*>(dst)[v] = *reinterpret_cast<const uint4*>(h);
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const long long cc = col + j;
+          if (cc < ld_out) dst[j] = __float2bfloat16_rn(cc < cols ? acc[j] + cst[j >> 4] : 0.f);
+        }
+      }
+    }
+    __syncthreads();  // this buffer is refilled two blocks from now (one, single-buffered)
+    if (nbuf != 2) {
+      const long long nb = blk + gridDim.x;
+      if (nb < nblocks) mix_issue(cs, msmem, nb, total_units);
+      asm volatile("cp.async.commit_group;" ::: "memory");
     }
   }
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+  if (!ok) report_error(err, kDevBadFormat, 1);
 }
 
 }  // namespace vq

@@ -262,14 +262,17 @@ struct Dec<kIQ4_XS> {
 };
 
 // ------------------------------------------ sub-block decoders (mix / gate-grad)
-// Chunk<F>::run(slot, c, a, b, q) decodes elements 32c .. 32c+31 of a unit as
-// exact small-integer codes q[j] (floats) plus scale/offset pairs:
-//   w[j] = a[h] * q[j] + b[h],   h = j / 16
-// (formats with one scale per 32 weights repeat the pair).  a and b are the
-// same float32 products the exact decoders form (d*sc, -dmin*m), so a*q + b
-// equals the exact decode up to its final rounding.  The mixture and
-// gate-gradient kernels (tolerance-checked) use this form: one FMA per weight,
-// with the scale work done once per sub-block.
+// Chunk<F>::qbytes(slot, c, a, b, qb) decodes elements 32c .. 32c+31 of a unit
+// as exact small-integer codes packed one per byte, qb[j] byte i = code of
+// element 4j + i plus a per-format bias, together with scale/offset pairs:
+//   w[4j+i] = a[h] * (byte_i(qb[j]) + 2^23 - kSub) + b[h],   h = (4j+i) / 16
+// (formats with one scale per 32 weights repeat the pair).  A byte becomes
+// the float 2^23 + byte with one byte permute (exponent bits 0x4B), so
+// subtracting kSub gives the code exactly.  a and b are the same float32
+// products the exact decoders form (d*sc, -dmin*m), so a*q + b equals the
+// exact decode up to its final rounding.  Chunk<F>::run returns the codes as
+// floats.  The mixture and gate-gradient kernels (tolerance-checked) use this
+// form: one FMA per weight, with the scale work done once per sub-block.
 template <int F>
 struct Chunk;
 
@@ -278,16 +281,27 @@ __device__ __forceinline__ void ld8(const uint32_t* s, int off, uint32_t (&w)[8]
   for (int j = 0; j < 8; ++j) w[j] = s[(off >> 2) + j];
 }
 
-// four bytes of x -> floats (byte value - sub), exact
-__device__ __forceinline__ void bytes4(uint32_t x, float sub, float* q) {
+// byte i of x as the float 2^23 + byte
+__device__ __forceinline__ float magic_byte(uint32_t x, int i) {
+  return __uint_as_float(__byte_perm(x, 0x4B000000u, 0x7440u + i));
+}
+
+template <int F>
+__device__ __forceinline__ void chunk_run(const uint32_t* s, int c, float (&a)[2], float (&b)[2], float (&q)[32]) {
+  uint32_t qb[8];
+  Chunk<F>::qbytes(s, c, a, b, qb);
 #pragma unroll
-  for (int j = 0; j < 4; ++j) q[j] = __uint_as_float(__byte_perm(x, 0x4B000000u, 0x7440u + j)) - sub;
+  for (int j = 0; j < 8; ++j)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) q[4 * j + i] = magic_byte(qb[j], i) - Chunk<F>::kSub;
 }
 
 template <>
 struct Chunk<kQ8_0> {
   static constexpr bool kMin = false;
-  __device__ __forceinline__ static void run(const uint32_t* s, int c, float (&a)[2], float (&b)[2], float (&q)[32]) {
+  static constexpr float kSub = 8388736.0f;  // 2^23 + 128: int8 codes stored with the sign bit flipped
+  __device__ __forceinline__ static void qbytes(const uint32_t* s, int c, float (&a)[2], float (&b)[2],
+                                                uint32_t (&qb)[8]) {
     const int dof = 34 * c;
     a[0] = a[1] = h2f(s[dof >> 2] >> (8 * (dof & 2)));
     b[0] = b[1] = 0.f;
@@ -299,14 +313,19 @@ struct Chunk<kQ8_0> {
     for (int j = 0; j < 8; ++j) w[j] = s[(al >> 2) + j];
     w[8] = sh ? s[(al >> 2) + 8] : 0u;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) bytes4(__funnelshift_r(w[j], w[j + 1], sh) ^ 0x80808080u, 8388736.0f, &q[4 * j]);
+    for (int j = 0; j < 8; ++j) qb[j] = __funnelshift_r(w[j], w[j + 1], sh) ^ 0x80808080u;
+  }
+  __device__ __forceinline__ static void run(const uint32_t* s, int c, float (&a)[2], float (&b)[2], float (&q)[32]) {
+    chunk_run<kQ8_0>(s, c, a, b, q);
   }
 };
 
 template <>
 struct Chunk<kQ4_K> {
   static constexpr bool kMin = true;
-  __device__ __forceinline__ static void run(const uint32_t* s, int c, float (&a)[2], float (&b)[2], float (&q)[32]) {
+  static constexpr float kSub = 8388608.0f;
+  __device__ __forceinline__ static void qbytes(const uint32_t* s, int c, float (&a)[2], float (&b)[2],
+                                                uint32_t (&qb)[8]) {
     const uint32_t w0 = s[0];
     uint32_t sc, mn;
     k4_scale_min_w(s, c, sc, mn);
@@ -316,14 +335,19 @@ struct Chunk<kQ4_K> {
     ld8(s, 16 + 32 * (c >> 1), w);
     const uint32_t sh = (c & 1) * 4;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) bytes4((w[j] >> sh) & 0x0F0F0F0Fu, 8388608.0f, &q[4 * j]);
+    for (int j = 0; j < 8; ++j) qb[j] = (w[j] >> sh) & 0x0F0F0F0Fu;
+  }
+  __device__ __forceinline__ static void run(const uint32_t* s, int c, float (&a)[2], float (&b)[2], float (&q)[32]) {
+    chunk_run<kQ4_K>(s, c, a, b, q);
   }
 };
 
 template <>
 struct Chunk<kQ5_K> {
   static constexpr bool kMin = true;
-  __device__ __forceinline__ static void run(const uint32_t* s, int c, float (&a)[2], float (&b)[2], float (&q)[32]) {
+  static constexpr float kSub = 8388608.0f;
+  __device__ __forceinline__ static void qbytes(const uint32_t* s, int c, float (&a)[2], float (&b)[2],
+                                                uint32_t (&qb)[8]) {
     const uint32_t w0 = s[0];
     uint32_t sc, mn;
     k4_scale_min_w(s, c, sc, mn);
@@ -334,15 +358,19 @@ struct Chunk<kQ5_K> {
     ld8(s, 16, h);
     const uint32_t sh = (c & 1) * 4;
 #pragma unroll
-    for (int j = 0; j < 8; ++j)
-      bytes4(((w[j] >> sh) & 0x0F0F0F0Fu) | (((h[j] >> c) & 0x01010101u) << 4), 8388608.0f, &q[4 * j]);
+    for (int j = 0; j < 8; ++j) qb[j] = ((w[j] >> sh) & 0x0F0F0F0Fu) | (((h[j] >> c) & 0x01010101u) << 4);
+  }
+  __device__ __forceinline__ static void run(const uint32_t* s, int c, float (&a)[2], float (&b)[2], float (&q)[32]) {
+    chunk_run<kQ5_K>(s, c, a, b, q);
   }
 };
 
 template <>
 struct Chunk<kQ6_K> {
   static constexpr bool kMin = false;
-  __device__ __forceinline__ static void run(const uint32_t* s, int c, float (&a)[2], float (&b)[2], float (&q)[32]) {
+  static constexpr float kSub = 8388640.0f;  // 2^23 + 32
+  __device__ __forceinline__ static void qbytes(const uint32_t* s, int c, float (&a)[2], float (&b)[2],
+                                                uint32_t (&qb)[8]) {
     const int h = c >> 2, g = c & 3;
     const float d = h2f(s[52]);
     const int so = 192 + 8 * h + 2 * g;
@@ -357,15 +385,19 @@ struct Chunk<kQ6_K> {
     ld8(s, 128 + 32 * h, hh);
     const uint32_t lsh = (g >> 1) * 4, hsh = 2 * g;
 #pragma unroll
-    for (int j = 0; j < 8; ++j)
-      bytes4(((l[j] >> lsh) & 0x0F0F0F0Fu) | (((hh[j] >> hsh) & 0x03030303u) << 4), 8388640.0f, &q[4 * j]);
+    for (int j = 0; j < 8; ++j) qb[j] = ((l[j] >> lsh) & 0x0F0F0F0Fu) | (((hh[j] >> hsh) & 0x03030303u) << 4);
+  }
+  __device__ __forceinline__ static void run(const uint32_t* s, int c, float (&a)[2], float (&b)[2], float (&q)[32]) {
+    chunk_run<kQ6_K>(s, c, a, b, q);
   }
 };
 
 template <>
 struct Chunk<kQ2_K> {
   static constexpr bool kMin = true;
-  __device__ __forceinline__ static void run(const uint32_t* s, int c, float (&a)[2], float (&b)[2], float (&q)[32]) {
+  static constexpr float kSub = 8388608.0f;
+  __device__ __forceinline__ static void qbytes(const uint32_t* s, int c, float (&a)[2], float (&b)[2],
+                                                uint32_t (&qb)[8]) {
     const int h = c >> 2, sft = c & 3;
     const uint32_t sw = s[c >> 1] >> (16 * (c & 1));  // scale bytes 2c, 2c+1
     const uint32_t wd = s[20];
@@ -377,14 +409,19 @@ struct Chunk<kQ2_K> {
     uint32_t w[8];
     ld8(s, 16 + 32 * h, w);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) bytes4((w[j] >> (2 * sft)) & 0x03030303u, 8388608.0f, &q[4 * j]);
+    for (int j = 0; j < 8; ++j) qb[j] = (w[j] >> (2 * sft)) & 0x03030303u;
+  }
+  __device__ __forceinline__ static void run(const uint32_t* s, int c, float (&a)[2], float (&b)[2], float (&q)[32]) {
+    chunk_run<kQ2_K>(s, c, a, b, q);
   }
 };
 
 template <>
 struct Chunk<kQ3_K> {
   static constexpr bool kMin = false;
-  __device__ __forceinline__ static void run(const uint32_t* s, int c, float (&a)[2], float (&b)[2], float (&q)[32]) {
+  static constexpr float kSub = 8388612.0f;  // 2^23 + 4
+  __device__ __forceinline__ static void qbytes(const uint32_t* s, int c, float (&a)[2], float (&b)[2],
+                                                uint32_t (&qb)[8]) {
     const int h = c >> 2, sft = c & 3;
     const float d = h2f(s[27]);
 #pragma unroll
@@ -399,28 +436,45 @@ struct Chunk<kQ3_K> {
     ld8(s, 32 + 32 * h, w);
     ld8(s, 0, m);
 #pragma unroll
-    for (int j = 0; j < 8; ++j)
-      bytes4(((w[j] >> (2 * sft)) & 0x03030303u) | (((m[j] >> c) & 0x01010101u) << 2), 8388612.0f, &q[4 * j]);
+    for (int j = 0; j < 8; ++j) qb[j] = ((w[j] >> (2 * sft)) & 0x03030303u) | (((m[j] >> c) & 0x01010101u) << 2);
+  }
+  __device__ __forceinline__ static void run(const uint32_t* s, int c, float (&a)[2], float (&b)[2], float (&q)[32]) {
+    chunk_run<kQ3_K>(s, c, a, b, q);
   }
 };
+
+// Four IQ4_NL codebook lookups at once: byte i of the result is
+// kvalues[nibble i of the low nibbles of x] + 128 (x holds 4 indices, one per byte).
+__device__ __forceinline__ uint32_t iq4nl4(uint32_t x) {
+  constexpr uint32_t k0 = 0xBFAD9881u, k1 = 0xF6EADDCFu, k2 = 0x26190D01u, k3 = 0x71594535u;
+  const uint32_t i3 = x & 0x07070707u;                                  // low 3 bits per byte
+  const uint32_t sel = (i3 | (i3 >> 4)) & 0x00770077u;                  // bytes -> nibbles (pairs)
+  const uint32_t sel16 = (sel & 0x77u) | ((sel >> 8) & 0x7700u);        // four 3-bit selectors
+  const uint32_t lo = __byte_perm(k0, k1, sel16);
+  const uint32_t hi = __byte_perm(k2, k3, sel16);
+  const uint32_t m = ((x >> 3) & 0x01010101u) * 0xFFu;                  // bit 3 set -> high half
+  return ((hi & m) | (lo & ~m)) ^ 0x80808080u;
+}
 
 template <>
 struct Chunk<kIQ4_XS> {
   static constexpr bool kMin = false;
-  __device__ __forceinline__ static void run(const uint32_t* s, int c, float (&a)[2], float (&b)[2], float (&q)[32]) {
+  static constexpr float kSub = 8388736.0f;  // 2^23 + 128
+  __device__ __forceinline__ static void qbytes(const uint32_t* s, int c, float (&a)[2], float (&b)[2],
+                                                uint32_t (&qb)[8]) {
     const uint32_t w0 = s[0];
     const uint32_t ls = ((byte_of(s, 4 + (c >> 1)) >> (4 * (c & 1))) & 15u) | ((((w0 >> 16) >> (2 * c)) & 3u) << 4);
     a[0] = a[1] = __fmul_rn(h2f(w0), u2f(ls) - 32.0f);
     b[0] = b[1] = 0.f;
-    uint32_t w[4];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) w[j] = s[2 + 4 * c + j];  // bytes 8 + 16c ..
-#pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      const uint32_t byte = (w[j >> 2] >> (8 * (j & 3))) & 0xFFu;
-      q[j] = u2f(static_cast<uint32_t>(iq4nl(byte & 15u) + 128)) - 128.0f;
-      q[j + 16] = u2f(static_cast<uint32_t>(iq4nl(byte >> 4) + 128)) - 128.0f;
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t w = s[2 + 4 * c + j];  // bytes 8 + 16c + 4j ..: elements 4j.. (low) and 16 + 4j.. (high)
+      qb[j] = iq4nl4(w & 0x0F0F0F0Fu);
+      qb[4 + j] = iq4nl4((w >> 4) & 0x0F0F0F0Fu);
     }
+  }
+  __device__ __forceinline__ static void run(const uint32_t* s, int c, float (&a)[2], float (&b)[2], float (&q)[32]) {
+    chunk_run<kIQ4_XS>(s, c, a, b, q);
   }
 };
 

@@ -88,50 +88,49 @@ __device__ __forceinline__ void tile_coords(const Params& p, int tile, int& m_bl
   n_blk = first_n + (r - m_blk * gn);
 }
 
-// Stage unit n_blk of rows row0 .. row0+31 (one candidate) into the warp's
-// slot rows (pitch kStagePitch words).  Lane l copies words l, l+32, l+64 of
-// every row; all loads of 8 rows are issued before their stores, so many
-// independent loads are in flight.
-__device__ __forceinline__ void stage_rows_warp(uint32_t* dst, const uint8_t* cbase, long long row0, int M,
-                                                int upr, int n_blk, int ub, int lane) {
+// Stage this lane's unit (ub bytes at `unit`, 2-byte aligned) into its own
+// slot row as ceil(ub / 4) aligned words.  The 16-byte aligned span around
+// the unit is read with 16-byte loads (it never leaves the 16-byte granules
+// that hold the unit's bytes) and realigned with funnel shifts; each lane
+// stages and later decodes only its own row, so no warp synchronisation is
+// needed between the two.
+__device__ __forceinline__ void stage_row_lane(uint32_t* slot, const uint8_t* unit, int ub) {
+  const uintptr_t a = reinterpret_cast<uintptr_t>(unit);
+  const uintptr_t a0 = a & ~uintptr_t(15);
+  const int n16 = static_cast<int>((((a + ub + 15) & ~uintptr_t(15)) - a0) >> 4);
+  const int d = static_cast<int>(a - a0);  // 0 .. 14, even
+  const int dw = d >> 2;                   // first superset word of the unit
+  const uint32_t sh = static_cast<uint32_t>(d & 2) * 8u;
   const int nw = (ub + 3) >> 2;
+  const uint4* src = reinterpret_cast<const uint4*>(a0);
+  // superset word g pairs with word g + 1: out[g - dw] = funnel(W[g], W[g + 1], sh)
+  uint32_t prev = 0u;
 #pragma unroll 1
-  for (int r0 = 0; r0 < 32; r0 += 8) {
-    uint32_t lo[8][3], hi[8][3], shv[8];
+  for (int t = 0; t < n16; ++t) {
+    const uint4 v = __ldg(src + t);
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-    for (int r = 0; r < 8; ++r) {
-      const long long rr = row0 + r0 + r;
-      const bool ok = rr < M;
-      const uintptr_t a = reinterpret_cast<uintptr_t>(cbase + (ok ? (rr * upr + n_blk) * ub : 0));
-      const uint32_t* s = reinterpret_cast<const uint32_t*>(a & ~uintptr_t(3));
-      shv[r] = static_cast<uint32_t>(a & 3u) * 8u;
-#pragma unroll
-      for (int j = 0; j < 3; ++j) {
-        const int w = lane + 32 * j;
-        lo[r][j] = (ok && w < nw) ? __ldg(s + w) : 0u;
-        hi[r][j] = (ok && w < nw && shv[r] != 0u && 4 * w + 3 <= ub) ? __ldg(s + w + 1) : 0u;
-      }
-    }
-#pragma unroll
-    for (int r = 0; r < 8; ++r) {
-#pragma unroll
-      for (int j = 0; j < 3; ++j) {
-        const int w = lane + 32 * j;
-        if (w < nw) dst[(r0 + r) * kStagePitch + w] = __funnelshift_r(lo[r][j], hi[r][j], shv[r]);
-      }
+    for (int i = 0; i < 4; ++i) {
+      const int o = 4 * t + i - 1 - dw;  // output word completed by this superset word
+      if (o >= 0 && o < nw) slot[o] = __funnelshift_r(prev, w[i], sh);
+      prev = w[i];
     }
   }
+  const int o = 4 * n16 - 1 - dw;
+  if (o >= 0 && o < nw) slot[o] = __funnelshift_r(prev, 0u, sh);
 }
 
 // Dot of one dW row (256 TMEM columns at t_row, fp32) with the decoded unit
 // in `slot` (this thread's row); columns at or beyond `cols` are skipped.
 // Per 32-weight sub-block with w = a[h] * q + b[h] (h = half):
-//   sum_j v_j w_j = sum_h a[h] * sum_{j in h} v_j q_j  (+ b[h] * sum_{j in h} v_j).
+//   sum_j v_j w_j = sum_h a[h] * sum_{j in h} v_j q_j  (+ b[h] * sum_{j in h} v_j),
+// with q_j = (2^23 + code byte) - kSub formed and accumulated as fp32 pairs.
 // All 32 lanes must call it (tcgen05.ld is warp-collective).
 template <int F>
 __device__ __forceinline__ float row_dot(const uint32_t* slot, uint32_t t_row, long long colbase, long long cols,
                                          bool row_ok) {
   float s = 0.f;
+  const uint64_t nsub = f2pack(-Chunk<F>::kSub, -Chunk<F>::kSub);
 #pragma unroll 1
   for (int c = 0; c < BN / 32; ++c) {
     float v[32];
@@ -143,19 +142,31 @@ __device__ __forceinline__ float row_dot(const uint32_t* slot, uint32_t t_row, l
         for (int j = 0; j < 32; ++j)
           if (col0 + j >= cols) v[j] = 0.f;
       }
-      float a[2], b[2], q[32];
-      Chunk<F>::run(slot, c, a, b, q);
-      float s1[2] = {0.f, 0.f};
+      float a[2], b[2];
+      uint32_t qb[8];
+      Chunk<F>::qbytes(slot, c, a, b, qb);
+      uint64_t acc[2] = {0ull, 0ull}, vs[2] = {0ull, 0ull};
 #pragma unroll
-      for (int j = 0; j < 32; ++j) s1[j >> 4] = fmaf(v[j], q[j], s1[j >> 4]);
-      s = fmaf(a[0], s1[0], s);
-      s = fmaf(a[1], s1[1], s);
-      if (Chunk<F>::kMin) {
-        float s0[2] = {0.f, 0.f};
+      for (int j = 0; j < 8; ++j) {
+        const uint64_t q01 = f2add(f2pack(magic_byte(qb[j], 0), magic_byte(qb[j], 1)), nsub);
+        const uint64_t q23 = f2add(f2pack(magic_byte(qb[j], 2), magic_byte(qb[j], 3)), nsub);
+        const uint64_t v01 = f2pack(v[4 * j], v[4 * j + 1]);
+        const uint64_t v23 = f2pack(v[4 * j + 2], v[4 * j + 3]);
+        acc[j >> 2] = f2fma(v01, q01, acc[j >> 2]);
+        acc[j >> 2] = f2fma(v23, q23, acc[j >> 2]);
+        if (Chunk<F>::kMin) {
+          vs[j >> 2] = f2add(vs[j >> 2], v01);
+          vs[j >> 2] = f2add(vs[j >> 2], v23);
+        }
+      }
 #pragma unroll
-        for (int j = 0; j < 32; ++j) s0[j >> 4] += v[j];
-        s = fmaf(b[0], s0[0], s);
-        s = fmaf(b[1], s0[1], s);
+      for (int h = 0; h < 2; ++h) {
+        const float2 p = f2unpack(acc[h]);
+        s = fmaf(a[h], p.x + p.y, s);
+        if (Chunk<F>::kMin) {
+          const float2 u = f2unpack(vs[h]);
+          s = fmaf(b[h], u.x + u.y, s);
+        }
       }
     }
   }
@@ -190,17 +201,16 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, uint8_t* stage, u
       }
     }
   } else {
-    // Gate-gradient epilogue.  For each candidate: the warp stages its 32
-    // rows' units (one 256-column unit per row) into its shared slot rows with
-    // coalesced aligned loads, then each thread decodes its own row from
-    // shared memory and dots it with the dW row read back from TMEM.
-    uint32_t* my_stage = reinterpret_cast<uint32_t*>(stage) + wq * (32 * kStagePitch);
+    // Gate-gradient epilogue.  For each candidate: each thread stages its own
+    // row's unit (one 256-column unit) into its shared slot row with 16-byte
+    // loads, decodes it from there and dots it with the dW row read back from
+    // TMEM; the warp then sums its 32 rows into one partial.
+    uint32_t* slot_row = reinterpret_cast<uint32_t*>(stage) + (wq * 32 + lane) * kStagePitch;
     const long long slot = (static_cast<long long>(m128) * p.num_n_blk + n_blk) * 4 + wq;
     const long long colbase = static_cast<long long>(n_blk) * BN;
+    const long long urow = (row_ok ? row : 0) * p.units_per_row + n_blk;
     for (int k = 0; k < p.cands.K; ++k) {
-      stage_rows_warp(my_stage, p.cands.ptr[k], row0, p.M, p.units_per_row, n_blk, p.cands.ubytes[k], lane);
-      __syncwarp();
-      const uint32_t* slot_row = my_stage + lane * kStagePitch;
+      stage_row_lane(slot_row, p.cands.ptr[k] + urow * p.cands.ubytes[k], p.cands.ubytes[k]);
       float s = 0.f;
       switch (p.cands.fmt[k]) {
         case kQ8_0: s = row_dot<kQ8_0>(slot_row, t_row, colbase, p.cols, row_ok); break;

@@ -283,13 +283,19 @@ int vq_mix(int K, const int* types, const void* const* blocks, const float* prob
   if (int rc = device_error_ptr(&err)) return rc;
   if (cols > 0x7fffffffLL) return fail(VQ_ERR_INVALID, "too many columns");
   const long long units = static_cast<long long>(rows) * (padded_cols / 256);
-  const long long grid = (units + vq::kMixUnits - 1) / vq::kMixUnits;
+  const long long nblocks = (units + vq::kMixUnits - 1) / vq::kMixUnits;
+  // One block of kMixUnits units per CTA, single-buffered: four resident
+  // CTAs per SM hide the copies better than persistent double-buffered CTAs
+  // at half the occupancy (measured on B200 for K = 1, 5 and 6).
+  const int buf = (vq::mix_smem_bytes(cs) + 15) & ~15;
+  const int nbuf = 1;
+  const int smem = buf;
+  const long long grid = nblocks;
   if (grid > 0x7fffffffLL) return fail(VQ_ERR_INVALID, "tensor too large");
-  const int smem = vq::stage_smem_bytes(cs, vq::kMixUnits);
   if (smem > 48 * 1024) VQ_CUDA(cudaFuncSetAttribute(vq::mix_units_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
   vq::mix_units_kernel<<<static_cast<unsigned>(grid), vq::kDecodeThreads, smem, static_cast<cudaStream_t>(stream)>>>(
       cs, probs, units, static_cast<int>(padded_cols / 256), static_cast<int>(cols),
-      static_cast<__nv_bfloat16*>(w_bf16), ldw, err);
+      static_cast<__nv_bfloat16*>(w_bf16), ldw, buf, nbuf, err);
   VQ_CUDA(cudaGetLastError());
   return 0;
 }
