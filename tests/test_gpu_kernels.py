@@ -363,3 +363,25 @@ def test_config2_shapes_properties(cuda):
     ref_part = ((ds.T @ xs) * w0).sum()
     assert abs(gpart.item() - ref_part.item()) <= 1e-3 * abs(ref_part.item()) + 1e-3
     assert _C.device_error() == 0
+
+
+@pytest.mark.parametrize("T,N,IN", [(1024, 2560, 2048), (640, 14336, 512)])
+def test_gategrad_stream_k_tail_matches_fp64(cuda, T, N, IN):
+    """Shapes whose tile count is not a multiple of the CTA-pair count, so the
+    last wave is split along K (stream-K pieces writing their own partial
+    slots): against fp64 <dy^T x, W_k> with W_k decoded bit-exactly."""
+    from voodoo_quant import _C
+    from voodoo_quant.quants import rtn
+
+    types = ["Q3_K", "Q4_K", "Q6_K", "Q8_0"]
+    g = torch.Generator(device="cpu").manual_seed(N + IN)
+    w = torch.randn(N, IN, generator=g) * 0.02
+    blocks = [rtn.quantize(w, q).to(cuda) for q in types]
+    x = _bf16(torch.randn(T, IN, generator=g)).to(cuda)
+    dy = _bf16(torch.randn(T, N, generator=g)).to(cuda)
+    dw = dy.double().T @ x.double()
+    ref = torch.stack([(dw * _C.dequant(b, q, N, IN).double()).sum() for q, b in zip(types, blocks)])
+    got = _C.gategrad(dy, x, types, blocks, N, IN, IN)
+    assert rel_err(got.double().cpu().numpy(), ref.cpu().numpy()) < 1e-3
+    assert torch.equal(got, _C.gategrad(dy, x, types, blocks, N, IN, IN))
+    assert _C.device_error() == 0

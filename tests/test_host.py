@@ -47,7 +47,8 @@ def test_library_validation_paths_without_gpu():
     # shape validation happens before any CUDA call
     assert lib.vq_dequant(12, None, 4, 100, None, None) == _C.VQ_ERR_INVALID
     assert lib.vq_dequant(12, None, 0, 256, None, None) == 0  # empty input is a no-op
-    assert lib.vq_gategrad_workspace_bytes(14336, 4096, 5) == 112 * 16 * 4 * 5 * 4
+    # per-tile slots (112 row blocks x 16 column blocks x 4 warps) + 16 stream-K slots per CTA pair (<= 128)
+    assert lib.vq_gategrad_workspace_bytes(14336, 4096, 5) == (112 * 16 * 4 + 16 * 128) * 5 * 4
 
 
 @pytest.mark.parametrize("fmt,ceiling", [("Q8_0", 0.02), ("Q6_K", 0.05), ("Q5_K", 0.08), ("Q4_K", 0.12),

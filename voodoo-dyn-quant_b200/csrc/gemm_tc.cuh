@@ -75,8 +75,48 @@ struct Params {
   int units_per_row;
   long long cols;
   float* partials;
+  // stream-K tail (paired gate-gradient kernel only): when set, the tiles
+  // left over after the full waves are split along K across all clusters;
+  // pieces that do not start at k-block 0 write the partial slots that
+  // follow the per-tile ones (sk_base), 16 per cluster.
+  int stream_k;
+  int sk_base;
   int* err;
 };
+
+// One unit of work of a persistent cluster: k-blocks [kb0, kb1) of a tile.
+// piece >= 0 marks a stream-K piece (the cluster's first or second).
+struct Seg {
+  int tile, kb0, kb1, piece;
+};
+
+// Segment i of cluster c out of C (the same sequence for every role).
+__device__ __forceinline__ bool get_seg(const Params& p, int c, int C, int i, Seg& sg) {
+  if (!p.stream_k) {
+    const int tile = c + i * C;
+    sg = {tile, 0, p.num_k_blk, -1};
+    return tile < p.num_tiles;
+  }
+  const int full = p.num_tiles / C;
+  if (i < full) {
+    sg = {c + i * C, 0, p.num_k_blk, -1};
+    return true;
+  }
+  const int KB = p.num_k_blk;
+  const long long U = static_cast<long long>(p.num_tiles - full * C) * KB;
+  const int lo = static_cast<int>(U * c / C), hi = static_cast<int>(U * (c + 1) / C);
+  const int j = i - full;
+  const int cut = (lo / KB + 1) * KB;  // end of the tile the range starts in
+  if (j == 0 && lo < hi) {
+    sg = {full * C + lo / KB, lo % KB, (hi < cut ? hi : cut) - (lo / KB) * KB, 0};
+    return true;
+  }
+  if (j == 1 && hi > cut) {
+    sg = {full * C + cut / KB, 0, hi - cut, 1};
+    return true;
+  }
+  return false;
+}
 
 __device__ __forceinline__ void tile_coords(const Params& p, int tile, int& m_blk, int& n_blk) {
   const int band = GROUP_N * p.num_m_blk;
@@ -103,17 +143,37 @@ __device__ __forceinline__ void stage_row_lane(uint32_t* slot, const uint8_t* un
   const uint32_t sh = static_cast<uint32_t>(d & 2) * 8u;
   const int nw = (ub + 3) >> 2;
   const uint4* src = reinterpret_cast<const uint4*>(a0);
+  if (d == 0 && (ub & 15) == 0) {  // 16-byte aligned unit of whole vectors: plain copy
+#pragma unroll 1
+    for (int t = 0; t < n16; ++t) {
+      const uint4 v = __ldg(src + t);
+      slot[4 * t] = v.x;
+      slot[4 * t + 1] = v.y;
+      slot[4 * t + 2] = v.z;
+      slot[4 * t + 3] = v.w;
+    }
+    return;
+  }
   // superset word g pairs with word g + 1: out[g - dw] = funnel(W[g], W[g + 1], sh)
   uint32_t prev = 0u;
 #pragma unroll 1
   for (int t = 0; t < n16; ++t) {
     const uint4 v = __ldg(src + t);
     const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    const int o0 = 4 * t - 1 - dw;  // output word completed by superset word 4t
+    if (o0 >= 0 && o0 + 3 < nw) {   // interior vector: all four outputs in range
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int o = 4 * t + i - 1 - dw;  // output word completed by this superset word
-      if (o >= 0 && o < nw) slot[o] = __funnelshift_r(prev, w[i], sh);
-      prev = w[i];
+      for (int i = 0; i < 4; ++i) {
+        slot[o0 + i] = __funnelshift_r(prev, w[i], sh);
+        prev = w[i];
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int o = o0 + i;
+        if (o >= 0 && o < nw) slot[o] = __funnelshift_r(prev, w[i], sh);
+        prev = w[i];
+      }
     }
   }
   const int o = 4 * n16 - 1 - dw;
@@ -179,7 +239,7 @@ __device__ __forceinline__ float row_dot(const uint32_t* slot, uint32_t t_row, l
 //   gate-gradient staging area (4 warps x 32 rows x kStagePitch words).
 template <int kEpi>
 __device__ __forceinline__ void epilogue_tile(const Params& p, uint8_t* stage, uint32_t t_row, long long row0,
-                                              int m128, int n_blk, int wq, int lane) {
+                                              int m128, int n_blk, int wq, int lane, long long slot_override = -1) {
   const long long row = row0 + lane;
   const bool row_ok = row < p.M;
   if (kEpi == kEpiStoreBf16) {
@@ -206,7 +266,8 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, uint8_t* stage, u
     // loads, decodes it from there and dots it with the dW row read back from
     // TMEM; the warp then sums its 32 rows into one partial.
     uint32_t* slot_row = reinterpret_cast<uint32_t*>(stage) + (wq * 32 + lane) * kStagePitch;
-    const long long slot = (static_cast<long long>(m128) * p.num_n_blk + n_blk) * 4 + wq;
+    const long long slot =
+        slot_override >= 0 ? slot_override : (static_cast<long long>(m128) * p.num_n_blk + n_blk) * 4 + wq;
     const long long colbase = static_cast<long long>(n_blk) * BN;
     const long long urow = (row_ok ? row : 0) * p.units_per_row + n_blk;
     for (int k = 0; k < p.cands.K; ++k) {
@@ -463,12 +524,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     if (lane == 0) {
       uint32_t it = 0;
       bool alive = true;
-      for (int tile = cluster_id; tile < p.num_tiles && alive; tile += num_clusters) {
+      Seg sg;
+      for (int si = 0; alive && get_seg(p, cluster_id, num_clusters, si, sg); ++si) {
         int m_blk, n_blk;
-        tile_coords(p, tile, m_blk, n_blk);
+        tile_coords(p, sg.tile, m_blk, n_blk);
         const int m0 = m_blk * 256 + 128 * static_cast<int>(rank);
         const int n0 = n_blk * BN + 128 * static_cast<int>(rank);
-        for (int kb = 0; kb < p.num_k_blk; ++kb, ++it) {
+        for (int kb = sg.kb0; kb < sg.kb1; ++kb, ++it) {
           const int s = it % PSTAGES;
           const uint32_t ph = (it / PSTAGES) & 1u;
           if (!mbar_wait(empty_bar(s), ph ^ 1u, abort_flag)) {
@@ -502,7 +564,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       constexpr uint32_t idesc = idesc_bf16_f32(256, BN, kAmn, kBmn);
       uint32_t it = 0, local = 0;
       bool alive = true;
-      for (int tile = cluster_id; tile < p.num_tiles && alive; tile += num_clusters, ++local) {
+      Seg sg;
+      for (int si = 0; alive && get_seg(p, cluster_id, num_clusters, si, sg); ++si, ++local) {
         const int acc = local & 1;
         const uint32_t aph = (local >> 1) & 1u;
         if (!mbar_wait(tempty_bar(acc), aph ^ 1u, abort_flag)) {
@@ -511,7 +574,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
-        for (int kb = 0; kb < p.num_k_blk; ++kb, ++it) {
+        for (int kb = sg.kb0; kb < sg.kb1; ++kb, ++it) {
           const int s = it % PSTAGES;
           const uint32_t ph = (it / PSTAGES) & 1u;
           if (!mbar_wait(full_bar(s), ph, abort_flag)) {
@@ -528,7 +591,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
                                         : smem_desc_sw128(a_addr + kk * 32, 16, 1024);
             const uint64_t bdesc = kBmn ? smem_desc_sw128(b_addr + kk * 2048, 64 * BK * 2, 1024)
                                         : smem_desc_sw128(b_addr + kk * 32, 16, 1024);
-            tc_mma_bf16_pair(d_tmem, adesc, bdesc, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+            tc_mma_bf16_pair(d_tmem, adesc, bdesc, idesc, (kb > sg.kb0 || kk > 0) ? 1u : 0u);
           }
           tc_commit_pair_mc(empty_bar(s), 0x3);  // frees stage s in both CTAs
         }
@@ -542,9 +605,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     const uint32_t tempty_leader0 = map_to_rank(tempty_bar(0), 0);
     const uint32_t tempty_leader1 = map_to_rank(tempty_bar(1), 0);
     uint32_t local = 0;
-    for (int tile = cluster_id; tile < p.num_tiles; tile += num_clusters, ++local) {
+    bool sk_written[2] = {false, false};
+    Seg sg;
+    for (int si = 0; get_seg(p, cluster_id, num_clusters, si, sg); ++si, ++local) {
       int m_blk, n_blk;
-      tile_coords(p, tile, m_blk, n_blk);
+      tile_coords(p, sg.tile, m_blk, n_blk);
       const int acc = local & 1;
       const uint32_t aph = (local >> 1) & 1u;
       if (!mbar_wait(tfull_bar(acc), aph, abort_flag)) {
@@ -554,11 +619,24 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       tc_fence_after();
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(32 * wq) << 16) + acc * BN;
       const int m128 = m_blk * 2 + static_cast<int>(rank);
+      long long slot = -1;  // the tile's own slots unless a stream-K piece after the tile's first
+      if (sg.piece >= 0 && sg.kb0 > 0) {
+        slot = p.sk_base + ((static_cast<long long>(cluster_id) * 2 + sg.piece) * 2 + rank) * 4 + wq;
+        sk_written[sg.piece] = true;
+      }
       epilogue_tile<kEpi>(p, smem + SL::stage_off, t_row, static_cast<long long>(m128) * 128 + 32 * wq, m128,
-                          n_blk, wq, lane);
+                          n_blk, wq, lane, slot);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(acc ? tempty_leader1 : tempty_leader0);
+    }
+    if (kEpi == kEpiGateGrad && p.stream_k && lane == 0) {
+      // stream-K slots this cluster did not fill read as zero in the reduction
+      for (int j = 0; j < 2; ++j) {
+        if (sk_written[j]) continue;
+        const long long slot = p.sk_base + ((static_cast<long long>(cluster_id) * 2 + j) * 2 + rank) * 4 + wq;
+        for (int k = 0; k < p.cands.K; ++k) p.partials[slot * p.cands.K + k] = 0.f;
+      }
     }
   }
 

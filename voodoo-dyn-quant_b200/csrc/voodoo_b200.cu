@@ -140,21 +140,43 @@ int build_candset(vq::CandSet* cs, int K, const int* types, const void* const* b
 // map box of a K-major B operand and the gate-gradient slot count depend on it).
 inline bool use_pair(long long M) { return M > vq::gemm::BM; }
 
+// Upper bound on CTA pairs of a paired launch (the stream-K partial slots of
+// the gate-gradient workspace are sized for it).
+constexpr int kMaxClusters = 128;
+
+// Gate-gradient partial slots the per-tile schedule writes.
+inline long long gategrad_tile_slots(long long N, long long Kin) {
+  const long long m128 = use_pair(N) ? 2 * ((N + 255) / 256) : (N + vq::gemm::BM - 1) / vq::gemm::BM;
+  return m128 * ((Kin + vq::gemm::BN - 1) / vq::gemm::BN) * 4;
+}
+
+// `used_slots` (gate-gradient launches): partial slots the launch writes.
 template <bool kAmn, bool kBmn, int kEpi>
-int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, vq::gemm::Params p, cudaStream_t st) {
+int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, vq::gemm::Params p, cudaStream_t st,
+                long long* used_slots = nullptr) {
   using namespace vq::gemm;
   const bool pair = use_pair(p.M);
   p.num_m_blk = pair ? (p.M + 255) / 256 : (p.M + BM - 1) / BM;
   p.num_n_blk = (p.N + BN - 1) / BN;
   p.num_k_blk = (p.K + BK - 1) / BK;
   p.num_tiles = p.num_m_blk * p.num_n_blk;
+  p.stream_k = 0;
+  p.sk_base = 0;
   int sms = 0;
   if (int rc = sm_count(&sms)) return rc;
+  if (used_slots != nullptr) *used_slots = gategrad_tile_slots(p.M, p.N);
   if (pair) {
     auto kern = gemm_pair_kernel<kAmn, kBmn, kEpi>;
     constexpr int smem = PairSmemLayout<kEpi>::total;
     VQ_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    const int clusters = p.num_tiles < sms / 2 ? p.num_tiles : sms / 2;
+    int clusters = p.num_tiles < sms / 2 ? p.num_tiles : sms / 2;
+    if (clusters > kMaxClusters) clusters = kMaxClusters;
+    if (kEpi == kEpiGateGrad && p.num_tiles % clusters != 0 && p.num_tiles > clusters) {
+      // split the last, partial wave of tiles along K across every cluster
+      p.stream_k = 1;
+      p.sk_base = static_cast<int>(gategrad_tile_slots(p.M, p.N));
+      if (used_slots != nullptr) *used_slots += 16LL * clusters;
+    }
     kern<<<2 * clusters, THREADS, smem, st>>>(ta, tb, p);
   } else {
     auto kern = gemm_kernel<kAmn, kBmn, kEpi>;
@@ -167,10 +189,10 @@ int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, vq::gemm::Params p
   return 0;
 }
 
-// Gate-gradient partial slots written by the kernel launch_gemm picks.
+// Gate-gradient partial slots a workspace must hold: the per-tile slots plus,
+// for paired launches, the stream-K slots (16 per cluster).
 inline long long gategrad_slots(long long N, long long Kin) {
-  const long long m128 = use_pair(N) ? 2 * ((N + 255) / 256) : (N + vq::gemm::BM - 1) / vq::gemm::BM;
-  return m128 * ((Kin + vq::gemm::BN - 1) / vq::gemm::BN) * 4;
+  return gategrad_tile_slots(N, Kin) + (use_pair(N) ? 16LL * kMaxClusters : 0);
 }
 
 int check_matrix(const void* p, long long rows, long long cols, long long ld, const char* name) {
@@ -384,8 +406,9 @@ int vq_gategrad(const void* dy, int64_t lddy, const void* x, int64_t ldx, int64_
   p.cols = Kin;
   p.partials = static_cast<float*>(workspace);
   if (int rc = device_error_ptr(&p.err)) return rc;
-  if (int rc = launch_gemm<true, true, vq::gemm::kEpiGateGrad>(ta, tb, p, st)) return rc;
-  const int slots = static_cast<int>(gategrad_slots(N, Kin));
+  long long used = 0;
+  if (int rc = launch_gemm<true, true, vq::gemm::kEpiGateGrad>(ta, tb, p, st, &used)) return rc;
+  const int slots = static_cast<int>(used);
   vq::gemm::gategrad_reduce_kernel<<<K, 512, 0, st>>>(p.partials, slots, K, grad_probs);
   VQ_CUDA(cudaGetLastError());
   return 0;
