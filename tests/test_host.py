@@ -196,3 +196,35 @@ def test_store_accounting():
     assert STORE.get("t.w") is m
     assert sum(l.nbytes for l in m._cand_layout) == sum(v.numel() for v in cb.values())
     assert all(l.offset % 256 == 0 for l in m._cand_layout)
+
+
+def test_gate_bank_matches_per_layer_probabilities_and_bytes():
+    """The batched per-step gate softmax equals each layer's own, and so do the
+    size term and its gradient."""
+    from voodoo_quant.layers import GateBank, total_effective_bytes
+
+    mods = {}
+    for i, (types, out_f, in_f) in enumerate([(("Q4_K", "Q8_0"), 32, 512), (("Q3_K", "Q4_K", "Q5_K", "Q6_K"), 16, 256),
+                                               (("Q6_K",), 8, 256)]):
+        m, _, _ = _module(types=types, out_f=out_f, in_f=in_f)
+        with torch.no_grad():
+            m.gates.copy_(torch.randn(len(types), generator=torch.Generator().manual_seed(i)))
+        m.set_temperature(0.3 + i)
+        mods[f"l{i}"] = m
+    ref_p = [m.soft_probs().detach() for m in mods.values()]
+    ref_b = total_effective_bytes(mods)
+    ref_b.backward()
+    ref_g = [m.gates.grad.clone() for m in mods.values()]
+    for m in mods.values():
+        m.gates.grad = None
+    bank = GateBank(mods)
+    bank.probs()
+    for m, p in zip(mods.values(), ref_p):
+        assert torch.allclose(m.get_probs(), p, rtol=1e-6, atol=1e-7)
+    b = bank.effective_bytes()
+    assert torch.allclose(b, ref_b, rtol=1e-6)
+    b.backward()
+    for m, g in zip(mods.values(), ref_g):
+        assert torch.allclose(m.gates.grad, g, rtol=1e-4, atol=1e-6)
+    bank.release()
+    assert all(m.__dict__.get("_bank_probs") is None for m in mods.values())

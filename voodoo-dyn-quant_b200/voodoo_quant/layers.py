@@ -334,6 +334,9 @@ class _MixedQuantBase(nn.Module):
         return F.softmax(self.gates / self.temperature, dim=0)
 
     def get_probs(self) -> torch.Tensor:
+        bank = self.__dict__.get("_bank_probs")
+        if bank is not None:  # this step's probabilities from a GateBank
+            return bank
         return self.soft_probs()
 
     def invalidate_candidate_cache(self):
@@ -470,10 +473,14 @@ class MixedQuantEmbedding(_MixedQuantBase):
         if spec is not None and spec.vocab_start is not None:
             from voodoo_quant.parallel import tp_all_reduce_sum
             v0, v1 = self.tp_vocab_start, self.tp_vocab_end
-            mask = (input < v0) | (input >= v1)
-            local = (input - v0).clamp(0, self.num_embeddings - 1)
-            emb = self._embedding_lookup(local)
-            emb = emb * (~mask).unsqueeze(-1).to(emb.device, emb.dtype)
+            ids = input.to(self._cand_arena.device)
+            in_shard = (ids >= v0) & (ids < v1)
+            # Only this shard's tokens are looked up: clamping the others to
+            # one row would funnel most of the batch's gradient into a single
+            # index of the lookup's backward.
+            emb_in = self._embedding_lookup(ids[in_shard] - v0)
+            emb = emb_in.new_zeros(*ids.shape, self.embedding_dim)
+            emb[in_shard] = emb_in
             return tp_all_reduce_sum(emb)
         return self._embedding_lookup(input)
 
@@ -590,6 +597,60 @@ def replace_embedding_with_mixed_quant(module: nn.Module, candidate_types: list[
                 child, candidate_types, full_name, skip_names, imatrix_dict, device, lazy, qbytes_device,
                 attention_candidates, non_attention_candidates, candidate_provider))
     return replaced
+
+
+class GateBank:
+    """All gated layers' softmax(g / tau) in one batched computation per step.
+
+    ``probs()`` pads every layer's gates into one [L, Kmax] matrix (-inf in
+    the padding), takes one softmax, and hands each layer a row view as the
+    probabilities its forward uses until ``release()``; ``effective_bytes``
+    is the same sum as ``total_effective_bytes`` from that matrix.  A step
+    then launches a handful of kernels for the gates instead of several per
+    layer for the forward and again for the size term.  Gradients reach each
+    layer's ``gates`` parameter through the padding as usual.
+    """
+
+    def __init__(self, replaced: dict[str, "_MixedQuantBase"]):
+        self.layers = list(replaced.values())
+        if not self.layers:
+            raise ValueError("GateBank needs at least one gated layer")
+        dev = self.layers[0].gates.device
+        self.kmax = max(l.num_candidates for l in self.layers)
+        L = len(self.layers)
+        idx, mask = [], torch.zeros(L, self.kmax, dtype=torch.bool)
+        bpwn = torch.zeros(L, self.kmax, dtype=torch.float64)
+        for i, l in enumerate(self.layers):
+            mask[i, :l.num_candidates] = True
+            out_eff = l.__dict__.get("_full_out_features") or l.out_features
+            in_eff = l.__dict__.get("_full_in_features") or l.in_features
+            for k, qt in enumerate(l.candidate_types):
+                bpwn[i, k] = bytes_per_weight(qt) * in_eff * out_eff
+            idx.extend(i * self.kmax + k for k in range(l.num_candidates))
+        self.flat_index = torch.tensor(idx, dtype=torch.long, device=dev)
+        self.valid = mask.to(dev)
+        self.bpwn = bpwn.to(torch.float32).to(dev)
+        self._p = None
+
+    def probs(self) -> torch.Tensor:
+        g = torch.cat([l.gates / l.temperature for l in self.layers])
+        padded = torch.full((len(self.layers) * self.kmax,), float("-inf"), dtype=g.dtype, device=g.device)
+        padded = padded.index_put((self.flat_index,), g)
+        p = torch.softmax(padded.view(len(self.layers), self.kmax), dim=1)
+        for i, l in enumerate(self.layers):
+            l._bank_probs = p[i, :l.num_candidates]
+        self._p = p
+        return p
+
+    def effective_bytes(self) -> torch.Tensor:
+        if self._p is None:
+            raise RuntimeError("GateBank.probs() must run first in this step")
+        return (self._p * self.bpwn).sum()
+
+    def release(self) -> None:
+        for l in self.layers:
+            l._bank_probs = None
+        self._p = None
 
 
 def total_effective_bytes(replaced: dict[str, _MixedQuantBase]) -> torch.Tensor:

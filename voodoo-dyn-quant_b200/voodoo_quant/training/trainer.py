@@ -23,7 +23,7 @@ from dataclasses import dataclass
 import torch
 import torch.nn as nn
 
-from voodoo_quant.layers import total_effective_bytes
+from voodoo_quant.layers import GateBank
 from voodoo_quant.training.loss import distillation_loss, tp_distillation_loss
 
 
@@ -93,6 +93,7 @@ class GatedDistillTrainer:
         for layer in replaced.values():
             layer.gates.requires_grad = True
         self.trainable = [layer.gates for layer in replaced.values()]
+        self.bank = GateBank(replaced)  # every layer's softmax(g / tau) in one batched op per step
         self.optimizer = torch.optim.AdamW(self.trainable, lr=args.lr, betas=(0.9, 0.95))
         self.scheduler = torch.optim.lr_scheduler.CosineAnnealingLR(self.optimizer, T_max=args.max_steps,
                                                                     eta_min=1e-3)
@@ -110,6 +111,7 @@ class GatedDistillTrainer:
         tau = anneal_temperature(self.step_idx, a.max_steps, a.temp_start, a.temp_end)
         for layer in self.replaced.values():
             layer.set_temperature(tau)
+        self.bank.probs()
         logits = self.student(input_ids=x, use_cache=False).logits
         with torch.no_grad():
             t_logits = self.teacher(input_ids=x, use_cache=False).logits
@@ -121,7 +123,7 @@ class GatedDistillTrainer:
             kd, lm, kl = distillation_loss(logits, t_logits, y, a.distill_temperature, a.distill_weight,
                                            ce_reduction=a.ce_reduction)
         del t_logits
-        current = total_effective_bytes(self.replaced).to(logits.device)
+        current = self.bank.effective_bytes().to(logits.device)
         if self.tp:
             from voodoo_quant.parallel import tp_all_reduce_sum
 
@@ -132,6 +134,7 @@ class GatedDistillTrainer:
         loss = kd + a.size_weight * size_loss
         self.optimizer.zero_grad(set_to_none=True)
         loss.backward()
+        self.bank.release()
         if self.tp:
             _tp_all_reduce_gate_grads(self.trainable)
         return {"loss": loss.detach(), "lm_loss": lm, "distill_loss": kl, "size_bytes": current.detach(),
