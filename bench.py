@@ -578,8 +578,11 @@ def run_model_step(args):
         return float(t.item())
 
     t_build = time.perf_counter()
-    trainer, shape = build_distill(args.workload, dev, seed=0, tp=world > 1,
+    trainer, shape = build_distill(args.workload, dev, seed=0, tp=world > 1, multicast=args.multicast,
                                    args=StepArgs(max_steps=args.warmup + args.steps + args.e2e_steps + 3))
+    from voodoo_quant import parallel as _par
+
+    multicast_on = _par.multicast_reducer() is not None
     torch.cuda.synchronize()
     t_build = time.perf_counter() - t_build
     x, y = S.random_tokens(shape, dev, seed=1)
@@ -648,6 +651,7 @@ def run_model_step(args):
                        "batch": shape.batch, "seq": shape.seq, "candidates": shape.candidates,
                        "gated_tensors": len(trainer.replaced), "budget": shape.budget,
                        "parallelism": f"tp{world}", "build_s": round(t_build, 1),
+                       "row_parallel_reduce": "nvls multimem.red in GEMM" if multicast_on else "nccl all-reduce",
                        "l2": "activations and logits far larger than L2"},
             "roofline": {"bound": "tensor", "kernel": "whole step", "flops_per_token": fpt,
                          "achieved": round(ach, 1), "peak": round(peak_t * world, 1), "unit": "TFLOP/s",
@@ -662,6 +666,7 @@ def run_model_step(args):
         }
         print(json.dumps(res), flush=True)
     if world > 1:
+        _par.enable_multicast_reduce(False)  # every rank releases the multicast buffers together
         dist.barrier()
         dist.destroy_process_group()
 
@@ -678,6 +683,8 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--cpu-tokens", type=int, default=2048)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--multicast", action="store_true",
+                    help="full-step workloads under TP: sum row-parallel outputs with multimem.red in the GEMM")
     ap.add_argument("--profile-step", action="store_true",
                     help="full-step workloads: print device time per kernel name for one step")
     ap.add_argument("--ncu-case", action="store_true", help="one launch per kernel at profiling sizes")

@@ -44,6 +44,7 @@ def _declare(lib):
         "vq_dequant": (_int, [_int, _vp, _i64, _i64, _vp, _vp]),
         "vq_mix": (_int, [_int, _vp, _vp, _vp, _i64, _i64, _i64, _vp, _i64, _vp]),
         "vq_linear_fwd": (_int, [_vp, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _vp]),
+        "vq_linear_fwd_mcred": (_int, [_vp, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _vp]),
         "vq_linear_dx": (_int, [_vp, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _vp]),
         "vq_gategrad_workspace_bytes": (ctypes.c_size_t, [_i64, _i64, _int]),
         "vq_gategrad": (_int, [_vp, _i64, _vp, _i64, _i64, _i64, _i64, _int, _vp, _vp, _i64, _vp,
@@ -72,7 +73,7 @@ def _declare(lib):
 
 EXPORTED = (
     "vq_last_error", "vq_abi_version", "vq_format_info", "vq_device_error", "vq_dequant", "vq_mix",
-    "vq_linear_fwd", "vq_linear_dx", "vq_gategrad_workspace_bytes", "vq_gategrad", "vq_gategrad_noalloc",
+    "vq_linear_fwd", "vq_linear_fwd_mcred", "vq_linear_dx", "vq_gategrad_workspace_bytes", "vq_gategrad", "vq_gategrad_noalloc",
     "vq_mixgemm_fwd",
     "vq_loss_fused", "vq_loss_stats", "vq_loss_combine", "vq_loss_grad",
     "vq_rmsnorm_fwd", "vq_rmsnorm_bwd", "vq_rope", "vq_swiglu_fwd", "vq_swiglu_bwd",
@@ -201,6 +202,14 @@ def linear_fwd(x: torch.Tensor, w: torch.Tensor, n_out: int | None = None, in_fe
     _check(_lib.vq_linear_fwd(x.data_ptr(), x.shape[0], kin, x.stride(0), w.data_ptr(), N, w.stride(0),
                               out.data_ptr(), out.stride(0), _stream(x)))
     return out
+
+
+def linear_fwd_mcred(x: torch.Tensor, w: torch.Tensor, n_out: int, in_features: int, y_multicast: int) -> None:
+    """Add x[T, Kin] w[N, Kin]^T into the NVLink multicast address `y_multicast` ([T, n_out] bf16)."""
+    _require_cuda(x, w)
+    x = _as_operand(x)
+    _check(_lib.vq_linear_fwd_mcred(x.data_ptr(), x.shape[0], in_features, x.stride(0), w.data_ptr(), n_out,
+                                    w.stride(0), y_multicast, n_out, _stream(x)))
 
 
 def linear_dx(dy: torch.Tensor, w: torch.Tensor, in_features: int, out: torch.Tensor | None = None) -> torch.Tensor:

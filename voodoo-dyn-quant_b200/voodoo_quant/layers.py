@@ -111,11 +111,14 @@ class _GatedLinearFunction(Function):
     """y = x W_mix^T with W_mix = sum_k p_k W_k; gradients for x and p."""
 
     @staticmethod
-    def forward(ctx, x: torch.Tensor, probs: torch.Tensor, layer: "MixedQuantLinear"):
+    def forward(ctx, x: torch.Tensor, probs: torch.Tensor, layer: "MixedQuantLinear", reducer=None):
         in_f, out_f = layer.in_features, layer.out_features
         x2 = _C._as_operand(x.reshape(-1, in_f))
         w_mix = layer._mix(probs)
-        y = _C.linear_fwd(x2, w_mix, out_f, in_f)
+        if reducer is not None:  # row-parallel: the output sum over the TP ranks, reduced in the GEMM
+            y = reducer.linear(x2, w_mix, out_f, in_f)
+        else:
+            y = _C.linear_fwd(x2, w_mix, out_f, in_f)
         ctx.layer = layer
         ctx.x_shape = x.shape
         ctx.x_dtype = x.dtype
@@ -147,7 +150,7 @@ class _GatedLinearFunction(Function):
             pending.wait()
         if dx is not None:
             dx = dx.to(ctx.x_dtype).reshape(ctx.x_shape)
-        return dx, dprobs, None
+        return dx, dprobs, None, None
 
 
 class _MixedWeightFunction(Function):
@@ -429,11 +432,14 @@ class MixedQuantLinear(_MixedQuantBase):
         spec = self.shard_spec
         if x.device != self._cand_arena.device:
             x = x.to(self._cand_arena.device)
-        out = _GatedLinearFunction.apply(x, self.get_probs().to(x.device), self)
         if spec is not None and spec.col_offset is not None:
-            from voodoo_quant.parallel import tp_all_reduce_sum
-            out = tp_all_reduce_sum(out)
-        return out
+            from voodoo_quant.parallel import multicast_reducer, tp_all_reduce_sum
+            red = multicast_reducer()
+            if red is not None:
+                # the all-reduce's backward is the identity, so the gradients are the local ones
+                return _GatedLinearFunction.apply(x, self.get_probs().to(x.device), self, red)
+            return tp_all_reduce_sum(_GatedLinearFunction.apply(x, self.get_probs().to(x.device), self))
+        return _GatedLinearFunction.apply(x, self.get_probs().to(x.device), self)
 
 
 class MixedQuantEmbedding(_MixedQuantBase):

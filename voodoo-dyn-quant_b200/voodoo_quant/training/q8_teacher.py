@@ -108,8 +108,14 @@ class _RowParallelQ8(nn.Module):
         self.inner = inner
         self.out_features, self.in_features = inner.out_features, inner.in_features
 
+    @torch.no_grad()
     def forward(self, x):
-        from voodoo_quant.parallel import tp_all_reduce_sum
+        from voodoo_quant.parallel import multicast_reducer, tp_all_reduce_sum
+        red = multicast_reducer()
+        if red is not None and x.is_cuda:  # partial outputs summed over the TP ranks inside the GEMM
+            x2 = _C._as_operand(x.reshape(-1, self.in_features))
+            y = red.linear(x2, self.inner.weight_bf16(), self.out_features, self.in_features)
+            return y.to(x.dtype).reshape(*x.shape[:-1], self.out_features)
         return tp_all_reduce_sum(self.inner(x))
 
 

@@ -157,7 +157,7 @@ class GatedDistillTrainer:
 
 def build_distill(shape_name: str, device, seed: int = 0, args: StepArgs | None = None,
                   candidate_provider=None, replace_embeddings: bool = True, tp: bool = False,
-                  fused_blocks: bool = True):
+                  fused_blocks: bool = True, multicast: bool = False):
     """Student (gated), Q8_0 teacher and trainer for a synthetic config.
 
     Under TP (an initialised process group adopted by voodoo_quant.parallel)
@@ -165,6 +165,11 @@ def build_distill(shape_name: str, device, seed: int = 0, args: StepArgs | None 
     candidates are packed from the FULL tensors and sliced per rank.  On a
     CUDA device ``fused_blocks`` routes the Llama blocks' RMSNorm, rotary
     embedding and SwiGLU through the fused kernels (``voodoo_quant.fused_blocks``).
+    Under TP with ``multicast``, row-parallel outputs are summed over NVLink
+    SHARP inside their GEMMs (``parallel.enable_multicast_reduce``) where the
+    GPUs support NVLink multicast; off by default: every rank's memory then
+    takes every rank's reductions, and an 8B step at TP-2 measured 774 ms
+    against 610 ms with NCCL's ring all-reduce.
     """
     from voodoo_quant.layers import replace_embedding_with_mixed_quant, replace_linear_with_mixed_quant
     from voodoo_quant.parallel import TP, tp_patch_model
@@ -197,6 +202,10 @@ def build_distill(shape_name: str, device, seed: int = 0, args: StepArgs | None 
 
         fuse_llama_blocks(base)
         fuse_llama_blocks(teacher)
+    if tp and TP.enabled:
+        from voodoo_quant.parallel import enable_multicast_reduce
+
+        enable_multicast_reduce(multicast)
     torch.cuda.empty_cache()
     trainer = GatedDistillTrainer(base, teacher, replaced, args or StepArgs(), shape.budget * total_8bit,
                                   non_targeted, tp=tp and TP.enabled)
