@@ -579,7 +579,8 @@ def run_model_step(args):
 
     t_build = time.perf_counter()
     trainer, shape = build_distill(args.workload, dev, seed=0, tp=world > 1, multicast=args.multicast,
-                                   args=StepArgs(max_steps=args.warmup + args.steps + args.e2e_steps + 3))
+                                   args=StepArgs(max_steps=args.warmup + args.steps + args.e2e_steps + 3,
+                                                 ptqr=args.ptqr))
     from voodoo_quant import parallel as _par
 
     multicast_on = _par.multicast_reducer() is not None
@@ -652,6 +653,7 @@ def run_model_step(args):
                        "gated_tensors": len(trainer.replaced), "budget": shape.budget,
                        "parallelism": f"tp{world}", "build_s": round(t_build, 1),
                        "row_parallel_reduce": "nvls multimem.red in GEMM" if multicast_on else "nccl all-reduce",
+                       "forward": "ptqr (one candidate per token)" if args.ptqr else "candidate mixture",
                        "l2": "activations and logits far larger than L2"},
             "roofline": {"bound": "tensor", "kernel": "whole step", "flops_per_token": fpt,
                          "achieved": round(ach, 1), "peak": round(peak_t * world, 1), "unit": "TFLOP/s",
@@ -683,6 +685,8 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--cpu-tokens", type=int, default=2048)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--ptqr", action="store_true",
+                    help="full-step workloads: per-token quant routing forward (one candidate per token)")
     ap.add_argument("--multicast", action="store_true",
                     help="full-step workloads under TP: sum row-parallel outputs with multimem.red in the GEMM")
     ap.add_argument("--profile-step", action="store_true",

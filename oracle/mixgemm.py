@@ -104,3 +104,34 @@ def gate_grad(probs: np.ndarray, dprobs: np.ndarray, tau: float) -> np.ndarray:
 
 def assignment(gates: np.ndarray, candidate_types: list[str]) -> str:
     return candidate_types[int(np.argmax(np.asarray(gates)))]
+
+
+def routed_linear_fwd(x: np.ndarray, cands: list[np.ndarray], routing: np.ndarray) -> np.ndarray:
+    """PTQR forward y[t] = x[t] W_{routing[t]}^T in float32 (reference
+    _RoutedMixedLinear.forward, voodoo_quant/layers.py:384-401).  Its
+    backward is the mixture's: dX = dY W_mix, g_k = <dY^T X, W_k>."""
+    y = np.zeros((x.shape[0], cands[0].shape[0]), np.float32)
+    for k, w in enumerate(cands):
+        rows = np.nonzero(routing == k)[0]
+        if rows.size:
+            y[rows] = x[rows].astype(np.float32) @ w.astype(np.float32).T
+    return y
+
+
+def bf16_round(a: np.ndarray) -> np.ndarray:
+    """float32 -> nearest bfloat16 (ties to even) -> float32; NaN stays NaN."""
+    u = np.ascontiguousarray(a, dtype=np.float32).view(np.uint32)
+    r = ((u + 0x7FFF + ((u >> 16) & 1)) & 0xFFFF0000).astype(np.uint32)
+    out = r.view(np.float32)
+    return np.where(np.isnan(a), np.float32(np.nan), out)
+
+
+def routed_rows(rows_by_cand: list[np.ndarray], routing: np.ndarray) -> np.ndarray:
+    """PTQR embedding rows: row i is candidate routing[i]'s decoded row,
+    rounded to bf16 (reference _MixedEmbeddingRowFunctionLazy with routing,
+    voodoo_quant/layers.py:702-728)."""
+    out = np.zeros_like(rows_by_cand[0], dtype=np.float32)
+    for k, r in enumerate(rows_by_cand):
+        sel = routing == k
+        out[sel] = r[sel]
+    return bf16_round(out)

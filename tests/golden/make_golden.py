@@ -14,6 +14,9 @@ What it records (all seeded, all small):
   dependency; the reference has no decoder for them).  Every format is also
   cross-checked against gguf-py here.  Each format carries edge blocks whose
   fp16 scales are +0, -0, subnormal, 65504, +inf, -inf and NaN.
+* ``ptqr_golden.npz`` -- the reference's per-token routed forwards
+  (``_RoutedMixedLinear``, ``_MixedEmbeddingRowFunctionLazy`` with a fixed
+  routing) and their straight-through backward.
 * ``mixlinear_golden.npz`` -- the reference's ``_MixedWeightFunction`` +
   ``F.linear`` autograd (``layers.py:322-363``, ``:1730-1731``) in float32:
   Y, dX, d(probs) and d(gates) for seeded X, dY, gates and packed candidates.
@@ -199,6 +202,69 @@ def main() -> None:
         loss[f"{case}/dlogits"] = student.model.logits.grad.numpy()
     np.savez_compressed(HERE / "loss_golden.npz", **loss)
     print("loss golden written")
+
+    # ---- PTQR (per-token routing) forward with the straight-through backward --
+    # A fixed routing stands in for the Gumbel sample so that the B200 path
+    # can be run on the same routing.
+    prng = np.random.default_rng(20261201)
+    ptqr = {}
+    fmts = ["Q4_K", "Q5_K", "Q6_K", "Q8_0"]
+    T, IN, OUT, tau = 40, 512, 64, 1.0
+    cands = []
+    for k, fmt in enumerate(fmts):
+        bs, bb, _ = FORMATS[fmt]
+        raw = random_blocks(prng, fmt, OUT * IN // bs, edge=False)
+        for off in FORMATS[fmt][2]:
+            vals = (prng.uniform(5e-4, 2e-3, size=raw.shape[0]) * prng.choice([-1, 1], raw.shape[0])).astype(np.float16)
+            raw[:, off:off + 2] = vals.view(np.uint8).reshape(-1, 2)
+        cands.append(torch.from_numpy(gq.dequantize(raw.reshape(-1), gg_type[fmt]).reshape(OUT, IN).astype(np.float32)))
+        ptqr[f"lin/cand{k}/bytes"] = raw
+    x = torch.from_numpy(prng.standard_normal((T, IN)).astype(np.float32)).requires_grad_(True)
+    gates = torch.from_numpy(prng.standard_normal(len(fmts)).astype(np.float32)).requires_grad_(True)
+    dy = torch.from_numpy(prng.standard_normal((T, OUT)).astype(np.float32))
+    routing = torch.from_numpy(prng.integers(0, len(fmts), size=T).astype(np.int64))
+    probs = F.softmax(gates / tau, dim=0)
+    probs.retain_grad()
+    y = L._RoutedMixedLinear.apply(torch.float32, probs, routing, x, *cands)
+    y.backward(dy)
+    ptqr["lin/formats"] = np.array(fmts)
+    ptqr["lin/tau"] = np.float32(tau)
+    ptqr["lin/x"] = x.detach().numpy()
+    ptqr["lin/dy"] = dy.numpy()
+    ptqr["lin/gates"] = gates.detach().numpy()
+    ptqr["lin/routing"] = routing.numpy()
+    ptqr["lin/y"] = y.detach().numpy()
+    ptqr["lin/dx"] = x.grad.numpy()
+    ptqr["lin/dprobs"] = probs.grad.numpy()
+    ptqr["lin/dgates"] = gates.grad.numpy()
+
+    V, D = 64, 512
+    qbytes = []
+    for k, fmt in enumerate(fmts):
+        bs, bb, _ = FORMATS[fmt]
+        raw = random_blocks(prng, fmt, V * D // bs, edge=False)
+        for off in FORMATS[fmt][2]:
+            vals = (prng.uniform(5e-4, 2e-3, size=raw.shape[0]) * prng.choice([-1, 1], raw.shape[0])).astype(np.float16)
+            raw[:, off:off + 2] = vals.view(np.uint8).reshape(-1, 2)
+        qbytes.append(torch.from_numpy(raw.copy()))
+        ptqr[f"emb/cand{k}/bytes"] = raw
+    row_ids = torch.from_numpy(np.sort(prng.choice(V, size=20, replace=False)).astype(np.int64))
+    eroute = torch.from_numpy(prng.integers(0, len(fmts), size=20).astype(np.int64))
+    egates = torch.from_numpy(prng.standard_normal(len(fmts)).astype(np.float32)).requires_grad_(True)
+    eprobs = F.softmax(egates, dim=0)
+    eprobs.retain_grad()
+    rows_out = L._MixedEmbeddingRowFunctionLazy.apply(torch.bfloat16, tuple(fmts), V, D, D, eprobs, eroute, row_ids,
+                                                      *qbytes)
+    G = torch.from_numpy(prng.standard_normal((20, D)).astype(np.float32))
+    rows_out.float().backward(G)
+    ptqr["emb/row_ids"] = row_ids.numpy()
+    ptqr["emb/routing"] = eroute.numpy()
+    ptqr["emb/gates"] = egates.detach().numpy()
+    ptqr["emb/grad_out"] = G.numpy()
+    ptqr["emb/rows"] = rows_out.detach().float().numpy()
+    ptqr["emb/dprobs"] = eprobs.grad.numpy()
+    np.savez_compressed(HERE / "ptqr_golden.npz", **ptqr)
+    print("ptqr golden written")
 
 
 if __name__ == "__main__":

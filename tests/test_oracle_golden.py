@@ -77,3 +77,38 @@ def test_loss_matches_reference_chunked_loss(golden_dir, case):
 
 def test_assignment_first_max_wins():
     assert mixgemm.assignment(np.array([0.5, 2.0, 2.0, -1.0]), ["a", "b", "c", "d"]) == "b"
+
+
+def test_ptqr_oracle_matches_reference_routed_functions(golden_dir):
+    """The routed forward and its straight-through backward against the
+    reference's own _RoutedMixedLinear / _MixedEmbeddingRowFunctionLazy."""
+    from oracle import ggml_blocks, mixgemm
+
+    z = np.load(golden_dir / "ptqr_golden.npz")
+    fmts = [str(f) for f in z["lin/formats"]]
+    y = z["lin/y"]
+    OUT, IN = z["lin/dy"].shape[1], z["lin/x"].shape[1]
+    cands = [ggml_blocks.dequantize(z[f"lin/cand{k}/bytes"], f, OUT, IN) for k, f in enumerate(fmts)]
+    x, dy, routing = z["lin/x"], z["lin/dy"], z["lin/routing"]
+    assert np.allclose(mixgemm.routed_linear_fwd(x, cands, routing), y, rtol=1e-4, atol=1e-5)
+    probs = mixgemm.softmax_probs(z["lin/gates"], float(z["lin/tau"]))
+    w_mix = mixgemm.mixed_weight(cands, probs)
+    assert np.allclose(mixgemm.linear_dx(dy, w_mix), z["lin/dx"], rtol=1e-4, atol=1e-5)
+    assert np.allclose(mixgemm.prob_grad(dy, x, cands), z["lin/dprobs"], rtol=1e-4, atol=1e-3)
+    # embedding rows: exact decode of the routed candidate, rounded once to bf16
+    V, D = 64, 512
+    rows = z["emb/row_ids"]
+    by_cand = [ggml_blocks.dequantize(z[f"emb/cand{k}/bytes"], f, V, D)[rows] for k, f in enumerate(fmts)]
+    got = mixgemm.routed_rows(by_cand, z["emb/routing"])
+    assert np.array_equal(got.view(np.uint32), z["emb/rows"].astype(np.float32).view(np.uint32))
+
+
+def test_routing_sampler_shares_follow_probabilities():
+    import torch
+    from voodoo_quant.layers import _sample_token_routing
+
+    torch.manual_seed(0)
+    p = torch.tensor([0.1, 0.6, 0.05, 0.25])
+    r = _sample_token_routing(p, 200000)
+    shares = torch.bincount(r, minlength=4).double() / r.numel()
+    assert torch.allclose(shares, p.double(), atol=5e-3)

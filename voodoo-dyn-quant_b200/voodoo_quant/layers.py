@@ -46,6 +46,37 @@ _CANDIDATE_CACHE_ROOT = CANDIDATE_CACHE_DIR
 KEEP_MIXED_WEIGHT = True
 
 
+# --------------------------------------------------------------------------- per-token quant routing
+class _PTQRState:
+    """Per-Token Quant Routing (reference voodoo_quant/layers.py:848-865).
+
+    When enabled, every gated layer runs each token through ONE candidate,
+    sampled from the gate probabilities, instead of the candidate mixture;
+    the backward stays the mixture's straight-through Jacobian.
+    """
+
+    enabled: bool = False
+
+
+_PTQR_STATE = _PTQRState()
+
+
+def set_ptqr(enabled: bool) -> None:
+    _PTQR_STATE.enabled = bool(enabled)
+
+
+def _sample_token_routing(probs: torch.Tensor, num_tokens: int) -> torch.Tensor:
+    """k*(t) ~ Categorical(probs) per token by Gumbel-argmax (reference :868-881).
+
+    The same torch operations as the reference, so a given generator state
+    yields the same routing.
+    """
+    u = torch.rand(probs.shape[0], num_tokens, device=probs.device)
+    gumbel = -torch.log((-torch.log(u.clamp_min(1e-9))).clamp_min(1e-9))
+    scores = torch.log(probs.clamp_min(1e-9)).unsqueeze(1) + gumbel
+    return scores.argmax(dim=0)
+
+
 # --------------------------------------------------------------------------- cache helpers
 def _tensor_hash(t: torch.Tensor | None) -> str:
     """SHA-256 (first 16 hex) of the tensor's float32 bytes, streamed in 4M-element chunks.
@@ -128,28 +159,79 @@ class _GatedLinearFunction(Function):
 
     @staticmethod
     def backward(ctx, dy: torch.Tensor):
-        layer = ctx.layer
-        x2, probs = ctx.saved_tensors
-        dy2 = _C._as_operand(dy.reshape(-1, layer.out_features))
-        dx = dprobs = None
-        pending = None
-        if ctx.needs_input_grad[0]:
-            w_mix = ctx.w_mix if ctx.w_mix is not None else layer._mix(probs)
-            dx = _C.linear_dx(dy2, w_mix, layer.in_features)
-            if layer.reduce_input_grad:
-                # column-parallel layer with a private input: sum the partial
-                # dX over the TP ranks while the gate-gradient GEMM runs
-                from voodoo_quant.parallel import tp_all_reduce_async
-                pending = tp_all_reduce_async(dx)
-        ctx.w_mix = None
-        if ctx.needs_input_grad[1]:
-            dprobs = _C.gategrad(dy2, x2, layer.candidate_types, layer._candidate_blocks(), layer.out_features,
-                                 layer.in_features, layer.padded_in_features,
-                                 workspace=layer._gategrad_workspace(x2.device)).to(probs.dtype)
-        if pending is not None:
-            pending.wait()
-        if dx is not None:
-            dx = dx.to(ctx.x_dtype).reshape(ctx.x_shape)
+        dx, dprobs = _gated_linear_backward(ctx, dy)
+        return dx, dprobs, None, None
+
+
+def _gated_linear_backward(ctx, dy: torch.Tensor):
+    """dX = dY W_mix and d probs_k = <dY^T X, W_k>: the mixture's Jacobian,
+    shared by the mixture forward and the routed (PTQR) forward."""
+    layer = ctx.layer
+    x2, probs = ctx.saved_tensors
+    dy2 = _C._as_operand(dy.reshape(-1, layer.out_features))
+    dx = dprobs = None
+    pending = None
+    if ctx.needs_input_grad[0]:
+        w_mix = ctx.w_mix if ctx.w_mix is not None else layer._mix(probs)
+        dx = _C.linear_dx(dy2, w_mix, layer.in_features)
+        if layer.reduce_input_grad:
+            # column-parallel layer with a private input: sum the partial
+            # dX over the TP ranks while the gate-gradient GEMM runs
+            from voodoo_quant.parallel import tp_all_reduce_async
+            pending = tp_all_reduce_async(dx)
+    ctx.w_mix = None
+    if ctx.needs_input_grad[1]:
+        dprobs = _C.gategrad(dy2, x2, layer.candidate_types, layer._candidate_blocks(), layer.out_features,
+                             layer.in_features, layer.padded_in_features,
+                             workspace=layer._gategrad_workspace(x2.device)).to(probs.dtype)
+    if pending is not None:
+        pending.wait()
+    if dx is not None:
+        dx = dx.to(ctx.x_dtype).reshape(ctx.x_shape)
+    return dx, dprobs
+
+
+class _RoutedGatedLinearFunction(Function):
+    """PTQR forward y[t] = x[t] W_{k(t)}^T, one candidate per token (reference
+    _RoutedMixedLinear, voodoo_quant/layers.py:366-428).
+
+    Tokens are grouped by candidate (a stable sort of the routing), each
+    group runs one tcgen05 GEMM against its candidate's bf16 decode (the
+    mixture kernel with a one-hot probability), and rows are scattered back;
+    the GEMM FLOPs equal one dense forward.  Backward is the mixture's
+    straight-through Jacobian: dX = dY W_mix, d p_k = <dY^T X, W_k>.
+    """
+
+    @staticmethod
+    def forward(ctx, x: torch.Tensor, probs: torch.Tensor, layer: "MixedQuantLinear", routing: torch.Tensor):
+        in_f, out_f = layer.in_features, layer.out_features
+        x2 = _C._as_operand(x.reshape(-1, in_f))
+        T = x2.shape[0]
+        routing = routing.to(x2.device).reshape(-1)
+        order = torch.argsort(routing, stable=True)
+        counts = torch.bincount(routing, minlength=layer.num_candidates).tolist()
+        xs = x2.index_select(0, order)
+        ys = torch.empty(T, out_f, dtype=torch.bfloat16, device=x2.device)
+        one = torch.ones(1, dtype=torch.float32, device=x2.device)
+        blocks = layer._candidate_blocks()
+        off = 0
+        for k, n in enumerate(counts):
+            if n == 0:
+                continue
+            w_k = _C.mix([layer.candidate_types[k]], [blocks[k]], one, out_f, layer.padded_in_features, in_f)
+            _C.linear_fwd(xs[off:off + n], w_k, out_f, in_f, out=ys[off:off + n])
+            off += n
+        y = torch.empty_like(ys).index_copy_(0, order, ys)
+        ctx.layer = layer
+        ctx.x_shape = x.shape
+        ctx.x_dtype = x.dtype
+        ctx.save_for_backward(x2, probs)
+        ctx.w_mix = None  # the backward mixes W_mix itself
+        return y.to(x.dtype).reshape(*x.shape[:-1], out_f)
+
+    @staticmethod
+    def backward(ctx, dy: torch.Tensor):
+        dx, dprobs = _gated_linear_backward(ctx, dy)
         return dx, dprobs, None, None
 
 
@@ -177,13 +259,25 @@ class _GatedEmbeddingRowsFunction(Function):
     """Mixed rows of a vocabulary-scale embedding; only the touched rows are decoded."""
 
     @staticmethod
-    def forward(ctx, probs: torch.Tensor, rows: torch.Tensor, layer: "MixedQuantEmbedding"):
-        blocks = layer._row_blocks(rows)
-        w = _C.mix(layer.candidate_types, blocks, probs, rows.numel(), layer.padded_in_features,
-                   layer.embedding_dim)
+    def forward(ctx, probs: torch.Tensor, rows: torch.Tensor, layer: "MixedQuantEmbedding",
+                routing: torch.Tensor | None = None):
+        D = layer.embedding_dim
+        if routing is None:
+            blocks = layer._row_blocks(rows)
+            w = _C.mix(layer.candidate_types, blocks, probs, rows.numel(), layer.padded_in_features, D)[:, :D]
+        else:
+            # PTQR: row i keeps candidate routing[i]'s decoded row (reference :712-717)
+            w = torch.empty(rows.numel(), D, dtype=torch.bfloat16, device=rows.device)
+            one = torch.ones(1, dtype=torch.float32, device=rows.device)
+            for k, qt in enumerate(layer.candidate_types):
+                idx = torch.nonzero(routing == k, as_tuple=False).squeeze(1)
+                if idx.numel() == 0:
+                    continue
+                blk = layer._row_blocks(rows.index_select(0, idx), only=k)
+                w[idx] = _C.mix([qt], blk, one, idx.numel(), layer.padded_in_features, D)[:, :D]
         ctx.layer = layer
         ctx.save_for_backward(rows)
-        return w[:, :layer.embedding_dim].to(layer.source_dtype)
+        return w.to(layer.source_dtype)
 
     @staticmethod
     def backward(ctx, g: torch.Tensor):
@@ -195,7 +289,7 @@ class _GatedEmbeddingRowsFunction(Function):
         for k, (qt, qb) in enumerate(zip(layer.candidate_types, blocks)):
             w = _C.dequant(qb, qt, rows.numel(), layer.padded_in_features)[:, :layer.embedding_dim]
             out[k] = (gf * w).sum()
-        return out, None, None
+        return out, None, None, None
 
 
 # --------------------------------------------------------------------------- modules
@@ -432,6 +526,14 @@ class MixedQuantLinear(_MixedQuantBase):
         spec = self.shard_spec
         if x.device != self._cand_arena.device:
             x = x.to(self._cand_arena.device)
+        if _PTQR_STATE.enabled:
+            probs = self.get_probs().to(x.device)
+            routing = _sample_token_routing(probs, x.numel() // x.shape[-1])
+            out = _RoutedGatedLinearFunction.apply(x, probs, self, routing)
+            if spec is not None and spec.col_offset is not None:
+                from voodoo_quant.parallel import tp_all_reduce_sum
+                out = tp_all_reduce_sum(out)
+            return out
         if spec is not None and spec.col_offset is not None:
             from voodoo_quant.parallel import multicast_reducer, tp_all_reduce_sum
             red = multicast_reducer()
@@ -460,9 +562,11 @@ class MixedQuantEmbedding(_MixedQuantBase):
             self.tp_vocab_start = shard_spec.vocab_start
             self.tp_vocab_end = shard_spec.vocab_start + num_embeddings
 
-    def _row_blocks(self, rows: torch.Tensor) -> list[torch.Tensor]:
+    def _row_blocks(self, rows: torch.Tensor, only: int | None = None) -> list[torch.Tensor]:
         out = []
-        for qt, qb in zip(self.candidate_types, self._candidate_blocks()):
+        for k, (qt, qb) in enumerate(zip(self.candidate_types, self._candidate_blocks())):
+            if only is not None and k != only:
+                continue
             info = get_quant_info(qt)
             nbpr = self.padded_in_features // info.block_size
             out.append(qb.view(self.num_embeddings, nbpr * info.block_bytes).index_select(0, rows).reshape(-1))
@@ -471,7 +575,12 @@ class MixedQuantEmbedding(_MixedQuantBase):
     def _embedding_lookup(self, ids: torch.Tensor) -> torch.Tensor:
         dev = self._cand_arena.device
         rows, inverse = torch.unique(ids.reshape(-1).to(dev), return_inverse=True)
-        mixed = _GatedEmbeddingRowsFunction.apply(self.get_probs().to(dev), rows, self)
+        probs = self.get_probs().to(dev)
+        if _PTQR_STATE.enabled:  # one candidate per (unique) row, reference layers.py:1810-1813
+            routing = _sample_token_routing(probs, rows.shape[0])
+            mixed = _GatedEmbeddingRowsFunction.apply(probs, rows, self, routing)
+        else:
+            mixed = _GatedEmbeddingRowsFunction.apply(probs, rows, self)
         return mixed[inverse].reshape(*ids.shape, self.embedding_dim)
 
     def forward(self, input: torch.Tensor) -> torch.Tensor:

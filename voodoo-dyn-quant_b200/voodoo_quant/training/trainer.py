@@ -23,7 +23,7 @@ from dataclasses import dataclass
 import torch
 import torch.nn as nn
 
-from voodoo_quant.layers import GateBank
+from voodoo_quant.layers import GateBank, set_ptqr
 from voodoo_quant.training.loss import distillation_loss, tp_distillation_loss
 
 
@@ -77,6 +77,7 @@ class StepArgs:
     temp_end: float = 0.01
     max_steps: int = 50
     ce_reduction: str = "valid"  # plain path: mean CE over non-ignored tokens
+    ptqr: bool = False  # per-token quant routing forward (reference --ptqr, trainer.py:1523,1612-1616)
 
 
 class GatedDistillTrainer:
@@ -94,6 +95,7 @@ class GatedDistillTrainer:
             layer.gates.requires_grad = True
         self.trainable = [layer.gates for layer in replaced.values()]
         self.bank = GateBank(replaced)  # every layer's softmax(g / tau) in one batched op per step
+        set_ptqr(args.ptqr)
         self.optimizer = torch.optim.AdamW(self.trainable, lr=args.lr, betas=(0.9, 0.95))
         self.scheduler = torch.optim.lr_scheduler.CosineAnnealingLR(self.optimizer, T_max=args.max_steps,
                                                                     eta_min=1e-3)
