@@ -94,6 +94,16 @@ int vq_gategrad(const void* dy, int64_t lddy, const void* x, int64_t ldx, int64_
                 const int* types, const void* const* blocks, int64_t padded_cols, void* workspace,
                 size_t workspace_bytes, float* grad_probs, void* stream);
 
+/* K1 for the per-token routed (PTQR) forward: rows of x are grouped by
+ * candidate, rows [group_off[g], group_off[g + 1]) use weight w[g] (w a HOST
+ * array of G <= 8 device pointers to bf16 [N, ldw]; group_off a DEVICE int
+ * array of G + 1 ascending offsets from 0 to T).  The kernel reads the
+ * offsets itself, so the caller needs no host copy of the group sizes.
+ * T > 128.  Replaces the per-candidate matmuls of _RoutedMixedLinear.forward,
+ * voodoo_quant/layers.py:384-401. */
+int vq_linear_fwd_grouped(const void* x, int64_t T, int64_t Kin, int64_t ldx, int G, const void* const* w,
+                          int64_t N, int64_t ldw, const int* group_off, void* y, int64_t ldy, void* stream);
+
 /* K1 with the row-parallel all-reduce fused in: adds this rank's
  * Y = X W^T [T, N] (bf16) into `y_multicast`, an NVLink multicast (NVSwitch
  * SHARP) address of a buffer every TP rank holds, with multimem.red from the

@@ -85,7 +85,19 @@ struct Params {
   // follow the per-tile ones (sk_base), 16 per cluster.
   int stream_k;
   int sk_base;
+  // grouped forward (paired kernel): rows [group_off[g], group_off[g + 1])
+  // of A are multiplied with B_g; ngroups = 0 for a plain GEMM
+  const int* group_off;
+  int ngroups;
   int* err;
+};
+
+constexpr int kMaxGroups = 8;
+
+// B-operand tensor maps of a paired launch: one, or one per group.
+template <int G>
+struct BMaps {
+  CUtensorMap m[G];
 };
 
 // One unit of work of a persistent cluster: k-blocks [kb0, kb1) of a tile.
@@ -95,11 +107,11 @@ struct Seg {
 };
 
 // Segment i of cluster c out of C (the same sequence for every role).
-__device__ __forceinline__ bool get_seg(const Params& p, int c, int C, int i, Seg& sg) {
+__device__ __forceinline__ bool get_seg(const Params& p, int ntiles, int c, int C, int i, Seg& sg) {
   if (!p.stream_k) {
     const int tile = c + i * C;
     sg = {tile, 0, p.num_k_blk, -1};
-    return tile < p.num_tiles;
+    return tile < ntiles;
   }
   const int full = p.num_tiles / C;
   if (i < full) {
@@ -243,9 +255,10 @@ __device__ __forceinline__ float row_dot(const uint32_t* slot, uint32_t t_row, l
 //   gate-gradient staging area (4 warps x 32 rows x kStagePitch words).
 template <int kEpi>
 __device__ __forceinline__ void epilogue_tile(const Params& p, uint8_t* stage, uint32_t t_row, long long row0,
-                                              int m128, int n_blk, int wq, int lane, long long slot_override = -1) {
+                                              int m128, int n_blk, int wq, int lane, long long slot_override = -1,
+                                              long long row_end = -1) {
   const long long row = row0 + lane;
-  const bool row_ok = row < p.M;
+  const bool row_ok = row >= 0 && row < (row_end >= 0 ? row_end : static_cast<long long>(p.M));
   if (kEpi == kEpiStoreBf16) {
     for (int c = 0; c < BN / 32; ++c) {
       float v[32];
@@ -498,15 +511,27 @@ struct PairSmemLayout {
   static constexpr int b_off = a_off + PSTAGES * PA_STAGE;
   static constexpr int bar_off = b_off + PSTAGES * PB_STAGE;
   static constexpr int n_bars = 2 * PSTAGES + 4;
-  static constexpr int misc_off = bar_off + n_bars * 8;
-  static constexpr int stage_off = misc_off + 16;
+  static constexpr int misc_off = bar_off + n_bars * 8;  // tmem base, abort flag, group m-tile prefix
+  static constexpr int grp_off = misc_off + 16;
+  static constexpr int stage_off = misc_off + 64;
   static constexpr int stage_bytes = (kEpi == 1) ? 4 * 32 * kStagePitch * 4 : 0;
   static constexpr int total = stage_off + stage_bytes;
 };
 
-template <bool kAmn, bool kBmn, int kEpi>
+// Grouped tile -> (group, first output row of the 256-row tile, column block),
+// row-major within a group; mt[g] is the prefix of the groups' 256-row tiles.
+__device__ __forceinline__ void group_tile(const Params& p, const int* mt, int tile, int& g, int& row_base,
+                                           int& n_blk) {
+  g = 0;
+  while (g + 1 < p.ngroups && tile >= mt[g + 1] * p.num_n_blk) ++g;
+  const int local = tile - mt[g] * p.num_n_blk;
+  n_blk = local % p.num_n_blk;
+  row_base = __ldg(p.group_off + g) + (local / p.num_n_blk) * 256;
+}
+
+template <bool kAmn, bool kBmn, int kEpi, int G = 1>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
-    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Params p) {
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ BMaps<G> tmB, Params p) {
   using SL = PairSmemLayout<kEpi>;
   extern __shared__ __align__(1024) uint8_t smem[];
   const uint32_t sbase = smem_u32(smem);
@@ -536,11 +561,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       mbar_init(tempty_bar(a), 8);  // 4 epilogue warps x 2 CTAs (used in the even CTA)
     }
     *abort_flag = 0;
+    if (G > 1) {  // 256-row tiles per group, from the device-side group offsets
+      int* mt = reinterpret_cast<int*>(smem + SL::grp_off);
+      mt[0] = 0;
+      for (int g = 0; g < p.ngroups; ++g) {  // group sizes clamped to [0, M]: at most M/256 + G tiles
+        int rows = __ldg(p.group_off + g + 1) - __ldg(p.group_off + g);
+        rows = rows < 0 ? 0 : (rows > p.M ? p.M : rows);
+        mt[g + 1] = mt[g] + (rows + 255) / 256;
+      }
+    }
     fence_barrier_init();
   }
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmA);
-    tma_prefetch_desc(&tmB);
+    for (int g = 0; g < (G > 1 ? p.ngroups : 1); ++g) tma_prefetch_desc(&tmB.m[g]);
   }
   if (warp == 2) {
     tmem_alloc_pair(smem_u32(tmem_holder), TMEM_COLS);
@@ -550,6 +584,23 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
   cluster_sync();  // barriers of both CTAs initialised, TMEM allocated
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
+  const int* mt = reinterpret_cast<const int*>(smem + SL::grp_off);
+  const int ntiles = G > 1 ? mt[p.ngroups] * p.num_n_blk : p.num_tiles;
+  // tile -> (B map, first output row of the 256-row tile, column block, end of its rows)
+  auto coords = [&](int tile, const CUtensorMap*& bmap, int& row_base, int& n_blk, int& row_end, int& m_blk) {
+    if (G > 1) {
+      int g;
+      group_tile(p, mt, tile, g, row_base, n_blk);
+      bmap = &tmB.m[g];
+      row_end = min(__ldg(p.group_off + g + 1), p.M);  // rows outside the group or the output are not stored
+      m_blk = 0;
+    } else {
+      tile_coords(p, tile, m_blk, n_blk);
+      bmap = &tmB.m[0];
+      row_base = m_blk * 256;
+      row_end = p.M;
+    }
+  };
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer (both CTAs)
@@ -557,10 +608,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       uint32_t it = 0;
       bool alive = true;
       Seg sg;
-      for (int si = 0; alive && get_seg(p, cluster_id, num_clusters, si, sg); ++si) {
-        int m_blk, n_blk;
-        tile_coords(p, sg.tile, m_blk, n_blk);
-        const int m0 = m_blk * 256 + 128 * static_cast<int>(rank);
+      for (int si = 0; alive && get_seg(p, ntiles, cluster_id, num_clusters, si, sg); ++si) {
+        int m_blk, n_blk, row_base, row_end;
+        const CUtensorMap* bmap;
+        coords(sg.tile, bmap, row_base, n_blk, row_end, m_blk);
+        const int m0 = row_base + 128 * static_cast<int>(rank);
         const int n0 = n_blk * BN + 128 * static_cast<int>(rank);
         for (int kb = sg.kb0; kb < sg.kb1; ++kb, ++it) {
           const int s = it % PSTAGES;
@@ -583,9 +635,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
           }
           if (kBmn) {
 #pragma unroll
-            for (int j = 0; j < 2; ++j) tma_load_2d_pair(b_dst + j * (64 * BK * 2), &tmB, fb, n0 + 64 * j, k0);
+            for (int j = 0; j < 2; ++j) tma_load_2d_pair(b_dst + j * (64 * BK * 2), bmap, fb, n0 + 64 * j, k0);
           } else {
-            tma_load_2d_pair(b_dst, &tmB, fb, k0, n0);
+            tma_load_2d_pair(b_dst, bmap, fb, k0, n0);
           }
         }
       }
@@ -597,7 +649,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       uint32_t it = 0, local = 0;
       bool alive = true;
       Seg sg;
-      for (int si = 0; alive && get_seg(p, cluster_id, num_clusters, si, sg); ++si, ++local) {
+      for (int si = 0; alive && get_seg(p, ntiles, cluster_id, num_clusters, si, sg); ++si, ++local) {
         const int acc = local & 1;
         const uint32_t aph = (local >> 1) & 1u;
         if (!mbar_wait(tempty_bar(acc), aph ^ 1u, abort_flag)) {
@@ -639,9 +691,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     uint32_t local = 0;
     bool sk_written[2] = {false, false};
     Seg sg;
-    for (int si = 0; get_seg(p, cluster_id, num_clusters, si, sg); ++si, ++local) {
-      int m_blk, n_blk;
-      tile_coords(p, sg.tile, m_blk, n_blk);
+    for (int si = 0; get_seg(p, ntiles, cluster_id, num_clusters, si, sg); ++si, ++local) {
+      int m_blk, n_blk, row_base, row_end;
+      const CUtensorMap* bmap;
+      coords(sg.tile, bmap, row_base, n_blk, row_end, m_blk);
       const int acc = local & 1;
       const uint32_t aph = (local >> 1) & 1u;
       if (!mbar_wait(tfull_bar(acc), aph, abort_flag)) {
@@ -656,8 +709,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
         slot = p.sk_base + ((static_cast<long long>(cluster_id) * 2 + sg.piece) * 2 + rank) * 4 + wq;
         sk_written[sg.piece] = true;
       }
-      epilogue_tile<kEpi>(p, smem + SL::stage_off, t_row, static_cast<long long>(m128) * 128 + 32 * wq, m128,
-                          n_blk, wq, lane, slot);
+      epilogue_tile<kEpi>(p, smem + SL::stage_off, t_row, static_cast<long long>(row_base) + 128 * rank + 32 * wq,
+                          m128, n_blk, wq, lane, slot, row_end);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(acc ? tempty_leader1 : tempty_leader0);

@@ -177,7 +177,9 @@ int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, vq::gemm::Params p
       p.sk_base = static_cast<int>(gategrad_tile_slots(p.M, p.N));
       if (used_slots != nullptr) *used_slots += 16LL * clusters;
     }
-    kern<<<2 * clusters, THREADS, smem, st>>>(ta, tb, p);
+    BMaps<1> bm;
+    bm.m[0] = tb;
+    kern<<<2 * clusters, THREADS, smem, st>>>(ta, bm, p);
   } else {
     auto kern = gemm_kernel<kAmn, kBmn, kEpi>;
     constexpr int smem = SmemLayout<kEpi>::total;
@@ -390,6 +392,49 @@ int vq_linear_fwd_mcred(const void* x, int64_t T, int64_t Kin, int64_t ldx, cons
   p.ldc = ldy;
   if (int rc = device_error_ptr(&p.err)) return rc;
   return launch_gemm<false, false, vq::gemm::kEpiMultimemRed>(ta, tb, p, st);
+}
+
+int vq_linear_fwd_grouped(const void* x, int64_t T, int64_t Kin, int64_t ldx, int G, const void* const* w,
+                          int64_t N, int64_t ldw, const int* group_off, void* y, int64_t ldy, void* stream) {
+  DeviceScope scope(y);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (G < 1 || G > vq::gemm::kMaxGroups) return fail(VQ_ERR_INVALID, "groups %d not in [1, %d]", G, vq::gemm::kMaxGroups);
+  if (w == nullptr || group_off == nullptr) return fail(VQ_ERR_INVALID, "null weight array or group offsets");
+  if (int rc = check_matrix(x, T, Kin, ldx, "x")) return rc;
+  if (int rc = check_matrix(y, T, N, ldy, "y")) return rc;
+  for (int g = 0; g < G; ++g)
+    if (int rc = check_matrix(w[g], N, Kin, ldw, "w")) return rc;
+  if (T == 0 || N == 0) return 0;
+  if (Kin == 0) return zero_rows(y, T, N, ldy, 2, st);
+  if (T > 0x7fffffff || N > 0x7fffffff || Kin > 0x7fffffff) return fail(VQ_ERR_INVALID, "dimension too large");
+  if (!use_pair(T)) return fail(VQ_ERR_INVALID, "grouped GEMM needs more than %d rows", vq::gemm::BM);
+  CUtensorMap ta;
+  vq::gemm::BMaps<vq::gemm::kMaxGroups> bm;
+  if (int rc = make_map(&ta, x, T, Kin, ldx, vq::gemm::BM)) return rc;
+  for (int g = 0; g < G; ++g)
+    if (int rc = make_map(&bm.m[g], w[g], N, Kin, ldw, 128)) return rc;
+  vq::gemm::Params p{};
+  p.M = static_cast<int>(T);
+  p.N = static_cast<int>(N);
+  p.K = static_cast<int>(Kin);
+  p.C = static_cast<__nv_bfloat16*>(y);
+  p.ldc = ldy;
+  p.group_off = group_off;
+  p.ngroups = G;
+  p.num_n_blk = static_cast<int>((N + vq::gemm::BN - 1) / vq::gemm::BN);
+  p.num_k_blk = static_cast<int>((Kin + vq::gemm::BK - 1) / vq::gemm::BK);
+  p.num_m_blk = static_cast<int>((T + 255) / 256) + G;  // upper bound on the groups' 256-row tiles
+  p.num_tiles = p.num_m_blk * p.num_n_blk;              // the kernel counts the exact tiles itself
+  if (int rc = device_error_ptr(&p.err)) return rc;
+  int sms = 0;
+  if (int rc = sm_count(&sms)) return rc;
+  auto kern = vq::gemm::gemm_pair_kernel<false, false, vq::gemm::kEpiStoreBf16, vq::gemm::kMaxGroups>;
+  constexpr int smem = vq::gemm::PairSmemLayout<vq::gemm::kEpiStoreBf16>::total;
+  VQ_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  const int clusters = p.num_tiles < sms / 2 ? p.num_tiles : sms / 2;
+  kern<<<2 * clusters, vq::gemm::THREADS, smem, st>>>(ta, bm, p);
+  VQ_CUDA(cudaGetLastError());
+  return 0;
 }
 
 size_t vq_gategrad_workspace_bytes(int64_t N, int64_t Kin, int K) {

@@ -44,6 +44,7 @@ def _declare(lib):
         "vq_dequant": (_int, [_int, _vp, _i64, _i64, _vp, _vp]),
         "vq_mix": (_int, [_int, _vp, _vp, _vp, _i64, _i64, _i64, _vp, _i64, _vp]),
         "vq_linear_fwd": (_int, [_vp, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _vp]),
+        "vq_linear_fwd_grouped": (_int, [_vp, _i64, _i64, _i64, _int, _vp, _i64, _i64, _vp, _vp, _i64, _vp]),
         "vq_linear_fwd_mcred": (_int, [_vp, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _vp]),
         "vq_linear_dx": (_int, [_vp, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _vp]),
         "vq_gategrad_workspace_bytes": (ctypes.c_size_t, [_i64, _i64, _int]),
@@ -73,7 +74,7 @@ def _declare(lib):
 
 EXPORTED = (
     "vq_last_error", "vq_abi_version", "vq_format_info", "vq_device_error", "vq_dequant", "vq_mix",
-    "vq_linear_fwd", "vq_linear_fwd_mcred", "vq_linear_dx", "vq_gategrad_workspace_bytes", "vq_gategrad", "vq_gategrad_noalloc",
+    "vq_linear_fwd", "vq_linear_fwd_grouped", "vq_linear_fwd_mcred", "vq_linear_dx", "vq_gategrad_workspace_bytes", "vq_gategrad", "vq_gategrad_noalloc",
     "vq_mixgemm_fwd",
     "vq_loss_fused", "vq_loss_stats", "vq_loss_combine", "vq_loss_grad",
     "vq_rmsnorm_fwd", "vq_rmsnorm_bwd", "vq_rope", "vq_swiglu_fwd", "vq_swiglu_bwd",
@@ -201,6 +202,21 @@ def linear_fwd(x: torch.Tensor, w: torch.Tensor, n_out: int | None = None, in_fe
         out = torch.empty(x.shape[0], N, dtype=torch.bfloat16, device=x.device)
     _check(_lib.vq_linear_fwd(x.data_ptr(), x.shape[0], kin, x.stride(0), w.data_ptr(), N, w.stride(0),
                               out.data_ptr(), out.stride(0), _stream(x)))
+    return out
+
+
+def linear_fwd_grouped(x: torch.Tensor, ws: list, n_out: int, in_features: int, group_off: torch.Tensor,
+                       out: torch.Tensor | None = None) -> torch.Tensor:
+    """y[rows of group g] = x[rows of group g] ws[g]^T; group_off (int32, device, G + 1) need not be on the host."""
+    _require_cuda(x, *ws)
+    x = _as_operand(x)
+    G = len(ws)
+    ptrs = (_vp * G)(*[w.data_ptr() for w in ws])
+    if out is None:
+        out = torch.empty(x.shape[0], n_out, dtype=torch.bfloat16, device=x.device)
+    go = group_off.to(torch.int32).contiguous()
+    _check(_lib.vq_linear_fwd_grouped(x.data_ptr(), x.shape[0], in_features, x.stride(0), G, ptrs, n_out,
+                                      ws[0].stride(0), go.data_ptr(), out.data_ptr(), out.stride(0), _stream(x)))
     return out
 
 

@@ -195,10 +195,11 @@ class _RoutedGatedLinearFunction(Function):
     """PTQR forward y[t] = x[t] W_{k(t)}^T, one candidate per token (reference
     _RoutedMixedLinear, voodoo_quant/layers.py:366-428).
 
-    Tokens are grouped by candidate (a stable sort of the routing), each
-    group runs one tcgen05 GEMM against its candidate's bf16 decode (the
-    mixture kernel with a one-hot probability), and rows are scattered back;
-    the GEMM FLOPs equal one dense forward.  Backward is the mixture's
+    Tokens are grouped by candidate (a stable sort of the routing) and one
+    grouped tcgen05 GEMM multiplies each group with its candidate's bf16
+    decode (the mixture kernel with a one-hot probability), reading the group
+    offsets on the device; rows are scattered back.  The GEMM FLOPs equal
+    one dense forward.  Backward is the mixture's
     straight-through Jacobian: dX = dY W_mix, d p_k = <dY^T X, W_k>.
     """
 
@@ -208,20 +209,29 @@ class _RoutedGatedLinearFunction(Function):
         x2 = _C._as_operand(x.reshape(-1, in_f))
         T = x2.shape[0]
         routing = routing.to(x2.device).reshape(-1)
-        order = torch.argsort(routing, stable=True)
-        counts = torch.bincount(routing, minlength=layer.num_candidates).tolist()
+        # 8-bit keys: one radix pass; the inverse permutation turns the
+        # scatter back into a (vectorised) row gather
+        order = torch.argsort(routing.to(torch.uint8), stable=True)
+        inv = torch.empty_like(order)
+        inv[order] = torch.arange(T, device=x2.device)
         xs = x2.index_select(0, order)
-        ys = torch.empty(T, out_f, dtype=torch.bfloat16, device=x2.device)
         one = torch.ones(1, dtype=torch.float32, device=x2.device)
         blocks = layer._candidate_blocks()
-        off = 0
-        for k, n in enumerate(counts):
-            if n == 0:
-                continue
-            w_k = _C.mix([layer.candidate_types[k]], [blocks[k]], one, out_f, layer.padded_in_features, in_f)
-            _C.linear_fwd(xs[off:off + n], w_k, out_f, in_f, out=ys[off:off + n])
-            off += n
-        y = torch.empty_like(ys).index_copy_(0, order, ys)
+        ws = [_C.mix([qt], [blocks[k]], one, out_f, layer.padded_in_features, in_f)
+              for k, qt in enumerate(layer.candidate_types)]
+        counts = torch.bincount(routing, minlength=layer.num_candidates)
+        if T > 128:  # one grouped GEMM; the group sizes stay on the device
+            group_off = torch.zeros(layer.num_candidates + 1, dtype=torch.int32, device=x2.device)
+            group_off[1:] = torch.cumsum(counts, 0)
+            ys = _C.linear_fwd_grouped(xs, ws, out_f, in_f, group_off)
+        else:
+            ys = torch.empty(T, out_f, dtype=torch.bfloat16, device=x2.device)
+            off = 0
+            for k, n in enumerate(counts.tolist()):
+                if n:
+                    _C.linear_fwd(xs[off:off + n], ws[k], out_f, in_f, out=ys[off:off + n])
+                    off += n
+        y = ys.index_select(0, inv)
         ctx.layer = layer
         ctx.x_shape = x.shape
         ctx.x_dtype = x.dtype
