@@ -228,6 +228,50 @@ def run_gpu(args):
     torch.cuda.synchronize()
     barrier()
 
+    # The timed steps replay one CUDA graph of the step (forward, backward and
+    # the TP collectives), so host launch overhead stays out of the GPU
+    # timeline; every rank uses the graph only if every rank captured it.
+    graph, graph_note = None, "off"
+    if not args.no_graph:
+        try:
+            side = torch.cuda.Stream(dev)
+            side.wait_stream(stream)
+            with torch.cuda.stream(side):
+                for _ in range(2):
+                    x.grad = None
+                    step(x, dy)
+            stream.wait_stream(side)
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            x.grad = None
+            with torch.cuda.graph(g):
+                step(x, dy)
+            graph, graph_note = g, "cuda graph of the step"
+            del g
+        except Exception as e:  # capture unsupported here: time the eager step
+            graph, graph_note = None, f"eager (capture failed: {type(e).__name__})"
+        ok = torch.tensor([1.0 if graph is not None else 0.0], device=dev)
+        if world > 1:
+            dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+        if ok.item() < 1.0:
+            graph = None
+            if graph_note.startswith("cuda graph"):
+                graph_note = "eager (another rank could not capture)"
+        torch.cuda.synchronize()
+        barrier()
+
+    def timed_step():
+        if graph is not None:
+            graph.replay()
+        else:
+            x.grad = None
+            step(x, dy)
+
+    for _ in range(args.warmup):
+        timed_step()
+    torch.cuda.synchronize()
+    barrier()
+
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     clk = ClockSampler(local).start()
     barrier()
@@ -235,8 +279,7 @@ def run_gpu(args):
     clk.mark_start()
     ev0.record(stream)
     for _ in range(args.steps):
-        x.grad = None
-        step(x, dy)
+        timed_step()
     ev1.record(stream)
     torch.cuda.synchronize()
     clk.mark_end()
@@ -348,7 +391,7 @@ def run_gpu(args):
             "vs_baseline": None,
             "dtype": "bf16",
             "data": "synthetic (seeded; candidates from the round-to-nearest GGUF packer)",
-            "config": config(world),
+            "config": config(world, {"timed_step": graph_note}),
             "roofline": {
                 "bound": "tensor",
                 "kernel": f"gemm_{dom}",
@@ -375,6 +418,8 @@ def run_gpu(args):
         if world == 1 and not args.no_cpu_baseline:
             out["cpu_baseline"] = cpu_baseline(args.cpu_tokens, repeats=1)
         print(json.dumps(out), flush=True)
+    graph = None  # the captured graph holds NCCL work: release it before the process group
+    torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -685,6 +730,7 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--cpu-tokens", type=int, default=2048)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-graph", action="store_true", help="time the eager step instead of a CUDA graph of it")
     ap.add_argument("--ptqr", action="store_true",
                     help="full-step workloads: per-token quant routing forward (one candidate per token)")
     ap.add_argument("--multicast", action="store_true",
