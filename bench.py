@@ -195,6 +195,8 @@ def run_gpu(args):
         from datetime import timedelta
         from voodoo_quant import parallel
 
+        if args.overlap_sms > 0:  # NCCL's CTAs must fit on the SMs the gate-gradient GEMM leaves free
+            os.environ.setdefault("NCCL_MAX_NCHANNELS", str(args.overlap_sms))
         dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=300))
         parallel.adopt_process_group(local)
     from voodoo_quant import _C
@@ -208,6 +210,10 @@ def run_gpu(args):
 
     if world > 1:
         layer.reduce_input_grad = True  # dX all-reduce overlapped with the gate-gradient GEMM
+        if args.overlap_sms > 0:
+            import voodoo_quant.layers as _layers
+
+            _layers.GATEGRAD_SM_RESERVE = args.overlap_sms
 
     def step(xin, dyin):
         xg = xin.requires_grad_(True) if not xin.requires_grad else xin
@@ -391,7 +397,8 @@ def run_gpu(args):
             "vs_baseline": None,
             "dtype": "bf16",
             "data": "synthetic (seeded; candidates from the round-to-nearest GGUF packer)",
-            "config": config(world, {"timed_step": graph_note}),
+            "config": config(world, {"timed_step": graph_note,
+                                     "dx_allreduce_overlap_sms": args.overlap_sms if world > 1 else 0}),
             "roofline": {
                 "bound": "tensor",
                 "kernel": f"gemm_{dom}",
@@ -731,6 +738,9 @@ def main():
     ap.add_argument("--cpu-tokens", type=int, default=2048)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true", help="time the eager step instead of a CUDA graph of it")
+    ap.add_argument("--overlap-sms", type=int, default=-1,
+                    help="TP: SMs the gate-gradient GEMM leaves to the concurrent dX all-reduce, which also caps "
+                         "NCCL's channels (default: 24 with more than one GPU, 0 otherwise; 24 measured best at TP-2)")
     ap.add_argument("--ptqr", action="store_true",
                     help="full-step workloads: per-token quant routing forward (one candidate per token)")
     ap.add_argument("--multicast", action="store_true",
@@ -739,6 +749,8 @@ def main():
                     help="full-step workloads: print device time per kernel name for one step")
     ap.add_argument("--ncu-case", action="store_true", help="one launch per kernel at profiling sizes")
     args = ap.parse_args()
+    if args.overlap_sms < 0:
+        args.overlap_sms = 24 if int(os.environ.get("WORLD_SIZE", "1")) > 1 else 0
     if args.ncu_case:
         run_ncu_case()
     elif args.impl == "reference":

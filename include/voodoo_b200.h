@@ -94,6 +94,15 @@ int vq_gategrad(const void* dy, int64_t lddy, const void* x, int64_t ldx, int64_
                 const int* types, const void* const* blocks, int64_t padded_cols, void* workspace,
                 size_t workspace_bytes, float* grad_probs, void* stream);
 
+/* Number of SMs later vq_gategrad / vq_gategrad_noalloc launches leave free
+ * (process-wide; 0 = use every SM).  A caller that has a collective in flight
+ * on another stream while the gate-gradient GEMM runs (the TP input-gradient
+ * all-reduce) reserves the SMs the collective's kernel needs, so the two
+ * actually run concurrently: the persistent GEMM otherwise occupies every SM
+ * and the collective waits for it.  No counterpart in the reference (its
+ * all-reduces are synchronous). */
+int vq_set_gategrad_sm_reserve(int sms);
+
 /* K1 for the per-token routed (PTQR) forward: rows of x are grouped by
  * candidate, rows [group_off[g], group_off[g + 1]) use weight w[g] (w a HOST
  * array of G <= 8 device pointers to bf16 [N, ldw]; group_off a DEVICE int

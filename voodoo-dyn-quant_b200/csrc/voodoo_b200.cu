@@ -144,6 +144,10 @@ inline bool use_pair(long long M) { return M > vq::gemm::BM; }
 // the gate-gradient workspace are sized for it).
 constexpr int kMaxClusters = 128;
 
+// SMs the gate-gradient GEMM leaves free (vq_set_gategrad_sm_reserve), for a
+// collective that runs concurrently on another stream.
+int g_gategrad_sm_reserve = 0;
+
 // Gate-gradient partial slots the per-tile schedule writes.
 inline long long gategrad_tile_slots(long long N, long long Kin) {
   const long long m128 = use_pair(N) ? 2 * ((N + 255) / 256) : (N + vq::gemm::BM - 1) / vq::gemm::BM;
@@ -169,7 +173,9 @@ int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, vq::gemm::Params p
     auto kern = gemm_pair_kernel<kAmn, kBmn, kEpi>;
     constexpr int smem = PairSmemLayout<kEpi>::total;
     VQ_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    int clusters = p.num_tiles < sms / 2 ? p.num_tiles : sms / 2;
+    int avail = sms;
+    if (kEpi == kEpiGateGrad && g_gategrad_sm_reserve > 0 && g_gategrad_sm_reserve < sms - 2) avail -= g_gategrad_sm_reserve;
+    int clusters = p.num_tiles < avail / 2 ? p.num_tiles : avail / 2;
     if (clusters > kMaxClusters) clusters = kMaxClusters;
     if (kEpi == kEpiGateGrad && p.num_tiles % clusters != 0 && p.num_tiles > clusters) {
       // split the last, partial wave of tiles along K across every cluster
@@ -434,6 +440,12 @@ int vq_linear_fwd_grouped(const void* x, int64_t T, int64_t Kin, int64_t ldx, in
   const int clusters = p.num_tiles < sms / 2 ? p.num_tiles : sms / 2;
   kern<<<2 * clusters, vq::gemm::THREADS, smem, st>>>(ta, bm, p);
   VQ_CUDA(cudaGetLastError());
+  return 0;
+}
+
+int vq_set_gategrad_sm_reserve(int sms) {
+  if (sms < 0) return fail(VQ_ERR_INVALID, "negative SM count");
+  g_gategrad_sm_reserve = sms;
   return 0;
 }
 

@@ -44,6 +44,7 @@ def _declare(lib):
         "vq_dequant": (_int, [_int, _vp, _i64, _i64, _vp, _vp]),
         "vq_mix": (_int, [_int, _vp, _vp, _vp, _i64, _i64, _i64, _vp, _i64, _vp]),
         "vq_linear_fwd": (_int, [_vp, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _vp]),
+        "vq_set_gategrad_sm_reserve": (_int, [_int]),
         "vq_linear_fwd_grouped": (_int, [_vp, _i64, _i64, _i64, _int, _vp, _i64, _i64, _vp, _vp, _i64, _vp]),
         "vq_linear_fwd_mcred": (_int, [_vp, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _vp]),
         "vq_linear_dx": (_int, [_vp, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _vp]),
@@ -74,7 +75,7 @@ def _declare(lib):
 
 EXPORTED = (
     "vq_last_error", "vq_abi_version", "vq_format_info", "vq_device_error", "vq_dequant", "vq_mix",
-    "vq_linear_fwd", "vq_linear_fwd_grouped", "vq_linear_fwd_mcred", "vq_linear_dx", "vq_gategrad_workspace_bytes", "vq_gategrad", "vq_gategrad_noalloc",
+    "vq_linear_fwd", "vq_linear_fwd_grouped", "vq_set_gategrad_sm_reserve", "vq_linear_fwd_mcred", "vq_linear_dx", "vq_gategrad_workspace_bytes", "vq_gategrad", "vq_gategrad_noalloc",
     "vq_mixgemm_fwd",
     "vq_loss_fused", "vq_loss_stats", "vq_loss_combine", "vq_loss_grad",
     "vq_rmsnorm_fwd", "vq_rmsnorm_bwd", "vq_rope", "vq_swiglu_fwd", "vq_swiglu_bwd",
@@ -238,6 +239,11 @@ def linear_dx(dy: torch.Tensor, w: torch.Tensor, in_features: int, out: torch.Te
     _check(_lib.vq_linear_dx(dy.data_ptr(), dy.shape[0], N, dy.stride(0), w.data_ptr(), in_features, w.stride(0),
                              out.data_ptr(), out.stride(0), _stream(dy)))
     return out
+
+
+def set_gategrad_sm_reserve(sms: int) -> None:
+    """SMs later gate-gradient GEMMs leave free for a concurrent collective (0 = none)."""
+    _check(load_library().vq_set_gategrad_sm_reserve(int(sms)))
 
 
 def gategrad(dy: torch.Tensor, x: torch.Tensor, qtypes, qbytes, n_out: int, in_features: int, padded_cols: int,

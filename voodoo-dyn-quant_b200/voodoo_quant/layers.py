@@ -45,6 +45,11 @@ _CANDIDATE_CACHE_ROOT = CANDIDATE_CACHE_DIR
 # layer).  False recomputes it in the backward (one more HBM-bound mix pass).
 KEEP_MIXED_WEIGHT = True
 
+# SMs the gate-gradient GEMM leaves free while the layer's input-gradient
+# all-reduce (reduce_input_grad under TP) is in flight, so that the two run
+# concurrently; match it to the collective's CTA count (NCCL channels).
+GATEGRAD_SM_RESERVE = 0
+
 
 # --------------------------------------------------------------------------- per-token quant routing
 class _PTQRState:
@@ -181,9 +186,15 @@ def _gated_linear_backward(ctx, dy: torch.Tensor):
             pending = tp_all_reduce_async(dx)
     ctx.w_mix = None
     if ctx.needs_input_grad[1]:
+        from voodoo_quant.parallel import TP
+        reserve = pending is not None and TP.enabled and GATEGRAD_SM_RESERVE > 0
+        if reserve:  # leave SMs to the all-reduce in flight so that it overlaps the GEMM
+            _C.set_gategrad_sm_reserve(GATEGRAD_SM_RESERVE)
         dprobs = _C.gategrad(dy2, x2, layer.candidate_types, layer._candidate_blocks(), layer.out_features,
                              layer.in_features, layer.padded_in_features,
                              workspace=layer._gategrad_workspace(x2.device)).to(probs.dtype)
+        if reserve:
+            _C.set_gategrad_sm_reserve(0)
     if pending is not None:
         pending.wait()
     if dx is not None:
