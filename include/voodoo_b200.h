@@ -94,6 +94,13 @@ int vq_gategrad(const void* dy, int64_t lddy, const void* x, int64_t ldx, int64_
                 const int* types, const void* const* blocks, int64_t padded_cols, void* workspace,
                 size_t workspace_bytes, float* grad_probs, void* stream);
 
+/* PTQR grouping in one launch: the stable counting sort of T routing keys
+ * (uint8, values in [0, K), K <= 8): order[p] = i and inv[i] = p (int64) for
+ * the element i placed at position p, group_off[K + 1] (int32) the first
+ * position of each candidate's group.  Replaces the per-candidate nonzero
+ * selections of _RoutedMixedLinear.forward, voodoo_quant/layers.py:390-396. */
+int vq_route_prep(const void* keys, int64_t T, int K, int64_t* order, int64_t* inv, int* group_off, void* stream);
+
 /* Number of SMs later vq_gategrad / vq_gategrad_noalloc launches leave free
  * (process-wide; 0 = use every SM).  A caller that has a collective in flight
  * on another stream while the gate-gradient GEMM runs (the TP input-gradient

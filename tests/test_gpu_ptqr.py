@@ -118,3 +118,43 @@ def test_grouped_gemm_matches_per_group_gemms(cuda, sizes):
             else:
                 assert rel_err(y[a:b].float().cpu().numpy(), ref.float().cpu().numpy()) < 1e-2
     assert _C.device_error() == 0
+
+
+@pytest.mark.parametrize("T,K", [(1, 4), (1000, 3), (16384, 6), (70001, 8)])
+def test_route_prep_is_a_stable_grouping(cuda, T, K):
+    from voodoo_quant import _C
+
+    g = torch.Generator(device="cpu").manual_seed(T + K)
+    keys = torch.randint(0, K, (T,), generator=g, dtype=torch.int64)
+    keys[: T // 3] = K - 1  # a skewed group
+    order, inv, off = _C.route_prep(keys.to(cuda), K)
+    ref = torch.argsort(keys, stable=True)
+    assert torch.equal(order.cpu(), ref)
+    assert torch.equal(inv.cpu()[ref], torch.arange(T))
+    counts = torch.bincount(keys, minlength=K)
+    assert torch.equal(off.cpu().long(), torch.cat([torch.zeros(1, dtype=torch.long), counts.cumsum(0)]))
+
+
+def test_bank_routing_never_picks_padding(cuda):
+    """Batched per-step routing for layers with different candidate counts:
+    only valid candidates, and shares that follow each layer's probabilities."""
+    from voodoo_quant.layers import GateBank, MixedQuantLinear
+    from voodoo_quant.quants import rtn
+
+    mods = {}
+    for i, types in enumerate([("Q4_K", "Q8_0"), ("Q3_K", "Q4_K", "Q5_K", "Q6_K", "Q8_0")]):
+        w = torch.randn(16, 256) * 0.02
+        m = MixedQuantLinear(256, 16, list(types), w.to(cuda), candidate_bytes={q: rtn.quantize(w, q) for q in types},
+                             tensor_name=f"bank.route.{i}")
+        with torch.no_grad():
+            m.gates.copy_(torch.linspace(-1, 1, len(types)))
+        mods[f"l{i}"] = m
+    bank = GateBank(mods)
+    bank.probs()
+    torch.manual_seed(0)
+    for m in mods.values():
+        r = bank.routing(m, 200000).long()
+        assert int(r.max()) < m.num_candidates
+        shares = torch.bincount(r, minlength=m.num_candidates).double().cpu() / r.numel()
+        assert torch.allclose(shares, m.get_probs().double().cpu(), atol=6e-3)
+    bank.release()

@@ -238,3 +238,82 @@ __global__ void __launch_bounds__(kEltThreads) swiglu_kernel(const __nv_bfloat16
 
 }  // namespace blocks
 }  // namespace vq
+
+namespace vq {
+namespace route {
+
+constexpr int kThreads = 1024;
+constexpr int kMaxKeys = 8;
+
+// Stable counting sort of T keys in [0, K) by one CTA: order[pos] = i and
+// inv[i] = pos for the element i that lands at position pos, group_off[k] =
+// first position of key k (group_off[K] = T).  Keys >= K go to the last group.
+// Thread t owns elements [t*E, (t+1)*E), so the per-thread counts, scanned
+// over the threads, give every element its stable position.
+__global__ void __launch_bounds__(kThreads) route_prep_kernel(const uint8_t* __restrict__ keys, long long T, int K,
+                                                              long long* __restrict__ order, long long* __restrict__ inv,
+                                                              int* __restrict__ group_off) {
+  __shared__ int cnt[kMaxKeys][kThreads];  // per-thread counts, then their exclusive scan
+  __shared__ int total[kMaxKeys];
+  const int t = threadIdx.x;
+  const long long E = (T + kThreads - 1) / kThreads;
+  const long long b = t * E, e = b + E < T ? b + E : T;
+  int c[kMaxKeys];
+#pragma unroll
+  for (int k = 0; k < kMaxKeys; ++k) c[k] = 0;
+  for (long long i = b; i < e; ++i) {
+    int k = keys[i];
+    k = k < K ? k : K - 1;
+#pragma unroll
+    for (int q = 0; q < kMaxKeys; ++q) c[q] += (q == k);
+  }
+#pragma unroll
+  for (int k = 0; k < kMaxKeys; ++k) cnt[k][t] = c[k];
+  __syncthreads();
+  // exclusive scan of each key's counts over the threads (one warp per key)
+  const int warp = t >> 5, lane = t & 31;
+  if (warp < K) {
+    int run = 0;
+    for (int base = 0; base < kThreads; base += 32) {
+      const int v = cnt[warp][base + lane];
+      int x = v;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += y;
+      }
+      cnt[warp][base + lane] = run + x - v;
+      run += __shfl_sync(0xffffffffu, x, 31);
+    }
+    if (lane == 0) total[warp] = run;
+  }
+  __syncthreads();
+  int start[kMaxKeys];
+  int acc = 0;
+#pragma unroll
+  for (int k = 0; k < kMaxKeys; ++k) {
+    start[k] = acc + (k < K ? cnt[k][t] : 0);
+    acc += k < K ? total[k] : 0;
+  }
+  if (t == 0) {
+    int a = 0;
+    for (int k = 0; k < K; ++k) {
+      group_off[k] = a;
+      a += total[k];
+    }
+    group_off[K] = a;
+  }
+  for (long long i = b; i < e; ++i) {
+    int k = keys[i];
+    k = k < K ? k : K - 1;
+    int pos = 0;
+#pragma unroll
+    for (int q = 0; q < kMaxKeys; ++q)
+      if (q == k) pos = start[q]++;
+    order[pos] = i;
+    inv[i] = pos;
+  }
+}
+
+}  // namespace route
+}  // namespace vq

@@ -787,3 +787,22 @@ int vq_swiglu_bwd(const void* gate, int64_t ldg, const void* up, int64_t ldu, co
 }
 
 }  // extern "C"
+
+extern "C" {
+
+int vq_route_prep(const void* keys, int64_t T, int K, int64_t* order, int64_t* inv, int* group_off, void* stream) {
+  DeviceScope scope(order);
+  if (K < 1 || K > vq::route::kMaxKeys) return fail(VQ_ERR_INVALID, "groups %d not in [1, %d]", K, vq::route::kMaxKeys);
+  if (T < 0) return fail(VQ_ERR_INVALID, "negative length");
+  if (group_off == nullptr) return fail(VQ_ERR_INVALID, "null group offsets");
+  if (T > 0 && (keys == nullptr || order == nullptr || inv == nullptr)) return fail(VQ_ERR_INVALID, "null pointer");
+  if (T > (1LL << 30)) return fail(VQ_ERR_INVALID, "too many elements");
+  vq::route::route_prep_kernel<<<1, vq::route::kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint8_t*>(keys), T, K, reinterpret_cast<long long*>(order), reinterpret_cast<long long*>(inv),
+      group_off);
+  VQ_CUDA(cudaGetLastError());
+  return 0;
+}
+
+}  // extern "C"
+

@@ -45,6 +45,7 @@ def _declare(lib):
         "vq_mix": (_int, [_int, _vp, _vp, _vp, _i64, _i64, _i64, _vp, _i64, _vp]),
         "vq_linear_fwd": (_int, [_vp, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _vp]),
         "vq_set_gategrad_sm_reserve": (_int, [_int]),
+        "vq_route_prep": (_int, [_vp, _i64, _int, _vp, _vp, _vp, _vp]),
         "vq_linear_fwd_grouped": (_int, [_vp, _i64, _i64, _i64, _int, _vp, _i64, _i64, _vp, _vp, _i64, _vp]),
         "vq_linear_fwd_mcred": (_int, [_vp, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _vp]),
         "vq_linear_dx": (_int, [_vp, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _vp]),
@@ -75,7 +76,7 @@ def _declare(lib):
 
 EXPORTED = (
     "vq_last_error", "vq_abi_version", "vq_format_info", "vq_device_error", "vq_dequant", "vq_mix",
-    "vq_linear_fwd", "vq_linear_fwd_grouped", "vq_set_gategrad_sm_reserve", "vq_linear_fwd_mcred", "vq_linear_dx", "vq_gategrad_workspace_bytes", "vq_gategrad", "vq_gategrad_noalloc",
+    "vq_linear_fwd", "vq_linear_fwd_grouped", "vq_set_gategrad_sm_reserve", "vq_route_prep", "vq_linear_fwd_mcred", "vq_linear_dx", "vq_gategrad_workspace_bytes", "vq_gategrad", "vq_gategrad_noalloc",
     "vq_mixgemm_fwd",
     "vq_loss_fused", "vq_loss_stats", "vq_loss_combine", "vq_loss_grad",
     "vq_rmsnorm_fwd", "vq_rmsnorm_bwd", "vq_rope", "vq_swiglu_fwd", "vq_swiglu_bwd",
@@ -239,6 +240,18 @@ def linear_dx(dy: torch.Tensor, w: torch.Tensor, in_features: int, out: torch.Te
     _check(_lib.vq_linear_dx(dy.data_ptr(), dy.shape[0], N, dy.stride(0), w.data_ptr(), in_features, w.stride(0),
                              out.data_ptr(), out.stride(0), _stream(dy)))
     return out
+
+
+def route_prep(keys: torch.Tensor, K: int):
+    """(order int64 [T], inv int64 [T], group_off int32 [K + 1]) of the stable grouping of uint8 keys."""
+    _require_cuda(keys)
+    keys = keys.to(torch.uint8).contiguous().reshape(-1)
+    T = keys.numel()
+    order = torch.empty(T, dtype=torch.int64, device=keys.device)
+    inv = torch.empty(T, dtype=torch.int64, device=keys.device)
+    off = torch.empty(K + 1, dtype=torch.int32, device=keys.device)
+    _check(_lib.vq_route_prep(keys.data_ptr(), T, K, order.data_ptr(), inv.data_ptr(), off.data_ptr(), _stream(keys)))
+    return order, inv, off
 
 
 def set_gategrad_sm_reserve(sms: int) -> None:

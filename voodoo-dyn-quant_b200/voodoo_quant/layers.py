@@ -220,28 +220,23 @@ class _RoutedGatedLinearFunction(Function):
         x2 = _C._as_operand(x.reshape(-1, in_f))
         T = x2.shape[0]
         routing = routing.to(x2.device).reshape(-1)
-        # 8-bit keys: one radix pass; the inverse permutation turns the
-        # scatter back into a (vectorised) row gather
-        order = torch.argsort(routing.to(torch.uint8), stable=True)
-        inv = torch.empty_like(order)
-        inv[order] = torch.arange(T, device=x2.device)
+        # one kernel: stable grouping order, its inverse (the scatter back
+        # becomes a vectorised row gather) and the group offsets
+        order, inv, group_off = _C.route_prep(routing, layer.num_candidates)
         xs = x2.index_select(0, order)
         one = torch.ones(1, dtype=torch.float32, device=x2.device)
         blocks = layer._candidate_blocks()
         ws = [_C.mix([qt], [blocks[k]], one, out_f, layer.padded_in_features, in_f)
               for k, qt in enumerate(layer.candidate_types)]
-        counts = torch.bincount(routing, minlength=layer.num_candidates)
         if T > 128:  # one grouped GEMM; the group sizes stay on the device
-            group_off = torch.zeros(layer.num_candidates + 1, dtype=torch.int32, device=x2.device)
-            group_off[1:] = torch.cumsum(counts, 0)
             ys = _C.linear_fwd_grouped(xs, ws, out_f, in_f, group_off)
         else:
             ys = torch.empty(T, out_f, dtype=torch.bfloat16, device=x2.device)
-            off = 0
-            for k, n in enumerate(counts.tolist()):
-                if n:
-                    _C.linear_fwd(xs[off:off + n], ws[k], out_f, in_f, out=ys[off:off + n])
-                    off += n
+            offs = group_off.tolist()
+            for k in range(layer.num_candidates):
+                a, b = offs[k], offs[k + 1]
+                if b > a:
+                    _C.linear_fwd(xs[a:b], ws[k], out_f, in_f, out=ys[a:b])
         y = ys.index_select(0, inv)
         ctx.layer = layer
         ctx.x_shape = x.shape
@@ -549,7 +544,9 @@ class MixedQuantLinear(_MixedQuantBase):
             x = x.to(self._cand_arena.device)
         if _PTQR_STATE.enabled:
             probs = self.get_probs().to(x.device)
-            routing = _sample_token_routing(probs, x.numel() // x.shape[-1])
+            n = x.numel() // x.shape[-1]
+            bank = self.__dict__.get("_bank_ref")
+            routing = bank.routing(self, n) if bank is not None else _sample_token_routing(probs, n)
             out = _RoutedGatedLinearFunction.apply(x, probs, self, routing)
             if spec is not None and spec.col_offset is not None:
                 from voodoo_quant.parallel import tp_all_reduce_sum
@@ -767,6 +764,7 @@ class GateBank:
         self.valid = mask.to(dev)
         self.bpwn = bpwn.to(torch.float32).to(dev)
         self._p = None
+        self._routes = {}
 
     def probs(self) -> torch.Tensor:
         g = torch.cat([l.gates / l.temperature for l in self.layers])
@@ -775,8 +773,29 @@ class GateBank:
         p = torch.softmax(padded.view(len(self.layers), self.kmax), dim=1)
         for i, l in enumerate(self.layers):
             l._bank_probs = p[i, :l.num_candidates]
+            l._bank_ref = self
+            l._bank_index = i
         self._p = p
+        self._routes = {}
         return p
+
+    def routing(self, layer: "_MixedQuantBase", num_tokens: int) -> torch.Tensor:
+        """This step's PTQR routing of `layer` over `num_tokens` tokens.
+
+        The first request for a token count samples every layer at once: the
+        reference's Gumbel-argmax per layer and token (_sample_token_routing)
+        as one [L, Kmax, T] draw, with the padding candidates never chosen.
+        """
+        r = self._routes.get(num_tokens)
+        if r is None:
+            p = self._p.detach()
+            u = torch.rand(p.shape[0], p.shape[1], num_tokens, device=p.device)
+            gumbel = -torch.log((-torch.log(u.clamp_min(1e-9))).clamp_min(1e-9))
+            scores = torch.log(p.clamp_min(1e-9)).unsqueeze(2) + gumbel
+            scores.masked_fill_(~self.valid.unsqueeze(2), float("-inf"))
+            r = scores.argmax(dim=1).to(torch.uint8)
+            self._routes[num_tokens] = r
+        return r[layer._bank_index]
 
     def effective_bytes(self) -> torch.Tensor:
         if self._p is None:
@@ -786,7 +805,9 @@ class GateBank:
     def release(self) -> None:
         for l in self.layers:
             l._bank_probs = None
+            l._bank_ref = None
         self._p = None
+        self._routes = {}
 
 
 def total_effective_bytes(replaced: dict[str, _MixedQuantBase]) -> torch.Tensor:
