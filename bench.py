@@ -195,10 +195,11 @@ def run_gpu(args):
         from datetime import timedelta
         from voodoo_quant import parallel
 
-        if args.overlap_sms > 0:  # NCCL's CTAs must fit on the SMs the gate-gradient GEMM leaves free
-            os.environ.setdefault("NCCL_MAX_NCHANNELS", str(args.overlap_sms))
         dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=300))
         parallel.adopt_process_group(local)
+        # the dX all-reduce runs on a second communicator whose CTAs fit on
+        # the SMs the gate-gradient GEMM (and later dX chunks) leave free
+        parallel.enable_input_grad_overlap(args.overlap_sms)
     from voodoo_quant import _C
     from voodoo_quant.parallel import all_reduce_gate_grads
 
@@ -209,11 +210,10 @@ def run_gpu(args):
     stream = torch.cuda.current_stream()
 
     if world > 1:
-        layer.reduce_input_grad = True  # dX all-reduce overlapped with the gate-gradient GEMM
-        if args.overlap_sms > 0:
-            import voodoo_quant.layers as _layers
+        import voodoo_quant.layers as _layers
 
-            _layers.GATEGRAD_SM_RESERVE = args.overlap_sms
+        layer.reduce_input_grad = True  # dX all-reduce overlapped with the gate-gradient GEMM
+        _layers.INPUT_GRAD_CHUNKS = args.dx_chunks
 
     def step(xin, dyin):
         xg = xin.requires_grad_(True) if not xin.requires_grad else xin
@@ -398,7 +398,8 @@ def run_gpu(args):
             "dtype": "bf16",
             "data": "synthetic (seeded; candidates from the round-to-nearest GGUF packer)",
             "config": config(world, {"timed_step": graph_note,
-                                     "dx_allreduce_overlap_sms": args.overlap_sms if world > 1 else 0}),
+                                     "dx_allreduce_overlap_sms": args.overlap_sms if world > 1 else 0,
+                                     "dx_chunks": args.dx_chunks if world > 1 else 1}),
             "roofline": {
                 "bound": "tensor",
                 "kernel": f"gemm_{dom}",
@@ -631,6 +632,7 @@ def run_model_step(args):
 
     t_build = time.perf_counter()
     trainer, shape = build_distill(args.workload, dev, seed=0, tp=world > 1, multicast=args.multicast,
+                                   overlap_sms=args.overlap_sms if world > 1 else 0,
                                    args=StepArgs(max_steps=args.warmup + args.steps + args.e2e_steps + 3,
                                                  ptqr=args.ptqr))
     from voodoo_quant import parallel as _par
@@ -704,6 +706,7 @@ def run_model_step(args):
                        "batch": shape.batch, "seq": shape.seq, "candidates": shape.candidates,
                        "gated_tensors": len(trainer.replaced), "budget": shape.budget,
                        "parallelism": f"tp{world}", "build_s": round(t_build, 1),
+                       "input_grad_overlap_sms": args.overlap_sms if world > 1 else 0,
                        "row_parallel_reduce": "nvls multimem.red in GEMM" if multicast_on else "nccl all-reduce",
                        "forward": "ptqr (one candidate per token)" if args.ptqr else "candidate mixture",
                        "l2": "activations and logits far larger than L2"},
@@ -739,8 +742,11 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true", help="time the eager step instead of a CUDA graph of it")
     ap.add_argument("--overlap-sms", type=int, default=-1,
-                    help="TP: SMs the gate-gradient GEMM leaves to the concurrent dX all-reduce, which also caps "
-                         "NCCL's channels (default: 24 with more than one GPU, 0 otherwise; 24 measured best at TP-2)")
+                    help="TP: SMs the gate-gradient GEMMs leave to the concurrent input-gradient all-reduces, which "
+                         "run on a communicator capped to that many CTAs (default: 24 with more than one GPU, "
+                         "0 otherwise; 24 measured best at TP-2)")
+    ap.add_argument("--dx-chunks", type=int, default=1,
+                    help="layer workload under TP: row chunks of dX, each all-reduced while the next is computed")
     ap.add_argument("--ptqr", action="store_true",
                     help="full-step workloads: per-token quant routing forward (one candidate per token)")
     ap.add_argument("--multicast", action="store_true",

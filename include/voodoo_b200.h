@@ -110,6 +110,12 @@ int vq_route_prep(const void* keys, int64_t T, int K, int64_t* order, int64_t* i
  * all-reduces are synchronous). */
 int vq_set_gategrad_sm_reserve(int sms);
 
+/* The same for the store-epilogue GEMMs (vq_linear_fwd, vq_linear_dx,
+ * vq_mixgemm_fwd): a caller that splits dX into row chunks and all-reduces
+ * chunk i while chunk i + 1 is computed leaves the collective its SMs.  No
+ * counterpart in the reference. */
+int vq_set_gemm_sm_reserve(int sms);
+
 /* K1 for the per-token routed (PTQR) forward: rows of x are grouped by
  * candidate, rows [group_off[g], group_off[g + 1]) use weight w[g] (w a HOST
  * array of G <= 8 device pointers to bf16 [N, ldw]; group_off a DEVICE int

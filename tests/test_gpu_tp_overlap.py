@@ -1,0 +1,81 @@
+"""TP-2 distillation step with the input-gradient all-reduces overlapped
+(gate-gradient GEMMs deferred beside them on a second communicator) against
+the same step without overlap, on 2 GPUs (skipped with fewer).
+
+The overlap only reorders launches and leaves SMs free; the gate-gradient
+GEMM's stream-K split depends on how many SMs it gets, so its fp32 partial
+sums may be added in another order.  Tolerance: loss 1e-5 relative, gate
+gradients 1e-3 relative per tensor (L2).
+"""
+
+from __future__ import annotations
+
+import os
+import socket
+import tempfile
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, outdir):
+    from datetime import timedelta
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    import torch.distributed as dist
+
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev, timeout=timedelta(seconds=120))
+    from voodoo_quant import _C, layers, parallel
+    from voodoo_quant.training import synthetic as S
+    from voodoo_quant.training.trainer import build_distill
+
+    # the smallest Llama shape whose TP-2 shards keep every input dimension 256-aligned
+    S.SHAPES["tp2_test"] = S.ModelShape(2, 512, 4, 2, 1024, 4096, False, head_dim=128,
+                                        candidates=["Q4_K", "Q6_K", "Q8_0"], batch=2, seq=256)
+    res = {}
+    try:
+        parallel.adopt_process_group(rank)
+        for sms in (0, 24):
+            trainer, shape = build_distill("tp2_test", dev, seed=0, tp=True, overlap_sms=sms)
+            deferred = sum(bool(m.__dict__.get("_defer_gategrad", False)) for m in trainer.replaced.values())
+            x, y = S.random_tokens(shape, dev, seed=1)
+            out = trainer.forward_backward(x, y)
+            torch.cuda.synchronize()
+            res[sms] = {"loss": float(out["loss"]), "deferred": deferred,
+                        "grads": {n: m.gates.grad.detach().cpu().clone() for n, m in trainer.replaced.items()},
+                        "left": layers.has_deferred_gategrads()}
+            del trainer
+        res["dev_err"] = _C.device_error()
+        torch.save(res, os.path.join(outdir, f"r{rank}.pt"))
+    finally:
+        torch.cuda.synchronize()
+        dist.barrier()
+        parallel.reset_tp()
+        dist.destroy_process_group()
+
+
+def test_overlapped_input_grad_allreduce_matches_plain_step():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    with tempfile.TemporaryDirectory() as td:
+        mp.start_processes(_worker, args=(2, _free_port(), td), nprocs=2, join=True, start_method="spawn")
+        rs = [torch.load(os.path.join(td, f"r{r}.pt")) for r in range(2)]
+    for r in rs:
+        assert r["dev_err"] == 0
+        a, b = r[0], r[24]
+        assert a["deferred"] == 0 and b["deferred"] > 0 and not b["left"]
+        assert abs(a["loss"] - b["loss"]) <= 1e-5 * abs(a["loss"])
+        for n, g in a["grads"].items():
+            h = b["grads"][n]
+            assert float((g - h).norm()) <= 1e-3 * float(g.norm()) + 1e-12, n

@@ -147,6 +147,13 @@ constexpr int kMaxClusters = 128;
 // SMs the gate-gradient GEMM leaves free (vq_set_gategrad_sm_reserve), for a
 // collective that runs concurrently on another stream.
 int g_gategrad_sm_reserve = 0;
+// SMs the store-epilogue GEMMs (forward, dX) leave free (vq_set_gemm_sm_reserve).
+int g_gemm_sm_reserve = 0;
+
+inline int sm_reserve(int epi, int sms) {
+  const int r = epi == vq::gemm::kEpiGateGrad ? g_gategrad_sm_reserve : epi == vq::gemm::kEpiStoreBf16 ? g_gemm_sm_reserve : 0;
+  return r > 0 && r < sms - 2 ? r : 0;
+}
 
 // Gate-gradient partial slots the per-tile schedule writes.
 inline long long gategrad_tile_slots(long long N, long long Kin) {
@@ -173,8 +180,7 @@ int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, vq::gemm::Params p
     auto kern = gemm_pair_kernel<kAmn, kBmn, kEpi>;
     constexpr int smem = PairSmemLayout<kEpi>::total;
     VQ_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    int avail = sms;
-    if (kEpi == kEpiGateGrad && g_gategrad_sm_reserve > 0 && g_gategrad_sm_reserve < sms - 2) avail -= g_gategrad_sm_reserve;
+    const int avail = sms - sm_reserve(kEpi, sms);
     int clusters = p.num_tiles < avail / 2 ? p.num_tiles : avail / 2;
     if (clusters > kMaxClusters) clusters = kMaxClusters;
     if (kEpi == kEpiGateGrad && p.num_tiles % clusters != 0 && p.num_tiles > clusters) {
@@ -190,7 +196,8 @@ int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, vq::gemm::Params p
     auto kern = gemm_kernel<kAmn, kBmn, kEpi>;
     constexpr int smem = SmemLayout<kEpi>::total;
     VQ_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    const int grid = p.num_tiles < sms ? p.num_tiles : sms;
+    const int avail = sms - sm_reserve(kEpi, sms);
+    const int grid = p.num_tiles < avail ? p.num_tiles : avail;
     kern<<<grid, THREADS, smem, st>>>(ta, tb, p);
   }
   VQ_CUDA(cudaGetLastError());
@@ -446,6 +453,12 @@ int vq_linear_fwd_grouped(const void* x, int64_t T, int64_t Kin, int64_t ldx, in
 int vq_set_gategrad_sm_reserve(int sms) {
   if (sms < 0) return fail(VQ_ERR_INVALID, "negative SM count");
   g_gategrad_sm_reserve = sms;
+  return 0;
+}
+
+int vq_set_gemm_sm_reserve(int sms) {
+  if (sms < 0) return fail(VQ_ERR_INVALID, "negative SM count");
+  g_gemm_sm_reserve = sms;
   return 0;
 }
 

@@ -45,6 +45,7 @@ def _declare(lib):
         "vq_mix": (_int, [_int, _vp, _vp, _vp, _i64, _i64, _i64, _vp, _i64, _vp]),
         "vq_linear_fwd": (_int, [_vp, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _vp]),
         "vq_set_gategrad_sm_reserve": (_int, [_int]),
+        "vq_set_gemm_sm_reserve": (_int, [_int]),
         "vq_route_prep": (_int, [_vp, _i64, _int, _vp, _vp, _vp, _vp]),
         "vq_linear_fwd_grouped": (_int, [_vp, _i64, _i64, _i64, _int, _vp, _i64, _i64, _vp, _vp, _i64, _vp]),
         "vq_linear_fwd_mcred": (_int, [_vp, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _vp]),
@@ -76,7 +77,7 @@ def _declare(lib):
 
 EXPORTED = (
     "vq_last_error", "vq_abi_version", "vq_format_info", "vq_device_error", "vq_dequant", "vq_mix",
-    "vq_linear_fwd", "vq_linear_fwd_grouped", "vq_set_gategrad_sm_reserve", "vq_route_prep", "vq_linear_fwd_mcred", "vq_linear_dx", "vq_gategrad_workspace_bytes", "vq_gategrad", "vq_gategrad_noalloc",
+    "vq_linear_fwd", "vq_linear_fwd_grouped", "vq_set_gategrad_sm_reserve", "vq_set_gemm_sm_reserve", "vq_route_prep", "vq_linear_fwd_mcred", "vq_linear_dx", "vq_gategrad_workspace_bytes", "vq_gategrad", "vq_gategrad_noalloc",
     "vq_mixgemm_fwd",
     "vq_loss_fused", "vq_loss_stats", "vq_loss_combine", "vq_loss_grad",
     "vq_rmsnorm_fwd", "vq_rmsnorm_bwd", "vq_rope", "vq_swiglu_fwd", "vq_swiglu_bwd",
@@ -259,9 +260,14 @@ def set_gategrad_sm_reserve(sms: int) -> None:
     _check(load_library().vq_set_gategrad_sm_reserve(int(sms)))
 
 
+def set_gemm_sm_reserve(sms: int) -> None:
+    """SMs later forward / dX GEMMs leave free for a concurrent collective (0 = none)."""
+    _check(load_library().vq_set_gemm_sm_reserve(int(sms)))
+
+
 def gategrad(dy: torch.Tensor, x: torch.Tensor, qtypes, qbytes, n_out: int, in_features: int, padded_cols: int,
-             workspace: torch.Tensor | None = None) -> torch.Tensor:
-    """grad_probs[k] = <dy^T x, W_k> (float32 [K]); dW is never materialised."""
+             workspace: torch.Tensor | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+    """grad_probs[k] = <dy^T x, W_k> (float32 [K], into `out` when given); dW is never materialised."""
     _require_cuda(dy, x, *qbytes)
     dy = _as_operand(dy)
     x = _as_operand(x)
@@ -269,7 +275,12 @@ def gategrad(dy: torch.Tensor, x: torch.Tensor, qtypes, qbytes, n_out: int, in_f
     need = _lib.vq_gategrad_workspace_bytes(n_out, in_features, K)
     if workspace is None or workspace.numel() * workspace.element_size() < need:
         workspace = torch.empty(max(need, 4), dtype=torch.uint8, device=x.device)
-    g = torch.empty(K, dtype=torch.float32, device=x.device)
+    if out is None:
+        g = torch.empty(K, dtype=torch.float32, device=x.device)
+    else:
+        if out.dtype != torch.float32 or out.numel() != K or not out.is_contiguous():
+            raise ValueError("gategrad: out must be a contiguous float32 tensor of K elements")
+        g = out
     _check(_lib.vq_gategrad(dy.data_ptr(), dy.stride(0), x.data_ptr(), x.stride(0), x.shape[0], n_out, in_features,
                             K, types, ptrs, padded_cols, workspace.data_ptr(), workspace.numel(), g.data_ptr(),
                             _stream(x)))

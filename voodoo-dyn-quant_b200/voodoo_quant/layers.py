@@ -50,6 +50,11 @@ KEEP_MIXED_WEIGHT = True
 # concurrently; match it to the collective's CTA count (NCCL channels).
 GATEGRAD_SM_RESERVE = 0
 
+# Row chunks of dX in a layer that all-reduces its own input gradient
+# (reduce_input_grad under TP): the all-reduce of chunk i runs while chunk
+# i + 1 and the gate-gradient GEMM are computed.  1 = one dX GEMM.
+INPUT_GRAD_CHUNKS = 1
+
 
 # --------------------------------------------------------------------------- per-token quant routing
 class _PTQRState:
@@ -168,6 +173,67 @@ class _GatedLinearFunction(Function):
         return dx, dprobs, None, None
 
 
+def _overlap_sms() -> int:
+    """SMs a GEMM leaves free while a TP collective runs beside it."""
+    from voodoo_quant.parallel import TP
+    if not TP.enabled:
+        return 0
+    return GATEGRAD_SM_RESERVE if GATEGRAD_SM_RESERVE > 0 else TP.overlap_sms
+
+
+def _row_chunks(T: int, n: int) -> list[tuple[int, int]]:
+    """n row ranges of [0, T) on 256-row boundaries (fewer when T is small)."""
+    step = max(256, (T + n - 1) // n + 255) // 256 * 256
+    return [(a, min(a + step, T)) for a in range(0, T, step)]
+
+
+def _gategrad_into(dy2, x2, layer, out=None, reserve: int = 0) -> torch.Tensor:
+    if reserve:  # leave SMs to the all-reduce in flight so that it overlaps the GEMM
+        _C.set_gategrad_sm_reserve(reserve)
+    try:
+        return _C.gategrad(dy2, x2, layer.candidate_types, layer._candidate_blocks(), layer.out_features,
+                           layer.in_features, layer.padded_in_features,
+                           workspace=layer._gategrad_workspace(x2.device), out=out)
+    finally:
+        if reserve:
+            _C.set_gategrad_sm_reserve(0)
+
+
+# Gate-gradient GEMMs deferred until the all-reduce of their module's input
+# gradient is in flight (TP): (dY, X, layer, destination row of the bank's
+# gradient buffer).  parallel._CopyToParallel.backward launches that
+# all-reduce asynchronously and then runs these beside it; the gate bank's
+# backward runs what is left, so every deferred GEMM precedes its reader.
+_DEFERRED: list = []
+
+
+def has_deferred_gategrads() -> bool:
+    return bool(_DEFERRED)
+
+
+def flush_deferred_gategrads(overlap_bytes: int = 0) -> None:
+    """Run the deferred gate-gradient GEMMs in order.  The first ones, about
+    as long as an all-reduce of `overlap_bytes` in flight, leave SMs to it."""
+    from voodoo_quant.parallel import TP
+    sms = _overlap_sms() if overlap_bytes else 0
+    w = max(TP.world_size, 2)
+    budget = overlap_bytes * 2.0 * (w - 1) / w / 450e9  # seconds at a ring bus bandwidth of 450 GB/s
+    items = list(_DEFERRED)
+    _DEFERRED.clear()
+    for dy2, x2, layer, out in items:
+        _gategrad_into(dy2, x2, layer, out=out, reserve=sms if budget > 0 else 0)
+        budget -= 2.0 * x2.shape[0] * layer.out_features * layer.in_features / 1.2e15
+
+
+def _defer_slot(layer) -> torch.Tensor | None:
+    """The bank gradient row this layer's gate gradient goes to when it is
+    deferred, else None."""
+    bank = layer.__dict__.get("_bank_ref")
+    if bank is None or not layer.__dict__.get("_defer_gategrad", False) or bank._dgrad is None:
+        return None
+    return bank._dgrad[layer._bank_index, :layer.num_candidates]
+
+
 def _gated_linear_backward(ctx, dy: torch.Tensor):
     """dX = dY W_mix and d probs_k = <dY^T X, W_k>: the mixture's Jacobian,
     shared by the mixture forward and the routed (PTQR) forward."""
@@ -175,28 +241,38 @@ def _gated_linear_backward(ctx, dy: torch.Tensor):
     x2, probs = ctx.saved_tensors
     dy2 = _C._as_operand(dy.reshape(-1, layer.out_features))
     dx = dprobs = None
-    pending = None
+    pending = []
     if ctx.needs_input_grad[0]:
         w_mix = ctx.w_mix if ctx.w_mix is not None else layer._mix(probs)
-        dx = _C.linear_dx(dy2, w_mix, layer.in_features)
         if layer.reduce_input_grad:
             # column-parallel layer with a private input: sum the partial
-            # dX over the TP ranks while the gate-gradient GEMM runs
+            # dX over the TP ranks (chunk by chunk) while the rest of dX and
+            # the gate-gradient GEMM run
             from voodoo_quant.parallel import tp_all_reduce_async
-            pending = tp_all_reduce_async(dx)
+            T = dy2.shape[0]
+            chunks = _row_chunks(T, INPUT_GRAD_CHUNKS) if INPUT_GRAD_CHUNKS > 1 else [(0, T)]
+            dx = torch.empty(T, layer.in_features, dtype=torch.bfloat16, device=dy2.device)
+            sms = _overlap_sms() if len(chunks) > 1 else 0
+            try:
+                for i, (a, b) in enumerate(chunks):
+                    if i == 1 and sms:  # later chunks leave SMs to the all-reduces in flight
+                        _C.set_gemm_sm_reserve(sms)
+                    _C.linear_dx(dy2[a:b], w_mix, layer.in_features, out=dx[a:b])
+                    pending.append(tp_all_reduce_async(dx[a:b], overlap=True))
+            finally:
+                if sms:
+                    _C.set_gemm_sm_reserve(0)
+        else:
+            dx = _C.linear_dx(dy2, w_mix, layer.in_features)
     ctx.w_mix = None
     if ctx.needs_input_grad[1]:
-        from voodoo_quant.parallel import TP
-        reserve = pending is not None and TP.enabled and GATEGRAD_SM_RESERVE > 0
-        if reserve:  # leave SMs to the all-reduce in flight so that it overlaps the GEMM
-            _C.set_gategrad_sm_reserve(GATEGRAD_SM_RESERVE)
-        dprobs = _C.gategrad(dy2, x2, layer.candidate_types, layer._candidate_blocks(), layer.out_features,
-                             layer.in_features, layer.padded_in_features,
-                             workspace=layer._gategrad_workspace(x2.device)).to(probs.dtype)
-        if reserve:
-            _C.set_gategrad_sm_reserve(0)
-    if pending is not None:
-        pending.wait()
+        slot = None if pending else _defer_slot(layer)
+        if slot is not None:  # runs beside the all-reduce of the module's input gradient
+            _DEFERRED.append((dy2, x2, layer, slot))
+        else:
+            dprobs = _gategrad_into(dy2, x2, layer, reserve=_overlap_sms() if pending else 0).to(probs.dtype)
+    for w in pending:
+        w.wait()
     if dx is not None:
         dx = dx.to(ctx.x_dtype).reshape(ctx.x_shape)
     return dx, dprobs
@@ -765,14 +841,25 @@ class GateBank:
         self.bpwn = bpwn.to(torch.float32).to(dev)
         self._p = None
         self._routes = {}
+        self._dgrad = None
+        # gate gradients of layers marked _defer_gategrad are written into a
+        # [L, Kmax] buffer (TP: they run beside an all-reduce) and reach the
+        # gates through the tap below
+        self.defer = any(l.__dict__.get("_defer_gategrad", False) for l in self.layers)
 
     def probs(self) -> torch.Tensor:
         g = torch.cat([l.gates / l.temperature for l in self.layers])
         padded = torch.full((len(self.layers) * self.kmax,), float("-inf"), dtype=g.dtype, device=g.device)
         padded = padded.index_put((self.flat_index,), g)
         p = torch.softmax(padded.view(len(self.layers), self.kmax), dim=1)
+        pl = p
+        if self.defer and torch.is_grad_enabled() and p.requires_grad:
+            self._dgrad = torch.zeros(p.shape, dtype=torch.float32, device=p.device)
+            pl = _BankTap.apply(p, self)
+        else:
+            self._dgrad = None
         for i, l in enumerate(self.layers):
-            l._bank_probs = p[i, :l.num_candidates]
+            l._bank_probs = pl[i, :l.num_candidates]
             l._bank_ref = self
             l._bank_index = i
         self._p = p
@@ -808,6 +895,24 @@ class GateBank:
             l._bank_ref = None
         self._p = None
         self._routes = {}
+        self._dgrad = None
+
+
+class _BankTap(Function):
+    """Identity on the bank's probabilities; its backward adds the gate
+    gradients that deferred layers wrote into the bank's buffer (after
+    running any deferred GEMM still queued)."""
+
+    @staticmethod
+    def forward(ctx, p: torch.Tensor, bank: GateBank) -> torch.Tensor:
+        ctx.bank = bank
+        ctx.dgrad = bank._dgrad
+        return p.view_as(p)
+
+    @staticmethod
+    def backward(ctx, g: torch.Tensor):
+        flush_deferred_gategrads()
+        return g + ctx.dgrad.to(g.dtype), None
 
 
 def total_effective_bytes(replaced: dict[str, _MixedQuantBase]) -> torch.Tensor:

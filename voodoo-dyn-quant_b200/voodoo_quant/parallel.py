@@ -49,6 +49,11 @@ class _TPState:
     group = None
     device: torch.device | None = None
     exact_input_grad = True
+    # second communicator for the input-gradient all-reduces that run beside
+    # gate-gradient GEMMs, limited to `overlap_sms` CTAs (the SMs the GEMMs
+    # leave free); None = those all-reduces use `group`
+    overlap_group = None
+    overlap_sms = 0
 
 
 TP = _TPState()
@@ -107,6 +112,48 @@ def reset_tp() -> None:
     TP.rank, TP.world_size, TP.local_rank = 0, 1, 0
     TP.group = None
     TP.device = None
+    TP.overlap_group = None
+    TP.overlap_sms = 0
+
+
+def enable_input_grad_overlap(sms: int) -> bool:
+    """Run input-gradient all-reduces beside the gate-gradient GEMMs.
+
+    Collective: every rank calls it with the same `sms`.  Creates a second
+    communicator whose collectives use at most `sms` CTAs (NCCL maxCTAs) and
+    makes the GEMMs that run beside them leave that many SMs free; the
+    forward's all-reduces keep the default communicator and all its
+    channels.  `sms` <= 0 turns the overlap off.  Returns whether it is on.
+    """
+    if not TP.enabled or sms <= 0:
+        TP.overlap_group, TP.overlap_sms = None, 0
+        return False
+    ranks = list(range(TP.world_size))
+    if dist.get_backend(TP.group) == "nccl":
+        opts = dist.ProcessGroupNCCL.Options()
+        opts.config.max_ctas = int(sms)
+        opts.config.min_ctas = min(int(sms), 8)
+        opts.is_high_priority_stream = True
+        TP.overlap_group = dist.new_group(ranks=ranks, backend="nccl", pg_options=opts)
+    else:
+        TP.overlap_group = dist.new_group(ranks=ranks, backend=dist.get_backend(TP.group))
+    TP.overlap_sms = int(sms)
+    return True
+
+
+def mark_deferred_gategrads(model: nn.Module) -> int:
+    """Let every gated layer inside a module whose input passes through the
+    f operator (attention, MLP) defer its gate-gradient GEMM until that
+    module's input-gradient all-reduce is in flight.  Returns the count."""
+    n = 0
+    for mod in model.modules():
+        if not getattr(mod, "_tp_input_copy", False):
+            continue
+        for sub in mod.modules():
+            if hasattr(sub, "gates") and hasattr(sub, "candidate_types") and sub is not mod:
+                sub._defer_gategrad = True
+                n += 1
+    return n
 
 
 def barrier() -> None:
@@ -141,8 +188,16 @@ class _CopyToParallel(Function):
 
     @staticmethod
     def backward(ctx, g):
+        from voodoo_quant import layers
+
         g = g.clone().contiguous()
-        dist.all_reduce(g, op=dist.ReduceOp.SUM, group=TP.group)
+        if layers.has_deferred_gategrads():
+            # the module's gate-gradient GEMMs run while the sum is in flight
+            work = tp_all_reduce_async(g, overlap=True)
+            layers.flush_deferred_gategrads(overlap_bytes=g.numel() * g.element_size())
+            work.wait()
+        else:
+            dist.all_reduce(g, op=dist.ReduceOp.SUM, group=TP.group)
         return g
 
 
@@ -166,12 +221,14 @@ class _Done:
         return None
 
 
-def tp_all_reduce_async(t: torch.Tensor):
+def tp_all_reduce_async(t: torch.Tensor, overlap: bool = False):
     """In-place all-reduce SUM of `t` on the TP group, returning a handle to
-    wait on (a no-op handle when TP is disabled)."""
+    wait on (a no-op handle when TP is disabled).  `overlap`: on the
+    communicator of the collectives that run beside GEMMs, when there is one."""
     if not TP.enabled:
         return _Done()
-    return dist.all_reduce(t, op=dist.ReduceOp.SUM, group=TP.group, async_op=True)
+    group = TP.overlap_group if overlap and TP.overlap_group is not None else TP.group
+    return dist.all_reduce(t, op=dist.ReduceOp.SUM, group=group, async_op=True)
 
 
 def tp_broadcast(t: torch.Tensor, src: int = 0) -> torch.Tensor:

@@ -159,7 +159,7 @@ class GatedDistillTrainer:
 
 def build_distill(shape_name: str, device, seed: int = 0, args: StepArgs | None = None,
                   candidate_provider=None, replace_embeddings: bool = True, tp: bool = False,
-                  fused_blocks: bool = True, multicast: bool = False):
+                  fused_blocks: bool = True, multicast: bool = False, overlap_sms: int = 0):
     """Student (gated), Q8_0 teacher and trainer for a synthetic config.
 
     Under TP (an initialised process group adopted by voodoo_quant.parallel)
@@ -171,7 +171,11 @@ def build_distill(shape_name: str, device, seed: int = 0, args: StepArgs | None 
     SHARP inside their GEMMs (``parallel.enable_multicast_reduce``) where the
     GPUs support NVLink multicast; off by default: every rank's memory then
     takes every rank's reductions, and an 8B step at TP-2 measured 774 ms
-    against 610 ms with NCCL's ring all-reduce.
+    against 610 ms with NCCL's ring all-reduce.  Under TP with
+    ``overlap_sms`` > 0, each attention / MLP block's gate-gradient GEMMs
+    run beside the all-reduce of the block's input gradient on a second
+    communicator limited to that many CTAs (``parallel.enable_input_grad_overlap``,
+    ``parallel.mark_deferred_gategrads``); the GEMMs leave those SMs free.
     """
     from voodoo_quant.layers import replace_embedding_with_mixed_quant, replace_linear_with_mixed_quant
     from voodoo_quant.parallel import TP, tp_patch_model
@@ -208,6 +212,11 @@ def build_distill(shape_name: str, device, seed: int = 0, args: StepArgs | None 
         from voodoo_quant.parallel import enable_multicast_reduce
 
         enable_multicast_reduce(multicast)
+        if overlap_sms > 0:
+            from voodoo_quant.parallel import enable_input_grad_overlap, mark_deferred_gategrads
+
+            if enable_input_grad_overlap(overlap_sms):
+                mark_deferred_gategrads(base)
     torch.cuda.empty_cache()
     trainer = GatedDistillTrainer(base, teacher, replaced, args or StepArgs(), shape.budget * total_8bit,
                                   non_targeted, tp=tp and TP.enabled)
