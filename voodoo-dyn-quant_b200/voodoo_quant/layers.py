@@ -291,7 +291,8 @@ class _RoutedGatedLinearFunction(Function):
     """
 
     @staticmethod
-    def forward(ctx, x: torch.Tensor, probs: torch.Tensor, layer: "MixedQuantLinear", routing: torch.Tensor):
+    def forward(ctx, x: torch.Tensor, probs: torch.Tensor, layer: "MixedQuantLinear", routing: torch.Tensor,
+                reduce_out: bool = False):
         in_f, out_f = layer.in_features, layer.out_features
         x2 = _C._as_operand(x.reshape(-1, in_f))
         T = x2.shape[0]
@@ -314,6 +315,9 @@ class _RoutedGatedLinearFunction(Function):
                 if b > a:
                     _C.linear_fwd(xs[a:b], ws[k], out_f, in_f, out=ys[a:b])
         y = ys.index_select(0, inv)
+        if reduce_out:
+            from voodoo_quant.parallel import all_reduce_
+            all_reduce_(y)
         ctx.layer = layer
         ctx.x_shape = x.shape
         ctx.x_dtype = x.dtype
@@ -324,7 +328,7 @@ class _RoutedGatedLinearFunction(Function):
     @staticmethod
     def backward(ctx, dy: torch.Tensor):
         dx, dprobs = _gated_linear_backward(ctx, dy)
-        return dx, dprobs, None, None
+        return dx, dprobs, None, None, None
 
 
 class _MixedWeightFunction(Function):
@@ -623,18 +627,17 @@ class MixedQuantLinear(_MixedQuantBase):
             n = x.numel() // x.shape[-1]
             bank = self.__dict__.get("_bank_ref")
             routing = bank.routing(self, n) if bank is not None else _sample_token_routing(probs, n)
-            out = _RoutedGatedLinearFunction.apply(x, probs, self, routing)
-            if spec is not None and spec.col_offset is not None:
-                from voodoo_quant.parallel import tp_all_reduce_sum
-                out = tp_all_reduce_sum(out)
-            return out
+            # row-parallel: the partial outputs are summed over the TP ranks in place
+            reduce_out = spec is not None and spec.col_offset is not None
+            return _RoutedGatedLinearFunction.apply(x, probs, self, routing, reduce_out)
         if spec is not None and spec.col_offset is not None:
-            from voodoo_quant.parallel import multicast_reducer, tp_all_reduce_sum
-            red = multicast_reducer()
-            if red is not None:
-                # the all-reduce's backward is the identity, so the gradients are the local ones
-                return _GatedLinearFunction.apply(x, self.get_probs().to(x.device), self, red)
-            return tp_all_reduce_sum(_GatedLinearFunction.apply(x, self.get_probs().to(x.device), self))
+            from voodoo_quant.parallel import multicast_reducer, nccl_row_reducer
+            # the output sum over the TP ranks happens inside the forward (in
+            # the GEMM epilogue with NVLink multicast, else an in-place NCCL
+            # all-reduce of the fresh GEMM output); its backward is the
+            # identity, so the gradients are the local ones
+            red = multicast_reducer() or nccl_row_reducer()
+            return _GatedLinearFunction.apply(x, self.get_probs().to(x.device), self, red)
         return _GatedLinearFunction.apply(x, self.get_probs().to(x.device), self)
 
 
@@ -680,7 +683,7 @@ class MixedQuantEmbedding(_MixedQuantBase):
     def forward(self, input: torch.Tensor) -> torch.Tensor:
         spec = self.shard_spec
         if spec is not None and spec.vocab_start is not None:
-            from voodoo_quant.parallel import tp_all_reduce_sum
+            from voodoo_quant.parallel import tp_all_reduce_sum_
             v0, v1 = self.tp_vocab_start, self.tp_vocab_end
             ids = input.to(self._cand_arena.device)
             in_shard = (ids >= v0) & (ids < v1)
@@ -690,7 +693,7 @@ class MixedQuantEmbedding(_MixedQuantBase):
             emb_in = self._embedding_lookup(ids[in_shard] - v0)
             emb = emb_in.new_zeros(*ids.shape, self.embedding_dim)
             emb[in_shard] = emb_in
-            return tp_all_reduce_sum(emb)
+            return tp_all_reduce_sum_(emb)
         return self._embedding_lookup(input)
 
 

@@ -210,6 +210,65 @@ def tp_all_reduce_sum(t: torch.Tensor) -> torch.Tensor:
 all_reduce_sum = tp_all_reduce_sum
 
 
+class _AllReduceSumInPlace(Function):
+    """`_AllReduceSum` without the copy: the input is summed in place."""
+
+    @staticmethod
+    def forward(ctx, t: torch.Tensor) -> torch.Tensor:
+        ctx.mark_dirty(t)
+        dist.all_reduce(t, op=dist.ReduceOp.SUM, group=TP.group)
+        return t
+
+    @staticmethod
+    def backward(ctx, g):
+        return g
+
+
+def tp_all_reduce_sum_(t: torch.Tensor) -> torch.Tensor:
+    """In-place `tp_all_reduce_sum` for a freshly produced contiguous tensor
+    nothing else holds (a GEMM or lookup output): saves the copy of a
+    [tokens, hidden] activation per row-parallel layer.  Autograd rejects it
+    (version check) if the producer saved the tensor for its backward; a
+    view that needs a gradient takes the copying path."""
+    if not TP.enabled:
+        return t
+    if not t.is_contiguous():
+        return tp_all_reduce_sum(t)
+    if torch.is_grad_enabled() and t.requires_grad:
+        if t._is_view():
+            return tp_all_reduce_sum(t)
+        return _AllReduceSumInPlace.apply(t)
+    dist.all_reduce(t, op=dist.ReduceOp.SUM, group=TP.group)
+    return t
+
+
+def all_reduce_(t: torch.Tensor) -> torch.Tensor:
+    """Plain in-place SUM over the TP group, outside autograd (a no-op without TP)."""
+    if TP.enabled:
+        dist.all_reduce(t, op=dist.ReduceOp.SUM, group=TP.group)
+    return t
+
+
+class _NcclRowReducer:
+    """Row-parallel GEMM whose fresh output is summed over the TP ranks in
+    place by NCCL (used inside the gated Linear's forward)."""
+
+    @staticmethod
+    def linear(x2: torch.Tensor, w: torch.Tensor, n_out: int, in_features: int) -> torch.Tensor:
+        from voodoo_quant import _C
+
+        y = _C.linear_fwd(x2, w, n_out, in_features)
+        return all_reduce_(y)
+
+
+_NCCL_ROW_REDUCER = _NcclRowReducer()
+
+
+def nccl_row_reducer():
+    """The in-place NCCL reducer for row-parallel gated Linears (None without TP)."""
+    return _NCCL_ROW_REDUCER if TP.enabled else None
+
+
 def tp_copy_to_parallel(t: torch.Tensor) -> torch.Tensor:
     if not TP.enabled or not TP.exact_input_grad:
         return t

@@ -110,13 +110,13 @@ class _RowParallelQ8(nn.Module):
 
     @torch.no_grad()
     def forward(self, x):
-        from voodoo_quant.parallel import multicast_reducer, tp_all_reduce_sum
+        from voodoo_quant.parallel import multicast_reducer, tp_all_reduce_sum_
         red = multicast_reducer()
         if red is not None and x.is_cuda:  # partial outputs summed over the TP ranks inside the GEMM
             x2 = _C._as_operand(x.reshape(-1, self.in_features))
             y = red.linear(x2, self.inner.weight_bf16(), self.out_features, self.in_features)
             return y.to(x.dtype).reshape(*x.shape[:-1], self.out_features)
-        return tp_all_reduce_sum(self.inner(x))
+        return tp_all_reduce_sum_(self.inner(x))
 
 
 class _VocabParallelQ8(nn.Module):
@@ -126,8 +126,8 @@ class _VocabParallelQ8(nn.Module):
         self.vocab_start, self.rows = vocab_start, rows
 
     def forward(self, ids):
-        from voodoo_quant.parallel import tp_all_reduce_sum
+        from voodoo_quant.parallel import tp_all_reduce_sum_
         mask = (ids < self.vocab_start) | (ids >= self.vocab_start + self.rows)
         out = self.inner((ids - self.vocab_start).clamp(0, self.rows - 1))
         out = out * (~mask).unsqueeze(-1).to(out.dtype)
-        return tp_all_reduce_sum(out)
+        return tp_all_reduce_sum_(out)
