@@ -728,10 +728,68 @@ def run_model_step(args):
         dist.destroy_process_group()
 
 
+def run_cache_load(args):
+    """Candidate-cache load (the store's I/O row): combined_lazy cache files
+    holding the six packed candidates (Q2_K..Q8_0) of 8B MLP-shaped tensors
+    [14336 x 4096] are memory-mapped and packed into HBM arenas, through the
+    pinned double-buffered staging (``cache.upload_staged``) and, for
+    comparison, through plain pageable copies.  Files are written first, so
+    the page cache is warm: this measures the host->HBM path, not the disk."""
+    import tempfile
+
+    import torch
+    from voodoo_quant import cache
+    from voodoo_quant.cache import pack_arena
+    from voodoo_quant.quants import rtn
+
+    dev = torch.device("cuda", 0)
+    types = ["Q2_K", "Q3_K", "Q4_K", "Q5_K", "Q6_K", "Q8_0"]
+    rows, cols, n_files = 14336, 4096, 4
+    with tempfile.TemporaryDirectory() as td:
+        paths = []
+        for i in range(n_files):
+            g = torch.Generator(device=dev).manual_seed(i)
+            w = torch.randn(rows, cols, device=dev, generator=g) * 0.02
+            qb = {qt: rtn.quantize(w, qt).cpu() for qt in types}
+            paths.append(os.path.join(td, f"combined_lazy_w{i:016x}_inone.pt"))
+            torch.save(qb, paths[-1])
+            del w, qb
+        nbytes = 0
+
+        def load_all():
+            nonlocal nbytes
+            nbytes = 0
+            arenas = []
+            for p in paths:
+                mm = torch.load(p, weights_only=True, map_location="cpu", mmap=True)
+                a, lay = pack_arena(types, [mm[qt] for qt in types], rows, cols, dev)
+                nbytes += sum(l.nbytes for l in lay)
+                arenas.append(a)
+            torch.cuda.synchronize()
+            return arenas
+
+        res = {}
+        for mode in ("staged", "pageable", "staged"):
+            cache._STAGE_MIN = (1 << 20) if mode == "staged" else (1 << 62)
+            t0 = time.perf_counter()
+            arenas = load_all()
+            dt = time.perf_counter() - t0
+            res[mode] = nbytes / dt / 1e9
+            del arenas
+        cache._STAGE_MIN = 1 << 20
+    print(json.dumps({"metric": "candidate cache load (mmap -> HBM arena)", "value": round(res["staged"], 2),
+                      "unit": "GB/s", "n_gpus": 1, "higher_is_better": True,
+                      "pageable_copy_gbs": round(res["pageable"], 2), "bytes_per_load": nbytes,
+                      "config": {"workload": f"{n_files} combined_lazy files, 6 candidates of [{rows}x{cols}]",
+                                 "page_cache": "warm", "staging": f"2 x {cache._STAGE_BYTES >> 20} MiB pinned"}}),
+          flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--workload", choices=["layer", "tiny", "0.6b", "8b"], default="layer",
-                    help="layer: the single gated-Linear step (default); others: full distillation step")
+    ap.add_argument("--workload", choices=["layer", "tiny", "0.6b", "8b", "cache-load"], default="layer",
+                    help="layer: the single gated-Linear step (default); tiny/0.6b/8b: full distillation step; "
+                         "cache-load: candidate-cache files into HBM (GB/s)")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=60)
     ap.add_argument("--warmup", type=int, default=3)
@@ -764,6 +822,8 @@ def main():
         run_ncu_case()
     elif args.impl == "reference":
         run_reference(args)
+    elif args.workload == "cache-load":
+        run_cache_load(args)
     elif args.workload != "layer":
         run_model_step(args)
     else:

@@ -116,6 +116,17 @@ int vq_set_gategrad_sm_reserve(int sms);
  * counterpart in the reference. */
 int vq_set_gemm_sm_reserve(int sms);
 
+/* GPU quantiser: weights [rows, ldw] (w_dtype 0 = float32, 1 = bfloat16;
+ * cols a multiple of 32) -> packed blocks out (rows * cols / 32 blocks of
+ * block_bytes).  Q8_0 (ggml type 8) only: byte-identical to ggml's
+ * reference rule (d = max|x| / 127 stored as fp16, q = roundf(x / d)).
+ * Replaces libggml's quantize_q8_0 behind ggml.quantize_tensor,
+ * voodoo_quant/ggml.py:171-221 (Q8_0 teacher, training/q8_teacher.py:101-128,
+ * and Q8_0 candidates, layers.py:1301-1340).  Other types return
+ * VQ_ERR_UNSUPPORTED. */
+int vq_quantize(int ggml_type, const void* w, int w_dtype, int64_t rows, int64_t cols, int64_t ldw, void* out,
+                void* stream);
+
 /* K1 for the per-token routed (PTQR) forward: rows of x are grouped by
  * candidate, rows [group_off[g], group_off[g + 1]) use weight w[g] (w a HOST
  * array of G <= 8 device pointers to bf16 [N, ldw]; group_off a DEVICE int

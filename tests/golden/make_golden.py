@@ -20,6 +20,13 @@ What it records (all seeded, all small):
 * ``mixlinear_golden.npz`` -- the reference's ``_MixedWeightFunction`` +
   ``F.linear`` autograd (``layers.py:322-363``, ``:1730-1731``) in float32:
   Y, dX, d(probs) and d(gates) for seeded X, dY, gates and packed candidates.
+* ``q8quant_golden.npz`` -- gguf-py 0.19.0's Q8_0 quantiser (its restatement
+  of ggml's reference ``quantize_row_q8_0``, which the reference reaches
+  through libggml, ``voodoo_quant/ggml.py:171-221``) on seeded float32
+  weights with edge blocks: all zero, exact .5 ties, the largest float below
+  1/2, signed zeros, tiny and huge magnitudes; and on the same weights
+  rounded to bfloat16.  ``--only q8quant`` regenerates just this file (it
+  needs gguf-py, not the reference checkout).
 * ``loss_golden.npz`` -- the reference's ``_chunked_forward_loss``
   (``training/trainer.py:753-832``) on seeded logits through an identity
   head: CE, KL and the gradient with respect to the student logits.
@@ -267,5 +274,31 @@ def main() -> None:
     print("ptqr golden written")
 
 
+def make_q8quant_golden() -> None:
+    import torch
+    from gguf import GGMLQuantizationType, quants
+
+    rng = np.random.default_rng(7)
+    w = (rng.standard_normal((24, 256)) * np.exp(rng.normal(0.0, 2.0, (24, 1)))).astype(np.float32)
+    w[0, :32] = 0.0
+    ties = np.array([127.0, 0.5, 1.5, 2.5, -0.5, -1.5, -2.5, np.nextafter(np.float32(0.5), np.float32(0)),
+                     -np.nextafter(np.float32(0.5), np.float32(0)), 126.5, -126.5, 63.5, 0.0, -0.0, 3.4999998, 1.0],
+                    dtype=np.float32)
+    w[1, :16] = ties
+    w[1, 16:32] = -ties
+    w[2, :32] = rng.standard_normal(32).astype(np.float32) * np.float32(1e-30)
+    w[3, :32] = rng.standard_normal(32).astype(np.float32) * np.float32(1e30)
+    w[4, :32] = -0.0
+    wb = torch.from_numpy(w).to(torch.bfloat16).float().numpy()
+    q = quants.quantize(w, GGMLQuantizationType.Q8_0).reshape(-1, 34)
+    qb = quants.quantize(wb, GGMLQuantizationType.Q8_0).reshape(-1, 34)
+    np.savez_compressed(HERE / "q8quant_golden.npz", w=w, q=q, w_bf16=wb, q_bf16=qb)
+    print("q8quant golden written")
+
+
 if __name__ == "__main__":
-    main()
+    if "--only" in sys.argv and sys.argv[sys.argv.index("--only") + 1] == "q8quant":
+        make_q8quant_golden()
+    else:
+        main()
+        make_q8quant_golden()

@@ -22,6 +22,7 @@
 #include "gemm_tc.cuh"
 #include "loss.cuh"
 #include "blocks.cuh"
+#include "quant.cuh"
 #include "../../include/voodoo_b200.h"
 
 namespace {
@@ -813,6 +814,33 @@ int vq_route_prep(const void* keys, int64_t T, int K, int64_t* order, int64_t* i
   vq::route::route_prep_kernel<<<1, vq::route::kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const uint8_t*>(keys), T, K, reinterpret_cast<long long*>(order), reinterpret_cast<long long*>(inv),
       group_off);
+  VQ_CUDA(cudaGetLastError());
+  return 0;
+}
+
+int vq_quantize(int ggml_type, const void* w, int w_dtype, int64_t rows, int64_t cols, int64_t ldw, void* out,
+                void* stream) {
+  DeviceScope scope(out);
+  if (ggml_type != vq::kQ8_0) return fail(VQ_ERR_UNSUPPORTED, "GPU quantiser: ggml type %d not supported (Q8_0 only)", ggml_type);
+  if (w_dtype != 0 && w_dtype != 1) return fail(VQ_ERR_INVALID, "weight dtype %d (0 = float32, 1 = bfloat16)", w_dtype);
+  if (rows < 0 || cols < 0) return fail(VQ_ERR_INVALID, "negative shape");
+  if (cols % 32 != 0) return fail(VQ_ERR_INVALID, "requires in_features %% 32 == 0, got %lld", (long long)cols);
+  if (ldw < cols) return fail(VQ_ERR_INVALID, "leading dimension %lld < %lld", (long long)ldw, (long long)cols);
+  const long long nblk = static_cast<long long>(rows) * (cols / 32);
+  if (nblk == 0) return 0;
+  if (w == nullptr || out == nullptr) return fail(VQ_ERR_INVALID, "null pointer");
+  int sms = 0;
+  if (int rc = sm_count(&sms)) return rc;
+  const long long warps_per_cta = vq::quant::kQ8Threads / 32;
+  long long grid = (nblk + warps_per_cta - 1) / warps_per_cta;
+  if (grid > 16LL * sms) grid = 16LL * sms;  // grid-stride beyond 16 resident CTAs per SM
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (w_dtype == 0)
+    vq::quant::q8_0_quantize_kernel<float><<<static_cast<unsigned>(grid), vq::quant::kQ8Threads, 0, st>>>(
+        static_cast<const float*>(w), rows, cols, ldw, static_cast<uint8_t*>(out));
+  else
+    vq::quant::q8_0_quantize_kernel<__nv_bfloat16><<<static_cast<unsigned>(grid), vq::quant::kQ8Threads, 0, st>>>(
+        static_cast<const __nv_bfloat16*>(w), rows, cols, ldw, static_cast<uint8_t*>(out));
   VQ_CUDA(cudaGetLastError());
   return 0;
 }

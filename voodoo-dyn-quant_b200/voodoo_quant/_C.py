@@ -42,6 +42,7 @@ def _declare(lib):
         "vq_format_info": (_int, [_int, ctypes.POINTER(_int), ctypes.POINTER(_int)]),
         "vq_device_error": (_int, [_vp, ctypes.POINTER(_int)]),
         "vq_dequant": (_int, [_int, _vp, _i64, _i64, _vp, _vp]),
+        "vq_quantize": (_int, [_int, _vp, _int, _i64, _i64, _i64, _vp, _vp]),
         "vq_mix": (_int, [_int, _vp, _vp, _vp, _i64, _i64, _i64, _vp, _i64, _vp]),
         "vq_linear_fwd": (_int, [_vp, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _vp]),
         "vq_set_gategrad_sm_reserve": (_int, [_int]),
@@ -77,7 +78,7 @@ def _declare(lib):
 
 EXPORTED = (
     "vq_last_error", "vq_abi_version", "vq_format_info", "vq_device_error", "vq_dequant", "vq_mix",
-    "vq_linear_fwd", "vq_linear_fwd_grouped", "vq_set_gategrad_sm_reserve", "vq_set_gemm_sm_reserve", "vq_route_prep", "vq_linear_fwd_mcred", "vq_linear_dx", "vq_gategrad_workspace_bytes", "vq_gategrad", "vq_gategrad_noalloc",
+    "vq_linear_fwd", "vq_linear_fwd_grouped", "vq_set_gategrad_sm_reserve", "vq_set_gemm_sm_reserve", "vq_quantize", "vq_route_prep", "vq_linear_fwd_mcred", "vq_linear_dx", "vq_gategrad_workspace_bytes", "vq_gategrad", "vq_gategrad_noalloc",
     "vq_mixgemm_fwd",
     "vq_loss_fused", "vq_loss_stats", "vq_loss_combine", "vq_loss_grad",
     "vq_rmsnorm_fwd", "vq_rmsnorm_bwd", "vq_rope", "vq_swiglu_fwd", "vq_swiglu_bwd",
@@ -141,6 +142,26 @@ def device_error(device: torch.device | None = None) -> int:
     st = torch.cuda.current_stream(device).cuda_stream
     _check(lib.vq_device_error(st, ctypes.byref(code)))
     return code.value
+
+
+def quantize(w: torch.Tensor, qtype: str) -> torch.Tensor:
+    """GPU quantiser: float32 / bfloat16 [rows, cols] -> uint8 [rows * cols / 32, 34] Q8_0 blocks
+    (byte-identical to ggml's reference rule); other types raise ValueError."""
+    _require_cuda(w)
+    if qtype not in GGML_TYPE:
+        raise ValueError(f"Unknown quant type: {qtype}. Supported: {list(GGML_TYPE)}")
+    if w.dim() != 2:
+        raise ValueError(f"quantize expects a 2-D weight, got shape {tuple(w.shape)}")
+    if w.dtype not in (torch.float32, torch.bfloat16):
+        w = w.to(torch.float32)
+    if w.stride(1) != 1:
+        w = w.contiguous()
+    be, bb = format_info(qtype)
+    rows, cols = w.shape
+    out = torch.empty(rows * (cols // be) if cols % be == 0 else 0, bb, dtype=torch.uint8, device=w.device)
+    _check(_lib.vq_quantize(GGML_TYPE[qtype], w.data_ptr(), 0 if w.dtype == torch.float32 else 1, rows, cols,
+                            w.stride(0), out.data_ptr(), _stream(w)))
+    return out
 
 
 def dequant(qbytes: torch.Tensor, qtype: str, rows: int, cols: int) -> torch.Tensor:

@@ -75,9 +75,65 @@ def pack_arena(types: list[str], qbytes: list[torch.Tensor], rows: int, padded_c
         layout.append(CandidateLayout(qt, off, expect, info.block_bytes))
         off += (expect + _ALIGN - 1) // _ALIGN * _ALIGN
     arena = torch.empty(max(off, _ALIGN), dtype=torch.uint8, device=device)
+    staged = []
     for lay, qb in zip(layout, qbytes):
-        arena[lay.offset:lay.offset + lay.nbytes].copy_(qb.reshape(-1).to(dtype=torch.uint8), non_blocking=False)
+        src = qb.reshape(-1).to(dtype=torch.uint8)
+        if arena.is_cuda and src.device.type == "cpu" and lay.nbytes >= _STAGE_MIN:
+            staged.append((lay, src))
+        else:
+            arena[lay.offset:lay.offset + lay.nbytes].copy_(src, non_blocking=False)
+    if staged:
+        upload_staged(arena, [(lay.offset, src) for lay, src in staged])
     return arena, layout
+
+
+# Host -> HBM upload of packed blocks that sit in host memory (typically the
+# mmap of a combined_lazy cache file): pages are copied into one of two pinned
+# staging buffers while the other one's asynchronous copy to the device runs,
+# so reading the file (page faults included) overlaps the PCIe transfer and
+# the copies run at pinned-memory speed instead of through pageable bounces.
+_STAGE_BYTES = 64 << 20
+_STAGE_MIN = 1 << 20
+_stage_bufs: list[torch.Tensor] = []
+
+
+def _staging_buffers() -> list[torch.Tensor]:
+    if not _stage_bufs:
+        _stage_bufs.extend(torch.empty(_STAGE_BYTES, dtype=torch.uint8).pin_memory() for _ in range(2))
+    return _stage_bufs
+
+
+def upload_staged(dst: torch.Tensor, pieces: list[tuple[int, torch.Tensor]]) -> int:
+    """Copy host uint8 tensors into the device tensor `dst` at byte offsets
+    (`pieces` = [(offset, host tensor)]) through double-buffered pinned
+    staging on a side stream; returns the bytes copied.  The caller's stream
+    waits for the copies."""
+    bufs = _staging_buffers()
+    dev = dst.device
+    side = torch.cuda.Stream(device=dev)
+    done = [None, None]
+    i = total = 0
+    for off, src in pieces:
+        src = src.reshape(-1)
+        n = src.numel()
+        for a in range(0, n, _STAGE_BYTES):
+            b = i & 1
+            if done[b] is not None:
+                done[b].synchronize()  # the copy that last read this buffer has finished
+            m = min(_STAGE_BYTES, n - a)
+            bufs[b][:m].copy_(src[a:a + m])
+            with torch.cuda.stream(side):
+                dst[off + a:off + a + m].copy_(bufs[b][:m], non_blocking=True)
+                ev = torch.cuda.Event()
+                ev.record(side)
+            done[b] = ev
+            i += 1
+            total += m
+    torch.cuda.current_stream(dev).wait_stream(side)
+    for ev in done:
+        if ev is not None:
+            ev.synchronize()  # the staging buffers may be reused by the next call
+    return total
 
 
 def arena_views(arena: torch.Tensor, layout: list[CandidateLayout]) -> list[torch.Tensor]:

@@ -149,8 +149,19 @@ def bytes_per_weight(quant_type: str) -> float:
 
 
 def quantize_tensor(weight: torch.Tensor, quant_type: str, imatrix: torch.Tensor | None = None) -> torch.Tensor:
-    """llama.cpp quantiser (libggml-base via ctypes) -> uint8 [nblocks, block_bytes]."""
+    """llama.cpp quantiser (libggml-base via ctypes) -> uint8 [nblocks, block_bytes].
+
+    A CUDA weight quantised to Q8_0 without an importance matrix takes the
+    sm_100a quantiser instead (``vq_quantize``: ggml's reference Q8_0 rule,
+    byte-identical) and the result stays on that device."""
     info = get_quant_info(quant_type)
+    if weight.is_cuda and quant_type == "Q8_0" and imatrix is None:
+        from voodoo_quant import _C
+
+        w = weight.detach()
+        if w.dim() != 2:
+            raise ValueError(f"quantize_tensor expects a 2-D weight, got shape {tuple(w.shape)}")
+        return _C.quantize(w, "Q8_0")
     weight = weight.detach().to("cpu", torch.float32).contiguous()
     out_features, in_features = weight.shape
     if in_features % info.block_size != 0:

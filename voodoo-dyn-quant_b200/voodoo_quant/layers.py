@@ -485,7 +485,7 @@ class _MixedQuantBase(nn.Module):
             padded, pim, _ = _pad_weight_and_imatrix(weight.to(torch.float32), padded_im if imatrix is not None else None)
             for qt, p in missing:
                 qb = quantize_tensor(padded, qt, pim)  # libggml, exactly as the reference
-                _atomic_torch_save(qb, p)
+                _atomic_torch_save(qb.cpu(), p)
                 found[qt] = qb
         return found
 

@@ -26,8 +26,11 @@ KVALUES_IQ4NL = (-127, -104, -83, -65, -49, -35, -22, -10, 1, 13, 25, 38, 53, 69
 
 
 def _roundf(v: torch.Tensor) -> torch.Tensor:
-    """C roundf (half away from zero)."""
-    return torch.sign(v) * torch.floor(torch.abs(v) + 0.5)
+    """C roundf (half away from zero), exactly: floor(|v|) plus one when the
+    fraction is at least 1/2 (floor(|v| + 0.5) would round 0.49999997 up)."""
+    a = torch.abs(v)
+    f = torch.floor(a)
+    return torch.sign(v) * (f + torch.floor(2 * (a - f)))
 
 
 def _f16_bytes(v: torch.Tensor) -> torch.Tensor:

@@ -90,6 +90,12 @@ def rtn_candidate_provider(name: str, weight: torch.Tensor, types: list[str]) ->
 
 
 def q8_quantizer(weight: torch.Tensor) -> torch.Tensor:
+    """Q8_0 teacher bytes: the sm_100a quantiser on CUDA weights, the same
+    rule in torch elsewhere (both ggml's reference Q8_0 rule)."""
+    if weight.is_cuda:
+        from voodoo_quant import _C
+
+        return _C.quantize(weight.detach(), "Q8_0")
     from voodoo_quant.quants import rtn
 
     return rtn.quantize(weight.detach().to(torch.float32), "Q8_0")
