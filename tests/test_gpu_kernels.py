@@ -385,3 +385,34 @@ def test_gategrad_stream_k_tail_matches_fp64(cuda, T, N, IN):
     assert rel_err(got.double().cpu().numpy(), ref.cpu().numpy()) < 1e-3
     assert torch.equal(got, _C.gategrad(dy, x, types, blocks, N, IN, IN))
     assert _C.device_error() == 0
+
+
+def test_sm_reserve_keeps_results(cuda):
+    """GEMMs that leave SMs free for a concurrent collective
+    (vq_set_gemm_sm_reserve, vq_set_gategrad_sm_reserve) compute the same
+    tiles with fewer CTAs: forward and dX bit-identical, gate gradients equal
+    to fp32 rounding (the stream-K split of the last wave may change)."""
+    from voodoo_quant import _C
+    from voodoo_quant.quants import rtn
+
+    types = ["Q4_K", "Q6_K", "Q8_0"]
+    T, N, IN = 2048, 3584, 4096
+    g = torch.Generator(device="cpu").manual_seed(17)
+    w = torch.randn(N, IN, generator=g) * 0.02
+    blocks = [rtn.quantize(w, q).to(cuda) for q in types]
+    x = _bf16(torch.randn(T, IN, generator=g)).to(cuda)
+    dy = _bf16(torch.randn(T, N, generator=g)).to(cuda)
+    wm = _bf16(w).to(cuda)
+    base = (_C.linear_fwd(x, wm, N, IN), _C.linear_dx(dy, wm, IN), _C.gategrad(dy, x, types, blocks, N, IN, IN))
+    try:
+        _C.set_gemm_sm_reserve(24)
+        _C.set_gategrad_sm_reserve(24)
+        res = (_C.linear_fwd(x, wm, N, IN), _C.linear_dx(dy, wm, IN), _C.gategrad(dy, x, types, blocks, N, IN, IN))
+    finally:
+        _C.set_gemm_sm_reserve(0)
+        _C.set_gategrad_sm_reserve(0)
+    assert torch.equal(base[0], res[0]) and torch.equal(base[1], res[1])
+    assert rel_err(res[2].double().cpu().numpy(), base[2].double().cpu().numpy()) < 1e-5
+    with pytest.raises(ValueError):
+        _C.set_gemm_sm_reserve(-1)
+    assert _C.device_error() == 0

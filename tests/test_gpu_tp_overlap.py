@@ -1,6 +1,7 @@
 """TP-2 distillation step with the input-gradient all-reduces overlapped
-(gate-gradient GEMMs deferred beside them on a second communicator) against
-the same step without overlap, on 2 GPUs (skipped with fewer).
+(gate-gradient GEMMs deferred beside them on a second communicator; then
+also the head's dX all-reduced in two row chunks) against the same step
+without overlap, on 2 GPUs (skipped with fewer).
 
 The overlap only reorders launches and leaves SMs free; the gate-gradient
 GEMM's stream-K split depends on how many SMs it gets, so its fp32 partial
@@ -46,16 +47,18 @@ def _worker(rank, world, port, outdir):
     res = {}
     try:
         parallel.adopt_process_group(rank)
-        for sms in (0, 24):
+        for sms, chunks in ((0, 1), (24, 1), (24, 2)):
+            layers.INPUT_GRAD_CHUNKS = chunks  # the head sums its own input gradient in row chunks
             trainer, shape = build_distill("tp2_test", dev, seed=0, tp=True, overlap_sms=sms)
             deferred = sum(bool(m.__dict__.get("_defer_gategrad", False)) for m in trainer.replaced.values())
             x, y = S.random_tokens(shape, dev, seed=1)
             out = trainer.forward_backward(x, y)
             torch.cuda.synchronize()
-            res[sms] = {"loss": float(out["loss"]), "deferred": deferred,
+            res[(sms, chunks)] = {"loss": float(out["loss"]), "deferred": deferred,
                         "grads": {n: m.gates.grad.detach().cpu().clone() for n, m in trainer.replaced.items()},
                         "left": layers.has_deferred_gategrads()}
             del trainer
+        layers.INPUT_GRAD_CHUNKS = 1
         res["dev_err"] = _C.device_error()
         torch.save(res, os.path.join(outdir, f"r{rank}.pt"))
     finally:
@@ -73,9 +76,12 @@ def test_overlapped_input_grad_allreduce_matches_plain_step():
         rs = [torch.load(os.path.join(td, f"r{r}.pt")) for r in range(2)]
     for r in rs:
         assert r["dev_err"] == 0
-        a, b = r[0], r[24]
-        assert a["deferred"] == 0 and b["deferred"] > 0 and not b["left"]
-        assert abs(a["loss"] - b["loss"]) <= 1e-5 * abs(a["loss"])
-        for n, g in a["grads"].items():
-            h = b["grads"][n]
-            assert float((g - h).norm()) <= 1e-3 * float(g.norm()) + 1e-12, n
+        a = r[(0, 1)]
+        assert a["deferred"] == 0
+        for key in ((24, 1), (24, 2)):
+            b = r[key]
+            assert b["deferred"] > 0 and not b["left"]
+            assert abs(a["loss"] - b["loss"]) <= 1e-5 * abs(a["loss"])
+            for n, g in a["grads"].items():
+                h = b["grads"][n]
+                assert float((g - h).norm()) <= 1e-3 * float(g.norm()) + 1e-12, (key, n)
