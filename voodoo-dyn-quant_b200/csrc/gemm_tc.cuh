@@ -54,6 +54,9 @@ constexpr int kEpiMultimemRed = 2;
 // fall in 32 different banks).  The dynamic shared-memory window starts
 // 1024-byte aligned on sm_100 (checked at run time), as SWIZZLE_128B needs.
 constexpr int kStagePitch = kMaxUnitWords + 1;  // 69 words
+// Row pitch of the second gate-gradient epilogue set: the widest unit it may
+// stage is Q6_K's 210 bytes = 53 words (odd, so again 32 distinct banks).
+constexpr int kStagePitch1 = 53;
 
 template <int kEpi>
 struct SmemLayout {
@@ -79,6 +82,9 @@ struct Params {
   int units_per_row;
   long long cols;
   float* partials;
+  // paired gate-gradient kernel: bit k set = candidate k runs in the second
+  // set of epilogue warps (never Q8_0, whose unit is too wide for its rows)
+  int set1_mask;
   // stream-K tail (paired gate-gradient kernel only): when set, the tiles
   // left over after the full waves are split along K across all clusters;
   // pieces that do not start at k-block 0 write the partial slots that
@@ -253,10 +259,12 @@ __device__ __forceinline__ float row_dot(const uint32_t* slot, uint32_t t_row, l
 //   row0: first output row of this warp's 32 TMEM lanes; m128: index of the
 //   128-row block (for the gate-gradient partial slots); stage: the
 //   gate-gradient staging area (4 warps x 32 rows x kStagePitch words).
+//   cand_set: -1 = every candidate, else only those of that epilogue set
+//   (Params::set1_mask); pitch: words per staging row of this warp's set.
 template <int kEpi>
 __device__ __forceinline__ void epilogue_tile(const Params& p, uint8_t* stage, uint32_t t_row, long long row0,
                                               int m128, int n_blk, int wq, int lane, long long slot_override = -1,
-                                              long long row_end = -1) {
+                                              long long row_end = -1, int cand_set = -1, int pitch = kStagePitch) {
   const long long row = row0 + lane;
   const bool row_ok = row >= 0 && row < (row_end >= 0 ? row_end : static_cast<long long>(p.M));
   if (kEpi == kEpiStoreBf16) {
@@ -309,12 +317,13 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, uint8_t* stage, u
     // row's unit (one 256-column unit) into its shared slot row with 16-byte
     // loads, decodes it from there and dots it with the dW row read back from
     // TMEM; the warp then sums its 32 rows into one partial.
-    uint32_t* slot_row = reinterpret_cast<uint32_t*>(stage) + (wq * 32 + lane) * kStagePitch;
+    uint32_t* slot_row = reinterpret_cast<uint32_t*>(stage) + (wq * 32 + lane) * pitch;
     const long long slot =
         slot_override >= 0 ? slot_override : (static_cast<long long>(m128) * p.num_n_blk + n_blk) * 4 + wq;
     const long long colbase = static_cast<long long>(n_blk) * BN;
     const long long urow = (row_ok ? row : 0) * p.units_per_row + n_blk;
     for (int k = 0; k < p.cands.K; ++k) {
+      if (cand_set >= 0 && ((p.set1_mask >> k) & 1) != cand_set) continue;
       stage_row_lane(slot_row, p.cands.ptr[k] + urow * p.cands.ubytes[k], p.cands.ubytes[k]);
       float s = 0.f;
       switch (p.cands.fmt[k]) {
@@ -501,21 +510,36 @@ __global__ void __launch_bounds__(THREADS, 1)
 // commits arrive on both CTAs' barriers (tcgen05.commit multicast); both CTAs'
 // TMA loads count on the even CTA's "full" barriers.  Each CTA's TMEM holds
 // the fp32 accumulator of its own 128 rows, so the epilogue is unchanged.
-constexpr int PSTAGES = 6;
 constexpr int PA_STAGE = 128 * BK * 2;  // 16 KiB
 constexpr int PB_STAGE = 128 * BK * 2;  // 16 KiB
 
+// Per-epilogue shape of the paired kernel.  The gate-gradient epilogue
+// (decode K candidates and dot them with the dW tile) would take longer than
+// a tile's main loop with one warp per TMEM lane quarter, stalling the MMAs
+// on the accumulator buffers; it runs two sets of four warps that split the
+// candidates, and one pipeline stage fewer makes room for the second set's
+// staging rows.
+template <int kEpi>
+struct PairCfg {
+  static constexpr int kEpiSets = kEpi == kEpiGateGrad ? 2 : 1;
+  static constexpr int kStages = kEpi == kEpiGateGrad ? 5 : 6;
+  static constexpr int kThreads = 128 + 128 * kEpiSets;  // TMA, MMA, TMEM-owner, spare warp + epilogue sets
+};
+
 template <int kEpi>
 struct PairSmemLayout {
+  static constexpr int kStages = PairCfg<kEpi>::kStages;
   static constexpr int a_off = 0;
-  static constexpr int b_off = a_off + PSTAGES * PA_STAGE;
-  static constexpr int bar_off = b_off + PSTAGES * PB_STAGE;
-  static constexpr int n_bars = 2 * PSTAGES + 4;
+  static constexpr int b_off = a_off + kStages * PA_STAGE;
+  static constexpr int bar_off = b_off + kStages * PB_STAGE;
+  static constexpr int n_bars = 2 * kStages + 4;
   static constexpr int misc_off = bar_off + n_bars * 8;  // tmem base, abort flag, group m-tile prefix
   static constexpr int grp_off = misc_off + 16;
   static constexpr int stage_off = misc_off + 64;
-  static constexpr int stage_bytes = (kEpi == 1) ? 4 * 32 * kStagePitch * 4 : 0;
+  static constexpr int stage1_off = stage_off + 4 * 32 * kStagePitch * 4;  // second set's rows
+  static constexpr int stage_bytes = (kEpi == 1) ? 4 * 32 * (kStagePitch + kStagePitch1) * 4 : 0;
   static constexpr int total = stage_off + stage_bytes;
+  static_assert(total <= 232448, "paired kernel shared memory above the 227 KB per-block limit");
 };
 
 // Grouped tile -> (group, first output row of the 256-row tile, column block),
@@ -530,9 +554,11 @@ __device__ __forceinline__ void group_tile(const Params& p, const int* mt, int t
 }
 
 template <bool kAmn, bool kBmn, int kEpi, int G = 1>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<kEpi>::kThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ BMaps<G> tmB, Params p) {
   using SL = PairSmemLayout<kEpi>;
+  constexpr int NST = PairCfg<kEpi>::kStages;
+  constexpr int kSets = PairCfg<kEpi>::kEpiSets;
   extern __shared__ __align__(1024) uint8_t smem[];
   const uint32_t sbase = smem_u32(smem);
   if ((sbase & 1023u) != 0) {  // uniform in both CTAs: the layout is identical
@@ -543,22 +569,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
   const bool leader = rank == 0;
   const uint32_t bar0 = sbase + SL::bar_off;
   auto full_bar = [&](int s) { return bar0 + 8u * s; };
-  auto empty_bar = [&](int s) { return bar0 + 8u * (PSTAGES + s); };
-  auto tfull_bar = [&](int a) { return bar0 + 8u * (2 * PSTAGES + a); };
-  auto tempty_bar = [&](int a) { return bar0 + 8u * (2 * PSTAGES + 2 + a); };
+  auto empty_bar = [&](int s) { return bar0 + 8u * (NST + s); };
+  auto tfull_bar = [&](int a) { return bar0 + 8u * (2 * NST + a); };
+  auto tempty_bar = [&](int a) { return bar0 + 8u * (2 * NST + 2 + a); };
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + SL::misc_off);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + SL::misc_off + 4);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int cluster_id = blockIdx.x >> 1, num_clusters = gridDim.x >> 1;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < PSTAGES; ++s) {
+    for (int s = 0; s < NST; ++s) {
       mbar_init(full_bar(s), 1);
       mbar_init(empty_bar(s), 1);
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(tfull_bar(a), 1);
-      mbar_init(tempty_bar(a), 8);  // 4 epilogue warps x 2 CTAs (used in the even CTA)
+      mbar_init(tempty_bar(a), 8 * kSets);  // 4 epilogue warps per set x 2 CTAs (used in the even CTA)
     }
     *abort_flag = 0;
     if (G > 1) {  // 256-row tiles per group, from the device-side group offsets
@@ -615,8 +641,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
         const int m0 = row_base + 128 * static_cast<int>(rank);
         const int n0 = n_blk * BN + 128 * static_cast<int>(rank);
         for (int kb = sg.kb0; kb < sg.kb1; ++kb, ++it) {
-          const int s = it % PSTAGES;
-          const uint32_t ph = (it / PSTAGES) & 1u;
+          const int s = it % NST;
+          const uint32_t ph = (it / NST) & 1u;
           if (!mbar_wait(empty_bar(s), ph ^ 1u, abort_flag)) {
             report_error(p.err, kDevWaitTimeout, 11);
             alive = false;
@@ -659,8 +685,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
         for (int kb = sg.kb0; kb < sg.kb1; ++kb, ++it) {
-          const int s = it % PSTAGES;
-          const uint32_t ph = (it / PSTAGES) & 1u;
+          const int s = it % NST;
+          const uint32_t ph = (it / NST) & 1u;
           if (!mbar_wait(full_bar(s), ph, abort_flag)) {
             report_error(p.err, kDevWaitTimeout, 13);
             alive = false;
@@ -686,6 +712,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
   } else if (warp >= 4) {
     // --------------------------------------------------------------- epilogue (both CTAs)
     const int wq = warp & 3;
+    const int eset = (warp - 4) >> 2;  // epilogue set (TMEM lane quarter wq in either set)
+    uint8_t* stage = smem + (eset ? SL::stage1_off : SL::stage_off);
+    const int pitch = eset ? kStagePitch1 : kStagePitch;
     const uint32_t tempty_leader0 = map_to_rank(tempty_bar(0), 0);
     const uint32_t tempty_leader1 = map_to_rank(tempty_bar(1), 0);
     uint32_t local = 0;
@@ -709,8 +738,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
         slot = p.sk_base + ((static_cast<long long>(cluster_id) * 2 + sg.piece) * 2 + rank) * 4 + wq;
         sk_written[sg.piece] = true;
       }
-      epilogue_tile<kEpi>(p, smem + SL::stage_off, t_row, static_cast<long long>(row_base) + 128 * rank + 32 * wq,
-                          m128, n_blk, wq, lane, slot, row_end);
+      epilogue_tile<kEpi>(p, stage, t_row, static_cast<long long>(row_base) + 128 * rank + 32 * wq, m128, n_blk, wq,
+                          lane, slot, row_end, kSets > 1 ? eset : -1, pitch);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(acc ? tempty_leader1 : tempty_leader0);
@@ -720,7 +749,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       for (int j = 0; j < 2; ++j) {
         if (sk_written[j]) continue;
         const long long slot = p.sk_base + ((static_cast<long long>(cluster_id) * 2 + j) * 2 + rank) * 4 + wq;
-        for (int k = 0; k < p.cands.K; ++k) p.partials[slot * p.cands.K + k] = 0.f;
+        for (int k = 0; k < p.cands.K; ++k)
+          if (kSets == 1 || ((p.set1_mask >> k) & 1) == eset) p.partials[slot * p.cands.K + k] = 0.f;
       }
     }
   }

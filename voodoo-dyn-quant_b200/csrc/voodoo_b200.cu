@@ -192,7 +192,7 @@ int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, vq::gemm::Params p
     }
     BMaps<1> bm;
     bm.m[0] = tb;
-    kern<<<2 * clusters, THREADS, smem, st>>>(ta, bm, p);
+    kern<<<2 * clusters, PairCfg<kEpi>::kThreads, smem, st>>>(ta, bm, p);
   } else {
     auto kern = gemm_kernel<kAmn, kBmn, kEpi>;
     constexpr int smem = SmemLayout<kEpi>::total;
@@ -203,6 +203,31 @@ int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, vq::gemm::Params p
   }
   VQ_CUDA(cudaGetLastError());
   return 0;
+}
+
+// Candidates of the second gate-gradient epilogue set (bit k): greedy split
+// by staged unit bytes plus a fixed per-candidate cost, largest first, with
+// Q8_0 (too wide for the second set's staging rows) always in the first set.
+inline int gategrad_set_split(int K, const int* types) {
+  int order[8], cost[8];
+  for (int k = 0; k < K; ++k) {
+    order[k] = k;
+    cost[k] = vq::unit_bytes(types[k]) + 96;
+  }
+  for (int i = 1; i < K; ++i)  // stable insertion sort by descending cost
+    for (int j = i; j > 0 && cost[order[j]] > cost[order[j - 1]]; --j) {
+      const int t = order[j];
+      order[j] = order[j - 1];
+      order[j - 1] = t;
+    }
+  int load[2] = {0, 0}, mask = 0;
+  for (int i = 0; i < K; ++i) {
+    const int k = order[i];
+    const int set = (types[k] == vq::kQ8_0 || load[0] <= load[1]) ? 0 : 1;
+    load[set] += cost[k];
+    if (set) mask |= 1 << k;
+  }
+  return mask;
 }
 
 // Gate-gradient partial slots a workspace must hold: the per-tile slots plus,
@@ -446,7 +471,7 @@ int vq_linear_fwd_grouped(const void* x, int64_t T, int64_t Kin, int64_t ldx, in
   constexpr int smem = vq::gemm::PairSmemLayout<vq::gemm::kEpiStoreBf16>::total;
   VQ_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
   const int clusters = p.num_tiles < sms / 2 ? p.num_tiles : sms / 2;
-  kern<<<2 * clusters, vq::gemm::THREADS, smem, st>>>(ta, bm, p);
+  kern<<<2 * clusters, vq::gemm::PairCfg<vq::gemm::kEpiStoreBf16>::kThreads, smem, st>>>(ta, bm, p);
   VQ_CUDA(cudaGetLastError());
   return 0;
 }
@@ -500,6 +525,7 @@ int vq_gategrad(const void* dy, int64_t lddy, const void* x, int64_t ldx, int64_
   p.units_per_row = static_cast<int>(padded_cols / 256);
   p.cols = Kin;
   p.partials = static_cast<float*>(workspace);
+  p.set1_mask = gategrad_set_split(K, types);
   if (int rc = device_error_ptr(&p.err)) return rc;
   long long used = 0;
   if (int rc = launch_gemm<true, true, vq::gemm::kEpiGateGrad>(ta, tb, p, st, &used)) return rc;
