@@ -41,7 +41,7 @@ METRIC = "gated-distill train tokens/s"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 # dram__bytes_read.sum + dram__bytes_write.sum per launch of each config-2 GEMM
 # at full size on one B200, from a single-pass ncu capture of this benchmark
-NCU_TRAFFIC_BYTES = {"fwd": 820.6e6, "dx": 1031.6e6, "gategrad": 1103.2e6}
+NCU_TRAFFIC_BYTES = {"fwd": 818.1e6, "dx": 1032.6e6, "gategrad": 1115.4e6}
 BPW = {"Q2_K": 84 / 256, "Q3_K": 110 / 256, "Q4_K": 144 / 256, "Q5_K": 176 / 256, "Q6_K": 210 / 256,
        "Q8_0": 34 / 32, "IQ4_XS": 136 / 256}
 
