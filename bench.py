@@ -634,7 +634,8 @@ def run_model_step(args):
     trainer, shape = build_distill(args.workload, dev, seed=0, tp=world > 1, multicast=args.multicast,
                                    overlap_sms=args.overlap_sms if world > 1 else 0,
                                    args=StepArgs(max_steps=args.warmup + args.steps + args.e2e_steps + 3,
-                                                 ptqr=args.ptqr))
+                                                 ptqr=args.ptqr, logits_chunk=args.logits_chunk,
+                                                 ce_reduction="tokens" if args.logits_chunk > 0 else "valid"))
     from voodoo_quant import parallel as _par
 
     multicast_on = _par.multicast_reducer() is not None
@@ -643,9 +644,11 @@ def run_model_step(args):
     x, y = S.random_tokens(shape, dev, seed=1)
     tokens = x.numel()
     stream = torch.cuda.current_stream()
+    torch.cuda.reset_peak_memory_stats(dev)
     for _ in range(args.warmup):
         trainer.step(x, y)
     torch.cuda.synchronize()
+    peak_gb = torch.cuda.max_memory_allocated(dev) / 1e9
     barrier()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     clk = ClockSampler(local).start()
@@ -709,6 +712,7 @@ def run_model_step(args):
                        "input_grad_overlap_sms": args.overlap_sms if world > 1 else 0,
                        "row_parallel_reduce": "nvls multimem.red in GEMM" if multicast_on else "nccl all-reduce",
                        "forward": "ptqr (one candidate per token)" if args.ptqr else "candidate mixture",
+                       "logits_chunk": args.logits_chunk, "peak_alloc_gb_rank0": round(peak_gb, 2),
                        "l2": "activations and logits far larger than L2"},
             "roofline": {"bound": "tensor", "kernel": "whole step", "flops_per_token": fpt,
                          "achieved": round(ach, 1), "peak": round(peak_t * world, 1), "unit": "TFLOP/s",
@@ -808,6 +812,8 @@ def main():
                          "(default: 2 with more than one GPU; TP-8 0.606 -> 0.585 ms per step)")
     ap.add_argument("--ptqr", action="store_true",
                     help="full-step workloads: per-token quant routing forward (one candidate per token)")
+    ap.add_argument("--logits-chunk", type=int, default=0,
+                    help="full-step workloads: head + loss per chunk of this many tokens (no [tokens, V] logits)")
     ap.add_argument("--multicast", action="store_true",
                     help="full-step workloads under TP: sum row-parallel outputs with multimem.red in the GEMM")
     ap.add_argument("--profile-step", action="store_true",

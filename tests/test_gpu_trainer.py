@@ -126,3 +126,36 @@ def test_tiny_distill_steps_reduce_loss_and_track_budget(cuda):
     # the uniform start (0.78 of the 8-bit bytes) is over the 0.45 budget; the size term drives the bytes down
     assert hist[-1]["size_bytes"].item() < hist[0]["size_bytes"].item()
     assert set(trainer.assignments().values()) <= set(shape.candidates)
+
+
+@pytest.mark.parametrize("tied", [False, True])
+def test_chunked_head_loss_equals_full_logits(cuda, tied):
+    """--logits_chunk: head + loss per chunk of tokens (the last chunk ragged)
+    gives the loss and gate gradients of the full-logits step (both with the
+    token-count reduction).  Tolerance: loss 1e-5 relative; gate gradients
+    1e-3 relative per tensor (the head's gate gradient is summed per chunk)."""
+    from voodoo_quant.training import synthetic as S
+    from voodoo_quant.training.trainer import StepArgs, build_distill
+
+    name = "tiny_tied" if tied else "tiny"
+    if tied:
+        base = S.SHAPES["tiny"]
+        S.SHAPES[name] = S.ModelShape(base.layers, base.hidden, base.heads, base.kv_heads, base.ffn, base.vocab, True,
+                                      candidates=list(base.candidates), batch=base.batch, seq=base.seq,
+                                      budget=base.budget)
+    out = {}
+    for chunk in (0, 100):
+        args = StepArgs(max_steps=4, ce_reduction="tokens", logits_chunk=chunk)
+        trainer, shape = build_distill(name, cuda, seed=3, args=args)
+        x, y = S.random_tokens(shape, cuda, seed=5)
+        r = trainer.forward_backward(x, y)
+        out[chunk] = (float(r["loss"]), float(r["lm_loss"]), float(r["distill_loss"]),
+                      {n: m.gates.grad.detach().clone() for n, m in trainer.replaced.items()})
+        del trainer
+    a, b = out[0], out[100]
+    for i in range(3):
+        assert abs(a[i] - b[i]) <= 1e-5 * abs(a[i]) + 1e-7, (i, a[i], b[i])
+    assert set(a[3]) == set(b[3])
+    for n, g in a[3].items():
+        h = b[3][n]
+        assert float((g - h).norm()) <= 1e-3 * float(g.norm()) + 1e-9, n

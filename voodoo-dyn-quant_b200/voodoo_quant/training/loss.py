@@ -7,6 +7,10 @@ Replaces the reference's loss blocks (voodoo_quant/training/trainer.py):
   plus ``distill_weight`` * mean per-token T^2 * KL;
 * chunked path :797-821 -- ``ce_reduction="tokens"``: both sums divided by
   the token count;
+* head-chunked path :753-832 -- ``chunked_head_loss``: the student and teacher
+  heads run per token chunk on the final hidden states, each chunk's loss is
+  back-propagated through the head at once, so no [tokens, V] logits tensor
+  ever exists (peak: one chunk's logits and gradient);
 * vocab-parallel path :915-1066 -- ``tp_distillation_loss``: each rank holds
   the logits of its vocabulary shard; per-row partial statistics from one
   pass over the shard are all-gathered once (one collective, instead of the
@@ -117,3 +121,59 @@ def tp_distillation_loss(student_shard: torch.Tensor, teacher_shard: torch.Tenso
     loss, ce_sum, kl_sum = _TPFusedDistillLoss.apply(s, t, y, int(vocab_start), float(temperature), ce_w, kl_w,
                                                      group)
     return loss, (ce_sum * ce_w).detach(), (kl_sum / max(n, 1)).detach()
+
+
+def chunked_head_loss(student_head, teacher_head, hidden: torch.Tensor, t_hidden: torch.Tensor,
+                      targets: torch.Tensor, chunk: int, temperature: float = 1.0, distill_weight: float = 1.0,
+                      vocab_start: int | None = None, group=None):
+    """Head + loss per token chunk (reference ``_chunked_forward_loss``,
+    voodoo_quant/training/trainer.py:753-832).
+
+    ``hidden`` / ``t_hidden`` are the final hidden states of the student and
+    teacher stacks ([..., H]); for each chunk of ``chunk`` tokens the student
+    head (gated or plain) and the teacher head produce that chunk's logits,
+    the fused kernel gives its CE + T^2 * KL and logit gradient, and the
+    chunk's loss is back-propagated through the student head immediately
+    (the head's gate gradients accumulate over the chunks).  Both terms are
+    token sums divided by the token count (``ce_reduction="tokens"``), so the
+    chunked loss equals the unchunked one.  With ``vocab_start`` the heads
+    are vocabulary-parallel shards and each chunk uses the TP loss.
+
+    Returns (grad of ``hidden`` [same shape, detached], loss, lm_loss,
+    distill_loss) with detached scalars; the caller back-propagates the
+    hidden-state gradient through the stack once.
+    """
+    if chunk <= 0:
+        raise ValueError(f"chunk must be positive, got {chunk}")
+    H = hidden.shape[-1]
+    s_flat = hidden.detach().reshape(-1, H)
+    t_flat = t_hidden.detach().reshape(-1, H)
+    y_flat = targets.reshape(-1)
+    n = s_flat.shape[0]
+    ce_w, kl_w = _weights(y_flat, n, distill_weight, "tokens")
+    h_grad = torch.zeros_like(s_flat)
+    loss = torch.zeros((), dtype=torch.float32, device=s_flat.device)
+    ce_tot = torch.zeros((), dtype=torch.float32, device=s_flat.device)
+    kl_tot = torch.zeros((), dtype=torch.float32, device=s_flat.device)
+    for i in range(0, n, chunk):
+        h_c = s_flat[i:i + chunk].requires_grad_(True)
+        s_c = student_head(h_c)
+        with torch.no_grad():
+            t_c = teacher_head(t_flat[i:i + chunk])
+        y_c = y_flat[i:i + chunk]
+        V = s_c.shape[-1]
+        if vocab_start is not None:
+            loss_c, ce_c, kl_c = _TPFusedDistillLoss.apply(s_c.reshape(-1, V), t_c.reshape(-1, V).detach(), y_c,
+                                                           int(vocab_start), float(temperature), ce_w, kl_w, group)
+        else:
+            loss_c, ce_c, kl_c = _FusedDistillLoss.apply(s_c.reshape(-1, V), t_c.reshape(-1, V).detach(), y_c,
+                                                         float(temperature), ce_w, kl_w)
+        del t_c
+        loss_c.backward()
+        if h_c.grad is not None:
+            h_grad[i:i + chunk] = h_c.grad
+        loss = loss + loss_c.detach()
+        ce_tot = ce_tot + ce_c
+        kl_tot = kl_tot + kl_c
+        del s_c, loss_c, h_c
+    return h_grad.reshape(hidden.shape), loss, (ce_tot * ce_w).detach(), (kl_tot / max(n, 1)).detach()

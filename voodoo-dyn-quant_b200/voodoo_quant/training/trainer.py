@@ -24,7 +24,7 @@ import torch
 import torch.nn as nn
 
 from voodoo_quant.layers import GateBank, set_ptqr
-from voodoo_quant.training.loss import distillation_loss, tp_distillation_loss
+from voodoo_quant.training.loss import chunked_head_loss, distillation_loss, tp_distillation_loss
 
 
 def anneal_temperature(step: int, max_steps: int, start: float, end: float) -> float:
@@ -78,6 +78,9 @@ class StepArgs:
     max_steps: int = 50
     ce_reduction: str = "valid"  # plain path: mean CE over non-ignored tokens
     ptqr: bool = False  # per-token quant routing forward (reference --ptqr, trainer.py:1523,1612-1616)
+    # head + loss per chunk of this many tokens, never materialising the
+    # [tokens, V] logits (reference --logits_chunk, trainer.py:753-832); 0 = off
+    logits_chunk: int = 0
 
 
 class GatedDistillTrainer:
@@ -113,11 +116,14 @@ class GatedDistillTrainer:
         tau = anneal_temperature(self.step_idx, a.max_steps, a.temp_start, a.temp_end)
         for layer in self.replaced.values():
             layer.set_temperature(tau)
+        self.optimizer.zero_grad(set_to_none=True)
         self.bank.probs()
+        v0 = self._vocab_start()
+        if a.logits_chunk > 0:
+            return self._forward_backward_chunked(x, y, a, tau, v0)
         logits = self.student(input_ids=x, use_cache=False).logits
         with torch.no_grad():
             t_logits = self.teacher(input_ids=x, use_cache=False).logits
-        v0 = self._vocab_start()
         if self.tp and v0 is not None:
             kd, lm, kl = tp_distillation_loss(logits, t_logits, y, v0, a.distill_temperature, a.distill_weight,
                                               ce_reduction="tokens")
@@ -134,12 +140,59 @@ class GatedDistillTrainer:
         rel = torch.abs(current / self.target_bytes - 1.0)
         size_loss = torch.relu(rel - a.size_tolerance) ** 2
         loss = kd + a.size_weight * size_loss
-        self.optimizer.zero_grad(set_to_none=True)
         loss.backward()
         self.bank.release()
         if self.tp:
             _tp_all_reduce_gate_grads(self.trainable)
         return {"loss": loss.detach(), "lm_loss": lm, "distill_loss": kl, "size_bytes": current.detach(),
+                "size_loss": size_loss.detach(), "tau": tau}
+
+    def _size_loss(self, device):
+        a = self.args
+        current = self.bank.effective_bytes().to(device)
+        if self.tp:
+            from voodoo_quant.parallel import tp_all_reduce_sum
+
+            current = tp_all_reduce_sum(current)
+        current = current + self.non_targeted_bytes
+        rel = torch.abs(current / self.target_bytes - 1.0)
+        return current, torch.relu(rel - a.size_tolerance) ** 2
+
+    def _forward_backward_chunked(self, x, y, a: StepArgs, tau: float, v0) -> dict:
+        """Stacks once, then head + loss per chunk of ``a.logits_chunk`` tokens
+        (``loss.chunked_head_loss``), then one backward through the student
+        stack and the gate bank.  While the chunks run, a gated head reads its
+        probabilities from a detached leaf, so each chunk's backward stays in
+        the head; the leaf's accumulated gradient joins the final backward."""
+        student, teacher = self.student, self.teacher
+        hidden = student.model(input_ids=x, use_cache=False).last_hidden_state
+        with torch.no_grad():
+            t_hidden = teacher.model(input_ids=x, use_cache=False).last_hidden_state
+        head = student.lm_head
+        row = head.__dict__.get("_bank_probs")
+        bank_ref = head.__dict__.get("_bank_ref")
+        leaf = row.detach().requires_grad_(True) if row is not None else None
+        if leaf is not None:  # (PTQR: the head then draws its own routing per chunk)
+            head._bank_probs, head._bank_ref = leaf, None
+        try:
+            h_grad, kd, lm, kl = chunked_head_loss(head, teacher.lm_head, hidden, t_hidden, y, a.logits_chunk,
+                                                   a.distill_temperature, a.distill_weight,
+                                                   vocab_start=v0 if self.tp else None)
+        finally:
+            if leaf is not None:
+                head._bank_probs, head._bank_ref = row, bank_ref
+        del t_hidden
+        current, size_loss = self._size_loss(hidden.device)
+        outs, grads = [hidden, a.size_weight * size_loss], [h_grad, None]
+        if leaf is not None and leaf.grad is not None:
+            outs.append(row)
+            grads.append(leaf.grad)
+        torch.autograd.backward(outs, grads)
+        self.bank.release()
+        if self.tp:
+            _tp_all_reduce_gate_grads(self.trainable)
+        loss = kd + a.size_weight * size_loss.detach()
+        return {"loss": loss, "lm_loss": lm, "distill_loss": kl, "size_bytes": current.detach(),
                 "size_loss": size_loss.detach(), "tau": tau}
 
     def apply_update(self) -> None:
