@@ -235,6 +235,23 @@ int vq_rmsnorm_fwd(const void* x, int64_t ldx, int64_t rows, int64_t D, const vo
 int vq_rmsnorm_bwd(const void* x, int64_t ldx, const void* dy, int64_t lddy, int64_t rows, int64_t D,
                    const void* weight, const float* rstd, void* dx, int64_t lddx, void* stream);
 
+/* Residual add fused into the RMSNorm that follows it: h = a + res (bf16
+ * add), y = weight * bf16(h * rsqrt(mean(h^2) + eps)); h, y and rstd are
+ * written.  Replaces `hidden_states = residual + hidden_states;
+ * post_attention_layernorm(hidden_states)` of Hugging Face
+ * LlamaDecoderLayer.forward in the student/teacher models the step runs
+ * (trainer.py:2538-2556). */
+int vq_add_rmsnorm_fwd(const void* a, int64_t lda, const void* res, int64_t ldres, int64_t rows, int64_t D,
+                       const void* weight, float eps, void* h, int64_t ldh, void* y, int64_t ldy, float* rstd,
+                       void* stream);
+
+/* Its backward: dx = (RMSNorm input gradient of dy at x = h) + dres in fp32,
+ * rounded once to bf16 -- the gradient of both a and res, where dres is the
+ * gradient reaching h through the later residual add. */
+int vq_rmsnorm_bwd_add(const void* x, int64_t ldx, const void* dy, int64_t lddy, const void* dres, int64_t lddres,
+                       int64_t rows, int64_t D, const void* weight, const float* rstd, void* dx, int64_t lddx,
+                       void* stream);
+
 /* Rotary embedding of q [B, S, Hq, D] and k [B, S, Hk, D] in one launch
  * (unit stride over D; HOST arrays q_strides/k_strides = {b, s, h} and
  * cs_strides = {b, s} in elements, multiples of 8) with cos/sin [B, S, D];

@@ -42,6 +42,35 @@ def test_rmsnorm_forward_backward(cuda, rows, D):
     assert _rel(dx, xf.grad) < 1e-2
 
 
+@pytest.mark.parametrize("rows,D", [(1, 1024), (300, 4096), (64, 5120), (3, 8)])
+def test_add_rmsnorm_forward_backward(cuda, rows, D):
+    """Residual add fused into RMSNorm: h is the bf16 sum torch computes, y is
+    RMSNorm(h) bit for bit, and the input gradient is RMSNorm'(dy) + dh
+    (fp32 sum, one rounding) within 1e-2 of an fp32 reference."""
+    from voodoo_quant import _C
+    from voodoo_quant.fused_blocks import add_rms_norm
+
+    g = torch.Generator(device="cpu").manual_seed(rows * 11 + D)
+    a = (torch.randn(rows, D, generator=g) * 2).to(cuda, torch.bfloat16)
+    res = (torch.randn(rows, D, generator=g) * 3).to(cuda, torch.bfloat16)
+    w = (1 + 0.3 * torch.randn(D, generator=g)).to(cuda, torch.bfloat16)
+    h, y, rstd = _C.add_rmsnorm_fwd(a, res, w, 1e-6)
+    assert torch.equal(h, a + res)
+    y1, rstd1 = _C.rmsnorm_fwd(h, w, 1e-6)
+    assert torch.equal(y, y1) and torch.equal(rstd, rstd1)
+    dy = torch.randn(rows, D, generator=g).to(cuda, torch.bfloat16)
+    dh = torch.randn(rows, D, generator=g).to(cuda, torch.bfloat16)
+    dx = _C.rmsnorm_bwd_add(h, dy, dh, w, rstd)
+    hf = h.float().requires_grad_(True)
+    _rms_ref(hf, w, 1e-6).backward(dy.float())
+    assert _rel(dx, hf.grad + dh.float()) < 1e-2
+    # through autograd: both inputs receive the same gradient
+    af, rf = a.clone().requires_grad_(True), res.clone().requires_grad_(True)
+    hh, yy = add_rms_norm(af, rf, w, 1e-6)
+    torch.autograd.backward([hh, yy], [dh, dy])
+    assert torch.equal(af.grad, dx) and torch.equal(rf.grad, dx)
+
+
 @pytest.mark.parametrize("B,S,Hq,Hk,D", [(2, 33, 4, 2, 128), (1, 8, 3, 1, 64), (2, 16, 8, 8, 16)])
 def test_rope_forward_backward(cuda, B, S, Hq, Hk, D):
     from voodoo_quant import _C
@@ -107,7 +136,8 @@ def test_fused_llama_blocks_match_unpatched_model(cuda):
     shape = S.ModelShape(2, 512, 4, 2, 1536, 2048, False, head_dim=128, batch=2, seq=64)
     ref = S.build_llama(shape, cuda, seed=4)
     fused = S.build_llama(shape, cuda, seed=4)
-    assert fuse_llama_blocks(fused) == 2 * 4 + 1 and fuse_llama_blocks(fused) == 0
+    # per layer: two norms, attention, MLP and the decoder layer (add + norm); plus the final norm
+    assert fuse_llama_blocks(fused) == 2 * 5 + 1 and fuse_llama_blocks(fused) == 0
     x, _ = S.random_tokens(shape, cuda, seed=5)
     e_ref = ref.model.embed_tokens(x).detach().requires_grad_(True)
     e_fus = e_ref.detach().clone().requires_grad_(True)

@@ -60,7 +60,7 @@ def test_fused_blocks_leave_cpu_models_unchanged():
     shape = S.SHAPES["tiny"]
     a = S.build_llama(shape, "cpu", seed=2)
     b = S.build_llama(shape, "cpu", seed=2)
-    assert fuse_llama_blocks(b) == 2 * 4 + 1
+    assert fuse_llama_blocks(b) == 2 * 5 + 1  # per layer: two norms, attention, MLP, decoder add + norm
     x = torch.randint(0, shape.vocab, (1, 16))
     with torch.no_grad():
         assert torch.equal(a(input_ids=x, use_cache=False).logits, b(input_ids=x, use_cache=False).logits)

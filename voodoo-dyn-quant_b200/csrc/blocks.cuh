@@ -70,11 +70,17 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
 }
 
 // One CTA per row (grid-stride); a thread keeps VPT vectors of 8 in registers.
-template <int VPT>
+// kAdd: the input is the residual sum h = bf16(x + res) (a bf16 add, as the
+// model's `residual + hidden_states`), written to h; the norm is taken of h.
+template <int VPT, bool kAdd = false>
 __global__ void __launch_bounds__(kNormThreads) rmsnorm_fwd_kernel(const __nv_bfloat16* __restrict__ x, long long ldx,
                                                                   const __nv_bfloat16* __restrict__ w, float eps,
                                                                   int rows, int D, __nv_bfloat16* __restrict__ y,
-                                                                  long long ldy, float* __restrict__ rstd) {
+                                                                  long long ldy, float* __restrict__ rstd,
+                                                                  const __nv_bfloat16* __restrict__ res = nullptr,
+                                                                  long long ldres = 0,
+                                                                  __nv_bfloat16* __restrict__ h = nullptr,
+                                                                  long long ldh = 0) {
   __shared__ float red[kNormThreads / 32];
   const int nvec = D >> 3;
   for (int row = blockIdx.x; row < rows; row += gridDim.x) {
@@ -86,6 +92,12 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_fwd_kernel(const __nv_bf
       const int c = threadIdx.x + j * kNormThreads;
       if (c < nvec) {
         v[j] = load8(xr + 8 * c);
+        if (kAdd) {
+          const V8 rv = load8(res + static_cast<long long>(row) * ldres + 8 * c);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) v[j].v[i] = bf16_round(v[j].v[i] + rv.v[i]);
+          store8(h + static_cast<long long>(row) * ldh + 8 * c, v[j]);
+        }
 #pragma unroll
         for (int i = 0; i < 8; ++i) ss = fmaf(v[j].v[i], v[j].v[i], ss);
       }
@@ -107,12 +119,16 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_fwd_kernel(const __nv_bf
   }
 }
 
-template <int VPT>
+// kAdd: dx = (the norm's input gradient) + dres in fp32, rounded once: the
+// gradient of a residual sum h that feeds both the norm and a later add.
+template <int VPT, bool kAdd = false>
 __global__ void __launch_bounds__(kNormThreads) rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ x, long long ldx,
                                                                   const __nv_bfloat16* __restrict__ dy, long long lddy,
                                                                   const __nv_bfloat16* __restrict__ w,
                                                                   const float* __restrict__ rstd, int rows, int D,
-                                                                  __nv_bfloat16* __restrict__ dx, long long lddx) {
+                                                                  __nv_bfloat16* __restrict__ dx, long long lddx,
+                                                                  const __nv_bfloat16* __restrict__ dres = nullptr,
+                                                                  long long lddres = 0) {
   __shared__ float red[kNormThreads / 32];
   const int nvec = D >> 3;
   for (int row = blockIdx.x; row < rows; row += gridDim.x) {
@@ -145,6 +161,11 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_bwd_kernel(const __nv_bf
         V8 o;
 #pragma unroll
         for (int i = 0; i < 8; ++i) o.v[i] = r * (g[j].v[i] - n[j].v[i] * m);
+        if (kAdd) {
+          const V8 dv = load8(dres + static_cast<long long>(row) * lddres + 8 * c);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) o.v[i] += dv.v[i];
+        }
         store8(dr + 8 * c, o);
       }
     }

@@ -748,6 +748,71 @@ int vq_rmsnorm_bwd(const void* x, int64_t ldx, const void* dy, int64_t lddy, int
   return 0;
 }
 
+int vq_add_rmsnorm_fwd(const void* a, int64_t lda, const void* res, int64_t ldres, int64_t rows, int64_t D,
+                       const void* weight, float eps, void* h, int64_t ldh, void* y, int64_t ldy, float* rstd,
+                       void* stream) {
+  DeviceScope scope(y);
+  if (D <= 0 || D % 8 != 0 || D > 8 * 8 * vq::blocks::kNormThreads)
+    return fail(VQ_ERR_INVALID, "RMSNorm width %lld must be a positive multiple of 8 up to %d", (long long)D,
+                8 * 8 * vq::blocks::kNormThreads);
+  if (int rc = check_rows16(a, rows, D, lda, "a")) return rc;
+  if (int rc = check_rows16(res, rows, D, ldres, "res")) return rc;
+  if (int rc = check_rows16(h, rows, D, ldh, "h")) return rc;
+  if (int rc = check_rows16(y, rows, D, ldy, "y")) return rc;
+  if (weight == nullptr || !aligned16(weight)) return fail(VQ_ERR_INVALID, "weight must be a 16-byte aligned pointer");
+  if (rows == 0) return 0;
+  if (rows > 0x7fffffff) return fail(VQ_ERR_INVALID, "too many rows");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int vpt = static_cast<int>((D / 8 + vq::blocks::kNormThreads - 1) / vq::blocks::kNormThreads);
+  const int grid = grid_for(rows, 16);
+  const auto* A = static_cast<const __nv_bfloat16*>(a);
+  const auto* R = static_cast<const __nv_bfloat16*>(res);
+  const auto* W = static_cast<const __nv_bfloat16*>(weight);
+  auto* H = static_cast<__nv_bfloat16*>(h);
+  auto* Y = static_cast<__nv_bfloat16*>(y);
+  using namespace vq::blocks;
+  const int n = static_cast<int>(rows), d = static_cast<int>(D);
+  if (vpt <= 1) rmsnorm_fwd_kernel<1, true><<<grid, kNormThreads, 0, st>>>(A, lda, W, eps, n, d, Y, ldy, rstd, R, ldres, H, ldh);
+  else if (vpt <= 2) rmsnorm_fwd_kernel<2, true><<<grid, kNormThreads, 0, st>>>(A, lda, W, eps, n, d, Y, ldy, rstd, R, ldres, H, ldh);
+  else if (vpt <= 4) rmsnorm_fwd_kernel<4, true><<<grid, kNormThreads, 0, st>>>(A, lda, W, eps, n, d, Y, ldy, rstd, R, ldres, H, ldh);
+  else rmsnorm_fwd_kernel<8, true><<<grid, kNormThreads, 0, st>>>(A, lda, W, eps, n, d, Y, ldy, rstd, R, ldres, H, ldh);
+  VQ_CUDA(cudaGetLastError());
+  return 0;
+}
+
+int vq_rmsnorm_bwd_add(const void* x, int64_t ldx, const void* dy, int64_t lddy, const void* dres, int64_t lddres,
+                       int64_t rows, int64_t D, const void* weight, const float* rstd, void* dx, int64_t lddx,
+                       void* stream) {
+  DeviceScope scope(dx);
+  if (D <= 0 || D % 8 != 0 || D > 8 * 8 * vq::blocks::kNormThreads)
+    return fail(VQ_ERR_INVALID, "RMSNorm width %lld must be a positive multiple of 8 up to %d", (long long)D,
+                8 * 8 * vq::blocks::kNormThreads);
+  if (int rc = check_rows16(x, rows, D, ldx, "x")) return rc;
+  if (int rc = check_rows16(dy, rows, D, lddy, "dy")) return rc;
+  if (int rc = check_rows16(dres, rows, D, lddres, "dres")) return rc;
+  if (int rc = check_rows16(dx, rows, D, lddx, "dx")) return rc;
+  if (weight == nullptr || !aligned16(weight)) return fail(VQ_ERR_INVALID, "weight must be a 16-byte aligned pointer");
+  if (rows == 0) return 0;
+  if (rstd == nullptr) return fail(VQ_ERR_INVALID, "null rstd");
+  if (rows > 0x7fffffff) return fail(VQ_ERR_INVALID, "too many rows");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int vpt = static_cast<int>((D / 8 + vq::blocks::kNormThreads - 1) / vq::blocks::kNormThreads);
+  const int grid = grid_for(rows, 16);
+  const auto* X = static_cast<const __nv_bfloat16*>(x);
+  const auto* G = static_cast<const __nv_bfloat16*>(dy);
+  const auto* DR = static_cast<const __nv_bfloat16*>(dres);
+  const auto* W = static_cast<const __nv_bfloat16*>(weight);
+  auto* DX = static_cast<__nv_bfloat16*>(dx);
+  using namespace vq::blocks;
+  const int n = static_cast<int>(rows), d = static_cast<int>(D);
+  if (vpt <= 1) rmsnorm_bwd_kernel<1, true><<<grid, kNormThreads, 0, st>>>(X, ldx, G, lddy, W, rstd, n, d, DX, lddx, DR, lddres);
+  else if (vpt <= 2) rmsnorm_bwd_kernel<2, true><<<grid, kNormThreads, 0, st>>>(X, ldx, G, lddy, W, rstd, n, d, DX, lddx, DR, lddres);
+  else if (vpt <= 4) rmsnorm_bwd_kernel<4, true><<<grid, kNormThreads, 0, st>>>(X, ldx, G, lddy, W, rstd, n, d, DX, lddx, DR, lddres);
+  else rmsnorm_bwd_kernel<8, true><<<grid, kNormThreads, 0, st>>>(X, ldx, G, lddy, W, rstd, n, d, DX, lddx, DR, lddres);
+  VQ_CUDA(cudaGetLastError());
+  return 0;
+}
+
 int vq_rope(const void* q, const int64_t* q_strides, int64_t Hq, const void* k, const int64_t* k_strides, int64_t Hk,
             const void* cos, const void* sin, const int64_t* cs_strides, int64_t B, int64_t S, int64_t D, int backward,
             void* q_out, void* k_out, void* stream) {

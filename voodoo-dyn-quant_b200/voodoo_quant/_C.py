@@ -65,6 +65,8 @@ def _declare(lib):
                                 _i64, _vp]),
         "vq_rmsnorm_fwd": (_int, [_vp, _i64, _i64, _i64, _vp, _f32, _vp, _i64, _vp, _vp]),
         "vq_rmsnorm_bwd": (_int, [_vp, _i64, _vp, _i64, _i64, _i64, _vp, _vp, _vp, _i64, _vp]),
+        "vq_add_rmsnorm_fwd": (_int, [_vp, _i64, _vp, _i64, _i64, _i64, _vp, _f32, _vp, _i64, _vp, _i64, _vp, _vp]),
+        "vq_rmsnorm_bwd_add": (_int, [_vp, _i64, _vp, _i64, _vp, _i64, _i64, _i64, _vp, _vp, _vp, _i64, _vp]),
         "vq_rope": (_int, [_vp, _vp, _i64, _vp, _vp, _i64, _vp, _vp, _vp, _i64, _i64, _i64, _int, _vp, _vp, _vp]),
         "vq_swiglu_fwd": (_int, [_vp, _i64, _vp, _i64, _i64, _i64, _vp, _i64, _vp]),
         "vq_swiglu_bwd": (_int, [_vp, _i64, _vp, _i64, _vp, _i64, _i64, _i64, _vp, _vp, _i64, _vp]),
@@ -81,7 +83,7 @@ EXPORTED = (
     "vq_linear_fwd", "vq_linear_fwd_grouped", "vq_set_gategrad_sm_reserve", "vq_set_gemm_sm_reserve", "vq_quantize", "vq_route_prep", "vq_linear_fwd_mcred", "vq_linear_dx", "vq_gategrad_workspace_bytes", "vq_gategrad", "vq_gategrad_noalloc",
     "vq_mixgemm_fwd",
     "vq_loss_fused", "vq_loss_stats", "vq_loss_combine", "vq_loss_grad",
-    "vq_rmsnorm_fwd", "vq_rmsnorm_bwd", "vq_rope", "vq_swiglu_fwd", "vq_swiglu_bwd",
+    "vq_rmsnorm_fwd", "vq_rmsnorm_bwd", "vq_add_rmsnorm_fwd", "vq_rmsnorm_bwd_add", "vq_rope", "vq_swiglu_fwd", "vq_swiglu_bwd",
 )
 
 
@@ -418,6 +420,40 @@ def rmsnorm_bwd(x: torch.Tensor, dy: torch.Tensor, weight: torch.Tensor, rstd: t
     dx = torch.empty(rows, D, dtype=torch.bfloat16, device=x.device)
     _check(_lib.vq_rmsnorm_bwd(x.data_ptr(), x.stride(0), dy.data_ptr(), dy.stride(0), rows, D, w.data_ptr(),
                                rstd.contiguous().data_ptr(), dx.data_ptr(), dx.stride(0), _stream(x)))
+    return dx
+
+
+def add_rmsnorm_fwd(a: torch.Tensor, res: torch.Tensor, weight: torch.Tensor, eps: float):
+    """(h = a + res, y = RMSNorm(h), rstd) for a, res [rows, D] bf16."""
+    _require_cuda(a, res, weight)
+    a = _rows_operand(a)
+    res = _rows_operand(res)
+    w = weight.to(torch.bfloat16).contiguous()
+    rows, D = a.shape
+    if res.shape != a.shape:
+        raise ValueError(f"add_rmsnorm: shapes {tuple(a.shape)} and {tuple(res.shape)} differ")
+    h = torch.empty(rows, D, dtype=torch.bfloat16, device=a.device)
+    y = torch.empty(rows, D, dtype=torch.bfloat16, device=a.device)
+    rstd = torch.empty(rows, dtype=torch.float32, device=a.device)
+    _check(_lib.vq_add_rmsnorm_fwd(a.data_ptr(), a.stride(0), res.data_ptr(), res.stride(0), rows, D, w.data_ptr(),
+                                   float(eps), h.data_ptr(), h.stride(0), y.data_ptr(), y.stride(0), rstd.data_ptr(),
+                                   _stream(a)))
+    return h, y, rstd
+
+
+def rmsnorm_bwd_add(x: torch.Tensor, dy: torch.Tensor, dres: torch.Tensor, weight: torch.Tensor,
+                    rstd: torch.Tensor) -> torch.Tensor:
+    """RMSNorm input gradient of dy at x, plus dres (fp32 sum, one rounding)."""
+    _require_cuda(x, dy, dres, weight, rstd)
+    x = _rows_operand(x)
+    dy = _rows_operand(dy)
+    dres = _rows_operand(dres)
+    w = weight.to(torch.bfloat16).contiguous()
+    rows, D = x.shape
+    dx = torch.empty(rows, D, dtype=torch.bfloat16, device=x.device)
+    _check(_lib.vq_rmsnorm_bwd_add(x.data_ptr(), x.stride(0), dy.data_ptr(), dy.stride(0), dres.data_ptr(),
+                                   dres.stride(0), rows, D, w.data_ptr(), rstd.contiguous().data_ptr(), dx.data_ptr(),
+                                   dx.stride(0), _stream(x)))
     return dx
 
 

@@ -49,6 +49,34 @@ class _RMSNormFn(Function):
         return (dx.view(gy.shape) if dx is not None else None), dw, None
 
 
+class _AddRMSNormFn(Function):
+    """h = a + res and y = RMSNorm(h) in one kernel (a decoder layer's
+    residual add and the norm after it).  Backward: both inputs get the
+    norm's input gradient plus the gradient reaching h directly, summed in
+    fp32 inside the norm's backward kernel."""
+
+    @staticmethod
+    def forward(ctx, a: torch.Tensor, res: torch.Tensor, weight: torch.Tensor, eps: float):
+        D = a.shape[-1]
+        h, y, rstd = _C.add_rmsnorm_fwd(a.reshape(-1, D), res.reshape(-1, D), weight, eps)
+        ctx.save_for_backward(h, weight, rstd)
+        return h.view(a.shape), y.view(a.shape)
+
+    @staticmethod
+    def backward(ctx, gh: torch.Tensor, gy: torch.Tensor):
+        h, weight, rstd = ctx.saved_tensors
+        D = h.shape[1]
+        gy2 = gy.reshape(-1, D)
+        dx = None
+        if ctx.needs_input_grad[0] or ctx.needs_input_grad[1]:
+            dx = _C.rmsnorm_bwd_add(h, gy2, gh.reshape(-1, D), weight, rstd).view(gy.shape)
+        dw = None
+        if ctx.needs_input_grad[2]:
+            n = (h.float() * rstd[:, None]).to(torch.bfloat16).float()
+            dw = (gy2.float() * n).sum(0).to(weight.dtype)
+        return (dx if ctx.needs_input_grad[0] else None), (dx if ctx.needs_input_grad[1] else None), dw, None
+
+
 class _RopeFn(Function):
     """q [B, S, Hq, D], k [B, S, Hk, D] -> rotated, contiguous [B, S, H, D]."""
 
@@ -84,6 +112,11 @@ class _SwiGLUFn(Function):
 
 def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
     return _RMSNormFn.apply(x, weight, eps)
+
+
+def add_rms_norm(a: torch.Tensor, res: torch.Tensor, weight: torch.Tensor, eps: float):
+    """(a + res, RMSNorm(a + res)) for bf16 [..., D] tensors."""
+    return _AddRMSNormFn.apply(a, res, weight, eps)
 
 
 def rope(q: torch.Tensor, k: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor):
@@ -132,14 +165,39 @@ def _attention_forward(self, hidden_states: torch.Tensor, position_embeddings=No
     return self.o_proj(o), None
 
 
+def _decoder_forward(self, hidden_states: torch.Tensor, attention_mask=None, position_ids=None,
+                     past_key_values=None, use_cache=False, position_embeddings=None, **kwargs):
+    """Hugging Face LlamaDecoderLayer.forward with the residual add after the
+    attention fused into the post-attention RMSNorm."""
+    norm = self.post_attention_layernorm
+    if not (_fusable(hidden_states) and getattr(norm, "weight", None) is not None
+            and norm.weight.dtype == torch.bfloat16 and hasattr(norm, "variance_epsilon")
+            and hidden_states.shape[-1] <= 8192):
+        return self._vq_orig_forward(hidden_states, attention_mask=attention_mask, position_ids=position_ids,
+                                     past_key_values=past_key_values, use_cache=use_cache,
+                                     position_embeddings=position_embeddings, **kwargs)
+    residual = hidden_states
+    x = self.input_layernorm(hidden_states)
+    x, _ = self.self_attn(hidden_states=x, attention_mask=attention_mask, position_ids=position_ids,
+                          past_key_values=past_key_values, use_cache=use_cache,
+                          position_embeddings=position_embeddings, **kwargs)
+    if _fusable(x) and x.shape == residual.shape:
+        h, x = add_rms_norm(x, residual, norm.weight, norm.variance_epsilon)
+    else:
+        h = residual + x
+        x = norm(h)
+    return h + self.mlp(x)
+
+
 def fuse_llama_blocks(model: torch.nn.Module) -> int:
     """Route the RMSNorm, attention (rotary) and MLP (SwiGLU) modules of a
-    Hugging Face Llama model through the fused kernels, in place; returns the
-    number of modules patched.  Idempotent."""
+    Hugging Face Llama model through the fused kernels, and each decoder
+    layer's post-attention residual add into its RMSNorm, in place; returns
+    the number of modules patched.  Idempotent."""
     from transformers.models.llama import modeling_llama as L
 
     table = ((L.LlamaRMSNorm, _rmsnorm_forward), (L.LlamaAttention, _attention_forward),
-             (L.LlamaMLP, _mlp_forward))
+             (L.LlamaMLP, _mlp_forward), (L.LlamaDecoderLayer, _decoder_forward))
     n = 0
     for m in model.modules():
         for cls, fwd in table:

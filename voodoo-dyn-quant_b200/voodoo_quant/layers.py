@@ -856,6 +856,7 @@ class GateBank:
         padded = padded.index_put((self.flat_index,), g)
         p = torch.softmax(padded.view(len(self.layers), self.kmax), dim=1)
         pl = p
+        _DEFERRED.clear()  # nothing left from a backward that did not finish
         if self.defer and torch.is_grad_enabled() and p.requires_grad:
             self._dgrad = torch.zeros(p.shape, dtype=torch.float32, device=p.device)
             pl = _BankTap.apply(p, self)
