@@ -190,13 +190,16 @@ class _CopyToParallel(Function):
     def backward(ctx, g):
         from voodoo_quant import layers
 
-        g = g.clone().contiguous()
         if layers.has_deferred_gategrads():
-            # the module's gate-gradient GEMMs run while the sum is in flight
+            # the module's gate-gradient GEMMs run while the sum is in flight;
+            # g is the sum of this module's gated layers' fresh input
+            # gradients, so it is reduced in place
+            g = g.contiguous()
             work = tp_all_reduce_async(g, overlap=True)
             layers.flush_deferred_gategrads(overlap_bytes=g.numel() * g.element_size())
             work.wait()
         else:
+            g = g.clone().contiguous()
             dist.all_reduce(g, op=dist.ReduceOp.SUM, group=TP.group)
         return g
 
