@@ -86,8 +86,11 @@ class _TPFusedDistillLoss(Function):
     def forward(ctx, s, t, y, vocab_start, temperature, ce_w, kl_w, group):
         stats = _C.loss_stats(s, t, y, vocab_start, temperature)            # [rows, 8]
         world = dist.get_world_size(group)
-        gathered = torch.empty((world,) + tuple(stats.shape), dtype=stats.dtype, device=stats.device)
+        # [world * rows, 8], viewed per rank: gloo wants the ranks stacked along dim 0
+        gathered = torch.empty((world * stats.shape[0],) + tuple(stats.shape[1:]), dtype=stats.dtype,
+                               device=stats.device)
         dist.all_gather_into_tensor(gathered, stats, group=group)
+        gathered = gathered.view((world,) + tuple(stats.shape))
         lse, ce, kl = _C.loss_combine(gathered, temperature)
         ctx.g = _C.loss_grad(s, t, y, vocab_start, temperature, lse, ce_w, kl_w) if s.requires_grad else None
         ctx.s_dtype = s.dtype
