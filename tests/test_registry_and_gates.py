@@ -1,0 +1,101 @@
+"""Host-side behaviour the reference's own unit tests pin, checked against
+this package on CPU (no kernels): the quant-type registry and ladder
+(reference tests/test_ggml.py), the gate temperature and per-role candidate
+menus (tests/test_invariants.py), and the error conventions of the
+boundary."""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+from voodoo_quant import ggml
+from oracle import ggml_blocks
+
+
+def test_registry_ladder_and_sizes():
+    types = ggml.list_quant_types()
+    assert {"IQ4_XS", "Q8_0", "Q2_K", "Q3_K"} <= set(types)
+    ladder = ggml.QUANT_LADDER
+    assert set(ladder) <= set(types)
+    sizes = [ggml.bytes_per_weight(q) for q in ladder]
+    assert sizes == sorted(sizes)  # coarse to fine
+    menu = ggml.default_candidate_types()
+    assert not any(q.startswith("TQ") for q in menu)
+    assert menu[0] == "IQ1_S" and menu[-1] == "Q8_0"
+    assert ggml.bytes_per_weight("Q8_0") == pytest.approx(34 / 32)
+    assert ggml.bytes_per_weight("IQ4_XS") == pytest.approx(136 / 256)
+    assert ggml.bytes_per_weight("Q2_K") == pytest.approx(84 / 256)
+    assert ggml.bytes_per_weight("Q3_K") == pytest.approx(110 / 256)
+    with pytest.raises(ValueError, match="Unknown quant type"):
+        ggml.get_quant_info("NOT_A_TYPE")
+
+
+def test_gpu_formats_match_the_block_layouts():
+    for q in ggml.GPU_FORMATS:
+        info = ggml.get_quant_info(q)
+        type_id, elems, nbytes = ggml_blocks.FORMATS[q]
+        assert (info.block_size, info.block_bytes) == (elems, nbytes), q
+        assert info.ggml_type == type_id, q
+
+
+def test_quantize_without_libggml_is_a_runtime_error():
+    if ggml.find_libggml() is not None:
+        pytest.skip("libggml-base present")
+    with pytest.raises(RuntimeError):
+        ggml.quantize_tensor(torch.zeros(4, 256), "Q4_K")
+
+
+def _layer(types, name="blk.0.mlp.up_proj"):
+    from voodoo_quant.layers import MixedQuantLinear
+    from voodoo_quant.quants import rtn
+
+    w = torch.randn(32, 256, generator=torch.Generator().manual_seed(1)) * 0.02
+    return MixedQuantLinear(256, 32, list(types), w, tensor_name=name,
+                            candidate_bytes={q: rtn.quantize(w, q) for q in types})
+
+
+def test_temperature_concentrates_the_mixture():
+    m = _layer(["Q4_K", "Q6_K", "Q8_0"])
+    with torch.no_grad():
+        m.gates.copy_(torch.tensor([0.1, 0.7, 0.3]))
+    m.set_temperature(1.0)
+    warm = m.soft_probs()
+    m.set_temperature(0.01)
+    cold = m.soft_probs()
+    assert torch.allclose(warm.sum(), torch.tensor(1.0)) and torch.allclose(cold.sum(), torch.tensor(1.0))
+    assert cold.max() > warm.max() and float(cold[1].detach()) > 0.999
+    assert m.get_assignment() == "Q6_K"
+    m.set_temperature(0.0)  # clamped, never a division by zero
+    assert m.temperature > 0 and torch.isfinite(m.soft_probs()).all()
+    # effective bytes: the probability-weighted bytes of the full tensor
+    eb = float(m.effective_bytes().detach())
+    probs = m.soft_probs().detach()
+    want = sum(float(p) * ggml.bytes_per_weight(q) for p, q in zip(probs, m.candidate_types)) * 32 * 256
+    assert eb == pytest.approx(want, rel=1e-6)
+
+
+def test_role_menus():
+    from voodoo_quant.layers import resolve_candidate_types
+
+    base = ["Q2_K", "Q3_K", "Q4_K", "Q5_K", "Q6_K", "Q8_0"]
+    attn, other = ["Q4_K", "Q5_K", "Q6_K", "Q8_0"], ["Q2_K", "Q3_K", "Q4_K"]
+    assert resolve_candidate_types("model.layers.0.self_attn.q_proj", base) == base
+    assert resolve_candidate_types("model.layers.0.self_attn.q_proj", base, attn, other) == attn
+    assert resolve_candidate_types("model.layers.0.mlp.down_proj", base, attn, other) == other
+    # a role menu never adds types outside the base menu
+    assert resolve_candidate_types("model.layers.0.mlp.up_proj", ["Q4_K", "Q8_0"], attn, other) == ["Q4_K"]
+
+
+def test_boundary_error_conventions():
+    from voodoo_quant.layers import MixedQuantLinear
+
+    w = torch.zeros(32, 256)
+    with pytest.raises(ValueError, match="Unknown quant type"):
+        MixedQuantLinear(256, 32, ["NOT_A_TYPE"], w)
+    with pytest.raises(ValueError, match="no B200 decoder"):
+        MixedQuantLinear(256, 32, ["IQ2_XS"], w)
+    m = _layer(["Q4_K", "Q8_0"])
+    with pytest.raises(RuntimeError):  # no CPU fallback for the gated forward
+        m(torch.zeros(2, 256))
+    assert issubclass(MixedQuantLinear, torch.nn.Module)
