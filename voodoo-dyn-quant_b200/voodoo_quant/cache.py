@@ -22,6 +22,7 @@ six candidates holds ~29 GB of packed blocks, well inside 180 GB of HBM.
 from __future__ import annotations
 
 import os
+import threading
 import weakref
 from dataclasses import dataclass
 from pathlib import Path
@@ -95,6 +96,7 @@ def pack_arena(types: list[str], qbytes: list[torch.Tensor], rows: int, padded_c
 _STAGE_BYTES = 64 << 20
 _STAGE_MIN = 1 << 20
 _stage_bufs: list[torch.Tensor] = []
+_stage_lock = threading.Lock()  # one upload at a time owns the staging buffers
 
 
 def _staging_buffers() -> list[torch.Tensor]:
@@ -107,7 +109,12 @@ def upload_staged(dst: torch.Tensor, pieces: list[tuple[int, torch.Tensor]]) -> 
     """Copy host uint8 tensors into the device tensor `dst` at byte offsets
     (`pieces` = [(offset, host tensor)]) through double-buffered pinned
     staging on a side stream; returns the bytes copied.  The caller's stream
-    waits for the copies."""
+    waits for the copies.  Thread-safe: concurrent calls take turns."""
+    with _stage_lock:
+        return _upload_staged(dst, pieces)
+
+
+def _upload_staged(dst: torch.Tensor, pieces: list[tuple[int, torch.Tensor]]) -> int:
     bufs = _staging_buffers()
     dev = dst.device
     side = torch.cuda.Stream(device=dev)
