@@ -805,8 +805,8 @@ def main():
     ap.add_argument("--no-graph", action="store_true", help="time the eager step instead of a CUDA graph of it")
     ap.add_argument("--overlap-sms", type=int, default=-1,
                     help="TP: SMs the gate-gradient GEMMs leave to the concurrent input-gradient all-reduces, which "
-                         "run on a communicator capped to that many CTAs (default: 24 with more than one GPU, "
-                         "0 otherwise; 24 measured best at TP-2)")
+                         "run on a communicator capped to that many CTAs (default: 32 with more than one GPU, "
+                         "0 otherwise)")
     ap.add_argument("--dx-chunks", type=int, default=-1,
                     help="layer workload under TP: row chunks of dX, each all-reduced while the next is computed "
                          "(default: 2 with more than one GPU; TP-8 0.606 -> 0.585 ms per step)")
@@ -821,7 +821,10 @@ def main():
     ap.add_argument("--ncu-case", action="store_true", help="one launch per kernel at profiling sizes")
     args = ap.parse_args()
     if args.overlap_sms < 0:
-        args.overlap_sms = 24 if int(os.environ.get("WORLD_SIZE", "1")) > 1 else 0
+        # NCCL's default channel count here: at TP-2 it measured 1.262 ms per
+        # layer step against 1.286 ms with 24 (and 1.30 ms without overlap);
+        # with more ranks the all-reduce outlasts the gate-gradient GEMM
+        args.overlap_sms = 32 if int(os.environ.get("WORLD_SIZE", "1")) > 1 else 0
     if args.dx_chunks < 0:
         args.dx_chunks = 2 if int(os.environ.get("WORLD_SIZE", "1")) > 1 else 1
     if args.ncu_case:
