@@ -99,3 +99,36 @@ def test_boundary_error_conventions():
     with pytest.raises(RuntimeError):  # no CPU fallback for the gated forward
         m(torch.zeros(2, 256))
     assert issubclass(MixedQuantLinear, torch.nn.Module)
+
+
+def test_row_chunks_cover_rows_on_256_boundaries():
+    from voodoo_quant.layers import _row_chunks
+
+    for T, n in [(600, 3), (8192, 2), (100, 4), (257, 2), (4096, 1)]:
+        ch = _row_chunks(T, n)
+        assert ch[0][0] == 0 and ch[-1][1] == T
+        assert all(a < b for a, b in ch) and all(ch[i][1] == ch[i + 1][0] for i in range(len(ch) - 1))
+        assert all(a % 256 == 0 for a, _ in ch) and len(ch) <= max(n, 1)
+
+
+def test_bank_routing_on_cpu():
+    """One batched Gumbel-argmax draw per step for every layer: padding
+    candidates are never chosen, each layer's shares follow its
+    probabilities, and a second request of the same size reuses the draw."""
+    from voodoo_quant.layers import GateBank
+
+    mods = {"a": _layer(["Q4_K", "Q8_0"], "l.a"), "b": _layer(["Q4_K", "Q5_K", "Q6_K", "Q8_0"], "l.b")}
+    with torch.no_grad():
+        mods["a"].gates.copy_(torch.tensor([0.4, -0.4]))
+        mods["b"].gates.copy_(torch.tensor([1.0, 0.0, -1.0, 0.5]))
+    bank = GateBank(mods)
+    bank.probs()
+    torch.manual_seed(0)
+    for m in mods.values():
+        r = bank.routing(m, 100000).long()
+        assert int(r.max()) < m.num_candidates
+        shares = torch.bincount(r, minlength=m.num_candidates).double() / r.numel()
+        assert torch.allclose(shares, m.get_probs().detach().double(), atol=8e-3)
+        assert torch.equal(bank.routing(m, 100000), r.to(torch.uint8))
+    bank.release()
+    assert mods["a"].__dict__.get("_bank_probs") is None
