@@ -233,3 +233,39 @@ def test_tp2_llama_model_matches_unsharded():
         e0, e1 = r["emb_rows"]
         assert torch.allclose(r["emb_grad"], m.model.embed_tokens.weight.grad[e0:e1], rtol=1e-9, atol=1e-12)
     assert rs[0]["v"][1] == rs[1]["v"][0] and rs[1]["v"][1] == 1000
+
+
+def _init_worker(rank, world, port, outdir):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), WORLD_SIZE=str(world), RANK=str(rank),
+                      LOCAL_RANK=str(rank))
+    from voodoo_quant import parallel as P
+
+    r, w = P.init_tp(backend="gloo", timeout_min=2)
+    res = {"rank": r, "world": w, "enabled": P.TP.enabled, "main": P.is_main_process()}
+    t = torch.full((3,), float(rank + 7))
+    P.tp_broadcast(t, src=1)
+    res["bcast"] = t.tolist()
+    gates = [torch.zeros(2, requires_grad=True), torch.zeros(3, requires_grad=True)]
+    for i, g in enumerate(gates):
+        g.grad = torch.arange(g.numel(), dtype=torch.float32) + 10 * i + rank
+    P.all_reduce_gate_grads(gates)
+    res["gates"] = [g.grad.tolist() for g in gates]
+    P.barrier()
+    P.tp_finalize()
+    res["after"] = (P.TP.enabled, P.TP.rank, P.TP.world_size)
+    torch.save(res, os.path.join(outdir, f"i{rank}.pt"))
+
+
+def test_env_init_broadcast_gate_grads_and_finalize():
+    """tp_init from torchrun-style env (reference parallel.py:44-96), broadcast,
+    the flat gate-gradient all-reduce and tp_finalize, over gloo."""
+    world = 2
+    with tempfile.TemporaryDirectory() as td:
+        mp.start_processes(_init_worker, args=(world, _free_port(), td), nprocs=world, join=True,
+                           start_method="spawn")
+        rs = [torch.load(os.path.join(td, f"i{r}.pt")) for r in range(world)]
+    for r, res in enumerate(rs):
+        assert (res["rank"], res["world"], res["enabled"], res["main"]) == (r, world, True, r == 0)
+        assert res["bcast"] == [8.0, 8.0, 8.0]
+        assert res["gates"] == [[1.0, 3.0], [21.0, 23.0, 25.0]]
+        assert res["after"] == (False, 0, 1)
