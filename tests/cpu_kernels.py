@@ -138,12 +138,33 @@ def _loss_grad(s, t, targets, vocab_start, temperature, row_lse, ce_weight, kl_w
     return g.to(torch.bfloat16)
 
 
+def _route_prep(keys, K):
+    k = keys.to(torch.int64).reshape(-1).clamp(max=K - 1)
+    order = torch.argsort(k, stable=True)
+    inv = torch.empty_like(order)
+    inv[order] = torch.arange(order.numel())
+    off = torch.zeros(K + 1, dtype=torch.int32)
+    off[1:] = torch.cumsum(torch.bincount(k, minlength=K), 0).to(torch.int32)
+    return order, inv, off
+
+
+def _linear_fwd_grouped(x, ws, n_out, in_features, group_off, out=None):
+    y = torch.empty(x.shape[0], n_out, dtype=torch.bfloat16) if out is None else out
+    off = group_off.tolist()
+    for g, w in enumerate(ws):
+        a, b = off[g], off[g + 1]
+        if b > a:
+            y[a:b] = _linear_fwd(x[a:b], w, n_out, in_features)
+    return y
+
+
 def install():
     from voodoo_quant import _C
     from voodoo_quant.layers import _MixedQuantBase
 
     table = [(_C, "mix", _mix), (_C, "linear_fwd", _linear_fwd), (_C, "linear_dx", _linear_dx),
              (_C, "gategrad", _gategrad), (_C, "dequant", _dequant), (_C, "loss_fused", _loss_fused),
+             (_C, "route_prep", _route_prep), (_C, "linear_fwd_grouped", _linear_fwd_grouped),
              (_C, "loss_stats", _loss_stats), (_C, "loss_combine", _loss_combine), (_C, "loss_grad", _loss_grad),
              (_C, "gategrad_workspace_bytes", lambda n, k, c: 4),
              (_C, "set_gategrad_sm_reserve", lambda n: None), (_C, "set_gemm_sm_reserve", lambda n: None),

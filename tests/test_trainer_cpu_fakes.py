@@ -123,3 +123,33 @@ def test_tp2_step_matches_one_process_with_and_without_overlap():
     # both ranks hold the same (all-reduced) gate gradients
     for n in ref[1]:
         assert torch.equal(rs[0]["plain"][1][n], rs[1]["plain"][1][n]), n
+
+
+def test_ptqr_step_with_concentrated_gates_equals_the_mixture():
+    """PTQR routes each token to one sampled candidate; with every gate
+    distribution concentrated on one candidate (low temperature, large gate
+    margin) the routed step and the mixture step give the same loss."""
+    import cpu_kernels
+    from voodoo_quant.layers import set_ptqr
+    from voodoo_quant.training import synthetic as S
+    from voodoo_quant.training.trainer import StepArgs, build_distill
+
+    _shapes()
+    undo = cpu_kernels.install()
+    out = {}
+    try:
+        for ptqr in (False, True):
+            args = StepArgs(max_steps=4, ce_reduction="tokens", ptqr=ptqr, temp_start=0.05, temp_end=0.05)
+            trainer, shape = build_distill("cpu_tied", "cpu", seed=3, args=args)
+            for m in trainer.replaced.values():
+                with torch.no_grad():
+                    m.gates.zero_()
+                    m.gates[-1] = 5.0  # the last candidate wins with probability ~1 at tau = 0.05
+            x, y = S.random_tokens(shape, "cpu", seed=5)
+            r = trainer.forward_backward(x, y)
+            out[ptqr] = float(r["loss"])
+            assert all(torch.isfinite(m.gates.grad).all() for m in trainer.replaced.values())
+    finally:
+        set_ptqr(False)
+        undo()
+    assert abs(out[True] - out[False]) <= 1e-4 * abs(out[False]), out
