@@ -269,3 +269,144 @@ def test_env_init_broadcast_gate_grads_and_finalize():
         assert res["bcast"] == [8.0, 8.0, 8.0]
         assert res["gates"] == [[1.0, 3.0], [21.0, 23.0, 25.0]]
         assert res["after"] == (False, 0, 1)
+
+
+def _qwen35(seed=0):
+    from transformers.models.qwen3_5 import configuration_qwen3_5 as C, modeling_qwen3_5 as M
+
+    cfg = C.Qwen3_5TextConfig(vocab_size=512, hidden_size=256, intermediate_size=512, num_hidden_layers=2,
+                              num_attention_heads=4, num_key_value_heads=2, head_dim=64, linear_num_key_heads=2,
+                              linear_num_value_heads=4, linear_key_head_dim=64, linear_value_head_dim=64,
+                              layer_types=["linear_attention", "full_attention"])
+    torch.manual_seed(seed)
+    return M.Qwen3_5ForCausalLM(cfg).float().eval()
+
+
+def _qwen35_worker(rank, world, port, outdir):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    import torch.distributed as dist
+    from voodoo_quant import parallel as P
+
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        P.adopt_process_group(0)
+        m = _qwen35()
+        for layer in m.model.layers:
+            if hasattr(layer, "linear_attn"):
+                P.tp_ssm(layer.linear_attn)
+            if hasattr(layer, "self_attn"):
+                P.tp_attention(layer.self_attn)
+            P.tp_mlp(layer.mlp)
+        x = torch.randint(0, 512, (2, 24), generator=torch.Generator().manual_seed(1))
+        with torch.no_grad():
+            y = m(input_ids=x, use_cache=False).logits
+        gdn = m.model.layers[0].linear_attn
+        torch.save({"y": y, "dims": (gdn.key_dim, gdn.value_dim, gdn.num_v_heads, gdn.conv_dim,
+                                     tuple(gdn.conv1d.weight.shape))}, os.path.join(outdir, f"q{rank}.pt"))
+    finally:
+        P.reset_tp()
+        dist.destroy_process_group()
+
+
+def test_qwen35_tp2_gated_attention_and_deltanet_match_unsharded():
+    """tp_attention (per-head q|gate pairs) and tp_ssm (Gated DeltaNet by
+    value heads, with the depthwise conv and per-head parameters made
+    rank-local) on a tiny Hugging Face Qwen3.5 text model: the TP-2 logits
+    equal the unsharded model's (fp32, 1e-5 relative)."""
+    pytest.importorskip("transformers.models.qwen3_5")
+    world = 2
+    with tempfile.TemporaryDirectory() as td:
+        mp.start_processes(_qwen35_worker, args=(world, _free_port(), td), nprocs=world, join=True,
+                           start_method="spawn")
+        rs = [torch.load(os.path.join(td, f"q{r}.pt")) for r in range(world)]
+    ref_model = _qwen35()
+    x = torch.randint(0, 512, (2, 24), generator=torch.Generator().manual_seed(1))
+    with torch.no_grad():
+        ref = ref_model(input_ids=x, use_cache=False).logits
+    for r in rs:
+        assert r["dims"] == (64, 128, 2, 256, (256, 1, 4))
+        assert float((r["y"] - ref).norm()) <= 1e-5 * float(ref.norm())
+
+
+_HEAD_LOCAL_NORMS = ("linear_attn.norm", "q_norm", "k_norm", "q_layernorm", "k_layernorm")
+
+
+def _hybrid(kind: str):
+    """Tiny fp64 Qwen3.5 (Gated DeltaNet + gated attention) or LFM2
+    (short conv + GQA attention) causal LM with seeded weights."""
+    torch.manual_seed(11)
+    if kind == "qwen35":
+        from transformers.models.qwen3_5 import configuration_qwen3_5 as C, modeling_qwen3_5 as M
+
+        cfg = C.Qwen3_5TextConfig(vocab_size=512, hidden_size=256, intermediate_size=512, num_hidden_layers=2,
+                                  num_attention_heads=4, num_key_value_heads=2, head_dim=64,
+                                  linear_num_key_heads=2, linear_num_value_heads=4, linear_key_head_dim=64,
+                                  linear_value_head_dim=64, layer_types=["linear_attention", "full_attention"])
+        m = M.Qwen3_5ForCausalLM(cfg)
+    else:
+        from transformers.models.lfm2 import configuration_lfm2 as C, modeling_lfm2 as M
+
+        cfg = C.Lfm2Config(vocab_size=512, hidden_size=256, intermediate_size=512, num_hidden_layers=2,
+                           num_attention_heads=4, num_key_value_heads=2, layer_types=["conv", "full_attention"])
+        m = M.Lfm2ForCausalLM(cfg)
+    m = m.double().eval()
+    with torch.no_grad():
+        for n, p in m.named_parameters():
+            if p.dim() >= 2:
+                p.copy_(torch.randn_like(p) * 0.05)
+    ids = torch.randint(0, 512, (2, 16), generator=torch.Generator().manual_seed(2))
+    G = torch.randn(2, 16, 512, dtype=torch.float64, generator=torch.Generator().manual_seed(4))
+    return m, ids, G
+
+
+def _hybrid_worker(rank, world, port, outdir, kind):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    import torch.distributed as dist
+    from voodoo_quant import parallel as P
+
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        P.adopt_process_group(0)
+        m, ids, G = _hybrid(kind)
+        P.tp_patch_model(m, verbose=False)
+        v0, v1 = m.lm_head.tp_vocab_start, m.lm_head.tp_vocab_end
+        logits = m(input_ids=ids, use_cache=False).logits
+        (logits * G[..., v0:v1]).sum().backward()
+        norms = {n: p.grad.clone() for n, p in m.named_parameters() if "norm" in n and p.grad is not None}
+        torch.save({"logits": logits.detach(), "v": (v0, v1), "norms": norms}, os.path.join(outdir, f"h{rank}.pt"))
+    finally:
+        P.reset_tp()
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("kind", ["qwen35", "lfm2"])
+def test_tp2_hybrid_adapters_match_unsharded(kind):
+    """tp_patch_model through the Qwen3.5 hybrid and LFM2 adapters: the TP-2
+    vocabulary-shard logits equal the unsharded model's (1e-6 relative: the
+    models compute parts in fp32), and every norm applied to the full hidden
+    state gets the unsharded gradient on every rank (exact input-gradient
+    operators at every sharded block)."""
+    pytest.importorskip(f"transformers.models.{'qwen3_5' if kind == 'qwen35' else 'lfm2'}")
+    with tempfile.TemporaryDirectory() as td:
+        mp.start_processes(_hybrid_worker, args=(2, _free_port(), td, kind), nprocs=2, join=True,
+                           start_method="spawn")
+        rs = [torch.load(os.path.join(td, f"h{r}.pt")) for r in range(2)]
+    m, ids, G = _hybrid(kind)
+    logits = m(input_ids=ids, use_cache=False).logits
+    (logits * G).sum().backward()
+    ref = dict(m.named_parameters())
+    for r in rs:
+        v0, v1 = r["v"]
+        ref_l = logits.detach()[..., v0:v1]
+        assert float((r["logits"] - ref_l).norm()) <= 1e-6 * float(ref_l.norm()), \
+            float((r["logits"] - ref_l).norm() / ref_l.norm())
+        assert r["norms"], "no norm gradients recorded"
+        for n, g in r["norms"].items():
+            if not any(k in n for k in _HEAD_LOCAL_NORMS):
+                assert float((g - ref[n].grad).norm()) <= 1e-5 * float(ref[n].grad.norm()) + 1e-12, n
+    # per-head norms run on each rank's own heads: their gradients are
+    # partial sums that add up to the unsharded one
+    for n in rs[0]["norms"]:
+        if any(k in n for k in _HEAD_LOCAL_NORMS):
+            total = rs[0]["norms"][n] + rs[1]["norms"][n]
+            assert float((total - ref[n].grad).norm()) <= 1e-5 * float(ref[n].grad.norm()) + 1e-12, n

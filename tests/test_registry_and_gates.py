@@ -132,3 +132,50 @@ def test_bank_routing_on_cpu():
         assert torch.equal(bank.routing(m, 100000), r.to(torch.uint8))
     bank.release()
     assert mods["a"].__dict__.get("_bank_probs") is None
+
+
+def test_reference_helpers_kept_for_drop_in():
+    """Names the reference's trainer and tools import from layers / parallel
+    exist and behave as there (layers.py:225-295, :821-836, :947-960;
+    parallel.py:393-408)."""
+    from voodoo_quant import layers, parallel
+    from voodoo_quant.quants import rtn
+
+    assert layers._format_duration(None) == "..." and layers._format_duration(4.23) == "4.2s"
+    assert layers._format_duration(123) == "2m03s" and layers._format_duration(3 * 3600 + 7 * 60) == "3h07m"
+    assert layers._quant_info_for("Q4_K").block_bytes == 144
+    layers.set_st_gumbel(False, 0.5, 1.0)
+    layers.set_st_gumbel_anneal(0.1, 0.9, 100)
+    layers.st_gumbel_step(3)
+    with pytest.raises(NotImplementedError):
+        layers.set_st_gumbel(True, 0.5, 1.0)
+    layers.install_heap_dump_handler()
+    w = torch.randn(12, 256, generator=torch.Generator().manual_seed(3))
+    full = rtn.quantize(w, "Q8_0")
+    assert torch.equal(parallel._slice_q8_bytes(full, 12, 256, row_range=(4, 9)), rtn.quantize(w[4:9], "Q8_0"))
+    assert torch.equal(parallel._slice_q8_bytes(full, 12, 256, col_range=(64, 192)),
+                       rtn.quantize(w[:, 64:192].contiguous(), "Q8_0"))
+    idx = torch.tensor([7, 1, 3])
+    assert torch.equal(parallel._slice_q8_bytes(full, 12, 256, row_index=idx), rtn.quantize(w[idx], "Q8_0"))
+    with pytest.raises(ValueError, match="32-aligned"):
+        parallel._slice_q8_bytes(full, 12, 256, col_range=(16, 80))
+
+
+def test_architecture_adapters():
+    from types import SimpleNamespace
+
+    from voodoo_quant.arch import adapter_for_config, adapter_for_gguf_arch
+
+    names = {t: adapter_for_config(SimpleNamespace(model_type=t)).__name__
+             for t in ("llama", "qwen3", "qwen3_5", "qwen3_5_text", "lfm2")}
+    assert names == {"llama": "LlamaDenseAdapter", "qwen3": "LlamaDenseAdapter", "qwen3_5": "QwenHybridAdapter",
+                     "qwen3_5_text": "QwenHybridAdapter", "lfm2": "LFM2Adapter"}
+    assert adapter_for_config(SimpleNamespace(model_type="gpt2")) is None
+    lfm = adapter_for_gguf_arch("lfm2")
+    assert lfm.gguf_name("model.layers.3.conv.in_proj.weight") == "blk.3.shortconv.in_proj.weight"
+    assert lfm.gguf_name("model.layers.0.self_attn.out_proj.weight") == "blk.0.attn_output.weight"
+    assert lfm.gguf_name("model.layers.5.feed_forward.w3.weight") == "blk.5.ffn_up.weight"
+    assert lfm.gguf_name("model.embed_tokens.weight") == "token_embd.weight" and lfm.transpose_embedding()
+    assert lfm.gguf_name("lm_head.weight") is None
+    assert adapter_for_gguf_arch("qwen35").gguf_name("model.layers.0.mlp.up_proj.weight") is None
+    assert adapter_for_gguf_arch("qwen35").is_attention_tensor("model.layers.0.linear_attn.in_proj_qkv.weight")

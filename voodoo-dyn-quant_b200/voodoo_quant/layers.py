@@ -75,6 +75,108 @@ def set_ptqr(enabled: bool) -> None:
     _PTQR_STATE.enabled = bool(enabled)
 
 
+# --------------------------------------------------------------------------- ST-Gumbel switches
+# The reference's straight-through Gumbel hardening (layers.py:821-846,
+# trainer --st_gumbel) routes a fraction of tokens through hard one-hot
+# candidates.  No benchmark configuration uses it and this path does not
+# implement it; the switches keep the reference's names so its trainer
+# imports and runs unchanged with the feature off, and turning it on fails
+# loudly instead of silently training something else.
+class _STGumbelState:
+    enabled = False
+    fraction = 0.0
+    gs_tau = 1.0
+    f_start = None
+    f_end = None
+    total_steps = 1
+    step = 0
+
+
+_ST_GUMBEL_STATE = _STGumbelState()
+
+
+def set_st_gumbel(enabled: bool, fraction: float = 0.0, gs_tau: float = 1.0) -> None:
+    if enabled:
+        raise NotImplementedError("ST-Gumbel hardening is not implemented on the B200 path; use PTQR (set_ptqr)")
+    _ST_GUMBEL_STATE.enabled = False
+    _ST_GUMBEL_STATE.fraction = float(fraction)
+    _ST_GUMBEL_STATE.gs_tau = float(gs_tau)
+
+
+def set_st_gumbel_anneal(f_start: float, f_end: float, total_steps: int) -> None:
+    _ST_GUMBEL_STATE.f_start = float(f_start)
+    _ST_GUMBEL_STATE.f_end = float(f_end)
+    _ST_GUMBEL_STATE.total_steps = max(int(total_steps), 1)
+
+
+def st_gumbel_step(step: int) -> None:
+    _ST_GUMBEL_STATE.step = int(step)
+
+
+# --------------------------------------------------------------------------- diagnostics and helpers
+def _heap_census(signum, frame) -> None:
+    """SIGUSR1: print live Python objects by type and CPU tensor bytes by dtype
+    (the reference's host-memory census, layers.py:225-274)."""
+    import collections
+    import gc
+
+    by_type, cpu_bytes = collections.Counter(), collections.Counter()
+    for obj in gc.get_objects():
+        try:
+            by_type[type(obj).__name__] += 1
+            if torch.is_tensor(obj) and obj.device.type == "cpu":
+                cpu_bytes[str(obj.dtype)] += obj.numel() * obj.element_size()
+        except Exception:
+            pass
+    lines = ["[heap-dump] top types:"] + [f"  {n}: {c}" for n, c in by_type.most_common(12)]
+    lines += ["[heap-dump] cpu tensor bytes by dtype:"] + [f"  {n}: {c}" for n, c in cpu_bytes.most_common(8)]
+    print("\n".join(lines), flush=True)
+
+
+def install_heap_dump_handler() -> None:
+    """Arm the SIGUSR1 heap census (a no-op where signals cannot be set)."""
+    try:
+        import signal
+
+        signal.signal(signal.SIGUSR1, _heap_census)
+    except Exception:
+        pass
+
+
+def _format_duration(seconds: float | None) -> str:
+    """Short duration text ('4.2s', '2m03s', '1h07m'); '...' when unknown."""
+    if seconds is None or seconds != seconds or seconds == float("inf"):
+        return "..."
+    seconds = max(float(seconds), 0.0)
+    if seconds < 60:
+        return f"{seconds:.1f}s"
+    m, s_ = divmod(int(seconds), 60)
+    if m < 60:
+        return f"{m}m{s_:02d}s"
+    h, m = divmod(m, 60)
+    return f"{h}h{m:02d}m"
+
+
+def _quant_info_for(quant_type: str):
+    """Block size / bytes of a quant type (reference layers.py:293-295)."""
+    return get_quant_info(quant_type)
+
+
+def dequantize_tensor_gpu(qweight: torch.Tensor, quant_type: str, out_features: int, in_features: int,
+                          device) -> torch.Tensor:
+    """Packed blocks -> bf16 [out_features, in_features] on `device`
+    (reference layers.py:298-319): the sm_100a decoder for the B200 formats,
+    the host decoder (libggml) for the others, as the reference falls back."""
+    device = torch.device(device)
+    if quant_type in GPU_FORMATS and device.type == "cuda":
+        w = _C.dequant(qweight.to(device), quant_type, out_features, in_features)
+    else:
+        from voodoo_quant.ggml import dequantize_tensor
+
+        w = dequantize_tensor(qweight.cpu(), quant_type, out_features, in_features).to(device)
+    return w[:, :in_features].to(torch.bfloat16)
+
+
 def _sample_token_routing(probs: torch.Tensor, num_tokens: int) -> torch.Tensor:
     """k*(t) ~ Categorical(probs) per token by Gumbel-argmax (reference :868-881).
 

@@ -639,6 +639,96 @@ def tp_attention_dense(attn: nn.Module, num_heads: int, num_kv_heads: int, head_
     _install_input_copy(attn)
 
 
+def tp_attention(attn: nn.Module) -> None:
+    """Gated attention whose q_proj emits a (q | gate) pair per head (the
+    reference's Qwen3.5 adapter, parallel.py:563-591): q_proj, k_proj and
+    v_proj split into contiguous equal row ranges -- whole heads, each head's
+    q and gate together -- and o_proj by the matching input columns; the
+    module's own forward then runs on the local heads."""
+    tp, r = TP.world_size, TP.rank
+    q, k, o = attn.q_proj, attn.k_proj, attn.o_proj
+    head_dim = getattr(attn, "head_dim", 0) or 1
+    if q.out_features % tp:
+        raise ValueError(f"q_proj out {q.out_features} not divisible by tp={tp}")
+    if k.out_features % (tp * head_dim):
+        raise ValueError(f"k_proj out {k.out_features} does not split into whole heads over tp={tp} "
+                         f"(head_dim {head_dim}); the TP degree must divide the KV-head count")
+    nq = q.out_features // tp
+    _shard_child(attn, "q_proj", row_offset=r * nq, row_len=nq)
+    for name in ("k_proj", "v_proj"):
+        m = getattr(attn, name)
+        if m.out_features % tp:
+            raise ValueError(f"{name} out {m.out_features} not divisible by tp={tp}")
+        n = m.out_features // tp
+        _shard_child(attn, name, row_offset=r * n, row_len=n)
+    if o.in_features % tp:
+        raise ValueError(f"o_proj in {o.in_features} not divisible by tp={tp}")
+    no = o.in_features // tp
+    _shard_child(attn, "o_proj", col_offset=r * no, col_len=no)
+    attn.tp_heads_local = q.out_features // (2 * head_dim * tp)
+    _install_input_copy(attn)
+
+
+def tp_ssm(gdn: nn.Module) -> None:
+    """Gated DeltaNet block sharded by value heads, key heads in lockstep (the
+    reference's Qwen3.5 adapter, parallel.py:594-646).
+
+    in_proj_qkv emits [q (key_dim) | k (key_dim) | v (value_dim)]; the rank
+    keeps its slice of each of the three, concatenated in that order, which is
+    also the channel order of the depthwise conv and of the module's split,
+    so the conv, the per-head dt_bias / A_log and the dimension attributes are
+    made rank-local the same way and the stock forward runs unchanged.
+    in_proj_z / in_proj_b / in_proj_a split by rows, out_proj by columns.
+    """
+    tp, r = TP.world_size, TP.rank
+    kd, vd, nv = gdn.key_dim, gdn.value_dim, gdn.num_v_heads
+    if kd % tp or vd % tp or nv % tp or gdn.num_k_heads % tp:
+        raise ValueError(f"SSM dims (key {kd}, value {vd}, v-heads {nv}, k-heads {gdn.num_k_heads}) "
+                         f"not divisible by tp={tp}")
+    kl, vl, nvl = kd // tp, vd // tp, nv // tp
+    keep = torch.cat([torch.arange(r * kl, (r + 1) * kl), torch.arange(kd + r * kl, kd + (r + 1) * kl),
+                      torch.arange(2 * kd + r * vl, 2 * kd + (r + 1) * vl)])
+    _shard_child(gdn, "in_proj_qkv", row_index=keep)
+    _shard_child(gdn, "in_proj_z", row_offset=r * vl, row_len=vl)
+    _shard_child(gdn, "in_proj_b", row_offset=r * nvl, row_len=nvl)
+    _shard_child(gdn, "in_proj_a", row_offset=r * nvl, row_len=nvl)
+    _shard_child(gdn, "out_proj", col_offset=r * vl, col_len=vl)
+    conv = gdn.conv1d
+    channels = 2 * kl + vl
+    pad = conv.padding[0] if isinstance(conv.padding, tuple) else conv.padding
+    local = nn.Conv1d(channels, channels, kernel_size=conv.kernel_size, groups=channels, padding=pad,
+                      bias=conv.bias is not None)
+    with torch.no_grad():
+        local.weight.copy_(conv.weight.data[keep.to(conv.weight.device)])
+        if conv.bias is not None:
+            local.bias.copy_(conv.bias.data[keep.to(conv.bias.device)])
+    gdn.conv1d = local.to(conv.weight.device, conv.weight.dtype)
+    with torch.no_grad():
+        gdn.dt_bias.data = gdn.dt_bias.data[r * nvl:(r + 1) * nvl].clone()
+        gdn.A_log.data = gdn.A_log.data[r * nvl:(r + 1) * nvl].clone()
+    gdn.num_v_heads, gdn.num_k_heads = nvl, gdn.num_k_heads // tp
+    gdn.key_dim, gdn.value_dim, gdn.conv_dim = kl, vl, channels
+    _install_input_copy(gdn)
+
+
+def _slice_q8_bytes(qb: torch.Tensor, full_out: int, full_in: int, row_index=None, row_range=None,
+                    col_range=None) -> torch.Tensor:
+    """Rank-local Q8_0 bytes ([nblocks, 34], 32 weights per block) of a full
+    tensor's blocks, by row index, row range and/or 32-aligned column range
+    (reference parallel.py:393-408)."""
+    q = qb.reshape(full_out, full_in // 32, 34)
+    if row_index is not None:
+        q = q[row_index.to(q.device)]
+    elif row_range is not None:
+        q = q[row_range[0]:row_range[1]]
+    if col_range is not None:
+        c0, c1 = col_range
+        if c0 % 32 or (c1 - c0) % 32:
+            raise ValueError(f"Q8_0 column slice [{c0}:{c1}] not 32-aligned")
+        q = q[:, c0 // 32:c1 // 32]
+    return q.reshape(-1, 34).contiguous()
+
+
 def _shard_lm_head(model: nn.Module) -> None:
     head, holder = None, None
     for h, attr in ((model, "lm_head"), (getattr(model, "model", None), "lm_head")):
