@@ -707,6 +707,8 @@ def run_model_step(args):
             "config": {"workload": f"{args.workload}: full gated distillation step", "layers": shape.layers,
                        "hidden": shape.hidden, "ffn": shape.ffn, "vocab": shape.vocab, "tied": shape.tied,
                        "batch": shape.batch, "seq": shape.seq, "candidates": shape.candidates,
+                       "attention_candidates": shape.attention_candidates,
+                       "row_scale_sigma": shape.row_scale_sigma,
                        "gated_tensors": len(trainer.replaced), "budget": shape.budget,
                        "parallelism": f"tp{world}", "build_s": round(t_build, 1),
                        "input_grad_overlap_sms": args.overlap_sms if world > 1 else 0,
@@ -791,9 +793,10 @@ def run_cache_load(args):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--workload", choices=["layer", "tiny", "0.6b", "8b", "cache-load"], default="layer",
-                    help="layer: the single gated-Linear step (default); tiny/0.6b/8b: full distillation step; "
-                         "cache-load: candidate-cache files into HBM (GB/s)")
+    ap.add_argument("--workload", choices=["layer", "tiny", "0.6b", "8b", "32b", "cache-load"], default="layer",
+                    help="layer: the single gated-Linear step (default); tiny/0.6b/8b/32b: full distillation step "
+                         "(32b: the TP-4 / TP-8 case, K=7 with per-role menus); cache-load: candidate-cache files "
+                         "into HBM (GB/s)")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=60)
     ap.add_argument("--warmup", type=int, default=3)

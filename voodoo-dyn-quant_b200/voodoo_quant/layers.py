@@ -290,11 +290,14 @@ def _row_chunks(T: int, n: int) -> list[tuple[int, int]]:
 
 
 def _gategrad_into(dy2, x2, layer, out=None, reserve: int = 0) -> torch.Tensor:
+    in_f, off = layer.in_features, layer.in_col_offset
+    if off:  # halo shard: zero inputs for the stored columns before the rank's own
+        x2 = F.pad(x2[:, :in_f], (off, 0))
     if reserve:  # leave SMs to the all-reduce in flight so that it overlaps the GEMM
         _C.set_gategrad_sm_reserve(reserve)
     try:
         return _C.gategrad(dy2, x2, layer.candidate_types, layer._candidate_blocks(), layer.out_features,
-                           layer.in_features, layer.padded_in_features,
+                           off + in_f, layer.padded_in_features,
                            workspace=layer._gategrad_workspace(x2.device), out=out)
     finally:
         if reserve:
@@ -405,8 +408,7 @@ class _RoutedGatedLinearFunction(Function):
         xs = x2.index_select(0, order)
         one = torch.ones(1, dtype=torch.float32, device=x2.device)
         blocks = layer._candidate_blocks()
-        ws = [_C.mix([qt], [blocks[k]], one, out_f, layer.padded_in_features, in_f)
-              for k, qt in enumerate(layer.candidate_types)]
+        ws = [layer._mix_of([qt], [blocks[k]], one) for k, qt in enumerate(layer.candidate_types)]
         if T > 128:  # one grouped GEMM; the group sizes stay on the device
             ys = _C.linear_fwd_grouped(xs, ws, out_f, in_f, group_off)
         else:
@@ -447,8 +449,9 @@ class _MixedWeightFunction(Function):
         layer = ctx.layer
         gf = g.to(torch.float32)
         out = torch.empty(layer.num_candidates, dtype=torch.float32, device=g.device)
+        off = layer.in_col_offset
         for k, (qt, qb) in enumerate(zip(layer.candidate_types, layer._candidate_blocks())):
-            w = _C.dequant(qb, qt, layer.out_features, layer.padded_in_features)[:, :layer.in_features]
+            w = _C.dequant(qb, qt, layer.out_features, layer.padded_in_features)[:, off:off + layer.in_features]
             out[k] = (gf * w).sum()
         return out, None
 
@@ -531,6 +534,9 @@ class _MixedQuantBase(nn.Module):
         qbytes = [candidate_bytes[qt] for qt in self.candidate_types]
         rows = shard_spec.full_out if shard_spec is not None else out_features
         self.padded_in_features = self._full_padded_in_features
+        # column of input 0 inside the stored blocks: nonzero only for a halo
+        # shard (parallel.ShardSpec.halo), whose blocks start before its columns
+        self.in_col_offset = shard_spec.in_col_offset if shard_spec is not None else 0
         if shard_spec is not None:
             qbytes = [shard_spec.slice_qbytes(qb, qt, self._full_padded_in_features)
                       for qb, qt in zip(qbytes, self.candidate_types)]
@@ -608,15 +614,25 @@ class _MixedQuantBase(nn.Module):
                 # Decoded on demand (bit-exact); never stored.
                 qb = self._candidate_blocks()[k]
                 w = _C.dequant(qb, self.candidate_types[k], self.out_features, self.padded_in_features)
-                return w[:, :self.in_features].to(self.source_dtype)
+                off = self.__dict__.get("in_col_offset", 0)
+                return w[:, off:off + self.in_features].to(self.source_dtype)
         return super().__getattr__(name)
 
     def _mix(self, probs: torch.Tensor) -> torch.Tensor:
-        return _C.mix(self.candidate_types, self._candidate_blocks(), probs.to(self._cand_arena.device),
-                      self.out_features, self.padded_in_features, self.in_features)
+        return self._mix_of(self.candidate_types, self._candidate_blocks(), probs.to(self._cand_arena.device))
+
+    def _mix_of(self, types: list[str], blocks: list[torch.Tensor], probs: torch.Tensor) -> torch.Tensor:
+        """bf16 W_mix [out, in] of the given candidates.  A halo shard mixes its
+        stored blocks up to its last column and returns the column window of
+        its inputs: a strided view whose base stays 16-byte aligned (the
+        offset is a multiple of 8 columns)."""
+        off = self.in_col_offset
+        w = _C.mix(types, blocks, probs, self.out_features, self.padded_in_features, off + self.in_features)
+        return w[:, off:off + self.in_features] if off else w
 
     def _gategrad_workspace(self, device: torch.device) -> torch.Tensor:
-        need = _C.gategrad_workspace_bytes(self.out_features, self.in_features, self.num_candidates)
+        need = _C.gategrad_workspace_bytes(self.out_features, self.in_features + self.in_col_offset,
+                                           self.num_candidates)
         if self._ws is None or self._ws.device != device or self._ws.numel() < need:
             self._ws = torch.empty(max(need, 4), dtype=torch.uint8, device=device)
         return self._ws

@@ -19,6 +19,15 @@ Differences from the reference, each for a reason:
   into 256-element units as evenly as possible (e.g. 25600 over 8 ranks =
   13,13,13,13,12,12,12,12 units), which the reference refuses
   (parallel.py:285-299).
+* Halo shards for head-aligned row-parallel inputs.  Where a rank's whole
+  attention heads end inside a 256-weight block (a 32B-shape o_proj at TP-8:
+  5 heads x 128 = 640 columns), the reference refuses the split
+  (parallel.py:266-272) and a block-aligned split would break heads and
+  their GQA groups.  ``ShardSpec(halo=True)`` keeps the rank's exact columns
+  but stores the packed blocks that cover them (768 columns); the gated
+  layer multiplies through the column window of its mixed weight, and its
+  gate gradient sees zero inputs outside the window, so the rank sums stay
+  exact (a block two ranks share is counted once, split by columns).
 * ``tp_init`` only binds a CUDA device when CUDA is available, so the gloo
   path runs on CPU-only hosts (the reference calls ``torch.cuda.set_device``
   unconditionally, parallel.py:71).
@@ -459,6 +468,24 @@ class ShardSpec:
     col_offset: int | None = None
     col_len: int | None = None
     vocab_start: int | None = None
+    # row-parallel slice whose ends need not fall on a 256-weight block: the
+    # rank stores the blocks covering its columns (see in_col_offset)
+    halo: bool = False
+
+    def col_units(self) -> tuple[int, int]:
+        """First and one-past-last 256-weight unit of the packed row that
+        this rank stores (the units covering its columns)."""
+        c0 = self.col_offset or 0
+        c1 = c0 + self.local_in
+        return c0 // UNIT, (c1 + UNIT - 1) // UNIT
+
+    @property
+    def in_col_offset(self) -> int:
+        """Column of the rank's first input inside its stored blocks: 0
+        unless a halo slice starts inside a block."""
+        if not self.halo or self.col_offset is None:
+            return 0
+        return self.col_offset - self.col_units()[0] * UNIT
 
     @property
     def local_out(self) -> int:
@@ -506,6 +533,10 @@ class ShardSpec:
         elif self.row_offset is not None:
             q2 = q2[self.row_offset:self.row_offset + self.row_len]
         if self.col_offset is not None:
+            if self.halo:
+                u0, u1 = self.col_units()
+                q2 = q2[:, u0 * UNIT // bs:u1 * UNIT // bs]
+                return q2.reshape(-1, bb)
             if self.col_offset % UNIT or self.col_len % UNIT:
                 raise ValueError(
                     f"{quant_type}: column slice [{self.col_offset}:{self.col_offset + self.col_len}] is not "
@@ -516,10 +547,28 @@ class ShardSpec:
     def local_padded_in(self, padded_full_in: int, candidate_types: list[str]) -> int:
         if self.col_len is None:
             return padded_full_in
+        if self.halo:
+            u0, u1 = self.col_units()
+            return (u1 - u0) * UNIT
         if self.col_len % UNIT:
             raise ValueError(f"the rank-local input slice {self.col_len} is not a multiple of {UNIT}; "
                              "use block_aligned_split for row-parallel shards")
         return self.col_len
+
+    def halo_weight(self, w_full: torch.Tensor) -> torch.Tensor:
+        """The full tensor's columns of the stored blocks ([rows, local padded
+        in]), zero-padded past the full width: what a block quantiser packs
+        into exactly the blocks ``slice_qbytes`` keeps."""
+        w = w_full
+        if self.row_index is not None:
+            w = w[self.row_index.to(w.device)]
+        elif self.row_offset is not None:
+            w = w[self.row_offset:self.row_offset + self.row_len]
+        u0, u1 = self.col_units()
+        w = w[:, u0 * UNIT:min(u1 * UNIT, w.shape[1])]
+        if w.shape[1] < (u1 - u0) * UNIT:
+            w = F.pad(w, (0, (u1 - u0) * UNIT - w.shape[1]))
+        return w.contiguous()
 
 
 class ColumnParallelLinear(nn.Linear):
@@ -573,7 +622,7 @@ _PARALLEL_TYPES = (ColumnParallelLinear, RowParallelLinear, VocabParallelEmbeddi
 
 
 def _shard_child(parent: nn.Module, name: str, *, row_offset=None, row_len=None, row_index=None,
-                 col_offset=None, col_len=None, vocab_start=None) -> nn.Module:
+                 col_offset=None, col_len=None, vocab_start=None, halo: bool = False) -> nn.Module:
     """Replace parent.<name> (nn.Linear / nn.Embedding) with its rank-local parallel module."""
     child = getattr(parent, name)
     if isinstance(child, _PARALLEL_TYPES):
@@ -581,7 +630,8 @@ def _shard_child(parent: nn.Module, name: str, *, row_offset=None, row_len=None,
     if isinstance(child, nn.Linear):
         w = child.weight.data
         spec = ShardSpec(full_out=w.shape[0], full_in=w.shape[1], row_offset=row_offset, row_len=row_len,
-                         row_index=row_index, col_offset=col_offset, col_len=col_len, vocab_start=vocab_start)
+                         row_index=row_index, col_offset=col_offset, col_len=col_len, vocab_start=vocab_start,
+                         halo=halo and col_offset is not None)
         sl = spec.slice_weight(w)
         new = ColumnParallelLinear(sl, spec, w, vocab_start) if col_offset is None else RowParallelLinear(sl, spec, w)
         setattr(parent, name, new)
@@ -626,15 +676,24 @@ def tp_mlp(mlp: nn.Module) -> None:
 
 
 def tp_attention_dense(attn: nn.Module, num_heads: int, num_kv_heads: int, head_dim: int) -> None:
-    """Llama-style attention: q/k/v column-parallel by whole heads, o row-parallel."""
+    """Llama-style attention: q/k/v column-parallel by whole heads, o row-parallel.
+
+    o_proj's rank-local input is the rank's heads; when that width is not a
+    multiple of the 256-weight block (40 heads x 128 at TP-8 = 640 columns)
+    the o_proj shard is a halo shard (``ShardSpec.halo``), so heads and GQA
+    groups stay whole.
+    """
     tp, r = TP.world_size, TP.rank
     if num_heads % tp or num_kv_heads % tp:
         raise ValueError(f"attention heads ({num_heads} q / {num_kv_heads} kv) must divide tp={tp}")
     hq, hk = num_heads // tp, num_kv_heads // tp
+    width = hq * head_dim
+    if width % UNIT and width % 8:
+        raise ValueError(f"o_proj rank-local input {width} is neither 256-block aligned nor a multiple of 8")
     _shard_child(attn, "q_proj", row_offset=r * hq * head_dim, row_len=hq * head_dim)
     _shard_child(attn, "k_proj", row_offset=r * hk * head_dim, row_len=hk * head_dim)
     _shard_child(attn, "v_proj", row_offset=r * hk * head_dim, row_len=hk * head_dim)
-    _shard_child(attn, "o_proj", col_offset=r * hq * head_dim, col_len=hq * head_dim)
+    _shard_child(attn, "o_proj", col_offset=r * width, col_len=width, halo=width % UNIT != 0)
     attn.tp_heads_local = hq
     _install_input_copy(attn)
 

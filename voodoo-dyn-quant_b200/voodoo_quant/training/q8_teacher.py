@@ -24,22 +24,38 @@ def _q8_rows(qweight: torch.Tensor, rows: int, cols: int) -> torch.Tensor:
 
 
 class Q8Linear(nn.Module):
-    """nn.Linear stand-in holding Q8_0 bytes; forward-only (teacher)."""
+    """nn.Linear stand-in holding Q8_0 bytes; forward-only (teacher).
 
-    def __init__(self, qbytes: torch.Tensor, out_features: int, in_features: int, bias=None, device=None):
+    ``qbytes`` holds rows of ``padded_in`` weights (default ``in_features``, a
+    multiple of 256); the inputs are columns ``[in_col_offset, in_col_offset +
+    in_features)`` of them -- a halo shard of a row-parallel Linear, whose
+    stored blocks cover more than the rank's own columns.
+    """
+
+    def __init__(self, qbytes: torch.Tensor, out_features: int, in_features: int, bias=None, device=None,
+                 padded_in: int | None = None, in_col_offset: int = 0):
         super().__init__()
         if bias is not None:
             raise NotImplementedError("Q8Linear does not support bias")
-        if in_features % 256:
-            raise ValueError(f"Q8Linear needs in_features % 256 == 0 on this path, got {in_features}")
+        padded = in_features if padded_in is None else padded_in
+        if padded % 256:
+            raise ValueError(f"Q8Linear needs in_features % 256 == 0 on this path, got {padded}")
+        if in_col_offset < 0 or in_col_offset % 8 or in_col_offset + in_features > padded:
+            raise ValueError(f"Q8Linear: input columns [{in_col_offset}, {in_col_offset + in_features}) "
+                             f"do not fit {padded} stored columns at a multiple of 8")
         self.out_features = out_features
         self.in_features = in_features
+        self.padded_in_features = padded
+        self.in_col_offset = in_col_offset
         dev = torch.device(device) if device is not None else qbytes.device
         self.register_buffer("qweight", qbytes.reshape(-1, 34).to(dev).contiguous())
         self.register_buffer("_one", torch.ones(1, dtype=torch.float32, device=dev), persistent=False)
 
     def weight_bf16(self) -> torch.Tensor:
-        return _C.mix(["Q8_0"], [self.qweight], self._one, self.out_features, self.in_features, self.in_features)
+        off = self.in_col_offset
+        w = _C.mix(["Q8_0"], [self.qweight], self._one, self.out_features, self.padded_in_features,
+                   off + self.in_features)
+        return w[:, off:off + self.in_features] if off else w
 
     @torch.no_grad()
     def forward(self, x: torch.Tensor) -> torch.Tensor:
@@ -82,7 +98,15 @@ def wrap_q8_teacher(model: nn.Module, quantizer: Callable[[torch.Tensor], torch.
             continue
         if isinstance(child, nn.Linear):
             w = child.weight.data
-            new = Q8Linear(quantizer(w), child.out_features, child.in_features, device=w.device)
+            spec = getattr(child, "tp_shard_spec", None)
+            if spec is not None and spec.halo:
+                # halo shard: pack the full tensor's blocks covering the rank's columns
+                full = child.tp_full_weight
+                new = Q8Linear(quantizer(spec.halo_weight(full)), child.out_features, child.in_features,
+                               device=w.device, padded_in=spec.local_padded_in(full.shape[1], ["Q8_0"]),
+                               in_col_offset=spec.in_col_offset)
+            else:
+                new = Q8Linear(quantizer(w), child.out_features, child.in_features, device=w.device)
             for attr in ("tp_shard_spec", "tp_vocab_start", "tp_vocab_end"):
                 if hasattr(child, attr):
                     setattr(new, attr, getattr(child, attr))

@@ -31,6 +31,21 @@ class ModelShape:
     batch: int = 1
     seq: int = 512
     budget: float = 0.45  # compression_ratio: target bytes / 8-bit bytes
+    # per-role candidate menus (the reference's --attention_candidates /
+    # --non_attention_candidates, layers.py:1878-1905); None = `candidates`
+    attention_candidates: list[str] | None = None
+    non_attention_candidates: list[str] | None = None
+    # sigma of per-row log-normal(0, sigma) scales on every weight matrix (0 = none)
+    row_scale_sigma: float = 0.0
+
+
+# Config 5's seven candidates in the order the configuration lists them.  Its
+# menus are per role: the MLP projections, the embedding and the head choose
+# among all seven (Q2_K to Q8_0), attention among the mid rungs and up
+# (Q4_K, IQ4_XS, Q5_K, Q6_K, Q8_0), as the reference's own configurations
+# give attention a higher menu than the MLP (configs/qwen38_27b_voodoo30_tp4.sh).
+K7 = ["IQ4_XS", "Q3_K", "Q4_K", "Q5_K", "Q6_K", "Q8_0", "Q2_K"]
+K7_ATTENTION = ["Q4_K", "IQ4_XS", "Q5_K", "Q6_K", "Q8_0"]
 
 
 SHAPES = {
@@ -41,6 +56,11 @@ SHAPES = {
     "0.6b": ModelShape(28, 1024, 16, 8, 3072, 151936, True, head_dim=128, batch=8, seq=2048, budget=0.45),
     # config 4: 8B Llama-3 shape
     "8b": ModelShape(32, 4096, 32, 8, 14336, 128256, False, batch=4, seq=4096, budget=0.30),
+    # config 5: 32B dense decoder, TP-4 / TP-8 (o_proj at TP-8 is a halo shard:
+    # 5 heads x 128 = 640 columns per rank; down_proj splits 13/12 blocks)
+    "32b": ModelShape(64, 5120, 40, 8, 25600, 152064, False, head_dim=128, candidates=list(K7), batch=2,
+                      seq=8192, budget=0.30, attention_candidates=list(K7_ATTENTION),
+                      non_attention_candidates=list(K7), row_scale_sigma=0.5),
 }
 
 
@@ -60,7 +80,10 @@ def llama_config(shape: ModelShape):
 
 
 def build_llama(shape: ModelShape, device, dtype=torch.bfloat16, seed: int = 0):
-    """Random-init LlamaForCausalLM on `device`: every weight N(0, 0.02), norms 1."""
+    """Random-init LlamaForCausalLM on `device`: every weight N(0, 0.02), norms 1.
+    With ``shape.row_scale_sigma`` > 0, each row of every weight matrix is then
+    scaled by its own log-normal(0, sigma) factor (drawn right after the
+    matrix, from the same generator)."""
     from transformers import LlamaForCausalLM
     from transformers.models.llama.modeling_llama import LlamaRotaryEmbedding
 
@@ -75,6 +98,9 @@ def build_llama(shape: ModelShape, device, dtype=torch.bfloat16, seed: int = 0):
                 p.fill_(1.0)
             else:
                 p.copy_(torch.randn(p.shape, generator=g, device=device, dtype=torch.float32).to(dtype) * 0.02)
+                if shape.row_scale_sigma > 0 and p.dim() == 2:
+                    z = torch.randn(p.shape[0], 1, generator=g, device=device, dtype=torch.float32)
+                    p.copy_((p.float() * torch.exp(z * shape.row_scale_sigma)).to(dtype))
     model.model.rotary_emb = LlamaRotaryEmbedding(cfg, device=device)
     if shape.tied:
         model.tie_weights()

@@ -229,6 +229,12 @@ def build_distill(shape_name: str, device, seed: int = 0, args: StepArgs | None 
     run beside the all-reduce of the block's input gradient on a second
     communicator limited to that many CTAs (``parallel.enable_input_grad_overlap``,
     ``parallel.mark_deferred_gategrads``); the GEMMs leave those SMs free.
+
+    Shapes with per-role menus pass them on as the reference's
+    ``--attention_candidates`` / ``--non_attention_candidates``.  The teacher
+    is built after the student's full weights are released (both models draw
+    the same seeded weights), so at most one full bf16 model is on the device
+    at a time -- 61.5 GB for the 32B shape.
     """
     from voodoo_quant.layers import replace_embedding_with_mixed_quant, replace_linear_with_mixed_quant
     from voodoo_quant.parallel import TP, tp_patch_model
@@ -237,25 +243,30 @@ def build_distill(shape_name: str, device, seed: int = 0, args: StepArgs | None 
 
     shape = S.SHAPES[shape_name]
     provider = candidate_provider or S.rtn_candidate_provider
+    menus = dict(attention_candidates=shape.attention_candidates,
+                 non_attention_candidates=shape.non_attention_candidates)
     base = S.build_llama(shape, device, seed=seed)
     meta = state_dict_meta(base)
     total_8bit = compute_total_8bit_bytes(meta)
-    teacher = S.build_llama(shape, device, seed=seed)
     if tp and TP.enabled:
         tp_patch_model(base, verbose=False)
-        tp_patch_model(teacher, verbose=False)
-    wrap_q8_teacher(teacher, S.q8_quantizer)
     skip = {"lm_head"} if shape.tied else set()
     replaced = replace_linear_with_mixed_quant(base, shape.candidates, skip_names=skip, device=device,
-                                               candidate_provider=provider)
+                                               candidate_provider=provider, **menus)
     if replace_embeddings:
         replaced.update(replace_embedding_with_mixed_quant(base, shape.candidates, device=device,
-                                                           candidate_provider=provider))
+                                                           candidate_provider=provider, **menus))
     targeted = {n + ".weight" for n in replaced}
     non_targeted = compute_non_targeted_8bit_bytes(meta, targeted)
     for m in base.modules():  # drop the full-weight references kept for candidate packing
         if hasattr(m, "tp_full_weight"):
             m.tp_full_weight = None
+    if torch.device(device).type == "cuda":
+        torch.cuda.empty_cache()
+    teacher = S.build_llama(shape, device, seed=seed)
+    if tp and TP.enabled:
+        tp_patch_model(teacher, verbose=False)
+    wrap_q8_teacher(teacher, S.q8_quantizer)
     if fused_blocks and torch.device(device).type == "cuda":
         from voodoo_quant.fused_blocks import fuse_llama_blocks
 
