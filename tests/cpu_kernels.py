@@ -9,6 +9,14 @@ parallelism over gloo, the deferred gate-gradient queue, the chunked head
 loss -- runs on CPU.  The stand-ins are consistent with one another, not
 with the kernels' exact rounding; the kernels themselves are checked by the
 GPU tests.  Returns an undo function.
+
+``install(precision="bf16")`` (the default) rounds operands and results to
+bf16 where the kernels do.  ``install(precision="fp32")`` keeps float32
+operands and results, for float32 models, so that the step's host logic can
+be compared with the reference's float32 step without bf16 rounding in the
+way; a single-candidate decode (the Q8_0 teacher's weights) is still
+rounded to bf16, as the reference's teacher does (dequantize_tensor_gpu,
+voodoo_quant/layers.py:298-319).
 """
 
 from __future__ import annotations
@@ -17,6 +25,9 @@ import numpy as np
 import torch
 
 from oracle import ggml_blocks
+
+# result dtype of the matmul / mixture / loss-gradient stand-ins (install())
+_OUT = torch.bfloat16
 
 
 def _decode(qb: torch.Tensor, qt: str, rows: int, cols: int) -> torch.Tensor:
@@ -30,8 +41,9 @@ def _mix(qtypes, qbytes, probs, rows, padded_cols, cols, out=None):
     for k, (qt, qb) in enumerate(zip(qtypes, qbytes)):
         w += p[k] * _decode(qb, qt, rows, padded_cols)
     ld = (cols + 7) // 8 * 8
-    res = torch.zeros(rows, ld, dtype=torch.bfloat16)
-    res[:, :cols] = w[:, :cols].to(torch.bfloat16)
+    dt = torch.bfloat16 if len(qtypes) == 1 else _OUT
+    res = torch.zeros(rows, ld, dtype=dt)
+    res[:, :cols] = w[:, :cols].to(dt)
     if out is not None:
         out.copy_(res)
         return out
@@ -41,7 +53,7 @@ def _mix(qtypes, qbytes, probs, rows, padded_cols, cols, out=None):
 def _linear_fwd(x, w, n_out=None, in_features=None, out=None):
     kin = x.shape[1] if in_features is None else in_features
     n = w.shape[0] if n_out is None else n_out
-    y = (x[:, :kin].float() @ w[:n, :kin].float().t()).to(torch.bfloat16)
+    y = (x[:, :kin].float() @ w[:n, :kin].float().t()).to(_OUT)
     if out is not None:
         out.copy_(y)
         return out
@@ -49,7 +61,7 @@ def _linear_fwd(x, w, n_out=None, in_features=None, out=None):
 
 
 def _linear_dx(dy, w, in_features, out=None):
-    r = (dy.float() @ w[:, :in_features].float()).to(torch.bfloat16)
+    r = (dy.float() @ w[:, :in_features].float()).to(_OUT)
     if out is not None:
         out.copy_(r)
         return out
@@ -88,7 +100,7 @@ def _loss_fused(s, t, targets, temperature, ce_weight, kl_weight, want_grad=True
     if want_grad:
         onehot = torch.zeros_like(s)
         onehot[valid, y[valid]] = 1.0
-        g = (ce_weight * (torch.softmax(s, 1) - onehot) + kl_weight * T * (ls.exp() - pt)).to(torch.bfloat16)
+        g = (ce_weight * (torch.softmax(s, 1) - onehot) + kl_weight * T * (ls.exp() - pt)).to(_OUT)
     return ce, kl, g
 
 
@@ -135,7 +147,7 @@ def _loss_grad(s, t, targets, vocab_start, temperature, row_lse, ce_weight, kl_w
     valid = (y >= 0).float()[:, None]
     g = ce_weight * valid * (torch.exp(s - row_lse[:, 0:1]) - onehot) + kl_weight * T * (
         torch.exp(s / T - row_lse[:, 1:2]) - torch.exp(t / T - row_lse[:, 2:3]))
-    return g.to(torch.bfloat16)
+    return g.to(_OUT)
 
 
 def _route_prep(keys, K):
@@ -149,7 +161,7 @@ def _route_prep(keys, K):
 
 
 def _linear_fwd_grouped(x, ws, n_out, in_features, group_off, out=None):
-    y = torch.empty(x.shape[0], n_out, dtype=torch.bfloat16) if out is None else out
+    y = torch.empty(x.shape[0], n_out, dtype=_OUT) if out is None else out
     off = group_off.tolist()
     for g, w in enumerate(ws):
         a, b = off[g], off[g + 1]
@@ -158,10 +170,19 @@ def _linear_fwd_grouped(x, ws, n_out, in_features, group_off, out=None):
     return y
 
 
-def install():
+def _as_operand_fp32(x: torch.Tensor) -> torch.Tensor:
+    return x if x.stride(-1) == 1 else x.contiguous()
+
+
+def install(precision: str = "bf16"):
+    global _OUT
     from voodoo_quant import _C
     from voodoo_quant.layers import _MixedQuantBase
 
+    if precision not in ("bf16", "fp32"):
+        raise ValueError(f"precision must be 'bf16' or 'fp32', got {precision!r}")
+    prev_out = _OUT
+    _OUT = torch.bfloat16 if precision == "bf16" else torch.float32
     table = [(_C, "mix", _mix), (_C, "linear_fwd", _linear_fwd), (_C, "linear_dx", _linear_dx),
              (_C, "gategrad", _gategrad), (_C, "dequant", _dequant), (_C, "loss_fused", _loss_fused),
              (_C, "route_prep", _route_prep), (_C, "linear_fwd_grouped", _linear_fwd_grouped),
@@ -169,12 +190,16 @@ def install():
              (_C, "gategrad_workspace_bytes", lambda n, k, c: 4),
              (_C, "set_gategrad_sm_reserve", lambda n: None), (_C, "set_gemm_sm_reserve", lambda n: None),
              (_MixedQuantBase, "_gategrad_workspace", lambda self, dev: None)]
+    if precision == "fp32":
+        table.append((_C, "_as_operand", _as_operand_fp32))
     saved = []
     for obj, name, fn in table:
         saved.append((obj, name, obj.__dict__.get(name), name in obj.__dict__))
         setattr(obj, name, fn)
 
     def undo():
+        global _OUT
+        _OUT = prev_out
         for obj, name, old, had in reversed(saved):
             if had:
                 setattr(obj, name, old)
