@@ -182,6 +182,15 @@ int vq_mixgemm_fwd(const void* x, int64_t T, int64_t Kin, int64_t ldx, int K, co
                    const void* const* blocks, const float* probs, int64_t N, int64_t padded_cols, void* w_mix,
                    int64_t ldw, void* y, int64_t ldy, void* stream);
 
+/* K2 convenience: vq_mix into w_mix[N, ldw] followed by vq_linear_dx, i.e.
+ * dx[T, Kin] = dy[T, N] * (sum_k probs[k] W_k).  For callers that keep no
+ * W_mix between the forward and the backward (the reference re-mixes in its
+ * backward, _MixedWeightFunctionLazy.backward, voodoo_quant/layers.py:
+ * 582-667, then multiplies through F.linear's autograd, :1731). */
+int vq_mixgemm_dx(const void* dy, int64_t T, int64_t N, int64_t lddy, int K, const int* types,
+                  const void* const* blocks, const float* probs, int64_t Kin, int64_t padded_cols, void* w_mix,
+                  int64_t ldw, void* dx, int64_t lddx, void* stream);
+
 /* K4 -- fused chunked-vocab CE + KL(teacher || student) on bf16 logits.
  * Per row r: row_ce[r] = lse(s) - s[y] (0 when targets[r] < 0) and
  * row_kl[r] = T^2 * KL(softmax(t/T) || softmax(s/T)); when dlogits != NULL it

@@ -47,6 +47,10 @@ def test_library_validation_paths_without_gpu():
     # shape validation happens before any CUDA call
     assert lib.vq_dequant(12, None, 4, 100, None, None) == _C.VQ_ERR_INVALID
     assert lib.vq_dequant(12, None, 0, 256, None, None) == 0  # empty input is a no-op
+    # the mixture conveniences validate their candidates before any launch
+    for fn in (lib.vq_mixgemm_fwd, lib.vq_mixgemm_dx):
+        assert fn(None, 8, 8, 8, 0, None, None, None, 8, 256, None, 256, None, 8, None) == _C.VQ_ERR_INVALID
+        assert b"candidates" in lib.vq_last_error()
     # per-tile slots (112 row blocks x 16 column blocks x 4 warps) + 16 stream-K slots per CTA pair (<= 128)
     assert lib.vq_gategrad_workspace_bytes(14336, 4096, 5) == (112 * 16 * 4 + 16 * 128) * 5 * 4
 

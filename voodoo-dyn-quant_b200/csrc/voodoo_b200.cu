@@ -559,6 +559,13 @@ int vq_mixgemm_fwd(const void* x, int64_t T, int64_t Kin, int64_t ldx, int K, co
   return vq_linear_fwd(x, T, Kin, ldx, w_mix, N, ldw, y, ldy, stream);
 }
 
+int vq_mixgemm_dx(const void* dy, int64_t T, int64_t N, int64_t lddy, int K, const int* types,
+                  const void* const* blocks, const float* probs, int64_t Kin, int64_t padded_cols, void* w_mix,
+                  int64_t ldw, void* dx, int64_t lddx, void* stream) {
+  if (int rc = vq_mix(K, types, blocks, probs, N, padded_cols, Kin, w_mix, ldw, stream)) return rc;
+  return vq_linear_dx(dy, T, N, lddy, w_mix, Kin, ldw, dx, lddx, stream);
+}
+
 int vq_loss_fused(const void* s_logits, int64_t lds, const void* t_logits, int64_t ldt, const int64_t* targets,
                   int64_t rows, int64_t V, float temperature, float ce_weight, float kl_weight, float* row_ce,
                   float* row_kl, void* dlogits, int64_t ldg, void* stream) {

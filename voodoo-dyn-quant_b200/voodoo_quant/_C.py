@@ -57,6 +57,8 @@ def _declare(lib):
         "vq_gategrad_noalloc": (_int, [_vp, _i64, _vp, _i64, _i64, _i64, _i64, _int, _vp, _vp, _i64, _vp, _vp]),
         "vq_mixgemm_fwd": (_int, [_vp, _i64, _i64, _i64, _int, _vp, _vp, _vp, _i64, _i64, _vp, _i64, _vp,
                                   _i64, _vp]),
+        "vq_mixgemm_dx": (_int, [_vp, _i64, _i64, _i64, _int, _vp, _vp, _vp, _i64, _i64, _vp, _i64, _vp,
+                                 _i64, _vp]),
         "vq_loss_fused": (_int, [_vp, _i64, _vp, _i64, _vp, _i64, _i64, _f32, _f32, _f32, _vp, _vp, _vp,
                                  _i64, _vp]),
         "vq_loss_stats": (_int, [_vp, _i64, _vp, _i64, _vp, _i64, _i64, _i64, _f32, _vp, _vp]),
@@ -81,7 +83,7 @@ def _declare(lib):
 EXPORTED = (
     "vq_last_error", "vq_abi_version", "vq_format_info", "vq_device_error", "vq_dequant", "vq_mix",
     "vq_linear_fwd", "vq_linear_fwd_grouped", "vq_set_gategrad_sm_reserve", "vq_set_gemm_sm_reserve", "vq_quantize", "vq_route_prep", "vq_linear_fwd_mcred", "vq_linear_dx", "vq_gategrad_workspace_bytes", "vq_gategrad", "vq_gategrad_noalloc",
-    "vq_mixgemm_fwd",
+    "vq_mixgemm_fwd", "vq_mixgemm_dx",
     "vq_loss_fused", "vq_loss_stats", "vq_loss_combine", "vq_loss_grad",
     "vq_rmsnorm_fwd", "vq_rmsnorm_bwd", "vq_add_rmsnorm_fwd", "vq_rmsnorm_bwd_add", "vq_rope", "vq_swiglu_fwd", "vq_swiglu_bwd",
 )
