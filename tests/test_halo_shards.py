@@ -50,7 +50,7 @@ def test_halo_slice_equals_packing_the_covering_columns(fmt):
         spec = ShardSpec(full_out=24, full_in=1280, col_offset=640 * r, col_len=640, halo=True)
         assert spec.col_units() == units and spec.in_col_offset == off
         assert spec.local_padded_in(1280, [fmt]) == 768
-        assert torch.equal(spec.halo_weight(w), w[:, units[0] * 256:units[1] * 256])
+        assert torch.equal(spec.local_block_weight(w), w[:, units[0] * 256:units[1] * 256])
         assert torch.equal(spec.slice_qbytes(full, fmt, 1280).reshape(-1),
                            rtn.quantize(w[:, units[0] * 256:units[1] * 256], fmt).reshape(-1))
         # without the halo flag the reference's refusal stands
@@ -63,9 +63,37 @@ def test_halo_slice_equals_packing_the_covering_columns(fmt):
     padded = torch.nn.functional.pad(w2, (0, 128))
     spec = ShardSpec(full_out=8, full_in=640, col_offset=320, col_len=320, halo=True)
     assert spec.col_units() == (1, 3) and spec.in_col_offset == 64
-    assert torch.equal(spec.halo_weight(w2), padded[:, 256:768])
+    assert torch.equal(spec.local_block_weight(w2), padded[:, 256:768])
     assert torch.equal(spec.slice_qbytes(rtn.quantize(padded, fmt), fmt, 768).reshape(-1),
                        rtn.quantize(padded[:, 256:768], fmt).reshape(-1))
+
+
+@pytest.mark.parametrize("fmt", HALO_TYPES)
+def test_packing_the_rank_part_equals_slicing_the_full_packing(fmt):
+    """The synthetic candidate provider packs only a rank's part under TP
+    (``ShardSpec.local_block_weight``); for every kind of shard -- rows, a
+    row index, block-aligned columns, halo columns, vocabulary rows of a
+    tensor whose width is not a multiple of 256 -- that equals the rank's
+    slice of the packed full tensor."""
+    from voodoo_quant.parallel import ShardSpec
+    from voodoo_quant.quants import rtn
+
+    torch.manual_seed(3)
+    w = torch.randn(40, 1280) * 0.02
+    w_odd = torch.randn(24, 640) * 0.02  # padded to 768 for packing
+    specs = [
+        (w, ShardSpec(full_out=40, full_in=1280, row_offset=8, row_len=20)),
+        (w, ShardSpec(full_out=40, full_in=1280, row_index=torch.tensor([3, 1, 30, 7, 22]))),
+        (w, ShardSpec(full_out=40, full_in=1280, col_offset=512, col_len=768)),
+        (w, ShardSpec(full_out=40, full_in=1280, col_offset=640, col_len=640, halo=True)),
+        (w_odd, ShardSpec(full_out=24, full_in=640, row_offset=12, row_len=12, vocab_start=12)),
+        (w_odd, ShardSpec(full_out=24, full_in=640, col_offset=320, col_len=320, halo=True)),
+    ]
+    for full_w, spec in specs:
+        padded = torch.nn.functional.pad(full_w, (0, -full_w.shape[1] % 256))
+        whole = rtn.quantize(padded, fmt)
+        local = rtn.quantize(spec.local_block_weight(full_w), fmt)
+        assert torch.equal(local.reshape(-1), spec.slice_qbytes(whole, fmt, padded.shape[1]).reshape(-1)), spec
 
 
 def test_32b_tp8_o_proj_geometry():
@@ -155,7 +183,7 @@ def test_q8_teacher_halo_layer_uses_the_covering_blocks():
         wf = full.weight_bf16()
         for r in range(2):
             spec = ShardSpec(full_out=16, full_in=1280, col_offset=640 * r, col_len=640, halo=True)
-            part = Q8Linear(rtn.quantize(spec.halo_weight(w), "Q8_0"), 16, 640,
+            part = Q8Linear(rtn.quantize(spec.local_block_weight(w), "Q8_0"), 16, 640,
                             padded_in=spec.local_padded_in(1280, ["Q8_0"]), in_col_offset=spec.in_col_offset)
             assert torch.equal(part.weight_bf16(), wf[:, 640 * r:640 * (r + 1)])
     finally:

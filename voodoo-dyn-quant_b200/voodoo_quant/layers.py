@@ -500,7 +500,8 @@ class _MixedQuantBase(nn.Module):
     def __init__(self, candidate_types: list[str], source_weight: torch.Tensor, out_features: int,
                  in_features: int, imatrix: torch.Tensor | None = None, device=None, lazy: bool = False,
                  tensor_name: str = "unknown", qbytes_device=None, shard_spec=None,
-                 full_source_weight: torch.Tensor | None = None, candidate_bytes: dict | None = None):
+                 full_source_weight: torch.Tensor | None = None, candidate_bytes: dict | None = None,
+                 candidate_bytes_local: bool = False):
         super().__init__()
         self.candidate_types = list(candidate_types)
         self.num_candidates = len(self.candidate_types)
@@ -538,8 +539,9 @@ class _MixedQuantBase(nn.Module):
         # shard (parallel.ShardSpec.halo), whose blocks start before its columns
         self.in_col_offset = shard_spec.in_col_offset if shard_spec is not None else 0
         if shard_spec is not None:
-            qbytes = [shard_spec.slice_qbytes(qb, qt, self._full_padded_in_features)
-                      for qb, qt in zip(qbytes, self.candidate_types)]
+            if not candidate_bytes_local:  # full-tensor candidates: keep this rank's blocks
+                qbytes = [shard_spec.slice_qbytes(qb, qt, self._full_padded_in_features)
+                          for qb, qt in zip(qbytes, self.candidate_types)]
             rows = shard_spec.local_out
             self.padded_in_features = shard_spec.local_padded_in(self._full_padded_in_features,
                                                                  self.candidate_types)
@@ -722,12 +724,13 @@ class MixedQuantLinear(_MixedQuantBase):
     def __init__(self, in_features: int, out_features: int, candidate_types: list[str],
                  source_weight: torch.Tensor, imatrix: torch.Tensor | None = None, device=None,
                  lazy: bool = False, tensor_name: str = "unknown", qbytes_device=None, shard_spec=None,
-                 full_source_weight: torch.Tensor | None = None, candidate_bytes: dict | None = None):
+                 full_source_weight: torch.Tensor | None = None, candidate_bytes: dict | None = None,
+                 candidate_bytes_local: bool = False):
         super().__init__(candidate_types=candidate_types, source_weight=source_weight,
                          out_features=out_features, in_features=in_features, imatrix=imatrix, device=device,
                          lazy=lazy, tensor_name=tensor_name, qbytes_device=qbytes_device,
                          shard_spec=shard_spec, full_source_weight=full_source_weight,
-                         candidate_bytes=candidate_bytes)
+                         candidate_bytes=candidate_bytes, candidate_bytes_local=candidate_bytes_local)
         if shard_spec is not None and shard_spec.vocab_start is not None:
             self.tp_vocab_start = shard_spec.vocab_start
             self.tp_vocab_end = shard_spec.vocab_start + out_features
@@ -765,12 +768,13 @@ class MixedQuantEmbedding(_MixedQuantBase):
     def __init__(self, num_embeddings: int, embedding_dim: int, candidate_types: list[str],
                  source_weight: torch.Tensor, imatrix: torch.Tensor | None = None, device=None,
                  lazy: bool = False, tensor_name: str = "unknown", qbytes_device=None, shard_spec=None,
-                 full_source_weight: torch.Tensor | None = None, candidate_bytes: dict | None = None):
+                 full_source_weight: torch.Tensor | None = None, candidate_bytes: dict | None = None,
+                 candidate_bytes_local: bool = False):
         super().__init__(candidate_types=candidate_types, source_weight=source_weight,
                          out_features=num_embeddings, in_features=embedding_dim, imatrix=imatrix,
                          device=device, lazy=lazy, tensor_name=tensor_name, qbytes_device=qbytes_device,
                          shard_spec=shard_spec, full_source_weight=full_source_weight,
-                         candidate_bytes=candidate_bytes)
+                         candidate_bytes=candidate_bytes, candidate_bytes_local=candidate_bytes_local)
         self.num_embeddings = num_embeddings
         self.embedding_dim = embedding_dim
         if shard_spec is not None and shard_spec.vocab_start is not None:
@@ -834,9 +838,14 @@ def resolve_candidate_types(tensor_name: str, base_candidates: list[str],
     return [qt for qt in group if qt in set(base_candidates)]
 
 
-def _provided(provider, name: str, weight: torch.Tensor, types: list[str]):
+def _provided(provider, name: str, weight: torch.Tensor, types: list[str], spec=None):
+    """Packed candidates from ``provider``: of the whole (256-padded) weight,
+    or, for a TP shard, of only the rank's rows and stored block columns
+    (``ShardSpec.local_block_weight``), which the layer then takes as they are."""
     if provider is None:
         return None
+    if spec is not None:
+        return provider(name, spec.local_block_weight(weight.detach()), types)
     padded, _, _ = _pad_weight_and_imatrix(weight.detach(), None)
     return provider(name, padded, types)
 
@@ -850,9 +859,12 @@ def replace_linear_with_mixed_quant(module: nn.Module, candidate_types: list[str
                                     qbytes_device=None, candidate_provider=None) -> dict[str, _MixedQuantBase]:
     """Recursively replace selected nn.Linear children (reference :1908-2066).
 
-    ``candidate_provider(name, full_weight, types) -> {qtype: uint8 blocks}``,
-    when given, supplies the packed candidates of the FULL tensor (padded to a
-    multiple of 256 columns) instead of the on-disk cache / libggml.
+    ``candidate_provider(name, weight, types) -> {qtype: uint8 blocks}``,
+    when given, supplies packed candidates instead of the on-disk cache /
+    libggml: of the whole tensor (padded to a multiple of 256 columns), or,
+    for a TP-sharded child, of the rank's part only
+    (``ShardSpec.local_block_weight``), which the packed formats allow
+    because they are block-local.
     """
     if candidate_types is None:
         candidate_types = list(GPU_FORMATS)
@@ -871,13 +883,16 @@ def replace_linear_with_mixed_quant(module: nn.Module, candidate_types: list[str
             im = imatrix_dict.get(full_name, imatrix_dict.get(full_name + ".weight"))
             types = resolve_candidate_types(full_name, candidate_types, attention_candidates, non_attention_candidates)
             full_w = getattr(child, "tp_full_weight", None)
+            spec = getattr(child, "tp_shard_spec", None)
+            local = candidate_provider is not None and spec is not None and full_w is not None
             new = MixedQuantLinear(
                 in_features=child.in_features, out_features=child.out_features, candidate_types=types,
                 source_weight=child.weight.data, imatrix=im, device=device, lazy=lazy, tensor_name=full_name,
-                qbytes_device=qbytes_device, shard_spec=getattr(child, "tp_shard_spec", None),
-                full_source_weight=full_w,
+                qbytes_device=qbytes_device, shard_spec=spec, full_source_weight=full_w,
                 candidate_bytes=_provided(candidate_provider, full_name,
-                                          full_w if full_w is not None else child.weight.data, types))
+                                          full_w if full_w is not None else child.weight.data, types,
+                                          spec if local else None),
+                candidate_bytes_local=local)
             if getattr(child, "_tp_input_copy", False):
                 # the sharded child summed its input gradient over the ranks
                 # through a pre-hook; the gated layer does it inside its backward
@@ -913,13 +928,16 @@ def replace_embedding_with_mixed_quant(module: nn.Module, candidate_types: list[
             im = imatrix_dict.get(full_name, imatrix_dict.get(full_name + ".weight"))
             types = resolve_candidate_types(full_name, candidate_types, attention_candidates, non_attention_candidates)
             full_w = getattr(child, "tp_full_weight", None)
+            spec = getattr(child, "tp_shard_spec", None)
+            local = candidate_provider is not None and spec is not None and full_w is not None
             new = MixedQuantEmbedding(
                 num_embeddings=child.num_embeddings, embedding_dim=child.embedding_dim, candidate_types=types,
                 source_weight=child.weight.data, imatrix=im, device=device, lazy=lazy, tensor_name=full_name,
-                qbytes_device=qbytes_device, shard_spec=getattr(child, "tp_shard_spec", None),
-                full_source_weight=full_w,
+                qbytes_device=qbytes_device, shard_spec=spec, full_source_weight=full_w,
                 candidate_bytes=_provided(candidate_provider, full_name,
-                                          full_w if full_w is not None else child.weight.data, types))
+                                          full_w if full_w is not None else child.weight.data, types,
+                                          spec if local else None),
+                candidate_bytes_local=local)
             setattr(module, name, new)
             replaced[full_name] = new
         else:

@@ -555,10 +555,12 @@ class ShardSpec:
                              "use block_aligned_split for row-parallel shards")
         return self.col_len
 
-    def halo_weight(self, w_full: torch.Tensor) -> torch.Tensor:
-        """The full tensor's columns of the stored blocks ([rows, local padded
-        in]), zero-padded past the full width: what a block quantiser packs
-        into exactly the blocks ``slice_qbytes`` keeps."""
+    def local_block_weight(self, w_full: torch.Tensor) -> torch.Tensor:
+        """This rank's rows of the full tensor over the 256-weight units it
+        stores (every unit without a column shard; the covering units of a
+        halo shard), zero-padded past the full width.  The packed formats are
+        block-local, so packing this gives exactly the blocks ``slice_qbytes``
+        keeps of the packed full tensor, at 1/world of the packing work."""
         w = w_full
         if self.row_index is not None:
             w = w[self.row_index.to(w.device)]

@@ -102,7 +102,7 @@ def wrap_q8_teacher(model: nn.Module, quantizer: Callable[[torch.Tensor], torch.
             if spec is not None and spec.halo:
                 # halo shard: pack the full tensor's blocks covering the rank's columns
                 full = child.tp_full_weight
-                new = Q8Linear(quantizer(spec.halo_weight(full)), child.out_features, child.in_features,
+                new = Q8Linear(quantizer(spec.local_block_weight(full)), child.out_features, child.in_features,
                                device=w.device, padded_in=spec.local_padded_in(full.shape[1], ["Q8_0"]),
                                in_col_offset=spec.in_col_offset)
             else:
