@@ -630,8 +630,17 @@ def run_model_step(args):
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
+    workload = args.workload
+    if args.layers > 0:
+        # a smoke run of the workload's build, memory plan and step with fewer
+        # decoder layers: a different (smaller) model, so its line names it
+        import dataclasses
+
+        base = S.SHAPES[args.workload]
+        workload = f"{args.workload}-{args.layers}l"
+        S.SHAPES[workload] = dataclasses.replace(base, layers=args.layers)
     t_build = time.perf_counter()
-    trainer, shape = build_distill(args.workload, dev, seed=0, tp=world > 1, multicast=args.multicast,
+    trainer, shape = build_distill(workload, dev, seed=0, tp=world > 1, multicast=args.multicast,
                                    overlap_sms=args.overlap_sms if world > 1 else 0,
                                    args=StepArgs(max_steps=args.warmup + args.steps + args.e2e_steps + 3,
                                                  ptqr=args.ptqr, logits_chunk=args.logits_chunk,
@@ -704,7 +713,9 @@ def run_model_step(args):
             "vs_baseline": None,
             "dtype": "bf16",
             "data": "synthetic (seeded random-init weights and tokens; candidates from the round-to-nearest packer)",
-            "config": {"workload": f"{args.workload}: full gated distillation step", "layers": shape.layers,
+            "config": {"workload": f"{args.workload}: full gated distillation step" + (
+                           f" -- SMOKE RUN with {shape.layers} of {S.SHAPES[args.workload].layers} layers, "
+                           "not the configuration" if args.layers > 0 else ""), "layers": shape.layers,
                        "hidden": shape.hidden, "ffn": shape.ffn, "vocab": shape.vocab, "tied": shape.tied,
                        "batch": shape.batch, "seq": shape.seq, "candidates": shape.candidates,
                        "attention_candidates": shape.attention_candidates,
@@ -819,6 +830,9 @@ def main():
                     help="full-step workloads: head + loss per chunk of this many tokens (no [tokens, V] logits)")
     ap.add_argument("--multicast", action="store_true",
                     help="full-step workloads under TP: sum row-parallel outputs with multimem.red in the GEMM")
+    ap.add_argument("--layers", type=int, default=0,
+                    help="full-step workloads: build only this many decoder layers (a smoke run of the build, "
+                         "memory plan and step; its line says so and is not the configuration's number)")
     ap.add_argument("--profile-step", action="store_true",
                     help="full-step workloads: print device time per kernel name for one step")
     ap.add_argument("--ncu-case", action="store_true", help="one launch per kernel at profiling sizes")
