@@ -644,7 +644,8 @@ def run_model_step(args):
                                    overlap_sms=args.overlap_sms if world > 1 else 0,
                                    args=StepArgs(max_steps=args.warmup + args.steps + args.e2e_steps + 3,
                                                  ptqr=args.ptqr, logits_chunk=args.logits_chunk,
-                                                 ce_reduction="tokens" if args.logits_chunk > 0 else "valid"))
+                                                 ce_reduction="tokens" if args.logits_chunk > 0 or args.graph_step
+                                                 else "valid", static_shapes=args.graph_step))
     from voodoo_quant import parallel as _par
 
     multicast_on = _par.multicast_reducer() is not None
@@ -654,8 +655,12 @@ def run_model_step(args):
     tokens = x.numel()
     stream = torch.cuda.current_stream()
     torch.cuda.reset_peak_memory_stats(dev)
+    step_fn = trainer.step
+    if args.graph_step:  # forward + backward recorded once, replayed per step (optimizer eager)
+        trainer.capture(x, y, warmup=args.warmup)
+        step_fn = trainer.replay_step
     for _ in range(args.warmup):
-        trainer.step(x, y)
+        step_fn(x, y)
     torch.cuda.synchronize()
     peak_gb = torch.cuda.max_memory_allocated(dev) / 1e9
     barrier()
@@ -666,7 +671,7 @@ def run_model_step(args):
     clk.mark_start()
     ev0.record(stream)
     for _ in range(args.steps):
-        out = trainer.step(x, y)
+        out = step_fn(x, y)
     ev1.record(stream)
     torch.cuda.synchronize()
     clk.mark_end()
@@ -685,14 +690,14 @@ def run_model_step(args):
     for _ in range(args.e2e_steps):
         xd = xh.to(dev, non_blocking=True)
         yd = yh.to(dev, non_blocking=True)
-        o = trainer.step(xd, yd)
+        o = step_fn(xd, yd)
         lh.copy_(o["loss"], non_blocking=True)
     e1.record(stream)
     torch.cuda.synchronize()
     e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.e2e_steps)
-    launches = _count_our_launches(lambda: trainer.step(x, y))
+    launches = _count_our_launches(lambda: step_fn(x, y))
     if args.profile_step:
-        _print_step_profile(lambda: trainer.step(x, y)) if rank == 0 else trainer.step(x, y)
+        _print_step_profile(lambda: step_fn(x, y)) if rank == 0 else step_fn(x, y)
     torch.cuda.synchronize()
 
     if rank == 0:
@@ -726,6 +731,8 @@ def run_model_step(args):
                        "row_parallel_reduce": "nvls multimem.red in GEMM" if multicast_on else "nccl all-reduce",
                        "forward": "ptqr (one candidate per token)" if args.ptqr else "candidate mixture",
                        "logits_chunk": args.logits_chunk, "peak_alloc_gb_rank0": round(peak_gb, 2),
+                       "step_graph": "forward + backward replayed from one CUDA graph" if args.graph_step
+                       else "eager",
                        "l2": "activations and logits far larger than L2"},
             "roofline": {"bound": "tensor", "kernel": "whole step", "flops_per_token": fpt,
                          "achieved": round(ach, 1), "peak": round(peak_t * world, 1), "unit": "TFLOP/s",
@@ -739,6 +746,8 @@ def run_model_step(args):
             "size_bytes_last": float(out["size_bytes"]),
         }
         print(json.dumps(res), flush=True)
+    trainer.release_graph()  # the graph holds collectives: drop it before the process group
+    torch.cuda.synchronize()
     if world > 1:
         _par.enable_multicast_reduce(False)  # every rank releases the multicast buffers together
         dist.barrier()
@@ -830,6 +839,9 @@ def main():
                     help="full-step workloads: head + loss per chunk of this many tokens (no [tokens, V] logits)")
     ap.add_argument("--multicast", action="store_true",
                     help="full-step workloads under TP: sum row-parallel outputs with multimem.red in the GEMM")
+    ap.add_argument("--graph-step", action="store_true",
+                    help="full-step workloads: record forward + backward as one CUDA graph (static-shape mode, "
+                         "CE over all tokens) and replay it each step; the optimizer stays eager")
     ap.add_argument("--layers", type=int, default=0,
                     help="full-step workloads: build only this many decoder layers (a smoke run of the build, "
                          "memory plan and step; its line says so and is not the configuration's number)")

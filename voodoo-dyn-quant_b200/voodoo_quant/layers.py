@@ -75,6 +75,29 @@ def set_ptqr(enabled: bool) -> None:
     _PTQR_STATE.enabled = bool(enabled)
 
 
+# --------------------------------------------------------------------------- static shapes
+class _StaticState:
+    """Static-shape mode (off by default): no host round trip and no
+    data-dependent shape in the step's host code, so that the whole forward
+    and backward can be recorded as one CUDA graph.  Embedding lookups then
+    decode one row per token, repeats included, instead of the unique rows
+    (``torch.unique`` reads its output size on the host); a vocabulary shard
+    looks every token up at a clamped row and zeroes the rows that belong to
+    other shards instead of gathering its own tokens (boolean indexing).
+    Values are unchanged: the gated embedding's backward is a dot product per
+    candidate, whose terms are the same per token either way.  PTQR keeps its
+    per-unique-row routing and so stays dynamic."""
+
+    enabled: bool = False
+
+
+_STATIC_STATE = _StaticState()
+
+
+def set_static_shapes(enabled: bool) -> None:
+    _STATIC_STATE.enabled = bool(enabled)
+
+
 # --------------------------------------------------------------------------- ST-Gumbel switches
 # The reference's straight-through Gumbel hardening (layers.py:821-846,
 # trainer --st_gumbel) routes a fraction of tokens through hard one-hot
@@ -793,8 +816,12 @@ class MixedQuantEmbedding(_MixedQuantBase):
 
     def _embedding_lookup(self, ids: torch.Tensor) -> torch.Tensor:
         dev = self._cand_arena.device
-        rows, inverse = torch.unique(ids.reshape(-1).to(dev), return_inverse=True)
         probs = self.get_probs().to(dev)
+        if _STATIC_STATE.enabled and not _PTQR_STATE.enabled:  # one row per token: no host round trip
+            rows = ids.reshape(-1).to(dev)
+            mixed = _GatedEmbeddingRowsFunction.apply(probs, rows, self)
+            return mixed.reshape(*ids.shape, self.embedding_dim)
+        rows, inverse = torch.unique(ids.reshape(-1).to(dev), return_inverse=True)
         if _PTQR_STATE.enabled:  # one candidate per (unique) row, reference layers.py:1810-1813
             routing = _sample_token_routing(probs, rows.shape[0])
             mixed = _GatedEmbeddingRowsFunction.apply(probs, rows, self, routing)
@@ -809,6 +836,12 @@ class MixedQuantEmbedding(_MixedQuantBase):
             v0, v1 = self.tp_vocab_start, self.tp_vocab_end
             ids = input.to(self._cand_arena.device)
             in_shard = (ids >= v0) & (ids < v1)
+            if _STATIC_STATE.enabled and not _PTQR_STATE.enabled:
+                # every token at a clamped row, other shards' rows zeroed; their
+                # gradient is then zero, so the gate dots are this shard's alone
+                local = (ids - v0).clamp(0, self.num_embeddings - 1)
+                emb = self._embedding_lookup(local) * in_shard.unsqueeze(-1).to(self.source_dtype)
+                return tp_all_reduce_sum_(emb)
             # Only this shard's tokens are looked up: clamping the others to
             # one row would funnel most of the batch's gradient into a single
             # index of the lookup's backward.
@@ -981,13 +1014,32 @@ class GateBank:
         self._p = None
         self._routes = {}
         self._dgrad = None
+        # the temperature as a device scalar (set_temperature); None = each
+        # layer's own Python float
+        self.tau_t: torch.Tensor | None = None
         # gate gradients of layers marked _defer_gategrad are written into a
         # [L, Kmax] buffer (TP: they run beside an all-reduce) and reach the
         # gates through the tap below
         self.defer = any(l.__dict__.get("_defer_gategrad", False) for l in self.layers)
 
+    def set_temperature(self, tau: float) -> None:
+        """Every layer's temperature, also held in a device scalar that
+        ``probs()`` divides by, so a recorded CUDA graph of the step reads
+        the current value when it is replayed (a Python float would be frozen
+        into it).  The division is the same float32 operation either way."""
+        for l in self.layers:
+            l.set_temperature(tau)
+        t = max(float(tau), 1e-6)
+        if self.tau_t is None:
+            self.tau_t = torch.full((), t, dtype=torch.float32, device=self.layers[0].gates.device)
+        else:
+            self.tau_t.fill_(t)
+
     def probs(self) -> torch.Tensor:
-        g = torch.cat([l.gates / l.temperature for l in self.layers])
+        if self.tau_t is not None:
+            g = torch.cat([l.gates for l in self.layers]) / self.tau_t
+        else:
+            g = torch.cat([l.gates / l.temperature for l in self.layers])
         padded = torch.full((len(self.layers) * self.kmax,), float("-inf"), dtype=g.dtype, device=g.device)
         padded = padded.index_put((self.flat_index,), g)
         p = torch.softmax(padded.view(len(self.layers), self.kmax), dim=1)

@@ -77,6 +77,14 @@ class Q8Embedding(nn.Module):
 
     @torch.no_grad()
     def forward(self, ids: torch.Tensor) -> torch.Tensor:
+        from voodoo_quant.layers import _STATIC_STATE
+
+        if _STATIC_STATE.enabled:  # one row per token, repeats included: no host round trip
+            flat = ids.reshape(-1)
+            sub = _q8_rows(self.qweight, self.num_embeddings, self.embedding_dim).index_select(0, flat)
+            w = _C.mix(["Q8_0"], [sub.reshape(-1)], self._one, flat.numel(), self.embedding_dim,
+                       self.embedding_dim)
+            return w[:, :self.embedding_dim].reshape(*ids.shape, self.embedding_dim)
         rows, inverse = torch.unique(ids.reshape(-1), return_inverse=True)
         sub = _q8_rows(self.qweight, self.num_embeddings, self.embedding_dim).index_select(0, rows)
         w = _C.mix(["Q8_0"], [sub.reshape(-1)], self._one, rows.numel(), self.embedding_dim, self.embedding_dim)

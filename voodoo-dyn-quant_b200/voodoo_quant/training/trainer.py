@@ -23,7 +23,7 @@ from dataclasses import dataclass
 import torch
 import torch.nn as nn
 
-from voodoo_quant.layers import GateBank, set_ptqr
+from voodoo_quant.layers import GateBank, set_ptqr, set_static_shapes
 from voodoo_quant.training.loss import chunked_head_loss, distillation_loss, tp_distillation_loss
 
 
@@ -81,6 +81,11 @@ class StepArgs:
     # head + loss per chunk of this many tokens, never materialising the
     # [tokens, V] logits (reference --logits_chunk, trainer.py:753-832); 0 = off
     logits_chunk: int = 0
+    # no host round trip in forward_backward (layers.set_static_shapes), so it
+    # can be recorded as a CUDA graph (GatedDistillTrainer.capture); needs
+    # ce_reduction="tokens" (the "valid" count is read on the host), which
+    # equals "valid" whenever no target is ignored
+    static_shapes: bool = False
 
 
 class GatedDistillTrainer:
@@ -99,6 +104,10 @@ class GatedDistillTrainer:
         self.trainable = [layer.gates for layer in replaced.values()]
         self.bank = GateBank(replaced)  # every layer's softmax(g / tau) in one batched op per step
         set_ptqr(args.ptqr)
+        if args.static_shapes and args.ce_reduction != "tokens" and args.logits_chunk <= 0:
+            raise ValueError("static_shapes needs ce_reduction='tokens': the 'valid' token count is read on the host")
+        set_static_shapes(args.static_shapes)
+        self._graph = None
         self.optimizer = torch.optim.AdamW(self.trainable, lr=args.lr, betas=(0.9, 0.95))
         self.scheduler = torch.optim.lr_scheduler.CosineAnnealingLR(self.optimizer, T_max=args.max_steps,
                                                                     eta_min=1e-3)
@@ -114,8 +123,12 @@ class GatedDistillTrainer:
         """Loss of one batch and its gate gradients (left in ``gates.grad``)."""
         a = self.args
         tau = anneal_temperature(self.step_idx, a.max_steps, a.temp_start, a.temp_end)
-        for layer in self.replaced.values():
-            layer.set_temperature(tau)
+        if a.static_shapes:
+            if not _capturing():  # a recorded step reads the scalar; replay_step sets it
+                self.bank.set_temperature(tau)
+        else:
+            for layer in self.replaced.values():
+                layer.set_temperature(tau)
         self.optimizer.zero_grad(set_to_none=True)
         self.bank.probs()
         v0 = self._vocab_start()
@@ -206,8 +219,65 @@ class GatedDistillTrainer:
         self.apply_update()
         return out
 
+    # ---- one CUDA graph per step (static_shapes) ----
+    def capture(self, x: torch.Tensor, y: torch.Tensor, warmup: int = 3) -> None:
+        """Record ``forward_backward`` on static copies of ``x`` / ``y`` as one
+        CUDA graph: every kernel and collective of the forward and backward,
+        launched by one replay instead of thousands of host calls.  The
+        optimizer stays eager (clip, AdamW and the schedule are a few launches
+        over the gates).  ``warmup`` eager steps run first on a side stream
+        (workspaces, communicators, cuDNN plans); they use the gates as they
+        are and update nothing."""
+        if not self.args.static_shapes:
+            raise RuntimeError("capture needs StepArgs(static_shapes=True)")
+        self._gx, self._gy = x.clone(), y.clone()
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for _ in range(warmup):
+                self.forward_backward(self._gx, self._gy)
+        torch.cuda.current_stream().wait_stream(side)
+        self.optimizer.zero_grad(set_to_none=True)
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()  # the graph allocates from its own pool: hand the warm-up's cache back
+        self.bank.set_temperature(anneal_temperature(self.step_idx, self.args.max_steps, self.args.temp_start,
+                                                     self.args.temp_end))
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            self._gout = self.forward_backward(self._gx, self._gy)
+        self._graph = graph
+
+    def replay_step(self, x: torch.Tensor, y: torch.Tensor) -> dict:
+        """One step through the recorded graph: this step's temperature into
+        the bank's scalar, the batch into the static inputs, replay (the
+        gates' gradients are rewritten in place), then the eager update.
+        Returns the step's outputs (tensors owned by the graph, overwritten
+        by the next replay)."""
+        if self._graph is None:
+            raise RuntimeError("replay_step needs capture() first")
+        a = self.args
+        tau = anneal_temperature(self.step_idx, a.max_steps, a.temp_start, a.temp_end)
+        self.bank.set_temperature(tau)
+        self._gx.copy_(x, non_blocking=True)
+        self._gy.copy_(y, non_blocking=True)
+        self._graph.replay()
+        self.apply_update()
+        out = dict(self._gout)
+        out["tau"] = tau
+        return out
+
+    def release_graph(self) -> None:
+        """Drop the recorded graph (before destroying a process group whose
+        collectives it holds)."""
+        self._graph = None
+        self._gout = None
+
     def assignments(self) -> dict[str, str]:
         return {name: layer.get_assignment() for name, layer in self.replaced.items()}
+
+
+def _capturing() -> bool:
+    return torch.cuda.is_available() and torch.cuda.is_current_stream_capturing()
 
 
 def build_distill(shape_name: str, device, seed: int = 0, args: StepArgs | None = None,
