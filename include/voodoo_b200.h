@@ -16,7 +16,10 @@
  *     thread-local message.  No C++ exception crosses this boundary.
  *   - Calls only enqueue work on `stream`: they never synchronise (except
  *     vq_device_error) and never allocate; scratch space is caller-provided.
- *   - Thread-safe for distinct streams.
+ *   - Thread-safe for distinct streams.  The one process-wide state is the
+ *     pair of SM reserves (vq_set_gategrad_sm_reserve, vq_set_gemm_sm_reserve):
+ *     read when a GEMM is launched, they set how many SMs its persistent grid
+ *     leaves free, never what it computes.
  */
 #ifndef VOODOO_B200_H
 #define VOODOO_B200_H

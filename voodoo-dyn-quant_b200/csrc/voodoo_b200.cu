@@ -13,6 +13,7 @@
 #include <cstdarg>
 #include <cstdint>
 #include <cstdio>
+#include <atomic>
 #include <cstring>
 #include <mutex>
 
@@ -86,16 +87,21 @@ int sm_count(int* n) {
   return 0;
 }
 
+// The driver's cuTensorMapEncodeTiled, looked up on first use (again after a
+// failed lookup); an atomic, since calls may come from several threads.
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  if (fn == nullptr) {
+  static std::atomic<PFN_cuTensorMapEncodeTiled_v12000> fn{nullptr};
+  PFN_cuTensorMapEncodeTiled_v12000 f = fn.load(std::memory_order_acquire);
+  if (f == nullptr) {
     void* p = nullptr;
     cudaDriverEntryPointQueryResult q;
     if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+        q == cudaDriverEntryPointSuccess) {
+      f = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+      fn.store(f, std::memory_order_release);
+    }
   }
-  return fn;
+  return f;
 }
 
 // Row-major bf16 matrix [rows][cols] with leading dimension ld (elements);
@@ -147,12 +153,14 @@ constexpr int kMaxClusters = 128;
 
 // SMs the gate-gradient GEMM leaves free (vq_set_gategrad_sm_reserve), for a
 // collective that runs concurrently on another stream.
-int g_gategrad_sm_reserve = 0;
+std::atomic<int> g_gategrad_sm_reserve{0};
 // SMs the store-epilogue GEMMs (forward, dX) leave free (vq_set_gemm_sm_reserve).
-int g_gemm_sm_reserve = 0;
+std::atomic<int> g_gemm_sm_reserve{0};
 
 inline int sm_reserve(int epi, int sms) {
-  const int r = epi == vq::gemm::kEpiGateGrad ? g_gategrad_sm_reserve : epi == vq::gemm::kEpiStoreBf16 ? g_gemm_sm_reserve : 0;
+  const int r = epi == vq::gemm::kEpiGateGrad   ? g_gategrad_sm_reserve.load(std::memory_order_relaxed)
+                : epi == vq::gemm::kEpiStoreBf16 ? g_gemm_sm_reserve.load(std::memory_order_relaxed)
+                                                 : 0;
   return r > 0 && r < sms - 2 ? r : 0;
 }
 
@@ -478,13 +486,13 @@ int vq_linear_fwd_grouped(const void* x, int64_t T, int64_t Kin, int64_t ldx, in
 
 int vq_set_gategrad_sm_reserve(int sms) {
   if (sms < 0) return fail(VQ_ERR_INVALID, "negative SM count");
-  g_gategrad_sm_reserve = sms;
+  g_gategrad_sm_reserve.store(sms, std::memory_order_relaxed);
   return 0;
 }
 
 int vq_set_gemm_sm_reserve(int sms) {
   if (sms < 0) return fail(VQ_ERR_INVALID, "negative SM count");
-  g_gemm_sm_reserve = sms;
+  g_gemm_sm_reserve.store(sms, std::memory_order_relaxed);
   return 0;
 }
 
