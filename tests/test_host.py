@@ -149,6 +149,40 @@ def test_candidate_cache_format_round_trip(tmp_path, monkeypatch):
     assert torch.equal(m2._qweight_0.cpu(), cb["Q5_K"])
 
 
+def test_missing_candidates_are_quantized_on_threads_and_cached(tmp_path, monkeypatch):
+    """Cache-cold candidates are quantized concurrently (one thread each, as
+    the reference's _quantize_candidates_parallel) and saved to the cache;
+    a second layer over the same weight then loads them without quantizing."""
+    import threading
+    import time
+
+    from voodoo_quant import layers
+    from voodoo_quant.quants import rtn
+
+    monkeypatch.setattr(layers, "_CANDIDATE_CACHE_ROOT", tmp_path)
+    types = ["Q4_K", "Q5_K", "Q6_K", "Q8_0"]
+    calls, threads = [], set()
+
+    def fake_quantize(w, qt, im=None):  # stands in for libggml's quantize_* (which runs outside the GIL)
+        calls.append(qt)
+        threads.add(threading.get_ident())
+        time.sleep(0.3)
+        return rtn.quantize(w, qt)
+
+    monkeypatch.setattr(layers, "quantize_tensor", fake_quantize)
+    monkeypatch.setenv("VOODOO_QUANT_WORKERS", "4")
+    w = torch.randn(16, 256) * 0.02
+    t0 = time.perf_counter()
+    m = layers.MixedQuantLinear(256, 16, types, w, tensor_name="cold.proj")
+    assert time.perf_counter() - t0 < 1.0  # four 0.3 s quantizations side by side, not 1.2 s in a row
+    assert sorted(calls) == sorted(types) and len(threads) == 4
+    for k, qt in enumerate(types):
+        assert torch.equal(getattr(m, f"_qweight_{k}").cpu(), rtn.quantize(w, qt))
+    calls.clear()
+    layers.MixedQuantLinear(256, 16, types, w, tensor_name="cold.proj")
+    assert calls == []  # served from the cache files written above
+
+
 def test_missing_candidates_need_libggml(tmp_path, monkeypatch):
     from voodoo_quant import ggml, layers
 

@@ -616,10 +616,22 @@ class _MixedQuantBase(nn.Module):
                 missing.append((qt, p))
         if missing:
             padded, pim, _ = _pad_weight_and_imatrix(weight.to(torch.float32), padded_im if imatrix is not None else None)
-            for qt, p in missing:
+
+            def quantize_one(item):
+                qt, p = item
                 qb = quantize_tensor(padded, qt, pim)  # libggml, exactly as the reference
                 _atomic_torch_save(qb.cpu(), p)
-                found[qt] = qb
+                return qt, qb
+
+            # one thread per missing candidate, as the reference does
+            # (_quantize_candidates_parallel, layers.py:1282-1340): libggml
+            # runs outside the GIL under ctypes
+            import concurrent.futures
+
+            workers = int(os.environ.get("VOODOO_QUANT_WORKERS", min(8, os.cpu_count() or 2)))
+            with concurrent.futures.ThreadPoolExecutor(max_workers=max(1, min(workers, len(missing)))) as ex:
+                for qt, qb in ex.map(quantize_one, missing):
+                    found[qt] = qb
         return found
 
     # ---- candidate access ----
