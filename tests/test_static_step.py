@@ -86,6 +86,49 @@ def test_static_step_equals_the_default_step():
     _close(st[2], ref[2], 1e-5)
 
 
+def test_static_ptqr_embedding_routes_each_table_row_once(monkeypatch):
+    """Static PTQR embedding: one candidate per table row (here row % K, a
+    stand-in draw), every token's row decoded by its row's candidate; the
+    backward is the mixture's straight-through Jacobian, as without PTQR."""
+    import cpu_kernels
+    from oracle import ggml_blocks
+    from voodoo_quant import layers
+    from voodoo_quant.quants import rtn
+
+    types = ["Q4_K", "Q6_K", "Q8_0"]
+    V, D, K = 64, 256, 3
+    torch.manual_seed(4)
+    w = torch.randn(V, D) * 0.02
+    cand = {q: rtn.quantize(w, q) for q in types}
+    ids = torch.randint(0, V, (2, 20))
+    ids[1, :5] = ids[0, :5]  # repeated tokens
+    g = torch.randn(2, 20, D)
+    monkeypatch.setattr(layers, "_sample_token_routing", lambda probs, n: torch.arange(n) % K)
+    undo = cpu_kernels.install()
+    try:
+        layers.set_static_shapes(True)
+        emb = layers.MixedQuantEmbedding(V, D, types, w, candidate_bytes=cand, tensor_name="emb")
+        with torch.no_grad():
+            emb.gates.copy_(torch.tensor([0.3, -0.2, 0.5]))
+        layers.set_ptqr(True)
+        out = emb(ids)
+        out.float().backward(g)
+        routed_grad = emb.gates.grad.clone()
+        emb.gates.grad = None
+        layers.set_ptqr(False)
+        emb(ids).float().backward(g)
+        mixture_grad = emb.gates.grad.clone()
+    finally:
+        layers.set_ptqr(False)
+        layers.set_static_shapes(False)
+        undo()
+    dec = [torch.from_numpy(ggml_blocks.dequantize(cand[q].numpy().reshape(-1), q, V, D)) for q in types]
+    flat = ids.reshape(-1)
+    expect = torch.stack([dec[int(i) % K][int(i)] for i in flat]).to(torch.bfloat16).reshape(2, 20, D)
+    assert torch.equal(out.detach().to(torch.bfloat16), expect)
+    assert torch.equal(routed_grad, mixture_grad)
+
+
 def test_static_mode_requires_the_token_reduction():
     import cpu_kernels
     from voodoo_quant.training.trainer import StepArgs, build_distill

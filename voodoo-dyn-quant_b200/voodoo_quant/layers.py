@@ -85,8 +85,11 @@ class _StaticState:
     looks every token up at a clamped row and zeroes the rows that belong to
     other shards instead of gathering its own tokens (boolean indexing).
     Values are unchanged: the gated embedding's backward is a dot product per
-    candidate, whose terms are the same per token either way.  PTQR keeps its
-    per-unique-row routing and so stays dynamic."""
+    candidate, whose terms are the same per token either way.  Under PTQR the
+    embedding draws one candidate for every row of its table (the reference
+    draws one per unique row it touches, layers.py:1810-1813: the same
+    distribution) and selects each token's row among the K decodes with a
+    mask instead of gathering the rows of each candidate."""
 
     enabled: bool = False
 
@@ -489,6 +492,17 @@ class _GatedEmbeddingRowsFunction(Function):
         if routing is None:
             blocks = layer._row_blocks(rows)
             w = _C.mix(layer.candidate_types, blocks, probs, rows.numel(), layer.padded_in_features, D)[:, :D]
+        elif _STATIC_STATE.enabled:
+            # PTQR without a host round trip: every row decoded by each
+            # candidate, row i keeping candidate routing[i]'s (K decodes of
+            # the batch's rows instead of one)
+            one = torch.ones(1, dtype=torch.float32, device=rows.device)
+            w = None
+            for k, qt in enumerate(layer.candidate_types):
+                wk = _C.mix([qt], layer._row_blocks(rows, only=k), one, rows.numel(), layer.padded_in_features,
+                            D)[:, :D]
+                sel = (routing == k).unsqueeze(1)
+                w = torch.where(sel, wk, w if w is not None else torch.zeros_like(wk))
         else:
             # PTQR: row i keeps candidate routing[i]'s decoded row (reference :712-717)
             w = torch.empty(rows.numel(), D, dtype=torch.bfloat16, device=rows.device)
@@ -829,9 +843,13 @@ class MixedQuantEmbedding(_MixedQuantBase):
     def _embedding_lookup(self, ids: torch.Tensor) -> torch.Tensor:
         dev = self._cand_arena.device
         probs = self.get_probs().to(dev)
-        if _STATIC_STATE.enabled and not _PTQR_STATE.enabled:  # one row per token: no host round trip
+        if _STATIC_STATE.enabled:  # one row per token: no host round trip
             rows = ids.reshape(-1).to(dev)
-            mixed = _GatedEmbeddingRowsFunction.apply(probs, rows, self)
+            if _PTQR_STATE.enabled:  # one candidate per table row, looked up per token
+                routing = _sample_token_routing(probs, self.num_embeddings).index_select(0, rows)
+                mixed = _GatedEmbeddingRowsFunction.apply(probs, rows, self, routing)
+            else:
+                mixed = _GatedEmbeddingRowsFunction.apply(probs, rows, self)
             return mixed.reshape(*ids.shape, self.embedding_dim)
         rows, inverse = torch.unique(ids.reshape(-1).to(dev), return_inverse=True)
         if _PTQR_STATE.enabled:  # one candidate per (unique) row, reference layers.py:1810-1813
@@ -848,7 +866,7 @@ class MixedQuantEmbedding(_MixedQuantBase):
             v0, v1 = self.tp_vocab_start, self.tp_vocab_end
             ids = input.to(self._cand_arena.device)
             in_shard = (ids >= v0) & (ids < v1)
-            if _STATIC_STATE.enabled and not _PTQR_STATE.enabled:
+            if _STATIC_STATE.enabled:
                 # every token at a clamped row, other shards' rows zeroed; their
                 # gradient is then zero, so the gate dots are this shard's alone
                 local = (ids - v0).clamp(0, self.num_embeddings - 1)
