@@ -129,6 +129,101 @@ def test_static_ptqr_embedding_routes_each_table_row_once(monkeypatch):
     assert torch.equal(routed_grad, mixture_grad)
 
 
+class _FakeGraphState:
+    capturing = False
+    owner = None
+
+
+class _FakeGraph:
+    """Stands in for torch.cuda.CUDAGraph on the host: replay() runs the
+    owner's forward_backward again while flagged as capturing (as a real
+    replay runs what was recorded without the host code) and writes the
+    results into the recorded output tensors in place."""
+
+    def replay(self):
+        t = _FakeGraphState.owner
+        _FakeGraphState.capturing = True
+        try:
+            out = t.forward_backward(t._gx, t._gy)
+        finally:
+            _FakeGraphState.capturing = False
+        for k, v in out.items():
+            if torch.is_tensor(v):
+                t._gout[k].copy_(v)
+
+
+class _FakeCapture:
+    def __init__(self, graph):
+        self.graph = graph
+
+    def __enter__(self):
+        _FakeGraphState.capturing = True
+
+    def __exit__(self, *exc):
+        _FakeGraphState.capturing = False
+        return False
+
+
+def test_replayed_steps_equal_eager_steps(monkeypatch):
+    """capture() / replay_step() control flow on the host, with a stand-in
+    for the CUDA graph: each replay takes this step's temperature from the
+    bank's device scalar (the recorded step never sets it), the new batch
+    from the static inputs, and the eager update after it; three replayed
+    steps give bit for bit the losses and gates of three eager steps."""
+    import contextlib
+
+    import cpu_kernels
+    from voodoo_quant import layers
+    from voodoo_quant.training import synthetic as S
+    from voodoo_quant.training import trainer as TR
+
+    class _Stream:
+        def wait_stream(self, other):
+            pass
+
+    monkeypatch.setattr(torch.cuda, "Stream", _Stream)
+    monkeypatch.setattr(torch.cuda, "current_stream", lambda *a, **k: _Stream())
+    monkeypatch.setattr(torch.cuda, "stream", lambda s: contextlib.nullcontext())
+    monkeypatch.setattr(torch.cuda, "synchronize", lambda *a, **k: None)
+    monkeypatch.setattr(torch.cuda, "empty_cache", lambda: None)
+    monkeypatch.setattr(torch.cuda, "CUDAGraph", _FakeGraph)
+    monkeypatch.setattr(torch.cuda, "graph", _FakeCapture)
+    monkeypatch.setattr(TR, "_capturing", lambda: _FakeGraphState.capturing)
+
+    batches = [S.random_tokens(S.SHAPES["tiny"], "cpu", seed=20 + i) for i in range(3)]
+    runs = {}
+    undo = cpu_kernels.install()
+    try:
+        for mode in ("eager", "replay"):
+            args = TR.StepArgs(max_steps=6, ce_reduction="tokens", static_shapes=True)
+            trainer, _ = TR.build_distill("tiny", "cpu", seed=3, args=args)
+            g = torch.Generator().manual_seed(9)
+            with torch.no_grad():
+                for layer in trainer.replaced.values():
+                    layer.gates.copy_(torch.randn(layer.num_candidates, generator=g))
+            if mode == "replay":
+                _FakeGraphState.owner = trainer
+                trainer.capture(*batches[0], warmup=2)
+                step = trainer.replay_step
+            else:
+                step = trainer.step
+            seq = []
+            for x, y in batches:
+                out = step(x, y)
+                seq.append((float(out["loss"]), out["tau"],
+                            [l.gates.detach().clone() for l in trainer.replaced.values()]))
+            runs[mode] = seq
+            trainer.release_graph()
+    finally:
+        undo()
+        layers.set_static_shapes(False)
+        _FakeGraphState.owner = None
+    assert len({tau for _, tau, _ in runs["eager"]}) == 3  # the temperature moves every step
+    for (le, te, ge), (lr_, tr_, gr) in zip(runs["eager"], runs["replay"]):
+        assert le == lr_ and te == tr_
+        assert all(torch.equal(a, b) for a, b in zip(ge, gr))
+
+
 def test_static_mode_requires_the_token_reduction():
     import cpu_kernels
     from voodoo_quant.training.trainer import StepArgs, build_distill
