@@ -37,6 +37,7 @@ Differences from the reference, each for a reason:
 
 from __future__ import annotations
 
+import contextlib
 import os
 from dataclasses import dataclass
 from datetime import timedelta
@@ -63,9 +64,44 @@ class _TPState:
     # leave free); None = those all-reduces use `group`
     overlap_group = None
     overlap_sms = 0
+    # third communicator for the teacher's forward collectives when the
+    # teacher runs on its own stream beside the student (enable_teacher_overlap)
+    teacher_group = None
+    # the communicator forward collectives use inside collectives_on(); None = group
+    forward_override = None
 
 
 TP = _TPState()
+
+
+def _fwd_group():
+    return TP.forward_override if TP.forward_override is not None else TP.group
+
+
+@contextlib.contextmanager
+def collectives_on(group):
+    """Forward-pass collectives issued inside the block (row-parallel sums,
+    vocabulary-parallel lookups) go to ``group`` instead of the TP group; a
+    model run on another stream beside the main one uses its own
+    communicator, so the two streams' collectives never interleave on one."""
+    prev = TP.forward_override
+    TP.forward_override = group
+    try:
+        yield
+    finally:
+        TP.forward_override = prev
+
+
+def enable_teacher_overlap() -> bool:
+    """A communicator of its own for the teacher's forward collectives, so the
+    teacher's forward can run on a second stream beside the student's.
+    Collective: every rank calls it.  Returns whether TP is on."""
+    if not TP.enabled:
+        TP.teacher_group = None
+        return False
+    if TP.teacher_group is None:
+        TP.teacher_group = dist.new_group(ranks=list(range(TP.world_size)), backend=dist.get_backend(TP.group))
+    return True
 
 
 def tp_init(backend: str = "nccl", timeout_min: int = 240) -> bool:
@@ -123,6 +159,8 @@ def reset_tp() -> None:
     TP.device = None
     TP.overlap_group = None
     TP.overlap_sms = 0
+    TP.teacher_group = None
+    TP.forward_override = None
 
 
 def enable_input_grad_overlap(sms: int) -> bool:
@@ -180,7 +218,7 @@ class _AllReduceSum(Function):
     @staticmethod
     def forward(ctx, t: torch.Tensor) -> torch.Tensor:
         out = t.clone().contiguous()
-        dist.all_reduce(out, op=dist.ReduceOp.SUM, group=TP.group)
+        dist.all_reduce(out, op=dist.ReduceOp.SUM, group=_fwd_group())
         return out
 
     @staticmethod
@@ -228,7 +266,7 @@ class _AllReduceSumInPlace(Function):
     @staticmethod
     def forward(ctx, t: torch.Tensor) -> torch.Tensor:
         ctx.mark_dirty(t)
-        dist.all_reduce(t, op=dist.ReduceOp.SUM, group=TP.group)
+        dist.all_reduce(t, op=dist.ReduceOp.SUM, group=_fwd_group())
         return t
 
     @staticmethod
@@ -250,14 +288,14 @@ def tp_all_reduce_sum_(t: torch.Tensor) -> torch.Tensor:
         if t._is_view():
             return tp_all_reduce_sum(t)
         return _AllReduceSumInPlace.apply(t)
-    dist.all_reduce(t, op=dist.ReduceOp.SUM, group=TP.group)
+    dist.all_reduce(t, op=dist.ReduceOp.SUM, group=_fwd_group())
     return t
 
 
 def all_reduce_(t: torch.Tensor) -> torch.Tensor:
     """Plain in-place SUM over the TP group, outside autograd (a no-op without TP)."""
     if TP.enabled:
-        dist.all_reduce(t, op=dist.ReduceOp.SUM, group=TP.group)
+        dist.all_reduce(t, op=dist.ReduceOp.SUM, group=_fwd_group())
     return t
 
 

@@ -86,6 +86,10 @@ class StepArgs:
     # ce_reduction="tokens" (the "valid" count is read on the host), which
     # equals "valid" whenever no target is ignored
     static_shapes: bool = False
+    # the teacher's forward on a second stream beside the student's, its
+    # collectives on a communicator of their own (parallel.enable_teacher_overlap),
+    # so each model's TP all-reduces can run under the other's kernels
+    teacher_stream: bool = False
 
 
 class GatedDistillTrainer:
@@ -108,6 +112,7 @@ class GatedDistillTrainer:
             raise ValueError("static_shapes needs ce_reduction='tokens': the 'valid' token count is read on the host")
         set_static_shapes(args.static_shapes)
         self._graph = None
+        self._tstream = None
         self.optimizer = torch.optim.AdamW(self.trainable, lr=args.lr, betas=(0.9, 0.95))
         self.scheduler = torch.optim.lr_scheduler.CosineAnnealingLR(self.optimizer, T_max=args.max_steps,
                                                                     eta_min=1e-3)
@@ -134,9 +139,14 @@ class GatedDistillTrainer:
         v0 = self._vocab_start()
         if a.logits_chunk > 0:
             return self._forward_backward_chunked(x, y, a, tau, v0)
-        logits = self.student(input_ids=x, use_cache=False).logits
-        with torch.no_grad():
-            t_logits = self.teacher(input_ids=x, use_cache=False).logits
+        if a.teacher_stream:
+            t_logits = self._teacher_fork(x, lambda: self.teacher(input_ids=x, use_cache=False).logits)
+            logits = self.student(input_ids=x, use_cache=False).logits
+            t_logits = self._teacher_join(t_logits)
+        else:
+            logits = self.student(input_ids=x, use_cache=False).logits
+            with torch.no_grad():
+                t_logits = self.teacher(input_ids=x, use_cache=False).logits
         if self.tp and v0 is not None:
             kd, lm, kl = tp_distillation_loss(logits, t_logits, y, v0, a.distill_temperature, a.distill_weight,
                                               ce_reduction="tokens")
@@ -178,9 +188,14 @@ class GatedDistillTrainer:
         probabilities from a detached leaf, so each chunk's backward stays in
         the head; the leaf's accumulated gradient joins the final backward."""
         student, teacher = self.student, self.teacher
-        hidden = student.model(input_ids=x, use_cache=False).last_hidden_state
-        with torch.no_grad():
-            t_hidden = teacher.model(input_ids=x, use_cache=False).last_hidden_state
+        if a.teacher_stream:
+            t_hidden = self._teacher_fork(x, lambda: teacher.model(input_ids=x, use_cache=False).last_hidden_state)
+            hidden = student.model(input_ids=x, use_cache=False).last_hidden_state
+            t_hidden = self._teacher_join(t_hidden)
+        else:
+            hidden = student.model(input_ids=x, use_cache=False).last_hidden_state
+            with torch.no_grad():
+                t_hidden = teacher.model(input_ids=x, use_cache=False).last_hidden_state
         head = student.lm_head
         row = head.__dict__.get("_bank_probs")
         bank_ref = head.__dict__.get("_bank_ref")
@@ -207,6 +222,30 @@ class GatedDistillTrainer:
         loss = kd + a.size_weight * size_loss.detach()
         return {"loss": loss, "lm_loss": lm, "distill_loss": kl, "size_bytes": current.detach(),
                 "size_loss": size_loss.detach(), "tau": tau}
+
+    def _teacher_fork(self, x: torch.Tensor, run):
+        """Issue the teacher's forward (``run``) on the teacher's stream, after
+        the work already queued on the current stream, with its collectives
+        on the teacher's communicator; the student's forward is issued next
+        on the current stream and the two run side by side."""
+        from voodoo_quant.parallel import TP, collectives_on
+
+        if self._tstream is None:
+            self._tstream = torch.cuda.Stream()
+        self._tstream.wait_stream(torch.cuda.current_stream())
+        if x.is_cuda:
+            x.record_stream(self._tstream)
+        with torch.cuda.stream(self._tstream), collectives_on(TP.teacher_group), torch.no_grad():
+            return run()
+
+    def _teacher_join(self, t: torch.Tensor) -> torch.Tensor:
+        """Make the current stream wait for the teacher's; its output is then
+        used (and its memory held) on the current stream."""
+        main = torch.cuda.current_stream()
+        main.wait_stream(self._tstream)
+        if t.is_cuda:
+            t.record_stream(main)
+        return t
 
     def apply_update(self) -> None:
         torch.nn.utils.clip_grad_norm_(self.trainable, max_norm=1.0)
@@ -343,8 +382,13 @@ def build_distill(shape_name: str, device, seed: int = 0, args: StepArgs | None 
         fuse_llama_blocks(base)
         fuse_llama_blocks(teacher)
     if tp and TP.enabled:
-        from voodoo_quant.parallel import enable_multicast_reduce
+        from voodoo_quant.parallel import enable_multicast_reduce, enable_teacher_overlap
 
+        if args is not None and args.teacher_stream:
+            if multicast:
+                raise ValueError("teacher_stream needs the NCCL row-parallel sums (multicast off): the multicast "
+                                 "buffers serve one stream at a time")
+            enable_teacher_overlap()
         enable_multicast_reduce(multicast)
         if overlap_sms > 0:
             from voodoo_quant.parallel import enable_input_grad_overlap, mark_deferred_gategrads
