@@ -646,7 +646,8 @@ def run_model_step(args):
                                                  ptqr=args.ptqr, logits_chunk=args.logits_chunk,
                                                  ce_reduction="tokens" if args.logits_chunk > 0 or args.graph_step
                                                  else "valid", static_shapes=args.graph_step,
-                                                 teacher_stream=args.teacher_stream))
+                                                 teacher_stream=args.teacher_stream,
+                                                 teacher_stream_sms=args.teacher_stream_sms))
     from voodoo_quant import parallel as _par
 
     multicast_on = _par.multicast_reducer() is not None
@@ -734,7 +735,8 @@ def run_model_step(args):
                        "logits_chunk": args.logits_chunk, "peak_alloc_gb_rank0": round(peak_gb, 2),
                        "step_graph": "forward + backward replayed from one CUDA graph" if args.graph_step
                        else "eager",
-                       "teacher": "own stream and communicator beside the student" if args.teacher_stream
+                       "teacher": (f"own stream and communicator beside the student, "
+                                   f"{args.teacher_stream_sms} SMs left to collectives") if args.teacher_stream
                        else "after the student, same stream",
                        "l2": "activations and logits far larger than L2"},
             "roofline": {"bound": "tensor", "kernel": "whole step", "flops_per_token": fpt,
@@ -848,6 +850,9 @@ def main():
     ap.add_argument("--teacher-stream", action="store_true",
                     help="full-step workloads: the teacher's forward on a second stream beside the student's, its "
                          "TP all-reduces on a communicator of their own")
+    ap.add_argument("--teacher-stream-sms", type=int, default=0,
+                    help="with --teacher-stream: SMs the forward GEMMs leave to the other stream's all-reduces "
+                         "(and the teacher communicator's CTA cap); 0 = none")
     ap.add_argument("--layers", type=int, default=0,
                     help="full-step workloads: build only this many decoder layers (a smoke run of the build, "
                          "memory plan and step; its line says so and is not the configuration's number)")

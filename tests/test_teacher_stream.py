@@ -7,7 +7,9 @@ they can run while the student's kernels run on the main stream.  On CPU
 stand-ins of tests/cpu_kernels.py for the kernels) this checks the wiring:
 the step is bit for bit the default step, plain and with the head + loss
 per token chunk, the teacher's forward collectives all go to the teacher's
-communicator, and the student's stay on the TP group.
+communicator, the student's stay on the TP group, and with an SM reserve
+the forward GEMMs leave it free while both forwards are issued and not
+after.
 """
 
 from __future__ import annotations
@@ -41,11 +43,12 @@ def _host_streams():
     torch.cuda.stream = lambda s: contextlib.nullcontext()
 
 
-def _step(teacher_stream: bool, chunk: int, log: list):
+def _step(teacher_stream: bool, chunk: int, log: list, sms: int = 0):
     from voodoo_quant.training import synthetic as S
     from voodoo_quant.training.trainer import StepArgs, build_distill
 
-    args = StepArgs(max_steps=8, ce_reduction="tokens", teacher_stream=teacher_stream, logits_chunk=chunk)
+    args = StepArgs(max_steps=8, ce_reduction="tokens", teacher_stream=teacher_stream, logits_chunk=chunk,
+                    teacher_stream_sms=sms)
     trainer, shape = build_distill("cpu_tp2", "cpu", seed=3, args=args, tp=True)
     g = torch.Generator().manual_seed(9)
     with torch.no_grad():
@@ -80,12 +83,18 @@ def _worker(rank, world, port, outdir):
 
     dist.all_reduce = logged
     undo = cpu_kernels.install()
+    from voodoo_quant import _C
+
+    reserves = []
+    _C.set_gemm_sm_reserve = reserves.append  # (undo restores the library's setter)
     try:
         P.adopt_process_group(0)
         res = {}
         for chunk in (0, 40):
             res[f"default{chunk}"] = _step(False, chunk, log)
-            res[f"stream{chunk}"] = _step(True, chunk, log)
+            reserves.clear()
+            res[f"stream{chunk}"] = _step(True, chunk, log, sms=16)
+            res[f"reserves{chunk}"] = list(reserves)
         res["teacher_group_made"] = P.TP.teacher_group is not None
         torch.save(res, os.path.join(outdir, f"r{rank}.pt"))
     finally:
@@ -111,5 +120,7 @@ def test_teacher_stream_step_equals_the_default_step_tp2():
             # teacher's share (one per row-parallel layer and the embedding)
             # moves to its own communicator, the rest stays
             assert "teacher" not in d[2]
+            # both forwards issued with 16 SMs left to collectives, then none
+            assert r[f"reserves{chunk}"] == [16, 0], r[f"reserves{chunk}"]
             n_teacher = s[2].count("teacher")
             assert n_teacher >= 3 and s[2].count("tp") == len(d[2]) - n_teacher, (chunk, s[2], d[2])

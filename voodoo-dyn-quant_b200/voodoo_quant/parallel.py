@@ -92,15 +92,24 @@ def collectives_on(group):
         TP.forward_override = prev
 
 
-def enable_teacher_overlap() -> bool:
+def enable_teacher_overlap(sms: int = 0) -> bool:
     """A communicator of its own for the teacher's forward collectives, so the
     teacher's forward can run on a second stream beside the student's.
-    Collective: every rank calls it.  Returns whether TP is on."""
+    With ``sms`` > 0 (NCCL) its collectives use at most that many CTAs, to fit
+    in the SMs the forward GEMMs then leave free.  Collective: every rank
+    calls it with the same ``sms``.  Returns whether TP is on."""
     if not TP.enabled:
         TP.teacher_group = None
         return False
     if TP.teacher_group is None:
-        TP.teacher_group = dist.new_group(ranks=list(range(TP.world_size)), backend=dist.get_backend(TP.group))
+        ranks = list(range(TP.world_size))
+        if sms > 0 and dist.get_backend(TP.group) == "nccl":
+            opts = dist.ProcessGroupNCCL.Options()
+            opts.config.max_ctas = int(sms)
+            opts.config.min_ctas = min(int(sms), 8)
+            TP.teacher_group = dist.new_group(ranks=ranks, backend="nccl", pg_options=opts)
+        else:
+            TP.teacher_group = dist.new_group(ranks=ranks, backend=dist.get_backend(TP.group))
     return True
 
 

@@ -18,6 +18,7 @@ Only the gates train; every other parameter is frozen, as in the reference
 
 from __future__ import annotations
 
+import contextlib
 from dataclasses import dataclass
 
 import torch
@@ -90,6 +91,9 @@ class StepArgs:
     # collectives on a communicator of their own (parallel.enable_teacher_overlap),
     # so each model's TP all-reduces can run under the other's kernels
     teacher_stream: bool = False
+    # with teacher_stream: SMs the forward GEMMs of both models leave free for
+    # the other stream's all-reduces (and the teacher's communicator's CTA cap); 0 = none
+    teacher_stream_sms: int = 0
 
 
 class GatedDistillTrainer:
@@ -140,8 +144,9 @@ class GatedDistillTrainer:
         if a.logits_chunk > 0:
             return self._forward_backward_chunked(x, y, a, tau, v0)
         if a.teacher_stream:
-            t_logits = self._teacher_fork(x, lambda: self.teacher(input_ids=x, use_cache=False).logits)
-            logits = self.student(input_ids=x, use_cache=False).logits
+            with self._forward_sm_reserve():
+                t_logits = self._teacher_fork(x, lambda: self.teacher(input_ids=x, use_cache=False).logits)
+                logits = self.student(input_ids=x, use_cache=False).logits
             t_logits = self._teacher_join(t_logits)
         else:
             logits = self.student(input_ids=x, use_cache=False).logits
@@ -189,8 +194,10 @@ class GatedDistillTrainer:
         the head; the leaf's accumulated gradient joins the final backward."""
         student, teacher = self.student, self.teacher
         if a.teacher_stream:
-            t_hidden = self._teacher_fork(x, lambda: teacher.model(input_ids=x, use_cache=False).last_hidden_state)
-            hidden = student.model(input_ids=x, use_cache=False).last_hidden_state
+            with self._forward_sm_reserve():
+                t_hidden = self._teacher_fork(
+                    x, lambda: teacher.model(input_ids=x, use_cache=False).last_hidden_state)
+                hidden = student.model(input_ids=x, use_cache=False).last_hidden_state
             t_hidden = self._teacher_join(t_hidden)
         else:
             hidden = student.model(input_ids=x, use_cache=False).last_hidden_state
@@ -237,6 +244,23 @@ class GatedDistillTrainer:
             x.record_stream(self._tstream)
         with torch.cuda.stream(self._tstream), collectives_on(TP.teacher_group), torch.no_grad():
             return run()
+
+    @contextlib.contextmanager
+    def _forward_sm_reserve(self):
+        """While both forwards are issued, the store-epilogue GEMMs (forward,
+        mixture-free dX) leave ``teacher_stream_sms`` SMs to the other
+        stream's collectives; no effect at 0."""
+        sms = self.args.teacher_stream_sms
+        if sms <= 0:
+            yield
+            return
+        from voodoo_quant import _C
+
+        _C.set_gemm_sm_reserve(sms)
+        try:
+            yield
+        finally:
+            _C.set_gemm_sm_reserve(0)
 
     def _teacher_join(self, t: torch.Tensor) -> torch.Tensor:
         """Make the current stream wait for the teacher's; its output is then
@@ -388,7 +412,7 @@ def build_distill(shape_name: str, device, seed: int = 0, args: StepArgs | None 
             if multicast:
                 raise ValueError("teacher_stream needs the NCCL row-parallel sums (multicast off): the multicast "
                                  "buffers serve one stream at a time")
-            enable_teacher_overlap()
+            enable_teacher_overlap(args.teacher_stream_sms)
         enable_multicast_reduce(multicast)
         if overlap_sms > 0:
             from voodoo_quant.parallel import enable_input_grad_overlap, mark_deferred_gategrads
