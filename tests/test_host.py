@@ -266,3 +266,43 @@ def test_gate_bank_matches_per_layer_probabilities_and_bytes():
         assert torch.allclose(m.gates.grad, g, rtol=1e-4, atol=1e-6)
     bank.release()
     assert all(m.__dict__.get("_bank_probs") is None for m in mods.values())
+
+
+def test_step_flops_per_token_roofline_denominators():
+    """The algorithmic FLOPs per token behind the full-step roofline: 6 x the
+    student's gated linear weights (forward, dX, gate-grad GEMM), 4 x a tied
+    unquantised head, 2 x the teacher's, causal attention 4 L (S/2) d x 4."""
+    import bench
+    from voodoo_quant.training import synthetic as S
+
+    def by_hand(L, H, q, kv, hd, F, V, S_, tied):
+        p = L * (H * (q + 2 * kv) * hd + q * hd * H + 3 * H * F)
+        return 6 * p + (4 if tied else 6) * V * H + 2 * (p + V * H) + 16 * L * (S_ / 2) * q * hd
+
+    assert bench.step_flops_per_token(S.SHAPES["8b"]) == by_hand(32, 4096, 32, 8, 128, 14336, 128256, 4096, False)
+    assert bench.step_flops_per_token(S.SHAPES["0.6b"]) == by_hand(28, 1024, 16, 8, 128, 3072, 151936, 2048, True)
+    assert bench.step_flops_per_token(S.SHAPES["32b"]) == by_hand(64, 5120, 40, 8, 128, 25600, 152064, 8192, False)
+    assert abs(bench.step_flops_per_token(S.SHAPES["8b"]) / 1e9 - 64.33) < 0.01
+
+
+def test_reference_arm_prints_one_contract_line():
+    """bench.py --impl reference (the reference's algorithm on the host) prints
+    one JSON line with the keys the benchmark contract names."""
+    import json
+    import subprocess
+    import sys
+    from pathlib import Path
+
+    root = Path(__file__).resolve().parents[1]
+    r = subprocess.run([sys.executable, "bench.py", "--impl", "reference", "--steps", "1", "--warmup", "1",
+                        "--cpu-tokens", "64"], cwd=root, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stderr[-2000:]
+    lines = [l for l in r.stdout.splitlines() if l.startswith("{")]
+    assert len(lines) == 1
+    out = json.loads(lines[0])
+    for key in ("metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step", "higher_is_better",
+                "scaling", "vs_baseline", "dtype", "data", "config", "impl", "cpu_baseline", "e2e"):
+        assert key in out, key
+    assert out["impl"] == "reference" and out["value"] > 0 and out["unit"] == "tokens/s"
+    assert out["cpu_baseline"]["kind"] == "port" and out["cpu_baseline"]["cores"] >= 1
+    assert out["e2e"]["h2d_bytes_per_step"] == 0 and "workload" in out["config"]
