@@ -51,3 +51,22 @@ def test_pack_arena_from_mmap(tmp_path):
     assert all(l.offset % 256 == 0 for l in layout)
     for qt, v in zip(TYPES, arena_views(arena, layout)):
         assert torch.equal(v, qb[qt].reshape(v.shape))
+
+
+def test_unreadable_or_short_cache_files_fail_loudly(tmp_path, monkeypatch):
+    """Host-side faults in the candidate cache stop the layer's construction
+    with an error that names the problem: a file that is not a torch file
+    (RuntimeError naming the file), and a candidate of the wrong size for the
+    tensor (ValueError with the expected and found sizes)."""
+    import pytest
+
+    monkeypatch.setattr(layers, "_CANDIDATE_CACHE_ROOT", tmp_path)
+    w = torch.randn(16, 256) * 0.02
+    path = layers._combined_cache_path("bad.proj", "lazy", layers._tensor_hash(w), "none")
+    path.write_bytes(b"not a torch file" * 10)
+    with pytest.raises(RuntimeError, match="cannot be read") as err:
+        layers.MixedQuantLinear(256, 16, ["Q4_K"], w, tensor_name="bad.proj")
+    assert str(path) in str(err.value)
+    torch.save({"Q4_K": rtn.quantize(w, "Q4_K")[:-1]}, path)  # one block short
+    with pytest.raises(ValueError, match="2160 != 2304"):
+        layers.MixedQuantLinear(256, 16, ["Q4_K"], w, tensor_name="bad.proj")

@@ -249,6 +249,17 @@ def _combined_cache_path(tensor_name: str, mode: str, weight_hash: str, imatrix_
     return d / f"combined_{mode}_w{weight_hash}_i{imatrix_hash}.pt"
 
 
+def _load_cache_file(path: Path, tensor_name: str):
+    """A candidate-cache file, memory-mapped; an unreadable one (truncated,
+    not a torch file) is an error that names it rather than a silent
+    re-quantisation or torch's bare message."""
+    try:
+        return torch.load(path, weights_only=True, map_location="cpu", mmap=True)
+    except Exception as e:
+        raise RuntimeError(f"{tensor_name}: candidate cache file {path} cannot be read ({e}); "
+                           "delete it to quantize the candidates again") from e
+
+
 def _atomic_torch_save(obj, path: Path) -> None:
     tmp = path.with_suffix(path.suffix + f".tmp{os.getpid()}")
     torch.save(obj, tmp)
@@ -614,7 +625,7 @@ class _MixedQuantBase(nn.Module):
         for nm in names:
             p = _combined_cache_path(nm, "lazy", wh, ih)
             if p.exists():
-                combined = torch.load(p, weights_only=True, map_location="cpu", mmap=True)
+                combined = _load_cache_file(p, name)
                 for qt in self.candidate_types:
                     if qt in combined and qt not in found:
                         found[qt] = combined[qt]
@@ -625,7 +636,7 @@ class _MixedQuantBase(nn.Module):
                 continue
             p = _candidate_cache_path(name, qt, "lazy", wh, ih)
             if p.exists():
-                found[qt] = torch.load(p, weights_only=True, map_location="cpu", mmap=True)
+                found[qt] = _load_cache_file(p, name)
             else:
                 missing.append((qt, p))
         if missing:
