@@ -128,7 +128,8 @@ def _layer(types, w, bytes_full, probs_gates, spec=None):
     return layer
 
 
-def test_halo_row_parallel_layer_sums_to_the_full_layer():
+@pytest.mark.parametrize("width", [640, 320])  # 2 ranks (offsets 0, 128) / 4 ranks (0, 64, 128, 192)
+def test_halo_row_parallel_layer_sums_to_the_full_layer(width):
     import cpu_kernels
     from voodoo_quant.parallel import ShardSpec
     from voodoo_quant.quants import rtn
@@ -149,19 +150,21 @@ def test_halo_row_parallel_layer_sums_to_the_full_layer():
         yf.backward(dy)
         y_sum = torch.zeros(T, out_f)
         g_sum = torch.zeros(len(types))
-        for r in range(2):
-            spec = ShardSpec(full_out=out_f, full_in=in_f, col_offset=640 * r, col_len=640, halo=True)
+        for r in range(in_f // width):
+            c0, c1 = width * r, width * (r + 1)
+            spec = ShardSpec(full_out=out_f, full_in=in_f, col_offset=c0, col_len=width, halo=True)
             part = _layer(types, w, cand, gates, spec)
-            assert part.in_col_offset == 128 * r and part.padded_in_features == 768
-            assert part._w_0.shape == (out_f, 640)
-            assert torch.equal(part._w_2, full._w_2[:, 640 * r:640 * (r + 1)])
-            assert torch.equal(part.get_mixed_weight(), full.get_mixed_weight()[:, 640 * r:640 * (r + 1)])
-            xr = x[:, 640 * r:640 * (r + 1)].clone().requires_grad_(True)
+            assert part.in_col_offset == c0 % 256
+            assert part.padded_in_features == ((c1 + 255) // 256 - c0 // 256) * 256
+            assert part._w_0.shape == (out_f, width)
+            assert torch.equal(part._w_2, full._w_2[:, c0:c1])
+            assert torch.equal(part.get_mixed_weight(), full.get_mixed_weight()[:, c0:c1])
+            xr = x[:, c0:c1].clone().requires_grad_(True)
             yr = part(xr)
             yr.backward(dy)
             y_sum += yr.detach().float()
             g_sum += part.gates.grad
-            assert torch.equal(xr.grad, xf.grad[:, 640 * r:640 * (r + 1)]), r
+            assert torch.equal(xr.grad, xf.grad[:, c0:c1]), r
     finally:
         undo()
     yf = yf.detach().float()
