@@ -647,7 +647,8 @@ def run_model_step(args):
                                                  ce_reduction="tokens" if args.logits_chunk > 0 or args.graph_step
                                                  else "valid", static_shapes=args.graph_step,
                                                  teacher_stream=args.teacher_stream,
-                                                 teacher_stream_sms=args.teacher_stream_sms))
+                                                 teacher_stream_sms=args.teacher_stream_sms,
+                                                 teacher_tp=args.teacher_tp))
     from voodoo_quant import parallel as _par
 
     multicast_on = _par.multicast_reducer() is not None
@@ -735,6 +736,7 @@ def run_model_step(args):
                        "logits_chunk": args.logits_chunk, "peak_alloc_gb_rank0": round(peak_gb, 2),
                        "step_graph": "forward + backward replayed from one CUDA graph" if args.graph_step
                        else "eager",
+                       "teacher_tp": args.teacher_tp or world,
                        "teacher": (f"own stream and communicator beside the student, "
                                    f"{args.teacher_stream_sms} SMs left to collectives") if args.teacher_stream
                        else "after the student, same stream",
@@ -853,6 +855,9 @@ def main():
     ap.add_argument("--teacher-stream-sms", type=int, default=0,
                     help="with --teacher-stream: SMs the forward GEMMs leave to the other stream's all-reduces "
                          "(and the teacher communicator's CTA cap); 0 = none")
+    ap.add_argument("--teacher-tp", type=int, default=0,
+                    help="full-step workloads under TP: the teacher's own TP degree t (groups of t ranks, each on "
+                         "its batch slice; one all-to-all of its logits); 0 = the student's")
     ap.add_argument("--layers", type=int, default=0,
                     help="full-step workloads: build only this many decoder layers (a smoke run of the build, "
                          "memory plan and step; its line says so and is not the configuration's number)")

@@ -172,6 +172,69 @@ def reset_tp() -> None:
     TP.forward_override = None
 
 
+def teacher_subgroups(t: int):
+    """Split the TP ranks into world / t groups of t consecutive ranks, one
+    communicator each, for a teacher sharded t ways that runs on 1 / (world / t)
+    of the batch per group.  Collective: every rank calls it with the same t.
+    Returns (this rank's group, its index, the rank's index within it)."""
+    W, r = TP.world_size, TP.rank
+    if t < 1 or W % t:
+        raise ValueError(f"teacher TP degree {t} does not divide the TP world size {W}")
+    mine = None
+    for g in range(W // t):
+        grp = dist.new_group(ranks=list(range(g * t, (g + 1) * t)), backend=dist.get_backend(TP.group))
+        if g == r // t:
+            mine = grp
+    return mine, r // t, r % t
+
+
+@contextlib.contextmanager
+def as_tp(rank: int, world: int, group):
+    """Inside the block this process is rank ``rank`` of a TP group of
+    ``world`` ranks on ``group`` (a sub-group of the TP ranks): what the arch
+    adapters read when they shard a model (``tp_patch_model``)."""
+    saved = (TP.rank, TP.world_size, TP.group)
+    TP.rank, TP.world_size, TP.group = rank, world, group
+    try:
+        yield
+    finally:
+        TP.rank, TP.world_size, TP.group = saved
+
+
+def redistribute_vocab_shards(local: torch.Tensor, t: int, group=None) -> torch.Tensor:
+    """Teacher logits from the (batch-slice, t-way vocabulary) layout to the
+    student's (whole batch, world-way vocabulary) layout, in one all-to-all.
+
+    ``local`` is this rank's [b, S, V / t]: the rows of batch slice g = rank // t
+    (b = B / G, G = world / t groups) and vocabulary part h = rank % t.  Student
+    rank r needs every row over columns [r V / world, (r + 1) V / world), which
+    lie in teacher part r // G; so rank (g, h) sends its G column chunks to
+    student ranks h G ... h G + G - 1 and each rank receives one [b, S, V / world]
+    chunk from rank (g', r // G) of every group g'.  Returns [B, S, V / world]."""
+    W, r = TP.world_size, TP.rank
+    G = W // t
+    h = r % t
+    b, S, Vt = local.shape
+    if Vt % G:
+        raise ValueError(f"teacher vocabulary part {Vt} does not split into {G} student slices")
+    Vw = Vt // G
+    n = b * S * Vw
+    send = local.reshape(b * S, G, Vw).permute(1, 0, 2).contiguous()  # chunk j -> student rank h G + j
+    in_splits, out_splits = [0] * W, [0] * W
+    for j in range(G):
+        in_splits[h * G + j] = n
+    for g2 in range(G):
+        out_splits[g2 * t + r // G] = n
+    # all-to-all moves bytes only: 16-bit logits travel as float16 bit patterns
+    # (every backend carries float16)
+    wire = send.view(torch.float16) if send.dtype == torch.bfloat16 else send
+    out = torch.empty(G * n, dtype=wire.dtype, device=local.device)
+    dist.all_to_all_single(out, wire.reshape(-1), out_splits, in_splits, group=group)
+    if send.dtype == torch.bfloat16:
+        out = out.view(torch.bfloat16)
+    return out.view(G * b, S, Vw)
+
+
 def enable_input_grad_overlap(sms: int) -> bool:
     """Run input-gradient all-reduces beside the gate-gradient GEMMs.
 

@@ -94,6 +94,13 @@ class StepArgs:
     # with teacher_stream: SMs the forward GEMMs of both models leave free for
     # the other stream's all-reduces (and the teacher's communicator's CTA cap); 0 = none
     teacher_stream_sms: int = 0
+    # TP degree of the teacher (0 = the student's): the teacher is sharded t
+    # ways inside groups of t consecutive ranks, each group runs it on its
+    # slice of the batch (the batch divides into world / t slices), and one
+    # all-to-all hands every rank its vocabulary slice of all the teacher's
+    # logits; each teacher all-reduce then moves 1 / (world / t) of the
+    # tokens among t ranks.  Plain loss path only (logits_chunk = 0).
+    teacher_tp: int = 0
 
 
 class GatedDistillTrainer:
@@ -117,6 +124,7 @@ class GatedDistillTrainer:
         set_static_shapes(args.static_shapes)
         self._graph = None
         self._tstream = None
+        self._tsplit = None  # (group, group index, rank in group, t) with a teacher of its own TP degree
         self.optimizer = torch.optim.AdamW(self.trainable, lr=args.lr, betas=(0.9, 0.95))
         self.scheduler = torch.optim.lr_scheduler.CosineAnnealingLR(self.optimizer, T_max=args.max_steps,
                                                                     eta_min=1e-3)
@@ -145,13 +153,13 @@ class GatedDistillTrainer:
             return self._forward_backward_chunked(x, y, a, tau, v0)
         if a.teacher_stream:
             with self._forward_sm_reserve():
-                t_logits = self._teacher_fork(x, lambda: self.teacher(input_ids=x, use_cache=False).logits)
+                t_logits = self._teacher_fork(x, lambda: self._teacher_logits(x))
                 logits = self.student(input_ids=x, use_cache=False).logits
             t_logits = self._teacher_join(t_logits)
         else:
             logits = self.student(input_ids=x, use_cache=False).logits
             with torch.no_grad():
-                t_logits = self.teacher(input_ids=x, use_cache=False).logits
+                t_logits = self._teacher_logits(x)
         if self.tp and v0 is not None:
             kd, lm, kl = tp_distillation_loss(logits, t_logits, y, v0, a.distill_temperature, a.distill_weight,
                                               ce_reduction="tokens")
@@ -229,6 +237,25 @@ class GatedDistillTrainer:
         loss = kd + a.size_weight * size_loss.detach()
         return {"loss": loss, "lm_loss": lm, "distill_loss": kl, "size_bytes": current.detach(),
                 "size_loss": size_loss.detach(), "tau": tau}
+
+    def _teacher_logits(self, x: torch.Tensor) -> torch.Tensor:
+        """The teacher's logits in the student's layout.  With a teacher of
+        its own TP degree, this rank's group runs the teacher on its batch
+        slice (collectives inside the group) and one all-to-all, on the
+        communicator the forward's collectives use here, redistributes the
+        vocabulary shards."""
+        if self._tsplit is None:
+            return self.teacher(input_ids=x, use_cache=False).logits
+        from voodoo_quant.parallel import TP, _fwd_group, collectives_on, redistribute_vocab_shards
+
+        group, g, _, t = self._tsplit
+        G = TP.world_size // t
+        if x.shape[0] % G:
+            raise ValueError(f"batch {x.shape[0]} does not split over {G} teacher groups (teacher_tp={t})")
+        b = x.shape[0] // G
+        with collectives_on(group):
+            local = self.teacher(input_ids=x[g * b:(g + 1) * b], use_cache=False).logits
+        return redistribute_vocab_shards(local, t, group=_fwd_group())
 
     def _teacher_fork(self, x: torch.Tensor, run):
         """Issue the teacher's forward (``run``) on the teacher's stream, after
@@ -397,8 +424,21 @@ def build_distill(shape_name: str, device, seed: int = 0, args: StepArgs | None 
     if torch.device(device).type == "cuda":
         torch.cuda.empty_cache()
     teacher = S.build_llama(shape, device, seed=seed)
+    tsplit = None
     if tp and TP.enabled:
-        tp_patch_model(teacher, verbose=False)
+        t = (args.teacher_tp if args is not None else 0) or TP.world_size
+        if t != TP.world_size:
+            from voodoo_quant.parallel import as_tp, teacher_subgroups
+
+            if args.logits_chunk > 0:
+                raise ValueError("teacher_tp needs the plain loss path (logits_chunk=0)")
+            group, g, h = teacher_subgroups(t)
+            if t > 1:
+                with as_tp(h, t, group):
+                    tp_patch_model(teacher, verbose=False)
+            tsplit = (group, g, h, t)
+        else:
+            tp_patch_model(teacher, verbose=False)
     wrap_q8_teacher(teacher, S.q8_quantizer)
     if fused_blocks and torch.device(device).type == "cuda":
         from voodoo_quant.fused_blocks import fuse_llama_blocks
@@ -422,4 +462,5 @@ def build_distill(shape_name: str, device, seed: int = 0, args: StepArgs | None 
     torch.cuda.empty_cache()
     trainer = GatedDistillTrainer(base, teacher, replaced, args or StepArgs(), shape.budget * total_8bit,
                                   non_targeted, tp=tp and TP.enabled)
+    trainer._tsplit = tsplit
     return trainer, shape
