@@ -125,6 +125,7 @@ class GatedDistillTrainer:
         self._graph = None
         self._tstream = None
         self._tsplit = None  # (group, group index, rank in group, t) with a teacher of its own TP degree
+        self._graph_keep = []  # tensors two streams of a recorded graph share
         self.optimizer = torch.optim.AdamW(self.trainable, lr=args.lr, betas=(0.9, 0.95))
         self.scheduler = torch.optim.lr_scheduler.CosineAnnealingLR(self.optimizer, T_max=args.max_steps,
                                                                     eta_min=1e-3)
@@ -267,8 +268,7 @@ class GatedDistillTrainer:
         if self._tstream is None:
             self._tstream = torch.cuda.Stream()
         self._tstream.wait_stream(torch.cuda.current_stream())
-        if x.is_cuda:
-            x.record_stream(self._tstream)
+        self._cross_stream_use(x, self._tstream)
         with torch.cuda.stream(self._tstream), collectives_on(TP.teacher_group), torch.no_grad():
             return run()
 
@@ -294,9 +294,18 @@ class GatedDistillTrainer:
         used (and its memory held) on the current stream."""
         main = torch.cuda.current_stream()
         main.wait_stream(self._tstream)
-        if t.is_cuda:
-            t.record_stream(main)
+        self._cross_stream_use(t, main)
         return t
+
+    def _cross_stream_use(self, t: torch.Tensor, stream) -> None:
+        """``t`` is used on ``stream`` too: tell the allocator (eager), or,
+        while a graph is recorded, keep it alive with the graph."""
+        if not t.is_cuda:
+            return
+        if _capturing():
+            self._graph_keep.append(t)
+        else:
+            t.record_stream(stream)
 
     def apply_update(self) -> None:
         torch.nn.utils.clip_grad_norm_(self.trainable, max_norm=1.0)
@@ -361,6 +370,7 @@ class GatedDistillTrainer:
         collectives it holds)."""
         self._graph = None
         self._gout = None
+        self._graph_keep = []
 
     def assignments(self) -> dict[str, str]:
         return {name: layer.get_assignment() for name, layer in self.replaced.items()}
