@@ -479,6 +479,23 @@ def cpu_baseline(t_sample: int, repeats: int = 1):
                       f"(BLAS threads = {cores}); candidates pre-decoded like the reference's cached _w_k"}
 
 
+def step_cpu_baseline(t_sample: int, flops_per_token: float):
+    """The full step's host baseline, from a bounded sample: the reference's
+    algorithm on the host (the float32 port) runs the gated-Linear step
+    (forward, dX, gate gradient) of an 8B-MLP-shaped layer [14336 x 4096],
+    K = 5, on ``t_sample`` tokens; its achieved GFLOP/s over the step's
+    algorithmic FLOPs per token gives the tokens/s the host would reach on
+    the whole step at that rate (attention and the loss run at GEMM speed in
+    this estimate, which flatters the host)."""
+    base = cpu_baseline(t_sample)
+    gflops = base["value"] * 6 * N_OUT * K_IN / 1e9
+    return {"value": round(gflops * 1e9 / flops_per_token, 3), "unit": "tokens/s", "cores": base["cores"],
+            "kind": "port", "gflops": round(gflops, 1),
+            "sample": f"{t_sample} tokens of an 8B-MLP-shaped gated layer [14336 x 4096], K=5, fwd + dX + gate "
+                      f"grad, float32 numpy on {base['cores']} threads = {gflops:.1f} GFLOP/s, divided by the "
+                      f"step's {flops_per_token / 1e9:.2f} GFLOP per token"}
+
+
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -752,6 +769,8 @@ def run_model_step(args):
             "loss_last": round(float(out["loss"]), 4),
             "size_bytes_last": float(out["size_bytes"]),
         }
+        if world == 1 and not args.no_cpu_baseline:
+            res["cpu_baseline"] = step_cpu_baseline(args.cpu_tokens, fpt)
         print(json.dumps(res), flush=True)
     trainer.release_graph()  # the graph holds collectives: drop it before the process group
     torch.cuda.synchronize()
