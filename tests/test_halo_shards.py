@@ -208,12 +208,14 @@ def _shapes():
         batch=2, seq=24, budget=0.30, row_scale_sigma=0.5)
 
 
-def _step(tp: bool):
+def _step(tp: bool, overlap_sms: int = 0):
     from voodoo_quant.training import synthetic as S
     from voodoo_quant.training.trainer import StepArgs, build_distill
 
     trainer, shape = build_distill("cpu_halo", "cpu", seed=3, args=StepArgs(max_steps=4, ce_reduction="tokens"),
-                                   tp=tp)
+                                   tp=tp, overlap_sms=overlap_sms)
+    if overlap_sms:  # the halo o_proj's gate-gradient GEMM is deferred beside the input-gradient all-reduce
+        assert trainer.replaced["model.layers.0.self_attn.o_proj"].__dict__.get("_defer_gategrad", False)
     x, y = S.random_tokens(shape, "cpu", seed=5)
     r = trainer.forward_backward(x, y)
     grads = {n: m.gates.grad.detach().clone() for n, m in trainer.replaced.items()}
@@ -234,7 +236,10 @@ def _worker(rank, world, port, outdir):
     undo = cpu_kernels.install()
     try:
         P.adopt_process_group(0)
-        torch.save(_step(True), os.path.join(outdir, f"r{rank}.pt"))
+        # plain, and with the gate-gradient GEMMs deferred beside the input-gradient
+        # all-reduces (the benchmark's TP default)
+        torch.save({"plain": _step(True), "deferred": _step(True, overlap_sms=24)},
+                   os.path.join(outdir, f"r{rank}.pt"))
     finally:
         undo()
         P.reset_tp()
@@ -263,12 +268,17 @@ def test_tp2_step_with_halo_o_proj_matches_one_process():
     o_proj = "model.layers.0.self_attn.o_proj"
     assert ref[2][o_proj] == ["Q4_K", "IQ4_XS", "Q8_0"]
     assert ref[2]["model.layers.0.mlp.down_proj"] == ["IQ4_XS", "Q3_K", "Q4_K", "Q8_0", "Q2_K"]
-    assert [r[3][o_proj] for r in rs] == [0, 128]
-    for r in rs:
+    assert [r["plain"][3][o_proj] for r in rs] == [0, 128]
+    for rr in rs:
+        r = rr["plain"]
         assert r[2] == ref[2]
         assert abs(r[0] - ref[0]) <= 2e-2 * abs(ref[0])
         for n, g in ref[1].items():
             assert _cos(r[1][n], g) > 0.999, n
             assert float((r[1][n] - g).norm()) <= 2e-2 * float(g.norm()) + 1e-9, n
+        # deferring the GEMMs changes when they run, not a value
+        d = rr["deferred"]
+        assert d[0] == r[0]
+        assert all(torch.equal(d[1][n], r[1][n]) for n in r[1])
     for n in ref[1]:
-        assert torch.equal(rs[0][1][n], rs[1][1][n]), n
+        assert torch.equal(rs[0]["plain"][1][n], rs[1]["plain"][1][n]), n
