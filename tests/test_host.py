@@ -306,3 +306,16 @@ def test_reference_arm_prints_one_contract_line():
     assert out["impl"] == "reference" and out["value"] > 0 and out["unit"] == "tokens/s"
     assert out["cpu_baseline"]["kind"] == "port" and out["cpu_baseline"]["cores"] >= 1
     assert out["e2e"]["h2d_bytes_per_step"] == 0 and "workload" in out["config"]
+
+
+def test_full_step_host_baseline_scales_the_layer_sample():
+    """The full-step lines' host baseline: the layer sample's GFLOP/s over the
+    step's FLOPs per token."""
+    import bench
+    from voodoo_quant.training import synthetic as S
+
+    fpt = bench.step_flops_per_token(S.SHAPES["8b"])
+    r = bench.step_cpu_baseline(32, fpt)
+    assert r["kind"] == "port" and r["unit"] == "tokens/s" and r["cores"] >= 1 and r["gflops"] > 0
+    assert abs(r["value"] - r["gflops"] * 1e9 / fpt) <= 1e-3 * r["value"] + 1e-3
+    assert "GFLOP per token" in r["sample"]
