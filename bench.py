@@ -1,23 +1,31 @@
-"""Benchmark of the gated-candidate training step on B200.
+"""Benchmark of the gated-candidate distillation step on B200.
 
-Workload (the single-GPU case the metric is quoted
-on): one gated Linear, X [8192 x 4096] bf16 N(0,1) with 1% of the channels
-(41, seeded randperm) scaled x20, base W [14336 x 4096] N(0, 0.02), K=5 packed
-candidates {Q3_K, Q4_K, Q5_K, Q6_K, Q8_0}, gates N(0,1), tau = 0.5,
-dY N(0,1).  A step is forward + dX + gate gradient through MixedQuantLinear's
-autograd (the public API): vq_mix, vq_linear_fwd, vq_linear_dx, vq_gategrad.
-Tokens per step = 8192.  Candidates are built by the round-to-nearest packer
-(libggml is unavailable), seeded; inputs are synthetic.
+Default workload (the configuration the metric
+"gated-distill train tokens/s at 1/2/4/8 B200" is quoted on): the full
+distillation step of a random-init 8B Llama-3-shape decoder -- 32 layers,
+hidden 4096, 32 query / 8 KV heads, SwiGLU 14336, vocabulary 128256, untied
+-- whose every Linear and the embedding are gated over K = 6 packed
+candidates (Q2_K ... Q8_0), against a Q8_0 teacher of the same weights;
+batch 4 x seq 4096 = 16384 tokens per step, loss CE + 1.0 KL, size budget
+30 %.  A step is the reference's step loop (voodoo_quant/training/trainer.py:
+2443-2666): student forward, teacher forward, fused loss, size term,
+backward, gate all-reduce, clip, AdamW, cosine LR.  Candidates come from the
+round-to-nearest GGUF packer (libggml is unavailable); weights and tokens are
+seeded synthetic draws.
 
---gpus N (torchrun, one process per GPU): the same layer tensor-parallel,
-column-parallel over its 14336 output rows (block-aligned split), with the
-exchange steps of a TP column-parallel layer: all-reduce of dX (exact input
-gradient) and all-reduce of the K gate gradients.  Total work is fixed
-("strong" scaling); value = tokens / max-over-ranks step time.
+--gpus N (torchrun, one process per GPU): both models tensor-parallel over
+the N GPUs (Llama adapter); every rank runs the same batch, total work is
+fixed ("strong" scaling); value = tokens / max-over-ranks step time.
 
---impl reference: the CPU path (the numpy restatement of the reference's
-float32 torch algorithm, layers.py:322-363 + F.linear) on the host cores, on
-a bounded token sample of the same layer, reported in the same unit.
+The line also carries ``mix_gemm``: the metric's second half, the fused
+mix-GEMM kernels of BASELINE.json configs[1] (one gated Linear X [8192 x 4096],
+W [14336 x 4096], K = 5) as fractions of the measured bf16 peak, timed on
+rank 0's GPU in the same run.  ``--workload layer`` makes that layer the
+whole benchmark.
+
+--impl reference: the reference's algorithm on the host cores (the float32
+numpy port of its torch CPU path, layers.py:322-363 + F.linear), on a bounded
+sample of the same workload, reported in the same unit (see run_reference).
 """
 
 from __future__ import annotations
@@ -38,12 +46,19 @@ T_TOK, N_OUT, K_IN = 8192, 14336, 4096
 TYPES = ["Q3_K", "Q4_K", "Q5_K", "Q6_K", "Q8_0"]
 TAU = 0.5
 METRIC = "gated-distill train tokens/s"
+LAYER_METRIC = "gated-Linear fwd + dX + gate-grad tokens/s (config 2)"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 # dram__bytes_read.sum + dram__bytes_write.sum per launch of each config-2 GEMM
 # at full size on one B200, from a single-pass ncu capture of this benchmark
 NCU_TRAFFIC_BYTES = {"fwd": 818.1e6, "dx": 1032.6e6, "gategrad": 1115.4e6}
 BPW = {"Q2_K": 84 / 256, "Q3_K": 110 / 256, "Q4_K": 144 / 256, "Q5_K": 176 / 256, "Q6_K": 210 / 256,
        "Q8_0": 34 / 32, "IQ4_XS": 136 / 256}
+WORKLOAD_NAMES = {
+    "tiny": "config1: tiny Llama gated distillation step",
+    "0.6b": "config3: ~0.6B dense decoder gated distillation step",
+    "8b": "config4: 8B Llama-3-shape gated distillation step",
+    "32b": "config5: 32B-shape dense decoder gated distillation step",
+}
 
 
 def peaks():
@@ -54,7 +69,7 @@ def peaks():
     return dict(FALLBACK_PEAKS), "fallback"
 
 
-def config(n_gpus: int, extra=None):
+def layer_config(n_gpus: int, extra=None):
     c = {
         "workload": "config2: gated Linear X[8192x4096] W[14336x4096], K=5 {Q3_K,Q4_K,Q5_K,Q6_K,Q8_0}, "
                     "tau=0.5, fwd+dX+gate-grad",
@@ -66,6 +81,18 @@ def config(n_gpus: int, extra=None):
     if extra:
         c.update(extra)
     return c
+
+
+def step_config(workload: str, shape, world: int) -> dict:
+    """The step workload's description: a function of the workload and N only,
+    so both arms print the same object."""
+    return {"workload": WORKLOAD_NAMES.get(workload, workload), "layers": shape.layers, "hidden": shape.hidden,
+            "heads": shape.heads, "kv_heads": shape.kv_heads, "ffn": shape.ffn, "vocab": shape.vocab,
+            "tied": shape.tied, "batch": shape.batch, "seq": shape.seq, "tokens_per_step": shape.batch * shape.seq,
+            "candidates": shape.candidates, "attention_candidates": shape.attention_candidates,
+            "row_scale_sigma": shape.row_scale_sigma, "budget": shape.budget, "loss": "CE + 1.0 * T^2 KL, T = 1",
+            "parallelism": f"tp{world}",
+            "l2": "activations, logits and packed candidates far larger than L2"}
 
 
 # ----------------------------------------------------------------------------- clocks
@@ -144,7 +171,7 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(inside), "samples_total": len(rows)}
 
 
-# ----------------------------------------------------------------------------- setup
+# ----------------------------------------------------------------------------- config-2 layer
 def make_layer(device, rank=0, world=1):
     import torch
     from voodoo_quant.layers import MixedQuantLinear
@@ -181,7 +208,80 @@ def make_inputs(device, n_out_local, seed=2):
     return x, dy
 
 
-# ----------------------------------------------------------------------------- GPU arm
+def time_layer_kernels(layer, x, dy, iters: int) -> dict:
+    """Average CUDA-event time (ms) of each kernel of the layer step, launched
+    back to back on the current stream: mix, forward GEMM, dX GEMM, gate-grad
+    GEMM (inputs larger than L2, so each launch streams from HBM)."""
+    import torch
+    from voodoo_quant import _C
+
+    stream = torch.cuda.current_stream()
+    n_loc = layer.out_features
+    blocks = layer._candidate_blocks()
+    probs = layer.get_probs().detach()
+    pad = layer.padded_in_features
+    ws = layer._gategrad_workspace(x.device)
+    wm = _C.mix(TYPES, blocks, probs, n_loc, pad, K_IN)
+    names = ["mix", "fwd", "dx", "gategrad"]
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(iters)]
+    for i in range(iters + 2):
+        e = evs[i - 2] if i >= 2 else None
+        if e: e[0].record(stream)
+        _C.mix(TYPES, blocks, probs, n_loc, pad, K_IN, out=wm)
+        if e: e[1].record(stream)
+        _C.linear_fwd(x, wm, n_loc, K_IN)
+        if e: e[2].record(stream)
+        _C.linear_dx(dy, wm, K_IN)
+        if e: e[3].record(stream)
+        _C.gategrad(dy, x, TYPES, blocks, n_loc, K_IN, pad, workspace=ws)
+        if e: e[4].record(stream)
+    torch.cuda.synchronize()
+    return {n: sum(e[j].elapsed_time(e[j + 1]) for e in evs) / len(evs) for j, n in enumerate(names)}
+
+
+def layer_kernel_summary(kt: dict, n_loc: int) -> dict:
+    """Per-kernel TFLOP/s (GEMMs: 2 T N Kin each) or GB/s (mix: packed bytes
+    read + bf16 W_mix written) and fractions of the measured burst peaks."""
+    pk, pk_kind = peaks()
+    peak_t = float(pk.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
+    peak_b = float(pk.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
+    flops_gemm = 2.0 * T_TOK * n_loc * K_IN
+    ach = {n: flops_gemm / (kt[n] * 1e-3) / 1e12 for n in ("fwd", "dx", "gategrad")}
+    mix_bytes = n_loc * K_IN * sum(BPW[q] for q in TYPES) + n_loc * K_IN * 2
+    kernels = {n: {"ms": round(kt[n], 4), "TFLOP/s": round(ach[n], 1), "frac": round(ach[n] / peak_t, 4)}
+               for n in ("fwd", "dx", "gategrad")}
+    kernels["mix"] = {"ms": round(kt["mix"], 4), "GB/s": round(mix_bytes / (kt["mix"] * 1e-3) / 1e9, 1),
+                      "frac": round(mix_bytes / (kt["mix"] * 1e-3) / 1e9 / peak_b, 4),
+                      "algorithmic_bytes": int(mix_bytes)}
+    gemm_ms = kt["fwd"] + kt["dx"] + kt["gategrad"]
+    all_ms = gemm_ms + kt["mix"]
+    return {"kernels": kernels, "peak_tflops": peak_t, "peak_gbs": peak_b,
+            "peak_source": f"{pk_kind} bf16_tflops / hbm_gbs (burst)",
+            "mix_gemm_frac": round(3 * flops_gemm / (gemm_ms * 1e-3) / 1e12 / peak_t, 4),
+            "mix_gemm_with_mix_frac": round(3 * flops_gemm / (all_ms * 1e-3) / 1e12 / peak_t, 4),
+            "ach": ach}
+
+
+def layer_kernel_fractions(dev, iters: int = 10) -> dict:
+    """The metric's second half on this GPU: the config-2 gated Linear's
+    kernels (mix, forward, dX, gate-grad GEMMs) as fractions of the measured
+    bf16 / HBM peaks; the layer is freed afterwards."""
+    import torch
+
+    layer = make_layer(dev)
+    x, dy = make_inputs(dev, N_OUT)
+    kt = time_layer_kernels(layer, x, dy, iters)
+    s = layer_kernel_summary(kt, N_OUT)
+    del layer, x, dy
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    s.pop("ach")
+    s["workload"] = layer_config(1)["workload"]
+    s["gemm_flops_each"] = 2.0 * T_TOK * N_OUT * K_IN
+    return s
+
+
+# ----------------------------------------------------------------------------- GPU arm: config-2 layer
 def run_gpu(args):
     import torch
     import torch.distributed as dist
@@ -300,26 +400,7 @@ def run_gpu(args):
     assert _C.device_error() == 0
 
     # ---- per-kernel breakdown (same stream, CUDA events per launch) ----
-    blocks = layer._candidate_blocks()
-    probs = layer.get_probs().detach()
-    pad = layer.padded_in_features
-    ws = layer._gategrad_workspace(dev)
-    wm = _C.mix(TYPES, blocks, probs, n_loc, pad, K_IN)
-    names = ["mix", "fwd", "dx", "gategrad"]
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(args.kernel_iters)]
-    for i in range(args.kernel_iters + 2):
-        e = evs[i - 2] if i >= 2 else None
-        if e: e[0].record(stream)
-        _C.mix(TYPES, blocks, probs, n_loc, pad, K_IN, out=wm)
-        if e: e[1].record(stream)
-        _C.linear_fwd(x, wm, n_loc, K_IN)
-        if e: e[2].record(stream)
-        _C.linear_dx(dy, wm, K_IN)
-        if e: e[3].record(stream)
-        _C.gategrad(dy, x, TYPES, blocks, n_loc, K_IN, pad, workspace=ws)
-        if e: e[4].record(stream)
-    torch.cuda.synchronize()
-    kt = {n: sum(e[j].elapsed_time(e[j + 1]) for e in evs) / len(evs) for j, n in enumerate(names)}
+    kt = time_layer_kernels(layer, x, dy, args.kernel_iters)
 
     # ---- e2e through the public API with host buffers ----
     # Every step copies its X and dY from pinned host memory and reads the
@@ -371,21 +452,12 @@ def run_gpu(args):
     e2e_ms = float(e2e_ms.item())
 
     if rank == 0:
-        pk, pk_kind = peaks()
-        flops_gemm = 2.0 * T_TOK * n_loc * K_IN
-        ach = {n: flops_gemm / (kt[n] * 1e-3) / 1e12 for n in ("fwd", "dx", "gategrad")}
-        packed = n_loc * K_IN * sum(BPW[q] for q in TYPES)
-        mix_bytes = packed + n_loc * K_IN * 2
+        s = layer_kernel_summary(kt, n_loc)
+        ach, peak_t = s["ach"], s["peak_tflops"]
         dom = max(("fwd", "dx", "gategrad"), key=lambda n: kt[n])
-        peak_t = float(pk.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
-        peak_b = float(pk.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
-        kernels = {n: {"ms": round(kt[n], 4), "TFLOP/s": round(ach[n], 1), "frac": round(ach[n] / peak_t, 4)}
-                   for n in ("fwd", "dx", "gategrad")}
-        kernels["mix"] = {"ms": round(kt["mix"], 4), "GB/s": round(mix_bytes / (kt["mix"] * 1e-3) / 1e9, 1),
-                          "frac": round(mix_bytes / (kt["mix"] * 1e-3) / 1e9 / peak_b, 4)}
-        gemm_ms = kt["fwd"] + kt["dx"] + kt["gategrad"]
+        flops_gemm = 2.0 * T_TOK * n_loc * K_IN
         out = {
-            "metric": METRIC,
+            "metric": LAYER_METRIC,
             "value": round(T_TOK / (ms * 1e-3), 1),
             "unit": "tokens/s",
             "n_gpus": world,
@@ -397,9 +469,9 @@ def run_gpu(args):
             "vs_baseline": None,
             "dtype": "bf16",
             "data": "synthetic (seeded; candidates from the round-to-nearest GGUF packer)",
-            "config": config(world, {"timed_step": graph_note,
-                                     "dx_allreduce_overlap_sms": args.overlap_sms if world > 1 else 0,
-                                     "dx_chunks": args.dx_chunks if world > 1 else 1}),
+            "config": layer_config(world),
+            "run": {"timed_step": graph_note, "dx_allreduce_overlap_sms": args.overlap_sms if world > 1 else 0,
+                    "dx_chunks": args.dx_chunks if world > 1 else 1},
             "roofline": {
                 "bound": "tensor",
                 "kernel": f"gemm_{dom}",
@@ -407,13 +479,13 @@ def run_gpu(args):
                 "peak": peak_t,
                 "unit": "TFLOP/s",
                 "frac": round(ach[dom] / peak_t, 4),
-                "peak_source": f"{pk_kind} bf16_tflops (burst)",
+                "peak_source": s["peak_source"],
                 "traffic": NCU_TRAFFIC_BYTES[dom] if world == 1 else None,
                 "traffic_unit": "bytes per launch (ncu dram read+write, full size)",
-                "mix_gemm_frac": round(3 * flops_gemm / (gemm_ms * 1e-3) / 1e12 / peak_t, 4),
+                "mix_gemm_frac": s["mix_gemm_frac"],
                 "step_frac": round(3 * flops_gemm / (ms * 1e-3) / 1e12 / peak_t, 4),
             },
-            "kernels": kernels,
+            "kernels": s["kernels"],
             "e2e": {
                 "value": round(T_TOK / (e2e_ms * 1e-3), 1),
                 "unit": "tokens/s",
@@ -424,7 +496,7 @@ def run_gpu(args):
             "clocks": clocks,
         }
         if world == 1 and not args.no_cpu_baseline:
-            out["cpu_baseline"] = cpu_baseline(args.cpu_tokens, repeats=1)
+            out["cpu_baseline"] = layer_cpu_baseline(args.cpu_tokens, repeats=1)
         print(json.dumps(out), flush=True)
     graph = None  # the captured graph holds NCCL work: release it before the process group
     torch.cuda.synchronize()
@@ -433,8 +505,12 @@ def run_gpu(args):
         dist.destroy_process_group()
 
 
-# ----------------------------------------------------------------------------- CPU (reference) arm
-def _cpu_setup(t_sample: int):
+# ----------------------------------------------------------------------------- host (reference algorithm)
+def _host_threads() -> int:
+    return os.cpu_count() or 1
+
+
+def _layer_host_setup(t_sample: int):
     import numpy as np
     import torch
 
@@ -446,7 +522,7 @@ def _cpu_setup(t_sample: int):
     w = torch.randn(N_OUT, K_IN) * 0.02
     blocks = [rtn.quantize(w, q).numpy() for q in TYPES]
     del w
-    threads = os.cpu_count() or 1
+    threads = _host_threads()
     cands = mixgemm.decode_candidates(blocks, TYPES, N_OUT, K_IN, K_IN, threads=threads)  # untimed (cached _w_k)
     rng = np.random.default_rng(2)
     x = rng.standard_normal((t_sample, K_IN), dtype=np.float32)
@@ -456,8 +532,8 @@ def _cpu_setup(t_sample: int):
     return mixgemm, cands, x, dy, gates
 
 
-def _cpu_step(mixgemm, cands, x, dy, gates):
-    threads = os.cpu_count() or 1
+def _layer_host_step(mixgemm, cands, x, dy, gates):
+    threads = _host_threads()
     p = mixgemm.softmax_probs(gates, TAU)
     wm = mixgemm.mixed_weight(cands, p, threads=threads)
     mixgemm.linear_fwd(x, wm)
@@ -466,58 +542,187 @@ def _cpu_step(mixgemm, cands, x, dy, gates):
     return mixgemm.gate_grad(p, g, TAU)
 
 
-def cpu_baseline(t_sample: int, repeats: int = 1):
-    cores = os.cpu_count() or 1
-    mixgemm, cands, x, dy, gates = _cpu_setup(t_sample)
-    _cpu_step(mixgemm, cands, x, dy, gates)
+def layer_cpu_baseline(t_sample: int, repeats: int = 1):
+    cores = _host_threads()
+    mixgemm, cands, x, dy, gates = _layer_host_setup(t_sample)
+    _layer_host_step(mixgemm, cands, x, dy, gates)
     t0 = time.perf_counter()
     for _ in range(repeats):
-        _cpu_step(mixgemm, cands, x, dy, gates)
+        _layer_host_step(mixgemm, cands, x, dy, gates)
     dt = (time.perf_counter() - t0) / repeats
     return {"value": round(t_sample / dt, 2), "unit": "tokens/s", "cores": cores, "kind": "port",
             "sample": f"{t_sample} of 8192 tokens of the config-2 layer (full N, Kin, K=5), float32 numpy "
-                      f"(BLAS threads = {cores}); candidates pre-decoded like the reference's cached _w_k"}
+                      f"(BLAS threads = {cores}); candidates pre-decoded like the reference's cached _w_k; "
+                      f"value = sample tokens / measured sample time"}
 
 
-def step_cpu_baseline(t_sample: int, flops_per_token: float):
-    """The full step's host baseline, from a bounded sample: the reference's
-    algorithm on the host (the float32 port) runs the gated-Linear step
-    (forward, dX, gate gradient) of an 8B-MLP-shaped layer [14336 x 4096],
-    K = 5, on ``t_sample`` tokens; its achieved GFLOP/s over the step's
-    algorithmic FLOPs per token gives the tokens/s the host would reach on
-    the whole step at that rate (attention and the loss run at GEMM speed in
-    this estimate, which flatters the host)."""
-    base = cpu_baseline(t_sample)
-    gflops = base["value"] * 6 * N_OUT * K_IN / 1e9
-    return {"value": round(gflops * 1e9 / flops_per_token, 3), "unit": "tokens/s", "cores": base["cores"],
-            "kind": "port", "gflops": round(gflops, 1),
-            "sample": f"{t_sample} tokens of an 8B-MLP-shaped gated layer [14336 x 4096], K=5, fwd + dX + gate "
-                      f"grad, float32 numpy on {base['cores']} threads = {gflops:.1f} GFLOP/s, divided by the "
-                      f"step's {flops_per_token / 1e9:.2f} GFLOP per token"}
+def layer_linear_shapes(shape) -> list[tuple[str, int, int, list[str]]]:
+    """(role, out_features, in_features, candidate menu) of one decoder layer's
+    seven gated Linears (q, k, v, o, gate, up, down)."""
+    hd = shape.head_dim or shape.hidden // shape.heads
+    h, f = shape.hidden, shape.ffn
+    att = shape.attention_candidates or shape.candidates
+    mlp = shape.non_attention_candidates or shape.candidates
+    return [("q_proj", shape.heads * hd, h, att), ("k_proj", shape.kv_heads * hd, h, att),
+            ("v_proj", shape.kv_heads * hd, h, att), ("o_proj", h, shape.heads * hd, att),
+            ("gate_proj", f, h, mlp), ("up_proj", f, h, mlp), ("down_proj", h, f, mlp)]
+
+
+def gated_linear_params(shape) -> float:
+    """Weights of every gated Linear of the step's student (layers + head)."""
+    p_layer = sum(o * i for _, o, i, _ in layer_linear_shapes(shape))
+    return float(shape.layers * p_layer + (0 if shape.tied else shape.vocab * shape.hidden))
+
+
+class HostLayerSample:
+    """A bounded host sample of a distillation-step workload: one decoder
+    layer's seven gated Linears at the workload's shapes and menus, each
+    stepped as the reference's float32 torch CPU path does it (cached
+    decoded candidates W_k; W_mix = sum_k p_k W_k; Y = X W_mix^T;
+    dX = dY W_mix; dW = dY^T X materialised; g_k = <dW, W_k>; softmax
+    backward to the gates -- voodoo_quant/layers.py:322-363 and F.linear's
+    autograd), in the oracle's numpy port, on ``tokens`` tokens.
+
+    Each step's time splits into per-weight work (the mixture and the K
+    reductions over dW, done once per tensor per step whatever the batch) and
+    per-token work (the three GEMMs).  ``full_step_s`` scales the first by the
+    student's gated weights over the layer's and the second by the whole
+    step's algorithmic FLOPs (step_flops_per_token x tokens per step) over
+    the sample's: the host's time for the full step at the rates this sample
+    measured.  Attention, the loss and the teacher's per-step Q8_0 decode then
+    run at GEMM speed or not at all, which flatters the host.
+
+    Candidate values are seeded normal draws (scaled copies of one draw per
+    tensor): the timed arithmetic does not depend on them, and decoding a
+    layer's 1.3 G candidate weights through the oracle decoders would take
+    longer than the whole timed run."""
+
+    def __init__(self, shape, tokens: int, seed: int = 0):
+        import numpy as np
+
+        sys.path.insert(0, str(ROOT))
+        from oracle import mixgemm
+
+        self.mixgemm = mixgemm
+        self.shape, self.tokens = shape, tokens
+        self.threads = _host_threads()
+        rng = np.random.default_rng(seed)
+        self.tensors = []
+        self.p_layer = 0
+        for role, n_out, n_in, types in layer_linear_shapes(shape):
+            base = rng.standard_normal((n_out, n_in), dtype=np.float32)
+            base *= np.float32(0.02)
+            cands = [base * np.float32(1.0 + 0.01 * k) for k in range(len(types))]
+            del base
+            gates = rng.standard_normal(len(types)).astype(np.float32)
+            x = rng.standard_normal((tokens, n_in), dtype=np.float32)
+            dy = rng.standard_normal((tokens, n_out), dtype=np.float32)
+            self.tensors.append((role, cands, gates, x, dy))
+            self.p_layer += n_out * n_in
+
+    def step(self) -> tuple[float, float]:
+        """One step of every tensor; returns (per-weight s, per-token s)."""
+        mg, th = self.mixgemm, self.threads
+        w_s = t_s = 0.0
+        for _, cands, gates, x, dy in self.tensors:
+            t0 = time.perf_counter()
+            p = mg.softmax_probs(gates, 1.0)
+            wm = mg.mixed_weight(cands, p, threads=th)
+            t1 = time.perf_counter()
+            mg.linear_fwd(x, wm)
+            mg.linear_dx(dy, wm)
+            dw = dy.T @ x
+            t2 = time.perf_counter()
+            g = mg.prob_grad_from_dw(dw, cands, threads=th)
+            mg.gate_grad(p, g, 1.0)
+            t3 = time.perf_counter()
+            w_s += (t1 - t0) + (t3 - t2)
+            t_s += t2 - t1
+        return w_s, t_s
+
+    def full_step_s(self, w_s: float, t_s: float) -> float:
+        fpt = step_flops_per_token(self.shape)
+        step_tokens = self.shape.batch * self.shape.seq
+        sample_flops = 6.0 * self.p_layer * self.tokens
+        return w_s * gated_linear_params(self.shape) / self.p_layer + t_s * fpt * step_tokens / sample_flops
+
+    def describe(self) -> str:
+        return (f"one decoder layer of the workload (7 gated Linears, {self.p_layer / 1e6:.0f} M weights, "
+                f"K = {len(self.shape.candidates)}) on {self.tokens} tokens per step: mixture, forward, dX, "
+                f"dW and the K reductions, float32 numpy on {self.threads} threads; full-step time = per-weight "
+                f"time x {gated_linear_params(self.shape) / self.p_layer:.1f} (student gated weights / layer's) "
+                f"+ per-token time x step FLOPs / sample FLOPs "
+                f"({step_flops_per_token(self.shape) / 1e9:.2f} GFLOP/token x {self.shape.batch * self.shape.seq} "
+                f"tokens); attention, loss and teacher decode counted at GEMM speed")
+
+
+def step_cpu_baseline(shape, tokens: int = 256, repeats: int = 2) -> dict:
+    """The full step's host baseline from HostLayerSample (rank 0, N = 1)."""
+    s = HostLayerSample(shape, tokens)
+    s.step()
+    w = t = 0.0
+    for _ in range(repeats):
+        a, b = s.step()
+        w, t = w + a, t + b
+    full = s.full_step_s(w / repeats, t / repeats)
+    return {"value": round(shape.batch * shape.seq / full, 4), "unit": "tokens/s", "cores": s.threads,
+            "kind": "port", "sample_ms_per_step": round((w + t) / repeats * 1e3, 1),
+            "full_step_s_estimate": round(full, 1), "sample": s.describe()}
 
 
 def run_reference(args):
+    """The reference arm: the reference's algorithm on the host cores (the
+    oracle's float32 numpy port; the reference itself is Python and does not
+    travel to the GPU box), rank 0 only, on the same workload, config, metric
+    and unit as the GPU arm.
+
+    * step workloads (default 8b): each step is one HostLayerSample step
+      (one decoder layer on ``--cpu-tokens`` tokens, timed as it runs);
+      ``ms_per_step`` is that measured time, ``value`` the full step's tokens
+      over the full-step time those rates give (HostLayerSample.full_step_s).
+    * layer: each step is the full config-2 layer step, all 8192 tokens.
+    """
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    mixgemm, cands, x, dy, gates = _cpu_setup(args.cpu_tokens)
-    for _ in range(args.warmup):
-        _cpu_step(mixgemm, cands, x, dy, gates)
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        _cpu_step(mixgemm, cands, x, dy, gates)
-    dt = (time.perf_counter() - t0) / args.steps
-    v = round(args.cpu_tokens / dt, 2)
-    cores = os.cpu_count() or 1
     world = int(os.environ.get("WORLD_SIZE", "1"))
+    cores = _host_threads()
+    if args.workload == "layer":
+        mixgemm, cands, x, dy, gates = _layer_host_setup(T_TOK)
+        for _ in range(args.warmup):
+            _layer_host_step(mixgemm, cands, x, dy, gates)
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            _layer_host_step(mixgemm, cands, x, dy, gates)
+        dt = (time.perf_counter() - t0) / args.steps
+        v = round(T_TOK / dt, 2)
+        metric, cfg, ms = LAYER_METRIC, layer_config(world), dt * 1e3
+        sample = "the full config-2 layer step (8192 tokens) per step, float32 numpy restatement of the " \
+                 "reference's torch CPU path, candidates pre-decoded like its cached _w_k"
+        extra = {}
+    else:
+        from voodoo_quant.training import synthetic as S
+
+        shape = S.SHAPES[args.workload]
+        s = HostLayerSample(shape, args.cpu_tokens)
+        for _ in range(args.warmup):
+            s.step()
+        w = t = 0.0
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            a, b = s.step()
+            w, t = w + a, t + b
+        dt = (time.perf_counter() - t0) / args.steps
+        full = s.full_step_s(w / args.steps, t / args.steps)
+        v = round(shape.batch * shape.seq / full, 4)
+        metric, cfg, ms = METRIC, step_config(args.workload, shape, world), dt * 1e3
+        sample = s.describe()
+        extra = {"full_step_s_estimate": round(full, 1), "sample_tokens_per_step": args.cpu_tokens}
     out = {
-        "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(dt * 1e3 * T_TOK / args.cpu_tokens, 2),
-        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic (seeded)", "config": config(world), "impl": "reference",
-        "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port",
-                         "sample": f"{args.cpu_tokens} of 8192 tokens per step, float32 numpy restatement "
-                                   "of the reference's torch CPU path"},
+        "metric": metric, "value": v, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms, 2), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded)", "config": cfg, "impl": "reference",
+        "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample, **extra},
         "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(out), flush=True)
@@ -554,7 +759,8 @@ def run_ncu_case():
 
 _OUR_KERNELS = ("gemm_kernel", "gemm_pair_kernel", "mix_units_kernel", "dequant_units_kernel",
                 "gategrad_reduce_kernel", "loss_fused_kernel", "loss_stats_kernel", "loss_combine_kernel",
-                "loss_grad_kernel")
+                "loss_grad_kernel", "rmsnorm_fwd_kernel", "rmsnorm_bwd_kernel", "rope_kernel", "swiglu_kernel",
+                "route_prep_kernel", "q8_0_quantize_kernel")
 
 
 def _count_our_launches(fn):
@@ -647,6 +853,10 @@ def run_model_step(args):
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
+    # the metric's second half (mix-GEMM kernels of config 2), on rank 0's GPU
+    # before the model is built
+    mix_gemm = layer_kernel_fractions(dev, args.kernel_iters) if rank == 0 and not args.no_layer_kernels else None
+
     workload = args.workload
     if args.layers > 0:
         # a smoke run of the workload's build, memory plan and step with fewer
@@ -725,6 +935,10 @@ def run_model_step(args):
         peak_t = float(pk.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"]))
         fpt = step_flops_per_token(shape)
         ach = fpt * tokens / (ms * 1e-3) / 1e12
+        cfg = step_config(args.workload, shape, world)
+        if args.layers > 0:
+            cfg["workload"] += (f" -- SMOKE RUN with {shape.layers} of {S.SHAPES[args.workload].layers} layers, "
+                                "not the configuration")
         res = {
             "metric": METRIC,
             "value": round(tokens / (ms * 1e-3), 1),
@@ -738,27 +952,19 @@ def run_model_step(args):
             "vs_baseline": None,
             "dtype": "bf16",
             "data": "synthetic (seeded random-init weights and tokens; candidates from the round-to-nearest packer)",
-            "config": {"workload": f"{args.workload}: full gated distillation step" + (
-                           f" -- SMOKE RUN with {shape.layers} of {S.SHAPES[args.workload].layers} layers, "
-                           "not the configuration" if args.layers > 0 else ""), "layers": shape.layers,
-                       "hidden": shape.hidden, "ffn": shape.ffn, "vocab": shape.vocab, "tied": shape.tied,
-                       "batch": shape.batch, "seq": shape.seq, "candidates": shape.candidates,
-                       "attention_candidates": shape.attention_candidates,
-                       "row_scale_sigma": shape.row_scale_sigma,
-                       "gated_tensors": len(trainer.replaced), "budget": shape.budget,
-                       "parallelism": f"tp{world}", "build_s": round(t_build, 1),
-                       "input_grad_overlap_sms": args.overlap_sms if world > 1 else 0,
-                       "row_parallel_reduce": "nvls multimem.red in GEMM" if multicast_on else "nccl all-reduce",
-                       "forward": "ptqr (one candidate per token)" if args.ptqr else "candidate mixture",
-                       "logits_chunk": args.logits_chunk, "peak_alloc_gb_rank0": round(peak_gb, 2),
-                       "step_graph": "forward + backward replayed from one CUDA graph" if args.graph_step
-                       else "eager",
-                       "teacher_tp": args.teacher_tp or world,
-                       "teacher": (f"own stream and communicator beside the student, "
-                                   f"{args.teacher_stream_sms} SMs left to collectives") if args.teacher_stream
-                       else "after the student, same stream",
-                       "l2": "activations and logits far larger than L2"},
-            "roofline": {"bound": "tensor", "kernel": "whole step", "flops_per_token": fpt,
+            "config": cfg,
+            "run": {"gated_tensors": len(trainer.replaced), "build_s": round(t_build, 1),
+                    "input_grad_overlap_sms": args.overlap_sms if world > 1 else 0,
+                    "row_parallel_reduce": "nvls multimem.red in GEMM" if multicast_on else "nccl all-reduce",
+                    "forward": "ptqr (one candidate per token)" if args.ptqr else "candidate mixture",
+                    "logits_chunk": args.logits_chunk, "peak_alloc_gb_rank0": round(peak_gb, 2),
+                    "step_graph": "forward + backward replayed from one CUDA graph" if args.graph_step
+                    else "eager",
+                    "teacher_tp": args.teacher_tp or world,
+                    "teacher": (f"own stream and communicator beside the student, "
+                                f"{args.teacher_stream_sms} SMs left to collectives") if args.teacher_stream
+                    else "after the student, same stream"},
+            "roofline": {"bound": "tensor", "kernel": "whole step (tcgen05 GEMMs dominate)", "flops_per_token": fpt,
                          "achieved": round(ach, 1), "peak": round(peak_t * world, 1), "unit": "TFLOP/s",
                          "frac": round(ach / (peak_t * world), 4),
                          "peak_source": f"{pk_kind} bf16_tflops_sustained x {world} GPUs", "traffic": None},
@@ -769,8 +975,10 @@ def run_model_step(args):
             "loss_last": round(float(out["loss"]), 4),
             "size_bytes_last": float(out["size_bytes"]),
         }
+        if mix_gemm is not None:
+            res["mix_gemm"] = mix_gemm
         if world == 1 and not args.no_cpu_baseline:
-            res["cpu_baseline"] = step_cpu_baseline(args.cpu_tokens, fpt)
+            res["cpu_baseline"] = step_cpu_baseline(shape, tokens=args.cpu_tokens)
         print(json.dumps(res), flush=True)
     trainer.release_graph()  # the graph holds collectives: drop it before the process group
     torch.cuda.synchronize()
@@ -839,58 +1047,64 @@ def run_cache_load(args):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--workload", choices=["layer", "tiny", "0.6b", "8b", "32b", "cache-load"], default="layer",
-                    help="layer: the single gated-Linear step (default); tiny/0.6b/8b/32b: full distillation step "
-                         "(32b: the TP-4 / TP-8 case, K=7 with per-role menus); cache-load: candidate-cache files "
-                         "into HBM (GB/s)")
+    ap.add_argument("--workload", choices=["8b", "layer", "tiny", "0.6b", "32b", "cache-load"], default="8b",
+                    help="8b (default): the config-4 distillation step at TP-N; tiny/0.6b/32b: the other step "
+                         "configurations (32b: the TP-4 / TP-8 case, K=7 with per-role menus); layer: the config-2 "
+                         "single gated-Linear step; cache-load: candidate-cache files into HBM (GB/s)")
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=60)
+    ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--kernel-iters", type=int, default=10)
-    ap.add_argument("--e2e-steps", type=int, default=10)
-    ap.add_argument("--cpu-tokens", type=int, default=2048)
+    ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--cpu-tokens", type=int, default=-1,
+                    help="host sample tokens (default: 256 for step workloads, 2048 for the layer)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--no-graph", action="store_true", help="time the eager step instead of a CUDA graph of it")
+    ap.add_argument("--no-layer-kernels", action="store_true",
+                    help="step workloads: skip the config-2 mix-GEMM kernel fractions (mix_gemm key)")
+    ap.add_argument("--no-graph", action="store_true", help="layer workload: time the eager step, not a CUDA graph")
     ap.add_argument("--overlap-sms", type=int, default=-1,
                     help="TP: SMs the gate-gradient GEMMs leave to the concurrent input-gradient all-reduces, which "
                          "run on a communicator capped to that many CTAs (default: 32 with more than one GPU, "
                          "0 otherwise)")
     ap.add_argument("--dx-chunks", type=int, default=-1,
                     help="layer workload under TP: row chunks of dX, each all-reduced while the next is computed "
-                         "(default: 2 with more than one GPU; TP-8 0.606 -> 0.585 ms per step)")
+                         "(default: 2 with more than one GPU)")
     ap.add_argument("--ptqr", action="store_true",
-                    help="full-step workloads: per-token quant routing forward (one candidate per token)")
+                    help="step workloads: per-token quant routing forward (one candidate per token)")
     ap.add_argument("--logits-chunk", type=int, default=0,
-                    help="full-step workloads: head + loss per chunk of this many tokens (no [tokens, V] logits)")
+                    help="step workloads: head + loss per chunk of this many tokens (no [tokens, V] logits)")
     ap.add_argument("--multicast", action="store_true",
-                    help="full-step workloads under TP: sum row-parallel outputs with multimem.red in the GEMM")
+                    help="step workloads under TP: sum row-parallel outputs with multimem.red in the GEMM")
     ap.add_argument("--graph-step", action="store_true",
-                    help="full-step workloads: record forward + backward as one CUDA graph (static-shape mode, "
+                    help="step workloads: record forward + backward as one CUDA graph (static-shape mode, "
                          "CE over all tokens) and replay it each step; the optimizer stays eager")
     ap.add_argument("--teacher-stream", action="store_true",
-                    help="full-step workloads: the teacher's forward on a second stream beside the student's, its "
+                    help="step workloads: the teacher's forward on a second stream beside the student's, its "
                          "TP all-reduces on a communicator of their own")
     ap.add_argument("--teacher-stream-sms", type=int, default=0,
                     help="with --teacher-stream: SMs the forward GEMMs leave to the other stream's all-reduces "
                          "(and the teacher communicator's CTA cap); 0 = none")
     ap.add_argument("--teacher-tp", type=int, default=0,
-                    help="full-step workloads under TP: the teacher's own TP degree t (groups of t ranks, each on "
+                    help="step workloads under TP: the teacher's own TP degree t (groups of t ranks, each on "
                          "its batch slice; one all-to-all of its logits); 0 = the student's")
     ap.add_argument("--layers", type=int, default=0,
-                    help="full-step workloads: build only this many decoder layers (a smoke run of the build, "
+                    help="step workloads: build only this many decoder layers (a smoke run of the build, "
                          "memory plan and step; its line says so and is not the configuration's number)")
     ap.add_argument("--profile-step", action="store_true",
-                    help="full-step workloads: print device time per kernel name for one step")
+                    help="step workloads: print device time per kernel name for one step")
     ap.add_argument("--ncu-case", action="store_true", help="one launch per kernel at profiling sizes")
     args = ap.parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
     if args.overlap_sms < 0:
         # NCCL's default channel count here: at TP-2 it measured 1.262 ms per
         # layer step against 1.286 ms with 24 (and 1.30 ms without overlap);
         # with more ranks the all-reduce outlasts the gate-gradient GEMM
-        args.overlap_sms = 32 if int(os.environ.get("WORLD_SIZE", "1")) > 1 else 0
+        args.overlap_sms = 32 if world > 1 else 0
     if args.dx_chunks < 0:
-        args.dx_chunks = 2 if int(os.environ.get("WORLD_SIZE", "1")) > 1 else 1
+        args.dx_chunks = 2 if world > 1 else 1
+    if args.cpu_tokens < 0:
+        args.cpu_tokens = 2048 if args.workload == "layer" else 256
     if args.ncu_case:
         run_ncu_case()
     elif args.impl == "reference":

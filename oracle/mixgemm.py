@@ -82,6 +82,13 @@ def prob_grad(dy: np.ndarray, x: np.ndarray, cands: list[np.ndarray], fp64: bool
     """g_k = <dY^T X, W_k> (dW materialised, as in the reference)."""
     dt = np.float64 if fp64 else np.float32
     dw = dy.astype(dt, copy=False).T @ x.astype(dt, copy=False)
+    return prob_grad_from_dw(dw, cands, threads=threads)
+
+
+def prob_grad_from_dw(dw: np.ndarray, cands: list[np.ndarray], threads: int = 1) -> np.ndarray:
+    """g_k = <dW, W_k> for a materialised dW (the reference's K reductions,
+    voodoo_quant/layers.py:355-363), summed per row chunk in float64."""
+    dt = dw.dtype
     chunks = _row_chunks(dw.shape[0], max(1, threads) * 4)
 
     def part(rng):

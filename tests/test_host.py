@@ -287,15 +287,20 @@ def test_step_flops_per_token_roofline_denominators():
 
 def test_reference_arm_prints_one_contract_line():
     """bench.py --impl reference (the reference's algorithm on the host) prints
-    one JSON line with the keys the benchmark contract names."""
+    one JSON line with the keys the benchmark contract names, the GPU arm's
+    config object for the same workload, and a ms_per_step it timed."""
     import json
     import subprocess
     import sys
     from pathlib import Path
 
+    import bench
+    from voodoo_quant.training import synthetic as S
+
     root = Path(__file__).resolve().parents[1]
-    r = subprocess.run([sys.executable, "bench.py", "--impl", "reference", "--steps", "1", "--warmup", "1",
-                        "--cpu-tokens", "64"], cwd=root, capture_output=True, text=True, timeout=600)
+    r = subprocess.run([sys.executable, "bench.py", "--impl", "reference", "--workload", "tiny", "--steps", "2",
+                        "--warmup", "1", "--cpu-tokens", "64"], cwd=root, capture_output=True, text=True,
+                       timeout=600)
     assert r.returncode == 0, r.stderr[-2000:]
     lines = [l for l in r.stdout.splitlines() if l.startswith("{")]
     assert len(lines) == 1
@@ -304,18 +309,33 @@ def test_reference_arm_prints_one_contract_line():
                 "scaling", "vs_baseline", "dtype", "data", "config", "impl", "cpu_baseline", "e2e"):
         assert key in out, key
     assert out["impl"] == "reference" and out["value"] > 0 and out["unit"] == "tokens/s"
+    assert out["metric"] == bench.METRIC
     assert out["cpu_baseline"]["kind"] == "port" and out["cpu_baseline"]["cores"] >= 1
-    assert out["e2e"]["h2d_bytes_per_step"] == 0 and "workload" in out["config"]
+    assert out["e2e"]["h2d_bytes_per_step"] == 0
+    assert out["config"] == json.loads(json.dumps(bench.step_config("tiny", S.SHAPES["tiny"], 1)))
+    assert 0 < out["ms_per_step"] < 60e3
 
 
 def test_full_step_host_baseline_scales_the_layer_sample():
-    """The full-step lines' host baseline: the layer sample's GFLOP/s over the
-    step's FLOPs per token."""
+    """The full-step host baseline: one decoder layer's seven gated Linears
+    timed on the host, per-weight time scaled by the student's gated weights
+    over the layer's, per-token time by the step's FLOPs over the sample's."""
     import bench
     from voodoo_quant.training import synthetic as S
 
-    fpt = bench.step_flops_per_token(S.SHAPES["8b"])
-    r = bench.step_cpu_baseline(32, fpt)
-    assert r["kind"] == "port" and r["unit"] == "tokens/s" and r["cores"] >= 1 and r["gflops"] > 0
-    assert abs(r["value"] - r["gflops"] * 1e9 / fpt) <= 1e-3 * r["value"] + 1e-3
-    assert "GFLOP per token" in r["sample"]
+    shape = S.SHAPES["tiny"]
+    s = bench.HostLayerSample(shape, 32)
+    roles = [r for r, *_ in s.tensors]
+    assert roles == ["q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj"]
+    assert s.p_layer == 256 * 256 * 4 + 3 * 256 * 768
+    assert bench.gated_linear_params(shape) == 2 * s.p_layer + 4096 * 256
+    w, t = s.step()
+    assert w > 0 and t > 0
+    full = s.full_step_s(w, t)
+    fpt = bench.step_flops_per_token(shape)
+    want = w * bench.gated_linear_params(shape) / s.p_layer + t * fpt * 256 / (6.0 * s.p_layer * 32)
+    assert abs(full - want) <= 1e-9 * want
+    r = bench.step_cpu_baseline(shape, tokens=32, repeats=1)
+    assert r["kind"] == "port" and r["unit"] == "tokens/s" and r["cores"] >= 1 and r["value"] > 0
+    assert abs(r["value"] - 256 / r["full_step_s_estimate"]) <= 0.05 * r["value"] + 1e-3
+    assert "GFLOP/token" in r["sample"]
