@@ -168,12 +168,22 @@ int vq_linear_fwd_mcred(const void* x, int64_t T, int64_t Kin, int64_t ldx, cons
  *     library until the process exits.  Shapes whose
  *     vq_gategrad_workspace_bytes exceeds it are rejected (VQ_ERR_INVALID)
  *     before anything runs; use vq_gategrad with a workspace for those.
+ *   - The array's memory is committed when the CUDA driver loads this
+ *     library's device code on a device, which happens lazily, at the first
+ *     call of any vq_* entry point that launches work there.  A process whose
+ *     pool will take nearly all device memory should make one such call on
+ *     each device before the pool reserves its memory.
  *   - The first call on a device looks up the array's device address with
- *     that device current (the device of grad_probs); make that first call
- *     before any stream capture on the device.
- *   - Every call shares the array.  Nothing in it needs to start at zero (each
- *     call writes every partial slot it reads back), but calls that overlap
- *     on the GPU (other streams, other threads) race on it: order them.
+ *     that device current (the device of grad_probs) and keeps it for the
+ *     process; make that first call before any stream capture on the device.
+ *     The address is not looked up again, so a process that resets a device
+ *     (cudaDeviceReset) must not call this entry point on it afterwards.
+ *   - Every call shares the array.  Nothing in it needs to start at zero: a
+ *     call that completes writes every partial slot it reads back.  A call
+ *     whose kernel gave up on a bounded wait (vq_device_error non-zero) may
+ *     sum partials an earlier call left, so its result is valid only while
+ *     vq_device_error reads 0.  Calls that overlap on the GPU (other streams,
+ *     other threads) race on the array: order them.
  *   - Allocates nothing: no cudaMalloc, cudaFree or allocating library call.
  * Arguments, results and errors are those of vq_gategrad. */
 int vq_gategrad_noalloc(const void* dy, int64_t lddy, const void* x, int64_t ldx, int64_t T, int64_t N, int64_t Kin,

@@ -149,3 +149,85 @@ def test_fused_llama_blocks_match_unpatched_model(cuda):
     l_fus.backward(gy)
     assert _rel(e_fus.grad, e_ref.grad) < 2e-2
     assert cosine(e_fus.grad.double().flatten().cpu().numpy(), e_ref.grad.double().flatten().cpu().numpy()) > 0.999
+
+
+def _gated(cuda, n_out, n_in, types, seed):
+    from voodoo_quant.layers import MixedQuantLinear
+    from voodoo_quant.quants import rtn
+
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    w = torch.randn(n_out, n_in, generator=g) * 0.02
+    layer = MixedQuantLinear(n_in, n_out, types, w.to(cuda), candidate_bytes={q: rtn.quantize(w, q) for q in types},
+                             tensor_name=f"group.{seed}")
+    with torch.no_grad():
+        layer.gates.copy_(torch.randn(len(types), generator=g))
+    layer.set_temperature(0.7)
+    return layer
+
+
+@pytest.mark.parametrize("outs", [(512, 128, 128), (1792, 1792)])
+def test_grouped_gated_projection_matches_separate_layers(cuda, outs):
+    """q/k/v (or gate/up) as one grouped GEMM: the output columns equal each
+    layer's own forward (the same mixture and dot products per output
+    element; 1e-3 relative), dX equals the sum of the layers' dX within bf16
+    rounding of the partial sums (1e-2 relative), and each layer's gate
+    gradient is the same gate-gradient GEMM over its column range
+    (bit-identical)."""
+    from voodoo_quant.layers import gated_linear_group, groupable
+
+    types = ["Q2_K", "Q4_K", "Q6_K", "Q8_0"]
+    n_in, T = 1024, 300
+    layers = [_gated(cuda, n, n_in, types, 40 + i) for i, n in enumerate(outs)]
+    assert groupable(layers)
+    g = torch.Generator(device="cpu").manual_seed(9)
+    x = torch.randn(T, n_in, generator=g).to(cuda, torch.bfloat16)
+    dy = torch.randn(T, sum(outs), generator=g).to(cuda, torch.bfloat16)
+
+    xa = x.clone().requires_grad_(True)
+    ya = gated_linear_group(layers, xa)
+    ya.backward(dy)
+    ga = [l.gates.grad.clone() for l in layers]
+    for l in layers:
+        l.gates.grad = None
+
+    xb = x.clone().requires_grad_(True)
+    yb = torch.cat([l(xb) for l in layers], dim=1)
+    yb.backward(dy)
+    gb = [l.gates.grad.clone() for l in layers]
+    torch.cuda.synchronize()
+    assert _rel(ya, yb) < 1e-3
+    assert _rel(xa.grad, xb.grad) < 1e-2
+    for a, b in zip(ga, gb):
+        assert torch.equal(a, b)
+
+
+def test_grouped_q8_teacher_projection_matches_separate_layers(cuda):
+    from voodoo_quant.quants import rtn
+    from voodoo_quant.training.q8_teacher import Q8Linear, q8_groupable, q8_linear_group
+
+    g = torch.Generator(device="cpu").manual_seed(11)
+    mods = []
+    for n in (512, 128, 128):
+        w = torch.randn(n, 768, generator=g) * 0.02
+        mods.append(Q8Linear(rtn.quantize(w, "Q8_0").to(cuda), n, 768))
+    assert q8_groupable(mods)
+    x = torch.randn(2, 70, 768, generator=g).to(cuda, torch.bfloat16)
+    y = q8_linear_group(mods, x)
+    assert y.shape == (2, 70, 768)
+    assert _rel(y, torch.cat([m(x) for m in mods], dim=-1)) < 1e-3
+
+
+def test_swiglu_pair_backward_layout(cuda):
+    """The grouped gate|up SwiGLU writes d gate | d up side by side."""
+    from voodoo_quant import _C
+    from voodoo_quant.fused_blocks import _SwiGLUPairFn
+
+    g = torch.Generator(device="cpu").manual_seed(12)
+    gu = torch.randn(3, 50, 2 * 1792, generator=g).to(cuda, torch.bfloat16).requires_grad_(True)
+    dy = torch.randn(3, 50, 1792, generator=g).to(cuda, torch.bfloat16)
+    y = _SwiGLUPairFn.apply(gu)
+    y.backward(dy)
+    a, u = gu.detach()[..., :1792].reshape(-1, 1792), gu.detach()[..., 1792:].reshape(-1, 1792)
+    assert torch.equal(y.reshape(-1, 1792), _C.swiglu_fwd(a, u))
+    da, du = _C.swiglu_bwd(a, u, dy.reshape(-1, 1792))
+    assert torch.equal(gu.grad.reshape(-1, 2 * 1792), torch.cat([da, du], dim=1))

@@ -3,22 +3,32 @@ restatement of the reference step (voodoo_quant/training/trainer.py:
 2443-2616): every gated weight is sum_k softmax(g / tau)_k * decode_k in fp32
 (decoded by the CPU oracle), rounded to bf16 and used through F.linear /
 F.embedding; the loss is F.cross_entropy + T^2 * KL on fp32 logits, plus the
-relu-squared size term.  The teacher is the Q8_0 teacher of the step itself.
+relu-squared size term.
 
-Tolerances: the loss within 2e-3 relative, the gate gradients of all layers
-(one flat vector) within 3e-2 relative L2 error and cosine > 0.999.  The
-torch path rounds dW to bf16 before the gate contraction, the B200 path does
-not, which dominates the gradient difference.
+The teacher is checked on its own first, against an independent path: every
+weight quantised by the oracle's Q8_0 rule (oracle/q8_quant.py, pinned to
+gguf-py), decoded by the oracle and used in float32 (F.linear / F.embedding
+in an fp32 copy of the model): logits within 1e-2 relative.  The
+restatement's KL then uses the step's own teacher logits, so the gate
+gradients compare the student path alone.
+
+Tolerances: the loss within 2e-3 relative; gate gradients per tensor cosine
+>= 0.999 with the reference's default arguments, and, with the size term off
+(the distillation gradient alone, a small difference signal between nearly
+equal candidates whose bf16 rounding sites differ between the two paths),
+>= 0.995 per tensor and >= 0.999 with relative L2 error < 3e-2 for all
+tensors as one vector.
 """
 
 from __future__ import annotations
 
+import numpy as np
 import pytest
 import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
-from oracle import ggml_blocks
+from oracle import ggml_blocks, q8_quant
 
 pytestmark = pytest.mark.gpu
 
@@ -59,14 +69,35 @@ def _set(model, name, mod):
     setattr(parent, last, mod)
 
 
-def test_tiny_distill_step_matches_torch_restatement(cuda):
+def _oracle_q8_teacher(shape, cuda, seed):
+    """fp32 copy of the model whose every Linear / Embedding weight is the
+    oracle's Q8_0 round trip of the bf16 weight."""
+    from voodoo_quant.training import synthetic as S
+
+    ref = S.build_llama(shape, cuda, seed=seed).float()
+    for mod in ref.modules():
+        if isinstance(mod, (nn.Linear, nn.Embedding)):
+            w = mod.weight.detach().cpu().numpy()
+            qb = q8_quant.quantize_q8_0(w)
+            dec = ggml_blocks.dequantize(qb, "Q8_0", w.shape[0], w.shape[1])
+            mod.weight.data = torch.from_numpy(dec).to(cuda)
+    for p in ref.parameters():
+        p.requires_grad = False
+    return ref
+
+
+# (distill_temperature, distill_weight, size_weight, size_tolerance), per-tensor cosine
+_ARGS = {"default": ((1.0, 1.0, 10.0, 0.02), 0.999), "kd": ((2.0, 0.7, 0.0, 0.0), 0.995)}
+
+
+@pytest.mark.parametrize("variant", ["default", "kd"])
+def test_tiny_distill_step_matches_torch_restatement(cuda, variant):
     from voodoo_quant.layers import MixedQuantEmbedding
     from voodoo_quant.training import synthetic as S
     from voodoo_quant.training.trainer import StepArgs, build_distill
 
-    # size_weight 0 keeps the kernel-dependent distillation gradient from being swamped by the
-    # size term, which is plain torch on both sides and is checked through its value instead
-    args = StepArgs(distill_temperature=2.0, distill_weight=0.7, size_weight=0.0, size_tolerance=0.0)
+    (Tk, kl_w, size_w, tol), per_tensor_cos = _ARGS[variant]
+    args = StepArgs(distill_temperature=Tk, distill_weight=kl_w, size_weight=size_w, size_tolerance=tol)
     trainer, shape = build_distill("tiny", cuda, seed=3, args=args)
     # move the gates off zero so the softmax, the mixture and the size term are all non-trivial
     g = torch.Generator(device="cpu").manual_seed(5)
@@ -75,6 +106,12 @@ def test_tiny_distill_step_matches_torch_restatement(cuda):
             layer.gates.copy_(torch.randn(layer.num_candidates, generator=g).to(cuda))
     trainer.step_idx = 7
     x, y = S.random_tokens(shape, cuda, seed=11)
+
+    # the step's teacher against the oracle's Q8_0 teacher in float32
+    with torch.no_grad():
+        t_logits = trainer.teacher(input_ids=x).logits.float()
+        t_oracle = _oracle_q8_teacher(shape, cuda, seed=3)(input_ids=x).logits.float()
+    assert float((t_logits - t_oracle).norm() / t_oracle.norm()) < 1e-2
 
     ref = S.build_llama(shape, cuda, seed=3)
     mods = {}
@@ -91,8 +128,6 @@ def test_tiny_distill_step_matches_torch_restatement(cuda):
         m.gates.requires_grad = True
 
     logits = ref(input_ids=x).logits.float()
-    with torch.no_grad():
-        t_logits = trainer.teacher(input_ids=x).logits.float()
     V = logits.shape[-1]
     T = args.distill_temperature
     lm = F.cross_entropy(logits.view(-1, V), y.view(-1))
@@ -100,17 +135,21 @@ def test_tiny_distill_step_matches_torch_restatement(cuda):
                   reduction="none").sum(-1).mul(T * T).mean()
     cur = sum(m.eff_bytes() for m in mods.values()) + trainer.non_targeted_bytes
     size = torch.relu(torch.abs(cur / trainer.target_bytes - 1.0) - args.size_tolerance) ** 2
-    loss = lm + args.distill_weight * kl
+    loss = lm + args.distill_weight * kl + args.size_weight * size
     loss.backward()
 
     assert abs(out["loss"].item() - loss.item()) <= 2e-3 * abs(loss.item())
     assert abs(out["size_bytes"].item() - cur.item()) <= 1e-5 * cur.item()
     assert out["size_loss"].item() == pytest.approx(size.item(), rel=1e-4)
-    ours = torch.cat([trainer.replaced[n].gates.grad.double() for n in mods])
-    theirs = torch.cat([mods[n].gates.grad.double() for n in mods])
-    assert torch.isfinite(ours).all()
-    rel = (ours - theirs).norm() / theirs.norm()
-    cos = torch.dot(ours, theirs) / (ours.norm() * theirs.norm())
+    ours = {n: trainer.replaced[n].gates.grad.double() for n in mods}
+    theirs = {n: mods[n].gates.grad.double() for n in mods}
+    for n in mods:
+        assert torch.isfinite(ours[n]).all(), n
+        c = torch.dot(ours[n], theirs[n]) / (ours[n].norm() * theirs[n].norm())
+        assert c >= per_tensor_cos, (n, c.item())
+    a, b = torch.cat([ours[n] for n in mods]), torch.cat([theirs[n] for n in mods])
+    rel = (a - b).norm() / b.norm()
+    cos = torch.dot(a, b) / (a.norm() * b.norm())
     assert rel < 3e-2 and cos > 0.999, (rel.item(), cos.item())
 
 

@@ -500,12 +500,19 @@ def swiglu_fwd(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
     return y
 
 
-def swiglu_bwd(gate: torch.Tensor, up: torch.Tensor, dy: torch.Tensor):
+def swiglu_bwd(gate: torch.Tensor, up: torch.Tensor, dy: torch.Tensor, out: torch.Tensor | None = None):
+    """(d gate, d up) of silu(gate) * up; with ``out`` ([rows, 2F] bf16,
+    contiguous) both are written into it side by side and returned as views."""
     _require_cuda(gate, up, dy)
     gate, up, dy = _rows_operand(gate), _rows_operand(up), _rows_operand(dy)
     rows, F = gate.shape
-    dg = torch.empty(rows, F, dtype=torch.bfloat16, device=gate.device)
-    du = torch.empty(rows, F, dtype=torch.bfloat16, device=gate.device)
+    if out is not None:
+        if out.dtype != torch.bfloat16 or tuple(out.shape) != (rows, 2 * F) or not out.is_contiguous():
+            raise ValueError("swiglu_bwd: out must be a contiguous bf16 [rows, 2F] tensor")
+        dg, du = out[:, :F], out[:, F:]
+    else:
+        dg = torch.empty(rows, F, dtype=torch.bfloat16, device=gate.device)
+        du = torch.empty(rows, F, dtype=torch.bfloat16, device=gate.device)
     _check(_lib.vq_swiglu_bwd(gate.data_ptr(), gate.stride(0), up.data_ptr(), up.stride(0), dy.data_ptr(), dy.stride(0),
                               rows, F, dg.data_ptr(), du.data_ptr(), dg.stride(0), _stream(gate)))
     return dg, du

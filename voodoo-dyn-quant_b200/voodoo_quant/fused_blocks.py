@@ -110,6 +110,42 @@ class _SwiGLUFn(Function):
         return dg.view(ctx.shape), du.view(ctx.shape)
 
 
+class _SwiGLUPairFn(Function):
+    """silu(gate) * up of a grouped gate|up projection output [..., 2F]; the
+    backward writes d gate and d up into one [rows, 2F] gradient, the layout
+    the grouped projection's backward reads."""
+
+    @staticmethod
+    def forward(ctx, gu: torch.Tensor):
+        F_ = gu.shape[-1] // 2
+        g2 = gu.reshape(-1, 2 * F_)
+        y = _C.swiglu_fwd(g2[:, :F_], g2[:, F_:])
+        ctx.save_for_backward(g2)
+        ctx.shape = gu.shape
+        return y.view(*gu.shape[:-1], F_)
+
+    @staticmethod
+    def backward(ctx, gy: torch.Tensor):
+        (g2,) = ctx.saved_tensors
+        F_ = g2.shape[1] // 2
+        dgu = torch.empty(g2.shape, dtype=torch.bfloat16, device=g2.device)
+        _C.swiglu_bwd(g2[:, :F_], g2[:, F_:], gy.reshape(-1, F_), out=dgu)
+        return dgu.view(ctx.shape)
+
+
+def _group_projection(mods, x: torch.Tensor):
+    """Linears that read the same input as one GEMM when they allow it (gated
+    student layers or Q8_0 teacher layers); None otherwise."""
+    from voodoo_quant.layers import gated_linear_group, groupable
+    from voodoo_quant.training.q8_teacher import q8_groupable, q8_linear_group
+
+    if groupable(mods):
+        return gated_linear_group(mods, x)
+    if q8_groupable(mods):
+        return q8_linear_group(mods, x)
+    return None
+
+
 def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
     return _RMSNormFn.apply(x, weight, eps)
 
@@ -140,6 +176,10 @@ def _rmsnorm_forward(self, hidden_states: torch.Tensor) -> torch.Tensor:
 def _mlp_forward(self, x: torch.Tensor) -> torch.Tensor:
     if not _fusable(x):
         return self._vq_orig_forward(x)
+    if self.gate_proj.out_features == self.up_proj.out_features:
+        gu = _group_projection((self.gate_proj, self.up_proj), x)
+        if gu is not None and _fusable(gu):
+            return self.down_proj(_SwiGLUPairFn.apply(gu))
     g = self.gate_proj(x)
     u = self.up_proj(x)
     if not (_fusable(g) and g.shape == u.shape):
@@ -149,14 +189,27 @@ def _mlp_forward(self, x: torch.Tensor) -> torch.Tensor:
 
 def _attention_forward(self, hidden_states: torch.Tensor, position_embeddings=None, attention_mask=None,
                        past_key_values=None, **kwargs):
+    if getattr(self, "_vq_causal_batches", False) and past_key_values is None:
+        # batches of the distillation step are causal and unpadded: the only
+        # mask Hugging Face builds for them is the causal one, which it
+        # materialises while a CUDA graph records instead of leaving it to
+        # is_causal
+        attention_mask = None
     if (past_key_values is not None or attention_mask is not None or position_embeddings is None
             or not _fusable(hidden_states) or self.head_dim % 16 or kwargs.get("output_attentions", False)):
         return self._vq_orig_forward(hidden_states, position_embeddings=position_embeddings,
                                      attention_mask=attention_mask, past_key_values=past_key_values, **kwargs)
     B, S = hidden_states.shape[:2]
-    q = self.q_proj(hidden_states).view(B, S, -1, self.head_dim)
-    k = self.k_proj(hidden_states).view(B, S, -1, self.head_dim)
-    v = self.v_proj(hidden_states).view(B, S, -1, self.head_dim)
+    qkv = _group_projection((self.q_proj, self.k_proj, self.v_proj), hidden_states)
+    if qkv is not None:  # one GEMM; q, k, v are column ranges of its output
+        nq, nk = self.q_proj.out_features, self.k_proj.out_features
+        q = qkv[..., :nq].view(B, S, -1, self.head_dim)
+        k = qkv[..., nq:nq + nk].view(B, S, -1, self.head_dim)
+        v = qkv[..., nq + nk:].view(B, S, -1, self.head_dim)
+    else:
+        q = self.q_proj(hidden_states).view(B, S, -1, self.head_dim)
+        k = self.k_proj(hidden_states).view(B, S, -1, self.head_dim)
+        v = self.v_proj(hidden_states).view(B, S, -1, self.head_dim)
     cos, sin = position_embeddings
     q, k = rope(q, k, cos, sin)
     o = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2), is_causal=S > 1,
@@ -189,11 +242,14 @@ def _decoder_forward(self, hidden_states: torch.Tensor, attention_mask=None, pos
     return h + self.mlp(x)
 
 
-def fuse_llama_blocks(model: torch.nn.Module) -> int:
+def fuse_llama_blocks(model: torch.nn.Module, causal_batches: bool = False) -> int:
     """Route the RMSNorm, attention (rotary) and MLP (SwiGLU) modules of a
     Hugging Face Llama model through the fused kernels, and each decoder
     layer's post-attention residual add into its RMSNorm, in place; returns
-    the number of modules patched.  Idempotent."""
+    the number of modules patched.  Idempotent.  ``causal_batches``: the
+    caller only ever feeds whole causal sequences without padding (the
+    distillation step), so the attention ignores the causal mask Hugging Face
+    passes while a CUDA graph records and keeps the fused path."""
     from transformers.models.llama import modeling_llama as L
 
     table = ((L.LlamaRMSNorm, _rmsnorm_forward), (L.LlamaAttention, _attention_forward),
@@ -207,4 +263,6 @@ def fuse_llama_blocks(model: torch.nn.Module) -> int:
                 m._vq_orig_forward = m.forward
                 m.forward = types.MethodType(fwd, m)
                 n += 1
+        if type(m) is L.LlamaAttention and causal_batches:
+            m._vq_causal_batches = True
     return n

@@ -420,6 +420,100 @@ def _gated_linear_backward(ctx, dy: torch.Tensor):
     return dx, dprobs
 
 
+class _GroupedGatedLinearFunction(Function):
+    """Gated Linears that read the same input (q/k/v, gate/up) as ONE GEMM:
+    each layer's mixture is written into its row range of one bf16 weight
+    [sum N_i, Kin], so the forward is one GEMM into Y [T, sum N_i] and the
+    input gradient one GEMM dX = dY W_cat (the sum over the layers happens
+    inside the GEMM's reduction, not as separate dX tensors added up).  Each
+    layer's gate gradient is its own gate-gradient GEMM over its column range
+    of dY.  Values are those of the per-layer path: the same mixtures, the
+    same products, fp32 accumulation (dX sums over sum N_i instead of adding
+    bf16 partial results, which is closer to the exact sum)."""
+
+    @staticmethod
+    def forward(ctx, x: torch.Tensor, layers: tuple, *probs: torch.Tensor):
+        in_f = layers[0].in_features
+        x2 = _C._as_operand(x.reshape(-1, in_f))
+        w_cat = _mix_group(layers, probs)
+        y = _C.linear_fwd(x2, w_cat, w_cat.shape[0], in_f)
+        ctx.layers = layers
+        ctx.x_shape = x.shape
+        ctx.x_dtype = x.dtype
+        ctx.save_for_backward(x2, *probs)
+        ctx.w_cat = w_cat if KEEP_MIXED_WEIGHT else None
+        return y.to(x.dtype).reshape(*x.shape[:-1], w_cat.shape[0])
+
+    @staticmethod
+    def backward(ctx, dy: torch.Tensor):
+        layers = ctx.layers
+        x2, *probs = ctx.saved_tensors
+        n_tot = sum(l.out_features for l in layers)
+        dy2 = _C._as_operand(dy.reshape(-1, n_tot))
+        dx = None
+        if ctx.needs_input_grad[0]:
+            w_cat = ctx.w_cat if ctx.w_cat is not None else _mix_group(layers, probs)
+            dx = _C.linear_dx(dy2, w_cat, layers[0].in_features)
+            dx = dx.to(ctx.x_dtype).reshape(ctx.x_shape)
+        ctx.w_cat = None
+        grads = []
+        a = 0
+        for i, layer in enumerate(layers):
+            b = a + layer.out_features
+            g = None
+            if ctx.needs_input_grad[2 + i]:
+                slot = _defer_slot(layer)
+                if slot is not None:  # runs beside the all-reduce of the module's input gradient
+                    _DEFERRED.append((dy2[:, a:b], x2, layer, slot))
+                else:
+                    g = _gategrad_into(dy2[:, a:b], x2, layer).to(probs[i].dtype)
+            grads.append(g)
+            a = b
+        return (dx, None, *grads)
+
+
+def _mix_group(layers, probs) -> torch.Tensor:
+    """The layers' bf16 mixtures stacked by rows into one [sum N_i, ld] weight."""
+    in_f = layers[0].in_features
+    ld = (in_f + 7) // 8 * 8
+    dev = layers[0]._cand_arena.device
+    w = torch.empty(sum(l.out_features for l in layers), ld, dtype=torch.bfloat16, device=dev)
+    a = 0
+    for layer, p in zip(layers, probs):
+        b = a + layer.out_features
+        _C.mix(layer.candidate_types, layer._candidate_blocks(), p.to(dev), layer.out_features,
+               layer.padded_in_features, in_f, out=w[a:b])
+        a = b
+    return w
+
+
+def groupable(layers) -> bool:
+    """Whether gated Linears can run as one grouped GEMM: same input width,
+    no halo or row-parallel shard, not PTQR-routed, no in-backward dX sum."""
+    if _PTQR_STATE.enabled or len(layers) < 2:
+        return False
+    l0 = layers[0]
+    for l in layers:
+        if not isinstance(l, MixedQuantLinear) or l.in_features != l0.in_features or l.in_col_offset or \
+                l.reduce_input_grad or l._cand_arena.device != l0._cand_arena.device or l.out_features % 8:
+            return False
+        spec = l.shard_spec
+        if spec is not None and spec.col_offset is not None:
+            return False
+    return True
+
+
+def gated_linear_group(layers, x: torch.Tensor) -> torch.Tensor:
+    """y = x [W_1; W_2; ...]^T for gated Linears sharing the input x (see
+    ``_GroupedGatedLinearFunction``): [..., sum N_i], layer i's outputs in
+    columns [sum_{j<i} N_j, sum_{j<=i} N_j)."""
+    layers = tuple(layers)
+    if x.device != layers[0]._cand_arena.device:
+        x = x.to(layers[0]._cand_arena.device)
+    probs = [l.get_probs().to(x.device) for l in layers]
+    return _GroupedGatedLinearFunction.apply(x, layers, *probs)
+
+
 class _RoutedGatedLinearFunction(Function):
     """PTQR forward y[t] = x[t] W_{k(t)}^T, one candidate per token (reference
     _RoutedMixedLinear, voodoo_quant/layers.py:366-428).

@@ -64,6 +64,33 @@ class Q8Linear(nn.Module):
         return y.to(x.dtype).reshape(*x.shape[:-1], self.out_features)
 
 
+def q8_groupable(mods) -> bool:
+    """Whether teacher Linears sharing an input can run as one GEMM."""
+    if len(mods) < 2:
+        return False
+    m0 = mods[0]
+    return all(type(m) is Q8Linear and m.in_features == m0.in_features and not m.in_col_offset and
+               m.out_features % 8 == 0 and m.qweight.device == m0.qweight.device for m in mods)
+
+
+@torch.no_grad()
+def q8_linear_group(mods, x: torch.Tensor) -> torch.Tensor:
+    """x [W_1; W_2; ...]^T for teacher Linears sharing the input x (q/k/v,
+    gate/up): each Q8_0 weight decoded into its row range of one bf16 weight,
+    then one GEMM; layer i's outputs in its column range of the result."""
+    in_f = mods[0].in_features
+    ld = (in_f + 7) // 8 * 8
+    n_tot = sum(m.out_features for m in mods)
+    w = torch.empty(n_tot, ld, dtype=torch.bfloat16, device=mods[0].qweight.device)
+    a = 0
+    for m in mods:
+        b = a + m.out_features
+        _C.mix(["Q8_0"], [m.qweight], m._one, m.out_features, m.padded_in_features, in_f, out=w[a:b])
+        a = b
+    y = _C.linear_fwd(x.reshape(-1, in_f), w, n_tot, in_f)
+    return y.to(x.dtype).reshape(*x.shape[:-1], n_tot)
+
+
 class Q8Embedding(nn.Module):
     """nn.Embedding stand-in holding Q8_0 bytes; decodes the touched rows."""
 

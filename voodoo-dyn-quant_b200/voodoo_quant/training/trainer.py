@@ -453,8 +453,8 @@ def build_distill(shape_name: str, device, seed: int = 0, args: StepArgs | None 
     if fused_blocks and torch.device(device).type == "cuda":
         from voodoo_quant.fused_blocks import fuse_llama_blocks
 
-        fuse_llama_blocks(base)
-        fuse_llama_blocks(teacher)
+        fuse_llama_blocks(base, causal_batches=True)
+        fuse_llama_blocks(teacher, causal_batches=True)
     if tp and TP.enabled:
         from voodoo_quant.parallel import enable_multicast_reduce, enable_teacher_overlap
 
