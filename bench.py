@@ -875,7 +875,8 @@ def run_model_step(args):
                                                  else "valid", static_shapes=args.graph_step,
                                                  teacher_stream=args.teacher_stream,
                                                  teacher_stream_sms=args.teacher_stream_sms,
-                                                 teacher_tp=args.teacher_tp))
+                                                 teacher_tp=args.teacher_tp,
+                                                 sequence_parallel=args.sequence_parallel and world > 1))
     from voodoo_quant import parallel as _par
 
     multicast_on = _par.multicast_reducer() is not None
@@ -961,6 +962,7 @@ def run_model_step(args):
                     "step_graph": "forward + backward replayed from one CUDA graph" if args.graph_step
                     else "eager",
                     "teacher_tp": args.teacher_tp or world,
+                    "sequence_parallel": bool(args.sequence_parallel and world > 1),
                     "teacher": (f"own stream and communicator beside the student, "
                                 f"{args.teacher_stream_sms} SMs left to collectives") if args.teacher_stream
                     else "after the student, same stream"},
@@ -1088,6 +1090,9 @@ def main():
     ap.add_argument("--teacher-tp", type=int, default=0,
                     help="step workloads under TP: the teacher's own TP degree t (groups of t ranks, each on "
                          "its batch slice; one all-to-all of its logits); 0 = the student's")
+    ap.add_argument("--sequence-parallel", action=argparse.BooleanOptionalAction, default=False,
+                    help="step workloads under TP: residual stream, norms and residual adds on token shards; "
+                         "all-gather / reduce-scatter around each block instead of all-reduces")
     ap.add_argument("--layers", type=int, default=0,
                     help="step workloads: build only this many decoder layers (a smoke run of the build, "
                          "memory plan and step; its line says so and is not the configuration's number)")

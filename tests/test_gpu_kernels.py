@@ -120,6 +120,43 @@ def test_mix_one_hot_is_rounded_decode(cuda):
         assert torch.equal(w, ref)
 
 
+def test_mix_full_size_and_unaligned_streams(cuda):
+    """A config-2-sized mixture (14336 x 4096, six candidates: each persistent
+    CTA walks many blocks, refilling its bulk-copy stages) against a float32
+    torch mixture of the exact decodes (2^-7 of the largest weight); one-hot
+    gates give bf16(decode) bit for bit; and candidate streams that start 2,
+    6 or 10 bytes past a 16-byte boundary give the same bits as aligned ones."""
+    from voodoo_quant import _C
+    from voodoo_quant.quants import rtn
+
+    types = ["Q2_K", "Q3_K", "Q4_K", "Q5_K", "Q6_K", "Q8_0"]
+    rows, cols = 14336, 4096
+    g = torch.Generator(device=cuda).manual_seed(17)
+    w = torch.randn(rows, cols, generator=g, device=cuda) * 0.02
+    blocks = [rtn.quantize(w, q) for q in types]
+    del w
+    probs = torch.softmax(torch.randn(len(types), generator=g, device=cuda), 0)
+    got = _C.mix(types, blocks, probs, rows, cols, cols)
+    ref = torch.zeros(rows, cols, device=cuda)
+    for k, (q, b) in enumerate(zip(types, blocks)):
+        ref += probs[k] * _C.dequant(b, q, rows, cols)
+    assert float((got.float() - ref).abs().max()) <= 2 ** -7 * float(ref.abs().max())
+    for k in (1, 4):  # Q3_K and Q6_K: units that start inside a word
+        one = torch.zeros(len(types), device=cuda)
+        one[k] = 1.0
+        w1 = _C.mix(types, blocks, one, rows, cols, cols)
+        assert torch.equal(w1, _C.dequant(blocks[k], types[k], rows, cols).to(torch.bfloat16)), types[k]
+    shifted = []
+    for k, b in enumerate(blocks):
+        off = (2, 6, 10)[k % 3]
+        buf = torch.zeros(b.numel() + 32, dtype=torch.uint8, device=cuda)
+        buf[off:off + b.numel()] = b.reshape(-1)
+        shifted.append(buf[off:off + b.numel()])
+    assert torch.equal(_C.mix(types, shifted, probs, rows, cols, cols), got)
+    torch.cuda.synchronize()
+    assert _C.device_error() == 0
+
+
 def _bf16(t):
     return t.to(torch.bfloat16)
 

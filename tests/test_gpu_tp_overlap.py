@@ -1,12 +1,17 @@
 """TP-2 distillation step with the input-gradient all-reduces overlapped
 (gate-gradient GEMMs deferred beside them on a second communicator; then
 also the head's dX all-reduced in two row chunks) against the same step
-without overlap, on 2 GPUs (skipped with fewer).
+without overlap, and the sequence-parallel step (token-shard residual
+stream, all-gather / reduce-scatter around every block) with and without
+the overlap, on 2 GPUs (skipped with fewer).
 
 The overlap only reorders launches and leaves SMs free; the gate-gradient
 GEMM's stream-K split depends on how many SMs it gets, so its fp32 partial
 sums may be added in another order.  Tolerance: loss 1e-5 relative, gate
-gradients 1e-3 relative per tensor (L2).
+gradients 1e-3 relative per tensor (L2).  Sequence parallelism sums the
+row-parallel outputs by reduce-scatter instead of all-reduce (another order
+of the bf16 partial sums): loss 2e-3 relative, gate gradients per tensor
+within 3e-2 relative with cosine >= 0.999.
 """
 
 from __future__ import annotations
@@ -39,7 +44,7 @@ def _worker(rank, world, port, outdir):
     dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev, timeout=timedelta(seconds=120))
     from voodoo_quant import _C, layers, parallel
     from voodoo_quant.training import synthetic as S
-    from voodoo_quant.training.trainer import build_distill
+    from voodoo_quant.training.trainer import StepArgs, build_distill
 
     # the smallest Llama shape whose TP-2 shards keep every input dimension 256-aligned
     S.SHAPES["tp2_test"] = S.ModelShape(2, 512, 4, 2, 1024, 4096, False, head_dim=128,
@@ -47,14 +52,15 @@ def _worker(rank, world, port, outdir):
     res = {}
     try:
         parallel.adopt_process_group(rank)
-        for sms, chunks in ((0, 1), (24, 1), (24, 2)):
+        for sms, chunks, sp in ((0, 1, False), (24, 1, False), (24, 2, False), (0, 1, True), (24, 1, True)):
             layers.INPUT_GRAD_CHUNKS = chunks  # the head sums its own input gradient in row chunks
-            trainer, shape = build_distill("tp2_test", dev, seed=0, tp=True, overlap_sms=sms)
+            trainer, shape = build_distill("tp2_test", dev, seed=0, tp=True, overlap_sms=sms,
+                                           args=StepArgs(sequence_parallel=sp))
             deferred = sum(bool(m.__dict__.get("_defer_gategrad", False)) for m in trainer.replaced.values())
             x, y = S.random_tokens(shape, dev, seed=1)
             out = trainer.forward_backward(x, y)
             torch.cuda.synchronize()
-            res[(sms, chunks)] = {"loss": float(out["loss"]), "deferred": deferred,
+            res[(sms, chunks, sp)] = {"loss": float(out["loss"]), "deferred": deferred,
                         "grads": {n: m.gates.grad.detach().cpu().clone() for n, m in trainer.replaced.items()},
                         "left": layers.has_deferred_gategrads()}
             del trainer
@@ -76,12 +82,20 @@ def test_overlapped_input_grad_allreduce_matches_plain_step():
         rs = [torch.load(os.path.join(td, f"r{r}.pt")) for r in range(2)]
     for r in rs:
         assert r["dev_err"] == 0
-        a = r[(0, 1)]
+        a = r[(0, 1, False)]
         assert a["deferred"] == 0
-        for key in ((24, 1), (24, 2)):
+        for key in ((24, 1, False), (24, 2, False), (24, 1, True)):
             b = r[key]
+            base = r[(0, 1, key[2])]
             assert b["deferred"] > 0 and not b["left"]
-            assert abs(a["loss"] - b["loss"]) <= 1e-5 * abs(a["loss"])
-            for n, g in a["grads"].items():
+            assert abs(base["loss"] - b["loss"]) <= 1e-5 * abs(base["loss"])
+            for n, g in base["grads"].items():
                 h = b["grads"][n]
                 assert float((g - h).norm()) <= 1e-3 * float(g.norm()) + 1e-12, (key, n)
+        sp = r[(0, 1, True)]
+        assert abs(sp["loss"] - a["loss"]) <= 2e-3 * abs(a["loss"])
+        for n, g in a["grads"].items():
+            h = sp["grads"][n].double()
+            gd = g.double()
+            assert float((h - gd).norm()) <= 3e-2 * float(gd.norm()) + 1e-12, n
+            assert float(h @ gd) >= 0.999 * float(h.norm() * gd.norm()), n

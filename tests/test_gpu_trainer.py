@@ -1,9 +1,9 @@
-"""The full distillation step on the B200 kernels against a plain-torch
+"""The full distillation step on the B200 kernels against a float32 torch
 restatement of the reference step (voodoo_quant/training/trainer.py:
-2443-2616): every gated weight is sum_k softmax(g / tau)_k * decode_k in fp32
-(decoded by the CPU oracle), rounded to bf16 and used through F.linear /
-F.embedding; the loss is F.cross_entropy + T^2 * KL on fp32 logits, plus the
-relu-squared size term.
+2443-2616): every gated weight is sum_k softmax(g / tau)_k * decode_k in
+float32 (decoded by the CPU oracle) used through F.linear / F.embedding in a
+float32 copy of the model; the loss is F.cross_entropy + T^2 * KL on its
+float32 logits, plus the relu-squared size term.
 
 The teacher is checked on its own first, against an independent path: every
 weight quantised by the oracle's Q8_0 rule (oracle/q8_quant.py, pinned to
@@ -12,18 +12,13 @@ in an fp32 copy of the model): logits within 1e-2 relative.  The
 restatement's KL then uses the step's own teacher logits, so the gate
 gradients compare the student path alone.
 
-The restatement rounds every weight to bf16 for the products, as the kernels
-do, and forms dW = dY^T X in float32 before the contraction with the
-candidates, as the gate-gradient kernel does in TMEM (a bf16-rounded dW, as
-plain autograd of a bf16 F.linear would give, costs the head's gradient 2 %
-of cosine on its own).
-
-Tolerances: the loss within 2e-3 relative; gate gradients per tensor cosine
->= 0.999 with the reference's default arguments, and, with the size term off
-(the distillation gradient alone, a small difference signal between nearly
-equal candidates whose bf16 rounding sites differ between the two paths),
->= 0.99 per tensor and >= 0.999 with relative L2 error < 3e-2 for all
-tensors as one vector.
+Tolerances (bf16 operands with fp32 accumulation against float32): the loss
+within 1e-2 relative; gate gradients of all tensors as one vector cosine >=
+0.999 with relative L2 error < 3e-2; per tensor, cosine >= 0.999 with the
+reference's default arguments, and >= 0.995 with the size term off (the
+distillation gradient alone, a small difference signal between nearly equal
+candidates, to which every bf16 rounding site of the step adds 1e-4 to 3e-4
+of cosine).
 """
 
 from __future__ import annotations
@@ -37,30 +32,6 @@ import torch.nn.functional as F
 from oracle import ggml_blocks, q8_quant
 
 pytestmark = pytest.mark.gpu
-
-
-class _Bf16OperandsFp32Grad(torch.autograd.Function):
-    """F.linear / F.embedding on the bf16-rounded weight, whose weight
-    gradient is formed in float32 (dW = dY^T X unrounded, as the gate-gradient
-    kernel forms it in TMEM) and flows to the float32 weight."""
-
-    @staticmethod
-    def forward(ctx, x, w32, embedding):
-        ctx.save_for_backward(x, w32)
-        ctx.embedding = embedding
-        wb = w32.to(torch.bfloat16)
-        return F.embedding(x, wb) if embedding else F.linear(x, wb)
-
-    @staticmethod
-    def backward(ctx, dy):
-        x, w32 = ctx.saved_tensors
-        if ctx.embedding:
-            dw = torch.zeros_like(w32).index_add_(0, x.reshape(-1), dy.reshape(-1, w32.shape[1]).float())
-            return None, dw, None
-        d2 = dy.reshape(-1, w32.shape[0])
-        dx = (d2 @ w32.to(torch.bfloat16)).reshape(*dy.shape[:-1], w32.shape[1])
-        dw = d2.float().t() @ x.reshape(-1, w32.shape[1]).float()
-        return dx, dw, None
 
 
 class _TorchGated(nn.Module):
@@ -88,7 +59,8 @@ class _TorchGated(nn.Module):
         return (torch.softmax(self.gates / self.tau, dim=0) * self.bpw).sum() * self.numel
 
     def forward(self, x):
-        return _Bf16OperandsFp32Grad.apply(x, self.weight32(), self.embedding)
+        w = self.weight32()
+        return F.embedding(x, w) if self.embedding else F.linear(x, w)
 
 
 def _set(model, name, mod):
@@ -117,7 +89,7 @@ def _oracle_q8_teacher(shape, cuda, seed):
 
 
 # (distill_temperature, distill_weight, size_weight, size_tolerance), per-tensor cosine
-_ARGS = {"default": ((1.0, 1.0, 10.0, 0.02), 0.999), "kd": ((2.0, 0.7, 0.0, 0.0), 0.99)}
+_ARGS = {"default": ((1.0, 1.0, 10.0, 0.02), 0.999), "kd": ((2.0, 0.7, 0.0, 0.0), 0.995)}
 
 
 @pytest.mark.parametrize("variant", ["default", "kd"])
@@ -143,7 +115,7 @@ def test_tiny_distill_step_matches_torch_restatement(cuda, variant):
         t_oracle = _oracle_q8_teacher(shape, cuda, seed=3)(input_ids=x).logits.float()
     assert float((t_logits - t_oracle).norm() / t_oracle.norm()) < 1e-2
 
-    ref = S.build_llama(shape, cuda, seed=3)
+    ref = S.build_llama(shape, cuda, seed=3).float()
     mods = {}
     for name, layer in trainer.replaced.items():
         mods[name] = _TorchGated(layer, isinstance(layer, MixedQuantEmbedding))
@@ -168,7 +140,7 @@ def test_tiny_distill_step_matches_torch_restatement(cuda, variant):
     loss = lm + args.distill_weight * kl + args.size_weight * size
     loss.backward()
 
-    assert abs(out["loss"].item() - loss.item()) <= 2e-3 * abs(loss.item())
+    assert abs(out["loss"].item() - loss.item()) <= 1e-2 * abs(loss.item())
     assert abs(out["size_bytes"].item() - cur.item()) <= 1e-5 * cur.item()
     assert out["size_loss"].item() == pytest.approx(size.item(), rel=1e-4)
     ours = {n: trainer.replaced[n].gates.grad.double() for n in mods}

@@ -39,17 +39,19 @@ def _shapes():
                                         batch=2, seq=48, budget=0.45)
 
 
-def _step(name: str, tp: bool, overlap_sms: int, chunk: int):
+def _step(name: str, tp: bool, overlap_sms: int, chunk: int, sp: bool = False):
     from voodoo_quant.training import synthetic as S
     from voodoo_quant.training.trainer import StepArgs, build_distill
 
-    args = StepArgs(max_steps=4, ce_reduction="tokens", logits_chunk=chunk)
+    args = StepArgs(max_steps=4, ce_reduction="tokens", logits_chunk=chunk, sequence_parallel=sp)
     trainer, shape = build_distill(name, "cpu", seed=3, args=args, tp=tp, overlap_sms=overlap_sms)
     x, y = S.random_tokens(shape, "cpu", seed=5)
     r = trainer.forward_backward(x, y)
     grads = {n: m.gates.grad.detach().clone() for n, m in trainer.replaced.items()}
     deferred = sum(bool(m.__dict__.get("_defer_gategrad", False)) for m in trainer.replaced.values())
-    return float(r["loss"]), grads, deferred
+    from voodoo_quant.parallel import sp_enabled
+    on = sp_enabled() and hasattr(trainer.student.model, "_vq_sp_orig_forward")
+    return float(r["loss"]), grads, deferred, on
 
 
 def _cos(a: torch.Tensor, b: torch.Tensor) -> float:
@@ -89,6 +91,9 @@ def _worker(rank, world, port, outdir):
         res = {"plain": _step("cpu_tp2", True, 0, 0)}
         res["overlap"] = _step("cpu_tp2", True, 24, 0)
         res["overlap_chunked"] = _step("cpu_tp2", True, 24, 40)
+        res["sp"] = _step("cpu_tp2", True, 0, 0, sp=True)
+        res["sp_overlap"] = _step("cpu_tp2", True, 24, 0, sp=True)
+        res["sp_chunked"] = _step("cpu_tp2", True, 24, 40, sp=True)
         torch.save(res, os.path.join(outdir, f"r{rank}.pt"))
     finally:
         undo()
@@ -120,9 +125,24 @@ def test_tp2_step_matches_one_process_with_and_without_overlap():
             assert float((ovc[1][n] - ov[1][n]).norm()) <= 1e-4 * float(ov[1][n].norm()) + 1e-9, n
             assert _cos(plain[1][n], g) > 0.999, n
             assert float((plain[1][n] - g).norm()) <= 2e-2 * float(g.norm()) + 1e-9, n
+    # sequence parallelism: the same step (token-shard residual stream,
+    # all-gather / reduce-scatter around each block), with and without the
+    # deferred gate-gradient overlap and with the chunked head
+    for r in rs:
+        sp, spo, spc = r["sp"], r["sp_overlap"], r["sp_chunked"]
+        assert sp[3] and spo[3] and spc[3] and not r["plain"][3]
+        assert sp[2] == 0 and spo[2] > 0
+        assert abs(sp[0] - ref[0]) <= 2e-2 * abs(ref[0]) and abs(spo[0] - sp[0]) <= 1e-6 * abs(sp[0])
+        assert abs(spc[0] - sp[0]) <= 1e-5 * abs(sp[0])
+        for n, g in ref[1].items():
+            assert _cos(sp[1][n], g) > 0.999, n
+            assert float((sp[1][n] - g).norm()) <= 2e-2 * float(g.norm()) + 1e-9, n
+            assert float((spo[1][n] - sp[1][n]).norm()) <= 1e-5 * float(sp[1][n].norm()) + 1e-9, n
+            assert float((spc[1][n] - sp[1][n]).norm()) <= 1e-4 * float(sp[1][n].norm()) + 1e-9, n
     # both ranks hold the same (all-reduced) gate gradients
     for n in ref[1]:
         assert torch.equal(rs[0]["plain"][1][n], rs[1]["plain"][1][n]), n
+        assert torch.equal(rs[0]["sp"][1][n], rs[1]["sp"][1][n]), n
 
 
 def test_ptqr_step_with_concentrated_gates_equals_the_mixture():

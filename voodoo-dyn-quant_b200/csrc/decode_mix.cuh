@@ -12,8 +12,8 @@
 // The dequant kernel stages a CTA's run of consecutive units into
 // word-aligned shared-memory slots with aligned 32-bit loads (2-byte aligned
 // GGUF blocks realigned with funnel shifts); the mix kernel copies each
-// candidate's contiguous span with 16-byte cp.async and realigns only the
-// units that are not word aligned.
+// candidate's contiguous span of a block of units with one bulk copy and
+// reads the fields of units that start inside a word through funnel shifts.
 #pragma once
 
 #include "formats.cuh"
@@ -90,212 +90,346 @@ __global__ void __launch_bounds__(kDecodeThreads) dequant_units_kernel(CandSet c
 }
 
 // ---------------------------------------------------------------- mixture
-// Shared-memory layout of one mix CTA (kMixUnits consecutive units): per
-// candidate a raw region holding the 16-byte aligned span of its units'
-// contiguous bytes (copied with cp.async), and, for a candidate whose units
-// are not all 4-byte aligned there (2-byte multiple unit sizes, or a base
-// pointer that is not 4-byte aligned), a region of word-aligned unit slots.
-__host__ __device__ inline int mix_raw_bytes(int ub) { return (kMixUnits * ub + 32 + 15) & ~15; }
-__host__ __device__ inline bool mix_realign(const CandSet& cs, int k) {
-  return ((cs.ubytes[k] & 3) != 0) || ((reinterpret_cast<uintptr_t>(cs.ptr[k]) & 3u) != 0);
-}
-inline int mix_smem_bytes(const CandSet& cs) {
+// One mix CTA owns blocks of kMixUnits consecutive units and walks them with
+// a stride of the grid (persistent).  Per block and candidate, one thread
+// copies the contiguous span of the block's units into a shared-memory
+// region with a single bulk copy (cp.async.bulk, completion counted on the
+// stage's mbarrier); kMixStages stages keep the next blocks' copies in
+// flight while the current one is mixed.  Units keep their byte layout in
+// shared memory: a unit whose size is not a multiple of 4 (Q3_K, Q6_K) or
+// whose stream base is not 16-byte aligned starts inside a word, and every
+// field is read as the two aligned words that hold it, joined by one funnel
+// shift that also applies the field's own bit shift.
+constexpr int kMixStages = 2;
+
+// Bytes of one candidate's region in a stage: the 16-byte aligned span of
+// kMixUnits units plus 32 bytes, so that a field read at a unit's end never
+// leaves the region.
+__host__ __device__ inline int mix_region_bytes(int ub) { return ((kMixUnits * ub + 15) & ~15) + 32 + 16; }
+inline int mix_stage_bytes(const CandSet& cs) {
   int s = 0;
-  for (int k = 0; k < cs.K; ++k) {
-    s += mix_raw_bytes(cs.ubytes[k]);
-    if (mix_realign(cs, k)) s += kMixUnits * unit_words(cs.fmt[k]) * 4;
-  }
+  for (int k = 0; k < cs.K; ++k) s += mix_region_bytes(cs.ubytes[k]);
   return s;
 }
 
-// Per-candidate addressing of one block in the mix CTA's buffer (bytes):
-// unit lu of the candidate is at slot + lu * stride, its raw bytes at
-// raw + lu * ub.
-struct MixCand {
-  int fmt, slot, stride, raw, ub;
-  float p;
+// A unit in shared memory: `s` is the word holding its first byte, which is
+// byte `delta` (0..3) of that word.
+struct URef {
+  const uint32_t* s;
+  int delta;
+  uint32_t sh;  // 8 * delta
+  // unit bytes [4 i, 4 i + 4) shifted right by `extra` bits (extra < 8)
+  __device__ __forceinline__ uint32_t wq(int i, int extra = 0) const {
+    return __funnelshift_r(s[i], s[i + 1], sh + extra);
+  }
+  // the 32 bits at any unit byte `off`
+  __device__ __forceinline__ uint32_t w(int off) const {
+    const int o = off + delta;
+    return __funnelshift_r(s[o >> 2], s[(o >> 2) + 1], 8 * (o & 3));
+  }
+  __device__ __forceinline__ uint32_t b16(int off) const { return w(off) & 0xFFFFu; }
+  __device__ __forceinline__ uint32_t b8(int off) const { return w(off) & 0xFFu; }
 };
 
-__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(gsrc) : "memory");
+// Scale and min of K-quant sub-block j from the 12-byte table at unit byte 4.
+__device__ __forceinline__ void k4_scale_min_u(const URef& u, int j, uint32_t& sc, uint32_t& mn) {
+  if (j < 4) {
+    sc = u.b8(4 + j) & 63u;
+    mn = u.b8(8 + j) & 63u;
+  } else {
+    const uint32_t hi = u.b8(8 + j);  // q[j + 4]
+    sc = (hi & 15u) | ((u.b8(j) >> 6) << 4);
+    mn = (hi >> 4) | ((u.b8(4 + j) >> 6) << 4);
+  }
 }
 
-// acc2[j] holds elements 2j, 2j+1; w = (p_k a[h]) * q + p_k b[h] with the
-// b part kept per half in cst.
+// Sub-block c (32 weights) of a unit as w = a[h] * q + b[h] (h = half of the
+// sub-block), with the codes q + kSub - 2^23 one per byte of qb.  The same
+// products, in the same order, as Chunk<F> (and so as the exact decoders up
+// to the last rounding).
 template <int F>
-__device__ __forceinline__ void mix_chunk(const uint32_t* slot, int c, float pk, uint64_t (&acc2)[16], float (&cst)[2]) {
+struct MixChunk;
+
+template <>
+struct MixChunk<kQ8_0> {
+  static constexpr bool kMin = false;
+  static constexpr float kSub = 8388736.0f;  // 2^23 + 128: int8 codes stored with the sign bit flipped
+  __device__ __forceinline__ static void get(const URef& u, int c, float (&a)[2], float (&b)[2], uint32_t (&qb)[8]) {
+    a[0] = a[1] = h2f(u.b16(34 * c));
+    b[0] = b[1] = 0.f;
+    const int o0 = 34 * c + 2 + u.delta;  // the block's codes
+    const uint32_t* q = u.s + (o0 >> 2);
+    const uint32_t shq = 8u * static_cast<uint32_t>(o0 & 3);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) qb[j] = __funnelshift_r(q[j], q[j + 1], shq) ^ 0x80808080u;
+  }
+};
+
+template <>
+struct MixChunk<kQ4_K> {
+  static constexpr bool kMin = true;
+  static constexpr float kSub = 8388608.0f;
+  __device__ __forceinline__ static void get(const URef& u, int c, float (&a)[2], float (&b)[2], uint32_t (&qb)[8]) {
+    const uint32_t w0 = u.wq(0);
+    uint32_t sc, mn;
+    k4_scale_min_u(u, c, sc, mn);
+    a[0] = a[1] = __fmul_rn(h2f(w0), u2f(sc));
+    b[0] = b[1] = -__fmul_rn(h2f(w0 >> 16), u2f(mn));
+#pragma unroll
+    for (int j = 0; j < 8; ++j) qb[j] = u.wq(4 + 8 * (c >> 1) + j, 4 * (c & 1)) & 0x0F0F0F0Fu;
+  }
+};
+
+template <>
+struct MixChunk<kQ5_K> {
+  static constexpr bool kMin = true;
+  static constexpr float kSub = 8388608.0f;
+  __device__ __forceinline__ static void get(const URef& u, int c, float (&a)[2], float (&b)[2], uint32_t (&qb)[8]) {
+    const uint32_t w0 = u.wq(0);
+    uint32_t sc, mn;
+    k4_scale_min_u(u, c, sc, mn);
+    a[0] = a[1] = __fmul_rn(h2f(w0), u2f(sc));
+    b[0] = b[1] = -__fmul_rn(h2f(w0 >> 16), u2f(mn));
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      qb[j] = (u.wq(12 + 8 * (c >> 1) + j, 4 * (c & 1)) & 0x0F0F0F0Fu) | ((u.wq(4 + j, c) & 0x01010101u) << 4);
+  }
+};
+
+template <>
+struct MixChunk<kQ6_K> {
+  static constexpr bool kMin = false;
+  static constexpr float kSub = 8388640.0f;  // 2^23 + 32
+  __device__ __forceinline__ static void get(const URef& u, int c, float (&a)[2], float (&b)[2], uint32_t (&qb)[8]) {
+    const int h = c >> 2, g = c & 3;
+    const float d = h2f(u.b16(208));
+    const uint32_t sw = u.b16(192 + 8 * h + 2 * g);  // two int8 scales
+    const int sc0 = static_cast<int>(static_cast<int8_t>(sw & 0xFFu));
+    const int sc1 = static_cast<int>(static_cast<int8_t>((sw >> 8) & 0xFFu));
+    a[0] = __fmul_rn(d, u2f(static_cast<uint32_t>(sc0 + 128)) - 128.0f);
+    a[1] = __fmul_rn(d, u2f(static_cast<uint32_t>(sc1 + 128)) - 128.0f);
+    b[0] = b[1] = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      qb[j] = (u.wq(16 * h + 8 * (g & 1) + j, 4 * (g >> 1)) & 0x0F0F0F0Fu) |
+              ((u.wq(32 + 8 * h + j, 2 * g) & 0x03030303u) << 4);
+  }
+};
+
+template <>
+struct MixChunk<kQ2_K> {
+  static constexpr bool kMin = true;
+  static constexpr float kSub = 8388608.0f;
+  __device__ __forceinline__ static void get(const URef& u, int c, float (&a)[2], float (&b)[2], uint32_t (&qb)[8]) {
+    const int h = c >> 2, sft = c & 3;
+    const uint32_t sw = u.b16(2 * c);  // scale bytes 2c, 2c+1
+    const uint32_t wd = u.wq(20);
+    const float d = h2f(wd), dmin = h2f(wd >> 16);
+    a[0] = __fmul_rn(d, u2f(sw & 15u));
+    b[0] = -__fmul_rn(dmin, u2f((sw >> 4) & 15u));
+    a[1] = __fmul_rn(d, u2f((sw >> 8) & 15u));
+    b[1] = -__fmul_rn(dmin, u2f((sw >> 12) & 15u));
+#pragma unroll
+    for (int j = 0; j < 8; ++j) qb[j] = u.wq(4 + 8 * h + j, 2 * sft) & 0x03030303u;
+  }
+};
+
+template <>
+struct MixChunk<kQ3_K> {
+  static constexpr bool kMin = false;
+  static constexpr float kSub = 8388612.0f;  // 2^23 + 4
+  __device__ __forceinline__ static void get(const URef& u, int c, float (&a)[2], float (&b)[2], uint32_t (&qb)[8]) {
+    const int h = c >> 2, sft = c & 3;
+    const float d = h2f(u.b16(108));
+#pragma unroll
+    for (int t = 0; t < 2; ++t) {
+      const int j16 = 2 * c + t;
+      const uint32_t lo = (u.b8(96 + (j16 & 7)) >> (4 * (j16 >> 3))) & 15u;
+      const uint32_t hi = (u.b8(104 + (j16 & 3)) >> (2 * (j16 >> 2))) & 3u;
+      a[t] = __fmul_rn(d, u2f(lo | (hi << 4)) - 32.0f);
+      b[t] = 0.f;
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      qb[j] = (u.wq(8 + 8 * h + j, 2 * sft) & 0x03030303u) | ((u.wq(j, c) & 0x01010101u) << 2);
+  }
+};
+
+template <>
+struct MixChunk<kIQ4_XS> {
+  static constexpr bool kMin = false;
+  static constexpr float kSub = 8388736.0f;  // 2^23 + 128
+  __device__ __forceinline__ static void get(const URef& u, int c, float (&a)[2], float (&b)[2], uint32_t (&qb)[8]) {
+    const uint32_t w0 = u.wq(0);
+    const uint32_t ls = ((u.b8(4 + (c >> 1)) >> (4 * (c & 1))) & 15u) | ((((w0 >> 16) >> (2 * c)) & 3u) << 4);
+    a[0] = a[1] = __fmul_rn(h2f(w0), u2f(ls) - 32.0f);
+    b[0] = b[1] = 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t w = u.wq(2 + 4 * c + j);  // elements 4j.. (low nibbles) and 16 + 4j.. (high)
+      qb[j] = iq4nl4(w & 0x0F0F0F0Fu);
+      qb[4 + j] = iq4nl4((w >> 4) & 0x0F0F0F0Fu);
+    }
+  }
+};
+
+// acc[j] holds elements 2j, 2j+1; w = (p_k a[h]) * q + p_k b[h], the b part
+// kept per half in cst.
+template <int F>
+__device__ __forceinline__ void mix_chunk(const URef& u, int c, float pk, float2 (&acc)[16], float (&cst)[2]) {
   float a[2], b[2];
   uint32_t qb[8];
-  Chunk<F>::qbytes(slot, c, a, b, qb);
-  const uint64_t pa[2] = {f2pack(pk * a[0], pk * a[0]), f2pack(pk * a[1], pk * a[1])};
-  const uint64_t nsub = f2pack(-Chunk<F>::kSub, -Chunk<F>::kSub);
-  if (Chunk<F>::kMin) {
+  MixChunk<F>::get(u, c, a, b, qb);
+  const float2 pa[2] = {make_float2(pk * a[0], pk * a[0]), make_float2(pk * a[1], pk * a[1])};
+  const float2 nsub = make_float2(-MixChunk<F>::kSub, -MixChunk<F>::kSub);
+  if (MixChunk<F>::kMin) {
     cst[0] = fmaf(pk, b[0], cst[0]);
     cst[1] = fmaf(pk, b[1], cst[1]);
   }
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
-    const uint64_t q01 = f2add(f2pack(magic_byte(qb[j], 0), magic_byte(qb[j], 1)), nsub);
-    const uint64_t q23 = f2add(f2pack(magic_byte(qb[j], 2), magic_byte(qb[j], 3)), nsub);
-    acc2[2 * j] = f2fma(pa[j >> 2], q01, acc2[2 * j]);
-    acc2[2 * j + 1] = f2fma(pa[j >> 2], q23, acc2[2 * j + 1]);
+    const float2 q01 = __fadd2_rn(make_float2(magic_byte(qb[j], 0), magic_byte(qb[j], 1)), nsub);
+    const float2 q23 = __fadd2_rn(make_float2(magic_byte(qb[j], 2), magic_byte(qb[j], 3)), nsub);
+    acc[2 * j] = __ffma2_rn(pa[j >> 2], q01, acc[2 * j]);
+    acc[2 * j + 1] = __ffma2_rn(pa[j >> 2], q23, acc[2 * j + 1]);
   }
 }
 
-// Issue the cp.async copies of block `blk` (kMixUnits units) of every
-// candidate into the raw regions of the buffer at `buf` (layout as above).
-__device__ __forceinline__ void mix_issue(const CandSet& cs, uint8_t* buf, long long blk, long long total_units) {
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(bar)
+               : "memory");
+}
+
+// Issue the bulk copies of block `blk` of every candidate into stage buffer
+// `buf`, completion on `bar` (one thread).
+__device__ __forceinline__ void mix_issue(const CandSet& cs, uint8_t* buf, uint32_t bar, long long blk,
+                                          long long total_units) {
   const long long u0 = blk * kMixUnits;
   const int nunits = static_cast<int>(min(static_cast<long long>(kMixUnits), total_units - u0));
-  int off = 0;
-  for (int k = 0; k < cs.K; ++k) {
+  // the 16-byte aligned span of candidate k's units [u0, u0 + nunits)
+  auto span = [&](int k, uintptr_t& a0) -> uint32_t {
     const int ub = cs.ubytes[k];
     const uintptr_t st = reinterpret_cast<uintptr_t>(cs.ptr[k]) + static_cast<uintptr_t>(u0) * ub;
-    const uintptr_t a0 = st & ~uintptr_t(15);
-    const int n16 = static_cast<int>((((st + static_cast<uintptr_t>(nunits) * ub + 15) & ~uintptr_t(15)) - a0) >> 4);
-    for (int i = threadIdx.x; i < n16; i += kDecodeThreads)
-      cp_async16(buf + off + 16 * i, reinterpret_cast<const void*>(a0 + 16 * static_cast<uintptr_t>(i)));
-    off += mix_raw_bytes(ub);
-    if (mix_realign(cs, k)) off += kMixUnits * unit_words(cs.fmt[k]) * 4;
+    a0 = st & ~uintptr_t(15);
+    return static_cast<uint32_t>(((st + static_cast<uintptr_t>(nunits) * ub + 15) & ~uintptr_t(15)) - a0);
+  };
+  uint32_t total = 0;
+  for (int k = 0; k < cs.K; ++k) {
+    uintptr_t a0;
+    total += span(k, a0);
+  }
+  mbar_arrive_expect_tx(bar, total);
+  int off = 0;
+  for (int k = 0; k < cs.K; ++k) {
+    uintptr_t a0;
+    const uint32_t n = span(k, a0);
+    bulk_g2s(smem_u32(buf + off), reinterpret_cast<const void*>(a0), n, bar);
+    off += mix_region_bytes(cs.ubytes[k]);
   }
 }
 
-// rows * units_per_row units in total (whole units: padded cols % 256 == 0),
-// in blocks of kMixUnits.  Persistent CTAs walk the blocks with a stride of
-// the grid; with two buffers the copies of the next block are in flight while
-// the current one is decoded.  One thread per 32-weight sub-block: its scales
-// are decoded once per candidate, then one packed FMA per two weights.
+// W_mix[o, i] = sum_k p_k W_k[o, i] -> bf16 [rows, ld_out] for rows *
+// units_per_row whole units; columns >= cols (the zero padding of
+// in_features) are written as 0.  Thread (lu, c) of a block mixes sub-block
+// c (32 weights) of unit lu over every candidate.
 #ifndef VQ_MIX_MIN_BLOCKS
-#define VQ_MIX_MIN_BLOCKS 4  // resident CTAs per SM the register budget is sized for
+#define VQ_MIX_MIN_BLOCKS 3  // resident CTAs per SM the register budget is sized for
 #endif
 __global__ void __launch_bounds__(kDecodeThreads, VQ_MIX_MIN_BLOCKS)
     mix_units_kernel(CandSet cs, const float* __restrict__ probs, long long total_units, int units_per_row, int cols,
-                     __nv_bfloat16* __restrict__ out, long long ld_out, int buf_bytes, int nbuf, int* err) {
-  extern __shared__ __align__(16) uint8_t msmem[];
-  __shared__ MixCand meta[kMaxCandidates];
+                     __nv_bfloat16* __restrict__ out, long long ld_out, int stage_bytes, int* err) {
+  extern __shared__ __align__(128) uint8_t msmem[];
+  __shared__ __align__(8) uint64_t bars[kMixStages];
+  __shared__ float pk_s[kMaxCandidates];
+  __shared__ int abort_flag;
   const long long nblocks = (total_units + kMixUnits - 1) / kMixUnits;
   const int tid = threadIdx.x;
   const int lu = tid >> 3, c = tid & 7;
-  bool ok = true;
-
-  long long blk = blockIdx.x;
-  if (blk < nblocks) mix_issue(cs, msmem, blk, total_units);
-  asm volatile("cp.async.commit_group;" ::: "memory");
-  for (int it = 0; blk < nblocks; blk += gridDim.x, ++it) {
-    uint8_t* buf = msmem + (nbuf == 2 ? (it & 1) * buf_bytes : 0);
-    if (nbuf == 2) {
-      const long long nb = blk + gridDim.x;
-      if (nb < nblocks) mix_issue(cs, msmem + ((it + 1) & 1) * buf_bytes, nb, total_units);
-      asm volatile("cp.async.commit_group;\ncp.async.wait_group 1;" ::: "memory");
-    } else {
-      asm volatile("cp.async.wait_group 0;" ::: "memory");
+  if (tid == 0) {
+    for (int s = 0; s < kMixStages; ++s) mbar_init(smem_u32(&bars[s]), 1);
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (tid < cs.K) pk_s[tid] = __ldg(probs + tid);
+  __syncthreads();
+  if (tid == 0) {
+    for (int s = 0; s < kMixStages; ++s) {
+      const long long b = blockIdx.x + static_cast<long long>(s) * gridDim.x;
+      if (b < nblocks) mix_issue(cs, msmem + s * stage_bytes, smem_u32(&bars[s]), b, total_units);
     }
-    __syncthreads();
-
+  }
+  bool fmt_ok = true;
+  int it = 0;
+  for (long long blk = blockIdx.x; blk < nblocks; blk += gridDim.x, ++it) {
+    const int st = it % kMixStages;
+    const uint32_t parity = static_cast<uint32_t>((it / kMixStages) & 1);
+    const bool ok = mbar_wait(smem_u32(&bars[st]), parity, &abort_flag);
+    if (!__syncthreads_and(ok)) {
+      if (tid == 0) report_error(err, kDevWaitTimeout, 20);
+      break;
+    }
+    const uint8_t* buf = msmem + st * stage_bytes;
     const long long u0 = blk * kMixUnits;
     const int nunits = static_cast<int>(min(static_cast<long long>(kMixUnits), total_units - u0));
-    // per-candidate unit addressing for this block, computed once
-    if (tid == 0) {
+    if (lu < nunits) {
+      float2 acc[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) acc[j] = make_float2(0.f, 0.f);
+      float cst[2] = {0.f, 0.f};
       int off = 0;
       for (int k = 0; k < cs.K; ++k) {
         const int ub = cs.ubytes[k];
-        const int delta = static_cast<int>((reinterpret_cast<uintptr_t>(cs.ptr[k]) + static_cast<uintptr_t>(u0) * ub) & 15u);
-        MixCand m;
-        m.fmt = cs.fmt[k];
-        m.p = __ldg(probs + k);
-        m.raw = off + delta;
-        m.ub = ub;
-        off += mix_raw_bytes(ub);
-        if (mix_realign(cs, k)) {
-          m.slot = off;
-          m.stride = 4 * ((ub + 3) >> 2);
-          off += kMixUnits * m.stride;
-        } else {
-          m.slot = m.raw;
-          m.stride = ub;
+        const int rel = static_cast<int>((reinterpret_cast<uintptr_t>(cs.ptr[k]) +
+                                          static_cast<uintptr_t>(u0) * ub) & 15u) + lu * ub;
+        const URef u{reinterpret_cast<const uint32_t*>(buf + off + (rel & ~3)), rel & 3,
+                     8u * static_cast<uint32_t>(rel & 3)};
+        const float pk = pk_s[k];
+        switch (cs.fmt[k]) {
+          case kQ8_0: mix_chunk<kQ8_0>(u, c, pk, acc, cst); break;
+          case kQ2_K: mix_chunk<kQ2_K>(u, c, pk, acc, cst); break;
+          case kQ3_K: mix_chunk<kQ3_K>(u, c, pk, acc, cst); break;
+          case kQ4_K: mix_chunk<kQ4_K>(u, c, pk, acc, cst); break;
+          case kQ5_K: mix_chunk<kQ5_K>(u, c, pk, acc, cst); break;
+          case kQ6_K: mix_chunk<kQ6_K>(u, c, pk, acc, cst); break;
+          case kIQ4_XS: mix_chunk<kIQ4_XS>(u, c, pk, acc, cst); break;
+          default: fmt_ok = false;
         }
-        meta[k] = m;
+        off += mix_region_bytes(ub);
       }
-    }
-    __syncthreads();
-    // word-align the units of candidates that need it (8 threads per unit)
-    bool any = false;
-    for (int k = 0; k < cs.K; ++k) {
-      const MixCand m = meta[k];
-      if (m.slot == m.raw) continue;
-      any = true;
-      if (lu < nunits) {
-        const int uw = m.stride >> 2;
-        const uint32_t* raw = reinterpret_cast<const uint32_t*>(buf + (m.raw & ~15));
-        uint32_t* dst = reinterpret_cast<uint32_t*>(buf + m.slot) + lu * uw;
-        const int b0 = (m.raw & 15) + lu * m.ub;
-        const uint32_t sh = static_cast<uint32_t>(b0 & 3) * 8u;
-        for (int w = c; w < uw; w += 8) {
-          const int i = (b0 >> 2) + w;
-          dst[w] = __funnelshift_r(raw[i], raw[i + 1], sh);
-        }
-      }
-    }
-    if (any) __syncthreads();
-
-    if (lu < nunits) {
-      uint64_t acc2[16];
-#pragma unroll
-      for (int j = 0; j < 16; ++j) acc2[j] = 0ull;
-      float cst[2] = {0.f, 0.f};
-      for (int k = 0; k < cs.K; ++k) {
-        const MixCand m = meta[k];
-        const uint32_t* slot = reinterpret_cast<const uint32_t*>(buf + m.slot + lu * m.stride);
-        switch (m.fmt) {
-          case kQ8_0: mix_chunk<kQ8_0>(slot, c, m.p, acc2, cst); break;
-          case kQ2_K: mix_chunk<kQ2_K>(slot, c, m.p, acc2, cst); break;
-          case kQ3_K: mix_chunk<kQ3_K>(slot, c, m.p, acc2, cst); break;
-          case kQ4_K: mix_chunk<kQ4_K>(slot, c, m.p, acc2, cst); break;
-          case kQ5_K: mix_chunk<kQ5_K>(slot, c, m.p, acc2, cst); break;
-          case kQ6_K: mix_chunk<kQ6_K>(slot, c, m.p, acc2, cst); break;
-          case kIQ4_XS: mix_chunk<kIQ4_XS>(slot, c, m.p, acc2, cst); break;
-          default: ok = false;
-        }
-      }
-      float acc[32];
-#pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const float2 v = f2unpack(acc2[j]);
-        acc[2 * j] = v.x;
-        acc[2 * j + 1] = v.y;
-      }
-      const long long u = u0 + lu;
-      const long long row = u / units_per_row;
-      const int col = static_cast<int>(u - row * units_per_row) * 256 + 32 * c;
+      const long long uu = u0 + lu;
+      const long long row = uu / units_per_row;
+      const int col = static_cast<int>(uu - row * units_per_row) * 256 + 32 * c;
       __nv_bfloat16* dst = out + row * ld_out + col;
       if (col + 32 <= cols && ((reinterpret_cast<uintptr_t>(dst) & 15u) == 0)) {
 #pragma unroll
         for (int v = 0; v < 4; ++v) {
-          __align__(16) __nv_bfloat162 h[4];
+          __align__(16) __nv_bfloat162 hv[4];
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
-            const int e = 8 * v + 2 * j;
-            h[j] = __floats2bfloat162_rn(acc[e] + cst[e >> 4], acc[e + 1] + cst[(e + 1) >> 4]);
+            const float2 e = acc[4 * v + j];
+            const float cs0 = cst[(8 * v + 2 * j) >> 4];
+            hv[j] = __floats2bfloat162_rn(e.x + cs0, e.y + cs0);
           }
-          reinterpret_cast<uint4*>(dst)[v] = *reinterpret_cast<const uint4*>(h);
+          reinterpret_cast<uint4*>(dst)[v] = *reinterpret_cast<const uint4*>(hv);
         }
       } else {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const long long cc = col + j;
-          if (cc < ld_out) dst[j] = __float2bfloat16_rn(cc < cols ? acc[j] + cst[j >> 4] : 0.f);
+        for (int j = 0; j < 16; ++j) {
+          const long long c0 = col + 2 * j;
+          const float cs0 = cst[(2 * j) >> 4];
+          if (c0 < ld_out) dst[2 * j] = __float2bfloat16_rn(c0 < cols ? acc[j].x + cs0 : 0.f);
+          if (c0 + 1 < ld_out) dst[2 * j + 1] = __float2bfloat16_rn(c0 + 1 < cols ? acc[j].y + cs0 : 0.f);
         }
       }
     }
-    __syncthreads();  // this buffer is refilled two blocks from now (one, single-buffered)
-    if (nbuf != 2) {
-      const long long nb = blk + gridDim.x;
-      if (nb < nblocks) mix_issue(cs, msmem, nb, total_units);
-      asm volatile("cp.async.commit_group;" ::: "memory");
+    __syncthreads();  // every thread is done with this stage: refill it
+    if (tid == 0) {
+      const long long nb = blk + static_cast<long long>(kMixStages) * gridDim.x;
+      if (nb < nblocks) mix_issue(cs, msmem + st * stage_bytes, smem_u32(&bars[st]), nb, total_units);
     }
   }
-  asm volatile("cp.async.wait_group 0;" ::: "memory");
-  if (!ok) report_error(err, kDevBadFormat, 1);
+  if (!fmt_ok) report_error(err, kDevBadFormat, 1);
 }
 
 }  // namespace vq

@@ -355,18 +355,20 @@ int vq_mix(int K, const int* types, const void* const* blocks, const float* prob
   if (cols > 0x7fffffffLL) return fail(VQ_ERR_INVALID, "too many columns");
   const long long units = static_cast<long long>(rows) * (padded_cols / 256);
   const long long nblocks = (units + vq::kMixUnits - 1) / vq::kMixUnits;
-  // One block of kMixUnits units per CTA, single-buffered: four resident
-  // CTAs per SM hide the copies better than persistent double-buffered CTAs
-  // at half the occupancy (measured on B200 for K = 1, 5 and 6).
-  const int buf = (vq::mix_smem_bytes(cs) + 15) & ~15;
-  const int nbuf = 1;
-  const int smem = buf;
-  const long long grid = nblocks;
-  if (grid > 0x7fffffffLL) return fail(VQ_ERR_INVALID, "tensor too large");
+  // Persistent CTAs, as many per SM as fit, each walking blocks of
+  // kMixUnits units with kMixStages bulk-copy stages in flight.
+  const int stage = vq::mix_stage_bytes(cs);
+  const int smem = vq::kMixStages * stage;
   if (smem > 48 * 1024) VQ_CUDA(cudaFuncSetAttribute(vq::mix_units_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  int per_sm = 0;
+  VQ_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, vq::mix_units_kernel, vq::kDecodeThreads, smem));
+  if (per_sm < 1) return fail(VQ_ERR_INVALID, "mixture of %d candidates does not fit one SM", K);
+  int sms = 0;
+  if (int rc = sm_count(&sms)) return rc;
+  const long long grid = std::min<long long>(nblocks, static_cast<long long>(sms) * per_sm);
   vq::mix_units_kernel<<<static_cast<unsigned>(grid), vq::kDecodeThreads, smem, static_cast<cudaStream_t>(stream)>>>(
       cs, probs, units, static_cast<int>(padded_cols / 256), static_cast<int>(cols),
-      static_cast<__nv_bfloat16*>(w_bf16), ldw, buf, nbuf, err);
+      static_cast<__nv_bfloat16*>(w_bf16), ldw, stage, err);
   VQ_CUDA(cudaGetLastError());
   return 0;
 }

@@ -218,10 +218,39 @@ def _attention_forward(self, hidden_states: torch.Tensor, position_embeddings=No
     return self.o_proj(o), None
 
 
+def _sp_decoder(self, h: torch.Tensor, position_embeddings, shape) -> torch.Tensor:
+    """One decoder layer under sequence parallelism: ``h`` is this rank's
+    [tokens / N, hidden] shard of the residual stream (tokens of the
+    flattened [B, S] batch, ranks in order).  The RMSNorms and residual adds
+    run on the shard; each block all-gathers its normalised input, runs its
+    column-parallel projections, attention (whole sequences, this rank's
+    heads) or SwiGLU, and its row-parallel projection on all tokens, and
+    reduce-scatters the partial output back to the shard."""
+    from voodoo_quant.parallel import sp_gather, sp_scatter
+
+    B, S = shape
+    norm = self.post_attention_layernorm
+    x = self.input_layernorm(h)
+    a, _ = self.self_attn(hidden_states=sp_gather(x).view(B, S, -1), position_embeddings=position_embeddings,
+                          attention_mask=None)
+    a = sp_scatter(a.reshape(B * S, -1))
+    if _fusable(a) and getattr(norm, "weight", None) is not None and norm.weight.dtype == torch.bfloat16 \
+            and hasattr(norm, "variance_epsilon") and a.shape[-1] <= 8192:
+        h, x = add_rms_norm(a, h, norm.weight, norm.variance_epsilon)
+    else:
+        h = h + a
+        x = norm(h)
+    m = self.mlp(sp_gather(x).view(B, S, -1))
+    return h + sp_scatter(m.reshape(B * S, -1))
+
+
 def _decoder_forward(self, hidden_states: torch.Tensor, attention_mask=None, position_ids=None,
-                     past_key_values=None, use_cache=False, position_embeddings=None, **kwargs):
+                     past_key_values=None, use_cache=False, position_embeddings=None, sp_shape=None, **kwargs):
     """Hugging Face LlamaDecoderLayer.forward with the residual add after the
-    attention fused into the post-attention RMSNorm."""
+    attention fused into the post-attention RMSNorm (``sp_shape`` = (B, S):
+    the sequence-parallel layer, ``_sp_decoder``)."""
+    if sp_shape is not None:
+        return _sp_decoder(self, hidden_states, position_embeddings, sp_shape)
     norm = self.post_attention_layernorm
     if not (_fusable(hidden_states) and getattr(norm, "weight", None) is not None
             and norm.weight.dtype == torch.bfloat16 and hasattr(norm, "variance_epsilon")
@@ -265,4 +294,57 @@ def fuse_llama_blocks(model: torch.nn.Module, causal_batches: bool = False) -> i
                 n += 1
         if type(m) is L.LlamaAttention and causal_batches:
             m._vq_causal_batches = True
+    return n
+
+
+def _sp_model_forward(self, input_ids=None, attention_mask=None, position_ids=None, past_key_values=None,
+                      inputs_embeds=None, use_cache=None, **kwargs):
+    """Hugging Face LlamaModel.forward for the distillation step under
+    sequence parallelism: the vocabulary-parallel embedding's partial sums are
+    reduce-scattered into token shards, the decoder layers run on the shards
+    (``_sp_decoder``), the final RMSNorm on the shard, and the normalised
+    hidden states of all tokens are all-gathered for the vocabulary-parallel
+    head.  Causal, unpadded, cache-free batches only."""
+    from transformers.modeling_outputs import BaseModelOutputWithPast
+
+    from voodoo_quant.parallel import sp_enabled, sp_gather, sp_scatter
+
+    if not sp_enabled():
+        return self._vq_sp_orig_forward(input_ids=input_ids, attention_mask=attention_mask,
+                                        position_ids=position_ids, past_key_values=past_key_values,
+                                        inputs_embeds=inputs_embeds, use_cache=use_cache, **kwargs)
+    if input_ids is None or inputs_embeds is not None or past_key_values is not None or use_cache or \
+            attention_mask is not None:
+        raise ValueError("sequence parallelism runs whole causal batches from input_ids only "
+                         "(no attention mask, cache or inputs_embeds)")
+    e = self.embed_tokens(input_ids)
+    B, S, H = e.shape
+    h = sp_scatter(e.reshape(B * S, H))
+    pos = torch.arange(S, device=e.device).unsqueeze(0) if position_ids is None else position_ids
+    pe = self.rotary_emb(e, position_ids=pos)
+    for layer in self.layers[: self.config.num_hidden_layers]:
+        h = layer(h, position_embeddings=pe, sp_shape=(B, S))
+    h = self.norm(h)
+    return BaseModelOutputWithPast(last_hidden_state=sp_gather(h).view(B, S, H))
+
+
+def use_sequence_parallel(model: torch.nn.Module) -> int:
+    """Let a tensor-parallel Hugging Face Llama model run sequence parallel
+    while ``parallel.enable_sequence_parallel`` is on: its LlamaModel forward
+    becomes ``_sp_model_forward`` and every decoder layer's forward
+    ``_decoder_forward`` (the layers of ``fuse_llama_blocks``, also where the
+    fused kernels do not apply).  Idempotent; returns the number of modules
+    patched."""
+    from transformers.models.llama import modeling_llama as L
+
+    n = 0
+    for m in model.modules():
+        if type(m) is L.LlamaModel and not hasattr(m, "_vq_sp_orig_forward"):
+            m._vq_sp_orig_forward = m.forward
+            m.forward = types.MethodType(_sp_model_forward, m)
+            n += 1
+        elif type(m) is L.LlamaDecoderLayer and not hasattr(m, "_vq_orig_forward"):
+            m._vq_orig_forward = m.forward
+            m.forward = types.MethodType(_decoder_forward, m)
+            n += 1
     return n

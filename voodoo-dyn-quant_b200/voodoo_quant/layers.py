@@ -386,7 +386,8 @@ def _gated_linear_backward(ctx, dy: torch.Tensor):
     pending = []
     if ctx.needs_input_grad[0]:
         w_mix = ctx.w_mix if ctx.w_mix is not None else layer._mix(probs)
-        if layer.reduce_input_grad:
+        from voodoo_quant.parallel import sp_enabled
+        if layer.reduce_input_grad and not sp_enabled():
             # column-parallel layer with a private input: sum the partial
             # dX over the TP ranks (chunk by chunk) while the rest of dX and
             # the gate-gradient GEMM run
@@ -902,10 +903,13 @@ class MixedQuantLinear(_MixedQuantBase):
             n = x.numel() // x.shape[-1]
             bank = self.__dict__.get("_bank_ref")
             routing = bank.routing(self, n) if bank is not None else _sample_token_routing(probs, n)
-            # row-parallel: the partial outputs are summed over the TP ranks in place
-            reduce_out = spec is not None and spec.col_offset is not None
+            # row-parallel: the partial outputs are summed over the TP ranks in
+            # place (sequence parallelism: by the block's reduce-scatter)
+            from voodoo_quant.parallel import sp_enabled
+            reduce_out = spec is not None and spec.col_offset is not None and not sp_enabled()
             return _RoutedGatedLinearFunction.apply(x, probs, self, routing, reduce_out)
-        if spec is not None and spec.col_offset is not None:
+        from voodoo_quant.parallel import sp_enabled
+        if spec is not None and spec.col_offset is not None and not sp_enabled():
             from voodoo_quant.parallel import multicast_reducer, nccl_row_reducer
             # the output sum over the TP ranks happens inside the forward (in
             # the GEMM epilogue with NVLink multicast, else an in-place NCCL
@@ -967,7 +971,7 @@ class MixedQuantEmbedding(_MixedQuantBase):
     def forward(self, input: torch.Tensor) -> torch.Tensor:
         spec = self.shard_spec
         if spec is not None and spec.vocab_start is not None:
-            from voodoo_quant.parallel import tp_all_reduce_sum_
+            from voodoo_quant.parallel import sp_enabled, tp_all_reduce_sum_
             v0, v1 = self.tp_vocab_start, self.tp_vocab_end
             ids = input.to(self._cand_arena.device)
             in_shard = (ids >= v0) & (ids < v1)
@@ -976,14 +980,14 @@ class MixedQuantEmbedding(_MixedQuantBase):
                 # gradient is then zero, so the gate dots are this shard's alone
                 local = (ids - v0).clamp(0, self.num_embeddings - 1)
                 emb = self._embedding_lookup(local) * in_shard.unsqueeze(-1).to(self.source_dtype)
-                return tp_all_reduce_sum_(emb)
+                return emb if sp_enabled() else tp_all_reduce_sum_(emb)
             # Only this shard's tokens are looked up: clamping the others to
             # one row would funnel most of the batch's gradient into a single
             # index of the lookup's backward.
             emb_in = self._embedding_lookup(ids[in_shard] - v0)
             emb = emb_in.new_zeros(*ids.shape, self.embedding_dim)
             emb[in_shard] = emb_in
-            return tp_all_reduce_sum_(emb)
+            return emb if sp_enabled() else tp_all_reduce_sum_(emb)
         return self._embedding_lookup(input)
 
 

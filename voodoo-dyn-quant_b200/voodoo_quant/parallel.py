@@ -69,6 +69,11 @@ class _TPState:
     teacher_group = None
     # the communicator forward collectives use inside collectives_on(); None = group
     forward_override = None
+    # sequence parallelism (enable_sequence_parallel): between the blocks the
+    # hidden state is a [tokens / N, hidden] shard of consecutive tokens;
+    # all-gather before the column-parallel inputs, reduce-scatter after the
+    # row-parallel outputs (instead of all-reducing replicated activations)
+    sequence_parallel = False
 
 
 TP = _TPState()
@@ -170,6 +175,7 @@ def reset_tp() -> None:
     TP.overlap_sms = 0
     TP.teacher_group = None
     TP.forward_override = None
+    TP.sequence_parallel = False
 
 
 def teacher_subgroups(t: int):
@@ -258,6 +264,95 @@ def enable_input_grad_overlap(sms: int) -> bool:
         TP.overlap_group = dist.new_group(ranks=ranks, backend=dist.get_backend(TP.group))
     TP.overlap_sms = int(sms)
     return True
+
+
+def sp_enabled() -> bool:
+    """Whether the TP hidden states between blocks are token shards."""
+    return TP.enabled and TP.sequence_parallel
+
+
+def enable_sequence_parallel(enable: bool = True) -> bool:
+    """Sequence parallelism for the models that ``use_sequence_parallel``
+    patched (voodoo_quant.fused_blocks): the residual stream, the RMSNorms
+    and the residual adds then run on each rank's [tokens / N, hidden] shard;
+    each attention / MLP block all-gathers its normalised input and
+    reduce-scatters its row-parallel output, which moves the same bytes as
+    the all-reduce it replaces.  Row-parallel layers and vocabulary-parallel
+    embeddings then return their partial sums.  Returns whether it is on."""
+    TP.sequence_parallel = bool(enable) and TP.enabled
+    return TP.sequence_parallel
+
+
+def _group_size(group) -> int:
+    return dist.get_world_size(group) if group is not None else TP.world_size
+
+
+class _SPGather(Function):
+    """Token shard [n, H] -> all tokens [N n, H] (rank order) over the forward
+    group; backward: reduce-scatter of the gradient, beside which the gate-
+    gradient GEMMs deferred by the block it feeds run (on the overlap
+    communicator, as for the f operator's all-reduce)."""
+
+    @staticmethod
+    def forward(ctx, x: torch.Tensor) -> torch.Tensor:
+        group = _fwd_group()
+        W = _group_size(group)
+        ctx.group = group
+        x = x.contiguous()
+        out = torch.empty((W * x.shape[0],) + tuple(x.shape[1:]), dtype=x.dtype, device=x.device)
+        dist.all_gather_into_tensor(out, x, group=group)
+        return out
+
+    @staticmethod
+    def backward(ctx, g):
+        from voodoo_quant import layers
+
+        g = g.contiguous()
+        W = _group_size(ctx.group)
+        out = torch.empty((g.shape[0] // W,) + tuple(g.shape[1:]), dtype=g.dtype, device=g.device)
+        if layers.has_deferred_gategrads() and ctx.group is TP.group:
+            grp = TP.overlap_group if TP.overlap_group is not None else TP.group
+            work = dist.reduce_scatter_tensor(out, g, group=grp, async_op=True)
+            layers.flush_deferred_gategrads(overlap_bytes=g.numel() * g.element_size())
+            work.wait()
+        else:
+            dist.reduce_scatter_tensor(out, g, group=ctx.group)
+        return out
+
+
+class _SPScatter(Function):
+    """Partial sums [N n, H] -> this rank's [n, H] token shard of their sum over
+    the forward group (reduce-scatter); backward: all-gather."""
+
+    @staticmethod
+    def forward(ctx, x: torch.Tensor) -> torch.Tensor:
+        group = _fwd_group()
+        W = _group_size(group)
+        ctx.group = group
+        x = x.contiguous()
+        if x.shape[0] % W:
+            raise ValueError(f"sequence parallelism: {x.shape[0]} tokens do not split over {W} ranks")
+        out = torch.empty((x.shape[0] // W,) + tuple(x.shape[1:]), dtype=x.dtype, device=x.device)
+        dist.reduce_scatter_tensor(out, x, group=group)
+        return out
+
+    @staticmethod
+    def backward(ctx, g):
+        g = g.contiguous()
+        W = _group_size(ctx.group)
+        out = torch.empty((W * g.shape[0],) + tuple(g.shape[1:]), dtype=g.dtype, device=g.device)
+        dist.all_gather_into_tensor(out, g, group=ctx.group)
+        return out
+
+
+def sp_gather(x: torch.Tensor) -> torch.Tensor:
+    """All tokens [N n, H] from the token shards [n, H] (sequence parallelism)."""
+    return _SPGather.apply(x)
+
+
+def sp_scatter(x: torch.Tensor) -> torch.Tensor:
+    """This rank's token shard of the sum over the ranks of x [N n, H]."""
+    return _SPScatter.apply(x)
 
 
 def mark_deferred_gategrads(model: nn.Module) -> int:
@@ -392,8 +487,8 @@ def nccl_row_reducer():
 
 
 def tp_copy_to_parallel(t: torch.Tensor) -> torch.Tensor:
-    if not TP.enabled or not TP.exact_input_grad:
-        return t
+    if not TP.enabled or not TP.exact_input_grad or TP.sequence_parallel:
+        return t  # (under sequence parallelism the block's input all-gather sums it in backward)
     return _CopyToParallel.apply(t)
 
 
@@ -707,7 +802,8 @@ class RowParallelLinear(nn.Linear):
         self.tp_full_weight = full_weight
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        return tp_all_reduce_sum(F.linear(x.to(self.weight.device), self.weight))
+        y = F.linear(x.to(self.weight.device), self.weight)
+        return y if sp_enabled() else tp_all_reduce_sum(y)
 
 
 class VocabParallelEmbedding(nn.Embedding):
@@ -727,7 +823,7 @@ class VocabParallelEmbedding(nn.Embedding):
         mask = (input < v0) | (input >= v1)
         out = F.embedding((input - v0).clamp(0, self.num_embeddings - 1), self.weight)
         out = out * (~mask).unsqueeze(-1).to(out.dtype)
-        return tp_all_reduce_sum(out)
+        return out if sp_enabled() else tp_all_reduce_sum(out)
 
 
 _PARALLEL_TYPES = (ColumnParallelLinear, RowParallelLinear, VocabParallelEmbedding)

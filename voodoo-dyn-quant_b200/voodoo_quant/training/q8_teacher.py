@@ -169,7 +169,9 @@ class _RowParallelQ8(nn.Module):
 
     @torch.no_grad()
     def forward(self, x):
-        from voodoo_quant.parallel import multicast_reducer, tp_all_reduce_sum_
+        from voodoo_quant.parallel import multicast_reducer, sp_enabled, tp_all_reduce_sum_
+        if sp_enabled():  # partial sums: the block reduce-scatters them
+            return self.inner(x)
         red = multicast_reducer()
         if red is not None and x.is_cuda:  # partial outputs summed over the TP ranks inside the GEMM
             x2 = _C._as_operand(x.reshape(-1, self.in_features))
@@ -185,8 +187,8 @@ class _VocabParallelQ8(nn.Module):
         self.vocab_start, self.rows = vocab_start, rows
 
     def forward(self, ids):
-        from voodoo_quant.parallel import tp_all_reduce_sum_
+        from voodoo_quant.parallel import sp_enabled, tp_all_reduce_sum_
         mask = (ids < self.vocab_start) | (ids >= self.vocab_start + self.rows)
         out = self.inner((ids - self.vocab_start).clamp(0, self.rows - 1))
         out = out * (~mask).unsqueeze(-1).to(out.dtype)
-        return tp_all_reduce_sum_(out)
+        return out if sp_enabled() else tp_all_reduce_sum_(out)

@@ -101,6 +101,11 @@ class StepArgs:
     # logits; each teacher all-reduce then moves 1 / (world / t) of the
     # tokens among t ranks.  Plain loss path only (logits_chunk = 0).
     teacher_tp: int = 0
+    # under TP: sequence parallelism (parallel.enable_sequence_parallel) --
+    # the residual stream, RMSNorms and residual adds on token shards, an
+    # all-gather before and a reduce-scatter after every block instead of
+    # the all-reduces of replicated activations
+    sequence_parallel: bool = False
 
 
 class GatedDistillTrainer:
@@ -455,6 +460,18 @@ def build_distill(shape_name: str, device, seed: int = 0, args: StepArgs | None 
 
         fuse_llama_blocks(base, causal_batches=True)
         fuse_llama_blocks(teacher, causal_batches=True)
+    if tp and TP.enabled:
+        from voodoo_quant.parallel import enable_sequence_parallel
+
+        sp = args is not None and args.sequence_parallel
+        if sp:
+            from voodoo_quant.fused_blocks import use_sequence_parallel
+
+            if multicast:
+                raise ValueError("sequence parallelism reduce-scatters the row-parallel outputs: multicast must be off")
+            use_sequence_parallel(base)
+            use_sequence_parallel(teacher)
+        enable_sequence_parallel(sp)
     if tp and TP.enabled:
         from voodoo_quant.parallel import enable_multicast_reduce, enable_teacher_overlap
 
