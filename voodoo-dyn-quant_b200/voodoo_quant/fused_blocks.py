@@ -203,9 +203,13 @@ def _attention_forward(self, hidden_states: torch.Tensor, position_embeddings=No
     qkv = _group_projection((self.q_proj, self.k_proj, self.v_proj), hidden_states)
     if qkv is not None:  # one GEMM; q, k, v are column ranges of its output
         nq, nk = self.q_proj.out_features, self.k_proj.out_features
-        q = qkv[..., :nq].view(B, S, -1, self.head_dim)
-        k = qkv[..., nq:nq + nk].view(B, S, -1, self.head_dim)
-        v = qkv[..., nq + nk:].view(B, S, -1, self.head_dim)
+        # split, not three slices: its backward concatenates the three
+        # gradients in one pass (a slice's backward zero-fills a full-size
+        # gradient per slice and autograd adds the three)
+        q, k, v = qkv.split([nq, nk, qkv.shape[-1] - nq - nk], dim=-1)
+        q = q.view(B, S, -1, self.head_dim)
+        k = k.view(B, S, -1, self.head_dim)
+        v = v.view(B, S, -1, self.head_dim)
     else:
         q = self.q_proj(hidden_states).view(B, S, -1, self.head_dim)
         k = self.k_proj(hidden_states).view(B, S, -1, self.head_dim)

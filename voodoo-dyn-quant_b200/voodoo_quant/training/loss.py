@@ -42,13 +42,22 @@ def _weights(targets: torch.Tensor, n: int, distill_weight: float, ce_reduction:
     return ce_w, distill_weight / max(n, 1)
 
 
+def _scaled(g: torch.Tensor, g_loss: torch.Tensor, unit: bool) -> torch.Tensor:
+    """The stored logits gradient times the loss's upstream gradient; with
+    ``unit`` the caller seeds the loss with 1 (``loss.backward()`` on a sum
+    in which the loss has coefficient 1), so the [tokens, V] gradient is
+    returned as it is instead of being multiplied by 1 in another pass."""
+    return g if unit else g * g_loss.to(g.dtype)
+
+
 class _FusedDistillLoss(Function):
     @staticmethod
     def forward(ctx, s: torch.Tensor, t: torch.Tensor, y: torch.Tensor, temperature: float, ce_w: float,
-                kl_w: float):
+                kl_w: float, unit_upstream: bool = False):
         need = s.requires_grad
         ce, kl, g = _C.loss_fused(s, t, y, temperature, ce_w, kl_w, want_grad=need)
         ctx.g = g
+        ctx.unit = unit_upstream
         ctx.s_dtype = s.dtype
         ce_sum, kl_sum = ce.sum(), kl.sum()
         ctx.mark_non_differentiable(ce_sum, kl_sum)
@@ -59,17 +68,19 @@ class _FusedDistillLoss(Function):
         g = ctx.g
         ctx.g = None
         if g is None:
-            return None, None, None, None, None, None
-        return (g * g_loss.to(g.dtype)).to(ctx.s_dtype), None, None, None, None, None
+            return None, None, None, None, None, None, None
+        return _scaled(g, g_loss, ctx.unit).to(ctx.s_dtype), None, None, None, None, None, None
 
 
 def distillation_loss(student_logits: torch.Tensor, teacher_logits: torch.Tensor, targets: torch.Tensor,
-                      temperature: float = 1.0, distill_weight: float = 1.0, ce_reduction: str = "valid"):
+                      temperature: float = 1.0, distill_weight: float = 1.0, ce_reduction: str = "valid",
+                      unit_upstream: bool = False):
     """Returns (loss, lm_loss, distill_loss) like the reference's plain path.
 
     ``loss = lm_loss + distill_weight * distill_loss`` is differentiable with
     respect to ``student_logits`` ([..., V]); lm_loss / distill_loss are
-    detached scalars (mean CE, mean per-token T^2 * KL).
+    detached scalars (mean CE, mean per-token T^2 * KL).  ``unit_upstream``:
+    the caller back-propagates with gradient 1 into ``loss`` (see ``_scaled``).
     """
     V = student_logits.shape[-1]
     s = student_logits.reshape(-1, V)
@@ -77,13 +88,13 @@ def distillation_loss(student_logits: torch.Tensor, teacher_logits: torch.Tensor
     y = targets.reshape(-1)
     n = s.shape[0]
     ce_w, kl_w = _weights(y, n, distill_weight, ce_reduction)
-    loss, ce_sum, kl_sum = _FusedDistillLoss.apply(s, t, y, float(temperature), ce_w, kl_w)
+    loss, ce_sum, kl_sum = _FusedDistillLoss.apply(s, t, y, float(temperature), ce_w, kl_w, bool(unit_upstream))
     return loss, (ce_sum * ce_w).detach(), (kl_sum / max(n, 1)).detach()
 
 
 class _TPFusedDistillLoss(Function):
     @staticmethod
-    def forward(ctx, s, t, y, vocab_start, temperature, ce_w, kl_w, group):
+    def forward(ctx, s, t, y, vocab_start, temperature, ce_w, kl_w, group, unit_upstream=False):
         stats = _C.loss_stats(s, t, y, vocab_start, temperature)            # [rows, 8]
         world = dist.get_world_size(group)
         # [world * rows, 8], viewed per rank: gloo wants the ranks stacked along dim 0
@@ -93,6 +104,7 @@ class _TPFusedDistillLoss(Function):
         gathered = gathered.view((world,) + tuple(stats.shape))
         lse, ce, kl = _C.loss_combine(gathered, temperature)
         ctx.g = _C.loss_grad(s, t, y, vocab_start, temperature, lse, ce_w, kl_w) if s.requires_grad else None
+        ctx.unit = unit_upstream
         ctx.s_dtype = s.dtype
         ce_sum, kl_sum = ce.sum(), kl.sum()
         ctx.mark_non_differentiable(ce_sum, kl_sum)
@@ -103,13 +115,13 @@ class _TPFusedDistillLoss(Function):
         g = ctx.g
         ctx.g = None
         if g is None:
-            return (None,) * 8
-        return (g * g_loss.to(g.dtype)).to(ctx.s_dtype), None, None, None, None, None, None, None
+            return (None,) * 9
+        return _scaled(g, g_loss, ctx.unit).to(ctx.s_dtype), None, None, None, None, None, None, None, None
 
 
 def tp_distillation_loss(student_shard: torch.Tensor, teacher_shard: torch.Tensor, targets: torch.Tensor,
                          vocab_start: int, temperature: float = 1.0, distill_weight: float = 1.0,
-                         ce_reduction: str = "tokens", group=None):
+                         ce_reduction: str = "tokens", group=None, unit_upstream: bool = False):
     """Vocabulary-parallel loss: every rank passes its [..., V/N] logits shard.
 
     The returned loss is the exact global loss on every rank; its gradient
@@ -122,7 +134,7 @@ def tp_distillation_loss(student_shard: torch.Tensor, teacher_shard: torch.Tenso
     n = s.shape[0]
     ce_w, kl_w = _weights(y, n, distill_weight, ce_reduction)
     loss, ce_sum, kl_sum = _TPFusedDistillLoss.apply(s, t, y, int(vocab_start), float(temperature), ce_w, kl_w,
-                                                     group)
+                                                     group, bool(unit_upstream))
     return loss, (ce_sum * ce_w).detach(), (kl_sum / max(n, 1)).detach()
 
 
@@ -167,10 +179,11 @@ def chunked_head_loss(student_head, teacher_head, hidden: torch.Tensor, t_hidden
         V = s_c.shape[-1]
         if vocab_start is not None:
             loss_c, ce_c, kl_c = _TPFusedDistillLoss.apply(s_c.reshape(-1, V), t_c.reshape(-1, V).detach(), y_c,
-                                                           int(vocab_start), float(temperature), ce_w, kl_w, group)
+                                                           int(vocab_start), float(temperature), ce_w, kl_w, group,
+                                                           True)
         else:
             loss_c, ce_c, kl_c = _FusedDistillLoss.apply(s_c.reshape(-1, V), t_c.reshape(-1, V).detach(), y_c,
-                                                         float(temperature), ce_w, kl_w)
+                                                         float(temperature), ce_w, kl_w, True)
         del t_c
         loss_c.backward()
         if h_c.grad is not None:

@@ -168,10 +168,10 @@ class GatedDistillTrainer:
                 t_logits = self._teacher_logits(x)
         if self.tp and v0 is not None:
             kd, lm, kl = tp_distillation_loss(logits, t_logits, y, v0, a.distill_temperature, a.distill_weight,
-                                              ce_reduction="tokens")
+                                              ce_reduction="tokens", unit_upstream=True)
         else:
             kd, lm, kl = distillation_loss(logits, t_logits, y, a.distill_temperature, a.distill_weight,
-                                           ce_reduction=a.ce_reduction)
+                                           ce_reduction=a.ce_reduction, unit_upstream=True)
         del t_logits
         current = self.bank.effective_bytes().to(logits.device)
         if self.tp:
