@@ -815,6 +815,23 @@ def step_flops_per_token(shape) -> float:
     return float(student + teacher + attn)
 
 
+def auto_teacher_tp(workload: str, world: int) -> int:
+    """The teacher's TP degree by default: the smallest t dividing the
+    world whose world / t groups each get a whole number of the batch's
+    sequences (each group runs the teacher on its slice, so fewer ranks
+    share each teacher all-reduce, or none at t = 1); 0 (the student's
+    degree) on one GPU or when none fits."""
+    if world <= 1 or workload not in WORKLOAD_NAMES:
+        return 0
+    from voodoo_quant.training import synthetic as S
+
+    batch = S.SHAPES[workload].batch
+    for t in range(1, world + 1):
+        if world % t == 0 and batch % (world // t) == 0:
+            return t if t < world else 0
+    return 0
+
+
 def run_model_step(args):
     """Full gated distillation step of a synthetic model config: student
     (every Linear and the embedding gated, K candidates) forward, Q8_0 teacher
@@ -887,9 +904,26 @@ def run_model_step(args):
     stream = torch.cuda.current_stream()
     torch.cuda.reset_peak_memory_stats(dev)
     step_fn = trainer.step
+    graph_note = "eager"
     if args.graph_step:  # forward + backward recorded once, replayed per step (optimizer eager)
-        trainer.capture(x, y, warmup=args.warmup)
-        step_fn = trainer.replay_step
+        ok, err = 1.0, ""
+        try:
+            trainer.capture(x, y, warmup=args.warmup)
+        except Exception as e:  # capture unsupported here: every rank falls back to the eager step
+            ok, err = 0.0, f"{type(e).__name__}: {str(e)[:120]}"
+            trainer.release_graph()
+            torch.cuda.synchronize()
+        flag = torch.tensor([ok], device=dev)
+        if world > 1:
+            dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+        if flag.item() == 1.0:
+            step_fn = trainer.replay_step
+            graph_note = "forward + backward replayed from one CUDA graph"
+        else:
+            trainer.release_graph()
+            graph_note = f"eager (graph capture failed: {err or 'on another rank'})"
+            if rank == 0:
+                print(f"[bench] {graph_note}", file=sys.stderr, flush=True)
     for _ in range(args.warmup):
         step_fn(x, y)
     torch.cuda.synchronize()
@@ -959,9 +993,9 @@ def run_model_step(args):
                     "row_parallel_reduce": "nvls multimem.red in GEMM" if multicast_on else "nccl all-reduce",
                     "forward": "ptqr (one candidate per token)" if args.ptqr else "candidate mixture",
                     "logits_chunk": args.logits_chunk, "peak_alloc_gb_rank0": round(peak_gb, 2),
-                    "step_graph": "forward + backward replayed from one CUDA graph" if args.graph_step
-                    else "eager",
+                    "step_graph": graph_note,
                     "teacher_tp": args.teacher_tp or world,
+                    "teacher_batch_slices": world // (args.teacher_tp or world),
                     "sequence_parallel": bool(args.sequence_parallel and world > 1),
                     "teacher": (f"own stream and communicator beside the student, "
                                 f"{args.teacher_stream_sms} SMs left to collectives") if args.teacher_stream
@@ -1078,18 +1112,20 @@ def main():
                     help="step workloads: head + loss per chunk of this many tokens (no [tokens, V] logits)")
     ap.add_argument("--multicast", action="store_true",
                     help="step workloads under TP: sum row-parallel outputs with multimem.red in the GEMM")
-    ap.add_argument("--graph-step", action="store_true",
+    ap.add_argument("--graph-step", action=argparse.BooleanOptionalAction, default=None,
                     help="step workloads: record forward + backward as one CUDA graph (static-shape mode, "
-                         "CE over all tokens) and replay it each step; the optimizer stays eager")
+                         "CE over all tokens) and replay it each step; the optimizer stays eager "
+                         "(default: on with more than one GPU)")
     ap.add_argument("--teacher-stream", action="store_true",
                     help="step workloads: the teacher's forward on a second stream beside the student's, its "
                          "TP all-reduces on a communicator of their own")
     ap.add_argument("--teacher-stream-sms", type=int, default=0,
                     help="with --teacher-stream: SMs the forward GEMMs leave to the other stream's all-reduces "
                          "(and the teacher communicator's CTA cap); 0 = none")
-    ap.add_argument("--teacher-tp", type=int, default=0,
+    ap.add_argument("--teacher-tp", type=int, default=-1,
                     help="step workloads under TP: the teacher's own TP degree t (groups of t ranks, each on "
-                         "its batch slice; one all-to-all of its logits); 0 = the student's")
+                         "its batch slice; one all-to-all of its logits); 0 = the student's; default: the "
+                         "smallest t whose groups split the batch evenly")
     ap.add_argument("--sequence-parallel", action=argparse.BooleanOptionalAction, default=False,
                     help="step workloads under TP: residual stream, norms and residual adds on token shards; "
                          "all-gather / reduce-scatter around each block instead of all-reduces")
@@ -1110,6 +1146,10 @@ def main():
         args.dx_chunks = 2 if world > 1 else 1
     if args.cpu_tokens < 0:
         args.cpu_tokens = 2048 if args.workload == "layer" else 256
+    if args.graph_step is None:
+        args.graph_step = world > 1 and args.workload != "layer" and args.logits_chunk <= 0 and not args.ptqr
+    if args.teacher_tp < 0:
+        args.teacher_tp = auto_teacher_tp(args.workload, world) if args.logits_chunk <= 0 else 0
     if args.ncu_case:
         run_ncu_case()
     elif args.impl == "reference":
