@@ -667,7 +667,7 @@ def step_cpu_baseline(shape, tokens: int = 256, repeats: int = 2) -> dict:
     full = s.full_step_s(w / repeats, t / repeats)
     return {"value": round(shape.batch * shape.seq / full, 4), "unit": "tokens/s", "cores": s.threads,
             "kind": "port", "sample_ms_per_step": round((w + t) / repeats * 1e3, 1),
-            "full_step_s_estimate": round(full, 1), "sample": s.describe()}
+            "full_step_s_estimate": float(f"{full:.4g}"), "sample": s.describe()}
 
 
 def run_reference(args):
@@ -717,7 +717,7 @@ def run_reference(args):
         v = round(shape.batch * shape.seq / full, 4)
         metric, cfg, ms = METRIC, step_config(args.workload, shape, world), dt * 1e3
         sample = s.describe()
-        extra = {"full_step_s_estimate": round(full, 1), "sample_tokens_per_step": args.cpu_tokens}
+        extra = {"full_step_s_estimate": float(f"{full:.4g}"), "sample_tokens_per_step": args.cpu_tokens}
     out = {
         "metric": metric, "value": v, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms, 2), "higher_is_better": True, "scaling": "strong",
