@@ -884,7 +884,7 @@ def run_model_step(args):
         workload = f"{args.workload}-{args.layers}l"
         S.SHAPES[workload] = dataclasses.replace(base, layers=args.layers)
     t_build = time.perf_counter()
-    trainer, shape = build_distill(workload, dev, seed=0, tp=world > 1, multicast=args.multicast,
+    trainer, shape = build_distill(workload, dev, seed=0, tp=world > 1,
                                    overlap_sms=args.overlap_sms if world > 1 else 0,
                                    args=StepArgs(max_steps=args.warmup + args.steps + args.e2e_steps + 3,
                                                  ptqr=args.ptqr, logits_chunk=args.logits_chunk,
@@ -894,9 +894,6 @@ def run_model_step(args):
                                                  teacher_stream_sms=args.teacher_stream_sms,
                                                  teacher_tp=args.teacher_tp,
                                                  sequence_parallel=args.sequence_parallel and world > 1))
-    from voodoo_quant import parallel as _par
-
-    multicast_on = _par.multicast_reducer() is not None
     torch.cuda.synchronize()
     t_build = time.perf_counter() - t_build
     x, y = S.random_tokens(shape, dev, seed=1)
@@ -990,7 +987,6 @@ def run_model_step(args):
             "config": cfg,
             "run": {"gated_tensors": len(trainer.replaced), "build_s": round(t_build, 1),
                     "input_grad_overlap_sms": args.overlap_sms if world > 1 else 0,
-                    "row_parallel_reduce": "nvls multimem.red in GEMM" if multicast_on else "nccl all-reduce",
                     "forward": "ptqr (one candidate per token)" if args.ptqr else "candidate mixture",
                     "logits_chunk": args.logits_chunk, "peak_alloc_gb_rank0": round(peak_gb, 2),
                     "step_graph": graph_note,
@@ -1019,7 +1015,6 @@ def run_model_step(args):
     trainer.release_graph()  # the graph holds collectives: drop it before the process group
     torch.cuda.synchronize()
     if world > 1:
-        _par.enable_multicast_reduce(False)  # every rank releases the multicast buffers together
         dist.barrier()
         dist.destroy_process_group()
 
@@ -1110,8 +1105,6 @@ def main():
                     help="step workloads: per-token quant routing forward (one candidate per token)")
     ap.add_argument("--logits-chunk", type=int, default=0,
                     help="step workloads: head + loss per chunk of this many tokens (no [tokens, V] logits)")
-    ap.add_argument("--multicast", action="store_true",
-                    help="step workloads under TP: sum row-parallel outputs with multimem.red in the GEMM")
     ap.add_argument("--graph-step", action=argparse.BooleanOptionalAction, default=None,
                     help="step workloads: record forward + backward as one CUDA graph (static-shape mode, "
                          "CE over all tokens) and replay it each step; the optimizer stays eager "

@@ -140,18 +140,6 @@ int vq_quantize(int ggml_type, const void* w, int w_dtype, int64_t rows, int64_t
 int vq_linear_fwd_grouped(const void* x, int64_t T, int64_t Kin, int64_t ldx, int G, const void* const* w,
                           int64_t N, int64_t ldw, const int* group_off, void* y, int64_t ldy, void* stream);
 
-/* K1 with the row-parallel all-reduce fused in: adds this rank's
- * Y = X W^T [T, N] (bf16) into `y_multicast`, an NVLink multicast (NVSwitch
- * SHARP) address of a buffer every TP rank holds, with multimem.red from the
- * GEMM epilogue, so the reduction travels over NVLink while the next tiles
- * are computed.  The caller zeroes every rank's buffer before any rank's
- * call and orders readers after every rank's call (one barrier); each rank's
- * buffer then holds the sum.  N and ldy multiples of 8, 16-byte aligned
- * address.  Replaces F.linear followed by _AllReduceSum.forward's NCCL
- * all-reduce for row-parallel Linears (voodoo_quant/parallel.py:140-167). */
-int vq_linear_fwd_mcred(const void* x, int64_t T, int64_t Kin, int64_t ldx, const void* w, int64_t N, int64_t ldw,
-                        void* y_multicast, int64_t ldy, void* stream);
-
 /* Largest scratch vq_gategrad_noalloc can use: 4 MiB, which covers every
  * unsharded layer up to a 152064 x 5120 vocabulary projection with 7
  * candidates (vq_gategrad_workspace_bytes gives the need of a shape). */

@@ -43,10 +43,6 @@ constexpr int GROUP_N = 8;            // raster: tiles sweep M inside a band of 
 
 constexpr int kEpiStoreBf16 = 0;
 constexpr int kEpiGateGrad = 1;
-// bf16 output tile added into a multicast (NVLink SHARP) address with
-// multimem.red: every rank's partial is summed in the switch and the sum
-// lands in each rank's copy of the buffer.
-constexpr int kEpiMultimemRed = 2;
 
 // Shared memory: STAGES x (A, B) operand slices, the mbarriers, and for the
 // gate-gradient epilogue one staging area per epilogue warp (32 rows x one
@@ -285,33 +281,6 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, uint8_t* stage, u
         }
       }
     }
-  } else if (kEpi == kEpiMultimemRed) {
-    for (int c = 0; c < BN / 32; ++c) {
-      float v[32];
-      tmem_ld_32cols(t_row + c * 32, v);
-      const long long col0 = static_cast<long long>(n_blk) * BN + c * 32;
-      if (row_ok && col0 < p.N) {
-        const uintptr_t dst = reinterpret_cast<uintptr_t>(p.C + row * p.ldc + col0);
-        uint32_t pk[16];
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
-          pk[j] = *reinterpret_cast<const uint32_t*>(&h);
-        }
-        if (col0 + 32 <= p.N) {  // base and ldc are 16-byte aligned (checked on the host)
-#pragma unroll
-          for (int j = 0; j < 4; ++j)
-            asm volatile("multimem.red.relaxed.sys.global.add.v4.bf16x2 [%0], {%1, %2, %3, %4};" ::"l"(dst + 16 * j),
-                         "r"(pk[4 * j]), "r"(pk[4 * j + 1]), "r"(pk[4 * j + 2]), "r"(pk[4 * j + 3])
-                         : "memory");
-        } else {  // N is a multiple of 8 (checked on the host): whole 16-byte groups
-          for (int j = 0; j < 4 && col0 + 8 * j < p.N; ++j)
-            asm volatile("multimem.red.relaxed.sys.global.add.v4.bf16x2 [%0], {%1, %2, %3, %4};" ::"l"(dst + 16 * j),
-                         "r"(pk[4 * j]), "r"(pk[4 * j + 1]), "r"(pk[4 * j + 2]), "r"(pk[4 * j + 3])
-                         : "memory");
-        }
-      }
-    }
   } else {
     // Gate-gradient epilogue.  For each candidate: each thread stages its own
     // row's unit (one 256-column unit) into its shared slot row with 16-byte
@@ -498,7 +467,6 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
   }
 
-  if (kEpi == kEpiMultimemRed) asm volatile("fence.acq_rel.sys;" ::: "memory");  // reductions before exit
   tc_fence_before();
   __syncthreads();
   if (warp == 2) {
@@ -763,7 +731,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<kEpi>::kThre
     }
   }
 
-  if (kEpi == kEpiMultimemRed) asm volatile("fence.acq_rel.sys;" ::: "memory");  // reductions before exit
   tc_fence_before();
   __syncthreads();
   cluster_sync();  // no CTA frees TMEM while the pair's MMAs or epilogues may still use it

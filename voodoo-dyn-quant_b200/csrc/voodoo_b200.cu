@@ -419,30 +419,6 @@ int vq_linear_dx(const void* dy, int64_t T, int64_t N, int64_t lddy, const void*
   return launch_gemm<false, true, vq::gemm::kEpiStoreBf16>(ta, tb, p, st);
 }
 
-int vq_linear_fwd_mcred(const void* x, int64_t T, int64_t Kin, int64_t ldx, const void* w, int64_t N, int64_t ldw,
-                        void* y_multicast, int64_t ldy, void* stream) {
-  DeviceScope scope(x);
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (int rc = check_matrix(x, T, Kin, ldx, "x")) return rc;
-  if (int rc = check_matrix(w, N, Kin, ldw, "w")) return rc;
-  if (int rc = check_matrix(y_multicast, T, N, ldy, "y")) return rc;
-  if (T == 0 || N == 0 || Kin == 0) return 0;  // adds nothing
-  if (N % 8 != 0 || ldy % 8 != 0 || (reinterpret_cast<uintptr_t>(y_multicast) & 15u) != 0)
-    return fail(VQ_ERR_INVALID, "multicast output needs N and ldy multiples of 8 and a 16-byte aligned address");
-  if (T > 0x7fffffff || N > 0x7fffffff || Kin > 0x7fffffff) return fail(VQ_ERR_INVALID, "dimension too large");
-  CUtensorMap ta, tb;
-  if (int rc = make_map(&ta, x, T, Kin, ldx, vq::gemm::BM)) return rc;
-  if (int rc = make_map(&tb, w, N, Kin, ldw, use_pair(T) ? 128 : vq::gemm::BN)) return rc;
-  vq::gemm::Params p{};
-  p.M = static_cast<int>(T);
-  p.N = static_cast<int>(N);
-  p.K = static_cast<int>(Kin);
-  p.C = static_cast<__nv_bfloat16*>(y_multicast);
-  p.ldc = ldy;
-  if (int rc = device_error_ptr(&p.err)) return rc;
-  return launch_gemm<false, false, vq::gemm::kEpiMultimemRed>(ta, tb, p, st);
-}
-
 int vq_linear_fwd_grouped(const void* x, int64_t T, int64_t Kin, int64_t ldx, int G, const void* const* w,
                           int64_t N, int64_t ldw, const int* group_off, void* y, int64_t ldy, void* stream) {
   DeviceScope scope(y);

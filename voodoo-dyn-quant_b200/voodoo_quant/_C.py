@@ -49,7 +49,6 @@ def _declare(lib):
         "vq_set_gemm_sm_reserve": (_int, [_int]),
         "vq_route_prep": (_int, [_vp, _i64, _int, _vp, _vp, _vp, _vp]),
         "vq_linear_fwd_grouped": (_int, [_vp, _i64, _i64, _i64, _int, _vp, _i64, _i64, _vp, _vp, _i64, _vp]),
-        "vq_linear_fwd_mcred": (_int, [_vp, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _vp]),
         "vq_linear_dx": (_int, [_vp, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _vp]),
         "vq_gategrad_workspace_bytes": (ctypes.c_size_t, [_i64, _i64, _int]),
         "vq_gategrad": (_int, [_vp, _i64, _vp, _i64, _i64, _i64, _i64, _int, _vp, _vp, _i64, _vp,
@@ -82,7 +81,7 @@ def _declare(lib):
 
 EXPORTED = (
     "vq_last_error", "vq_abi_version", "vq_format_info", "vq_device_error", "vq_dequant", "vq_mix",
-    "vq_linear_fwd", "vq_linear_fwd_grouped", "vq_set_gategrad_sm_reserve", "vq_set_gemm_sm_reserve", "vq_quantize", "vq_route_prep", "vq_linear_fwd_mcred", "vq_linear_dx", "vq_gategrad_workspace_bytes", "vq_gategrad", "vq_gategrad_noalloc",
+    "vq_linear_fwd", "vq_linear_fwd_grouped", "vq_set_gategrad_sm_reserve", "vq_set_gemm_sm_reserve", "vq_quantize", "vq_route_prep", "vq_linear_dx", "vq_gategrad_workspace_bytes", "vq_gategrad", "vq_gategrad_noalloc",
     "vq_mixgemm_fwd", "vq_mixgemm_dx",
     "vq_loss_fused", "vq_loss_stats", "vq_loss_combine", "vq_loss_grad",
     "vq_rmsnorm_fwd", "vq_rmsnorm_bwd", "vq_add_rmsnorm_fwd", "vq_rmsnorm_bwd_add", "vq_rope", "vq_swiglu_fwd", "vq_swiglu_bwd",
@@ -246,14 +245,6 @@ def linear_fwd_grouped(x: torch.Tensor, ws: list, n_out: int, in_features: int, 
     _check(_lib.vq_linear_fwd_grouped(x.data_ptr(), x.shape[0], in_features, x.stride(0), G, ptrs, n_out,
                                       ws[0].stride(0), go.data_ptr(), out.data_ptr(), out.stride(0), _stream(x)))
     return out
-
-
-def linear_fwd_mcred(x: torch.Tensor, w: torch.Tensor, n_out: int, in_features: int, y_multicast: int) -> None:
-    """Add x[T, Kin] w[N, Kin]^T into the NVLink multicast address `y_multicast` ([T, n_out] bf16)."""
-    _require_cuda(x, w)
-    x = _as_operand(x)
-    _check(_lib.vq_linear_fwd_mcred(x.data_ptr(), x.shape[0], in_features, x.stride(0), w.data_ptr(), n_out,
-                                    w.stride(0), y_multicast, n_out, _stream(x)))
 
 
 def linear_dx(dy: torch.Tensor, w: torch.Tensor, in_features: int, out: torch.Tensor | None = None) -> torch.Tensor:

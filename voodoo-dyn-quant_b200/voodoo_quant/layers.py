@@ -910,12 +910,11 @@ class MixedQuantLinear(_MixedQuantBase):
             return _RoutedGatedLinearFunction.apply(x, probs, self, routing, reduce_out)
         from voodoo_quant.parallel import sp_enabled
         if spec is not None and spec.col_offset is not None and not sp_enabled():
-            from voodoo_quant.parallel import multicast_reducer, nccl_row_reducer
-            # the output sum over the TP ranks happens inside the forward (in
-            # the GEMM epilogue with NVLink multicast, else an in-place NCCL
-            # all-reduce of the fresh GEMM output); its backward is the
-            # identity, so the gradients are the local ones
-            red = multicast_reducer() or nccl_row_reducer()
+            from voodoo_quant.parallel import nccl_row_reducer
+            # the output sum over the TP ranks happens inside the forward (an
+            # in-place NCCL all-reduce of the fresh GEMM output); its backward
+            # is the identity, so the gradients are the local ones
+            red = nccl_row_reducer()
             return _GatedLinearFunction.apply(x, self.get_probs().to(x.device), self, red)
         return _GatedLinearFunction.apply(x, self.get_probs().to(x.device), self)
 

@@ -513,106 +513,6 @@ def tp_broadcast(t: torch.Tensor, src: int = 0) -> torch.Tensor:
     return t
 
 
-class MulticastReducer:
-    """Row-parallel Linear outputs summed through NVLink SHARP in the GEMM.
-
-    The GEMM epilogue of each rank adds its partial Y = X W^T tile by tile
-    into a multicast address (``vq_linear_fwd_mcred``), so the NVSwitch
-    reduces while the GEMM is still computing; this replaces F.linear plus a
-    separate NCCL all-reduce (reference ``_AllReduceSum``).  Two symmetric
-    buffers alternate: use n reduces into buffer n % 2, then one tiny NCCL
-    all-reduce orders every rank's reductions before the local copy-out, and
-    the buffer is zeroed right after the copy.  The next use of that buffer
-    (n + 2) starts only after every rank has passed barrier n + 1, which each
-    rank reaches after its zeroing, so one barrier per use suffices.
-
-    Buffers are allocated on first use (a collective step: every rank runs
-    the same forward).  ``release()`` frees them on every rank together.
-    """
-
-    def __init__(self, group=None):
-        self.group = group
-        self.bufs = None
-        self.handles = None
-        self.mc = None
-        self.n = 0
-        self.flag = None
-
-    def _ensure(self, elems: int, device: torch.device) -> None:
-        if self.bufs is not None and self.bufs[0].numel() >= elems:
-            return
-        import torch.distributed._symmetric_memory as symm
-
-        self.release()
-        bufs = [symm.empty(elems, dtype=torch.bfloat16, device=device) for _ in range(2)]
-        handles = [symm.rendezvous(b, self.group if self.group is not None else dist.group.WORLD) for b in bufs]
-        if not all(h.has_multicast_support for h in handles):
-            raise RuntimeError("NVLink multicast is not available on this TP group")
-        for b in bufs:
-            b.zero_()
-        self.flag = torch.zeros(1, dtype=torch.float32, device=device)
-        dist.all_reduce(self.flag, group=self.group)  # every rank's buffers are zero before first use
-        self.bufs, self.handles = bufs, handles
-        # the multicast address of each buffer's first element, whether the
-        # handle's pointers are to the allocation or to the tensor
-        self.mc = []
-        for b, h in zip(bufs, handles):
-            delta = b.data_ptr() - int(h.buffer_ptrs[h.rank])
-            if h.multicast_ptr == 0 or delta < 0 or b.numel() * b.element_size() > h.buffer_size:
-                raise RuntimeError("unexpected symmetric-memory layout for the multicast buffer")
-            self.mc.append(int(h.multicast_ptr) + delta)
-
-    def linear(self, x2: torch.Tensor, w: torch.Tensor, n_out: int, in_features: int) -> torch.Tensor:
-        """sum over the TP ranks of x2 @ w[:, :in_features]^T as a new [T, n_out] bf16 tensor."""
-        from voodoo_quant import _C
-
-        T = x2.shape[0]
-        self._ensure(T * n_out, x2.device)
-        b = self.n & 1
-        self.n += 1
-        _C.linear_fwd_mcred(x2, w, n_out, in_features, self.mc[b])
-        dist.all_reduce(self.flag, group=self.group)  # every rank's reductions have landed
-        view = self.bufs[b][:T * n_out].view(T, n_out)
-        y = view.clone()
-        view.zero_()
-        return y
-
-    def release(self) -> None:
-        if self.bufs is None:
-            return
-        torch.cuda.synchronize()
-        dist.barrier(group=self.group)
-        self.bufs = self.handles = self.mc = None
-        self.flag = None
-
-
-_MC_REDUCER: MulticastReducer | None = None
-
-
-def enable_multicast_reduce(enable: bool = True) -> MulticastReducer | None:
-    """Route row-parallel Linear outputs (gated and Q8_0 teacher) through a
-    MulticastReducer on the TP group (a collective call).  Returns None, and
-    leaves the NCCL path in place, without TP or without NVLink multicast."""
-    global _MC_REDUCER
-    if _MC_REDUCER is not None:
-        _MC_REDUCER.release()
-        _MC_REDUCER = None
-    if not (enable and TP.enabled):
-        return None
-    red = MulticastReducer(TP.group)
-    try:
-        red._ensure(8, torch.device("cuda", torch.cuda.current_device()))
-    except RuntimeError:
-        red.release()
-        return None
-    _MC_REDUCER = red
-    return red
-
-
-def multicast_reducer() -> MulticastReducer | None:
-    return _MC_REDUCER
-
-
 def all_reduce_gate_grads(params) -> None:
     """Sum the gate gradients of every rank with ONE flat all-reduce.
 

@@ -169,14 +169,9 @@ class _RowParallelQ8(nn.Module):
 
     @torch.no_grad()
     def forward(self, x):
-        from voodoo_quant.parallel import multicast_reducer, sp_enabled, tp_all_reduce_sum_
+        from voodoo_quant.parallel import sp_enabled, tp_all_reduce_sum_
         if sp_enabled():  # partial sums: the block reduce-scatters them
             return self.inner(x)
-        red = multicast_reducer()
-        if red is not None and x.is_cuda:  # partial outputs summed over the TP ranks inside the GEMM
-            x2 = _C._as_operand(x.reshape(-1, self.in_features))
-            y = red.linear(x2, self.inner.weight_bf16(), self.out_features, self.in_features)
-            return y.to(x.dtype).reshape(*x.shape[:-1], self.out_features)
         return tp_all_reduce_sum_(self.inner(x))
 
 

@@ -387,7 +387,7 @@ def _capturing() -> bool:
 
 def build_distill(shape_name: str, device, seed: int = 0, args: StepArgs | None = None,
                   candidate_provider=None, replace_embeddings: bool = True, tp: bool = False,
-                  fused_blocks: bool = True, multicast: bool = False, overlap_sms: int = 0):
+                  fused_blocks: bool = True, overlap_sms: int = 0):
     """Student (gated), Q8_0 teacher and trainer for a synthetic config.
 
     Under TP (an initialised process group adopted by voodoo_quant.parallel)
@@ -395,11 +395,7 @@ def build_distill(shape_name: str, device, seed: int = 0, args: StepArgs | None 
     candidates are packed from the FULL tensors and sliced per rank.  On a
     CUDA device ``fused_blocks`` routes the Llama blocks' RMSNorm, rotary
     embedding and SwiGLU through the fused kernels (``voodoo_quant.fused_blocks``).
-    Under TP with ``multicast``, row-parallel outputs are summed over NVLink
-    SHARP inside their GEMMs (``parallel.enable_multicast_reduce``) where the
-    GPUs support NVLink multicast; off by default: every rank's memory then
-    takes every rank's reductions, and an 8B step at TP-2 measured 774 ms
-    against 610 ms with NCCL's ring all-reduce.  Under TP with
+    Under TP with
     ``overlap_sms`` > 0, each attention / MLP block's gate-gradient GEMMs
     run beside the all-reduce of the block's input gradient on a second
     communicator limited to that many CTAs (``parallel.enable_input_grad_overlap``,
@@ -467,20 +463,14 @@ def build_distill(shape_name: str, device, seed: int = 0, args: StepArgs | None 
         if sp:
             from voodoo_quant.fused_blocks import use_sequence_parallel
 
-            if multicast:
-                raise ValueError("sequence parallelism reduce-scatters the row-parallel outputs: multicast must be off")
             use_sequence_parallel(base)
             use_sequence_parallel(teacher)
         enable_sequence_parallel(sp)
     if tp and TP.enabled:
-        from voodoo_quant.parallel import enable_multicast_reduce, enable_teacher_overlap
+        from voodoo_quant.parallel import enable_teacher_overlap
 
         if args is not None and args.teacher_stream:
-            if multicast:
-                raise ValueError("teacher_stream needs the NCCL row-parallel sums (multicast off): the multicast "
-                                 "buffers serve one stream at a time")
             enable_teacher_overlap(args.teacher_stream_sms)
-        enable_multicast_reduce(multicast)
         if overlap_sms > 0:
             from voodoo_quant.parallel import enable_input_grad_overlap, mark_deferred_gategrads
 
