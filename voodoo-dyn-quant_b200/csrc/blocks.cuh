@@ -220,9 +220,34 @@ __global__ void __launch_bounds__(kRopeThreads) rope_kernel(RopeSide q, RopeSide
   }
 }
 
-__device__ __forceinline__ float sigmoidf_(float a) { return 1.f / (1.f + __expf(-a)); }
+__device__ __forceinline__ float sigmoidf_(float a) { return __fdividef(1.f, 1.f + __expf(-a)); }
 
-// Flat grid-stride over rows x (F / 8) vectors.
+template <bool kBackward>
+__device__ __forceinline__ void swiglu_apply(const V8& av, const V8& uv, const V8& gv, __nv_bfloat16* out0,
+                                             __nv_bfloat16* out1) {
+  if (kBackward) {
+    V8 da, du;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float sg = sigmoidf_(av.v[j]);
+      const float act = av.v[j] * sg;
+      da.v[j] = gv.v[j] * uv.v[j] * (sg * (1.f + av.v[j] * (1.f - sg)));
+      du.v[j] = gv.v[j] * act;
+    }
+    store8(out0, da);
+    store8(out1, du);
+  } else {
+    V8 y;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) y.v[j] = av.v[j] * sigmoidf_(av.v[j]) * uv.v[j];
+    store8(out0, y);
+  }
+}
+
+// Grid-stride over rows x (F / 8) vectors, two vectors per thread and
+// iteration whose loads are all issued before either is computed; the
+// (row, vector) position advances by the stride's quotient and remainder,
+// with no division in the loop.
 template <bool kBackward>
 __global__ void __launch_bounds__(kEltThreads) swiglu_kernel(const __nv_bfloat16* __restrict__ a, long long lda,
                                                              const __nv_bfloat16* __restrict__ u, long long ldu,
@@ -231,28 +256,37 @@ __global__ void __launch_bounds__(kEltThreads) swiglu_kernel(const __nv_bfloat16
                                                              __nv_bfloat16* __restrict__ out1, long long ldo) {
   const int nvec = F >> 3;
   const long long total = static_cast<long long>(rows) * nvec;
-  for (long long i = blockIdx.x * static_cast<long long>(kEltThreads) + threadIdx.x; i < total;
-       i += static_cast<long long>(gridDim.x) * kEltThreads) {
-    const long long r = i / nvec;
-    const int c = static_cast<int>(i - r * nvec) * 8;
-    const V8 av = load8(a + r * lda + c), uv = load8(u + r * ldu + c);
-    if (kBackward) {
-      const V8 gv = load8(dy + r * lddy + c);
-      V8 da, du;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const float sg = sigmoidf_(av.v[j]);
-        const float act = av.v[j] * sg;
-        da.v[j] = gv.v[j] * uv.v[j] * (sg * (1.f + av.v[j] * (1.f - sg)));
-        du.v[j] = gv.v[j] * act;
-      }
-      store8(out0 + r * ldo + c, da);
-      store8(out1 + r * ldo + c, du);
-    } else {
-      V8 y;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) y.v[j] = av.v[j] * sigmoidf_(av.v[j]) * uv.v[j];
-      store8(out0 + r * ldo + c, y);
+  const long long stride = static_cast<long long>(gridDim.x) * kEltThreads;
+  const long long i0 = static_cast<long long>(blockIdx.x) * kEltThreads + threadIdx.x;
+  if (i0 >= total) return;
+  const long long dr = stride / nvec;
+  const int dc = static_cast<int>(stride - dr * nvec);
+  long long r = i0 / nvec;
+  int c = static_cast<int>(i0 - r * nvec);
+  for (long long i = i0; i < total; i += 2 * stride) {
+    long long r2 = r + dr;
+    int c2 = c + dc;
+    if (c2 >= nvec) {
+      c2 -= nvec;
+      ++r2;
+    }
+    const bool second = i + stride < total;
+    const V8 a0 = load8(a + r * lda + 8 * c), u0 = load8(u + r * ldu + 8 * c);
+    V8 g0, a1, u1, g1;
+    if (kBackward) g0 = load8(dy + r * lddy + 8 * c);
+    if (second) {
+      a1 = load8(a + r2 * lda + 8 * c2);
+      u1 = load8(u + r2 * ldu + 8 * c2);
+      if (kBackward) g1 = load8(dy + r2 * lddy + 8 * c2);
+    }
+    swiglu_apply<kBackward>(a0, u0, g0, out0 + r * ldo + 8 * c, kBackward ? out1 + r * ldo + 8 * c : nullptr);
+    if (second)
+      swiglu_apply<kBackward>(a1, u1, g1, out0 + r2 * ldo + 8 * c2, kBackward ? out1 + r2 * ldo + 8 * c2 : nullptr);
+    r = r2 + dr;
+    c = c2 + dc;
+    if (c >= nvec) {
+      c -= nvec;
+      ++r;
     }
   }
 }
