@@ -291,14 +291,6 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, uint8_t* stage, u
         slot_override >= 0 ? slot_override : (static_cast<long long>(m128) * p.num_n_blk + n_blk) * 4 + wq;
     const long long colbase = static_cast<long long>(n_blk) * BN;
     const long long urow = (row_ok ? row : 0) * p.units_per_row + n_blk;
-    // Pull this row's unit of every candidate of the set towards L2 now: the
-    // units are staged one candidate at a time, each after the previous one's
-    // dot, so the later ones would otherwise start from DRAM latency.
-    for (int k = 0; k < p.cands.K; ++k) {
-      if (cand_set >= 0 && ((p.set1_mask >> k) & 1) != cand_set) continue;
-      const uint8_t* unit = p.cands.ptr[k] + urow * p.cands.ubytes[k];
-      for (int off = 0; off < p.cands.ubytes[k]; off += 128) prefetch_l2(unit + off);
-    }
     for (int k = 0; k < p.cands.K; ++k) {
       if (cand_set >= 0 && ((p.set1_mask >> k) & 1) != cand_set) continue;
       stage_row_lane(slot_row, p.cands.ptr[k] + urow * p.cands.ubytes[k], p.cands.ubytes[k]);
