@@ -1076,12 +1076,70 @@ def run_cache_load(args):
           flush=True)
 
 
+def run_collectives(args):
+    """The TP group's collectives alone (torchrun, one process per GPU): NCCL
+    all-reduce, reduce-scatter and all-gather of bf16 tensors the size of the
+    8B step's hidden state ([16384, 4096] = 134.2 MB) and an eighth of it,
+    after 5 warm-up calls, 20 calls timed with CUDA events, max over ranks.
+    Bus bandwidth in the nccl-tests convention (all-reduce 2 (N - 1) / N,
+    reduce-scatter and all-gather (N - 1) / N of the full tensor's bytes)."""
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world < 2:
+        print(json.dumps({"metric": "collectives", "unavailable": "needs torchrun with 2 or more GPUs"}))
+        return
+    dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
+    res = {}
+    for mb in (16.8, 134.2):
+        n = int(mb * 1e6 / 2)
+        n -= n % (world * 8)
+        x = torch.randn(n, device=dev).to(torch.bfloat16)
+        shard = torch.empty(n // world, device=dev, dtype=torch.bfloat16)
+        full = torch.empty(n, device=dev, dtype=torch.bfloat16)
+        for op in ("all_reduce", "reduce_scatter", "all_gather"):
+            def f():
+                if op == "all_reduce":
+                    dist.all_reduce(x)
+                elif op == "reduce_scatter":
+                    dist.reduce_scatter_tensor(shard, x)
+                else:
+                    dist.all_gather_into_tensor(full, shard)
+            for _ in range(5):
+                f()
+            torch.cuda.synchronize()
+            dist.barrier()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(20):
+                f()
+            e1.record()
+            torch.cuda.synchronize()
+            t = torch.tensor([e0.elapsed_time(e1) / 20], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+            factor = 2 * (world - 1) / world if op == "all_reduce" else (world - 1) / world
+            res[f"{op}_{mb}MB"] = {"ms": round(ms, 4), "bus_GBps": round(n * 2 * factor / (ms * 1e-3) / 1e9, 1)}
+    if rank == 0:
+        print(json.dumps({"metric": "TP collectives (bf16)", "n_gpus": world, "results": res,
+                          "nccl": ".".join(str(v) for v in torch.cuda.nccl.version())}), flush=True)
+    dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--workload", choices=["8b", "layer", "tiny", "0.6b", "32b", "cache-load"], default="8b",
+    ap.add_argument("--workload", choices=["8b", "layer", "tiny", "0.6b", "32b", "cache-load", "collectives"],
+                    default="8b",
                     help="8b (default): the config-4 distillation step at TP-N; tiny/0.6b/32b: the other step "
                          "configurations (32b: the TP-4 / TP-8 case, K=7 with per-role menus); layer: the config-2 "
-                         "single gated-Linear step; cache-load: candidate-cache files into HBM (GB/s)")
+                         "single gated-Linear step; cache-load: candidate-cache files into HBM (GB/s); "
+                         "collectives: the TP group's NCCL all-reduce / reduce-scatter / all-gather alone")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
@@ -1149,6 +1207,8 @@ def main():
         run_reference(args)
     elif args.workload == "cache-load":
         run_cache_load(args)
+    elif args.workload == "collectives":
+        run_collectives(args)
     elif args.workload != "layer":
         run_model_step(args)
     else:
