@@ -1090,11 +1090,11 @@ def run_collectives(args):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
-    dev = torch.device("cuda", local)
-    torch.cuda.set_device(dev)
     if world < 2:
         print(json.dumps({"metric": "collectives", "unavailable": "needs torchrun with 2 or more GPUs"}))
         return
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
     dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
     res = {}
     for mb in (16.8, 134.2):
