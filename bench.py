@@ -1076,6 +1076,76 @@ def run_cache_load(args):
           flush=True)
 
 
+def run_gemm_shapes(args):
+    """The gated Linear's kernels at every distinct projection shape of the
+    8B step (one GPU, T = 16384 tokens): per shape and TP degree (1 and 8:
+    the rank's shard), the mixture, forward, dX and gate-gradient GEMMs timed
+    with CUDA events (after 2 warm-up calls, ``--kernel-iters`` timed),
+    as TFLOP/s (2 T N Kin each) and fractions of the measured burst peak;
+    six candidates Q2_K..Q8_0.  Inputs are larger than L2 for the large
+    shapes; small shards partly live in L2, as they do in the step."""
+    import torch
+    from voodoo_quant import _C
+    from voodoo_quant.quants import rtn
+    from voodoo_quant.training import synthetic as S
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    shape = S.SHAPES["8b"]
+    types = list(shape.candidates)
+    T = shape.batch * shape.seq
+    pk, pk_kind = peaks()
+    peak_t = float(pk.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
+    g = torch.Generator(device=dev).manual_seed(0)
+    rows = []
+    seen = set()
+    for tp in (1, 8):
+        for role, n_out, n_in, _ in layer_linear_shapes(shape) + [("lm_head", shape.vocab, shape.hidden, None)]:
+            if role in ("q_proj", "k_proj", "v_proj", "gate_proj", "up_proj", "lm_head"):
+                n, kin = n_out // tp, n_in  # column-parallel: output rows split
+            else:
+                n, kin = n_out, n_in // tp  # row-parallel: input columns split
+            key = (n, kin)
+            if key in seen:
+                continue
+            seen.add(key)
+            w = torch.randn(n, kin, device=dev, generator=g) * 0.02
+            blocks = [rtn.quantize(w, q) for q in types]
+            del w
+            probs = torch.softmax(torch.randn(len(types), device=dev, generator=g), 0)
+            x = torch.randn(T, kin, device=dev, generator=g).to(torch.bfloat16)
+            dy = torch.randn(T, n, device=dev, generator=g).to(torch.bfloat16)
+            wm = _C.mix(types, blocks, probs, n, kin, kin)
+            ws = torch.empty(max(_C.gategrad_workspace_bytes(n, kin, len(types)), 4), dtype=torch.uint8, device=dev)
+            fns = {"mix": lambda: _C.mix(types, blocks, probs, n, kin, kin, out=wm),
+                   "fwd": lambda: _C.linear_fwd(x, wm, n, kin),
+                   "dx": lambda: _C.linear_dx(dy, wm, kin),
+                   "gategrad": lambda: _C.gategrad(dy, x, types, blocks, n, kin, kin, workspace=ws)}
+            res = {"role": role, "tp": tp, "N": n, "Kin": kin}
+            for name, fn in fns.items():
+                for _ in range(2):
+                    fn()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                for _ in range(args.kernel_iters):
+                    fn()
+                e1.record()
+                torch.cuda.synchronize()
+                ms = e0.elapsed_time(e1) / args.kernel_iters
+                if name == "mix":
+                    res["mix_ms"] = round(ms, 4)
+                else:
+                    tf = 2.0 * T * n * kin / (ms * 1e-3) / 1e12
+                    res[name] = {"ms": round(ms, 4), "TFLOP/s": round(tf, 1), "frac": round(tf / peak_t, 3)}
+            rows.append(res)
+            del blocks, x, dy, wm, ws
+            torch.cuda.empty_cache()
+    assert _C.device_error() == 0
+    print(json.dumps({"metric": "gated-Linear kernels per 8B projection shape", "tokens": T, "candidates": types,
+                      "peak_tflops": peak_t, "peak_source": f"{pk_kind} bf16_tflops (burst)", "shapes": rows}),
+          flush=True)
+
+
 def run_collectives(args):
     """The TP group's collectives alone (torchrun, one process per GPU): NCCL
     all-reduce, reduce-scatter and all-gather of bf16 tensors the size of the
@@ -1134,12 +1204,14 @@ def run_collectives(args):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--workload", choices=["8b", "layer", "tiny", "0.6b", "32b", "cache-load", "collectives"],
+    ap.add_argument("--workload", choices=["8b", "layer", "tiny", "0.6b", "32b", "cache-load", "collectives",
+                                           "gemm-shapes"],
                     default="8b",
                     help="8b (default): the config-4 distillation step at TP-N; tiny/0.6b/32b: the other step "
                          "configurations (32b: the TP-4 / TP-8 case, K=7 with per-role menus); layer: the config-2 "
                          "single gated-Linear step; cache-load: candidate-cache files into HBM (GB/s); "
-                         "collectives: the TP group's NCCL all-reduce / reduce-scatter / all-gather alone")
+                         "collectives: the TP group's NCCL all-reduce / reduce-scatter / all-gather alone; "
+                         "gemm-shapes: the gated Linear's kernels at every 8B projection shape (TP-1 and TP-8 shards)")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
@@ -1209,6 +1281,8 @@ def main():
         run_cache_load(args)
     elif args.workload == "collectives":
         run_collectives(args)
+    elif args.workload == "gemm-shapes":
+        run_gemm_shapes(args)
     elif args.workload != "layer":
         run_model_step(args)
     else:
