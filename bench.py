@@ -757,6 +757,34 @@ def run_ncu_case():
     print("ncu case ok", flush=True)
 
 
+def run_ncu_case_tp8():
+    """One launch each of the forward, dX and gate-gradient GEMMs at two TP-8
+    shard shapes of the 8B step (T = 16384): q_proj (N = 512, Kin = 4096) and
+    o_proj (N = 4096, Kin = 512), six candidates -- the small-shard GEMMs
+    whose fixed per-tile costs dominate at TP-8."""
+    import torch
+    from voodoo_quant import _C
+    from voodoo_quant.quants import rtn
+
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(0)
+    types = ["Q2_K", "Q3_K", "Q4_K", "Q5_K", "Q6_K", "Q8_0"]
+    T = 16384
+    for n, kin in ((512, 4096), (4096, 512)):
+        w = torch.randn(n, kin, device=dev, generator=g) * 0.02
+        blocks = [rtn.quantize(w, q) for q in types]
+        probs = torch.softmax(torch.randn(len(types), device=dev, generator=g), 0)
+        wm = _C.mix(types, blocks, probs, n, kin, kin)
+        x = torch.randn(T, kin, device=dev, generator=g).to(torch.bfloat16)
+        dy = torch.randn(T, n, device=dev, generator=g).to(torch.bfloat16)
+        _C.linear_fwd(x, wm, n, kin)
+        _C.linear_dx(dy, wm, kin)
+        _C.gategrad(dy, x, types, blocks, n, kin, kin)
+    torch.cuda.synchronize()
+    assert _C.device_error() == 0
+    print("ncu tp8 case ok", flush=True)
+
+
 _OUR_KERNELS = ("gemm_kernel", "gemm_pair_kernel", "mix_units_kernel", "dequant_units_kernel",
                 "gategrad_reduce_kernel", "loss_fused_kernel", "loss_stats_kernel", "loss_combine_kernel",
                 "loss_grad_kernel", "rmsnorm_fwd_kernel", "rmsnorm_bwd_kernel", "rope_kernel", "swiglu_kernel",
@@ -1257,7 +1285,9 @@ def main():
                          "memory plan and step; its line says so and is not the configuration's number)")
     ap.add_argument("--profile-step", action="store_true",
                     help="step workloads: print device time per kernel name for one step")
-    ap.add_argument("--ncu-case", action="store_true", help="one launch per kernel at profiling sizes")
+    ap.add_argument("--ncu-case", nargs="?", const="config2", default=None, choices=["config2", "tp8"],
+                    help="one launch per kernel at profiling sizes (config2: mix, GEMMs, loss; tp8: the GEMMs at two "
+                         "TP-8 shard shapes)")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if args.overlap_sms < 0:
@@ -1273,7 +1303,9 @@ def main():
         args.graph_step = world > 1 and args.workload != "layer" and args.logits_chunk <= 0 and not args.ptqr
     if args.teacher_tp < 0:
         args.teacher_tp = auto_teacher_tp(args.workload, world) if args.logits_chunk <= 0 else 0
-    if args.ncu_case:
+    if args.ncu_case == "tp8":
+        run_ncu_case_tp8()
+    elif args.ncu_case:
         run_ncu_case()
     elif args.impl == "reference":
         run_reference(args)
