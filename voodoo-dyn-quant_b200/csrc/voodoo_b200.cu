@@ -146,6 +146,11 @@ int build_candset(vq::CandSet* cs, int K, const int* types, const void* const* b
 // 128, else by 128 on single CTAs.  `pair` reports the choice (the tensor
 // map box of a K-major B operand and the gate-gradient slot count depend on it).
 inline bool use_pair(long long M) { return M > vq::gemm::BM; }
+// The gate-gradient GEMM always runs on CTA pairs: its stream-K split (the
+// paired kernel's) then spreads even a few row blocks over every SM, where
+// a 1-CTA launch of a 128-row layer (a KV projection's TP shard) would keep
+// one SM per 256 columns busy.
+inline bool gategrad_pair(long long) { return true; }
 
 // Upper bound on CTA pairs of a paired launch (the stream-K partial slots of
 // the gate-gradient workspace are sized for it).
@@ -166,7 +171,7 @@ inline int sm_reserve(int epi, int sms) {
 
 // Gate-gradient partial slots the per-tile schedule writes.
 inline long long gategrad_tile_slots(long long N, long long Kin) {
-  const long long m128 = use_pair(N) ? 2 * ((N + 255) / 256) : (N + vq::gemm::BM - 1) / vq::gemm::BM;
+  const long long m128 = gategrad_pair(N) ? 2 * ((N + 255) / 256) : (N + vq::gemm::BM - 1) / vq::gemm::BM;
   return m128 * ((Kin + vq::gemm::BN - 1) / vq::gemm::BN) * 4;
 }
 
@@ -175,7 +180,7 @@ template <bool kAmn, bool kBmn, int kEpi>
 int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, vq::gemm::Params p, cudaStream_t st,
                 long long* used_slots = nullptr) {
   using namespace vq::gemm;
-  const bool pair = use_pair(p.M);
+  const bool pair = kEpi == vq::gemm::kEpiGateGrad ? gategrad_pair(p.M) : use_pair(p.M);
   p.num_m_blk = pair ? (p.M + 255) / 256 : (p.M + BM - 1) / BM;
   p.num_n_blk = (p.N + BN - 1) / BN;
   p.num_k_blk = (p.K + BK - 1) / BK;
@@ -191,9 +196,13 @@ int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, vq::gemm::Params p
     VQ_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     const int avail = sms - sm_reserve(kEpi, sms);
     int clusters = p.num_tiles < avail / 2 ? p.num_tiles : avail / 2;
+    // At most half as many gate-gradient tiles as pairs: split them all along
+    // K over every pair (each piece decodes its tile's candidates again, so
+    // a split pays only where it at least doubles the pairs at work).
+    if (kEpi == kEpiGateGrad && 2 * p.num_tiles <= avail / 2) clusters = avail / 2;
     if (clusters > kMaxClusters) clusters = kMaxClusters;
-    if (kEpi == kEpiGateGrad && p.num_tiles % clusters != 0 && p.num_tiles > clusters) {
-      // split the last, partial wave of tiles along K across every cluster
+    if (kEpi == kEpiGateGrad && p.num_tiles % clusters != 0 && (p.num_tiles > clusters || 2 * p.num_tiles <= clusters)) {
+      // split the last, partial wave of tiles (or all of them) along K across every cluster
       p.stream_k = 1;
       p.sk_base = static_cast<int>(gategrad_tile_slots(p.M, p.N));
       if (used_slots != nullptr) *used_slots += 16LL * clusters;
@@ -241,7 +250,7 @@ inline int gategrad_set_split(int K, const int* types) {
 // Gate-gradient partial slots a workspace must hold: the per-tile slots plus,
 // for paired launches, the stream-K slots (16 per cluster).
 inline long long gategrad_slots(long long N, long long Kin) {
-  return gategrad_tile_slots(N, Kin) + (use_pair(N) ? 16LL * kMaxClusters : 0);
+  return gategrad_tile_slots(N, Kin) + (gategrad_pair(N) ? 16LL * kMaxClusters : 0);
 }
 
 int check_matrix(const void* p, long long rows, long long cols, long long ld, const char* name) {
