@@ -194,6 +194,32 @@ def test_linear_fwd_exact_small_integers(cuda):
     assert torch.equal(_C.linear_dx(dy, w, K), (dy.double() @ w.double()).to(torch.bfloat16))
 
 
+@pytest.mark.parametrize("T,N,K,ld_pad,col_off", [(333, 1000, 512, 24, 0), (4100, 4096, 512, 64, 0),
+                                                   (129, 256, 64, 8, 0), (257, 520, 128, 3, 0),
+                                                   (300, 768, 192, 0, 1)])
+def test_linear_store_edges_exact(cuda, T, N, K, ld_pad, col_off):
+    """The paired store epilogue writes bulk tensor stores of 32 x 32 boxes
+    where the output allows it (16-byte aligned base and row pitch) and row
+    by row elsewhere (odd pitch, unaligned base): both against the exact
+    product, with ragged last rows and columns, and every element outside
+    the output (padding between rows, rows past its end) left untouched."""
+    from voodoo_quant import _C
+
+    g = torch.Generator(device="cpu").manual_seed(T + N + K + ld_pad)
+    x = torch.randint(-3, 4, (T, K), generator=g).to(cuda, torch.bfloat16)
+    w = torch.randint(-3, 4, (N, K), generator=g).to(cuda, torch.bfloat16)
+    dy = torch.randint(-3, 4, (T, N), generator=g).to(cuda, torch.bfloat16)
+    for width, fn, ref in ((N, lambda o: _C.linear_fwd(x, w, out=o), x.double() @ w.double().T),
+                           (K, lambda o: _C.linear_dx(dy, w, K, out=o), dy.double() @ w.double())):
+        big = torch.full((T + 40, width + ld_pad + col_off), float("inf"), dtype=torch.bfloat16, device=cuda)
+        out = big[:T, col_off:col_off + width]
+        fn(out)
+        assert torch.equal(out, ref.to(torch.bfloat16))
+        assert torch.isinf(big[:T, :col_off]).all() and torch.isinf(big[:T, col_off + width:]).all()
+        assert torch.isinf(big[T:]).all()
+    assert _C.device_error() == 0
+
+
 @pytest.mark.parametrize("types,T,N,IN", [
     (["Q4_K", "Q5_K", "Q6_K", "Q8_0"], 256, 256, 512),
     (["Q3_K", "Q4_K", "Q5_K", "Q6_K", "Q8_0"], 300, 200, 768),

@@ -53,6 +53,14 @@ constexpr int kStagePitch = kMaxUnitWords + 1;  // 69 words
 // Row pitch of the second gate-gradient epilogue set: the widest unit it may
 // stage is Q6_K's 210 bytes = 53 words (odd, so again 32 distinct banks).
 constexpr int kStagePitch1 = 53;
+// One bulk-store buffer of the paired store epilogue: 32 rows x 32 bf16.
+constexpr int kOutBufBytes = 32 * 32 * 2;
+
+// Two floats rounded to bf16 (nearest even), packed low = a, high = b.
+__device__ __forceinline__ uint32_t bf16x2_bits(float a, float b) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
 
 template <int kEpi>
 struct SmemLayout {
@@ -73,6 +81,9 @@ struct Params {
   // kEpiStoreBf16
   __nv_bfloat16* C;
   long long ldc;
+  // paired store kernel: write C through the tensor map BMaps::c (32 x 32
+  // boxes, 64-byte swizzle) instead of per-row 16-byte stores
+  int tma_store;
   // kEpiGateGrad: candidate rows = M (out features), valid columns = cols
   CandSet cands;
   int units_per_row;
@@ -96,10 +107,12 @@ struct Params {
 
 constexpr int kMaxGroups = 8;
 
-// B-operand tensor maps of a paired launch: one, or one per group.
+// B-operand tensor maps of a paired launch (one, or one per group), and the
+// output map of the store epilogue (used when Params::tma_store is set).
 template <int G>
 struct BMaps {
   CUtensorMap m[G];
+  CUtensorMap c;
 };
 
 // One unit of work of a persistent cluster: k-blocks [kb0, kb1) of a tile.
@@ -249,6 +262,42 @@ __device__ __forceinline__ float row_dot(const uint32_t* slot, uint32_t t_row, l
     }
   }
   return s;
+}
+
+// Store epilogue of one warp's 32 rows of a 128 x 256 accumulator tile
+// through TMA: each 32-column slice is converted to bf16 into a 2 KB buffer
+// in the 64-byte-swizzled layout of the output map's 32 x 32 box (16-byte
+// chunk c of row r at r * 64 + ((c ^ (r >> 1) & 3) * 16), so each quarter-warp
+// of 16-byte shared stores hits all 32 banks once) and written by one bulk
+// tensor store from lane 0.  The warp's two buffers alternate (`it` counts
+// the warp's slices); rows and columns past the map's extent are not written.
+__device__ __forceinline__ void epilogue_store_tma(const Params& p, const CUtensorMap* tmc, uint8_t* bufs,
+                                                   uint32_t t_row, int row0, int n_blk, int lane, uint32_t& it) {
+  for (int c = 0; c < BN / 32; ++c) {
+    const int col0 = n_blk * BN + c * 32;
+    if (col0 >= p.N) break;  // uniform across the warp
+    float v[32];
+    tmem_ld_32cols(t_row + c * 32, v);
+    uint8_t* buf = bufs + (it & 1u) * kOutBufBytes;
+    if (lane == 0) bulk_wait_read<1>();  // the store that last read this buffer is done with it
+    __syncwarp();
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      uint4 q;
+      q.x = bf16x2_bits(v[8 * j + 0], v[8 * j + 1]);
+      q.y = bf16x2_bits(v[8 * j + 2], v[8 * j + 3]);
+      q.z = bf16x2_bits(v[8 * j + 4], v[8 * j + 5]);
+      q.w = bf16x2_bits(v[8 * j + 6], v[8 * j + 7]);
+      *reinterpret_cast<uint4*>(buf + lane * 64 + ((j ^ ((lane >> 1) & 3)) << 4)) = q;
+    }
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      tma_store_2d(tmc, smem_u32(buf), col0, row0);
+      bulk_commit();
+    }
+    ++it;
+  }
 }
 
 // Epilogue of one 128 x 256 accumulator tile held in this CTA's TMEM.
@@ -506,7 +555,11 @@ struct PairSmemLayout {
   static constexpr int stage_off = misc_off + 64;
   static constexpr int stage1_off = stage_off + 4 * 32 * kStagePitch * 4;  // second set's rows
   static constexpr int stage_bytes = (kEpi == 1) ? 4 * 32 * (kStagePitch + kStagePitch1) * 4 : 0;
-  static constexpr int total = stage_off + stage_bytes;
+  // store epilogue: two 2 KB bulk-store buffers per epilogue warp, 1024-byte
+  // aligned (the 64-byte swizzle pattern repeats every 512 bytes)
+  static constexpr int out_off = (stage_off + 1023) & ~1023;
+  static constexpr int out_bytes = (kEpi == 0) ? 4 * 2 * kOutBufBytes : 0;
+  static constexpr int total = kEpi == 0 ? out_off + out_bytes : stage_off + stage_bytes;
   static_assert(total <= 232448, "paired kernel shared memory above the 227 KB per-block limit");
 };
 
@@ -685,7 +738,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<kEpi>::kThre
     const int pitch = eset ? kStagePitch1 : kStagePitch;
     const uint32_t tempty_leader0 = map_to_rank(tempty_bar(0), 0);
     const uint32_t tempty_leader1 = map_to_rank(tempty_bar(1), 0);
-    uint32_t local = 0;
+    uint32_t local = 0, out_it = 0;
     bool sk_written[2] = {false, false};
     Seg sg;
     for (int si = 0; get_seg(p, ntiles, cluster_id, num_clusters, si, sg); ++si, ++local) {
@@ -706,12 +759,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<kEpi>::kThre
         slot = p.sk_base + ((static_cast<long long>(cluster_id) * 2 + sg.piece) * 2 + rank) * 4 + wq;
         sk_written[sg.piece] = true;
       }
-      epilogue_tile<kEpi>(p, stage, t_row, static_cast<long long>(row_base) + 128 * rank + 32 * wq, m128, n_blk, wq,
-                          lane, slot, row_end, kSets > 1 ? eset : -1, pitch);
+      const int row0 = row_base + 128 * static_cast<int>(rank) + 32 * wq;
+      // bulk stores clip at the output's last row, not at a group's end: a
+      // warp whose rows straddle a group boundary stores row by row
+      if (kEpi == kEpiStoreBf16 && p.tma_store && (row_end == p.M || row0 + 32 <= row_end))
+        epilogue_store_tma(p, &tmB.c, smem + SL::out_off + wq * 2 * kOutBufBytes, t_row, row0, n_blk, lane, out_it);
+      else
+        epilogue_tile<kEpi>(p, stage, t_row, row0, m128, n_blk, wq, lane, slot, row_end, kSets > 1 ? eset : -1,
+                            pitch);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(acc ? tempty_leader1 : tempty_leader0);
     }
+    if (kEpi == kEpiStoreBf16 && lane == 0) bulk_wait_all();  // no bulk store still reads shared memory
     if (kEpi == kEpiGateGrad && p.stream_k && lane == 0) {
       // stream-K slots this cluster did not fill read as zero in the reduction
       for (int j = 0; j < 2; ++j) {

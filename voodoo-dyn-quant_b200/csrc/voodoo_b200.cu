@@ -123,6 +123,25 @@ int make_map(CUtensorMap* m, const void* base, long long rows, long long cols, l
   return 0;
 }
 
+// Output map of the paired store epilogue: bf16 C [rows][cols] (leading
+// dimension ld) in 32 x 32 boxes with the 64-byte swizzle.  Returns false,
+// and the epilogue stores row by row, where the bulk store cannot address C
+// (base not 16-byte aligned, row pitch not a multiple of 16 bytes, C
+// narrower or shorter than one box) or the driver declines the map.
+bool make_out_map(CUtensorMap* m, const void* base, long long rows, long long cols, long long ld) {
+  auto fn = encode_fn();
+  if (fn == nullptr || (reinterpret_cast<uintptr_t>(base) & 15u) != 0 || (ld * 2) % 16 != 0 || rows < 32 ||
+      cols < 32)
+    return false;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld * 2)};
+  cuuint32_t box[2] = {32u, 32u};
+  cuuint32_t estr[2] = {1u, 1u};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 bool known_format(int f) { return vq::unit_bytes(f) > 0; }
 
 int build_candset(vq::CandSet* cs, int K, const int* types, const void* const* blocks) {
@@ -207,8 +226,9 @@ int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, vq::gemm::Params p
       p.sk_base = static_cast<int>(gategrad_tile_slots(p.M, p.N));
       if (used_slots != nullptr) *used_slots += 16LL * clusters;
     }
-    BMaps<1> bm;
+    BMaps<1> bm{};
     bm.m[0] = tb;
+    p.tma_store = kEpi == kEpiStoreBf16 && make_out_map(&bm.c, p.C, p.M, p.N, p.ldc);
     kern<<<2 * clusters, PairCfg<kEpi>::kThreads, smem, st>>>(ta, bm, p);
   } else {
     auto kern = gemm_kernel<kAmn, kBmn, kEpi>;
@@ -443,7 +463,7 @@ int vq_linear_fwd_grouped(const void* x, int64_t T, int64_t Kin, int64_t ldx, in
   if (T > 0x7fffffff || N > 0x7fffffff || Kin > 0x7fffffff) return fail(VQ_ERR_INVALID, "dimension too large");
   if (!use_pair(T)) return fail(VQ_ERR_INVALID, "grouped GEMM needs more than %d rows", vq::gemm::BM);
   CUtensorMap ta;
-  vq::gemm::BMaps<vq::gemm::kMaxGroups> bm;
+  vq::gemm::BMaps<vq::gemm::kMaxGroups> bm{};
   if (int rc = make_map(&ta, x, T, Kin, ldx, vq::gemm::BM)) return rc;
   for (int g = 0; g < G; ++g)
     if (int rc = make_map(&bm.m[g], w[g], N, Kin, ldw, 128)) return rc;
@@ -459,6 +479,7 @@ int vq_linear_fwd_grouped(const void* x, int64_t T, int64_t Kin, int64_t ldx, in
   p.num_k_blk = static_cast<int>((Kin + vq::gemm::BK - 1) / vq::gemm::BK);
   p.num_m_blk = static_cast<int>((T + 255) / 256) + G;  // upper bound on the groups' 256-row tiles
   p.num_tiles = p.num_m_blk * p.num_n_blk;              // the kernel counts the exact tiles itself
+  p.tma_store = make_out_map(&bm.c, y, T, N, ldy);
   if (int rc = device_error_ptr(&p.err)) return rc;
   int sms = 0;
   if (int rc = sm_count(&sms)) return rc;
