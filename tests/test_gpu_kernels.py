@@ -428,11 +428,15 @@ def test_config2_shapes_properties(cuda):
     assert _C.device_error() == 0
 
 
-@pytest.mark.parametrize("T,N,IN", [(1024, 2560, 2048), (640, 14336, 512)])
+@pytest.mark.parametrize("T,N,IN", [(1024, 2560, 2048), (640, 14336, 512), (2048, 512, 4096), (1000, 768, 2048),
+                                    (4096, 128, 4096)])
 def test_gategrad_stream_k_tail_matches_fp64(cuda, T, N, IN):
     """Shapes whose tile count is not a multiple of the CTA-pair count, so the
     last wave is split along K (stream-K pieces writing their own partial
-    slots): against fp64 <dy^T x, W_k> with W_k decoded bit-exactly."""
+    slots), and shapes with at most half as many tiles as pairs, where every
+    tile is split (two or three row blocks walking the same column ranges
+    together, or one): against fp64 <dy^T x, W_k> with W_k decoded
+    bit-exactly."""
     from voodoo_quant import _C
     from voodoo_quant.quants import rtn
 

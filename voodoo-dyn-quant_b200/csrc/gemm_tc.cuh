@@ -121,6 +121,24 @@ struct Seg {
   int tile, kb0, kb1, piece;
 };
 
+__device__ __forceinline__ void tile_coords(const Params& p, int tile, int& m_blk, int& n_blk) {
+  const int band = GROUP_N * p.num_m_blk;
+  const int g = tile / band;
+  const int first_n = g * GROUP_N;
+  const int gn = min(GROUP_N, p.num_n_blk - first_n);
+  const int r = tile - g * band;
+  m_blk = r / gn;
+  n_blk = first_n + (r - m_blk * gn);
+}
+
+// Inverse of tile_coords.
+__device__ __forceinline__ int tile_index(const Params& p, int m_blk, int n_blk) {
+  const int g = n_blk / GROUP_N;
+  const int first_n = g * GROUP_N;
+  const int gn = min(GROUP_N, p.num_n_blk - first_n);
+  return g * GROUP_N * p.num_m_blk + m_blk * gn + (n_blk - first_n);
+}
+
 // Segment i of cluster c out of C (the same sequence for every role).
 __device__ __forceinline__ bool get_seg(const Params& p, int ntiles, int c, int C, int i, Seg& sg) {
   if (!p.stream_k) {
@@ -134,6 +152,30 @@ __device__ __forceinline__ bool get_seg(const Params& p, int ntiles, int c, int 
     return true;
   }
   const int KB = p.num_k_blk;
+  const int Gm = p.num_m_blk;
+  if (full == 0 && Gm > 1 && p.num_n_blk <= C / Gm) {
+    // Every tile split (fewer tiles than clusters): cluster c works on row
+    // block c % Gm, and the clusters of the Gm row blocks that share an index
+    // c / Gm walk the same (column block, k-block) range at the same time,
+    // so each B k-slice is read from DRAM once for all row blocks.  A range
+    // is at most one tile long (num_n_blk <= C / Gm), so it touches two tiles
+    // at most.
+    const int g = c % Gm, ic = c / Gm;
+    const int Cg = C / Gm + (g < C % Gm ? 1 : 0);
+    const long long Ug = static_cast<long long>(p.num_n_blk) * KB;
+    const int lo = static_cast<int>(Ug * ic / Cg), hi = static_cast<int>(Ug * (ic + 1) / Cg);
+    const int cut = (lo / KB + 1) * KB;
+    const int j = i - full;
+    if (j == 0 && lo < hi) {
+      sg = {tile_index(p, g, lo / KB), lo % KB, (hi < cut ? hi : cut) - (lo / KB) * KB, 0};
+      return true;
+    }
+    if (j == 1 && hi > cut) {
+      sg = {tile_index(p, g, cut / KB), 0, hi - cut, 1};
+      return true;
+    }
+    return false;
+  }
   const long long U = static_cast<long long>(p.num_tiles - full * C) * KB;
   const int lo = static_cast<int>(U * c / C), hi = static_cast<int>(U * (c + 1) / C);
   const int j = i - full;
@@ -147,16 +189,6 @@ __device__ __forceinline__ bool get_seg(const Params& p, int ntiles, int c, int 
     return true;
   }
   return false;
-}
-
-__device__ __forceinline__ void tile_coords(const Params& p, int tile, int& m_blk, int& n_blk) {
-  const int band = GROUP_N * p.num_m_blk;
-  const int g = tile / band;
-  const int first_n = g * GROUP_N;
-  const int gn = min(GROUP_N, p.num_n_blk - first_n);
-  const int r = tile - g * band;
-  m_blk = r / gn;
-  n_blk = first_n + (r - m_blk * gn);
 }
 
 // Stage this lane's unit (ub bytes at `unit`, 2-byte aligned) into its own
