@@ -97,6 +97,23 @@ int vq_gategrad(const void* dy, int64_t lddy, const void* x, int64_t ldx, int64_
                 const int* types, const void* const* blocks, int64_t padded_cols, void* workspace,
                 size_t workspace_bytes, float* grad_probs, void* stream);
 
+/* Bytes of scratch vq_gategrad_grouped needs for G layers of N_total rows in
+ * all, Kin columns, K candidates each. */
+size_t vq_gategrad_grouped_workspace_bytes(int64_t N_total, int64_t Kin, int G, int K);
+
+/* K3 for G <= 4 gated Linears that read the same input x (q/k/v, gate/up):
+ * one gate-gradient GEMM over dy [T, N_total], whose columns are the layers'
+ * outputs side by side (layer g: rows[g] columns, a multiple of 32), with
+ * layer g's K candidates at blocks[g * K + k] (the same K formats `types` for
+ * every layer).  grad_probs[g * ld_grad + k] = <dy_g^T x, W_{g,k}>.  Results
+ * equal G vq_gategrad calls up to the order of fp32 partial sums.  Batches the
+ * per-layer _MixedWeightFunction.backward of voodoo_quant/layers.py:355-363
+ * for layers whose forwards share one input. */
+int vq_gategrad_grouped(const void* dy, int64_t lddy, const void* x, int64_t ldx, int64_t T, int G,
+                        const int64_t* rows, int64_t Kin, int K, const int* types, const void* const* blocks,
+                        int64_t padded_cols, void* workspace, size_t workspace_bytes, float* grad_probs,
+                        int64_t ld_grad, void* stream);
+
 /* PTQR grouping in one launch: the stable counting sort of T routing keys
  * (uint8, values in [0, K), K <= 8): order[p] = i and inv[i] = p (int64) for
  * the element i placed at position p, group_off[K + 1] (int32) the first

@@ -78,6 +78,18 @@ def _gategrad(dy, x, qtypes, qbytes, n_out, in_features, padded_cols, workspace=
     return g
 
 
+def _gategrad_grouped(dy, x, qtypes, qbytes_per_layer, rows, in_features, padded_cols, workspace=None, out=None):
+    g, a = [], 0
+    for n, qbytes in zip(rows, qbytes_per_layer):
+        g.append(_gategrad(dy[:, a:a + n], x, qtypes, qbytes, n, in_features, padded_cols))
+        a += n
+    g = torch.stack(g)
+    if out is not None:
+        out.copy_(g)
+        return out
+    return g
+
+
 def _dequant(qb, qt, rows, cols):
     return _decode(qb, qt, rows, cols)
 
@@ -188,6 +200,8 @@ def install(precision: str = "bf16"):
              (_C, "route_prep", _route_prep), (_C, "linear_fwd_grouped", _linear_fwd_grouped),
              (_C, "loss_stats", _loss_stats), (_C, "loss_combine", _loss_combine), (_C, "loss_grad", _loss_grad),
              (_C, "gategrad_workspace_bytes", lambda n, k, c: 4),
+             (_C, "gategrad_grouped", _gategrad_grouped),
+             (_C, "gategrad_grouped_workspace_bytes", lambda n, k, g, c: 4),
              (_C, "set_gategrad_sm_reserve", lambda n: None), (_C, "set_gemm_sm_reserve", lambda n: None),
              (_MixedQuantBase, "_gategrad_workspace", lambda self, dev: None)]
     if precision == "fp32":

@@ -232,3 +232,96 @@ def test_deferred_and_chunked_input_grad_gloo_tp2():
     # gate gradients are rank-local partial sums (the trainer all-reduces them)
     for n in ("q", "k", "o"):
         assert torch.allclose(res[0]["deferred"][n] + res[1]["deferred"][n], ref[n], rtol=0.02, atol=1e-3), n
+
+
+class _GroupedBlock(nn.Module):
+    """q and k as one grouped gated projection: y = o(tanh(q x) * k x)."""
+
+    def __init__(self, q, k, o, grouped: bool):
+        super().__init__()
+        self.q, self.k, self.o, self.grouped = q, k, o, grouped
+
+    def forward(self, x):
+        from voodoo_quant.layers import gated_linear_group
+
+        if self.grouped:
+            qk = gated_linear_group([self.q, self.k], x)
+            q, k = qk.split([self.q.out_features, self.k.out_features], dim=-1)
+        else:
+            q, k = self.q(x), self.k(x)
+        return self.o(torch.tanh(q.float()).to(torch.bfloat16) * k)
+
+
+def test_grouped_gategrads_direct_and_deferred():
+    """The gate gradients of a grouped q|k projection come from one grouped
+    gate-gradient call -- written straight into the gate bank's gradient rows
+    when deferred -- and equal those of the separate layers."""
+    from voodoo_quant import _C, layers
+    from voodoo_quant import parallel as P
+    from voodoo_quant.layers import GateBank, groupable
+
+    undo = _install_fakes()
+    calls = []
+    saved_mix, saved_grp = _C.__dict__.get("mix"), _C.__dict__.get("gategrad_grouped")
+
+    def mix(qtypes, qbytes, probs, rows, padded, cols, out=None):
+        w = (probs.float().view(-1, 1, 1) * torch.stack(qbytes)).sum(0).to(torch.bfloat16)
+        if out is None:
+            return w
+        out[:, :cols].copy_(w[:, :cols])
+        return out
+
+    def gategrad_grouped(dy, x, qtypes, qbytes_per_layer, rows, in_features, padded_cols, workspace=None, out=None):
+        calls.append(tuple(rows))
+        g, a = [], 0
+        for n, qb in zip(rows, qbytes_per_layer):
+            g.append(_C.gategrad(dy[:, a:a + n], x, qtypes, qb, n, in_features, padded_cols))
+            a += n
+        g = torch.stack(g)
+        if out is None:
+            return g
+        out.copy_(g)
+        return out
+
+    _C.mix, _C.gategrad_grouped = mix, gategrad_grouped
+    _C.gategrad_grouped_workspace_bytes = lambda n, k, g, c: 4
+    try:
+        d, h = 256, 512
+        gen = torch.Generator().manual_seed(11)
+        wq, wk = (torch.randn(h, d, generator=gen) * 0.05 for _ in range(2))
+        wo = torch.randn(d, h, generator=gen) * 0.05
+        res = {}
+        for grouped, defer in ((False, False), (True, False), (True, True)):
+            blk = _GroupedBlock(_gated(d, h, wq, "b.q"), _gated(d, h, wk, "b.k"), _gated(h, d, wo, "b.o"), grouped)
+            if grouped:
+                assert groupable([blk.q, blk.k])
+            root = nn.ModuleDict({"blk": blk})
+            P._install_input_copy(blk)
+            if defer:
+                assert P.mark_deferred_gategrads(root) == 3
+            bank = GateBank({"q": blk.q, "k": blk.k, "o": blk.o})
+            g = torch.Generator().manual_seed(5)
+            x = torch.randn(2, 300, d, generator=g).to(torch.bfloat16).requires_grad_(True)
+            gy = torch.randn(2, 300, d, generator=g)
+            bank.probs()
+            del calls[:]
+            loss = (blk(x).float() * gy).sum()
+            loss.backward()
+            bank.release()
+            assert not layers.has_deferred_gategrads()
+            assert calls == ([(h, h)] if grouped else []), calls
+            res[(grouped, defer)] = {"x": x.grad.float().clone(),
+                                     **{n: getattr(blk, n).gates.grad.clone() for n in ("q", "k", "o")}}
+    finally:
+        for name, old in (("mix", saved_mix), ("gategrad_grouped", saved_grp)):
+            setattr(_C, name, old)
+        del _C.gategrad_grouped_workspace_bytes
+        undo()
+    base = res[(False, False)]
+    for key in ((True, False), (True, True)):
+        # dX: one GEMM over both layers' columns instead of two bf16 dX added
+        assert float((res[key]["x"] - base["x"]).norm()) <= 1e-2 * float(base["x"].norm()), key
+        for n in ("q", "k", "o"):
+            assert torch.allclose(res[key][n], base[n], rtol=1e-5, atol=1e-6), (key, n)
+    for n in ("q", "k", "o"):
+        assert torch.equal(res[(True, False)][n], res[(True, True)][n]), n

@@ -170,9 +170,9 @@ def test_grouped_gated_projection_matches_separate_layers(cuda, outs):
     """q/k/v (or gate/up) as one grouped GEMM: the output columns equal each
     layer's own forward (the same mixture and dot products per output
     element; 1e-3 relative), dX equals the sum of the layers' dX within bf16
-    rounding of the partial sums (1e-2 relative), and each layer's gate
-    gradient is the same gate-gradient GEMM over its column range
-    (bit-identical)."""
+    rounding of the partial sums (1e-2 relative), and the layers' gate
+    gradients, from one grouped gate-gradient GEMM, equal each layer's own
+    within the order of fp32 partial sums (1e-4 relative)."""
     from voodoo_quant.layers import gated_linear_group, groupable
 
     types = ["Q2_K", "Q4_K", "Q6_K", "Q8_0"]
@@ -198,7 +198,7 @@ def test_grouped_gated_projection_matches_separate_layers(cuda, outs):
     assert _rel(ya, yb) < 1e-3
     assert _rel(xa.grad, xb.grad) < 1e-2
     for a, b in zip(ga, gb):
-        assert torch.equal(a, b)
+        assert _rel(a, b) < 1e-4
 
 
 def test_grouped_q8_teacher_projection_matches_separate_layers(cuda):

@@ -454,6 +454,42 @@ def test_gategrad_stream_k_tail_matches_fp64(cuda, T, N, IN):
     assert _C.device_error() == 0
 
 
+@pytest.mark.parametrize("T,rows,IN", [(2048, (512, 128, 128), 4096), (1000, (1792, 1792), 2048),
+                                       (300, (256, 32), 512)])
+def test_gategrad_grouped_matches_fp64(cuda, T, rows, IN):
+    """Layers side by side in dY's columns (q/k/v, gate/up) through one
+    grouped gate-gradient GEMM: each layer's gradients against fp64
+    <dy_g^T x, W_{g,k}> (1e-3 relative), written `ld` floats apart into a
+    wider buffer whose other entries stay untouched, and within 1e-4 of
+    the per-layer launches (fp32 partial sums split differently along K)."""
+    from voodoo_quant import _C
+    from voodoo_quant.quants import rtn
+
+    types = ["Q3_K", "Q4_K", "Q6_K", "Q8_0"]
+    g = torch.Generator(device="cpu").manual_seed(T + IN)
+    blocks = []
+    for n in rows:
+        w = torch.randn(n, IN, generator=g) * 0.02
+        blocks.append([rtn.quantize(w, q).to(cuda) for q in types])
+    x = _bf16(torch.randn(T, IN, generator=g)).to(cuda)
+    dy = _bf16(torch.randn(T, sum(rows), generator=g)).to(cuda)
+    buf = torch.full((len(rows), 8), 7.0, device=cuda)
+    got = _C.gategrad_grouped(dy, x, types, blocks, list(rows), IN, IN, out=buf[:, :len(types)])
+    assert torch.all(buf[:, len(types):] == 7.0)
+    a = 0
+    for i, n in enumerate(rows):
+        dw = dy[:, a:a + n].double().T @ x.double()
+        ref = torch.stack([(dw * _C.dequant(b, q, n, IN).double()).sum() for q, b in zip(types, blocks[i])])
+        assert rel_err(got[i].double().cpu().numpy(), ref.cpu().numpy()) < 1e-3, i
+        one = _C.gategrad(dy[:, a:a + n], x, types, blocks[i], n, IN, IN)
+        assert rel_err(got[i].cpu().numpy(), one.cpu().numpy()) < 1e-4, i
+        a += n
+    assert torch.equal(got, _C.gategrad_grouped(dy, x, types, blocks, list(rows), IN, IN))
+    with pytest.raises(ValueError):
+        _C.gategrad_grouped(dy[:, :sum(rows) - 16], x, types, blocks, [rows[0], rows[1] - 16] + list(rows[2:]), IN, IN)
+    assert _C.device_error() == 0
+
+
 def test_sm_reserve_keeps_results(cuda):
     """GEMMs that leave SMs free for a concurrent collective
     (vq_set_gemm_sm_reserve, vq_set_gategrad_sm_reserve) compute the same

@@ -55,6 +55,8 @@ constexpr int kStagePitch = kMaxUnitWords + 1;  // 69 words
 constexpr int kStagePitch1 = 53;
 // One bulk-store buffer of the paired store epilogue: 32 rows x 32 bf16.
 constexpr int kOutBufBytes = 32 * 32 * 2;
+// Layers of one grouped gate-gradient launch (q/k/v, gate/up).
+constexpr int kMaxGGroups = 4;
 
 // Two floats rounded to bf16 (nearest even), packed low = a, high = b.
 __device__ __forceinline__ uint32_t bf16x2_bits(float a, float b) {
@@ -102,6 +104,14 @@ struct Params {
   // of A are multiplied with B_g; ngroups = 0 for a plain GEMM
   const int* group_off;
   int ngroups;
+  // grouped gate gradient: gg_groups > 1 layers stacked by rows (dY's
+  // columns), layer g owning rows [gg_row[g], gg_row[g + 1]) (multiples of
+  // 32, so each epilogue warp's rows belong to one layer) with candidates
+  // gg_ptr[g][k] of the formats in `cands`; partial slots hold gg_groups x K
+  // values, layer g's at g * K, zero for the layers a warp does not cover
+  int gg_groups;
+  int gg_row[kMaxGGroups + 1];
+  const uint8_t* gg_ptr[kMaxGGroups][kMaxCandidates];
   int* err;
 };
 
@@ -371,10 +381,18 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, uint8_t* stage, u
     const long long slot =
         slot_override >= 0 ? slot_override : (static_cast<long long>(m128) * p.num_n_blk + n_blk) * 4 + wq;
     const long long colbase = static_cast<long long>(n_blk) * BN;
-    const long long urow = (row_ok ? row : 0) * p.units_per_row + n_blk;
+    int gi = 0;  // layer of this warp's rows (grouped launch)
+    long long lrow = row;
+    if (p.gg_groups > 1) {
+      while (gi + 1 < p.gg_groups && row0 >= p.gg_row[gi + 1]) ++gi;
+      lrow = row - p.gg_row[gi];
+    }
+    const int KK = p.gg_groups > 1 ? p.gg_groups * p.cands.K : p.cands.K;
+    const long long urow = (row_ok ? lrow : 0) * p.units_per_row + n_blk;
     for (int k = 0; k < p.cands.K; ++k) {
       if (cand_set >= 0 && ((p.set1_mask >> k) & 1) != cand_set) continue;
-      stage_row_lane(slot_row, p.cands.ptr[k] + urow * p.cands.ubytes[k], p.cands.ubytes[k]);
+      const uint8_t* base = p.gg_groups > 1 ? p.gg_ptr[gi][k] : p.cands.ptr[k];
+      stage_row_lane(slot_row, base + urow * p.cands.ubytes[k], p.cands.ubytes[k]);
       float s = 0.f;
       switch (p.cands.fmt[k]) {
         case kQ8_0: s = row_dot<kQ8_0>(slot_row, t_row, colbase, p.cols, row_ok); break;
@@ -388,7 +406,10 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, uint8_t* stage, u
       }
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-      if (lane == 0) p.partials[slot * p.cands.K + k] = s;
+      if (lane == 0) {
+        float* dst = p.partials + slot * KK + k;
+        for (int g = 0; g < KK / p.cands.K; ++g) dst[g * p.cands.K] = g == gi ? s : 0.f;
+      }
       __syncwarp();
     }
   }
@@ -809,8 +830,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<kEpi>::kThre
       for (int j = 0; j < 2; ++j) {
         if (sk_written[j]) continue;
         const long long slot = p.sk_base + ((static_cast<long long>(cluster_id) * 2 + j) * 2 + rank) * 4 + wq;
+        const int ng = p.gg_groups > 1 ? p.gg_groups : 1;
         for (int k = 0; k < p.cands.K; ++k)
-          if (kSets == 1 || ((p.set1_mask >> k) & 1) == eset) p.partials[slot * p.cands.K + k] = 0.f;
+          if (kSets == 1 || ((p.set1_mask >> k) & 1) == eset)
+            for (int g = 0; g < ng; ++g) p.partials[(slot * ng + g) * p.cands.K + k] = 0.f;
       }
     }
   }
@@ -824,24 +847,26 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<kEpi>::kThre
   }
 }
 
-// grad_p[k] = sum over slots (in slot order) of partials[slot][k], in fp64;
-// a slot is one (tile, epilogue warp) pair.  One CTA per candidate; the
+// grad_p[c / K * ld + c % K] = sum over slots (in slot order) of
+// partials[slot][c], c < KK (KK = K, or layers x K for a grouped launch, each
+// layer's K gradients written ld floats after the previous layer's), in fp64;
+// a slot is one (tile, epilogue warp) pair.  One CTA per value; the
 // per-thread strided sums and the tree below have a fixed shape, so the
 // result is deterministic.
 __global__ void __launch_bounds__(512) gategrad_reduce_kernel(const float* __restrict__ partials, int num_slots,
-                                                              int K, float* __restrict__ grad_p) {
+                                                              int KK, int K, long long ld, float* __restrict__ grad_p) {
   __shared__ double sh[512];
   const int k = blockIdx.x;
   double s = 0.0;
   for (int t = threadIdx.x; t < num_slots; t += blockDim.x)
-    s += static_cast<double>(partials[static_cast<long long>(t) * K + k]);
+    s += static_cast<double>(partials[static_cast<long long>(t) * KK + k]);
   sh[threadIdx.x] = s;
   __syncthreads();
   for (int w = blockDim.x / 2; w > 0; w >>= 1) {
     if (threadIdx.x < w) sh[threadIdx.x] += sh[threadIdx.x + w];
     __syncthreads();
   }
-  if (threadIdx.x == 0) grad_p[k] = static_cast<float>(sh[0]);
+  if (threadIdx.x == 0) grad_p[(k / K) * ld + k % K] = static_cast<float>(sh[0]);
 }
 
 }  // namespace gemm

@@ -546,7 +546,73 @@ int vq_gategrad(const void* dy, int64_t lddy, const void* x, int64_t ldx, int64_
   long long used = 0;
   if (int rc = launch_gemm<true, true, vq::gemm::kEpiGateGrad>(ta, tb, p, st, &used)) return rc;
   const int slots = static_cast<int>(used);
-  vq::gemm::gategrad_reduce_kernel<<<K, 512, 0, st>>>(p.partials, slots, K, grad_probs);
+  vq::gemm::gategrad_reduce_kernel<<<K, 512, 0, st>>>(p.partials, slots, K, K, K, grad_probs);
+  VQ_CUDA(cudaGetLastError());
+  return 0;
+}
+
+size_t vq_gategrad_grouped_workspace_bytes(int64_t N_total, int64_t Kin, int G, int K) {
+  if (N_total <= 0 || Kin <= 0 || G <= 0 || K <= 0) return 0;
+  return static_cast<size_t>(gategrad_slots(N_total, Kin)) * G * K * sizeof(float);
+}
+
+int vq_gategrad_grouped(const void* dy, int64_t lddy, const void* x, int64_t ldx, int64_t T, int G,
+                        const int64_t* rows, int64_t Kin, int K, const int* types, const void* const* blocks,
+                        int64_t padded_cols, void* workspace, size_t workspace_bytes, float* grad_probs,
+                        int64_t ld_grad, void* stream) {
+  DeviceScope scope(grad_probs);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  using vq::gemm::kMaxGGroups;
+  if (G < 1 || G > kMaxGGroups) return fail(VQ_ERR_INVALID, "layers %d not in [1, %d]", G, kMaxGGroups);
+  if (rows == nullptr || blocks == nullptr) return fail(VQ_ERR_INVALID, "null row-count or block array");
+  if (grad_probs == nullptr) return fail(VQ_ERR_INVALID, "null grad_probs");
+  if (ld_grad < K) return fail(VQ_ERR_INVALID, "grad_probs row stride %lld < K = %d", (long long)ld_grad, K);
+  vq::CandSet cs;
+  if (int rc = build_candset(&cs, K, types, blocks)) return rc;
+  int64_t N = 0;
+  for (int g = 0; g < G; ++g) {
+    if (rows[g] <= 0 || rows[g] % 32 != 0)
+      return fail(VQ_ERR_INVALID, "layer %d: %lld rows, not a positive multiple of 32", g, (long long)rows[g]);
+    vq::CandSet cg;
+    if (int rc = build_candset(&cg, K, types, blocks + static_cast<size_t>(g) * K)) return rc;
+    N += rows[g];
+  }
+  if (int rc = check_matrix(dy, T, N, lddy, "dy")) return rc;
+  if (int rc = check_matrix(x, T, Kin, ldx, "x")) return rc;
+  if (padded_cols < Kin || padded_cols % 256 != 0)
+    return fail(VQ_ERR_INVALID, "padded in_features %lld must be a multiple of 256 and >= %lld", (long long)padded_cols,
+                (long long)Kin);
+  if (T == 0 || Kin == 0) {
+    for (int g = 0; g < G; ++g) VQ_CUDA(cudaMemsetAsync(grad_probs + g * ld_grad, 0, sizeof(float) * K, st));
+    return 0;
+  }
+  if (T > 0x7fffffff || N > 0x7fffffff || Kin > 0x7fffffff) return fail(VQ_ERR_INVALID, "dimension too large");
+  const size_t need = vq_gategrad_grouped_workspace_bytes(N, Kin, G, K);
+  if (workspace == nullptr || workspace_bytes < need)
+    return fail(VQ_ERR_INVALID, "grouped gate-grad workspace of %zu bytes required, got %zu", need, workspace_bytes);
+  CUtensorMap ta, tb;
+  if (int rc = make_map(&ta, dy, T, N, lddy, 64)) return rc;
+  if (int rc = make_map(&tb, x, T, Kin, ldx, 64)) return rc;
+  vq::gemm::Params p{};
+  p.M = static_cast<int>(N);
+  p.N = static_cast<int>(Kin);
+  p.K = static_cast<int>(T);
+  p.cands = cs;
+  p.units_per_row = static_cast<int>(padded_cols / 256);
+  p.cols = Kin;
+  p.partials = static_cast<float*>(workspace);
+  p.set1_mask = gategrad_set_split(K, types);
+  p.gg_groups = G;
+  p.gg_row[0] = 0;
+  for (int g = 0; g < G; ++g) {
+    p.gg_row[g + 1] = p.gg_row[g] + static_cast<int>(rows[g]);
+    for (int k = 0; k < K; ++k) p.gg_ptr[g][k] = static_cast<const uint8_t*>(blocks[static_cast<size_t>(g) * K + k]);
+  }
+  if (int rc = device_error_ptr(&p.err)) return rc;
+  long long used = 0;
+  if (int rc = launch_gemm<true, true, vq::gemm::kEpiGateGrad>(ta, tb, p, st, &used)) return rc;
+  vq::gemm::gategrad_reduce_kernel<<<G * K, 512, 0, st>>>(p.partials, static_cast<int>(used), G * K, K, ld_grad,
+                                                          grad_probs);
   VQ_CUDA(cudaGetLastError());
   return 0;
 }

@@ -54,6 +54,9 @@ def _declare(lib):
         "vq_gategrad": (_int, [_vp, _i64, _vp, _i64, _i64, _i64, _i64, _int, _vp, _vp, _i64, _vp,
                                ctypes.c_size_t, _vp, _vp]),
         "vq_gategrad_noalloc": (_int, [_vp, _i64, _vp, _i64, _i64, _i64, _i64, _int, _vp, _vp, _i64, _vp, _vp]),
+        "vq_gategrad_grouped_workspace_bytes": (ctypes.c_size_t, [_i64, _i64, _int, _int]),
+        "vq_gategrad_grouped": (_int, [_vp, _i64, _vp, _i64, _i64, _int, _vp, _i64, _int, _vp, _vp, _i64, _vp,
+                                       ctypes.c_size_t, _vp, _i64, _vp]),
         "vq_mixgemm_fwd": (_int, [_vp, _i64, _i64, _i64, _int, _vp, _vp, _vp, _i64, _i64, _vp, _i64, _vp,
                                   _i64, _vp]),
         "vq_mixgemm_dx": (_int, [_vp, _i64, _i64, _i64, _int, _vp, _vp, _vp, _i64, _i64, _vp, _i64, _vp,
@@ -82,6 +85,7 @@ def _declare(lib):
 EXPORTED = (
     "vq_last_error", "vq_abi_version", "vq_format_info", "vq_device_error", "vq_dequant", "vq_mix",
     "vq_linear_fwd", "vq_linear_fwd_grouped", "vq_set_gategrad_sm_reserve", "vq_set_gemm_sm_reserve", "vq_quantize", "vq_route_prep", "vq_linear_dx", "vq_gategrad_workspace_bytes", "vq_gategrad", "vq_gategrad_noalloc",
+    "vq_gategrad_grouped_workspace_bytes", "vq_gategrad_grouped",
     "vq_mixgemm_fwd", "vq_mixgemm_dx",
     "vq_loss_fused", "vq_loss_stats", "vq_loss_combine", "vq_loss_grad",
     "vq_rmsnorm_fwd", "vq_rmsnorm_bwd", "vq_add_rmsnorm_fwd", "vq_rmsnorm_bwd_add", "vq_rope", "vq_swiglu_fwd", "vq_swiglu_bwd",
@@ -320,6 +324,38 @@ def gategrad_noalloc(dy: torch.Tensor, x: torch.Tensor, qtypes, qbytes, n_out: i
 
 def gategrad_workspace_bytes(n_out: int, in_features: int, K: int) -> int:
     return int(load_library().vq_gategrad_workspace_bytes(n_out, in_features, K))
+
+
+def gategrad_grouped_workspace_bytes(n_total: int, in_features: int, G: int, K: int) -> int:
+    return int(load_library().vq_gategrad_grouped_workspace_bytes(n_total, in_features, G, K))
+
+
+def gategrad_grouped(dy: torch.Tensor, x: torch.Tensor, qtypes, qbytes_per_layer, rows, in_features: int,
+                     padded_cols: int, workspace: torch.Tensor | None = None,
+                     out: torch.Tensor | None = None) -> torch.Tensor:
+    """grad[g, k] = <dy_g^T x, W_{g,k}> for layers g side by side in dy's
+    columns (rows[g] each, a multiple of 32), all with the formats `qtypes`:
+    one gate-gradient GEMM (float32 [G, K], into `out` -- rows K floats
+    apart or further, unit column stride -- when given)."""
+    G = len(rows)
+    _require_cuda(dy, x, *[b for bs in qbytes_per_layer for b in bs])
+    dy = _as_operand(dy)
+    x = _as_operand(x)
+    K = len(qtypes)
+    types = (_int * K)(*[GGML_TYPE[q] for q in qtypes])
+    ptrs = (_vp * (G * K))(*[b.data_ptr() for bs in qbytes_per_layer for b in bs])
+    rws = (ctypes.c_int64 * G)(*[int(r) for r in rows])
+    need = _lib.vq_gategrad_grouped_workspace_bytes(sum(rows), in_features, G, K)
+    if workspace is None or workspace.numel() * workspace.element_size() < need:
+        workspace = torch.empty(max(need, 4), dtype=torch.uint8, device=x.device)
+    if out is None:
+        out = torch.empty(G, K, dtype=torch.float32, device=x.device)
+    elif out.dtype != torch.float32 or out.dim() != 2 or tuple(out.shape) != (G, K) or out.stride(1) != 1:
+        raise ValueError("gategrad_grouped: out must be float32 [G, K] with unit column stride")
+    _check(_lib.vq_gategrad_grouped(dy.data_ptr(), dy.stride(0), x.data_ptr(), x.stride(0), x.shape[0], G, rws,
+                                    in_features, K, types, ptrs, padded_cols, workspace.data_ptr(), workspace.numel(),
+                                    out.data_ptr(), out.stride(0), _stream(x)))
+    return out
 
 
 def loss_fused(s: torch.Tensor, t: torch.Tensor, targets: torch.Tensor, temperature: float, ce_weight: float,

@@ -341,9 +341,66 @@ def _gategrad_into(dy2, x2, layer, out=None, reserve: int = 0) -> torch.Tensor:
             _C.set_gategrad_sm_reserve(0)
 
 
+def _gg_groupable(layers) -> bool:
+    """Whether the gate gradients of gated Linears that share an input run as
+    one grouped gate-gradient GEMM: two to four layers, the same candidate
+    formats and padded width, each a multiple of 32 output rows."""
+    l0 = layers[0]
+    return 2 <= len(layers) <= 4 and all(
+        l.candidate_types == l0.candidate_types and l.padded_in_features == l0.padded_in_features and
+        l.out_features % 32 == 0 and not l.in_col_offset for l in layers)
+
+
+def _gategrad_group_into(dy2, x2, layers, out=None, reserve: int = 0) -> torch.Tensor:
+    """[G, K] gate gradients of `layers` (outputs side by side in dy2's
+    columns) from one grouped gate-gradient GEMM."""
+    l0 = layers[0]
+    rows = [l.out_features for l in layers]
+    need = _C.gategrad_grouped_workspace_bytes(sum(rows), l0.in_features, len(layers), l0.num_candidates)
+    ws = getattr(l0, "_gws", None)
+    if ws is None or ws.device != x2.device or ws.numel() < need:
+        ws = torch.empty(max(need, 4), dtype=torch.uint8, device=x2.device)
+        l0._gws = ws
+    if reserve:
+        _C.set_gategrad_sm_reserve(reserve)
+    try:
+        return _C.gategrad_grouped(dy2, x2, l0.candidate_types, [l._candidate_blocks() for l in layers], rows,
+                                   l0.in_features, l0.padded_in_features, workspace=ws, out=out)
+    finally:
+        if reserve:
+            _C.set_gategrad_sm_reserve(0)
+
+
+def _group_rows_view(slots):
+    """The bank-gradient rows `slots` as one [G, K] view when they are
+    consecutive rows of one buffer, else None."""
+    s0 = slots[0]
+    if s0.dim() != 1 or s0.stride(0) != 1:
+        return None
+    base = s0._base if s0._base is not None else None
+    if base is None or base.dim() != 2:
+        return None
+    ld = base.stride(0)
+    for i, s in enumerate(slots):
+        if s.numel() != s0.numel() or s.data_ptr() != s0.data_ptr() + i * ld * s0.element_size():
+            return None
+    return s0.as_strided((len(slots), s0.numel()), (ld, 1))
+
+
+def _group_gategrad_to_slots(dy2, x2, layers, slots, reserve: int = 0) -> None:
+    view = _group_rows_view(slots)
+    if view is not None:
+        _gategrad_group_into(dy2, x2, layers, out=view, reserve=reserve)
+        return
+    g = _gategrad_group_into(dy2, x2, layers, reserve=reserve)
+    for i, s in enumerate(slots):
+        s.copy_(g[i])
+
+
 # Gate-gradient GEMMs deferred until the all-reduce of their module's input
 # gradient is in flight (TP): (dY, X, layer, destination row of the bank's
-# gradient buffer).  parallel._CopyToParallel.backward launches that
+# gradient buffer), or (dY, X, tuple of layers, list of their rows) for a
+# grouped gate-gradient GEMM.  parallel._CopyToParallel.backward launches that
 # all-reduce asynchronously and then runs these beside it; the gate bank's
 # backward runs what is left, so every deferred GEMM precedes its reader.
 _DEFERRED: list = []
@@ -363,6 +420,10 @@ def flush_deferred_gategrads(overlap_bytes: int = 0) -> None:
     items = list(_DEFERRED)
     _DEFERRED.clear()
     for dy2, x2, layer, out in items:
+        if isinstance(layer, tuple):
+            _group_gategrad_to_slots(dy2, x2, layer, out, reserve=sms if budget > 0 else 0)
+            budget -= 2.0 * x2.shape[0] * sum(l.out_features for l in layer) * layer[0].in_features / 1.2e15
+            continue
         _gategrad_into(dy2, x2, layer, out=out, reserve=sms if budget > 0 else 0)
         budget -= 2.0 * x2.shape[0] * layer.out_features * layer.in_features / 1.2e15
 
@@ -457,6 +518,16 @@ class _GroupedGatedLinearFunction(Function):
             dx = _C.linear_dx(dy2, w_cat, layers[0].in_features)
             dx = dx.to(ctx.x_dtype).reshape(ctx.x_shape)
         ctx.w_cat = None
+        need = [ctx.needs_input_grad[2 + i] for i in range(len(layers))]
+        if all(need) and _gg_groupable(layers):
+            # every layer's gate gradient from one GEMM over all of dY's columns
+            slots = [_defer_slot(l) for l in layers]
+            if all(s is not None for s in slots):  # beside the all-reduce of the input gradient
+                _DEFERRED.append((dy2, x2, tuple(layers), slots))
+                return (dx, None, *([None] * len(layers)))
+            if all(s is None for s in slots):
+                g = _gategrad_group_into(dy2, x2, layers)
+                return (dx, None, *[g[i].to(p.dtype) for i, p in enumerate(probs)])
         grads = []
         a = 0
         for i, layer in enumerate(layers):
