@@ -988,6 +988,12 @@ def run_model_step(args):
     launches = _count_our_launches(lambda: step_fn(x, y))
     if args.profile_step:
         _print_step_profile(lambda: step_fn(x, y)) if rank == 0 else step_fn(x, y)
+    if args.ncu_step:  # one more step inside cudaProfilerStart/Stop, for ncu --profile-from-start off
+        torch.cuda.synchronize()
+        torch.cuda.profiler.start()
+        step_fn(x, y)
+        torch.cuda.synchronize()
+        torch.cuda.profiler.stop()
     torch.cuda.synchronize()
 
     if rank == 0:
@@ -1285,6 +1291,9 @@ def main():
     ap.add_argument("--layers", type=int, default=0,
                     help="step workloads: build only this many decoder layers (a smoke run of the build, "
                          "memory plan and step; its line says so and is not the configuration's number)")
+    ap.add_argument("--ncu-step", action="store_true",
+                    help="step workloads: after the timed region, run one more step between cudaProfilerStart and "
+                         "cudaProfilerStop (for ncu --profile-from-start off: that step's launches only)")
     ap.add_argument("--profile-step", action="store_true",
                     help="step workloads: print device time per kernel name for one step")
     ap.add_argument("--ncu-case", nargs="?", const="config2", default=None, choices=["config2", "tp8"],

@@ -2,6 +2,7 @@
 
 from __future__ import annotations
 
+import os
 import sys
 from pathlib import Path
 
@@ -13,6 +14,13 @@ for p in (ROOT, ROOT / "voodoo-dyn-quant_b200"):
         sys.path.insert(0, str(p))
 
 GOLDEN = ROOT / "tests" / "golden"
+
+# Multi-process CPU tests (gloo ranks started with spawn) run 2-4 torch
+# processes side by side; each would otherwise start one thread per core and
+# the ranks slow each other down several-fold.  Children read this at import;
+# this process keeps its own thread count.
+if "OMP_NUM_THREADS" not in os.environ:
+    os.environ["OMP_NUM_THREADS"] = str(max(1, (os.cpu_count() or 4) // 4))
 
 
 def pytest_configure(config):
