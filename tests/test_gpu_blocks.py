@@ -151,6 +151,44 @@ def test_fused_llama_blocks_match_unpatched_model(cuda):
     assert cosine(e_fus.grad.double().flatten().cpu().numpy(), e_ref.grad.double().flatten().cpu().numpy()) > 0.999
 
 
+def test_chained_residual_adds_match_layer_by_layer(cuda):
+    """With causal_batches the LlamaModel forward hands each layer's MLP
+    output to the next RMSNorm unsummed (one add + norm kernel): logits
+    bit-identical to the layer-by-layer fused forward (the same bf16 sums and
+    norms), the embedding's gradient within bf16 rounding of it (the two
+    gradient branches of a residual sum added in fp32 before one rounding),
+    and both close to the unpatched Hugging Face model."""
+    from voodoo_quant.fused_blocks import fuse_llama_blocks
+    from voodoo_quant.training import synthetic as S
+
+    shape = S.ModelShape(3, 512, 4, 2, 1536, 2048, False, head_dim=128, batch=2, seq=64)
+    ref = S.build_llama(shape, cuda, seed=4)
+    m = S.build_llama(shape, cuda, seed=4)
+    assert fuse_llama_blocks(m, causal_batches=True) == 3 * 5 + 1 + 1
+    x, _ = S.random_tokens(shape, cuda, seed=5)
+    gy = torch.randn(shape.batch, shape.seq, shape.vocab, generator=torch.Generator(device=cuda).manual_seed(6),
+                     device=cuda)
+
+    def run(model):
+        model.zero_grad(set_to_none=True)
+        logits = model(input_ids=x, use_cache=False).logits
+        logits.backward(gy.to(logits.dtype))
+        return logits.detach(), model.model.embed_tokens.weight.grad.detach().clone()
+
+    l_chain, g_chain = run(m)
+    chained = m.model.forward
+    m.model.forward = m.model._vq_chain_orig_forward
+    try:
+        l_layer, g_layer = run(m)
+    finally:
+        m.model.forward = chained
+    l_ref, g_ref = run(ref)
+    assert torch.equal(l_chain, l_layer)
+    assert _rel(g_chain, g_layer) < 1e-2
+    assert _rel(l_chain, l_ref) < 1e-2 and _rel(g_chain, g_ref) < 2e-2
+    assert cosine(g_chain.double().flatten().cpu().numpy(), g_ref.double().flatten().cpu().numpy()) > 0.999
+
+
 def _gated(cuda, n_out, n_in, types, seed):
     from voodoo_quant.layers import MixedQuantLinear
     from voodoo_quant.quants import rtn

@@ -32,8 +32,7 @@ struct V8 {  // 8 bf16 values widened to fp32
   float v[8];
 };
 
-__device__ __forceinline__ V8 load8(const __nv_bfloat16* p) {
-  const uint4 raw = *reinterpret_cast<const uint4*>(p);
+__device__ __forceinline__ V8 widen8(const uint4& raw) {
   const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
   V8 r;
 #pragma unroll
@@ -44,6 +43,8 @@ __device__ __forceinline__ V8 load8(const __nv_bfloat16* p) {
   }
   return r;
 }
+
+__device__ __forceinline__ V8 load8(const __nv_bfloat16* p) { return widen8(*reinterpret_cast<const uint4*>(p)); }
 
 __device__ __forceinline__ void store8(__nv_bfloat16* p, const V8& r) {
   uint4 raw;
@@ -121,8 +122,11 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_fwd_kernel(const __nv_bf
 
 // kAdd: dx = (the norm's input gradient) + dres in fp32, rounded once: the
 // gradient of a residual sum h that feeds both the norm and a later add.
+// x and dy stay in registers as raw bf16 between the two passes (4 registers
+// per 8 values instead of 8), so more rows are in flight per SM; the second
+// pass widens them again and recomputes x*r and dy*w exactly as the first.
 template <int VPT, bool kAdd = false>
-__global__ void __launch_bounds__(kNormThreads) rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ x, long long ldx,
+__global__ void __launch_bounds__(kNormThreads, VPT <= 4 ? 8 : 4) rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ x, long long ldx,
                                                                   const __nv_bfloat16* __restrict__ dy, long long lddy,
                                                                   const __nv_bfloat16* __restrict__ w,
                                                                   const float* __restrict__ rstd, int rows, int D,
@@ -135,21 +139,23 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_bwd_kernel(const __nv_bf
     const float r = rstd[row];
     const __nv_bfloat16* xr = x + static_cast<long long>(row) * ldx;
     const __nv_bfloat16* gr = dy + static_cast<long long>(row) * lddy;
-    V8 n[VPT], g[VPT];
+    uint4 xq[VPT], gq[VPT];
     float dot = 0.f;
 #pragma unroll
     for (int j = 0; j < VPT; ++j) {
       const int c = threadIdx.x + j * kNormThreads;
       if (c < nvec) {
-        n[j] = load8(xr + 8 * c);
-        g[j] = load8(gr + 8 * c);
-        const V8 wv = load8(w + 8 * c);
+        xq[j] = *reinterpret_cast<const uint4*>(xr + 8 * c);
+        gq[j] = *reinterpret_cast<const uint4*>(gr + 8 * c);
+      }
+    }
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          n[j].v[i] *= r;
-          g[j].v[i] *= wv.v[i];
-          dot = fmaf(g[j].v[i], n[j].v[i], dot);
-        }
+    for (int j = 0; j < VPT; ++j) {
+      const int c = threadIdx.x + j * kNormThreads;
+      if (c < nvec) {
+        const V8 n = widen8(xq[j]), g = widen8(gq[j]), wv = load8(w + 8 * c);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) dot = fmaf(g.v[i] * wv.v[i], n.v[i] * r, dot);
       }
     }
     const float m = block_sum(dot, red) / static_cast<float>(D);
@@ -158,9 +164,13 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_bwd_kernel(const __nv_bf
     for (int j = 0; j < VPT; ++j) {
       const int c = threadIdx.x + j * kNormThreads;
       if (c < nvec) {
+        const V8 n = widen8(xq[j]), g = widen8(gq[j]), wv = load8(w + 8 * c);
         V8 o;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) o.v[i] = r * (g[j].v[i] - n[j].v[i] * m);
+        for (int i = 0; i < 8; ++i) {
+          const float nn = n.v[i] * r, gg = g.v[i] * wv.v[i];
+          o.v[i] = r * (gg - nn * m);
+        }
         if (kAdd) {
           const V8 dv = load8(dres + static_cast<long long>(row) * lddres + 8 * c);
 #pragma unroll

@@ -275,6 +275,63 @@ def _decoder_forward(self, hidden_states: torch.Tensor, attention_mask=None, pos
     return h + self.mlp(x)
 
 
+def _norm_weights_fusable(norm) -> bool:
+    w = getattr(norm, "weight", None)
+    return (w is not None and w.is_cuda and w.dtype == torch.bfloat16 and hasattr(norm, "variance_epsilon")
+            and w.shape[-1] % 8 == 0 and w.shape[-1] <= 8192)
+
+
+def _chained_model_forward(self, input_ids=None, attention_mask=None, position_ids=None, past_key_values=None,
+                           inputs_embeds=None, use_cache=None, **kwargs):
+    """Hugging Face LlamaModel.forward for whole causal batches (the
+    distillation step) with every residual add fused into the RMSNorm that
+    reads its sum: a layer hands its MLP output on unsummed, and the next
+    layer's input norm (or the final norm) adds it to the residual stream
+    and normalises in one kernel, as the post-attention norm already does.
+    Values are those of the layer-by-layer forward (the same bf16 sums, the
+    same norms); anything else goes to the stock forward."""
+    from transformers.modeling_outputs import BaseModelOutputWithPast
+
+    from voodoo_quant.parallel import sp_enabled
+
+    plain = (sp_enabled() or input_ids is None or inputs_embeds is not None or past_key_values is not None
+             or use_cache or attention_mask is not None or position_ids is not None
+             or kwargs.get("cache_position") is not None
+             or any(kwargs.get(k) for k in ("output_hidden_states", "output_attentions")))
+    layers = self.layers[: self.config.num_hidden_layers]
+    if not plain:
+        plain = not (_norm_weights_fusable(self.norm) and all(
+            hasattr(l, "_vq_orig_forward") and hasattr(l.self_attn, "_vq_orig_forward")
+            and hasattr(l.mlp, "_vq_orig_forward") and _norm_weights_fusable(l.input_layernorm)
+            and _norm_weights_fusable(l.post_attention_layernorm) for l in layers))
+    if plain:
+        return self._vq_chain_orig_forward(input_ids=input_ids, attention_mask=attention_mask,
+                                           position_ids=position_ids, past_key_values=past_key_values,
+                                           inputs_embeds=inputs_embeds, use_cache=use_cache, **kwargs)
+    h = self.embed_tokens(input_ids)
+    S = h.shape[1]
+    pe = self.rotary_emb(h, position_ids=torch.arange(S, device=h.device).unsqueeze(0))
+    if not _fusable(h):  # not the bf16 stream the norms expect: layer by layer
+        for layer in layers:
+            h = layer(h, position_embeddings=pe)
+        return BaseModelOutputWithPast(last_hidden_state=self.norm(h))
+    pending = None  # the previous layer's MLP output, not yet added to h
+    for layer in layers:
+        n1, n2 = layer.input_layernorm, layer.post_attention_layernorm
+        if pending is None:
+            x = rms_norm(h, n1.weight, n1.variance_epsilon)
+        else:
+            h, x = add_rms_norm(pending, h, n1.weight, n1.variance_epsilon)
+        a, _ = layer.self_attn(hidden_states=x, attention_mask=None, position_embeddings=pe)
+        h, x = add_rms_norm(a, h, n2.weight, n2.variance_epsilon)
+        pending = layer.mlp(x)
+    if pending is None:
+        out = rms_norm(h, self.norm.weight, self.norm.variance_epsilon)
+    else:
+        _, out = add_rms_norm(pending, h, self.norm.weight, self.norm.variance_epsilon)
+    return BaseModelOutputWithPast(last_hidden_state=out)
+
+
 def fuse_llama_blocks(model: torch.nn.Module, causal_batches: bool = False) -> int:
     """Route the RMSNorm, attention (rotary) and MLP (SwiGLU) modules of a
     Hugging Face Llama model through the fused kernels, and each decoder
@@ -282,7 +339,9 @@ def fuse_llama_blocks(model: torch.nn.Module, causal_batches: bool = False) -> i
     the number of modules patched.  Idempotent.  ``causal_batches``: the
     caller only ever feeds whole causal sequences without padding (the
     distillation step), so the attention ignores the causal mask Hugging Face
-    passes while a CUDA graph records and keeps the fused path."""
+    passes while a CUDA graph records and keeps the fused path, and the
+    LlamaModel forward chains every residual add into the next RMSNorm
+    (``_chained_model_forward``)."""
     from transformers.models.llama import modeling_llama as L
 
     table = ((L.LlamaRMSNorm, _rmsnorm_forward), (L.LlamaAttention, _attention_forward),
@@ -298,6 +357,10 @@ def fuse_llama_blocks(model: torch.nn.Module, causal_batches: bool = False) -> i
                 n += 1
         if type(m) is L.LlamaAttention and causal_batches:
             m._vq_causal_batches = True
+        if type(m) is L.LlamaModel and causal_batches and not hasattr(m, "_vq_chain_orig_forward"):
+            m._vq_chain_orig_forward = m.forward
+            m.forward = types.MethodType(_chained_model_forward, m)
+            n += 1
     return n
 
 
