@@ -76,6 +76,19 @@ int vq_mix(int K, const int* types, const void* const* blocks, const float* prob
 int vq_linear_fwd(const void* x, int64_t T, int64_t Kin, int64_t ldx, const void* w, int64_t N, int64_t ldw,
                   void* y, int64_t ldy, void* stream);
 
+/* K1 with the SwiGLU of a Llama MLP in its epilogue: h[T, F] =
+ * silu(x w_gate^T) * (x w_up^T), w[2F, Kin] holding the gate rows then the up
+ * rows.  Each gate/up output is rounded to bf16 before the activation, so h
+ * equals a gate|up GEMM into bf16 followed by vq_swiglu_fwd bit for bit;
+ * the [T, 2F] gate|up output is never written.  T > 128, F a multiple of
+ * 128 (VQ_ERR_UNSUPPORTED otherwise).  For forward-only (teacher) MLPs:
+ * replaces Q8Linear.forward for gate_proj and up_proj
+ * (voodoo_quant/training/q8_teacher.py:101-128) and the act_fn(gate) * up of
+ * the Hugging Face LlamaMLP.forward (transformers modeling_llama.py:183)
+ * around them. */
+int vq_linear_fwd_swiglu(const void* x, int64_t T, int64_t Kin, int64_t ldx, const void* w, int64_t F, int64_t ldw,
+                         void* h, int64_t ldh, void* stream);
+
 /* K2 -- dx[T, Kin] = dy[T, N] * w[N, Kin] (w read MN-major by TMA, no
  * transpose copy).  Replaces the input-gradient half of F.linear's autograd
  * in MixedQuantLinear.forward, voodoo_quant/layers.py:1731. */

@@ -255,6 +255,37 @@ def test_grouped_q8_teacher_projection_matches_separate_layers(cuda):
     assert _rel(y, torch.cat([m(x) for m in mods], dim=-1)) < 1e-3
 
 
+def test_teacher_mlp_swiglu_in_the_gemm_epilogue(cuda):
+    """A forward-only (teacher) MLP runs gate|up and the SwiGLU as one GEMM:
+    equal, bit for bit, to the grouped gate|up GEMM followed by the SwiGLU
+    kernel, and the fused MLP module takes that path under no_grad."""
+    from voodoo_quant.fused_blocks import _SwiGLUPairFn, _mlp_forward
+    from voodoo_quant.quants import rtn
+    from voodoo_quant.training.q8_teacher import Q8Linear, q8_linear_group, q8_swiglu_group, q8_swiglu_ok
+
+    g = torch.Generator(device="cpu").manual_seed(13)
+    mods = []
+    for n, k in ((1024, 768), (1024, 768), (768, 1024)):
+        w = torch.randn(n, k, generator=g) * 0.02
+        mods.append(Q8Linear(rtn.quantize(w, "Q8_0").to(cuda), n, k))
+    gate, up, down = mods
+    x = torch.randn(2, 150, 768, generator=g).to(cuda, torch.bfloat16)
+    assert q8_swiglu_ok(gate, up, x)
+    h = q8_swiglu_group(gate, up, x)
+    ref = _SwiGLUPairFn.apply(q8_linear_group((gate, up), x))
+    assert h.shape == (2, 150, 1024) and torch.equal(h, ref)
+
+    class _MLP(torch.nn.Module):
+        pass
+
+    mlp = _MLP()
+    mlp.gate_proj, mlp.up_proj, mlp.down_proj = gate, up, down
+    with torch.no_grad():
+        y = _mlp_forward(mlp, x)
+    assert torch.equal(y, down(ref))
+    assert not q8_swiglu_ok(gate, up, x[:, :60])  # 120 tokens: below one CTA-pair tile
+
+
 def test_swiglu_pair_backward_layout(cuda):
     """The grouped gate|up SwiGLU writes d gate | d up side by side."""
     from voodoo_quant import _C

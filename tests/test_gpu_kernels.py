@@ -220,6 +220,33 @@ def test_linear_store_edges_exact(cuda, T, N, K, ld_pad, col_off):
     assert _C.device_error() == 0
 
 
+@pytest.mark.parametrize("T,F,K,ld_pad,col_off", [(300, 256, 512, 0, 0), (4096, 1792, 4096, 0, 0),
+                                                   (1000, 1024, 1000, 16, 0), (257, 384, 256, 3, 1)])
+def test_linear_fwd_swiglu_equals_gemm_then_swiglu(cuda, T, F, K, ld_pad, col_off):
+    """The gate|up GEMM with the SwiGLU in its epilogue against the same GEMM
+    into a bf16 [T, 2F] output followed by the SwiGLU kernel: bit for bit
+    (ragged row and K tails, bulk stores and, for an unaligned output, row
+    stores), with nothing written outside the output."""
+    from voodoo_quant import _C
+
+    g = torch.Generator(device="cpu").manual_seed(T + F + K)
+    x = _bf16(torch.randn(T, K, generator=g)).to(cuda)
+    w = _bf16(torch.randn(2 * F, K, generator=g) * 0.05).to(cuda)
+    gu = _C.linear_fwd(x, w, 2 * F, K)
+    ref = _C.swiglu_fwd(gu[:, :F], gu[:, F:])
+    big = torch.full((T + 8, F + ld_pad + col_off), float("inf"), dtype=torch.bfloat16, device=cuda)
+    out = big[:T, col_off:col_off + F]
+    _C.linear_fwd_swiglu(x, w, F, K, out=out)
+    assert torch.equal(out, ref)
+    assert torch.isinf(big[T:]).all() and torch.isinf(big[:T, :col_off]).all()
+    assert torch.isinf(big[:T, col_off + F:]).all()
+    with pytest.raises(ValueError):
+        _C.linear_fwd_swiglu(x[:, :K], w[: 2 * (F - 64)], F - 64, K)  # not a multiple of 128 features
+    with pytest.raises(ValueError):
+        _C.linear_fwd_swiglu(x[:128], w, F, K)  # 128 rows: no CTA-pair tile
+    assert _C.device_error() == 0
+
+
 @pytest.mark.parametrize("types,T,N,IN", [
     (["Q4_K", "Q5_K", "Q6_K", "Q8_0"], 256, 256, 512),
     (["Q3_K", "Q4_K", "Q5_K", "Q6_K", "Q8_0"], 300, 200, 768),

@@ -43,6 +43,7 @@ constexpr int GROUP_N = 8;            // raster: tiles sweep M inside a band of 
 
 constexpr int kEpiStoreBf16 = 0;
 constexpr int kEpiGateGrad = 1;
+constexpr int kEpiSwiGLU = 2;  // paired kernel only: h = silu(gate) * up of a gate|up GEMM
 
 // Shared memory: STAGES x (A, B) operand slices, the mbarriers, and for the
 // gate-gradient epilogue one staging area per epilogue warp (32 rows x one
@@ -86,6 +87,10 @@ struct Params {
   // paired store kernel: write C through the tensor map BMaps::c (32 x 32
   // boxes, 64-byte swizzle) instead of per-row 16-byte stores
   int tma_store;
+  // kEpiSwiGLU: B holds the gate rows [0, N) and the up rows [up_row,
+  // up_row + N); a tile covers 128 output columns, the even CTA of the pair
+  // loading gate rows and the odd one the matching up rows
+  int up_row;
   // kEpiGateGrad: candidate rows = M (out features), valid columns = cols
   CandSet cands;
   int units_per_row;
@@ -339,6 +344,67 @@ __device__ __forceinline__ void epilogue_store_tma(const Params& p, const CUtens
       bulk_commit();
     }
     ++it;
+  }
+}
+
+// silu(g) * u with the operations, and the order, of the SwiGLU kernel.
+__device__ __forceinline__ float silu_mul(float g, float u) {
+  const float sg = __fdividef(1.f, 1.f + __expf(-g));
+  return g * sg * u;
+}
+
+__device__ __forceinline__ float bf16_rn(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+// SwiGLU epilogue of one warp's 32 rows: TMEM columns [0, 128) of the tile
+// are gate outputs and [128, 256) the up outputs of the same 128 features
+// (n_blk * 128 + j).  Each is rounded to bf16 first, as a GEMM writing
+// gate|up in bf16 would, so h = bf16(silu(g) * u) equals the SwiGLU
+// kernel's result on that output bit for bit.  Stored like the store
+// epilogue: a bulk tensor store per 32 x 32 box, or row by row where the
+// output map is not usable.
+__device__ __forceinline__ void epilogue_swiglu(const Params& p, const CUtensorMap* tmc, uint8_t* bufs,
+                                                uint32_t t_row, int row0, int n_blk, int lane, uint32_t& it) {
+  const long long row = static_cast<long long>(row0) + lane;
+  for (int c = 0; c < 4; ++c) {
+    const int col0 = n_blk * 128 + c * 32;
+    if (col0 >= p.N) break;  // uniform across the warp
+    float g[32], u[32];
+    tmem_ld_32cols(t_row + c * 32, g);
+    tmem_ld_32cols(t_row + 128 + c * 32, u);
+    uint32_t hb[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+      hb[j] = bf16x2_bits(silu_mul(bf16_rn(g[2 * j]), bf16_rn(u[2 * j])),
+                          silu_mul(bf16_rn(g[2 * j + 1]), bf16_rn(u[2 * j + 1])));
+    if (p.tma_store) {
+      uint8_t* buf = bufs + (it & 1u) * kOutBufBytes;
+      if (lane == 0) bulk_wait_read<1>();  // the store that last read this buffer is done with it
+      __syncwarp();
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        *reinterpret_cast<uint4*>(buf + lane * 64 + ((j ^ ((lane >> 1) & 3)) << 4)) =
+            make_uint4(hb[4 * j], hb[4 * j + 1], hb[4 * j + 2], hb[4 * j + 3]);
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        tma_store_2d(tmc, smem_u32(buf), col0, row0);
+        bulk_commit();
+      }
+      ++it;
+    } else if (row < p.M) {
+      __nv_bfloat16* dst = p.C + row * p.ldc + col0;
+      if (col0 + 32 <= p.N && ((reinterpret_cast<uintptr_t>(dst) & 15u) == 0)) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          reinterpret_cast<uint4*>(dst)[j] = make_uint4(hb[4 * j], hb[4 * j + 1], hb[4 * j + 2], hb[4 * j + 3]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (col0 + j < p.N)
+            dst[j] = __ushort_as_bfloat16(
+                static_cast<unsigned short>((j & 1) ? hb[j >> 1] >> 16 : hb[j >> 1] & 0xFFFFu));
+      }
+    }
   }
 }
 
@@ -611,8 +677,8 @@ struct PairSmemLayout {
   // store epilogue: two 2 KB bulk-store buffers per epilogue warp, 1024-byte
   // aligned (the 64-byte swizzle pattern repeats every 512 bytes)
   static constexpr int out_off = (stage_off + 1023) & ~1023;
-  static constexpr int out_bytes = (kEpi == 0) ? 4 * 2 * kOutBufBytes : 0;
-  static constexpr int total = kEpi == 0 ? out_off + out_bytes : stage_off + stage_bytes;
+  static constexpr int out_bytes = (kEpi != kEpiGateGrad) ? 4 * 2 * kOutBufBytes : 0;
+  static constexpr int total = kEpi != kEpiGateGrad ? out_off + out_bytes : stage_off + stage_bytes;
   static_assert(total <= 232448, "paired kernel shared memory above the 227 KB per-block limit");
 };
 
@@ -713,7 +779,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<kEpi>::kThre
         const CUtensorMap* bmap;
         coords(sg.tile, bmap, row_base, n_blk, row_end, m_blk);
         const int m0 = row_base + 128 * static_cast<int>(rank);
-        const int n0 = n_blk * BN + 128 * static_cast<int>(rank);
+        const int n0 = kEpi == kEpiSwiGLU ? n_blk * 128 + (rank ? p.up_row : 0)
+                                          : n_blk * BN + 128 * static_cast<int>(rank);
         for (int kb = sg.kb0; kb < sg.kb1; ++kb, ++it) {
           const int s = it % NST;
           const uint32_t ph = (it / NST) & 1u;
@@ -815,7 +882,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<kEpi>::kThre
       const int row0 = row_base + 128 * static_cast<int>(rank) + 32 * wq;
       // bulk stores clip at the output's last row, not at a group's end: a
       // warp whose rows straddle a group boundary stores row by row
-      if (kEpi == kEpiStoreBf16 && p.tma_store && (row_end == p.M || row0 + 32 <= row_end))
+      if (kEpi == kEpiSwiGLU)
+        epilogue_swiglu(p, &tmB.c, smem + SL::out_off + wq * 2 * kOutBufBytes, t_row, row0, n_blk, lane, out_it);
+      else if (kEpi == kEpiStoreBf16 && p.tma_store && (row_end == p.M || row0 + 32 <= row_end))
         epilogue_store_tma(p, &tmB.c, smem + SL::out_off + wq * 2 * kOutBufBytes, t_row, row0, n_blk, lane, out_it);
       else
         epilogue_tile<kEpi>(p, stage, t_row, row0, m128, n_blk, wq, lane, slot, row_end, kSets > 1 ? eset : -1,
@@ -824,7 +893,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<kEpi>::kThre
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(acc ? tempty_leader1 : tempty_leader0);
     }
-    if (kEpi == kEpiStoreBf16 && lane == 0) bulk_wait_all();  // no bulk store still reads shared memory
+    if (kEpi != kEpiGateGrad && lane == 0) bulk_wait_all();  // no bulk store still reads shared memory
     if (kEpi == kEpiGateGrad && p.stream_k && lane == 0) {
       // stream-K slots this cluster did not fill read as zero in the reduction
       for (int j = 0; j < 2; ++j) {

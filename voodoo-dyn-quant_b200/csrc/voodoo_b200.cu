@@ -448,6 +448,50 @@ int vq_linear_dx(const void* dy, int64_t T, int64_t N, int64_t lddy, const void*
   return launch_gemm<false, true, vq::gemm::kEpiStoreBf16>(ta, tb, p, st);
 }
 
+int vq_linear_fwd_swiglu(const void* x, int64_t T, int64_t Kin, int64_t ldx, const void* w, int64_t F, int64_t ldw,
+                         void* h, int64_t ldh, void* stream) {
+  DeviceScope scope(h);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (int rc = check_matrix(x, T, Kin, ldx, "x")) return rc;
+  if (int rc = check_matrix(w, 2 * F, Kin, ldw, "w")) return rc;
+  if (int rc = check_matrix(h, T, F, ldh, "h")) return rc;
+  if (T == 0 || F == 0) return 0;
+  if (Kin == 0) return zero_rows(h, T, F, ldh, 2, st);
+  if (T > 0x7fffffff || 2 * F > 0x7fffffff || Kin > 0x7fffffff) return fail(VQ_ERR_INVALID, "dimension too large");
+  if (!use_pair(T) || F % 128 != 0)
+    return fail(VQ_ERR_UNSUPPORTED, "fused SwiGLU GEMM needs more than %d rows and a multiple of 128 features",
+                vq::gemm::BM);
+  using namespace vq::gemm;
+  CUtensorMap ta;
+  BMaps<1> bm{};
+  if (int rc = make_map(&ta, x, T, Kin, ldx, BM)) return rc;
+  if (int rc = make_map(&bm.m[0], w, 2 * F, Kin, ldw, 128)) return rc;
+  Params p{};
+  p.M = static_cast<int>(T);
+  p.N = static_cast<int>(F);
+  p.K = static_cast<int>(Kin);
+  p.C = static_cast<__nv_bfloat16*>(h);
+  p.ldc = ldh;
+  p.up_row = static_cast<int>(F);
+  p.num_m_blk = static_cast<int>((T + 255) / 256);
+  p.num_n_blk = static_cast<int>(F / 128);
+  p.num_k_blk = static_cast<int>((Kin + BK - 1) / BK);
+  p.num_tiles = p.num_m_blk * p.num_n_blk;
+  p.tma_store = make_out_map(&bm.c, h, T, F, ldh);
+  if (int rc = device_error_ptr(&p.err)) return rc;
+  int sms = 0;
+  if (int rc = sm_count(&sms)) return rc;
+  auto kern = gemm_pair_kernel<false, false, kEpiSwiGLU>;
+  constexpr int smem = PairSmemLayout<kEpiSwiGLU>::total;
+  VQ_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  const int avail = sms - sm_reserve(kEpiStoreBf16, sms);
+  int clusters = p.num_tiles < avail / 2 ? p.num_tiles : avail / 2;
+  if (clusters > kMaxClusters) clusters = kMaxClusters;
+  kern<<<2 * clusters, PairCfg<kEpiSwiGLU>::kThreads, smem, st>>>(ta, bm, p);
+  VQ_CUDA(cudaGetLastError());
+  return 0;
+}
+
 int vq_linear_fwd_grouped(const void* x, int64_t T, int64_t Kin, int64_t ldx, int G, const void* const* w,
                           int64_t N, int64_t ldw, const int* group_off, void* y, int64_t ldy, void* stream) {
   DeviceScope scope(y);

@@ -45,6 +45,7 @@ def _declare(lib):
         "vq_quantize": (_int, [_int, _vp, _int, _i64, _i64, _i64, _vp, _vp]),
         "vq_mix": (_int, [_int, _vp, _vp, _vp, _i64, _i64, _i64, _vp, _i64, _vp]),
         "vq_linear_fwd": (_int, [_vp, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _vp]),
+        "vq_linear_fwd_swiglu": (_int, [_vp, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _vp]),
         "vq_set_gategrad_sm_reserve": (_int, [_int]),
         "vq_set_gemm_sm_reserve": (_int, [_int]),
         "vq_route_prep": (_int, [_vp, _i64, _int, _vp, _vp, _vp, _vp]),
@@ -84,7 +85,7 @@ def _declare(lib):
 
 EXPORTED = (
     "vq_last_error", "vq_abi_version", "vq_format_info", "vq_device_error", "vq_dequant", "vq_mix",
-    "vq_linear_fwd", "vq_linear_fwd_grouped", "vq_set_gategrad_sm_reserve", "vq_set_gemm_sm_reserve", "vq_quantize", "vq_route_prep", "vq_linear_dx", "vq_gategrad_workspace_bytes", "vq_gategrad", "vq_gategrad_noalloc",
+    "vq_linear_fwd", "vq_linear_fwd_swiglu", "vq_linear_fwd_grouped", "vq_set_gategrad_sm_reserve", "vq_set_gemm_sm_reserve", "vq_quantize", "vq_route_prep", "vq_linear_dx", "vq_gategrad_workspace_bytes", "vq_gategrad", "vq_gategrad_noalloc",
     "vq_gategrad_grouped_workspace_bytes", "vq_gategrad_grouped",
     "vq_mixgemm_fwd", "vq_mixgemm_dx",
     "vq_loss_fused", "vq_loss_stats", "vq_loss_combine", "vq_loss_grad",
@@ -233,6 +234,20 @@ def linear_fwd(x: torch.Tensor, w: torch.Tensor, n_out: int | None = None, in_fe
         out = torch.empty(x.shape[0], N, dtype=torch.bfloat16, device=x.device)
     _check(_lib.vq_linear_fwd(x.data_ptr(), x.shape[0], kin, x.stride(0), w.data_ptr(), N, w.stride(0),
                               out.data_ptr(), out.stride(0), _stream(x)))
+    return out
+
+
+def linear_fwd_swiglu(x: torch.Tensor, w: torch.Tensor, F: int, in_features: int | None = None,
+                      out: torch.Tensor | None = None) -> torch.Tensor:
+    """h[T, F] = silu(x w[:F]^T) * (x w[F:2F]^T) in one GEMM (gate|up rounded
+    to bf16 before the activation); T > 128 and F a multiple of 128."""
+    _require_cuda(x, w)
+    kin = x.shape[1] if in_features is None else in_features
+    x = _as_operand(x)
+    if out is None:
+        out = torch.empty(x.shape[0], F, dtype=torch.bfloat16, device=x.device)
+    _check(_lib.vq_linear_fwd_swiglu(x.data_ptr(), x.shape[0], kin, x.stride(0), w.data_ptr(), F, w.stride(0),
+                                     out.data_ptr(), out.stride(0), _stream(x)))
     return out
 
 

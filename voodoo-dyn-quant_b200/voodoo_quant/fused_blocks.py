@@ -176,6 +176,11 @@ def _rmsnorm_forward(self, hidden_states: torch.Tensor) -> torch.Tensor:
 def _mlp_forward(self, x: torch.Tensor) -> torch.Tensor:
     if not _fusable(x):
         return self._vq_orig_forward(x)
+    if not torch.is_grad_enabled():  # a forward-only (teacher) MLP: SwiGLU in the gate|up GEMM's epilogue
+        from voodoo_quant.training.q8_teacher import q8_swiglu_group, q8_swiglu_ok
+
+        if q8_swiglu_ok(self.gate_proj, self.up_proj, x):
+            return self.down_proj(q8_swiglu_group(self.gate_proj, self.up_proj, x))
     if self.gate_proj.out_features == self.up_proj.out_features:
         gu = _group_projection((self.gate_proj, self.up_proj), x)
         if gu is not None and _fusable(gu):

@@ -91,6 +91,29 @@ def q8_linear_group(mods, x: torch.Tensor) -> torch.Tensor:
     return y.to(x.dtype).reshape(*x.shape[:-1], n_tot)
 
 
+def q8_swiglu_ok(gate, up, x: torch.Tensor) -> bool:
+    """Whether a teacher MLP's gate/up pair can run as one GEMM with the
+    SwiGLU in its epilogue (more than 128 tokens, a multiple of 128 features)."""
+    return (q8_groupable((gate, up)) and gate.out_features == up.out_features and gate.out_features % 128 == 0
+            and x.numel() // max(gate.in_features, 1) > 128)
+
+
+@torch.no_grad()
+def q8_swiglu_group(gate, up, x: torch.Tensor) -> torch.Tensor:
+    """silu(x W_gate^T) * (x W_up^T) for a teacher MLP: both Q8_0 weights
+    decoded into one bf16 [2F, Kin] weight, then one GEMM whose epilogue
+    applies the SwiGLU (``vq_linear_fwd_swiglu``); the [tokens, 2F] gate|up
+    output is never written.  Equal to ``q8_linear_group`` followed by the
+    SwiGLU kernel."""
+    in_f, F_ = gate.in_features, gate.out_features
+    ld = (in_f + 7) // 8 * 8
+    w = torch.empty(2 * F_, ld, dtype=torch.bfloat16, device=gate.qweight.device)
+    _C.mix(["Q8_0"], [gate.qweight], gate._one, F_, gate.padded_in_features, in_f, out=w[:F_])
+    _C.mix(["Q8_0"], [up.qweight], up._one, F_, up.padded_in_features, in_f, out=w[F_:])
+    h = _C.linear_fwd_swiglu(x.reshape(-1, in_f), w, F_, in_f)
+    return h.to(x.dtype).reshape(*x.shape[:-1], F_)
+
+
 class Q8Embedding(nn.Module):
     """nn.Embedding stand-in holding Q8_0 bytes; decodes the touched rows."""
 
