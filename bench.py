@@ -1182,6 +1182,67 @@ def run_gemm_shapes(args):
           flush=True)
 
 
+def _time_fn(fn, iters):
+    """ms per call of fn with CUDA events (2 warm-up calls; the timed calls
+    queue behind one more, so host launch time stays hidden)."""
+    import torch
+
+    for _ in range(2):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    fn()
+    e0.record()
+    for _ in range(iters):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / iters
+
+
+def run_fused_mix(args):
+    """The forward of a gated Linear two ways (one GPU): the mix kernel
+    writing W_mix to HBM and the GEMM reading it, against one GEMM whose
+    producer warps decode and mix the operand tiles in shared memory
+    (``vq_mixgemm_fwd_fused``).  Config 2 (K = 5) and the teacher's K = 1
+    Q8_0 decode at two 8B projection shapes (T = 16384)."""
+    import torch
+    from voodoo_quant import _C
+    from voodoo_quant.quants import rtn
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    pk, pk_kind = peaks()
+    peak_t = float(pk.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
+    g = torch.Generator(device=dev).manual_seed(0)
+    cases = [("config2", T_TOK, 14336, 4096, list(TYPES)),
+             ("teacher gate|up 8B", 16384, 28672, 4096, ["Q8_0"]),
+             ("teacher down 8B", 16384, 4096, 14336, ["Q8_0"])]
+    rows = []
+    for name, T, n, kin, types in cases:
+        w = torch.randn(n, kin, device=dev, generator=g) * 0.02
+        blocks = [rtn.quantize(w, q) for q in types]
+        del w
+        probs = torch.softmax(torch.randn(len(types), device=dev, generator=g), 0)
+        x = torch.randn(T, kin, device=dev, generator=g).to(torch.bfloat16)
+        wm = _C.mix(types, blocks, probs, n, kin, kin)
+        y = torch.empty(T, n, dtype=torch.bfloat16, device=dev)
+        t_mix = _time_fn(lambda: _C.mix(types, blocks, probs, n, kin, kin, out=wm), args.kernel_iters)
+        t_fwd = _time_fn(lambda: _C.linear_fwd(x, wm, n, kin, out=y), args.kernel_iters)
+        t_fused = _time_fn(lambda: _C.mixgemm_fwd_fused(x, types, blocks, probs, n, kin, kin, out=y),
+                           args.kernel_iters)
+        tf = 2.0 * T * n * kin / 1e12
+        rows.append({"case": name, "T": T, "N": n, "Kin": kin, "candidates": types, "mix_ms": round(t_mix, 4),
+                     "gemm_ms": round(t_fwd, 4), "separate_ms": round(t_mix + t_fwd, 4),
+                     "fused_ms": round(t_fused, 4), "fused_TFLOP/s": round(tf / (t_fused * 1e-3), 1),
+                     "fused_frac": round(tf / (t_fused * 1e-3) / peak_t, 3)})
+        del blocks, x, wm, y
+        torch.cuda.empty_cache()
+    assert _C.device_error() == 0
+    print(json.dumps({"metric": "gated-Linear forward: mix + GEMM vs decoded-operand GEMM", "peak_tflops": peak_t,
+                      "peak_source": f"{pk_kind} bf16_tflops (burst)", "cases": rows}), flush=True)
+
+
 def run_collectives(args):
     """The TP group's collectives alone (torchrun, one process per GPU): NCCL
     all-reduce, reduce-scatter and all-gather of bf16 tensors the size of the
@@ -1241,13 +1302,14 @@ def run_collectives(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--workload", choices=["8b", "layer", "tiny", "0.6b", "32b", "cache-load", "collectives",
-                                           "gemm-shapes"],
+                                           "gemm-shapes", "fused-mix"],
                     default="8b",
                     help="8b (default): the config-4 distillation step at TP-N; tiny/0.6b/32b: the other step "
                          "configurations (32b: the TP-4 / TP-8 case, K=7 with per-role menus); layer: the config-2 "
                          "single gated-Linear step; cache-load: candidate-cache files into HBM (GB/s); "
                          "collectives: the TP group's NCCL all-reduce / reduce-scatter / all-gather alone; "
-                         "gemm-shapes: the gated Linear's kernels at every 8B projection shape (TP-1 and TP-8 shards)")
+                         "gemm-shapes: the gated Linear's kernels at every 8B projection shape (TP-1 and TP-8 shards); "
+                         "fused-mix: the forward as mix + GEMM against one GEMM decoding its operand tiles")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
@@ -1326,6 +1388,8 @@ def main():
         run_collectives(args)
     elif args.workload == "gemm-shapes":
         run_gemm_shapes(args)
+    elif args.workload == "fused-mix":
+        run_fused_mix(args)
     elif args.workload != "layer":
         run_model_step(args)
     else:

@@ -213,6 +213,17 @@ int vq_mixgemm_fwd(const void* x, int64_t T, int64_t Kin, int64_t ldx, int K, co
                    const void* const* blocks, const float* probs, int64_t N, int64_t padded_cols, void* w_mix,
                    int64_t ldw, void* y, int64_t ldy, void* stream);
 
+/* K1 as ONE kernel: y[T, N] = x[T, Kin] * W_mix^T with W_mix = sum_k
+ * probs[k] * W_k decoded and mixed by producer warps straight into the
+ * GEMM's shared-memory operand tiles (no W_mix in HBM).  Each B tile is
+ * decoded again for every 256-row tile of x, so the decode work grows with T
+ * / 256; the result equals vq_mix followed by vq_linear_fwd bit for bit.
+ * T > 128 (VQ_ERR_UNSUPPORTED otherwise).  Replaces _MixedWeightFunction.forward
+ * + F.linear, voodoo_quant/layers.py:336-352,1730-1731, as one launch. */
+int vq_mixgemm_fwd_fused(const void* x, int64_t T, int64_t Kin, int64_t ldx, int K, const int* types,
+                         const void* const* blocks, const float* probs, int64_t N, int64_t padded_cols, void* y,
+                         int64_t ldy, void* stream);
+
 /* K2 convenience: vq_mix into w_mix[N, ldw] followed by vq_linear_dx, i.e.
  * dx[T, Kin] = dy[T, N] * (sum_k probs[k] W_k).  For callers that keep no
  * W_mix between the forward and the backward (the reference re-mixes in its

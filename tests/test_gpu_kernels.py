@@ -220,6 +220,34 @@ def test_linear_store_edges_exact(cuda, T, N, K, ld_pad, col_off):
     assert _C.device_error() == 0
 
 
+@pytest.mark.parametrize("types,T,N,IN", [
+    (["Q3_K", "Q4_K", "Q5_K", "Q6_K", "Q8_0"], 1000, 1000, 1000),
+    (["Q8_0"], 4096, 4096, 4096),
+    (["IQ4_XS", "Q3_K", "Q4_K", "Q5_K", "Q6_K", "Q8_0", "Q2_K"], 300, 768, 512),
+    (["Q2_K", "Q3_K", "Q4_K", "Q5_K", "Q6_K", "Q8_0"], 2048, 1792, 4096),
+])
+def test_mixgemm_fwd_fused_equals_mix_then_gemm(cuda, types, T, N, IN):
+    """The forward with the mixture decoded by producer warps into the GEMM's
+    shared-memory operand tiles against the mix kernel followed by the plain
+    GEMM: bit for bit (the same decode arithmetic, the same bf16 operand,
+    the same tcgen05 accumulation), with ragged rows, columns and K and
+    every candidate format."""
+    from voodoo_quant import _C
+    from voodoo_quant.quants import rtn
+
+    padded = (IN + 255) // 256 * 256
+    g = torch.Generator(device="cpu").manual_seed(T + N + IN + len(types))
+    w = torch.randn(N, padded, generator=g) * 0.02
+    blocks = [rtn.quantize(w, q).to(cuda) for q in types]
+    probs = torch.softmax(torch.randn(len(types), generator=g), 0).to(cuda)
+    x = _bf16(torch.randn(T, IN, generator=g)).to(cuda)
+    wm = _C.mix(types, blocks, probs, N, padded, IN)
+    ref = _C.linear_fwd(x, wm, N, IN)
+    got = _C.mixgemm_fwd_fused(x, types, blocks, probs, N, padded, IN)
+    assert torch.equal(got, ref)
+    assert _C.device_error() == 0
+
+
 @pytest.mark.parametrize("T,F,K,ld_pad,col_off", [(300, 256, 512, 0, 0), (4096, 1792, 4096, 0, 0),
                                                    (1000, 1024, 1000, 16, 0), (257, 384, 256, 3, 1)])
 def test_linear_fwd_swiglu_equals_gemm_then_swiglu(cuda, T, F, K, ld_pad, col_off):

@@ -26,6 +26,7 @@
 #pragma once
 
 #include "common.cuh"
+#include "decode_mix.cuh"
 #include "formats.cuh"
 
 namespace vq {
@@ -87,6 +88,9 @@ struct Params {
   // paired store kernel: write C through the tensor map BMaps::c (32 x 32
   // boxes, 64-byte swizzle) instead of per-row 16-byte stores
   int tma_store;
+  // decoded-B forward (paired kernel, kMixB): device float[K] mixture
+  // weights of `cands`; valid columns = cols, units_per_row as above
+  const float* mix_probs;
   // kEpiSwiGLU: B holds the gate rows [0, N) and the up rows [up_row,
   // up_row + N); a tile covers 128 output columns, the even CTA of the pair
   // loading gate rows and the odd one the matching up rows
@@ -408,6 +412,61 @@ __device__ __forceinline__ void epilogue_swiglu(const Params& p, const CUtensorM
   }
 }
 
+// One row of a CTA's B half for k-block [k0, k0 + 64) of a mixed weight,
+// decoded and mixed into shared memory by its own thread: W[nrow, k] =
+// sum_k p_k decode(W_k)[nrow, k] with mix_units_kernel's arithmetic (the
+// same candidate order, products and single bf16 rounding, so the tile
+// equals the mix kernel's W_mix bit for bit), columns at or past `cols` and
+// rows at or past N as zero.  Written in the 128-byte-swizzled K-major
+// layout a TMA load of the tile would produce: 16-byte chunk j of row r at
+// chunk j ^ (r & 7).  Each candidate unit is first staged into the thread's
+// own slot row (16-byte loads that stay inside the unit's 16-byte granules).
+__device__ __forceinline__ void mix_b_row(const Params& p, uint8_t* brow, uint32_t* slot_row, int nrow, int k0,
+                                          int r7) {
+  uint32_t packed[32];
+  if (nrow < p.N) {
+    const int c0 = (k0 & 255) >> 5;  // the k-block's first 32-weight sub-block of its unit
+    const long long unit = static_cast<long long>(nrow) * p.units_per_row + (k0 >> 8);
+    float2 acc0[16], acc1[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) acc0[j] = acc1[j] = make_float2(0.f, 0.f);
+    float cst0[2] = {0.f, 0.f}, cst1[2] = {0.f, 0.f};
+    for (int k = 0; k < p.cands.K; ++k) {
+      const int ub = p.cands.ubytes[k];
+      stage_row_lane(slot_row, p.cands.ptr[k] + unit * ub, ub);
+      const URef u{slot_row, 0, 0u};
+      const float pk = __ldg(p.mix_probs + k);
+      switch (p.cands.fmt[k]) {
+        case kQ8_0: mix_chunk<kQ8_0>(u, c0, pk, acc0, cst0); mix_chunk<kQ8_0>(u, c0 + 1, pk, acc1, cst1); break;
+        case kQ2_K: mix_chunk<kQ2_K>(u, c0, pk, acc0, cst0); mix_chunk<kQ2_K>(u, c0 + 1, pk, acc1, cst1); break;
+        case kQ3_K: mix_chunk<kQ3_K>(u, c0, pk, acc0, cst0); mix_chunk<kQ3_K>(u, c0 + 1, pk, acc1, cst1); break;
+        case kQ4_K: mix_chunk<kQ4_K>(u, c0, pk, acc0, cst0); mix_chunk<kQ4_K>(u, c0 + 1, pk, acc1, cst1); break;
+        case kQ5_K: mix_chunk<kQ5_K>(u, c0, pk, acc0, cst0); mix_chunk<kQ5_K>(u, c0 + 1, pk, acc1, cst1); break;
+        case kQ6_K: mix_chunk<kQ6_K>(u, c0, pk, acc0, cst0); mix_chunk<kQ6_K>(u, c0 + 1, pk, acc1, cst1); break;
+        case kIQ4_XS:
+          mix_chunk<kIQ4_XS>(u, c0, pk, acc0, cst0);
+          mix_chunk<kIQ4_XS>(u, c0 + 1, pk, acc1, cst1);
+          break;
+        default: break;  // the host checked every format
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const int e0 = k0 + 2 * j, e1 = k0 + 32 + 2 * j;  // columns of acc0[j].x and acc1[j].x
+      const float c0v = cst0[j >> 3], c1v = cst1[j >> 3];
+      packed[j] = e0 < p.cols ? bf16x2_bits(acc0[j].x + c0v, e0 + 1 < p.cols ? acc0[j].y + c0v : 0.f) : 0u;
+      packed[16 + j] = e1 < p.cols ? bf16x2_bits(acc1[j].x + c1v, e1 + 1 < p.cols ? acc1[j].y + c1v : 0.f) : 0u;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) packed[j] = 0u;
+  }
+#pragma unroll
+  for (int j = 0; j < 8; ++j)
+    *reinterpret_cast<uint4*>(brow + ((j ^ r7) << 4)) =
+        make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]);
+}
+
 // Epilogue of one 128 x 256 accumulator tile held in this CTA's TMEM.
 //   row0: first output row of this warp's 32 TMEM lanes; m128: index of the
 //   128-row block (for the gate-gradient partial slots); stage: the
@@ -662,9 +721,12 @@ struct PairCfg {
   static constexpr int kThreads = 128 + 128 * kEpiSets;  // TMA, MMA, TMEM-owner, spare warp + epilogue sets
 };
 
-template <int kEpi>
+// kMixB: the B operand (the mixed weight) is decoded and mixed into shared
+// memory by four producer warps per CTA instead of loaded by TMA; each of
+// their threads stages one candidate unit at a time (kStagePitch words).
+template <int kEpi, bool kMixB = false>
 struct PairSmemLayout {
-  static constexpr int kStages = PairCfg<kEpi>::kStages;
+  static constexpr int kStages = kMixB ? 5 : PairCfg<kEpi>::kStages;
   static constexpr int a_off = 0;
   static constexpr int b_off = a_off + kStages * PA_STAGE;
   static constexpr int bar_off = b_off + kStages * PB_STAGE;
@@ -678,7 +740,10 @@ struct PairSmemLayout {
   // aligned (the 64-byte swizzle pattern repeats every 512 bytes)
   static constexpr int out_off = (stage_off + 1023) & ~1023;
   static constexpr int out_bytes = (kEpi != kEpiGateGrad) ? 4 * 2 * kOutBufBytes : 0;
-  static constexpr int total = kEpi != kEpiGateGrad ? out_off + out_bytes : stage_off + stage_bytes;
+  static constexpr int mixb_off = out_off + out_bytes;
+  static constexpr int mixb_bytes = kMixB ? 128 * kStagePitch * 4 : 0;
+  static constexpr int total =
+      kEpi != kEpiGateGrad ? mixb_off + mixb_bytes : stage_off + stage_bytes;
   static_assert(total <= 232448, "paired kernel shared memory above the 227 KB per-block limit");
 };
 
@@ -693,12 +758,14 @@ __device__ __forceinline__ void group_tile(const Params& p, const int* mt, int t
   row_base = __ldg(p.group_off + g) + (local / p.num_n_blk) * 256;
 }
 
-template <bool kAmn, bool kBmn, int kEpi, int G = 1>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<kEpi>::kThreads, 1)
+template <bool kAmn, bool kBmn, int kEpi, int G = 1, bool kMixB = false>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<kEpi>::kThreads + (kMixB ? 128 : 0), 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ BMaps<G> tmB, Params p) {
-  using SL = PairSmemLayout<kEpi>;
-  constexpr int NST = PairCfg<kEpi>::kStages;
+  using SL = PairSmemLayout<kEpi, kMixB>;
+  constexpr int NST = SL::kStages;
   constexpr int kSets = PairCfg<kEpi>::kEpiSets;
+  static_assert(!kMixB || (!kAmn && !kBmn && kEpi == kEpiStoreBf16 && G == 1),
+                "decoded B operand: forward store GEMM only");
   extern __shared__ __align__(1024) uint8_t smem[];
   const uint32_t sbase = smem_u32(smem);
   if ((sbase & 1023u) != 0) {  // uniform in both CTAs: the layout is identical
@@ -719,7 +786,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<kEpi>::kThre
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < NST; ++s) {
-      mbar_init(full_bar(s), 1);
+      mbar_init(full_bar(s), kMixB ? 1 + 8 : 1);  // (kMixB: + 4 decoding warps x 2 CTAs)
       mbar_init(empty_bar(s), 1);
     }
     for (int a = 0; a < 2; ++a) {
@@ -790,7 +857,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<kEpi>::kThre
             break;
           }
           const uint32_t fb = map_to_rank(full_bar(s), 0);
-          if (leader) mbar_arrive_expect_tx(full_bar(s), 2 * (PA_STAGE + PB_STAGE));
+          if (leader) mbar_arrive_expect_tx(full_bar(s), kMixB ? 2 * PA_STAGE : 2 * (PA_STAGE + PB_STAGE));
           const uint32_t a_dst = sbase + SL::a_off + s * PA_STAGE;
           const uint32_t b_dst = sbase + SL::b_off + s * PB_STAGE;
           const int k0 = kb * BK;
@@ -800,7 +867,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<kEpi>::kThre
           } else {
             tma_load_2d_pair(a_dst, &tmA, fb, k0, m0);
           }
-          if (kBmn) {
+          if (kMixB) {
+            // B is written by the decoding warps
+          } else if (kBmn) {
 #pragma unroll
             for (int j = 0; j < 2; ++j) tma_load_2d_pair(b_dst + j * (64 * BK * 2), bmap, fb, n0 + 64 * j, k0);
           } else {
@@ -848,6 +917,36 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<kEpi>::kThre
         }
         if (!alive) break;
         tc_commit_pair_mc(tfull_bar(acc), 0x3);  // accumulators ready in both CTAs
+      }
+    }
+  } else if (kMixB && warp >= 4 + 4 * kSets) {
+    // ------------------------------------------------- B producer: decode + mix (both CTAs)
+    const int dt = threadIdx.x - (4 + 4 * kSets) * 32;  // this thread's row of the CTA's 128-row B half
+    uint32_t* slot_row = reinterpret_cast<uint32_t*>(smem + SL::mixb_off) + dt * kStagePitch;
+    uint32_t it = 0;
+    bool alive = true;
+    Seg sg;
+    for (int si = 0; alive && get_seg(p, ntiles, cluster_id, num_clusters, si, sg); ++si) {
+      int m_blk, n_blk, row_base, row_end;
+      const CUtensorMap* bmap;
+      coords(sg.tile, bmap, row_base, n_blk, row_end, m_blk);
+      const int nrow = n_blk * BN + 128 * static_cast<int>(rank) + dt;
+      for (int kb = sg.kb0; kb < sg.kb1; ++kb, ++it) {
+        const int s = it % NST;
+        const uint32_t ph = (it / NST) & 1u;
+        int ok = 1;
+        if (lane == 0) ok = mbar_wait(empty_bar(s), ph ^ 1u, abort_flag) ? 1 : 0;
+        ok = __shfl_sync(0xffffffffu, ok, 0);  // one decision for the whole warp
+        __syncwarp();
+        if (!ok) {
+          if (lane == 0) report_error(p.err, kDevWaitTimeout, 16);
+          alive = false;
+          break;
+        }
+        mix_b_row(p, smem + SL::b_off + s * PB_STAGE + dt * 128, slot_row, nrow, kb * BK, dt & 7);
+        fence_proxy_async_smem();  // the tensor cores read these rows through the async proxy
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(map_to_rank(full_bar(s), 0));
       }
     }
   } else if (warp >= 4) {

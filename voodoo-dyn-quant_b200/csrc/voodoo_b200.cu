@@ -685,6 +685,57 @@ int vq_mixgemm_fwd(const void* x, int64_t T, int64_t Kin, int64_t ldx, int K, co
   return vq_linear_fwd(x, T, Kin, ldx, w_mix, N, ldw, y, ldy, stream);
 }
 
+int vq_mixgemm_fwd_fused(const void* x, int64_t T, int64_t Kin, int64_t ldx, int K, const int* types,
+                         const void* const* blocks, const float* probs, int64_t N, int64_t padded_cols, void* y,
+                         int64_t ldy, void* stream) {
+  DeviceScope scope(y);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  vq::CandSet cs;
+  if (int rc = build_candset(&cs, K, types, blocks)) return rc;
+  if (probs == nullptr) return fail(VQ_ERR_INVALID, "null probs");
+  if (int rc = check_matrix(x, T, Kin, ldx, "x")) return rc;
+  if (int rc = check_matrix(y, T, N, ldy, "y")) return rc;
+  if (padded_cols < Kin || padded_cols % 256 != 0)
+    return fail(VQ_ERR_INVALID, "padded in_features %lld must be a multiple of 256 and >= %lld", (long long)padded_cols,
+                (long long)Kin);
+  if (T == 0 || N == 0) return 0;
+  if (Kin == 0) return zero_rows(y, T, N, ldy, 2, st);
+  if (T > 0x7fffffff || N > 0x7fffffff || Kin > 0x7fffffff) return fail(VQ_ERR_INVALID, "dimension too large");
+  if (!use_pair(T)) return fail(VQ_ERR_UNSUPPORTED, "decoded-operand GEMM needs more than %d rows", vq::gemm::BM);
+  using namespace vq::gemm;
+  CUtensorMap ta;
+  BMaps<1> bm{};
+  if (int rc = make_map(&ta, x, T, Kin, ldx, BM)) return rc;
+  Params p{};
+  p.M = static_cast<int>(T);
+  p.N = static_cast<int>(N);
+  p.K = static_cast<int>(Kin);
+  p.C = static_cast<__nv_bfloat16*>(y);
+  p.ldc = ldy;
+  p.cands = cs;
+  p.units_per_row = static_cast<int>(padded_cols / 256);
+  p.cols = Kin;
+  p.mix_probs = probs;
+  p.num_m_blk = static_cast<int>((T + 255) / 256);
+  p.num_n_blk = static_cast<int>((N + BN - 1) / BN);
+  p.num_k_blk = static_cast<int>((Kin + BK - 1) / BK);
+  p.num_tiles = p.num_m_blk * p.num_n_blk;
+  p.tma_store = make_out_map(&bm.c, y, T, N, ldy);
+  if (int rc = device_error_ptr(&p.err)) return rc;
+  int sms = 0;
+  if (int rc = sm_count(&sms)) return rc;
+  auto kern = gemm_pair_kernel<false, false, kEpiStoreBf16, 1, true>;
+  constexpr int smem = PairSmemLayout<kEpiStoreBf16, true>::total;
+  static_assert(smem <= 232448, "decoded-operand GEMM shared memory above the 227 KB per-block limit");
+  VQ_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  const int avail = sms - sm_reserve(kEpiStoreBf16, sms);
+  int clusters = p.num_tiles < avail / 2 ? p.num_tiles : avail / 2;
+  if (clusters > kMaxClusters) clusters = kMaxClusters;
+  kern<<<2 * clusters, PairCfg<kEpiStoreBf16>::kThreads + 128, smem, st>>>(ta, bm, p);
+  VQ_CUDA(cudaGetLastError());
+  return 0;
+}
+
 int vq_mixgemm_dx(const void* dy, int64_t T, int64_t N, int64_t lddy, int K, const int* types,
                   const void* const* blocks, const float* probs, int64_t Kin, int64_t padded_cols, void* w_mix,
                   int64_t ldw, void* dx, int64_t lddx, void* stream) {

@@ -60,6 +60,8 @@ def _declare(lib):
                                        ctypes.c_size_t, _vp, _i64, _vp]),
         "vq_mixgemm_fwd": (_int, [_vp, _i64, _i64, _i64, _int, _vp, _vp, _vp, _i64, _i64, _vp, _i64, _vp,
                                   _i64, _vp]),
+        "vq_mixgemm_fwd_fused": (_int, [_vp, _i64, _i64, _i64, _int, _vp, _vp, _vp, _i64, _i64, _vp, _i64,
+                                        _vp]),
         "vq_mixgemm_dx": (_int, [_vp, _i64, _i64, _i64, _int, _vp, _vp, _vp, _i64, _i64, _vp, _i64, _vp,
                                  _i64, _vp]),
         "vq_loss_fused": (_int, [_vp, _i64, _vp, _i64, _vp, _i64, _i64, _f32, _f32, _f32, _vp, _vp, _vp,
@@ -87,7 +89,7 @@ EXPORTED = (
     "vq_last_error", "vq_abi_version", "vq_format_info", "vq_device_error", "vq_dequant", "vq_mix",
     "vq_linear_fwd", "vq_linear_fwd_swiglu", "vq_linear_fwd_grouped", "vq_set_gategrad_sm_reserve", "vq_set_gemm_sm_reserve", "vq_quantize", "vq_route_prep", "vq_linear_dx", "vq_gategrad_workspace_bytes", "vq_gategrad", "vq_gategrad_noalloc",
     "vq_gategrad_grouped_workspace_bytes", "vq_gategrad_grouped",
-    "vq_mixgemm_fwd", "vq_mixgemm_dx",
+    "vq_mixgemm_fwd", "vq_mixgemm_fwd_fused", "vq_mixgemm_dx",
     "vq_loss_fused", "vq_loss_stats", "vq_loss_combine", "vq_loss_grad",
     "vq_rmsnorm_fwd", "vq_rmsnorm_bwd", "vq_add_rmsnorm_fwd", "vq_rmsnorm_bwd_add", "vq_rope", "vq_swiglu_fwd", "vq_swiglu_bwd",
 )
@@ -234,6 +236,22 @@ def linear_fwd(x: torch.Tensor, w: torch.Tensor, n_out: int | None = None, in_fe
         out = torch.empty(x.shape[0], N, dtype=torch.bfloat16, device=x.device)
     _check(_lib.vq_linear_fwd(x.data_ptr(), x.shape[0], kin, x.stride(0), w.data_ptr(), N, w.stride(0),
                               out.data_ptr(), out.stride(0), _stream(x)))
+    return out
+
+
+def mixgemm_fwd_fused(x: torch.Tensor, qtypes, qbytes, probs: torch.Tensor, n_out: int, padded_cols: int,
+                      in_features: int | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+    """y = x W_mix^T with the mixture decoded into the GEMM's operand tiles
+    (vq_mixgemm_fwd_fused); equal to ``mix`` then ``linear_fwd``."""
+    _require_cuda(x, probs, *qbytes)
+    kin = x.shape[1] if in_features is None else in_features
+    x = _as_operand(x)
+    K, types, ptrs = _cand_arrays(qtypes, qbytes)
+    p = probs.to(torch.float32).contiguous()
+    if out is None:
+        out = torch.empty(x.shape[0], n_out, dtype=torch.bfloat16, device=x.device)
+    _check(_lib.vq_mixgemm_fwd_fused(x.data_ptr(), x.shape[0], kin, x.stride(0), K, types, ptrs, p.data_ptr(), n_out,
+                                     padded_cols, out.data_ptr(), out.stride(0), _stream(x)))
     return out
 
 
