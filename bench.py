@@ -921,6 +921,8 @@ def run_model_step(args):
                                                  teacher_stream=args.teacher_stream,
                                                  teacher_stream_sms=args.teacher_stream_sms,
                                                  teacher_tp=args.teacher_tp,
+                                                 joint_teacher=bool(args.joint_teacher),
+                                                 joint_teacher_sms=args.joint_teacher_sms,
                                                  sequence_parallel=args.sequence_parallel and world > 1))
     torch.cuda.synchronize()
     t_build = time.perf_counter() - t_build
@@ -1027,8 +1029,10 @@ def run_model_step(args):
                     "teacher_tp": args.teacher_tp or world,
                     "teacher_batch_slices": world // (args.teacher_tp or world),
                     "sequence_parallel": bool(args.sequence_parallel and world > 1),
-                    "teacher": (f"own stream and communicator beside the student, "
-                                f"{args.teacher_stream_sms} SMs left to collectives") if args.teacher_stream
+                    "teacher": (f"layers interleaved with the student's forward all-reduces, "
+                                f"{args.joint_teacher_sms} SMs left to them") if trainer._joint_ok()
+                    else (f"own stream and communicator beside the student, "
+                          f"{args.teacher_stream_sms} SMs left to collectives") if args.teacher_stream
                     else "after the student, same stream"},
             "roofline": {"bound": "tensor", "kernel": "whole step (tcgen05 GEMMs dominate)", "flops_per_token": fpt,
                          "achieved": round(ach, 1), "peak": round(peak_t * world, 1), "unit": "TFLOP/s",
@@ -1347,6 +1351,12 @@ def main():
                     help="step workloads under TP: the teacher's own TP degree t (groups of t ranks, each on "
                          "its batch slice; one all-to-all of its logits); 0 = the student's; default: the "
                          "smallest t whose groups split the batch evenly")
+    ap.add_argument("--joint-teacher", action=argparse.BooleanOptionalAction, default=None,
+                    help="step workloads under TP with a TP-1 teacher on each rank's batch slice: issue each "
+                         "teacher decoder block while the matching student block's forward all-reduce is in flight "
+                         "(default: on with 4 or more GPUs, where it was measured faster)")
+    ap.add_argument("--joint-teacher-sms", type=int, default=32,
+                    help="with --joint-teacher: SMs the teacher's GEMMs leave to the all-reduce in flight")
     ap.add_argument("--sequence-parallel", action=argparse.BooleanOptionalAction, default=False,
                     help="step workloads under TP: residual stream, norms and residual adds on token shards; "
                          "all-gather / reduce-scatter around each block instead of all-reduces")
@@ -1376,6 +1386,8 @@ def main():
         args.graph_step = world > 1 and args.workload != "layer" and args.logits_chunk <= 0 and not args.ptqr
     if args.teacher_tp < 0:
         args.teacher_tp = auto_teacher_tp(args.workload, world) if args.logits_chunk <= 0 else 0
+    if args.joint_teacher is None:
+        args.joint_teacher = world >= 4
     if args.ncu_case == "tp8":
         run_ncu_case_tp8()
     elif args.ncu_case:

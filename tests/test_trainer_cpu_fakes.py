@@ -39,11 +39,11 @@ def _shapes():
                                         batch=2, seq=48, budget=0.45)
 
 
-def _step(name: str, tp: bool, overlap_sms: int, chunk: int, sp: bool = False):
+def _step(name: str, tp: bool, overlap_sms: int, chunk: int, sp: bool = False, **step_args):
     from voodoo_quant.training import synthetic as S
     from voodoo_quant.training.trainer import StepArgs, build_distill
 
-    args = StepArgs(max_steps=4, ce_reduction="tokens", logits_chunk=chunk, sequence_parallel=sp)
+    args = StepArgs(max_steps=4, ce_reduction="tokens", logits_chunk=chunk, sequence_parallel=sp, **step_args)
     trainer, shape = build_distill(name, "cpu", seed=3, args=args, tp=tp, overlap_sms=overlap_sms)
     x, y = S.random_tokens(shape, "cpu", seed=5)
     r = trainer.forward_backward(x, y)
@@ -51,7 +51,7 @@ def _step(name: str, tp: bool, overlap_sms: int, chunk: int, sp: bool = False):
     deferred = sum(bool(m.__dict__.get("_defer_gategrad", False)) for m in trainer.replaced.values())
     from voodoo_quant.parallel import sp_enabled
     on = sp_enabled() and hasattr(trainer.student.model, "_vq_sp_orig_forward")
-    return float(r["loss"]), grads, deferred, on
+    return float(r["loss"]), grads, deferred, on, trainer._joint_ok()
 
 
 def _cos(a: torch.Tensor, b: torch.Tensor) -> float:
@@ -94,6 +94,8 @@ def _worker(rank, world, port, outdir):
         res["sp"] = _step("cpu_tp2", True, 0, 0, sp=True)
         res["sp_overlap"] = _step("cpu_tp2", True, 24, 0, sp=True)
         res["sp_chunked"] = _step("cpu_tp2", True, 24, 40, sp=True)
+        res["tt1"] = _step("cpu_tp2", True, 24, 0, teacher_tp=1)
+        res["joint"] = _step("cpu_tp2", True, 24, 0, teacher_tp=1, joint_teacher=True)
         torch.save(res, os.path.join(outdir, f"r{rank}.pt"))
     finally:
         undo()
@@ -139,6 +141,14 @@ def test_tp2_step_matches_one_process_with_and_without_overlap():
             assert float((sp[1][n] - g).norm()) <= 2e-2 * float(g.norm()) + 1e-9, n
             assert float((spo[1][n] - sp[1][n]).norm()) <= 1e-5 * float(sp[1][n].norm()) + 1e-9, n
             assert float((spc[1][n] - sp[1][n]).norm()) <= 1e-4 * float(sp[1][n].norm()) + 1e-9, n
+    # the teacher's layers interleaved with the student's forward all-reduces
+    # (teacher at TP-1 on each rank's batch slice): the same step exactly
+    for r in rs:
+        tt1, joint = r["tt1"], r["joint"]
+        assert joint[4] and not tt1[4]
+        assert joint[0] == tt1[0]
+        for n in ref[1]:
+            assert torch.equal(joint[1][n], tt1[1][n]), n
     # both ranks hold the same (all-reduced) gate gradients
     for n in ref[1]:
         assert torch.equal(rs[0]["plain"][1][n], rs[1]["plain"][1][n]), n

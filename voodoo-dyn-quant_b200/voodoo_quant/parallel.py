@@ -74,6 +74,10 @@ class _TPState:
     # all-gather before the column-parallel inputs, reduce-scatter after the
     # row-parallel outputs (instead of all-reducing replicated activations)
     sequence_parallel = False
+    # row-parallel outputs returned as partial sums for the caller to reduce
+    # (deferred_row_sums(): the step that interleaves teacher layers with the
+    # student's forward all-reduces)
+    defer_row_sums = False
 
 
 TP = _TPState()
@@ -176,6 +180,7 @@ def reset_tp() -> None:
     TP.teacher_group = None
     TP.forward_override = None
     TP.sequence_parallel = False
+    TP.defer_row_sums = False
 
 
 def teacher_subgroups(t: int):
@@ -264,6 +269,29 @@ def enable_input_grad_overlap(sms: int) -> bool:
         TP.overlap_group = dist.new_group(ranks=ranks, backend=dist.get_backend(TP.group))
     TP.overlap_sms = int(sms)
     return True
+
+
+@contextlib.contextmanager
+def deferred_row_sums(on: bool = True):
+    """Inside the block, a row-parallel gated Linear starts the all-reduce of
+    its output in place without waiting for it (``take_row_sums`` hands the
+    caller the handles, which it waits on before reading the outputs)."""
+    prev = TP.defer_row_sums
+    TP.defer_row_sums = bool(on) and TP.enabled
+    try:
+        yield
+    finally:
+        TP.defer_row_sums = prev
+
+
+_ROW_SUMS: list = []
+
+
+def take_row_sums() -> list:
+    """The handles of the row-parallel sums started since the last call."""
+    works = list(_ROW_SUMS)
+    _ROW_SUMS.clear()
+    return works
 
 
 def sp_enabled() -> bool:
@@ -481,9 +509,28 @@ class _NcclRowReducer:
 _NCCL_ROW_REDUCER = _NcclRowReducer()
 
 
+class _AsyncRowReducer:
+    """`_NcclRowReducer` that only starts the in-place all-reduce (inside
+    ``deferred_row_sums``); the handle goes to ``take_row_sums``."""
+
+    @staticmethod
+    def linear(x2: torch.Tensor, w: torch.Tensor, n_out: int, in_features: int) -> torch.Tensor:
+        from voodoo_quant import _C
+
+        y = _C.linear_fwd(x2, w, n_out, in_features)
+        _ROW_SUMS.append(dist.all_reduce(y, op=dist.ReduceOp.SUM, group=_fwd_group(), async_op=True))
+        return y
+
+
+_ASYNC_ROW_REDUCER = _AsyncRowReducer()
+
+
 def nccl_row_reducer():
-    """The in-place NCCL reducer for row-parallel gated Linears (None without TP)."""
-    return _NCCL_ROW_REDUCER if TP.enabled else None
+    """The in-place NCCL reducer for row-parallel gated Linears (None without
+    TP); inside ``deferred_row_sums`` the one that leaves the sum in flight."""
+    if not TP.enabled:
+        return None
+    return _ASYNC_ROW_REDUCER if TP.defer_row_sums else _NCCL_ROW_REDUCER
 
 
 def tp_copy_to_parallel(t: torch.Tensor) -> torch.Tensor:

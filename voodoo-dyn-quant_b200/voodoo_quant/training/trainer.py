@@ -106,6 +106,12 @@ class StepArgs:
     # all-gather before and a reduce-scatter after every block instead of
     # the all-reduces of replicated activations
     sequence_parallel: bool = False
+    # under TP with a teacher at TP-1 on its batch slice (teacher_tp = 1):
+    # run the teacher's layers interleaved with the student's, each teacher
+    # block issued while the student block's forward all-reduce is in flight
+    # (its GEMMs leaving `joint_teacher_sms` SMs to the all-reduce)
+    joint_teacher: bool = False
+    joint_teacher_sms: int = 32
 
 
 class GatedDistillTrainer:
@@ -157,7 +163,9 @@ class GatedDistillTrainer:
         v0 = self._vocab_start()
         if a.logits_chunk > 0:
             return self._forward_backward_chunked(x, y, a, tau, v0)
-        if a.teacher_stream:
+        if self._joint_ok():
+            logits, t_logits = self._joint_forward(x)
+        elif a.teacher_stream:
             with self._forward_sm_reserve():
                 t_logits = self._teacher_fork(x, lambda: self._teacher_logits(x))
                 logits = self.student(input_ids=x, use_cache=False).logits
@@ -243,6 +251,89 @@ class GatedDistillTrainer:
         loss = kd + a.size_weight * size_loss.detach()
         return {"loss": loss, "lm_loss": lm, "distill_loss": kl, "size_bytes": current.detach(),
                 "size_loss": size_loss.detach(), "tau": tau}
+
+    def _joint_ok(self) -> bool:
+        """Whether this step interleaves the teacher with the student
+        (StepArgs.joint_teacher; TP with a TP-1 teacher on the rank's batch
+        slice, the plain loss path, no sequence parallelism)."""
+        from voodoo_quant.parallel import sp_enabled
+
+        a = self.args
+        return (a.joint_teacher and self.tp and self._tsplit is not None and self._tsplit[3] == 1
+                and a.logits_chunk <= 0 and not sp_enabled()
+                and hasattr(getattr(self.student, "model", None), "layers")
+                and hasattr(getattr(self.teacher, "model", None), "layers"))
+
+    def _joint_forward(self, x: torch.Tensor):
+        """Student logits (autograd) and teacher logits (no grad, in the
+        student's vocabulary layout) with the teacher's decoder layers
+        interleaved between the student's: each student block's row-parallel
+        output is summed by an all-reduce started in place,
+        the teacher's matching block is issued while it is in flight, and the
+        student waits for the sum only when it reads it (row-parallel gated
+        layers start their in-place sums inside ``deferred_row_sums``).  The
+        same operations
+        and sums as the two forwards one after the other."""
+        from voodoo_quant import _C
+        from voodoo_quant.parallel import TP, _fwd_group, deferred_row_sums, redistribute_vocab_shards, take_row_sums
+
+        _, g, _, t = self._tsplit
+        G = TP.world_size // t
+        if x.shape[0] % G:
+            raise ValueError(f"batch {x.shape[0]} does not split over {G} teacher groups (teacher_tp={t})")
+        b = x.shape[0] // G
+        xt = x[g * b:(g + 1) * b]
+        sm, tm = self.student.model, self.teacher.model
+        s_layers = sm.layers[: sm.config.num_hidden_layers]
+        t_layers = tm.layers[: tm.config.num_hidden_layers]
+        if len(s_layers) != len(t_layers):
+            raise ValueError("joint teacher schedule needs as many teacher layers as student layers")
+        hs = sm.embed_tokens(x)
+        pe_s = sm.rotary_emb(hs, position_ids=torch.arange(hs.shape[1], device=hs.device).unsqueeze(0))
+        with torch.no_grad():
+            ht = tm.embed_tokens(xt)
+            pe_t = tm.rotary_emb(ht, position_ids=torch.arange(ht.shape[1], device=ht.device).unsqueeze(0))
+
+        @contextlib.contextmanager
+        def beside_sum():  # the teacher's GEMMs leave SMs to the all-reduce in flight
+            n = self.args.joint_teacher_sms
+            if n > 0:
+                _C.set_gemm_sm_reserve(n)
+            try:
+                with torch.no_grad():
+                    yield
+            finally:
+                if n > 0:
+                    _C.set_gemm_sm_reserve(0)
+
+        pend_s = pend_t = None
+        xt_n = None
+        for ls, lt in zip(s_layers, t_layers):
+            hs, xs = _res_norm(pend_s, hs, ls.input_layernorm)
+            with deferred_row_sums():
+                a = ls.self_attn(hidden_states=xs, attention_mask=None, position_embeddings=pe_s)[0]
+            works = take_row_sums()  # o_proj's sum, in flight
+            with beside_sum():
+                ht, xt_n = _res_norm(pend_t, ht, lt.input_layernorm)
+                at = lt.self_attn(hidden_states=xt_n, attention_mask=None, position_embeddings=pe_t)[0]
+                ht, xt_n = _res_norm(at, ht, lt.post_attention_layernorm)
+            for w in works:
+                w.wait()
+            hs, xs = _res_norm(a, hs, ls.post_attention_layernorm)
+            with deferred_row_sums():
+                m = ls.mlp(xs)
+            works = take_row_sums()  # down_proj's sum, in flight
+            with beside_sum():
+                pend_t = lt.mlp(xt_n)
+            for w in works:
+                w.wait()
+            pend_s = m
+        hs, out_s = _res_norm(pend_s, hs, sm.norm)
+        with torch.no_grad():
+            _, out_t = _res_norm(pend_t, ht, tm.norm)
+            t_local = self.teacher.lm_head(out_t)
+        logits = self.student.lm_head(out_s)
+        return logits, redistribute_vocab_shards(t_local, t, group=_fwd_group())
 
     def _teacher_logits(self, x: torch.Tensor) -> torch.Tensor:
         """The teacher's logits in the student's layout.  With a teacher of
@@ -379,6 +470,19 @@ class GatedDistillTrainer:
 
     def assignments(self) -> dict[str, str]:
         return {name: layer.get_assignment() for name, layer in self.replaced.items()}
+
+
+def _res_norm(pending, h: torch.Tensor, norm):
+    """(h + pending, norm(h + pending)), or (h, norm(h)) without a pending
+    output: one add + RMSNorm kernel where the fused kernels apply."""
+    if pending is None:
+        return h, norm(h)
+    from voodoo_quant.fused_blocks import _fusable, _norm_weights_fusable, add_rms_norm
+
+    if _fusable(h) and _norm_weights_fusable(norm):
+        return add_rms_norm(pending, h, norm.weight, norm.variance_epsilon)
+    h = h + pending
+    return h, norm(h)
 
 
 def _capturing() -> bool:
