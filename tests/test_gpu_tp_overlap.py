@@ -3,7 +3,9 @@
 also the head's dX all-reduced in two row chunks) against the same step
 without overlap, and the sequence-parallel step (token-shard residual
 stream, all-gather / reduce-scatter around every block) with and without
-the overlap, on 2 GPUs (skipped with fewer).
+the overlap, and the step whose TP-1 teacher runs interleaved with the
+student's forward all-reduces against the same teacher run after the
+student, on 2 GPUs (skipped with fewer).
 
 The overlap only reorders launches and leaves SMs free; the gate-gradient
 GEMM's stream-K split depends on how many SMs it gets, so its fp32 partial
@@ -52,15 +54,19 @@ def _worker(rank, world, port, outdir):
     res = {}
     try:
         parallel.adopt_process_group(rank)
-        for sms, chunks, sp in ((0, 1, False), (24, 1, False), (24, 2, False), (0, 1, True), (24, 1, True)):
+        for sms, chunks, sp, extra in ((0, 1, False, None), (24, 1, False, None), (24, 2, False, None),
+                                       (0, 1, True, None), (24, 1, True, None), (24, 1, False, "tt1"),
+                                       (24, 1, False, "joint")):
             layers.INPUT_GRAD_CHUNKS = chunks  # the head sums its own input gradient in row chunks
+            kw = {} if extra is None else {"teacher_tp": 1, "joint_teacher": extra == "joint"}
             trainer, shape = build_distill("tp2_test", dev, seed=0, tp=True, overlap_sms=sms,
-                                           args=StepArgs(sequence_parallel=sp))
+                                           args=StepArgs(sequence_parallel=sp, **kw))
+            joint = trainer._joint_ok()
             deferred = sum(bool(m.__dict__.get("_defer_gategrad", False)) for m in trainer.replaced.values())
             x, y = S.random_tokens(shape, dev, seed=1)
             out = trainer.forward_backward(x, y)
             torch.cuda.synchronize()
-            res[(sms, chunks, sp)] = {"loss": float(out["loss"]), "deferred": deferred,
+            res[extra or (sms, chunks, sp)] = {"loss": float(out["loss"]), "deferred": deferred, "joint": joint,
                         "grads": {n: m.gates.grad.detach().cpu().clone() for n, m in trainer.replaced.items()},
                         "left": layers.has_deferred_gategrads()}
             del trainer
@@ -92,6 +98,13 @@ def test_overlapped_input_grad_allreduce_matches_plain_step():
             for n, g in base["grads"].items():
                 h = b["grads"][n]
                 assert float((g - h).norm()) <= 1e-3 * float(g.norm()) + 1e-12, (key, n)
+        # the teacher (TP-1, each rank's batch slice) interleaved with the
+        # student's forward all-reduces: the same step
+        tt1, joint = r["tt1"], r["joint"]
+        assert joint["joint"] and not tt1["joint"]
+        assert abs(tt1["loss"] - joint["loss"]) <= 1e-5 * abs(tt1["loss"])
+        for n, g in tt1["grads"].items():
+            assert float((g - joint["grads"][n]).norm()) <= 1e-3 * float(g.norm()) + 1e-12, n
         sp = r[(0, 1, True)]
         assert abs(sp["loss"] - a["loss"]) <= 2e-3 * abs(a["loss"])
         for n, g in a["grads"].items():
