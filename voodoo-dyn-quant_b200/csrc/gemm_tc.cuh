@@ -13,16 +13,25 @@
 // Warp roles (256 threads): warp 0 issues TMA, warp 1 issues tcgen05.mma
 // (one thread), warp 2 owns the TMEM allocation, warps 4-7 run the epilogue.
 // The accumulator is double buffered in TMEM (2 x 256 fp32 columns) so the
-// epilogue of tile i overlaps the main loop of tile i+1.
+// epilogue of tile i overlaps the main loop of tile i+1.  gemm_pair_kernel
+// runs the same roles on a CTA pair (cta_group::2, 256-row tiles), with a
+// second set of epilogue warps for the gate gradient, and optionally four
+// more warps that decode and mix the B operand into shared memory instead of
+// TMA (kMixB).
 //
 // Epilogues:
-//   kEpiStoreBf16 : D -> bf16 C[M, N] (row-major, leading dimension ldc).
+//   kEpiStoreBf16 : D -> bf16 C[M, N] (row-major, leading dimension ldc),
+//                   through bulk tensor stores of 32 x 32 boxes where C allows.
 //   kEpiGateGrad  : D is a 128 x 256 tile of dW; each epilogue thread owns one
 //                   output row and dots it against the re-decoded candidate
 //                   weights of the same 256-column unit, giving per-tile
 //                   partial sums of g_k = <dW, W_k> that are written to
 //                   partials[tile][warp][k] and reduced in fixed order by
 //                   gategrad_reduce_kernel.  dW never reaches global memory.
+//                   Several layers stacked by rows (q/k/v, gate/up) share one
+//                   launch, each warp decoding its own layer's candidates.
+//   kEpiSwiGLU    : paired kernel only; D holds 128 gate and the matching 128
+//                   up outputs, the epilogue writes h = silu(gate) * up.
 #pragma once
 
 #include "common.cuh"
