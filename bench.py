@@ -918,8 +918,6 @@ def run_model_step(args):
                                                  ptqr=args.ptqr, logits_chunk=args.logits_chunk,
                                                  ce_reduction="tokens" if args.logits_chunk > 0 or args.graph_step
                                                  else "valid", static_shapes=args.graph_step,
-                                                 teacher_stream=args.teacher_stream,
-                                                 teacher_stream_sms=args.teacher_stream_sms,
                                                  teacher_tp=args.teacher_tp,
                                                  joint_teacher=bool(args.joint_teacher),
                                                  joint_teacher_sms=args.joint_teacher_sms,
@@ -1031,8 +1029,6 @@ def run_model_step(args):
                     "sequence_parallel": bool(args.sequence_parallel and world > 1),
                     "teacher": (f"layers interleaved with the student's forward all-reduces, "
                                 f"{args.joint_teacher_sms} SMs left to them") if trainer._joint_ok()
-                    else (f"own stream and communicator beside the student, "
-                          f"{args.teacher_stream_sms} SMs left to collectives") if args.teacher_stream
                     else "after the student, same stream"},
             "roofline": {"bound": "tensor", "kernel": "whole step (tcgen05 GEMMs dominate)", "flops_per_token": fpt,
                          "achieved": round(ach, 1), "peak": round(peak_t * world, 1), "unit": "TFLOP/s",
@@ -1341,12 +1337,6 @@ def main():
                     help="step workloads: record forward + backward as one CUDA graph (static-shape mode, "
                          "CE over all tokens) and replay it each step; the optimizer stays eager "
                          "(default: on with more than one GPU)")
-    ap.add_argument("--teacher-stream", action="store_true",
-                    help="step workloads: the teacher's forward on a second stream beside the student's, its "
-                         "TP all-reduces on a communicator of their own")
-    ap.add_argument("--teacher-stream-sms", type=int, default=0,
-                    help="with --teacher-stream: SMs the forward GEMMs leave to the other stream's all-reduces "
-                         "(and the teacher communicator's CTA cap); 0 = none")
     ap.add_argument("--teacher-tp", type=int, default=-1,
                     help="step workloads under TP: the teacher's own TP degree t (groups of t ranks, each on "
                          "its batch slice; one all-to-all of its logits); 0 = the student's; default: the "

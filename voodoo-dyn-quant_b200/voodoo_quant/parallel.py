@@ -64,9 +64,6 @@ class _TPState:
     # leave free); None = those all-reduces use `group`
     overlap_group = None
     overlap_sms = 0
-    # third communicator for the teacher's forward collectives when the
-    # teacher runs on its own stream beside the student (enable_teacher_overlap)
-    teacher_group = None
     # the communicator forward collectives use inside collectives_on(); None = group
     forward_override = None
     # sequence parallelism (enable_sequence_parallel): between the blocks the
@@ -99,27 +96,6 @@ def collectives_on(group):
         yield
     finally:
         TP.forward_override = prev
-
-
-def enable_teacher_overlap(sms: int = 0) -> bool:
-    """A communicator of its own for the teacher's forward collectives, so the
-    teacher's forward can run on a second stream beside the student's.
-    With ``sms`` > 0 (NCCL) its collectives use at most that many CTAs, to fit
-    in the SMs the forward GEMMs then leave free.  Collective: every rank
-    calls it with the same ``sms``.  Returns whether TP is on."""
-    if not TP.enabled:
-        TP.teacher_group = None
-        return False
-    if TP.teacher_group is None:
-        ranks = list(range(TP.world_size))
-        if sms > 0 and dist.get_backend(TP.group) == "nccl":
-            opts = dist.ProcessGroupNCCL.Options()
-            opts.config.max_ctas = int(sms)
-            opts.config.min_ctas = min(int(sms), 8)
-            TP.teacher_group = dist.new_group(ranks=ranks, backend="nccl", pg_options=opts)
-        else:
-            TP.teacher_group = dist.new_group(ranks=ranks, backend=dist.get_backend(TP.group))
-    return True
 
 
 def tp_init(backend: str = "nccl", timeout_min: int = 240) -> bool:
@@ -177,7 +153,6 @@ def reset_tp() -> None:
     TP.device = None
     TP.overlap_group = None
     TP.overlap_sms = 0
-    TP.teacher_group = None
     TP.forward_override = None
     TP.sequence_parallel = False
     TP.defer_row_sums = False

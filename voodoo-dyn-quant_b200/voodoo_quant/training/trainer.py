@@ -87,13 +87,6 @@ class StepArgs:
     # ce_reduction="tokens" (the "valid" count is read on the host), which
     # equals "valid" whenever no target is ignored
     static_shapes: bool = False
-    # the teacher's forward on a second stream beside the student's, its
-    # collectives on a communicator of their own (parallel.enable_teacher_overlap),
-    # so each model's TP all-reduces can run under the other's kernels
-    teacher_stream: bool = False
-    # with teacher_stream: SMs the forward GEMMs of both models leave free for
-    # the other stream's all-reduces (and the teacher's communicator's CTA cap); 0 = none
-    teacher_stream_sms: int = 0
     # TP degree of the teacher (0 = the student's): the teacher is sharded t
     # ways inside groups of t consecutive ranks, each group runs it on its
     # slice of the batch (the batch divides into world / t slices), and one
@@ -134,9 +127,7 @@ class GatedDistillTrainer:
             raise ValueError("static_shapes needs ce_reduction='tokens': the 'valid' token count is read on the host")
         set_static_shapes(args.static_shapes)
         self._graph = None
-        self._tstream = None
         self._tsplit = None  # (group, group index, rank in group, t) with a teacher of its own TP degree
-        self._graph_keep = []  # tensors two streams of a recorded graph share
         self.optimizer = torch.optim.AdamW(self.trainable, lr=args.lr, betas=(0.9, 0.95))
         self.scheduler = torch.optim.lr_scheduler.CosineAnnealingLR(self.optimizer, T_max=args.max_steps,
                                                                     eta_min=1e-3)
@@ -165,11 +156,6 @@ class GatedDistillTrainer:
             return self._forward_backward_chunked(x, y, a, tau, v0)
         if self._joint_ok():
             logits, t_logits = self._joint_forward(x)
-        elif a.teacher_stream:
-            with self._forward_sm_reserve():
-                t_logits = self._teacher_fork(x, lambda: self._teacher_logits(x))
-                logits = self.student(input_ids=x, use_cache=False).logits
-            t_logits = self._teacher_join(t_logits)
         else:
             logits = self.student(input_ids=x, use_cache=False).logits
             with torch.no_grad():
@@ -215,16 +201,9 @@ class GatedDistillTrainer:
         probabilities from a detached leaf, so each chunk's backward stays in
         the head; the leaf's accumulated gradient joins the final backward."""
         student, teacher = self.student, self.teacher
-        if a.teacher_stream:
-            with self._forward_sm_reserve():
-                t_hidden = self._teacher_fork(
-                    x, lambda: teacher.model(input_ids=x, use_cache=False).last_hidden_state)
-                hidden = student.model(input_ids=x, use_cache=False).last_hidden_state
-            t_hidden = self._teacher_join(t_hidden)
-        else:
-            hidden = student.model(input_ids=x, use_cache=False).last_hidden_state
-            with torch.no_grad():
-                t_hidden = teacher.model(input_ids=x, use_cache=False).last_hidden_state
+        hidden = student.model(input_ids=x, use_cache=False).last_hidden_state
+        with torch.no_grad():
+            t_hidden = teacher.model(input_ids=x, use_cache=False).last_hidden_state
         head = student.lm_head
         row = head.__dict__.get("_bank_probs")
         bank_ref = head.__dict__.get("_bank_ref")
@@ -354,55 +333,6 @@ class GatedDistillTrainer:
             local = self.teacher(input_ids=x[g * b:(g + 1) * b], use_cache=False).logits
         return redistribute_vocab_shards(local, t, group=_fwd_group())
 
-    def _teacher_fork(self, x: torch.Tensor, run):
-        """Issue the teacher's forward (``run``) on the teacher's stream, after
-        the work already queued on the current stream, with its collectives
-        on the teacher's communicator; the student's forward is issued next
-        on the current stream and the two run side by side."""
-        from voodoo_quant.parallel import TP, collectives_on
-
-        if self._tstream is None:
-            self._tstream = torch.cuda.Stream()
-        self._tstream.wait_stream(torch.cuda.current_stream())
-        self._cross_stream_use(x, self._tstream)
-        with torch.cuda.stream(self._tstream), collectives_on(TP.teacher_group), torch.no_grad():
-            return run()
-
-    @contextlib.contextmanager
-    def _forward_sm_reserve(self):
-        """While both forwards are issued, the store-epilogue GEMMs (forward,
-        mixture-free dX) leave ``teacher_stream_sms`` SMs to the other
-        stream's collectives; no effect at 0."""
-        sms = self.args.teacher_stream_sms
-        if sms <= 0:
-            yield
-            return
-        from voodoo_quant import _C
-
-        _C.set_gemm_sm_reserve(sms)
-        try:
-            yield
-        finally:
-            _C.set_gemm_sm_reserve(0)
-
-    def _teacher_join(self, t: torch.Tensor) -> torch.Tensor:
-        """Make the current stream wait for the teacher's; its output is then
-        used (and its memory held) on the current stream."""
-        main = torch.cuda.current_stream()
-        main.wait_stream(self._tstream)
-        self._cross_stream_use(t, main)
-        return t
-
-    def _cross_stream_use(self, t: torch.Tensor, stream) -> None:
-        """``t`` is used on ``stream`` too: tell the allocator (eager), or,
-        while a graph is recorded, keep it alive with the graph."""
-        if not t.is_cuda:
-            return
-        if _capturing():
-            self._graph_keep.append(t)
-        else:
-            t.record_stream(stream)
-
     def apply_update(self) -> None:
         torch.nn.utils.clip_grad_norm_(self.trainable, max_norm=1.0)
         self.optimizer.step()
@@ -466,7 +396,6 @@ class GatedDistillTrainer:
         collectives it holds)."""
         self._graph = None
         self._gout = None
-        self._graph_keep = []
 
     def assignments(self) -> dict[str, str]:
         return {name: layer.get_assignment() for name, layer in self.replaced.items()}
@@ -571,10 +500,6 @@ def build_distill(shape_name: str, device, seed: int = 0, args: StepArgs | None 
             use_sequence_parallel(teacher)
         enable_sequence_parallel(sp)
     if tp and TP.enabled:
-        from voodoo_quant.parallel import enable_teacher_overlap
-
-        if args is not None and args.teacher_stream:
-            enable_teacher_overlap(args.teacher_stream_sms)
         if overlap_sms > 0:
             from voodoo_quant.parallel import enable_input_grad_overlap, mark_deferred_gategrads
 
